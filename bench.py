@@ -1,0 +1,448 @@
+#!/usr/bin/env python
+"""Decode benchmark of libl3g on B200.
+
+Default workload: Llama-3.1-8B-shaped synthetic Q8_0 model (dim 4096, 32
+layers, 32/8 heads, FFN 14336, vocab 128256, llama3 RoPE scaling), KV cache
+prefilled with 4096 seeded tokens, then greedy decode at batch 1.  One
+"step" is one decoded token.  With --gpus N (under torchrun) the model is
+tensor-parallel over N GPUs.
+
+Prints one JSON line:
+  value  decode tok/s with the step loop resident on the device (each token
+         fed from the previous step's on-device argmax), CUDA-event timed;
+  e2e    the same tok/s through the public per-step call
+         (l3g_forward_argmax: host token in, pinned H2D, graph, D2H result);
+  roofline       the dominant kernel (the Q8_0 matvec, FFN up/gate shape)
+                 timed live with CUDA events against measured HBM bandwidth;
+  decode_roofline  (weight + KV bytes per token) x tok/s / HBM bandwidth;
+  cpu_baseline   the oracle (C restatement + the reference's own simd.c) on
+                 the host cores, on a bounded sample of the same workload.
+
+--impl reference times only the reference's CPU path (the oracle) on this
+workload.  --workload matvec runs the Q8_0 matvec microbench instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llama3.go_b200"))
+
+METRIC = "decode tok/s at 1/2/4/8 B200 (Llama-8B-shape Q8_0, bs1); % of HBM roofline"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="l3g", choices=["l3g", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec"])
+    ap.add_argument("--config", default="llama3.1-8b")
+    ap.add_argument("--prefill", type=int, default=4096)
+    ap.add_argument("--kv", default="f32", choices=["f32", "f16"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--iters", type=int, default=1000, help="matvec microbench iterations")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9 and r[0].strip() == str(self.idx)]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+
+
+def physical_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local < len(parts) and parts[local].strip().isdigit():
+            return int(parts[local])
+    return local
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Dist:
+    def __init__(self, world, rank, local):
+        import torch
+        self.world, self.rank, self.local = world, rank, local
+        self.torch = torch
+        self.pg = None
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+            self.dist = dist
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast_bytes(self, b):
+        if not self.pg:
+            return b
+        obj = [b]
+        self.dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.pg:
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU path (the oracle): cpu_baseline and the reference arm
+# ---------------------------------------------------------------------------
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_decode_rate(cfg, T, prefill, seconds, max_steps, seed):
+    """Greedy decode steps of the reference's chat path (ForwardTopK with
+    topK 40, argmax over the items) at position `prefill`, the KV cache of the
+    earlier positions filled with seeded values (the step's cost does not
+    depend on them).  Returns (tok/s, steps, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle
+    oracle.build()
+    threads = host_cores()
+    om = oracle.OracleModel(cfg, T, threads=threads)
+    om.new_state(prefill + max_steps + 2)
+    K, V = om.kv_arrays()
+    rng = np.random.default_rng(seed)
+    chunk = 1 << 24
+    for arr in (K, V):
+        for i in range(0, arr.size, chunk):
+            n = min(chunk, arr.size - i)
+            arr[i:i + n] = rng.random(n, dtype=np.float32) - 0.5
+    om.pos = prefill - 1
+    tok = int(rng.integers(0, cfg.vocab))
+    t0 = time.perf_counter()
+    ids, lg = om.forward_topk(tok, 40)
+    first = time.perf_counter() - t0
+    n = int(max(1, min(max_steps, round(seconds / max(first, 1e-6)))))
+    tok = int(ids[int(np.argmax(lg))])
+    t0 = time.perf_counter()
+    for _ in range(n):
+        ids, lg = om.forward_topk(tok, 40)
+        tok = int(ids[int(np.argmax(lg))])
+    el = time.perf_counter() - t0
+    om.close()
+    return n / el, n, om.threads
+
+
+def make_host_model(cfg, seed, device):
+    import synthetic
+    return synthetic.make_model(cfg, seed=seed, device=device)
+
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    import synthetic
+    import torch
+    cfg = synthetic.CONFIGS[args.config]
+    dev = f"cuda:{local}" if torch.cuda.is_available() else "cpu"
+    T = make_host_model(cfg, args.seed, dev)
+    # each step is one decoded token; at most ~90 s of timed CPU work so the
+    # whole run ends within a few minutes
+    rate, n, threads = cpu_decode_rate(cfg, T, args.prefill, 90.0, max(1, args.steps), args.seed + 1)
+    sample = (f"{n} greedy decode steps of the {cfg.name} shape at position {args.prefill} "
+              f"(KV of earlier positions seeded), ForwardTopK path, topK 40")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": round(1000.0 / rate, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": f"{cfg.name}-shape Q8_0 bs1 greedy decode after {args.prefill}-token prefill",
+                   "model": cfg.name, "global_batch": 1, "seq_len": args.prefill, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample,
+                         "what": "C restatement of internal/llama/infer.go linked to the reference's own "
+                                 "internal/llama/simd.c (AVX2, compiled from the reference tree)"},
+        "e2e": {"value": round(rate, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# the GPU arm
+# ---------------------------------------------------------------------------
+def time_matvec_kernel(l3g, cfg, seed, hbm):
+    """Live timing of the dominant kernel: the Q8_0 matvec on the FFN up/gate
+    shape ([2*n_ff x n_emb], the largest per-layer matrix), rotating over
+    copies that together exceed L2, CUDA events on the launching stream."""
+    import numpy as np
+    import synthetic
+    import torch
+    rows, cols = 2 * cfg.n_ff, cfg.n_emb
+    ncopy = 3
+    mats = []
+    for i in range(ncopy):
+        g = torch.Generator(device="cuda").manual_seed(seed * 31 + i)
+        w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g, device="cuda") * 0.02, torch)
+        mats.append(l3g.Matrix(w.cpu().numpy(), rows, cols))
+        del w
+    x = torch.randn(cols, device="cuda")
+    nb = cols // 32
+    d = torch.empty(nb, device="cuda")
+    q = torch.empty(nb * 32, dtype=torch.int8, device="cuda")
+    l3g.quantize_q8_0_device(x.data_ptr(), cols, d.data_ptr(), q.data_ptr())
+    out = torch.empty(rows, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for i in range(6):
+        mats[i % ncopy].matvec(d.data_ptr(), q.data_ptr(), out.data_ptr(), stream=stream)
+    iters = 90
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(iters):
+        mats[i % ncopy].matvec(d.data_ptr(), q.data_ptr(), out.data_ptr(), stream=stream)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    alg = rows * cols // 32 * 34 + cols + nb * 4 + rows * 4
+    for mtx in mats:
+        mtx.Close()
+    return {"kernel": "k_matvec (Q8_0 matvec, FFN up/gate shape %dx%d)" % (rows, cols),
+            "bytes_per_launch": alg, "ms_per_launch": ms, "achieved_gbs": alg / ms / 1e6}
+
+
+def run_l3g(args):
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        args.gpus = world
+    import numpy as np
+    import torch
+    import build
+    build.build(quiet=True)
+    import l3g
+    import synthetic
+    D = Dist(world, rank, local)
+    torch.cuda.set_device(local)
+    hbm, hbm_kind = peaks()
+    cfg = synthetic.CONFIGS[args.config]
+
+    T = make_host_model(cfg, args.seed, f"cuda:{local}")
+    torch.cuda.empty_cache()
+    nid = D.bcast_bytes(l3g.nccl_unique_id() if (world > 1 and rank == 0) else None) if world > 1 else None
+    kv = l3g.L3G_KV_F16 if args.kv == "f16" else l3g.L3G_KV_F32
+    opts = l3g.default_options(world, rank, local, kv, nid)
+    m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, opts)
+    ctx = args.prefill + args.warmup + args.steps + 2
+    if ctx > cfg.ctx_len:
+        raise SystemExit(f"prefill+warmup+steps exceeds the model context {cfg.ctx_len}")
+    s = m.NewState(ctx)
+    ws = m.NewWorkspace(ctx, 40)
+    prompt = synthetic.prompt_ids(cfg, args.prefill, seed=args.seed)
+    t0 = time.perf_counter()
+    m.Prefill(s, prompt[:-1], ws)
+    prefill_s = time.perf_counter() - t0
+    p0 = s.Pos
+
+    # value: device-resident greedy loop
+    warm, _ = m.DecodeGreedy(s, int(prompt[-1]), max(1, args.warmup), ws)
+    D.barrier()
+    clk = Clocks(physical_index(local))
+    toks, dev_ms = m.DecodeGreedy(s, int(warm[-1]), args.steps, ws)
+    D.barrier()
+    clocks = clk.stop()
+    dev_ms = D.max(dev_ms)
+    value = args.steps / (dev_ms / 1000.0)
+    kernels = ws.kernels_per_step()
+
+    # e2e: the public per-step call, host token in / host token out
+    s.Pos = p0
+    tok = int(prompt[-1])
+    for _ in range(max(1, args.warmup)):
+        tok, _ = m.ForwardArgmax(s, tok, ws)
+    D.barrier()
+    t0 = time.perf_counter()
+    e2e_toks = []
+    for _ in range(args.steps):
+        tok, _ = m.ForwardArgmax(s, tok, ws)
+        e2e_toks.append(tok)
+    D.barrier()
+    e2e_s = D.max(time.perf_counter() - t0)
+    e2e = args.steps / e2e_s
+    same = bool(np.array_equal(np.array(e2e_toks, np.int32), toks))
+
+    # roofline of the whole decode step (weights + KV read per token)
+    es = 2 if args.kv == "f16" else 4
+    first_pos = p0 + max(1, args.warmup)
+    kv_bytes = sum(cfg.kv_bytes(first_pos + i + 1, es) for i in range(args.steps)) / args.steps
+    step_bytes = cfg.weight_bytes() + kv_bytes
+    decode_gbs = step_bytes * value / 1e9
+    mv = time_matvec_kernel(l3g, cfg, args.seed, hbm) if rank == 0 else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, n, threads = cpu_decode_rate(cfg, T, args.prefill, args.cpu_seconds, 64, args.seed + 1)
+        cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{n} greedy decode steps of the {cfg.name} shape at position {args.prefill} "
+                         f"(KV of earlier positions seeded), ForwardTopK path, topK 40; C restatement "
+                         f"of infer.go + the reference's own simd.c"}
+    m.Close()
+    D.close()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}-shape Q8_0 bs1 greedy decode after {args.prefill}-token prefill",
+                   "model": cfg.name, "global_batch": 1, "seq_len": args.prefill,
+                   "parallelism": f"tp{world}", "kv_dtype": args.kv,
+                   "l2": "inputs larger than L2: every step streams %.2f GB of weights" % (cfg.weight_bytes() / 1e9),
+                   "weights": "seeded N(0,0.02) quantized to Q8_0, norms 1.0; random-init synthetic"},
+        "roofline": {"bound": "hbm", "achieved": round(mv["achieved_gbs"], 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(mv["achieved_gbs"] / hbm, 4), "traffic": None,
+                     "kernel": mv["kernel"], "bytes_per_launch": mv["bytes_per_launch"],
+                     "ms_per_launch": round(mv["ms_per_launch"], 5), "peak_kind": hbm_kind},
+        "decode_roofline": {"bytes_per_token": int(step_bytes), "weight_bytes": cfg.weight_bytes(),
+                            "kv_bytes_avg": int(kv_bytes), "achieved_gbs": round(decode_gbs, 1),
+                            "frac": round(decode_gbs / (hbm * world), 4), "peak_gbs_aggregate": hbm * world},
+        "e2e": {"value": round(e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 16,
+                "api": "l3g_forward_argmax per step (pinned H2D token+pos, graph, D2H result)",
+                "tokens_match_device_loop": same},
+        "gpu_launches": kernels * args.steps,
+        "kernels_per_step": kernels,
+        "clocks": clocks,
+        "prefill_s": round(prefill_s, 3),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_matvec(args):
+    """Q8_0 matvec microbench over the 8B shapes: GB/s of weights + x + out."""
+    import torch
+    import build
+    build.build(quiet=True)
+    import l3g
+    import synthetic
+    hbm, kind = peaks()
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    for rows, cols in ((4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
+        alg = rows * cols // 32 * 34 + cols + cols // 32 * 4 + rows * 4
+        ncopy = max(1, -(-4 * l2 // alg))
+        g = torch.Generator(device="cuda").manual_seed(rows + cols)
+        w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g, device="cuda") * 0.02, torch)
+        host = w.cpu().numpy()
+        del w
+        mats = [l3g.Matrix(host, rows, cols) for _ in range(ncopy)]
+        x = torch.randn(cols, device="cuda")
+        d = torch.empty(cols // 32, device="cuda")
+        q = torch.empty(cols, dtype=torch.int8, device="cuda")
+        l3g.quantize_q8_0_device(x.data_ptr(), cols, d.data_ptr(), q.data_ptr())
+        out = torch.empty(rows, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+        for i in range(5):
+            mats[i % ncopy].matvec(d.data_ptr(), q.data_ptr(), out.data_ptr(), stream=st)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(args.iters):
+            mats[i % ncopy].matvec(d.data_ptr(), q.data_ptr(), out.data_ptr(), stream=st)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.iters
+        gbs = alg / ms / 1e6
+        print(json.dumps({"workload": "q8_0 matvec microbench", "shape": [rows, cols], "iters": args.iters,
+                          "copies_rotated": ncopy, "bytes_per_launch": alg, "us_per_launch": round(ms * 1e3, 3),
+                          "achieved_gbs": round(gbs, 1), "peak_gbs": hbm, "frac": round(gbs / hbm, 4),
+                          "peak_kind": kind}), flush=True)
+        for mtx in mats:
+            mtx.Close()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.workload == "matvec":
+        return run_matvec(args)
+    return run_l3g(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

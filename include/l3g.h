@@ -1,0 +1,222 @@
+/*
+ * l3g.h -- C ABI of libl3g.so, the B200 (sm_100a) decode library for
+ * llama3.go.  Plain pointers and sizes only, so a cgo shim (build tag
+ * "cuda") can replace:
+ *   - the cgo SIMD kernels   internal/llama/simd.h:7-9 (matvec_q8_c,
+ *     dot_product), bound in matvec_cgo.go:14-30 and dot_cgo.go:16-22;
+ *   - the goroutine pool     internal/llama/workers.go:21-116
+ *     (WorkerPool.Run / ParallelFor), held as Model.Pool (model.go:52);
+ *   - the per-token forward  internal/llama/infer.go:21-267 and :269-511.
+ * The Go Model / State / Workspace / Sampler API stays; each of its calls maps
+ * onto one entry point below.
+ *
+ * Conventions
+ *   - Every function returns an int status: L3G_OK (0) or a negative code;
+ *     l3g_last_error() returns the message of the calling thread's last
+ *     failure.  Messages reuse the reference's wording where one exists
+ *     (e.g. "context length exceeded (%d)", infer.go:23).
+ *   - Host pointers unless a parameter says "device".  The library owns all
+ *     device memory; it keeps no caller pointer after a call returns.
+ *   - A state / workspace is used by one host thread at a time (as the
+ *     reference's Workspace, workspace.go:3-4).
+ *   - Tensor-parallel runs use one process (or thread) per GPU; ranks pass
+ *     the same l3g_options.nccl_id, obtained on rank 0 from
+ *     l3g_nccl_unique_id() and shared by the caller.
+ */
+#ifndef L3G_H
+#define L3G_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define L3G_VERSION 1
+
+/* status codes */
+#define L3G_OK 0
+#define L3G_E_INVALID (-1) /* bad argument, shape or tensor type          */
+#define L3G_E_CUDA (-2)    /* CUDA runtime error                          */
+#define L3G_E_NCCL (-3)    /* NCCL missing or failed                      */
+#define L3G_E_CTX (-4)     /* context length exceeded, infer.go:22-24     */
+#define L3G_E_TOKEN (-5)   /* token out of range, infer.go:514-516        */
+#define L3G_E_FORMAT (-6)  /* GGUF parse / missing tensor or hyperparam   */
+#define L3G_E_DEVICE (-7)  /* a kernel's own check failed (bounded wait
+                              ran out, index out of range): see message  */
+
+/* ggml tensor type ids, internal/llama/q8_0.go:7-11 */
+#define L3G_TYPE_F32 0
+#define L3G_TYPE_F16 1
+#define L3G_TYPE_Q8_0 8
+
+/* KV cache element type */
+#define L3G_KV_F32 0 /* the reference's layout type (state.go:8-9)      */
+#define L3G_KV_F16 1 /* half the KV bytes per token                      */
+
+typedef struct l3g_model l3g_model;
+typedef struct l3g_state l3g_state;
+typedef struct l3g_workspace l3g_workspace;
+typedef struct l3g_matrix l3g_matrix;
+
+/* HyperParams, internal/llama/model.go:10-21.  llama3 RoPE frequency scaling,
+ * absent from the reference (rope.go:15-37), is taken from an optional f32
+ * tensor "rope_freqs.weight" of rope_dim/2 divisors (llama.cpp's
+ * convention); without it the tables are exactly the reference's. */
+typedef struct {
+  int32_t vocab_size;
+  int32_t n_layers;
+  int32_t n_emb;
+  int32_t n_heads;
+  int32_t n_heads_kv;
+  int32_t n_ff;
+  int32_t rope_dim;
+  int32_t ctx_len;
+  float rms_eps;
+  float rope_base;
+} l3g_hparams;
+
+/* One tensor of the model file: gguf.TensorInfo + Tensor.Data
+ * (internal/gguf/gguf.go:47-53, internal/llama/tensor.go:9-12).  dims are
+ * ne0-first ([cols, rows] for matrices).  data points at the tensor's first
+ * byte (e.g. into the mmapped GGUF); nbytes may be 0 (then derived). */
+typedef struct {
+  const char *name;
+  uint32_t type;
+  uint32_t n_dims;
+  uint64_t dims[4];
+  const void *data;
+  uint64_t nbytes;
+} l3g_tensor;
+
+/* Placement of a model: single GPU or tensor-parallel rank. */
+typedef struct {
+  int32_t world_size; /* 1 = single GPU                                   */
+  int32_t rank;       /* 0 .. world_size-1                                */
+  int32_t device;     /* CUDA device ordinal, -1 = the current device      */
+  int32_t kv_dtype;   /* L3G_KV_F32 or L3G_KV_F16                         */
+  uint8_t nccl_id[128]; /* ncclUniqueId shared by all ranks (world > 1)   */
+} l3g_options;
+
+/* TopKItem, internal/llama/topk.go:5-8 */
+typedef struct {
+  int32_t id;
+  float logit;
+} l3g_topk_item;
+
+/* ---- library ----------------------------------------------------------- */
+const char *l3g_last_error(void);
+int l3g_version(void);
+int l3g_device_count(int32_t *n);
+/* ncclGetUniqueId for rank 0 of a tensor-parallel group. */
+int l3g_nccl_unique_id(uint8_t out[128]);
+void l3g_options_default(l3g_options *opt);
+
+/* ---- model: LoadModel (model.go:55-156), Close (model.go:158-166) ------- */
+/* Uploads the Q8_0 blocks once (values unchanged, repacked into 16-byte
+ * aligned tiles) plus f32 norms; keeps no host pointer.  Tensor names as
+ * model.go:83-138; output.weight optional (tied, model.go:91-94). */
+int l3g_model_load(const l3g_hparams *hp, const l3g_tensor *tensors,
+                   int32_t n_tensors, const l3g_options *opt,
+                   l3g_model **out);
+/* Same, parsing the GGUF file itself (gguf.go:64-234, readHyperParams
+ * model.go:168-219). */
+int l3g_model_load_gguf(const char *path, const l3g_options *opt,
+                        l3g_model **out);
+int l3g_model_hparams(const l3g_model *m, l3g_hparams *out);
+void l3g_model_free(l3g_model *m);
+
+/* ---- state: NewState (state.go:51-64), KV cache in HBM ------------------ */
+int l3g_state_new(l3g_model *m, int32_t ctx_len, l3g_state **out);
+int l3g_state_pos(const l3g_state *s, int32_t *pos);
+int l3g_state_ctx_len(const l3g_state *s, int32_t *ctx_len);
+/* Moves the write position (0 <= pos <= ctx): rewinds a session for reuse
+ * (the REPL's /reset, main.go:120-122) without reallocating. */
+int l3g_state_set_pos(l3g_state *s, int32_t pos);
+void l3g_state_free(l3g_state *s);
+
+/* ---- workspace: NewWorkspace (workspace.go:35-69) ------------------------ */
+/* Device activations, scratch, stream and the captured per-step CUDA graphs.
+ * ctx_len <= 0 or > model ctx is clamped like workspace.go:36-41; top_k <= 0
+ * means 40 (workspace.go:42-44). */
+int l3g_workspace_new(l3g_model *m, int32_t ctx_len, int32_t top_k,
+                      l3g_workspace **out);
+void l3g_workspace_free(l3g_workspace *ws);
+
+/* ---- per-token forward ---------------------------------------------------- */
+/* ForwardIntoWorkspace, infer.go:21-267: one token through all layers; fills
+ * logits_out[vocab] (host) when non-NULL, otherwise skips the logits matvec
+ * like infer.go:250 (prefill).  Advances the state's position. */
+int l3g_forward(l3g_model *m, l3g_state *s, l3g_workspace *ws, int32_t token,
+                float *logits_out);
+/* ForwardTopKIntoWorkspace, infer.go:269-511: the top_k largest logits
+ * (top_k <= 0 means 40, at most 64), sorted by descending logit, ties by
+ * lower id.  *n_items receives the count. */
+int l3g_forward_topk(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                     int32_t token, int32_t top_k, l3g_topk_item *items,
+                     int32_t *n_items);
+/* Greedy decode step: argmax (lowest id on ties) of the logits that
+ * l3g_forward would return, computed on the device. */
+int l3g_forward_argmax(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                       int32_t token, int32_t *next_token, float *max_logit);
+/* ingest, cmd/go-llama-chat/main.go:276-286: l3g_forward without logits for
+ * each token in turn. */
+int l3g_prefill(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                const int32_t *tokens, int32_t n);
+/* The decode loop of cmd/go-llama-chat/main.go:141-165 with a greedy
+ * sampler: n steps, each fed the previous step's argmax, replayed back to
+ * back on the device with no host round trip in between.  out_tokens[i]
+ * (host, n entries) is the argmax after step i; device_ms (nullable)
+ * receives the device time of the n steps (CUDA events on the workspace's
+ * stream).  Advances the position by n. */
+int l3g_decode_greedy(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                      int32_t first_token, int32_t n, int32_t *out_tokens,
+                      float *device_ms);
+/* Kernels of this library one step launches (greedy variant), for launch
+ * accounting. */
+int l3g_workspace_kernels_per_step(l3g_workspace *ws, int32_t *n);
+
+/* ---- Q8_0 matvec drop-in: matvec_q8_c (simd.h:8) / matVecQ8_0 ------------ */
+/* Uploads a GGUF Q8_0 matrix (rows x cols, 34-byte blocks, host bytes). */
+int l3g_matrix_upload(const void *q8_0_rows, int32_t rows, int32_t cols,
+                      int32_t device, l3g_matrix **out);
+/* out[r] = sum_b (fp16(w.d[r,b]) * x_scales[b]) * (sum_i w.q[r,b,i] *
+ * x_qs[b*32+i]) for r in [start_row, end_row).  x_scales, x_qs, out are
+ * DEVICE pointers; stream is a cudaStream_t (NULL = default stream). */
+int l3g_matvec_q8(const l3g_matrix *w, const float *x_scales,
+                  const int8_t *x_qs, float *out, int32_t start_row,
+                  int32_t end_row, void *stream);
+void l3g_matrix_free(l3g_matrix *w);
+int l3g_matrix_device_bytes(const l3g_matrix *w, uint64_t *bytes);
+
+/* QuantizeQ8_0Into, q8_0.go:22-79, on the device (DEVICE pointers): d has
+ * ceil(n/32) floats, qs ceil(n/32)*32 bytes. */
+int l3g_quantize_q8_0(const float *x, int32_t n, float *d, int8_t *qs,
+                      void *stream);
+
+/* ---- inspection (tests, debugging) --------------------------------------- */
+/* KV entries of one layer for positions [pos0, pos0+npos) in the reference
+ * layout [pos][kv_head][head_dim] (f32, host), this rank's kv heads only. */
+int l3g_state_read_kv(const l3g_state *s, int32_t layer, int32_t pos0,
+                      int32_t npos, float *k_out, float *v_out);
+/* Workspace buffers after the last forward (f32, host). */
+#define L3G_BUF_HIDDEN 0  /* residual stream x after the last layer [n_emb]  */
+#define L3G_BUF_Q 1       /* last layer's roped query [local heads * hd]     */
+#define L3G_BUF_ATTN 2    /* last layer's attention output [local heads*hd]  */
+#define L3G_BUF_FFN_ACT 3 /* last layer's SwiGLU output [local n_ff]         */
+#define L3G_BUF_LOGITS 4  /* logits of the last forward that made them [V]   */
+int l3g_workspace_read(const l3g_workspace *ws, int32_t which, float *out,
+                       int32_t n);
+
+/* Runs a kernel that waits, with the library's bounded-wait helper, on a
+ * barrier nothing completes; *status receives the device error code the
+ * kernel reports (L3G_E_DEVICE expected).  Exercises failure detection
+ * without hanging the GPU. */
+int l3g_selftest_bounded_wait(int32_t device, int32_t timeout_us,
+                              int32_t *status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* L3G_H */

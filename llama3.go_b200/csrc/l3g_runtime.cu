@@ -1,0 +1,1304 @@
+// Host runtime of libl3g: model upload and repack, KV state, workspaces and
+// the per-step CUDA graphs, behind the C ABI of include/l3g.h.
+//
+// One decode step is one CUDA graph: a host->device copy of {token, pos},
+// the embed kernel, per layer five kernels (QKV+RoPE+KV-append, split-K
+// attention, Wo, up/gate+SwiGLU, down; plus an NCCL all-reduce after Wo and
+// down when tensor-parallel), the logits kernel with fused argmax, and a
+// device->host copy of the 16-byte result.  Kernels are launched with
+// programmatic stream serialization so each one's weight prefetch overlaps
+// the tail of its predecessor.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "l3g.h"
+#include "l3g_internal.h"
+#include "l3g_kernels.cuh"
+
+using namespace l3g;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+static thread_local std::string g_err;
+
+int l3g_fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                     \
+  do {                                                                     \
+    cudaError_t e_ = (expr);                                               \
+    if (e_ != cudaSuccess)                                                 \
+      return l3g_fail(L3G_E_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+extern "C" const char* l3g_last_error(void) { return g_err.c_str(); }
+extern "C" int l3g_version(void) { return L3G_VERSION; }
+
+extern "C" int l3g_device_count(int32_t* n) {
+  int c = 0;
+  CUDA_TRY(cudaGetDeviceCount(&c));
+  if (n) *n = c;
+  return L3G_OK;
+}
+
+extern "C" void l3g_options_default(l3g_options* opt) {
+  if (!opt) return;
+  memset(opt, 0, sizeof *opt);
+  opt->world_size = 1;
+  opt->rank = 0;
+  opt->device = -1;
+  opt->kv_dtype = L3G_KV_F32;
+}
+
+// ---------------------------------------------------------------------------
+// NCCL, bound at run time (the process may already hold torch's copy)
+// ---------------------------------------------------------------------------
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t,
+                            ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t,
+                            ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+static NcclApi* nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    api.GetUniqueId = (decltype(api.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+    api.CommInitRank = (decltype(api.CommInitRank))dlsym(h, "ncclCommInitRank");
+    api.AllReduce = (decltype(api.AllReduce))dlsym(h, "ncclAllReduce");
+    api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
+    api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
+    api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
+    api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce &&
+             api.AllGather && api.CommDestroy && api.GetErrorString;
+  });
+  return &api;
+}
+
+#define NCCL_TRY(expr)                                                      \
+  do {                                                                      \
+    ncclResult_t r_ = (expr);                                               \
+    if (r_ != ncclSuccess)                                                  \
+      return l3g_fail(L3G_E_NCCL, "%s: %s", #expr, nccl()->GetErrorString(r_)); \
+  } while (0)
+
+extern "C" int l3g_nccl_unique_id(uint8_t out[128]) {
+  NcclApi* api = nccl();
+  if (!api->ok) return l3g_fail(L3G_E_NCCL, "libnccl.so.2 not found");
+  ncclUniqueId id;
+  NCCL_TRY(api->GetUniqueId(&id));
+  static_assert(sizeof(id) == 128, "ncclUniqueId size");
+  memcpy(out, &id, 128);
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// kernel set-up
+// ---------------------------------------------------------------------------
+static int sm_count(int dev) {
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 1;
+}
+
+static int setup_kernels() {
+  static int rc = -100;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const int big = 227 * 1024;
+    cudaError_t e = cudaSuccess;
+#define SETK(k) \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, big)
+    SETK((k_matvec<PRO_PREQ, EPI_STORE>));
+    SETK((k_matvec<PRO_QUANT, EPI_STORE>));
+    SETK((k_matvec<PRO_RMS, EPI_QKV>));
+    SETK((k_matvec<PRO_RMS, EPI_SWIGLU>));
+    SETK((k_matvec<PRO_RMS, EPI_LOGITS>));
+    SETK((k_attention<1, float>));
+    SETK((k_attention<2, float>));
+    SETK((k_attention<4, float>));
+    SETK((k_attention<8, float>));
+    SETK((k_attention<2, __half>));
+    SETK((k_attention<4, __half>));
+    SETK((k_attention<8, __half>));
+    SETK(k_topk_final);
+#undef SETK
+    rc = e == cudaSuccess ? 0 : (int)e;
+  });
+  if (rc) return l3g_fail(L3G_E_CUDA, "kernel attribute set-up: %s", cudaGetErrorString((cudaError_t)rc));
+  return L3G_OK;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                          size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ---------------------------------------------------------------------------
+// tiled Q8_0 matrices
+// ---------------------------------------------------------------------------
+struct DevMat {
+  Q8Tiles t{};
+  uint8_t* buf = nullptr;
+  size_t bytes = 0;
+  int nstages = 2;
+  int smem = 0;
+};
+
+// Row-group size: the one whose busiest CTA (one CTA per SM) streams the
+// fewest rows; ties go to the larger group (fewer barriers).  Column slices
+// keep a tile near TILE_TARGET int8 bytes.
+static Q8Tiles plan_tiles(int rows, int cols, int nsm) {
+  int best_wr = 8;
+  long long best = LLONG_MAX;
+  for (int wr : {8, 4, 2}) {
+    const int ng = (rows + wr - 1) / wr;
+    const int grid = std::min(ng, nsm);
+    const long long per = (ng + grid - 1) / grid;
+    const long long cost = per * wr;
+    if (best == LLONG_MAX || cost * 1000 < best * 995) {
+      best = cost;
+      best_wr = wr;
+    }
+  }
+  Q8Tiles t{};
+  t.rows = rows;
+  t.cols = cols;
+  t.wr = best_wr;
+  const int nb = cols / 32;
+  int nsl = std::max(1, (cols * best_wr + TILE_TARGET - 1) / TILE_TARGET);
+  while (nb % nsl) ++nsl;
+  t.nslices = nsl;
+  t.ck = cols / nsl;
+  t.tile_bytes = align_up(best_wr * t.ck + best_wr * (t.ck / 32) * 2, 16);
+  t.n_groups = (rows + best_wr - 1) / best_wr;
+  return t;
+}
+
+static void finish_plan(DevMat& m) {
+  m.nstages = std::max(2, std::min(MAX_STAGES, RING_BYTES / m.t.tile_bytes));
+  m.smem = mv_smem_bytes(m.t.cols, m.nstages, m.t.tile_bytes);
+}
+
+struct RowSrc {         // rows [row0, row0+n) of a host GGUF Q8_0 tensor
+  const uint8_t* host;
+  int row0, n;
+};
+
+// Uploads the needed source rows, repacks them into tiles on the device.
+static int upload_tiled(DevMat& out, const RowSrc* segs, int nseg,
+                        bool interleave2, int src_cols, int blk0, int cols,
+                        int nsm, size_t* dev_bytes) {
+  int rows = 0;
+  for (int i = 0; i < nseg; ++i) rows += segs[i].n;
+  out.t = plan_tiles(rows, cols, nsm);
+  finish_plan(out);
+  out.bytes = (size_t)out.t.n_groups * out.t.nslices * out.t.tile_bytes;
+  CUDA_TRY(cudaMalloc(&out.buf, out.bytes));
+  out.t.data = out.buf;
+  *dev_bytes += out.bytes;
+  const size_t row_bytes = (size_t)(src_cols / 32) * 34;
+  RepackArgs ra{};
+  std::vector<uint8_t*> staging(nseg, nullptr);
+  for (int i = 0; i < nseg; ++i) {
+    const size_t nbytes = row_bytes * segs[i].n;
+    CUDA_TRY(cudaMalloc(&staging[i], nbytes ? nbytes : 16));
+    CUDA_TRY(cudaMemcpy(staging[i], segs[i].host + row_bytes * segs[i].row0,
+                        nbytes, cudaMemcpyHostToDevice));
+    ra.src[i] = staging[i];
+    ra.src_row0[i] = 0;
+    ra.seg_rows[i] = segs[i].n;
+  }
+  ra.nseg = nseg;
+  ra.interleave2 = interleave2 ? 1 : 0;
+  ra.src_blocks = src_cols / 32;
+  ra.blk0 = blk0;
+  ra.dst = out.t;
+  ra.out = out.buf;
+  k_repack<<<2048, 256>>>(ra);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  for (auto* p : staging) cudaFree(p);
+  if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "repack: %s", cudaGetErrorString(e));
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+struct LayerW {
+  DevMat qkv, wo, upgate, down;
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+};
+
+struct l3g_model {
+  l3g_hparams hp{};
+  int world = 1, rank = 0, device = 0, kv_f16 = 0, nsm = 1;
+  int hd = 0, hq_l = 0, hkv_l = 0, group = 1, ff_l = 0, v_l = 0, v_off = 0;
+  int rope_half = 0;
+  std::vector<double> inv_freq;
+  std::vector<LayerW> layers;
+  DevMat logits;
+  float* out_norm = nullptr;
+  uint8_t* emb = nullptr;  // raw GGUF Q8_0 token_embd (all rows)
+  ncclComm_t comm = nullptr;
+  size_t dev_bytes = 0;
+};
+
+static const l3g_tensor* find_tensor(const l3g_tensor* ts, int n, const char* name) {
+  for (int i = 0; i < n; ++i)
+    if (ts[i].name && strcmp(ts[i].name, name) == 0) return &ts[i];
+  return nullptr;
+}
+
+static int check_matrix(const l3g_tensor* t, const char* name, int cols, int rows) {
+  if (!t) return l3g_fail(L3G_E_FORMAT, "missing tensor \"%s\"", name);
+  if (t->type != L3G_TYPE_Q8_0)
+    return l3g_fail(L3G_E_INVALID, "tensor \"%s\" has type %u, want Q8_0 (8)", name, t->type);
+  if (t->n_dims != 2 || (int64_t)t->dims[0] != cols || (int64_t)t->dims[1] != rows)
+    return l3g_fail(L3G_E_INVALID, "tensor \"%s\" dims [%llu %llu], want [%d %d]", name,
+                    (unsigned long long)t->dims[0], (unsigned long long)t->dims[1], cols, rows);
+  if (!t->data) return l3g_fail(L3G_E_INVALID, "tensor \"%s\" has no data", name);
+  const uint64_t need = (uint64_t)rows * (cols / 32) * 34;
+  if (t->nbytes && t->nbytes < need)
+    return l3g_fail(L3G_E_INVALID, "tensor \"%s\" truncated", name);
+  return L3G_OK;
+}
+
+// norm vectors: readVectorAnyToF32 (tensor_read.go:43-52), F32 or F16
+static int upload_vector(const l3g_tensor* t, const char* name, int n, float** out,
+                         size_t* dev_bytes) {
+  if (!t) return l3g_fail(L3G_E_FORMAT, "missing tensor \"%s\"", name);
+  std::vector<float> v(n);
+  if (t->type == L3G_TYPE_F32) {
+    if (t->nbytes && t->nbytes < (uint64_t)n * 4)
+      return l3g_fail(L3G_E_INVALID, "tensor \"%s\" truncated", name);
+    memcpy(v.data(), t->data, (size_t)n * 4);
+  } else if (t->type == L3G_TYPE_F16) {
+    if (t->nbytes && t->nbytes < (uint64_t)n * 2)
+      return l3g_fail(L3G_E_INVALID, "tensor \"%s\" truncated", name);
+    const uint16_t* h = static_cast<const uint16_t*>(t->data);
+    for (int i = 0; i < n; ++i) v[i] = l3g_f16_to_f32(h[i]);
+  } else {
+    return l3g_fail(L3G_E_INVALID, "unsupported vector type %u for \"%s\"", t->type, name);
+  }
+  CUDA_TRY(cudaMalloc(out, (size_t)n * 4));
+  CUDA_TRY(cudaMemcpy(*out, v.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+  *dev_bytes += (size_t)n * 4;
+  return L3G_OK;
+}
+
+static void free_mat(DevMat& m) {
+  if (m.buf) cudaFree(m.buf);
+  m.buf = nullptr;
+}
+
+extern "C" void l3g_model_free(l3g_model* m) {
+  if (!m) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(m->device);
+  for (auto& L : m->layers) {
+    free_mat(L.qkv);
+    free_mat(L.wo);
+    free_mat(L.upgate);
+    free_mat(L.down);
+    if (L.attn_norm) cudaFree(L.attn_norm);
+    if (L.ffn_norm) cudaFree(L.ffn_norm);
+  }
+  free_mat(m->logits);
+  if (m->out_norm) cudaFree(m->out_norm);
+  if (m->emb) cudaFree(m->emb);
+  if (m->comm) nccl()->CommDestroy(m->comm);
+  cudaSetDevice(prev);
+  delete m;
+}
+
+static int validate_hparams(const l3g_hparams& hp, int world) {
+  if (hp.vocab_size <= 0 || hp.n_layers <= 0 || hp.n_emb <= 0 || hp.n_heads <= 0 ||
+      hp.n_ff <= 0)
+    return l3g_fail(L3G_E_FORMAT, "missing required llama.* hyperparams in gguf");
+  if (hp.n_emb % hp.n_heads)
+    return l3g_fail(L3G_E_INVALID, "n_emb %d not divisible by n_heads %d", hp.n_emb, hp.n_heads);
+  const int hd = hp.n_emb / hp.n_heads;
+  if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
+    return l3g_fail(L3G_E_INVALID, "head_dim %d unsupported (32, 64, 128 or 256)", hd);
+  if (hp.n_heads_kv <= 0 || hp.n_heads % hp.n_heads_kv)
+    return l3g_fail(L3G_E_INVALID, "n_heads %d not a multiple of n_heads_kv %d", hp.n_heads,
+                    hp.n_heads_kv);
+  if (hp.n_heads / hp.n_heads_kv > MAXG)
+    return l3g_fail(L3G_E_INVALID, "GQA group %d above %d", hp.n_heads / hp.n_heads_kv, MAXG);
+  if (hp.n_emb % 32 || hp.n_ff % 32)
+    return l3g_fail(L3G_E_INVALID, "n_emb and n_ff must be multiples of 32");
+  if (hp.rope_dim <= 0 || hp.rope_dim > hd || hp.rope_dim % 2)
+    return l3g_fail(L3G_E_INVALID, "rope_dim %d must be even and <= head_dim %d", hp.rope_dim, hd);
+  if (hp.ctx_len <= 0) return l3g_fail(L3G_E_INVALID, "ctx_len %d", hp.ctx_len);
+  if (world < 1) return l3g_fail(L3G_E_INVALID, "world_size %d", world);
+  if (hp.n_heads % world || hp.n_heads_kv % world)
+    return l3g_fail(L3G_E_INVALID, "heads %d/%d not divisible by %d ranks", hp.n_heads,
+                    hp.n_heads_kv, world);
+  if ((hp.n_heads / world * hd) % 32)
+    return l3g_fail(L3G_E_INVALID, "per-rank attention width not a multiple of 32");
+  if (hp.n_ff % (32 * world))
+    return l3g_fail(L3G_E_INVALID, "n_ff %d not divisible into Q8_0 blocks over %d ranks",
+                    hp.n_ff, world);
+  return L3G_OK;
+}
+
+extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, int32_t nt,
+                              const l3g_options* opt_in, l3g_model** out) {
+  if (!hp_in || !ts || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  *out = nullptr;
+  l3g_options opt;
+  if (opt_in)
+    opt = *opt_in;
+  else
+    l3g_options_default(&opt);
+  l3g_hparams hp = *hp_in;
+  if (hp.n_heads_kv == 0) hp.n_heads_kv = hp.n_heads;          // model.go:212-214
+  if (hp.rope_dim == 0 && hp.n_heads) hp.rope_dim = hp.n_emb / hp.n_heads;  // :215-217
+  int rc = validate_hparams(hp, opt.world_size);
+  if (rc) return rc;
+  if (opt.rank < 0 || opt.rank >= opt.world_size)
+    return l3g_fail(L3G_E_INVALID, "rank %d outside world %d", opt.rank, opt.world_size);
+  if (opt.kv_dtype != L3G_KV_F32 && opt.kv_dtype != L3G_KV_F16)
+    return l3g_fail(L3G_E_INVALID, "kv_dtype %d", opt.kv_dtype);
+
+  int dev = opt.device;
+  if (dev < 0) CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaSetDevice(dev));
+  if ((rc = setup_kernels())) return rc;
+
+  auto* m = new l3g_model();
+  m->hp = hp;
+  m->world = opt.world_size;
+  m->rank = opt.rank;
+  m->device = dev;
+  m->kv_f16 = opt.kv_dtype == L3G_KV_F16;
+  m->nsm = sm_count(dev);
+  m->hd = hp.n_emb / hp.n_heads;
+  m->hq_l = hp.n_heads / m->world;
+  m->hkv_l = hp.n_heads_kv / m->world;
+  m->group = hp.n_heads / hp.n_heads_kv;
+  m->ff_l = hp.n_ff / m->world;
+  m->v_l = (hp.vocab_size + m->world - 1) / m->world;
+  m->v_off = m->rank * m->v_l;
+  m->rope_half = hp.rope_dim / 2;
+  auto bail = [&](int code) {
+    l3g_model_free(m);
+    return code;
+  };
+
+  // RoPE inverse frequencies, NewRopeCache rope.go:20-25, divided by the
+  // optional llama3 factors
+  m->inv_freq.resize(m->rope_half);
+  const l3g_tensor* rf = find_tensor(ts, nt, "rope_freqs.weight");
+  if (rf && (rf->type != L3G_TYPE_F32 || rf->dims[0] < (uint64_t)m->rope_half))
+    return bail(l3g_fail(L3G_E_INVALID, "rope_freqs.weight must be F32 [%d]", m->rope_half));
+  for (int i = 0; i < m->rope_half; ++i) {
+    const double e = (double)(2 * i) / (double)hp.rope_dim;
+    m->inv_freq[i] = 1.0 / pow((double)hp.rope_base, e);
+    if (rf) m->inv_freq[i] /= (double)static_cast<const float*>(rf->data)[i];
+  }
+
+  const int ne = hp.n_emb, hd = m->hd;
+  char name[96];
+  // embedding (all rows, raw, for the lookup) and output projection shard
+  const l3g_tensor* emb = find_tensor(ts, nt, "token_embd.weight");
+  if ((rc = check_matrix(emb, "token_embd.weight", ne, hp.vocab_size))) return bail(rc);
+  const size_t emb_bytes = (size_t)hp.vocab_size * (ne / 32) * 34;
+  if (cudaMalloc(&m->emb, emb_bytes) != cudaSuccess ||
+      cudaMemcpy(m->emb, emb->data, emb_bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(l3g_fail(L3G_E_CUDA, "embedding upload failed"));
+  m->dev_bytes += emb_bytes;
+  const l3g_tensor* outp = find_tensor(ts, nt, "output.weight");
+  if (!outp) outp = emb;  // tied, model.go:91-94
+  else if ((rc = check_matrix(outp, "output.weight", ne, hp.vocab_size))) return bail(rc);
+  {
+    const int v1 = std::min(hp.vocab_size, m->v_off + m->v_l);
+    RowSrc seg{static_cast<const uint8_t*>(outp->data), m->v_off, v1 - m->v_off};
+    if ((rc = upload_tiled(m->logits, &seg, 1, false, ne, 0, ne, m->nsm, &m->dev_bytes)))
+      return bail(rc);
+  }
+  if ((rc = upload_vector(find_tensor(ts, nt, "output_norm.weight"), "output_norm.weight", ne,
+                          &m->out_norm, &m->dev_bytes)))
+    return bail(rc);
+
+  m->layers.resize(hp.n_layers);
+  const int kvdim = hp.n_heads_kv * hd;
+  for (int l = 0; l < hp.n_layers; ++l) {
+    LayerW& L = m->layers[l];
+    auto T = [&](const char* suffix) {
+      snprintf(name, sizeof name, "blk.%d.%s", l, suffix);
+      return find_tensor(ts, nt, name);
+    };
+    auto chk = [&](const char* suffix, int cols, int rows) {
+      snprintf(name, sizeof name, "blk.%d.%s", l, suffix);
+      return check_matrix(find_tensor(ts, nt, name), name, cols, rows);
+    };
+    if ((rc = chk("attn_q.weight", ne, ne)) || (rc = chk("attn_k.weight", ne, kvdim)) ||
+        (rc = chk("attn_v.weight", ne, kvdim)) || (rc = chk("attn_output.weight", ne, ne)) ||
+        (rc = chk("ffn_up.weight", ne, hp.n_ff)) || (rc = chk("ffn_gate.weight", ne, hp.n_ff)) ||
+        (rc = chk("ffn_down.weight", hp.n_ff, ne)))
+      return bail(rc);
+    const auto* wq = static_cast<const uint8_t*>(T("attn_q.weight")->data);
+    const auto* wk = static_cast<const uint8_t*>(T("attn_k.weight")->data);
+    const auto* wv = static_cast<const uint8_t*>(T("attn_v.weight")->data);
+    const auto* wo = static_cast<const uint8_t*>(T("attn_output.weight")->data);
+    const auto* wu = static_cast<const uint8_t*>(T("ffn_up.weight")->data);
+    const auto* wg = static_cast<const uint8_t*>(T("ffn_gate.weight")->data);
+    const auto* wd = static_cast<const uint8_t*>(T("ffn_down.weight")->data);
+    // this rank's heads: q rows, k rows, v rows concatenated
+    RowSrc qkv[3] = {{wq, m->rank * m->hq_l * hd, m->hq_l * hd},
+                     {wk, m->rank * m->hkv_l * hd, m->hkv_l * hd},
+                     {wv, m->rank * m->hkv_l * hd, m->hkv_l * hd}};
+    if ((rc = upload_tiled(L.qkv, qkv, 3, false, ne, 0, ne, m->nsm, &m->dev_bytes)))
+      return bail(rc);
+    // Wo: all rows, this rank's head columns
+    const int ac = m->hq_l * hd;
+    RowSrc wos{wo, 0, ne};
+    if ((rc = upload_tiled(L.wo, &wos, 1, false, ne, m->rank * ac / 32, ac, m->nsm,
+                           &m->dev_bytes)))
+      return bail(rc);
+    // up/gate interleaved (up_i, gate_i) for this rank's FFN rows
+    RowSrc ug[2] = {{wu, m->rank * m->ff_l, m->ff_l}, {wg, m->rank * m->ff_l, m->ff_l}};
+    if ((rc = upload_tiled(L.upgate, ug, 2, true, ne, 0, ne, m->nsm, &m->dev_bytes)))
+      return bail(rc);
+    // down: all rows, this rank's FFN columns
+    RowSrc ds{wd, 0, ne};
+    if ((rc = upload_tiled(L.down, &ds, 1, false, hp.n_ff, m->rank * m->ff_l / 32, m->ff_l,
+                           m->nsm, &m->dev_bytes)))
+      return bail(rc);
+    snprintf(name, sizeof name, "blk.%d.attn_norm.weight", l);
+    if ((rc = upload_vector(find_tensor(ts, nt, name), name, ne, &L.attn_norm, &m->dev_bytes)))
+      return bail(rc);
+    snprintf(name, sizeof name, "blk.%d.ffn_norm.weight", l);
+    if ((rc = upload_vector(find_tensor(ts, nt, name), name, ne, &L.ffn_norm, &m->dev_bytes)))
+      return bail(rc);
+  }
+
+  if (m->world > 1) {
+    NcclApi* api = nccl();
+    if (!api->ok) return bail(l3g_fail(L3G_E_NCCL, "libnccl.so.2 not found"));
+    ncclUniqueId id;
+    memcpy(&id, opt.nccl_id, sizeof id);
+    ncclResult_t r = api->CommInitRank(&m->comm, m->world, id, m->rank);
+    if (r != ncclSuccess)
+      return bail(l3g_fail(L3G_E_NCCL, "ncclCommInitRank: %s", api->GetErrorString(r)));
+  }
+  *out = m;
+  return L3G_OK;
+}
+
+extern "C" int l3g_model_hparams(const l3g_model* m, l3g_hparams* out) {
+  if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  *out = m->hp;
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// state
+// ---------------------------------------------------------------------------
+struct l3g_state {
+  l3g_model* m = nullptr;
+  int ctx = 0, pos = 0;
+  void* kc = nullptr;
+  void* vc = nullptr;
+  size_t layer_elems = 0;  // per layer: local kv heads * ctx * hd
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  uint64_t serial = 0;
+};
+
+static uint64_t next_serial() {
+  static std::mutex mu;
+  static uint64_t s = 0;
+  std::lock_guard<std::mutex> g(mu);
+  return ++s;
+}
+
+extern "C" void l3g_state_free(l3g_state* s) {
+  if (!s) return;
+  cudaSetDevice(s->m->device);
+  if (s->kc) cudaFree(s->kc);
+  if (s->vc) cudaFree(s->vc);
+  if (s->rope_cos) cudaFree(s->rope_cos);
+  if (s->rope_sin) cudaFree(s->rope_sin);
+  delete s;
+}
+
+extern "C" int l3g_state_new(l3g_model* m, int32_t ctx, l3g_state** out) {
+  if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  *out = nullptr;
+  if (ctx <= 0) ctx = m->hp.ctx_len;  // state.go:52-57
+  if (ctx > m->hp.ctx_len) ctx = m->hp.ctx_len;
+  CUDA_TRY(cudaSetDevice(m->device));
+  auto* s = new l3g_state();
+  s->m = m;
+  s->ctx = ctx;
+  s->serial = next_serial();
+  s->layer_elems = (size_t)m->hkv_l * ctx * m->hd;
+  const size_t es = m->kv_f16 ? 2 : 4;
+  const size_t kvb = s->layer_elems * m->hp.n_layers * es;
+  cudaError_t e = cudaMalloc(&s->kc, kvb);
+  if (e == cudaSuccess) e = cudaMalloc(&s->vc, kvb);
+  if (e == cudaSuccess) e = cudaMemset(s->kc, 0, kvb);
+  if (e == cudaSuccess) e = cudaMemset(s->vc, 0, kvb);
+  // RoPE tables, NewRopeCache rope.go:27-34 (f64 angles, f32 tables)
+  const int half = m->rope_half;
+  std::vector<float> c((size_t)ctx * half), sn((size_t)ctx * half);
+  for (int p = 0; p < ctx; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double ang = (double)p * m->inv_freq[i];
+      c[(size_t)p * half + i] = (float)cos(ang);
+      sn[(size_t)p * half + i] = (float)sin(ang);
+    }
+  const size_t tb = std::max<size_t>(4, c.size() * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&s->rope_cos, tb);
+  if (e == cudaSuccess) e = cudaMalloc(&s->rope_sin, tb);
+  if (e == cudaSuccess && !c.empty())
+    e = cudaMemcpy(s->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && !sn.empty())
+    e = cudaMemcpy(s->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    l3g_state_free(s);
+    return l3g_fail(L3G_E_CUDA, "state allocation: %s", cudaGetErrorString(e));
+  }
+  *out = s;
+  return L3G_OK;
+}
+
+extern "C" int l3g_state_pos(const l3g_state* s, int32_t* pos) {
+  if (!s || !pos) return l3g_fail(L3G_E_INVALID, "null argument");
+  *pos = s->pos;
+  return L3G_OK;
+}
+extern "C" int l3g_state_ctx_len(const l3g_state* s, int32_t* ctx) {
+  if (!s || !ctx) return l3g_fail(L3G_E_INVALID, "null argument");
+  *ctx = s->ctx;
+  return L3G_OK;
+}
+extern "C" int l3g_state_set_pos(l3g_state* s, int32_t pos) {
+  if (!s) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (pos < 0 || pos > s->ctx) return l3g_fail(L3G_E_INVALID, "pos %d outside [0, %d]", pos, s->ctx);
+  s->pos = pos;
+  return L3G_OK;
+}
+
+extern "C" int l3g_state_read_kv(const l3g_state* s, int32_t layer, int32_t pos0, int32_t npos,
+                                 float* k_out, float* v_out) {
+  if (!s || !k_out || !v_out) return l3g_fail(L3G_E_INVALID, "null argument");
+  const l3g_model* m = s->m;
+  if (layer < 0 || layer >= m->hp.n_layers || pos0 < 0 || npos < 0 || pos0 + npos > s->ctx)
+    return l3g_fail(L3G_E_INVALID, "kv range out of bounds");
+  CUDA_TRY(cudaSetDevice(m->device));
+  const int hd = m->hd, nh = m->hkv_l;
+  const size_t es = m->kv_f16 ? 2 : 4;
+  std::vector<uint8_t> kb((size_t)npos * hd * es), vb(kb.size());
+  for (int h = 0; h < nh; ++h) {
+    const size_t off = ((size_t)layer * s->layer_elems + ((size_t)h * s->ctx + pos0) * hd) * es;
+    CUDA_TRY(cudaMemcpy(kb.data(), static_cast<uint8_t*>(s->kc) + off, kb.size(),
+                        cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(vb.data(), static_cast<uint8_t*>(s->vc) + off, vb.size(),
+                        cudaMemcpyDeviceToHost));
+    for (int p = 0; p < npos; ++p)
+      for (int d = 0; d < hd; ++d) {
+        const size_t src = (size_t)p * hd + d, dst = ((size_t)p * nh + h) * hd + d;
+        if (es == 4) {
+          k_out[dst] = reinterpret_cast<float*>(kb.data())[src];
+          v_out[dst] = reinterpret_cast<float*>(vb.data())[src];
+        } else {
+          k_out[dst] = l3g_f16_to_f32(reinterpret_cast<uint16_t*>(kb.data())[src]);
+          v_out[dst] = l3g_f16_to_f32(reinterpret_cast<uint16_t*>(vb.data())[src]);
+        }
+      }
+  }
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// workspace and the step graphs
+// ---------------------------------------------------------------------------
+// V_GREEDY_DEV: the token and position come from the previous replay's
+// argmax on the device (k_advance), no host copies inside the graph.
+enum Variant { V_PREFILL = 0, V_ARGMAX = 1, V_LOGITS = 2, V_TOPK = 3, V_GREEDY_DEV = 4 };
+constexpr int MAX_TOPK = 64;
+
+struct StepGraph {
+  int variant, k;
+  uint64_t state_serial;
+  cudaGraphExec_t exec;
+};
+
+struct l3g_workspace {
+  l3g_model* m = nullptr;
+  int ctx = 0, topk = 40;
+  cudaStream_t stream = nullptr;
+  int* d_io = nullptr;
+  int* h_io = nullptr;       // pinned {token, pos, 0, 0}
+  Result* d_res = nullptr;
+  Result* h_res = nullptr;   // pinned
+  Result* d_gather = nullptr;  // [world] per-rank argmax results
+  float* x[2] = {nullptr, nullptr};
+  float* y = nullptr;
+  float* q = nullptr;
+  float* attn = nullptr;
+  float* act = nullptr;
+  float* logits = nullptr;     // [world * v_l]: local shard first, gathered when TP
+  float* logits_full = nullptr;
+  float* h_logits = nullptr;   // pinned [vocab]
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  unsigned* att_cnt = nullptr;
+  float* am_val = nullptr;
+  int* am_idx = nullptr;
+  unsigned* am_cnt = nullptr;
+  uint64_t* tk_part = nullptr;
+  int* d_tk_ids = nullptr;
+  float* d_tk_logits = nullptr;
+  int* h_tk_ids = nullptr;
+  float* h_tk_logits = nullptr;
+  int n_splits = 1, att_P = 16, att_ns = 4, att_stage = 0, att_smem = 0;
+  int tk_chunks = 0;
+  int* d_tokens = nullptr;     // [ctx] tokens of a device-fed greedy run
+  int kernels = 0;             // kernel launches counted during a capture
+  int kernels_greedy = 0;      // ... of the greedy variant
+  std::vector<StepGraph> graphs;
+  bool logits_valid = false;
+};
+
+static void ws_release(l3g_workspace* ws) {
+  for (auto& g : ws->graphs) cudaGraphExecDestroy(g.exec);
+  ws->graphs.clear();
+  void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
+                   ws->attn, ws->act, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
+                   ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
+                   ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens};
+  for (void* p : dptrs)
+    if (p) cudaFree(p);
+  void* hptrs[] = {ws->h_io, ws->h_res, ws->h_logits, ws->h_tk_ids, ws->h_tk_logits};
+  for (void* p : hptrs)
+    if (p) cudaFreeHost(p);
+  if (ws->stream) cudaStreamDestroy(ws->stream);
+}
+
+extern "C" void l3g_workspace_free(l3g_workspace* ws) {
+  if (!ws) return;
+  cudaSetDevice(ws->m->device);
+  ws_release(ws);
+  delete ws;
+}
+
+extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_workspace** out) {
+  if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  *out = nullptr;
+  if (ctx <= 0) ctx = m->hp.ctx_len;  // workspace.go:36-41
+  if (ctx > m->hp.ctx_len) ctx = m->hp.ctx_len;
+  if (topk <= 0) topk = 40;           // workspace.go:42-44
+  if (topk > MAX_TOPK) return l3g_fail(L3G_E_INVALID, "top_k %d above %d", topk, MAX_TOPK);
+  CUDA_TRY(cudaSetDevice(m->device));
+  auto* ws = new l3g_workspace();
+  ws->m = m;
+  ws->ctx = ctx;
+  ws->topk = topk;
+  const int ne = m->hp.n_emb, hd = m->hd;
+  const int G = m->group;
+  const size_t es = m->kv_f16 ? 2 : 4;
+  // attention geometry: splits fill the SMs; a stage is ~16 KB of K+V
+  ws->att_P = std::max(NW, (int)(16384 / (2 * hd * es)));
+  ws->att_stage = 2 * ws->att_P * hd * (int)es;
+  ws->att_ns = 4;
+  ws->n_splits = std::max(1, std::min(m->nsm / m->hkv_l, (ctx + ws->att_P - 1) / ws->att_P));
+  const int scratch = (NW * MAXG * 2 + NW * G * hd) * 4;
+  ws->att_smem = AT_HEAD + std::max(ws->att_ns * ws->att_stage, scratch);
+  const int vloc = m->v_l;
+  ws->tk_chunks = (m->v_l * m->world + TOPK_CHUNK - 1) / TOPK_CHUNK;
+  cudaError_t e = cudaStreamCreateWithFlags(&ws->stream, cudaStreamNonBlocking);
+#define DM(p, bytes) \
+  if (e == cudaSuccess) e = cudaMalloc(&(p), (bytes))
+#define HM(p, bytes) \
+  if (e == cudaSuccess) e = cudaMallocHost(&(p), (bytes))
+  DM(ws->d_io, 16);
+  HM(ws->h_io, 16);
+  DM(ws->d_res, sizeof(Result));
+  HM(ws->h_res, sizeof(Result));
+  DM(ws->d_gather, sizeof(Result) * m->world);
+  DM(ws->x[0], ne * 4);
+  DM(ws->x[1], ne * 4);
+  DM(ws->y, ne * 4);
+  DM(ws->q, (size_t)m->hq_l * hd * 4);
+  DM(ws->attn, (size_t)m->hq_l * hd * 4);
+  DM(ws->act, (size_t)m->ff_l * 4);
+  DM(ws->logits, (size_t)vloc * 4);
+  DM(ws->logits_full, (size_t)vloc * m->world * 4);
+  HM(ws->h_logits, (size_t)vloc * m->world * 4);
+  DM(ws->part_o, (size_t)m->hkv_l * ws->n_splits * G * hd * 4);
+  DM(ws->part_ml, (size_t)m->hkv_l * ws->n_splits * G * 2 * 4);
+  DM(ws->att_cnt, (size_t)m->hkv_l * 4);
+  DM(ws->am_val, (size_t)m->nsm * 4);
+  DM(ws->am_idx, (size_t)m->nsm * 4);
+  DM(ws->am_cnt, 4);
+  DM(ws->tk_part, (size_t)ws->tk_chunks * MAX_TOPK * 8);
+  DM(ws->d_tokens, (size_t)ctx * 4);
+  DM(ws->d_tk_ids, MAX_TOPK * 4);
+  DM(ws->d_tk_logits, MAX_TOPK * 4);
+  HM(ws->h_tk_ids, MAX_TOPK * 4);
+  HM(ws->h_tk_logits, MAX_TOPK * 4);
+#undef DM
+#undef HM
+  if (e == cudaSuccess) e = cudaMemset(ws->d_res, 0, sizeof(Result));
+  if (e == cudaSuccess) e = cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->am_cnt, 0, 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->x[0], 0, ne * 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->x[1], 0, ne * 4);
+  if (e == cudaSuccess) {
+    // logits shards beyond the vocabulary stay -inf
+    std::vector<float> ninf((size_t)vloc * m->world, -INFINITY);
+    e = cudaMemcpy(ws->logits, ninf.data(), (size_t)vloc * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(ws->logits_full, ninf.data(), ninf.size() * 4, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess) {
+    ws_release(ws);
+    delete ws;
+    return l3g_fail(L3G_E_CUDA, "workspace allocation: %s", cudaGetErrorString(e));
+  }
+  *out = ws;
+  return L3G_OK;
+}
+
+// grid / launch helpers -------------------------------------------------------
+static MatvecArgs mv_args(const DevMat& w) {
+  MatvecArgs a{};
+  a.w = w.t;
+  a.nstages = w.nstages;
+  a.row_lo = 0;
+  a.row_hi = w.t.rows;
+  return a;
+}
+
+template <int PRO, int EPI>
+static cudaError_t launch_mv(const DevMat& w, const MatvecArgs& a, int nsm, cudaStream_t st) {
+  const int gl = a.row_lo / w.t.wr;
+  const int ng = (a.row_hi + w.t.wr - 1) / w.t.wr - gl;
+  const int grid = std::max(1, std::min(ng, nsm));
+  return launch(k_matvec<PRO, EPI>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
+}
+
+static cudaError_t launch_attention(const l3g_workspace* ws, const AttnArgs& a, cudaStream_t st) {
+  const l3g_model* m = ws->m;
+  dim3 grid(m->hkv_l, ws->n_splits);
+  const int dpl = m->hd / 32;
+  const size_t smem = ws->att_smem;
+  if (m->kv_f16) {
+    if (dpl == 2) return launch(k_attention<2, __half>, grid, dim3(NTHREADS), smem, st, a);
+    if (dpl == 4) return launch(k_attention<4, __half>, grid, dim3(NTHREADS), smem, st, a);
+    if (dpl == 8) return launch(k_attention<8, __half>, grid, dim3(NTHREADS), smem, st, a);
+    return cudaErrorInvalidValue;
+  }
+  if (dpl == 1) return launch(k_attention<1, float>, grid, dim3(NTHREADS), smem, st, a);
+  if (dpl == 2) return launch(k_attention<2, float>, grid, dim3(NTHREADS), smem, st, a);
+  if (dpl == 4) return launch(k_attention<4, float>, grid, dim3(NTHREADS), smem, st, a);
+  return launch(k_attention<8, float>, grid, dim3(NTHREADS), smem, st, a);
+}
+
+// merges the per-rank argmax results gathered by NCCL (largest logit, lowest
+// id on ties; first error wins)
+__global__ void k_merge_argmax(const Result* g, int world, Result* out) {
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  Result best = g[0];
+  int err = g[0].err, where = g[0].where;
+  for (int r = 1; r < world; ++r) {
+    const Result c = g[r];
+    if (c.logit > best.logit || (c.logit == best.logit && c.token < best.token)) best = c;
+    if (!err && c.err) {
+      err = c.err;
+      where = c.where;
+    }
+  }
+  out->token = best.token;
+  out->logit = best.logit;
+  out->err = err;
+  out->where = where;
+}
+
+// Enqueues one decode step on ws->stream (captured into a graph).
+static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int k) {
+  l3g_model* m = ws->m;
+  const l3g_hparams& hp = m->hp;
+  cudaStream_t st = ws->stream;
+  const int ne = hp.n_emb, hd = m->hd;
+  const size_t es = m->kv_f16 ? 2 : 4;
+  ws->kernels = 0;
+#define KL(expr)  \
+  do {            \
+    CUDA_TRY(expr); \
+    ++ws->kernels; \
+  } while (0)
+  if (variant != V_GREEDY_DEV)
+    CUDA_TRY(cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, st));
+  KL(launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
+                  hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res));
+  for (int l = 0; l < hp.n_layers; ++l) {
+    const LayerW& L = m->layers[l];
+    uint8_t* kc = static_cast<uint8_t*>(s->kc) + (size_t)l * s->layer_elems * es;
+    uint8_t* vc = static_cast<uint8_t*>(s->vc) + (size_t)l * s->layer_elems * es;
+    {  // RMSNorm -> act-quant -> QKV -> RoPE -> KV append, infer.go:67-127
+      MatvecArgs a = mv_args(L.qkv);
+      a.x_in = ws->x[0];
+      a.y_in = l ? ws->y : nullptr;
+      a.norm_w = L.attn_norm;
+      a.x_out = ws->x[1];
+      a.eps = hp.rms_eps;
+      a.out = ws->q;
+      a.nq = m->hq_l * hd;
+      a.nkv = m->hkv_l * hd;
+      a.head_dim = hd;
+      a.rope_half = m->rope_half;
+      a.ctx = s->ctx;
+      a.kv_f16 = m->kv_f16;
+      a.rope_cos = s->rope_cos;
+      a.rope_sin = s->rope_sin;
+      a.io = ws->d_io;
+      a.kc = kc;
+      a.vc = vc;
+      a.res = ws->d_res;
+      KL((launch_mv<PRO_RMS, EPI_QKV>(L.qkv, a, m->nsm, st)));
+    }
+    {  // attention, infer.go:130-175
+      AttnArgs a{};
+      a.q = ws->q;
+      a.kc = kc;
+      a.vc = vc;
+      a.ctx = s->ctx;
+      a.hd = hd;
+      a.group = m->group;
+      a.n_splits = ws->n_splits;
+      a.P = ws->att_P;
+      a.nstages = ws->att_ns;
+      a.stage_bytes = ws->att_stage;
+      a.scale = (float)(1.0 / sqrt((double)hd));
+      a.io = ws->d_io;
+      a.part_o = ws->part_o;
+      a.part_ml = ws->part_ml;
+      a.counters = ws->att_cnt;
+      a.out = ws->attn;
+      a.res = ws->d_res;
+      KL(launch_attention(ws, a, st));
+    }
+    {  // act-quant -> Wo, infer.go:178-187 (residual add fused downstream)
+      MatvecArgs a = mv_args(L.wo);
+      a.x_in = ws->attn;
+      a.out = ws->y;
+      a.res = ws->d_res;
+      KL((launch_mv<PRO_QUANT, EPI_STORE>(L.wo, a, m->nsm, st)));
+    }
+    if (m->world > 1)
+      NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));
+    {  // residual -> RMSNorm -> act-quant -> up/gate -> SwiGLU, infer.go:189-230
+      MatvecArgs a = mv_args(L.upgate);
+      a.x_in = ws->x[1];
+      a.y_in = ws->y;
+      a.norm_w = L.ffn_norm;
+      a.x_out = ws->x[0];
+      a.eps = hp.rms_eps;
+      a.out = ws->act;
+      a.res = ws->d_res;
+      KL((launch_mv<PRO_RMS, EPI_SWIGLU>(L.upgate, a, m->nsm, st)));
+    }
+    {  // act-quant -> down, infer.go:233-242
+      MatvecArgs a = mv_args(L.down);
+      a.x_in = ws->act;
+      a.out = ws->y;
+      a.res = ws->d_res;
+      KL((launch_mv<PRO_QUANT, EPI_STORE>(L.down, a, m->nsm, st)));
+    }
+    if (m->world > 1)
+      NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));
+  }
+  if (variant != V_PREFILL) {
+    // residual -> final RMSNorm -> act-quant -> logits + argmax, infer.go:250-262
+    MatvecArgs a = mv_args(m->logits);
+    a.x_in = ws->x[0];
+    a.y_in = ws->y;
+    a.norm_w = m->out_norm;
+    a.x_out = ws->x[1];
+    a.eps = hp.rms_eps;
+    a.out = ws->logits;
+    a.row_offset = m->v_off;
+    a.am_val = ws->am_val;
+    a.am_idx = ws->am_idx;
+    a.am_counter = ws->am_cnt;
+    a.res = ws->d_res;
+    KL((launch_mv<PRO_RMS, EPI_LOGITS>(m->logits, a, m->nsm, st)));
+    const float* full = ws->logits;
+    if (m->world > 1) {
+      NCCL_TRY(nccl()->AllGather(ws->d_res, ws->d_gather, sizeof(Result) / 4, ncclInt32, m->comm, st));
+      KL(launch(k_merge_argmax, dim3(1), dim3(32), 0, st, (const Result*)ws->d_gather,
+                      m->world, ws->d_res));
+      if (variant == V_LOGITS || variant == V_TOPK) {
+        NCCL_TRY(nccl()->AllGather(ws->logits, ws->logits_full, m->v_l, ncclFloat, m->comm, st));
+        full = ws->logits_full;
+      }
+    }
+    if (variant == V_LOGITS)
+      CUDA_TRY(cudaMemcpyAsync(ws->h_logits, full, (size_t)hp.vocab_size * 4,
+                               cudaMemcpyDeviceToHost, st));
+    if (variant == V_TOPK) {
+      const int nv = hp.vocab_size;
+      const int chunks = (nv + TOPK_CHUNK - 1) / TOPK_CHUNK;
+      KL(launch(k_topk_partial, dim3(chunks), dim3(512), 0, st, full, nv, k, 0, ws->tk_part));
+      int cap = 1;
+      while (cap < chunks * k) cap <<= 1;
+      KL(launch(k_topk_final, dim3(1), dim3(1024), (size_t)cap * 8, st,
+                      (const uint64_t*)ws->tk_part, chunks * k, cap, k, ws->d_tk_ids,
+                      ws->d_tk_logits));
+      CUDA_TRY(cudaMemcpyAsync(ws->h_tk_ids, ws->d_tk_ids, k * 4, cudaMemcpyDeviceToHost, st));
+      CUDA_TRY(cudaMemcpyAsync(ws->h_tk_logits, ws->d_tk_logits, k * 4, cudaMemcpyDeviceToHost, st));
+    }
+  }
+  if (variant == V_GREEDY_DEV)
+    KL(launch(k_advance, dim3(1), dim3(32), 0, st, ws->d_io, (const Result*)ws->d_res,
+              ws->d_tokens));
+  else
+    CUDA_TRY(cudaMemcpyAsync(ws->h_res, ws->d_res, sizeof(Result), cudaMemcpyDeviceToHost, st));
+#undef KL
+  return L3G_OK;
+}
+
+static int get_graph(l3g_workspace* ws, const l3g_state* s, int variant, int k,
+                     cudaGraphExec_t* out) {
+  for (auto& g : ws->graphs)
+    if (g.variant == variant && g.k == k && g.state_serial == s->serial) {
+      *out = g.exec;
+      return L3G_OK;
+    }
+  // a workspace serves one state at a time: drop graphs of other states
+  for (auto it = ws->graphs.begin(); it != ws->graphs.end();) {
+    if (it->state_serial != s->serial) {
+      cudaGraphExecDestroy(it->exec);
+      it = ws->graphs.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  CUDA_TRY(cudaStreamBeginCapture(ws->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(ws, s, variant, k);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ws->stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "graph capture: %s", cudaGetErrorString(e));
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  ws->graphs.push_back({variant, k, s->serial, exec});
+  if (variant == V_GREEDY_DEV) ws->kernels_greedy = ws->kernels;
+  *out = exec;
+  return L3G_OK;
+}
+
+// One step: the checks of ForwardIntoWorkspace (infer.go:22-33,514-516),
+// the graph replay, the device error word, position advance (infer.go:265).
+static int run_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token, int variant,
+                    int k) {
+  if (!m || !s) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (!ws) return l3g_fail(L3G_E_INVALID, "workspace is nil");
+  if (s->m != m || ws->m != m)
+    return l3g_fail(L3G_E_INVALID, "state or workspace belongs to another model");
+  if (s->pos >= s->ctx) return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+  if (ws->ctx < s->ctx)
+    return l3g_fail(L3G_E_INVALID, "workspace ctxLen=%d < state ctxLen=%d", ws->ctx, s->ctx);
+  if (token < 0 || token >= m->hp.vocab_size)
+    return l3g_fail(L3G_E_TOKEN, "token out of range: %d", token);
+  CUDA_TRY(cudaSetDevice(m->device));
+  cudaGraphExec_t exec;
+  int rc = get_graph(ws, s, variant, k, &exec);
+  if (rc) return rc;
+  ws->h_io[0] = token;
+  ws->h_io[1] = s->pos;
+  CUDA_TRY(cudaGraphLaunch(exec, ws->stream));
+  CUDA_TRY(cudaStreamSynchronize(ws->stream));
+  if (ws->h_res->err) {
+    const int code = ws->h_res->err, where = ws->h_res->where;
+    cudaMemset(ws->d_res, 0, sizeof(Result));
+    // an aborted kernel may have left its last-CTA counters mid-count
+    cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 4);
+    cudaMemset(ws->am_cnt, 0, 4);
+    ws->logits_valid = false;
+    return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d (%s)", code, where,
+                    code == ERR_TIMEOUT ? "bounded wait ran out" : "bad input");
+  }
+  ws->logits_valid = variant != V_PREFILL;
+  s->pos++;
+  return L3G_OK;
+}
+
+extern "C" int l3g_forward(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token,
+                           float* logits_out) {
+  const int rc = run_step(m, s, ws, token, logits_out ? V_LOGITS : V_PREFILL, 0);
+  if (rc == L3G_OK && logits_out)
+    memcpy(logits_out, ws->h_logits, (size_t)m->hp.vocab_size * 4);
+  return rc;
+}
+
+extern "C" int l3g_forward_argmax(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token,
+                                  int32_t* next, float* logit) {
+  const int rc = run_step(m, s, ws, token, V_ARGMAX, 0);
+  if (rc == L3G_OK) {
+    if (next) *next = ws->h_res->token;
+    if (logit) *logit = ws->h_res->logit;
+  }
+  return rc;
+}
+
+extern "C" int l3g_forward_topk(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token,
+                                int32_t top_k, l3g_topk_item* items, int32_t* n_items) {
+  if (top_k <= 0) top_k = 40;  // infer.go:279-281
+  if (top_k > MAX_TOPK) return l3g_fail(L3G_E_INVALID, "top_k %d above %d", top_k, MAX_TOPK);
+  if (m && top_k > m->hp.vocab_size) top_k = m->hp.vocab_size;
+  if (!items) return l3g_fail(L3G_E_INVALID, "null argument");
+  const int rc = run_step(m, s, ws, token, V_TOPK, top_k);
+  if (rc == L3G_OK) {
+    for (int i = 0; i < top_k; ++i) {
+      items[i].id = ws->h_tk_ids[i];
+      items[i].logit = ws->h_tk_logits[i];
+    }
+    if (n_items) *n_items = top_k;
+  }
+  return rc;
+}
+
+extern "C" int l3g_prefill(l3g_model* m, l3g_state* s, l3g_workspace* ws, const int32_t* tokens,
+                           int32_t n) {
+  if (n > 0 && !tokens) return l3g_fail(L3G_E_INVALID, "null argument");
+  for (int i = 0; i < n; ++i) {
+    const int rc = run_step(m, s, ws, tokens[i], V_PREFILL, 0);
+    if (rc) return rc;
+  }
+  return L3G_OK;
+}
+
+extern "C" int l3g_decode_greedy(l3g_model* m, l3g_state* s, l3g_workspace* ws,
+                                 int32_t first_token, int32_t n, int32_t* out_tokens,
+                                 float* device_ms) {
+  if (!m || !s || !out_tokens) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (!ws) return l3g_fail(L3G_E_INVALID, "workspace is nil");
+  if (s->m != m || ws->m != m)
+    return l3g_fail(L3G_E_INVALID, "state or workspace belongs to another model");
+  if (n <= 0) return L3G_OK;
+  if (ws->ctx < s->ctx)
+    return l3g_fail(L3G_E_INVALID, "workspace ctxLen=%d < state ctxLen=%d", ws->ctx, s->ctx);
+  if (s->pos + n > s->ctx) return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+  if (first_token < 0 || first_token >= m->hp.vocab_size)
+    return l3g_fail(L3G_E_TOKEN, "token out of range: %d", first_token);
+  CUDA_TRY(cudaSetDevice(m->device));
+  cudaGraphExec_t exec;
+  int rc = get_graph(ws, s, V_GREEDY_DEV, 0, &exec);
+  if (rc) return rc;
+  cudaEvent_t e0, e1;
+  CUDA_TRY(cudaEventCreate(&e0));
+  CUDA_TRY(cudaEventCreate(&e1));
+  ws->h_io[0] = first_token;
+  ws->h_io[1] = s->pos;
+  ws->h_io[2] = 0;
+  ws->h_io[3] = 0;
+  cudaError_t e = cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, ws->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(e0, ws->stream);
+  for (int i = 0; i < n && e == cudaSuccess; ++i) e = cudaGraphLaunch(exec, ws->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(e1, ws->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(ws->h_res, ws->d_res, sizeof(Result), cudaMemcpyDeviceToHost, ws->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ws->stream);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(out_tokens, ws->d_tokens, (size_t)n * 4, cudaMemcpyDeviceToHost);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "greedy decode: %s", cudaGetErrorString(e));
+  if (ws->h_res->err) {
+    const int code = ws->h_res->err, where = ws->h_res->where;
+    cudaMemset(ws->d_res, 0, sizeof(Result));
+    return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d", code, where);
+  }
+  if (device_ms) *device_ms = ms;
+  ws->logits_valid = true;
+  s->pos += n;
+  return L3G_OK;
+}
+
+extern "C" int l3g_workspace_kernels_per_step(l3g_workspace* ws, int32_t* n) {
+  if (!ws || !n) return l3g_fail(L3G_E_INVALID, "null argument");
+  *n = ws->kernels_greedy;
+  return L3G_OK;
+}
+
+extern "C" int l3g_workspace_read(const l3g_workspace* ws, int32_t which, float* out, int32_t n) {
+  if (!ws || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  const l3g_model* m = ws->m;
+  const float* src = nullptr;
+  int cnt = 0;
+  switch (which) {
+    case L3G_BUF_HIDDEN: src = ws->x[1]; cnt = m->hp.n_emb; break;
+    case L3G_BUF_Q: src = ws->q; cnt = m->hq_l * m->hd; break;
+    case L3G_BUF_ATTN: src = ws->attn; cnt = m->hq_l * m->hd; break;
+    case L3G_BUF_FFN_ACT: src = ws->act; cnt = m->ff_l; break;
+    case L3G_BUF_LOGITS:
+      if (!ws->logits_valid) return l3g_fail(L3G_E_INVALID, "no logits computed yet");
+      src = m->world > 1 ? ws->logits_full : ws->logits;
+      cnt = m->world > 1 ? m->hp.vocab_size : m->v_l;
+      break;
+    default: return l3g_fail(L3G_E_INVALID, "unknown buffer %d", which);
+  }
+  if (n < cnt) return l3g_fail(L3G_E_INVALID, "buffer needs %d floats", cnt);
+  CUDA_TRY(cudaSetDevice(m->device));
+  CUDA_TRY(cudaMemcpy(out, src, (size_t)cnt * 4, cudaMemcpyDeviceToHost));
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// standalone matvec (matvec_q8_c drop-in) and quantization
+// ---------------------------------------------------------------------------
+struct l3g_matrix {
+  DevMat w;
+  int device = 0, nsm = 1;
+  Result* d_res = nullptr;  // device error word of the kernel's bounded waits
+};
+
+extern "C" void l3g_matrix_free(l3g_matrix* w) {
+  if (!w) return;
+  cudaSetDevice(w->device);
+  free_mat(w->w);
+  if (w->d_res) cudaFree(w->d_res);
+  delete w;
+}
+
+extern "C" int l3g_matrix_upload(const void* q8, int32_t rows, int32_t cols, int32_t device,
+                                 l3g_matrix** out) {
+  if (!q8 || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  *out = nullptr;
+  if (rows <= 0 || cols <= 0 || cols % 32)
+    return l3g_fail(L3G_E_INVALID, "matvec: cols=%d not multiple of 32", cols);
+  int dev = device;
+  if (dev < 0) CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaSetDevice(dev));
+  int rc = setup_kernels();
+  if (rc) return rc;
+  auto* w = new l3g_matrix();
+  w->device = dev;
+  w->nsm = sm_count(dev);
+  RowSrc seg{static_cast<const uint8_t*>(q8), 0, rows};
+  size_t bytes = 0;
+  rc = upload_tiled(w->w, &seg, 1, false, cols, 0, cols, w->nsm, &bytes);
+  if (rc == L3G_OK && (cudaMalloc(&w->d_res, sizeof(Result)) != cudaSuccess ||
+                       cudaMemset(w->d_res, 0, sizeof(Result)) != cudaSuccess))
+    rc = l3g_fail(L3G_E_CUDA, "matrix result word allocation failed");
+  if (rc) {
+    l3g_matrix_free(w);
+    return rc;
+  }
+  *out = w;
+  return L3G_OK;
+}
+
+extern "C" int l3g_matrix_device_bytes(const l3g_matrix* w, uint64_t* bytes) {
+  if (!w || !bytes) return l3g_fail(L3G_E_INVALID, "null argument");
+  *bytes = w->w.bytes;
+  return L3G_OK;
+}
+
+extern "C" int l3g_matvec_q8(const l3g_matrix* w, const float* x_scales, const int8_t* x_qs,
+                             float* out, int32_t start, int32_t end, void* stream) {
+  if (!w || !x_scales || !x_qs || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (start < 0 || end > w->w.t.rows || start >= end)
+    return l3g_fail(L3G_E_INVALID, "row range [%d, %d) outside [0, %d)", start, end, w->w.t.rows);
+  if (((uintptr_t)x_qs & 15) || ((uintptr_t)x_scales & 3) || ((uintptr_t)out & 3))
+    return l3g_fail(L3G_E_INVALID, "x_qs must be 16-byte aligned, x_scales/out 4-byte");
+  CUDA_TRY(cudaSetDevice(w->device));
+  MatvecArgs a = mv_args(w->w);
+  a.row_lo = start;
+  a.row_hi = end;
+  a.xd_in = x_scales;
+  a.xqs_in = x_qs;
+  a.out = out;
+  a.res = w->d_res;
+  CUDA_TRY((launch_mv<PRO_PREQ, EPI_STORE>(w->w, a, w->nsm, (cudaStream_t)stream)));
+  return L3G_OK;
+}
+
+extern "C" int l3g_quantize_q8_0(const float* x, int32_t n, float* d, int8_t* qs, void* stream) {
+  if (!x || !d || !qs || n <= 0) return l3g_fail(L3G_E_INVALID, "bad argument");
+  const int nb = (n + 31) / 32;
+  const int threads = 256;
+  const int blocks = (nb * 32 + threads - 1) / threads;
+  k_quantize<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, n, d, qs);
+  CUDA_TRY(cudaGetLastError());
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// failure-detection self test
+// ---------------------------------------------------------------------------
+extern "C" int l3g_selftest_bounded_wait(int32_t device, int32_t timeout_us, int32_t* status) {
+  if (!status) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (timeout_us <= 0 || timeout_us > 1000000)
+    return l3g_fail(L3G_E_INVALID, "timeout_us must be in (0, 1e6]");
+  int dev = device;
+  if (dev < 0) CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaSetDevice(dev));
+  Result* d = nullptr;
+  CUDA_TRY(cudaMalloc(&d, sizeof(Result)));
+  cudaMemset(d, 0, sizeof(Result));
+  k_selftest_wait<<<1, 32>>>(d, (unsigned long long)timeout_us * 1000ull);
+  cudaError_t e = cudaDeviceSynchronize();
+  Result h{};
+  if (e == cudaSuccess) e = cudaMemcpy(&h, d, sizeof h, cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "selftest: %s", cudaGetErrorString(e));
+  *status = h.err == ERR_TIMEOUT ? L3G_E_DEVICE : (h.err ? -100 - h.err : L3G_OK);
+  return L3G_OK;
+}
