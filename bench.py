@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--iters", type=int, default=1000, help="matvec microbench iterations")
+    ap.add_argument("--shapes", default="4096x4096,1024x4096,14336x4096,4096x14336,128256x4096",
+                    help="matvec microbench shapes, rows x cols")
     return ap.parse_args()
 
 
@@ -319,7 +321,9 @@ def run_l3g(args):
     warm, _ = m.DecodeGreedy(s, int(prompt[-1]), max(1, args.warmup), ws)
     D.barrier()
     clk = Clocks(physical_index(local))
+    torch.cuda.nvtx.range_push("l3g_decode")
     toks, dev_ms = m.DecodeGreedy(s, int(warm[-1]), args.steps, ws)
+    torch.cuda.nvtx.range_pop()
     D.barrier()
     clocks = clk.stop()
     dev_ms = D.max(dev_ms)
@@ -401,7 +405,8 @@ def run_matvec(args):
     import synthetic
     hbm, kind = peaks()
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
-    for rows, cols in ((4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
+    shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s]
+    for rows, cols in shapes:
         alg = rows * cols // 32 * 34 + cols + cols // 32 * 4 + rows * 4
         ncopy = max(1, -(-4 * l2 // alg))
         g = torch.Generator(device="cuda").manual_seed(rows + cols)

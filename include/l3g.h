@@ -113,6 +113,23 @@ int l3g_device_count(int32_t *n);
 int l3g_nccl_unique_id(uint8_t out[128]);
 void l3g_options_default(l3g_options *opt);
 
+/* Tensor-parallel shard of one rank (the reference has no parallelism beyond
+ * its goroutine pool, workers.go:88-116; this is the split the library uses):
+ * attention by heads, FFN by rows, Wo / down by the matching columns, logits
+ * by vocab rows.  Row / column ranges are [start, start + count). */
+typedef struct {
+  int32_t q_row0, q_rows;         /* rows of attn_q                       */
+  int32_t kv_row0, kv_rows;       /* rows of attn_k and attn_v            */
+  int32_t o_col0, o_cols;         /* columns of attn_output               */
+  int32_t ff_row0, ff_rows;       /* rows of ffn_up and ffn_gate          */
+  int32_t down_col0, down_cols;   /* columns of ffn_down                  */
+  int32_t vocab_row0, vocab_rows; /* rows of output.weight (or tied emb)  */
+  int32_t vocab_stride;           /* rows per rank before the last shard  */
+} l3g_shard;
+/* Host-only: validates hp for world_size ranks and fills this rank's shard. */
+int l3g_shard_plan(const l3g_hparams *hp, int32_t world_size, int32_t rank,
+                   l3g_shard *out);
+
 /* ---- model: LoadModel (model.go:55-156), Close (model.go:158-166) ------- */
 /* Uploads the Q8_0 blocks once (values unchanged, repacked into 16-byte
  * aligned tiles) plus f32 norms; keeps no host pointer.  Tensor names as

@@ -384,6 +384,43 @@ static int validate_hparams(const l3g_hparams& hp, int world) {
   return L3G_OK;
 }
 
+static void apply_hparam_defaults(l3g_hparams& hp) {
+  if (hp.n_heads_kv == 0) hp.n_heads_kv = hp.n_heads;                       // model.go:212-214
+  if (hp.rope_dim == 0 && hp.n_heads) hp.rope_dim = hp.n_emb / hp.n_heads;  // :215-217
+}
+
+extern "C" int l3g_shard_plan(const l3g_hparams* hp_in, int32_t world, int32_t rank,
+                              l3g_shard* out) {
+  if (!hp_in || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  l3g_hparams hp = *hp_in;
+  apply_hparam_defaults(hp);
+  int rc = validate_hparams(hp, world);
+  if (rc) return rc;
+  if (rank < 0 || rank >= world)
+    return l3g_fail(L3G_E_INVALID, "rank %d outside world %d", rank, world);
+  const int hd = hp.n_emb / hp.n_heads;
+  const int hq = hp.n_heads / world, hkv = hp.n_heads_kv / world, ff = hp.n_ff / world;
+  const int vl = (hp.vocab_size + world - 1) / world;
+  l3g_shard s{};
+  s.q_row0 = rank * hq * hd;
+  s.q_rows = hq * hd;
+  s.kv_row0 = rank * hkv * hd;
+  s.kv_rows = hkv * hd;
+  s.o_col0 = rank * hq * hd;
+  s.o_cols = hq * hd;
+  s.ff_row0 = rank * ff;
+  s.ff_rows = ff;
+  s.down_col0 = rank * ff;
+  s.down_cols = ff;
+  s.vocab_stride = vl;
+  s.vocab_row0 = rank * vl;
+  s.vocab_rows = std::min(hp.vocab_size, s.vocab_row0 + vl) - s.vocab_row0;
+  if (s.vocab_rows < 1)
+    return l3g_fail(L3G_E_INVALID, "vocab %d too small for %d ranks", hp.vocab_size, world);
+  *out = s;
+  return L3G_OK;
+}
+
 extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, int32_t nt,
                               const l3g_options* opt_in, l3g_model** out) {
   if (!hp_in || !ts || !out) return l3g_fail(L3G_E_INVALID, "null argument");
@@ -394,12 +431,10 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
   else
     l3g_options_default(&opt);
   l3g_hparams hp = *hp_in;
-  if (hp.n_heads_kv == 0) hp.n_heads_kv = hp.n_heads;          // model.go:212-214
-  if (hp.rope_dim == 0 && hp.n_heads) hp.rope_dim = hp.n_emb / hp.n_heads;  // :215-217
-  int rc = validate_hparams(hp, opt.world_size);
+  apply_hparam_defaults(hp);
+  l3g_shard sh;
+  int rc = l3g_shard_plan(&hp, opt.world_size, opt.rank, &sh);
   if (rc) return rc;
-  if (opt.rank < 0 || opt.rank >= opt.world_size)
-    return l3g_fail(L3G_E_INVALID, "rank %d outside world %d", opt.rank, opt.world_size);
   if (opt.kv_dtype != L3G_KV_F32 && opt.kv_dtype != L3G_KV_F16)
     return l3g_fail(L3G_E_INVALID, "kv_dtype %d", opt.kv_dtype);
 
@@ -420,8 +455,8 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
   m->hkv_l = hp.n_heads_kv / m->world;
   m->group = hp.n_heads / hp.n_heads_kv;
   m->ff_l = hp.n_ff / m->world;
-  m->v_l = (hp.vocab_size + m->world - 1) / m->world;
-  m->v_off = m->rank * m->v_l;
+  m->v_l = sh.vocab_stride;
+  m->v_off = sh.vocab_row0;
   m->rope_half = hp.rope_dim / 2;
   auto bail = [&](int code) {
     l3g_model_free(m);
@@ -454,8 +489,7 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
   if (!outp) outp = emb;  // tied, model.go:91-94
   else if ((rc = check_matrix(outp, "output.weight", ne, hp.vocab_size))) return bail(rc);
   {
-    const int v1 = std::min(hp.vocab_size, m->v_off + m->v_l);
-    RowSrc seg{static_cast<const uint8_t*>(outp->data), m->v_off, v1 - m->v_off};
+    RowSrc seg{static_cast<const uint8_t*>(outp->data), sh.vocab_row0, sh.vocab_rows};
     if ((rc = upload_tiled(m->logits, &seg, 1, false, ne, 0, ne, m->nsm, &m->dev_bytes)))
       return bail(rc);
   }
@@ -488,24 +522,23 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
     const auto* wg = static_cast<const uint8_t*>(T("ffn_gate.weight")->data);
     const auto* wd = static_cast<const uint8_t*>(T("ffn_down.weight")->data);
     // this rank's heads: q rows, k rows, v rows concatenated
-    RowSrc qkv[3] = {{wq, m->rank * m->hq_l * hd, m->hq_l * hd},
-                     {wk, m->rank * m->hkv_l * hd, m->hkv_l * hd},
-                     {wv, m->rank * m->hkv_l * hd, m->hkv_l * hd}};
+    RowSrc qkv[3] = {{wq, sh.q_row0, sh.q_rows},
+                     {wk, sh.kv_row0, sh.kv_rows},
+                     {wv, sh.kv_row0, sh.kv_rows}};
     if ((rc = upload_tiled(L.qkv, qkv, 3, false, ne, 0, ne, m->nsm, &m->dev_bytes)))
       return bail(rc);
     // Wo: all rows, this rank's head columns
-    const int ac = m->hq_l * hd;
     RowSrc wos{wo, 0, ne};
-    if ((rc = upload_tiled(L.wo, &wos, 1, false, ne, m->rank * ac / 32, ac, m->nsm,
+    if ((rc = upload_tiled(L.wo, &wos, 1, false, ne, sh.o_col0 / 32, sh.o_cols, m->nsm,
                            &m->dev_bytes)))
       return bail(rc);
     // up/gate interleaved (up_i, gate_i) for this rank's FFN rows
-    RowSrc ug[2] = {{wu, m->rank * m->ff_l, m->ff_l}, {wg, m->rank * m->ff_l, m->ff_l}};
+    RowSrc ug[2] = {{wu, sh.ff_row0, sh.ff_rows}, {wg, sh.ff_row0, sh.ff_rows}};
     if ((rc = upload_tiled(L.upgate, ug, 2, true, ne, 0, ne, m->nsm, &m->dev_bytes)))
       return bail(rc);
     // down: all rows, this rank's FFN columns
     RowSrc ds{wd, 0, ne};
-    if ((rc = upload_tiled(L.down, &ds, 1, false, hp.n_ff, m->rank * m->ff_l / 32, m->ff_l,
+    if ((rc = upload_tiled(L.down, &ds, 1, false, hp.n_ff, sh.down_col0 / 32, sh.down_cols,
                            m->nsm, &m->dev_bytes)))
       return bail(rc);
     snprintf(name, sizeof name, "blk.%d.attn_norm.weight", l);

@@ -53,6 +53,13 @@ class Options(C.Structure):
                 ("kv_dtype", C.c_int32), ("nccl_id", C.c_uint8 * 128)]
 
 
+class Shard(C.Structure):
+    """l3g_shard: one tensor-parallel rank's row / column ranges."""
+    _fields_ = [(n, C.c_int32) for n in (
+        "q_row0", "q_rows", "kv_row0", "kv_rows", "o_col0", "o_cols", "ff_row0", "ff_rows",
+        "down_col0", "down_cols", "vocab_row0", "vocab_rows", "vocab_stride")]
+
+
 class TopKItem(C.Structure):
     """TopKItem, topk.go:5-8."""
     _fields_ = [("ID", C.c_int32), ("Logit", C.c_float)]
@@ -80,6 +87,7 @@ def lib():
         "l3g_device_count": (C.c_int, [C.POINTER(C.c_int32)]),
         "l3g_nccl_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
         "l3g_options_default": (None, [C.POINTER(Options)]),
+        "l3g_shard_plan": (C.c_int, [C.POINTER(HyperParams), C.c_int32, C.c_int32, C.POINTER(Shard)]),
         "l3g_model_load": (C.c_int, [C.POINTER(HyperParams), C.POINTER(_Tensor), C.c_int32,
                                      C.POINTER(Options), C.POINTER(_P)]),
         "l3g_model_load_gguf": (C.c_int, [C.c_char_p, C.POINTER(Options), C.POINTER(_P)]),
@@ -142,6 +150,13 @@ def default_options(world_size=1, rank=0, device=-1, kv_dtype=L3G_KV_F32, nccl_i
     if nccl_id is not None:
         C.memmove(o.nccl_id, bytes(nccl_id), 128)
     return o
+
+
+def shard_plan(hp: HyperParams, world_size: int, rank: int) -> Shard:
+    """The library's tensor-parallel split for one rank (host-only)."""
+    s = Shard()
+    _check(lib().l3g_shard_plan(C.byref(hp), world_size, rank, C.byref(s)))
+    return s
 
 
 def nccl_unique_id() -> bytes:
