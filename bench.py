@@ -346,6 +346,15 @@ def run_l3g(args):
     e2e = args.steps / e2e_s
     same = bool(np.array_equal(np.array(e2e_toks, np.int32), toks))
 
+    # per-kernel device time of one step at this context (eager, serialized)
+    s.Pos = p0 + max(1, args.warmup)
+    prof = {}
+    for _ in range(3):
+        for kind, us in m.ProfileStep(s, tok, ws):
+            prof[kind] = prof.get(kind, 0.0) + us / 3
+        s.Pos = p0 + max(1, args.warmup)
+    prof = {k: round(v, 1) for k, v in sorted(prof.items(), key=lambda kv: -kv[1])}
+
     # roofline of the whole decode step (weights + KV read per token)
     es = 2 if args.kv == "f16" else 4
     first_pos = p0 + max(1, args.warmup)
@@ -387,6 +396,7 @@ def run_l3g(args):
                 "tokens_match_device_loop": same},
         "gpu_launches": kernels * args.steps,
         "kernels_per_step": kernels,
+        "step_profile_us": prof,
         "clocks": clocks,
         "prefill_s": round(prefill_s, 3),
     }

@@ -194,6 +194,22 @@ int l3g_decode_greedy(l3g_model *m, l3g_state *s, l3g_workspace *ws,
  * accounting. */
 int l3g_workspace_kernels_per_step(l3g_workspace *ws, int32_t *n);
 
+/* Profiling (the device counterpart of the chat CLI's -cpuprofile,
+ * cmd/go-llama-chat/main.go:35-54): runs one greedy step eagerly, each kernel
+ * serialized and bracketed by CUDA events, and reports per launch its kind
+ * (L3G_K_*) and device time in microseconds.  Advances the position like a
+ * step.  *n is the capacity on entry and the count on return. */
+#define L3G_K_EMBED 0
+#define L3G_K_QKV 1
+#define L3G_K_ATTN 2
+#define L3G_K_WO 3
+#define L3G_K_UPGATE 4
+#define L3G_K_DOWN 5
+#define L3G_K_LOGITS 6
+#define L3G_K_OTHER 7
+int l3g_profile_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                     int32_t token, int32_t *kinds, float *us, int32_t *n);
+
 /* ---- Q8_0 matvec drop-in: matvec_q8_c (simd.h:8) / matVecQ8_0 ------------ */
 /* Uploads a GGUF Q8_0 matrix (rows x cols, 34-byte blocks, host bytes). */
 int l3g_matrix_upload(const void *q8_0_rows, int32_t rows, int32_t cols,

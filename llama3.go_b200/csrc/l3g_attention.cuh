@@ -1,0 +1,325 @@
+// Split-K GQA attention of libl3g (included by l3g_kernels.cuh), the
+// attention loop of ForwardIntoWorkspace (internal/llama/infer.go:130-175).
+//
+// Grid (local kv heads, splits).  CTA (g, s) takes a contiguous range of
+// positions of kv head g for the `group` query heads sharing it, streams the
+// K and V rows of P positions per stage through a shared-memory ring (two
+// ~16 KB bulk copies per stage), and keeps an online softmax per warp:
+//   - lanes split the head dimension (DPL = hd / 32 values each);
+//   - a warp takes NBW = P / 8 positions of each stage in sub-batches of
+//     32 / GP positions (GP = group rounded up to a power of two), computes
+//     the partial dots of every (position, head) pair and transpose-reduces
+//     them so lane i ends with complete score i (31 shuffles per sub-batch);
+//   - probabilities are broadcast through a warp-private buffer for the V
+//     accumulation.
+// The per-warp states merge in the CTA, the CTAs of one kv head merge in
+// split order in whichever CTA finishes last (deterministic).
+#pragma once
+
+struct AttnArgs {
+  const float* q;     // [local q heads][hd], roped
+  const void* kc;     // this layer [local kv heads][ctx][hd]
+  const void* vc;
+  int ctx, hd, group, n_splits, P, nstages, stage_bytes;
+  float scale;        // float32(1/sqrt(hd)), infer.go:130
+  const int* io;      // io[1] = position of this token
+  float* part_o;      // [kv heads][splits][group][hd]
+  float* part_ml;     // [kv heads][splits][group][2]
+  unsigned* counters; // [kv heads], zero between launches
+  float* out;         // [local q heads][hd]
+  Result* res;
+};
+
+struct AttnSmem {
+  uint64_t full[MAX_STAGES];
+  uint64_t empty[MAX_STAGES];
+  int abort_flag;
+  int issued;
+  int last;
+};
+constexpr int AT_HEAD = 512;
+static_assert(sizeof(AttnSmem) <= AT_HEAD, "attn smem head");
+
+// Shared memory after the head: per-warp probability buffer [NW][32] and
+// head statistics [NW][MAXG][4], then the ring (reused as merge scratch).
+constexpr int AT_BUF = (NW * 32 + NW * MAXG * 4) * 4;
+__host__ __device__ __forceinline__ int at_ring_offset() { return AT_HEAD + align_up(AT_BUF, 128); }
+
+template <int DPL, typename KT>
+__device__ __forceinline__ void load_row(const KT* p, float* v) {
+  if constexpr (sizeof(KT) == 4) {
+    if constexpr (DPL == 4) {
+      const float4 t = *reinterpret_cast<const float4*>(p);
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else if constexpr (DPL == 2) {
+      const float2 t = *reinterpret_cast<const float2*>(p);
+      v[0] = t.x; v[1] = t.y;
+    } else {
+      v[0] = *reinterpret_cast<const float*>(p);
+    }
+  } else {
+    const __half* h = reinterpret_cast<const __half*>(p);
+    if constexpr (DPL == 4) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(h);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    } else {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(h));
+      v[0] = a.x; v[1] = a.y;
+    }
+  }
+}
+
+// v[i] on every lane -> lane l returns sum over lanes of v[l].
+__device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int k = 16; k >= 1; k >>= 1) {
+    const bool upper = lane & k;
+#pragma unroll
+    for (int j = 0; j < k; ++j) {
+      const float send = upper ? v[j] : v[j + k];
+      const float keep = upper ? v[j + k] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, k);
+    }
+  }
+  return v[0];
+}
+
+template <int DPL, typename KT, int GP>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_attention(const __grid_constant__ AttnArgs a) {
+  constexpr int SB = 32 / GP;  // positions per sub-batch
+  extern __shared__ __align__(1024) uint8_t smem[];
+  AttnSmem* sh = reinterpret_cast<AttnSmem*>(smem);
+  float* pbuf_all = reinterpret_cast<float*>(smem + AT_HEAD);
+  float* hbuf_all = pbuf_all + NW * 32;
+  uint8_t* ring = smem + at_ring_offset();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x, split = blockIdx.y, S = a.n_splits;
+  const int hd = a.hd, G = a.group, ns = a.nstages, P = a.P;
+  const int pos = a.io[1];  // written by the step's host copy, not a kernel
+  const int n = pos + 1;
+  const int chunk = align_up((n + S - 1) / S, P);
+  const int t0 = min(n, split * chunk), t1 = min(n, t0 + chunk);
+  const int nst = (t1 - t0 + P - 1) / P;
+  const size_t head_off = (size_t)kvh * a.ctx * hd;
+  const int half_stage = a.stage_bytes / 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&sh->full[s], 1);
+      mbar_init(&sh->empty[s], NW);
+    }
+    sh->abort_flag = 0;
+    sh->issued = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == NW) {
+    if (lane == 0) {
+      bool waited = false;
+      for (int st = 0; st < nst; ++st) {
+        const int s = st % ns;
+        if (st >= ns &&
+            !mbar_wait(&sh->empty[s], ((st / ns) - 1) & 1, &sh->abort_flag, a.res, 4))
+          break;
+        const int ta = t0 + st * P, tb = min(t1, ta + P);
+        // past positions are immutable: only the stage holding this step's
+        // own K/V (written by the QKV kernel) waits for the previous grid
+        if (!waited && tb > pos) {
+          pdl_wait();
+          waited = true;
+        }
+        const uint32_t bytes = (uint32_t)((tb - ta) * hd * sizeof(KT));
+        const size_t off = (head_off + (size_t)ta * hd) * sizeof(KT);
+        mbar_arrive_expect_tx(&sh->full[s], 2 * bytes);
+        bulk_g2s(ring + (size_t)s * a.stage_bytes,
+                 static_cast<const uint8_t*>(a.kc) + off, bytes, &sh->full[s]);
+        bulk_g2s(ring + (size_t)s * a.stage_bytes + half_stage,
+                 static_cast<const uint8_t*>(a.vc) + off, bytes, &sh->full[s]);
+        *(volatile int*)&sh->issued = st + 1;
+      }
+    }
+    return;
+  }
+
+  pdl_wait();  // q comes from the previous kernel
+  float q[GP][DPL];
+#pragma unroll
+  for (int h = 0; h < GP; ++h)
+#pragma unroll
+    for (int j = 0; j < DPL; ++j)
+      q[h][j] = h < G ? a.q[((size_t)kvh * G + h) * hd + lane * DPL + j] : 0.0f;
+  float m[GP], l[GP], o[GP][DPL];
+#pragma unroll
+  for (int h = 0; h < GP; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) o[h][j] = 0.0f;
+  }
+  float* pbuf = pbuf_all + warp * 32;
+  float* hbuf = hbuf_all + warp * MAXG * 4;
+  const int nbw = P / NW;          // positions of a stage this warp takes
+  const int my_h = lane % GP;      // after the transpose-reduce: lane -> (pos, head)
+  const int my_p = lane / GP;
+
+  int consumed = 0;
+  for (int st = 0; st < nst; ++st) {
+    const int s = st % ns;
+    const bool ok = mbar_wait(&sh->full[s], (st / ns) & 1, &sh->abort_flag, a.res, 5);
+    if (ok) {
+      consumed = st + 1;
+      const int cnt = min(t1, t0 + st * P + P) - (t0 + st * P);
+      const KT* Ks = reinterpret_cast<const KT*>(ring + (size_t)s * a.stage_bytes);
+      const KT* Vs = reinterpret_cast<const KT*>(ring + (size_t)s * a.stage_bytes + half_stage);
+      for (int sb = 0; sb < nbw; sb += SB) {
+        const int p0 = warp * nbw + sb;      // first position of the sub-batch
+        const int np = min(SB, nbw - sb);    // positions of this warp in it
+        // partial dots of (position, head), then the transpose-reduce
+        float v[32];
+#pragma unroll
+        for (int p = 0; p < SB; ++p) {
+          float kv[DPL];
+          if (p < np && p0 + p < cnt) {
+            load_row<DPL, KT>(Ks + (size_t)(p0 + p) * hd + lane * DPL, kv);
+          } else {
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) kv[j] = 0.0f;
+          }
+#pragma unroll
+          for (int h = 0; h < GP; ++h) {
+            float d = 0.0f;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) d = fmaf(q[h][j], kv[j], d);
+            v[p * GP + h] = d;
+          }
+        }
+        const float dot = transpose_reduce32(v, lane);
+        const bool valid = my_p < np && p0 + my_p < cnt && my_h < G;
+        const float sc = valid ? dot * a.scale : -INFINITY;
+        // per-head maximum and sum over the sub-batch's positions
+        float mb = sc;
+#pragma unroll
+        for (int off = GP; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        float mo = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < GP; ++h)
+          if (h == my_h) mo = m[h];
+        const float mn = fmaxf(mo, mb);
+        const float pe = valid ? expf(sc - mn) : 0.0f;
+        const float corr = mn == -INFINITY ? 1.0f : expf(mo - mn);
+        float lb = pe;
+#pragma unroll
+        for (int off = GP; off < 32; off <<= 1) lb += __shfl_xor_sync(0xffffffffu, lb, off);
+        pbuf[lane] = pe;
+        if (lane < GP) {
+          hbuf[lane * 4 + 0] = mn;
+          hbuf[lane * 4 + 1] = corr;
+          hbuf[lane * 4 + 2] = lb;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int h = 0; h < GP; ++h) {
+          const float c = hbuf[h * 4 + 1];
+          m[h] = hbuf[h * 4 + 0];
+          l[h] = fmaf(l[h], c, hbuf[h * 4 + 2]);
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) o[h][j] *= c;
+        }
+        for (int p = 0; p < np && p0 + p < cnt; ++p) {
+          float vv[DPL];
+          load_row<DPL, KT>(Vs + (size_t)(p0 + p) * hd + lane * DPL, vv);
+#pragma unroll
+          for (int h = 0; h < GP; ++h) {
+            const float w = pbuf[p * GP + h];
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) o[h][j] = fmaf(w, vv[j], o[h][j]);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sh->empty[s]);
+  }
+
+  // drain after an abort, then reuse the ring as merge scratch
+  if (*(volatile int*)&sh->abort_flag && threadIdx.x == 0) {
+    const int issued = *(volatile int*)&sh->issued;
+    for (int t = consumed; t < issued; ++t) {
+      int dummy = 0;
+      mbar_wait(&sh->full[t % ns], (t / ns) & 1, &dummy, a.res, 6, 100000000ull);
+    }
+  }
+  consumer_sync();
+  float* sm_ml = reinterpret_cast<float*>(ring);  // [NW][G][2], then [S][G][2]
+  float* sm_o = sm_ml + NW * MAXG * 2;            // [NW][G][hd]
+#pragma unroll
+  for (int h = 0; h < GP; ++h) {
+    if (h < G) {
+      if (lane == 0) {
+        sm_ml[(warp * MAXG + h) * 2] = m[h];
+        sm_ml[(warp * MAXG + h) * 2 + 1] = l[h];
+      }
+#pragma unroll
+      for (int j = 0; j < DPL; ++j)
+        sm_o[((size_t)warp * G + h) * hd + lane * DPL + j] = o[h][j];
+    }
+  }
+  consumer_sync();
+  const size_t pbase = ((size_t)kvh * S + split) * G;
+  for (int idx = threadIdx.x; idx < G * hd; idx += NW * 32) {
+    const int h = idx / hd, d = idx % hd;
+    float M = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_ml[(w * MAXG + h) * 2]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < NW; ++w) {
+        const float mw = sm_ml[(w * MAXG + h) * 2];
+        if (mw == -INFINITY) continue;
+        const float e = expf(mw - M);
+        L = fmaf(sm_ml[(w * MAXG + h) * 2 + 1], e, L);
+        O = fmaf(sm_o[((size_t)w * G + h) * hd + d], e, O);
+      }
+    }
+    a.part_o[(pbase + h) * hd + d] = O;
+    if (d == 0) {
+      a.part_ml[(pbase + h) * 2] = M;
+      a.part_ml[(pbase + h) * 2 + 1] = L;
+    }
+  }
+  __threadfence();
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(a.counters + kvh, 1u);
+    sh->last = prev == (unsigned)S - 1;
+  }
+  consumer_sync();
+  if (!*(volatile int*)&sh->last) return;
+  __threadfence();
+  // merge the splits: their (m, l) pairs into shared memory first, then each
+  // (head, dim) issues its partial-output loads back to back
+  float* sm_split = sm_ml;  // [S][G][2] (the ring holds S * G * 2 floats)
+  for (int i = threadIdx.x; i < S * G * 2; i += NW * 32)
+    sm_split[i] = __ldcg(a.part_ml + (size_t)kvh * S * G * 2 + i);
+  consumer_sync();
+  for (int idx = threadIdx.x; idx < G * hd; idx += NW * 32) {
+    const int h = idx / hd, d = idx % hd;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, sm_split[(s2 * G + h) * 2]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll 8
+    for (int s2 = 0; s2 < S; ++s2) {
+      const float ms = sm_split[(s2 * G + h) * 2];
+      const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
+      L = fmaf(sm_split[(s2 * G + h) * 2 + 1], e, L);
+      O = fmaf(__ldcg(a.part_o + (((size_t)kvh * S + s2) * G + h) * hd + d), e, O);
+    }
+    a.out[((size_t)kvh * G + h) * hd + d] = __fmul_rn(O, __fdiv_rn(1.0f, L));
+  }
+  if (threadIdx.x == 0) a.counters[kvh] = 0u;
+}

@@ -136,18 +136,28 @@ static int setup_kernels() {
     cudaError_t e = cudaSuccess;
 #define SETK(k) \
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, big)
-    SETK((k_matvec<PRO_PREQ, EPI_STORE>));
-    SETK((k_matvec<PRO_QUANT, EPI_STORE>));
-    SETK((k_matvec<PRO_RMS, EPI_QKV>));
-    SETK((k_matvec<PRO_RMS, EPI_SWIGLU>));
-    SETK((k_matvec<PRO_RMS, EPI_LOGITS>));
-    SETK((k_attention<1, float>));
-    SETK((k_attention<2, float>));
-    SETK((k_attention<4, float>));
-    SETK((k_attention<8, float>));
-    SETK((k_attention<2, __half>));
-    SETK((k_attention<4, __half>));
-    SETK((k_attention<8, __half>));
+#define SETMV(P, E)                  \
+  SETK((k_matvec<P, E, 1>));         \
+  SETK((k_matvec<P, E, 2>));         \
+  SETK((k_matvec<P, E, 4>));         \
+  SETK((k_matvec<P, E, 8>))
+    SETMV(PRO_PREQ, EPI_STORE);
+    SETMV(PRO_QUANT, EPI_STORE);
+    SETMV(PRO_RMS, EPI_QKV);
+    SETMV(PRO_RMS, EPI_SWIGLU);
+    SETMV(PRO_RMS, EPI_LOGITS);
+#undef SETMV
+#define SETAT(D, T)                  \
+  SETK((k_attention<D, T, 1>));      \
+  SETK((k_attention<D, T, 2>));      \
+  SETK((k_attention<D, T, 4>));      \
+  SETK((k_attention<D, T, 8>))
+    SETAT(1, float);
+    SETAT(2, float);
+    SETAT(4, float);
+    SETAT(2, __half);
+    SETAT(4, __half);
+#undef SETAT
     SETK(k_topk_final);
 #undef SETK
     rc = e == cudaSuccess ? 0 : (int)e;
@@ -155,6 +165,10 @@ static int setup_kernels() {
   if (rc) return l3g_fail(L3G_E_CUDA, "kernel attribute set-up: %s", cudaGetErrorString((cudaError_t)rc));
   return L3G_OK;
 }
+
+// Eager profiling launches every kernel fully serialized (no programmatic
+// dependent launch) so CUDA events between kernels time each one alone.
+static thread_local bool g_serialize = false;
 
 template <typename... KArgs, typename... Args>
 static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block,
@@ -168,7 +182,7 @@ static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = g_serialize ? 0 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
@@ -183,38 +197,51 @@ struct DevMat {
   int smem = 0;
 };
 
-// Row-group size: the one whose busiest CTA (one CTA per SM) streams the
-// fewest rows; ties go to the larger group (fewer barriers).  Column slices
-// keep a tile near TILE_TARGET int8 bytes.
-static Q8Tiles plan_tiles(int rows, int cols, int nsm) {
-  int best_wr = 8;
-  long long best = LLONG_MAX;
-  for (int wr : {8, 4, 2}) {
-    const int ng = (rows + wr - 1) / wr;
-    const int grid = std::min(ng, nsm);
-    const long long per = (ng + grid - 1) / grid;
-    const long long cost = per * wr;
-    if (best == LLONG_MAX || cost * 1000 < best * 995) {
-      best = cost;
-      best_wr = wr;
-    }
-  }
+// Per-CTA cost of one tile on the bulk-copy path, in ns: a fixed ~250 ns per
+// copy plus its bytes at ~100 GB/s (fitted on B200 with a streaming probe).
+static double tile_cost_ns(int tile_bytes) { return 250.0 + tile_bytes / 100.0; }
+
+static Q8Tiles make_tiles(int rows, int cols, int rpw) {
   Q8Tiles t{};
   t.rows = rows;
   t.cols = cols;
-  t.wr = best_wr;
+  t.wr = NW * rpw;
   const int nb = cols / 32;
-  int nsl = std::max(1, (cols * best_wr + TILE_TARGET - 1) / TILE_TARGET);
+  int nsl = std::max(1, (int)(((long long)cols * t.wr + TILE_TARGET - 1) / TILE_TARGET));
   while (nb % nsl) ++nsl;
   t.nslices = nsl;
   t.ck = cols / nsl;
-  t.tile_bytes = align_up(best_wr * t.ck + best_wr * (t.ck / 32) * 2, 16);
-  t.n_groups = (rows + best_wr - 1) / best_wr;
+  t.tile_bytes = align_up(t.wr * t.ck + t.wr * (t.ck / 32) * 2, 16);
+  t.n_groups = (rows + t.wr - 1) / t.wr;
   return t;
 }
 
+// Rows per warp: the layout whose busiest CTA (one CTA per SM) finishes
+// first under tile_cost_ns, bounded below by the HBM time of the matrix;
+// ties go to fewer rows per warp.
+static Q8Tiles plan_tiles(int rows, int cols, int nsm) {
+  Q8Tiles best{};
+  double best_t = 1e300;
+  for (int rpw : {1, 2, 4, 8}) {
+    const Q8Tiles t = make_tiles(rows, cols, rpw);
+    const long long ntiles = (long long)t.n_groups * t.nslices;
+    const long long grid = std::min<long long>(t.n_groups, nsm);
+    const long long groups_per_cta = (t.n_groups + grid - 1) / grid;
+    const double cta_ns = groups_per_cta * t.nslices * tile_cost_ns(t.tile_bytes);
+    const double hbm_ns = (double)ntiles * t.tile_bytes / 7000.0;  // ~7 TB/s read
+    const double tt = std::max(cta_ns, hbm_ns);
+    if (tt < best_t * 0.98) {
+      best_t = tt;
+      best = t;
+    }
+  }
+  return best;
+}
+
+// Stages: as many tiles as fit the per-CTA share (at least 2).
 static void finish_plan(DevMat& m) {
-  m.nstages = std::max(2, std::min(MAX_STAGES, RING_BYTES / m.t.tile_bytes));
+  const int fixed = mv_smem_bytes(m.t.cols, 0, m.t.tile_bytes);
+  m.nstages = std::max(2, std::min(MAX_STAGES, (CTA_SMEM_SHARE - fixed) / m.t.tile_bytes));
   m.smem = mv_smem_bytes(m.t.cols, m.nstages, m.t.tile_bytes);
 }
 
@@ -360,8 +387,8 @@ static int validate_hparams(const l3g_hparams& hp, int world) {
   if (hp.n_emb % hp.n_heads)
     return l3g_fail(L3G_E_INVALID, "n_emb %d not divisible by n_heads %d", hp.n_emb, hp.n_heads);
   const int hd = hp.n_emb / hp.n_heads;
-  if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
-    return l3g_fail(L3G_E_INVALID, "head_dim %d unsupported (32, 64, 128 or 256)", hd);
+  if (hd != 32 && hd != 64 && hd != 128)
+    return l3g_fail(L3G_E_INVALID, "head_dim %d unsupported (32, 64 or 128)", hd);
   if (hp.n_heads_kv <= 0 || hp.n_heads % hp.n_heads_kv)
     return l3g_fail(L3G_E_INVALID, "n_heads %d not a multiple of n_heads_kv %d", hp.n_heads,
                     hp.n_heads_kv);
@@ -369,6 +396,10 @@ static int validate_hparams(const l3g_hparams& hp, int world) {
     return l3g_fail(L3G_E_INVALID, "GQA group %d above %d", hp.n_heads / hp.n_heads_kv, MAXG);
   if (hp.n_emb % 32 || hp.n_ff % 32)
     return l3g_fail(L3G_E_INVALID, "n_emb and n_ff must be multiples of 32");
+  // the matvec prologues hold their input vector in registers
+  if (hp.n_emb > 8192) return l3g_fail(L3G_E_INVALID, "n_emb %d above 8192", hp.n_emb);
+  if (world >= 1 && hp.n_ff / world > 16384)
+    return l3g_fail(L3G_E_INVALID, "n_ff per rank %d above 16384", hp.n_ff / world);
   if (hp.rope_dim <= 0 || hp.rope_dim > hd || hp.rope_dim % 2)
     return l3g_fail(L3G_E_INVALID, "rope_dim %d must be even and <= head_dim %d", hp.rope_dim, hd);
   if (hp.ctx_len <= 0) return l3g_fail(L3G_E_INVALID, "ctx_len %d", hp.ctx_len);
@@ -437,6 +468,8 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
   if (rc) return rc;
   if (opt.kv_dtype != L3G_KV_F32 && opt.kv_dtype != L3G_KV_F16)
     return l3g_fail(L3G_E_INVALID, "kv_dtype %d", opt.kv_dtype);
+  if (opt.kv_dtype == L3G_KV_F16 && hp.n_emb / hp.n_heads < 64)
+    return l3g_fail(L3G_E_INVALID, "f16 KV cache needs head_dim >= 64");
 
   int dev = opt.device;
   if (dev < 0) CUDA_TRY(cudaGetDevice(&dev));
@@ -730,11 +763,14 @@ struct l3g_workspace {
   float* d_tk_logits = nullptr;
   int* h_tk_ids = nullptr;
   float* h_tk_logits = nullptr;
-  int n_splits = 1, att_P = 16, att_ns = 4, att_stage = 0, att_smem = 0;
+  int n_splits = 1, att_P = 16, att_ns = 3, att_stage = 0, att_smem = 0, att_gp = 1;
   int tk_chunks = 0;
   int* d_tokens = nullptr;     // [ctx] tokens of a device-fed greedy run
   int kernels = 0;             // kernel launches counted during a capture
   int kernels_greedy = 0;      // ... of the greedy variant
+  bool profiling = false;      // record an event after every kernel
+  std::vector<int> prof_kind;
+  std::vector<cudaEvent_t> prof_ev;
   std::vector<StepGraph> graphs;
   bool logits_valid = false;
 };
@@ -776,13 +812,16 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   const int ne = m->hp.n_emb, hd = m->hd;
   const int G = m->group;
   const size_t es = m->kv_f16 ? 2 : 4;
-  // attention geometry: splits fill the SMs; a stage is ~16 KB of K+V
-  ws->att_P = std::max(NW, (int)(16384 / (2 * hd * es)));
+  // attention geometry: splits fill the SMs; a stage holds P positions, the
+  // K and V halves each one ~16 KB bulk copy; three stages in flight
+  ws->att_P = std::max(NW, (int)(16384 / (hd * es)));
   ws->att_stage = 2 * ws->att_P * hd * (int)es;
-  ws->att_ns = 4;
+  ws->att_ns = 3;
+  ws->att_gp = 1;
+  while (ws->att_gp < G) ws->att_gp <<= 1;
   ws->n_splits = std::max(1, std::min(m->nsm / m->hkv_l, (ctx + ws->att_P - 1) / ws->att_P));
-  const int scratch = (NW * MAXG * 2 + NW * G * hd) * 4;
-  ws->att_smem = AT_HEAD + std::max(ws->att_ns * ws->att_stage, scratch);
+  const int scratch = std::max((NW * MAXG * 2 + NW * G * hd) * 4, ws->n_splits * G * 2 * 4);
+  ws->att_smem = at_ring_offset() + std::max(ws->att_ns * ws->att_stage, scratch);
   const int vloc = m->v_l;
   ws->tk_chunks = (m->v_l * m->world + TOPK_CHUNK - 1) / TOPK_CHUNK;
   cudaError_t e = cudaStreamCreateWithFlags(&ws->stream, cudaStreamNonBlocking);
@@ -854,7 +893,25 @@ static cudaError_t launch_mv(const DevMat& w, const MatvecArgs& a, int nsm, cuda
   const int gl = a.row_lo / w.t.wr;
   const int ng = (a.row_hi + w.t.wr - 1) / w.t.wr - gl;
   const int grid = std::max(1, std::min(ng, nsm));
-  return launch(k_matvec<PRO, EPI>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
+  switch (w.t.wr / NW) {
+    case 1: return launch(k_matvec<PRO, EPI, 1>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
+    case 2: return launch(k_matvec<PRO, EPI, 2>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
+    case 4: return launch(k_matvec<PRO, EPI, 4>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
+    case 8: return launch(k_matvec<PRO, EPI, 8>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int DPL, typename KT>
+static cudaError_t launch_attention_g(const l3g_workspace* ws, const AttnArgs& a, cudaStream_t st,
+                                      dim3 grid, size_t smem) {
+  switch (ws->att_gp) {
+    case 1: return launch(k_attention<DPL, KT, 1>, grid, dim3(NTHREADS), smem, st, a);
+    case 2: return launch(k_attention<DPL, KT, 2>, grid, dim3(NTHREADS), smem, st, a);
+    case 4: return launch(k_attention<DPL, KT, 4>, grid, dim3(NTHREADS), smem, st, a);
+    case 8: return launch(k_attention<DPL, KT, 8>, grid, dim3(NTHREADS), smem, st, a);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 static cudaError_t launch_attention(const l3g_workspace* ws, const AttnArgs& a, cudaStream_t st) {
@@ -863,15 +920,14 @@ static cudaError_t launch_attention(const l3g_workspace* ws, const AttnArgs& a, 
   const int dpl = m->hd / 32;
   const size_t smem = ws->att_smem;
   if (m->kv_f16) {
-    if (dpl == 2) return launch(k_attention<2, __half>, grid, dim3(NTHREADS), smem, st, a);
-    if (dpl == 4) return launch(k_attention<4, __half>, grid, dim3(NTHREADS), smem, st, a);
-    if (dpl == 8) return launch(k_attention<8, __half>, grid, dim3(NTHREADS), smem, st, a);
+    if (dpl == 2) return launch_attention_g<2, __half>(ws, a, st, grid, smem);
+    if (dpl == 4) return launch_attention_g<4, __half>(ws, a, st, grid, smem);
     return cudaErrorInvalidValue;
   }
-  if (dpl == 1) return launch(k_attention<1, float>, grid, dim3(NTHREADS), smem, st, a);
-  if (dpl == 2) return launch(k_attention<2, float>, grid, dim3(NTHREADS), smem, st, a);
-  if (dpl == 4) return launch(k_attention<4, float>, grid, dim3(NTHREADS), smem, st, a);
-  return launch(k_attention<8, float>, grid, dim3(NTHREADS), smem, st, a);
+  if (dpl == 1) return launch_attention_g<1, float>(ws, a, st, grid, smem);
+  if (dpl == 2) return launch_attention_g<2, float>(ws, a, st, grid, smem);
+  if (dpl == 4) return launch_attention_g<4, float>(ws, a, st, grid, smem);
+  return cudaErrorInvalidValue;
 }
 
 // merges the per-rank argmax results gathered by NCCL (largest logit, lowest
@@ -903,14 +959,21 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
   const int ne = hp.n_emb, hd = m->hd;
   const size_t es = m->kv_f16 ? 2 : 4;
   ws->kernels = 0;
-#define KL(expr)  \
-  do {            \
-    CUDA_TRY(expr); \
-    ++ws->kernels; \
+#define KL(kind, expr)                                 \
+  do {                                                 \
+    CUDA_TRY(expr);                                    \
+    ++ws->kernels;                                     \
+    if (ws->profiling) {                               \
+      cudaEvent_t ev_;                                 \
+      CUDA_TRY(cudaEventCreate(&ev_));                 \
+      CUDA_TRY(cudaEventRecord(ev_, st));              \
+      ws->prof_kind.push_back(kind);                   \
+      ws->prof_ev.push_back(ev_);                      \
+    }                                                  \
   } while (0)
   if (variant != V_GREEDY_DEV)
     CUDA_TRY(cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, st));
-  KL(launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
+  KL(L3G_K_EMBED, launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
                   hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res));
   for (int l = 0; l < hp.n_layers; ++l) {
     const LayerW& L = m->layers[l];
@@ -936,7 +999,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.kc = kc;
       a.vc = vc;
       a.res = ws->d_res;
-      KL((launch_mv<PRO_RMS, EPI_QKV>(L.qkv, a, m->nsm, st)));
+      KL(L3G_K_QKV, (launch_mv<PRO_RMS, EPI_QKV>(L.qkv, a, m->nsm, st)));
     }
     {  // attention, infer.go:130-175
       AttnArgs a{};
@@ -957,14 +1020,14 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.counters = ws->att_cnt;
       a.out = ws->attn;
       a.res = ws->d_res;
-      KL(launch_attention(ws, a, st));
+      KL(L3G_K_ATTN, launch_attention(ws, a, st));
     }
     {  // act-quant -> Wo, infer.go:178-187 (residual add fused downstream)
       MatvecArgs a = mv_args(L.wo);
       a.x_in = ws->attn;
       a.out = ws->y;
       a.res = ws->d_res;
-      KL((launch_mv<PRO_QUANT, EPI_STORE>(L.wo, a, m->nsm, st)));
+      KL(L3G_K_WO, (launch_mv<PRO_QUANT, EPI_STORE>(L.wo, a, m->nsm, st)));
     }
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));
@@ -977,14 +1040,14 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.eps = hp.rms_eps;
       a.out = ws->act;
       a.res = ws->d_res;
-      KL((launch_mv<PRO_RMS, EPI_SWIGLU>(L.upgate, a, m->nsm, st)));
+      KL(L3G_K_UPGATE, (launch_mv<PRO_RMS, EPI_SWIGLU>(L.upgate, a, m->nsm, st)));
     }
     {  // act-quant -> down, infer.go:233-242
       MatvecArgs a = mv_args(L.down);
       a.x_in = ws->act;
       a.out = ws->y;
       a.res = ws->d_res;
-      KL((launch_mv<PRO_QUANT, EPI_STORE>(L.down, a, m->nsm, st)));
+      KL(L3G_K_DOWN, (launch_mv<PRO_QUANT, EPI_STORE>(L.down, a, m->nsm, st)));
     }
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));
@@ -1003,11 +1066,11 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     a.am_idx = ws->am_idx;
     a.am_counter = ws->am_cnt;
     a.res = ws->d_res;
-    KL((launch_mv<PRO_RMS, EPI_LOGITS>(m->logits, a, m->nsm, st)));
+    KL(L3G_K_LOGITS, (launch_mv<PRO_RMS, EPI_LOGITS>(m->logits, a, m->nsm, st)));
     const float* full = ws->logits;
     if (m->world > 1) {
       NCCL_TRY(nccl()->AllGather(ws->d_res, ws->d_gather, sizeof(Result) / 4, ncclInt32, m->comm, st));
-      KL(launch(k_merge_argmax, dim3(1), dim3(32), 0, st, (const Result*)ws->d_gather,
+      KL(L3G_K_OTHER, launch(k_merge_argmax, dim3(1), dim3(32), 0, st, (const Result*)ws->d_gather,
                       m->world, ws->d_res));
       if (variant == V_LOGITS || variant == V_TOPK) {
         NCCL_TRY(nccl()->AllGather(ws->logits, ws->logits_full, m->v_l, ncclFloat, m->comm, st));
@@ -1020,10 +1083,10 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     if (variant == V_TOPK) {
       const int nv = hp.vocab_size;
       const int chunks = (nv + TOPK_CHUNK - 1) / TOPK_CHUNK;
-      KL(launch(k_topk_partial, dim3(chunks), dim3(512), 0, st, full, nv, k, 0, ws->tk_part));
+      KL(L3G_K_OTHER, launch(k_topk_partial, dim3(chunks), dim3(512), 0, st, full, nv, k, 0, ws->tk_part));
       int cap = 1;
       while (cap < chunks * k) cap <<= 1;
-      KL(launch(k_topk_final, dim3(1), dim3(1024), (size_t)cap * 8, st,
+      KL(L3G_K_OTHER, launch(k_topk_final, dim3(1), dim3(1024), (size_t)cap * 8, st,
                       (const uint64_t*)ws->tk_part, chunks * k, cap, k, ws->d_tk_ids,
                       ws->d_tk_logits));
       CUDA_TRY(cudaMemcpyAsync(ws->h_tk_ids, ws->d_tk_ids, k * 4, cudaMemcpyDeviceToHost, st));
@@ -1031,7 +1094,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     }
   }
   if (variant == V_GREEDY_DEV)
-    KL(launch(k_advance, dim3(1), dim3(32), 0, st, ws->d_io, (const Result*)ws->d_res,
+    KL(L3G_K_OTHER, launch(k_advance, dim3(1), dim3(32), 0, st, ws->d_io, (const Result*)ws->d_res,
               ws->d_tokens));
   else
     CUDA_TRY(cudaMemcpyAsync(ws->h_res, ws->d_res, sizeof(Result), cudaMemcpyDeviceToHost, st));
@@ -1201,6 +1264,55 @@ extern "C" int l3g_decode_greedy(l3g_model* m, l3g_state* s, l3g_workspace* ws,
   if (device_ms) *device_ms = ms;
   ws->logits_valid = true;
   s->pos += n;
+  return L3G_OK;
+}
+
+extern "C" int l3g_profile_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token,
+                                int32_t* kinds, float* us, int32_t* n) {
+  if (!m || !s || !ws || !kinds || !us || !n) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (s->m != m || ws->m != m)
+    return l3g_fail(L3G_E_INVALID, "state or workspace belongs to another model");
+  if (s->pos >= s->ctx) return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+  if (ws->ctx < s->ctx)
+    return l3g_fail(L3G_E_INVALID, "workspace ctxLen=%d < state ctxLen=%d", ws->ctx, s->ctx);
+  if (token < 0 || token >= m->hp.vocab_size)
+    return l3g_fail(L3G_E_TOKEN, "token out of range: %d", token);
+  CUDA_TRY(cudaSetDevice(m->device));
+  cudaEvent_t e0;
+  CUDA_TRY(cudaEventCreate(&e0));
+  ws->h_io[0] = token;
+  ws->h_io[1] = s->pos;
+  ws->profiling = true;
+  g_serialize = true;
+  int rc = L3G_OK;
+  cudaError_t e = cudaEventRecord(e0, ws->stream);
+  if (e == cudaSuccess) rc = enqueue_step(ws, s, V_ARGMAX, 0);
+  g_serialize = false;
+  ws->profiling = false;
+  if (e == cudaSuccess && rc == L3G_OK) e = cudaStreamSynchronize(ws->stream);
+  const int cnt = (int)ws->prof_ev.size();
+  if (e == cudaSuccess && rc == L3G_OK) {
+    cudaEvent_t prev = e0;
+    for (int i = 0; i < cnt && i < *n; ++i) {
+      float ms = 0.0f;
+      cudaEventElapsedTime(&ms, prev, ws->prof_ev[i]);
+      kinds[i] = ws->prof_kind[i];
+      us[i] = ms * 1000.0f;
+      prev = ws->prof_ev[i];
+    }
+  }
+  for (auto ev : ws->prof_ev) cudaEventDestroy(ev);
+  ws->prof_ev.clear();
+  ws->prof_kind.clear();
+  cudaEventDestroy(e0);
+  if (rc) return rc;
+  if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "profile step: %s", cudaGetErrorString(e));
+  if (ws->h_res->err) {
+    cudaMemset(ws->d_res, 0, sizeof(Result));
+    return l3g_fail(L3G_E_DEVICE, "device check failed during profiling");
+  }
+  *n = std::min(cnt, *n);
+  s->pos++;
   return L3G_OK;
 }
 

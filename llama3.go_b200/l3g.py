@@ -109,6 +109,8 @@ def lib():
         "l3g_decode_greedy": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.POINTER(C.c_int32),
                                         C.POINTER(C.c_float)]),
         "l3g_workspace_kernels_per_step": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+        "l3g_profile_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_float),
+                                       C.POINTER(C.c_int32)]),
         "l3g_matrix_upload": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_P)]),
         "l3g_matvec_q8": (C.c_int, [_P, _P, _P, _P, C.c_int32, C.c_int32, _P]),
         "l3g_matrix_free": (None, [_P]),
@@ -249,6 +251,17 @@ class Model:
         arr = np.ascontiguousarray(tokens, dtype=np.int32)
         _check(lib().l3g_prefill(self._h, s._h, _ws(ws), arr.ctypes.data_as(C.POINTER(C.c_int32)),
                                  arr.size))
+
+    KERNEL_KINDS = ("embed", "qkv_rope_kv", "attention", "wo", "upgate_swiglu", "down", "logits_argmax",
+                    "other")
+
+    def ProfileStep(self, s: "State", token: int, ws: "Workspace", cap: int = 4096):
+        """One step run eagerly with every kernel timed alone: [(kind, us)]."""
+        kinds = (C.c_int32 * cap)()
+        us = (C.c_float * cap)()
+        n = C.c_int32(cap)
+        _check(lib().l3g_profile_step(self._h, s._h, _ws(ws), int(token), kinds, us, C.byref(n)))
+        return [(self.KERNEL_KINDS[kinds[i]], float(us[i])) for i in range(n.value)]
 
     def DecodeGreedy(self, s: "State", first_token: int, n: int, ws: "Workspace"):
         """n greedy steps fed on the device; returns (tokens, device_ms)."""
