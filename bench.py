@@ -285,6 +285,42 @@ def time_matvec_kernel(l3g, cfg, seed, hbm):
             "bytes_per_launch": alg, "ms_per_launch": ms, "achieved_gbs": alg / ms / 1e6}
 
 
+def trace_summary(m, s, ws, tok, pos, reps=3):
+    """Device timeline of one step replayed as its graph (kernels overlapping
+    as in the timed loop): per kind, the time between consecutive kernel
+    completions (sums to the step), the span from entry to exit, and the
+    time from dependency release to the end of the prologue."""
+    import numpy as np
+    acc = {}
+    step_us = []
+    for _ in range(reps):
+        s.Pos = pos
+        recs = [(k, st) for k, st in m.TraceStep(s, tok, ws) if (st[:, 0] > 0).any()]
+        first = min(st[:, 0][st[:, 0] > 0].min() for _, st in recs)
+        prev_exit = first
+        for kind, st in recs:
+            live = st[:, 0] > 0
+            ent = st[live, 0].min()
+            ext = st[live, 4].max()
+            released = st[live, 1].min()
+            d = acc.setdefault(kind, {"critical": 0.0, "span": 0.0, "prologue": 0.0, "wake": 0.0, "n": 0})
+            d["critical"] += (ext - prev_exit) / 1e3
+            d["span"] += (ext - ent) / 1e3
+            d["wake"] += max(0, released - prev_exit) / 1e3
+            pro = st[live, 2]
+            if (pro > 0).all():
+                d["prologue"] += (pro.max() - released) / 1e3
+            d["n"] += 1
+            prev_exit = max(prev_exit, ext)
+        step_us.append((prev_exit - first) / 1e3)
+    out = {k: {"critical_us": round(v["critical"] / reps, 1), "avg_span_us": round(v["span"] / v["n"], 2),
+               "avg_wake_us": round(v["wake"] / v["n"], 2), "avg_prologue_us": round(v["prologue"] / v["n"], 2),
+               "launches": v["n"] // reps}
+           for k, v in sorted(acc.items(), key=lambda kv: -kv[1]["critical"])}
+    out["traced_step_us"] = round(float(np.mean(step_us)), 1)
+    return out
+
+
 def run_l3g(args):
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -354,6 +390,7 @@ def run_l3g(args):
             prof[kind] = prof.get(kind, 0.0) + us / 3
         s.Pos = p0 + max(1, args.warmup)
     prof = {k: round(v, 1) for k, v in sorted(prof.items(), key=lambda kv: -kv[1])}
+    timeline = trace_summary(m, s, ws, tok, p0 + max(1, args.warmup))
 
     # roofline of the whole decode step (weights + KV read per token)
     es = 2 if args.kv == "f16" else 4
@@ -397,6 +434,7 @@ def run_l3g(args):
         "gpu_launches": kernels * args.steps,
         "kernels_per_step": kernels,
         "step_profile_us": prof,
+        "step_timeline_us": timeline,
         "clocks": clocks,
         "prefill_s": round(prefill_s, 3),
     }

@@ -209,6 +209,16 @@ int l3g_workspace_kernels_per_step(l3g_workspace *ws, int32_t *n);
 #define L3G_K_OTHER 7
 int l3g_profile_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                      int32_t token, int32_t *kinds, float *us, int32_t *n);
+/* Device timeline of one greedy step replayed as its CUDA graph (kernels
+ * overlapping as in production): for each launch i, kinds[i] (L3G_K_*) and
+ * stamps[(i * L3G_TRACE_CTAS + cta) * 8 + e] = %globaltimer (ns) of CTA cta
+ * at e = {entry, dependency wait done, prologue done, tile loop done, exit};
+ * zero where a launch or CTA records nothing.  Advances the position by one.
+ * *n is the capacity in launches on entry and the count on return. */
+#define L3G_TRACE_CTAS 256
+int l3g_trace_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                   int32_t token, uint64_t *stamps, int32_t *kinds,
+                   int32_t *n);
 
 /* ---- Q8_0 matvec drop-in: matvec_q8_c (simd.h:8) / matVecQ8_0 ------------ */
 /* Uploads a GGUF Q8_0 matrix (rows x cols, 34-byte blocks, host bytes). */

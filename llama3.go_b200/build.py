@@ -17,8 +17,13 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libl3g.so")
 SOURCES = [os.path.join(CSRC, f) for f in ("l3g_runtime.cu", "l3g_gguf.cpp")]
-DEPS = SOURCES + [os.path.join(CSRC, f) for f in ("l3g_kernels.cuh", "l3g_internal.h")] + [
-    os.path.join(ROOT, "include", "l3g.h")]
+
+
+def deps():
+    """Every source and header the library is built from."""
+    files = [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC))
+             if f.endswith((".cu", ".cuh", ".cpp", ".h"))]
+    return files + [os.path.join(ROOT, "include", "l3g.h"), os.path.abspath(__file__)]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -33,7 +38,7 @@ def stale() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    return any(os.path.getmtime(d) > t for d in DEPS)
+    return any(os.path.getmtime(d) > t for d in deps())
 
 
 def build(force: bool = False, ptxas_verbose: bool = False, quiet: bool = False) -> str:

@@ -1,10 +1,11 @@
 // Split-K GQA attention of libl3g (included by l3g_kernels.cuh), the
 // attention loop of ForwardIntoWorkspace (internal/llama/infer.go:130-175).
 //
+// The KV cache interleaves K and V per position: [kv head][pos][K hd | V hd].
 // Grid (local kv heads, splits).  CTA (g, s) takes a contiguous range of
 // positions of kv head g for the `group` query heads sharing it, streams the
-// K and V rows of P positions per stage through a shared-memory ring (two
-// ~16 KB bulk copies per stage), and keeps an online softmax per warp:
+// K|V rows of P positions per stage through a shared-memory ring (one ~32 KB
+// bulk copy per stage), and keeps an online softmax per warp:
 //   - lanes split the head dimension (DPL = hd / 32 values each);
 //   - a warp takes NBW = P / 8 positions of each stage in sub-batches of
 //     32 / GP positions (GP = group rounded up to a power of two), computes
@@ -18,8 +19,7 @@
 
 struct AttnArgs {
   const float* q;     // [local q heads][hd], roped
-  const void* kc;     // this layer [local kv heads][ctx][hd]
-  const void* vc;
+  const void* kv;     // this layer [local kv heads][ctx][2][hd]
   int ctx, hd, group, n_splits, P, nstages, stage_bytes;
   float scale;        // float32(1/sqrt(hd)), infer.go:130
   const int* io;      // io[1] = position of this token
@@ -28,6 +28,8 @@ struct AttnArgs {
   unsigned* counters; // [kv heads], zero between launches
   float* out;         // [local q heads][hd]
   Result* res;
+  unsigned long long* trace;  // device timeline (nullptr: off)
+  int trace_seq;
 };
 
 struct AttnSmem {
@@ -103,8 +105,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int chunk = align_up((n + S - 1) / S, P);
   const int t0 = min(n, split * chunk), t1 = min(n, t0 + chunk);
   const int nst = (t1 - t0 + P - 1) / P;
-  const size_t head_off = (size_t)kvh * a.ctx * hd;
-  const int half_stage = a.stage_bytes / 2;
+  const size_t head_off = (size_t)kvh * a.ctx * 2 * hd;
+  const int row = 2 * hd;  // elements per position: K then V
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
@@ -117,6 +119,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   __syncthreads();
   pdl_launch_dependents();
+  trace_mark(a.trace, a.trace_seq, TR_ENTRY);
 
   if (warp == NW) {
     if (lane == 0) {
@@ -133,13 +136,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           pdl_wait();
           waited = true;
         }
-        const uint32_t bytes = (uint32_t)((tb - ta) * hd * sizeof(KT));
-        const size_t off = (head_off + (size_t)ta * hd) * sizeof(KT);
-        mbar_arrive_expect_tx(&sh->full[s], 2 * bytes);
+        const uint32_t bytes = (uint32_t)((tb - ta) * row * sizeof(KT));
+        const size_t off = (head_off + (size_t)ta * row) * sizeof(KT);
+        mbar_arrive_expect_tx(&sh->full[s], bytes);
         bulk_g2s(ring + (size_t)s * a.stage_bytes,
-                 static_cast<const uint8_t*>(a.kc) + off, bytes, &sh->full[s]);
-        bulk_g2s(ring + (size_t)s * a.stage_bytes + half_stage,
-                 static_cast<const uint8_t*>(a.vc) + off, bytes, &sh->full[s]);
+                 static_cast<const uint8_t*>(a.kv) + off, bytes, &sh->full[s]);
         *(volatile int*)&sh->issued = st + 1;
       }
     }
@@ -147,6 +148,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 
   pdl_wait();  // q comes from the previous kernel
+  trace_mark(a.trace, a.trace_seq, TR_WAITED);
   float q[GP][DPL];
 #pragma unroll
   for (int h = 0; h < GP; ++h)
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       consumed = st + 1;
       const int cnt = min(t1, t0 + st * P + P) - (t0 + st * P);
       const KT* Ks = reinterpret_cast<const KT*>(ring + (size_t)s * a.stage_bytes);
-      const KT* Vs = reinterpret_cast<const KT*>(ring + (size_t)s * a.stage_bytes + half_stage);
+      const KT* Vs = Ks + hd;
       for (int sb = 0; sb < nbw; sb += SB) {
         const int p0 = warp * nbw + sb;      // first position of the sub-batch
         const int np = min(SB, nbw - sb);    // positions of this warp in it
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int p = 0; p < SB; ++p) {
           float kv[DPL];
           if (p < np && p0 + p < cnt) {
-            load_row<DPL, KT>(Ks + (size_t)(p0 + p) * hd + lane * DPL, kv);
+            load_row<DPL, KT>(Ks + (size_t)(p0 + p) * row + lane * DPL, kv);
           } else {
 #pragma unroll
             for (int j = 0; j < DPL; ++j) kv[j] = 0.0f;
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int p = 0; p < np && p0 + p < cnt; ++p) {
           float vv[DPL];
-          load_row<DPL, KT>(Vs + (size_t)(p0 + p) * hd + lane * DPL, vv);
+          load_row<DPL, KT>(Vs + (size_t)(p0 + p) * row + lane * DPL, vv);
 #pragma unroll
           for (int h = 0; h < GP; ++h) {
             const float w = pbuf[p * GP + h];
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) mbar_arrive(&sh->empty[s]);
   }
 
+  trace_mark(a.trace, a.trace_seq, TR_LOOP);
   // drain after an abort, then reuse the ring as merge scratch
   if (*(volatile int*)&sh->abort_flag && threadIdx.x == 0) {
     const int issued = *(volatile int*)&sh->issued;
@@ -292,34 +295,77 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       a.part_ml[(pbase + h) * 2 + 1] = L;
     }
   }
-  __threadfence();
+  // publish: the CTA barrier orders every thread's partial stores before
+  // thread 0's device-scope fence and count (release); the CTA that brings
+  // the count to S fences again before reading the others' partials (acquire)
   consumer_sync();
   if (threadIdx.x == 0) {
+    __threadfence();
     const unsigned prev = atomicAdd(a.counters + kvh, 1u);
-    sh->last = prev == (unsigned)S - 1;
+    const bool last = prev == (unsigned)S - 1;
+    if (last) __threadfence();
+    sh->last = last;
   }
   consumer_sync();
-  if (!*(volatile int*)&sh->last) return;
-  __threadfence();
-  // merge the splits: their (m, l) pairs into shared memory first, then each
-  // (head, dim) issues its partial-output loads back to back
-  float* sm_split = sm_ml;  // [S][G][2] (the ring holds S * G * 2 floats)
+  trace_mark(a.trace, a.trace_seq, 5);  // partial published
+  if (!*(volatile int*)&sh->last) {
+    trace_mark(a.trace, a.trace_seq, TR_EXIT);
+    return;
+  }
+  // Merge the splits of this kv head.  Their (m, l) pairs, then the split
+  // weights e_s = exp(m_s - M) per head, go to shared memory; the partial
+  // outputs are staged through the ring in chunks of splits with every
+  // thread's 16-byte loads in flight at once, and accumulated in split order.
+  const int gh = G * hd;
+  float* sm_split = reinterpret_cast<float*>(ring);             // [S][G][2]
+  float* sm_w = sm_split + align_up(S * G * 2, 4);              // [S][G] weights
+  float* sm_tot = sm_w + align_up(S * G, 4);                    // [G] sum of l_s e_s
+  float* sm_part = sm_tot + align_up(MAXG, 4);                  // [chunk][G][hd]
   for (int i = threadIdx.x; i < S * G * 2; i += NW * 32)
     sm_split[i] = __ldcg(a.part_ml + (size_t)kvh * S * G * 2 + i);
   consumer_sync();
-  for (int idx = threadIdx.x; idx < G * hd; idx += NW * 32) {
-    const int h = idx / hd, d = idx % hd;
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
     float M = -INFINITY;
     for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, sm_split[(s2 * G + h) * 2]);
-    float L = 0.0f, O = 0.0f;
-#pragma unroll 8
+    float L = 0.0f;
     for (int s2 = 0; s2 < S; ++s2) {
       const float ms = sm_split[(s2 * G + h) * 2];
       const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
+      sm_w[s2 * G + h] = e;
       L = fmaf(sm_split[(s2 * G + h) * 2 + 1], e, L);
-      O = fmaf(__ldcg(a.part_o + (((size_t)kvh * S + s2) * G + h) * hd + d), e, O);
     }
-    a.out[((size_t)kvh * G + h) * hd + d] = __fmul_rn(O, __fdiv_rn(1.0f, L));
+    sm_tot[h] = L;
+  }
+  const int ring_bytes = a.nstages * a.stage_bytes;
+  const int used = (int)((reinterpret_cast<uint8_t*>(sm_part) - ring));
+  const int chunk_s = max(1, (ring_bytes - used) / (gh * 4));
+  float acc2[4] = {0.f, 0.f, 0.f, 0.f};  // outputs idx = threadIdx.x + k * 256
+  for (int c0 = 0; c0 < S; c0 += chunk_s) {
+    const int cs = min(chunk_s, S - c0);
+    consumer_sync();  // previous chunk consumed (and sm_w ready)
+    const float4* src = reinterpret_cast<const float4*>(a.part_o + ((size_t)kvh * S + c0) * gh);
+    float4* dst = reinterpret_cast<float4*>(sm_part);
+    const int n4 = cs * gh / 4;
+    for (int i = threadIdx.x; i < n4; i += NW * 32) dst[i] = __ldcg(src + i);
+    consumer_sync();
+    trace_mark(a.trace, a.trace_seq, 6);  // split partials staged
+    for (int k = 0; k < 4; ++k) {
+      const int idx = threadIdx.x + k * NW * 32;
+      if (idx >= gh) break;
+      const int h = idx / hd;
+      float O = acc2[k];
+      for (int s2 = 0; s2 < cs; ++s2) O = fmaf(sm_part[s2 * gh + idx], sm_w[(c0 + s2) * G + h], O);
+      acc2[k] = O;
+    }
+  }
+  trace_mark(a.trace, a.trace_seq, 7);  // merged
+  for (int k = 0; k < 4; ++k) {
+    const int idx = threadIdx.x + k * NW * 32;
+    if (idx >= gh) break;
+    const int h = idx / hd;
+    a.out[(size_t)kvh * gh + idx] = __fmul_rn(acc2[k], __fdiv_rn(1.0f, sm_tot[h]));
   }
   if (threadIdx.x == 0) a.counters[kvh] = 0u;
+  trace_mark(a.trace, a.trace_seq, TR_EXIT);
 }

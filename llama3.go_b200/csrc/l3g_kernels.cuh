@@ -103,6 +103,20 @@ __device__ __forceinline__ uint64_t gtime() {
   return t;
 }
 
+// Device timeline (off when tr == nullptr): thread 0 of every CTA (up to
+// TRACE_CTAS per launch) stamps %globaltimer at a few points; launch `seq` of
+// the step owns tr[(seq * TRACE_CTAS + cta) * 8 + event].
+enum { TR_ENTRY = 0, TR_WAITED = 1, TR_PROLOGUE = 2, TR_LOOP = 3, TR_EXIT = 4 };
+constexpr int TRACE_CTAS = 256;
+__device__ __forceinline__ void trace_mark(unsigned long long* tr, int seq, int ev) {
+  if (tr == nullptr || threadIdx.x != 0) return;
+  const unsigned lin = blockIdx.x + blockIdx.y * gridDim.x;
+  if (lin >= (unsigned)TRACE_CTAS) return;
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  tr[((size_t)seq * TRACE_CTAS + lin) * 8 + ev] = t;
+}
+
 __device__ __forceinline__ void report(Result* res, int code, int where) {
   if (atomicCAS(&res->err, 0, code) == 0) atomicExch(&res->where, where);
 }

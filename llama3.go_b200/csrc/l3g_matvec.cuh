@@ -36,14 +36,15 @@ struct MatvecArgs {
   const float* rope_cos;  // [ctx][rope_half]
   const float* rope_sin;
   const int* io;          // io[0] token, io[1] position
-  void* kc;               // this layer's K cache [kv heads][ctx][hd]
-  void* vc;
+  void* kv;               // this layer's KV cache [kv heads][ctx][2][hd] (K|V)
   // EPI_LOGITS: fused argmax
   int row_offset;         // vocab id of local row 0
   float* am_val;          // [gridDim.x] per-CTA best
   int* am_idx;
   unsigned* am_counter;   // zero between launches
   Result* res;            // error word, argmax result
+  unsigned long long* trace;  // device timeline (nullptr: off)
+  int trace_seq;
 };
 
 // Row-group partial sums: a ring of slots, one per group in flight.  Warps
@@ -72,9 +73,11 @@ __host__ __device__ __forceinline__ int mv_smem_bytes(int cols, int nstages,
          nstages * tile_bytes;
 }
 
-template <int PRO>
+// VK: float4 of the input row per thread for PRO_RMS (C <= 1024 * VK).
+template <int PRO, int VK>
 __device__ __forceinline__ void mv_prologue(const MatvecArgs& a, float* xd,
-                                            int8_t* xqs, MatvecSmem* sh) {
+                                            int8_t* xqs, MatvecSmem* sh,
+                                            const float4 (&w)[VK]) {
   const int C = a.w.cols;
   const int nb = C >> 5;
   const int tid = threadIdx.x;  // < NW*32
@@ -84,70 +87,93 @@ __device__ __forceinline__ void mv_prologue(const MatvecArgs& a, float* xd,
     for (int i = tid * 16; i < C; i += NW * 32 * 16)
       *reinterpret_cast<int4*>(xqs + i) =
           *reinterpret_cast<const int4*>(a.xqs_in + i);
+  } else if constexpr (PRO == PRO_QUANT) {
+    // Element i of float4 k of thread t is x[4 * (t + 256 k) + i]; eight
+    // consecutive threads cover one 32-value block.  Loads run one chunk of
+    // four float4 ahead of the quantization (a register double buffer), so
+    // the L2 round trips overlap instead of serializing.
+    const int nv = C >> 2;
+    const int nk = (nv + NW * 32 - 1) / (NW * 32);
+    const float4* x4 = reinterpret_cast<const float4*>(a.x_in);
+    auto ld = [&](int k) {
+      const int i = tid + k * NW * 32;
+      return (k < nk && i < nv) ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    auto qz = [&](const float4& u, int k) {
+      if (k < nk) {  // uniform over the CTA
+        const int i = tid + k * NW * 32;
+        quant_quad(u, i < nv, i >> 3, lane & 7, xd, xqs);
+      }
+    };
+    float4 a0 = ld(0), a1 = ld(1), a2 = ld(2), a3 = ld(3);
+    for (int c = 0; c < nk; c += 8) {
+      const float4 b0 = ld(c + 4), b1 = ld(c + 5), b2 = ld(c + 6), b3 = ld(c + 7);
+      qz(a0, c);
+      qz(a1, c + 1);
+      qz(a2, c + 2);
+      qz(a3, c + 3);
+      a0 = ld(c + 8);
+      a1 = ld(c + 9);
+      a2 = ld(c + 10);
+      a3 = ld(c + 11);
+      qz(b0, c + 4);
+      qz(b1, c + 5);
+      qz(b2, c + 6);
+      qz(b3, c + 7);
+    }
+    trace_mark(a.trace, a.trace_seq, 7);  // quantized
   } else {
-    // Every thread issues all of its float4 loads before using any, so the
-    // prologue costs one L2 round trip; element i of float4 k of thread t is
-    // x[4 * (t + k * 256) + i], and 8 consecutive threads cover one block.
-    constexpr int MAXK = PRO == PRO_RMS ? 8 : 16;  // C <= 8192 / 16384
+    // residual add (infer.go:189-191 / :244-246), rmsNorm (math.go:5-14),
+    // then the block quantization; w (the norm weights, loaded before the
+    // dependency wait) and v hold this thread's VK float4 of the row.
     const int nv = C >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(a.x_in);
-    float4 v[MAXK];
+    const float4* y4 = reinterpret_cast<const float4*>(a.y_in);
+    float4 v[VK], y[VK];
 #pragma unroll
-    for (int k = 0; k < MAXK; ++k) {
+    for (int k = 0; k < VK; ++k) {
       const int i = tid + k * NW * 32;
       v[k] = i < nv ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      y[k] = (a.y_in && i < nv) ? y4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    float scale = 1.0f;
-    float4 w[PRO == PRO_RMS ? MAXK : 1];
-    if constexpr (PRO == PRO_RMS) {
-      // residual add (infer.go:189-191 / :244-246) then rmsNorm (math.go:5-14)
-      const float4* y4 = reinterpret_cast<const float4*>(a.y_in);
-      const float4* w4 = reinterpret_cast<const float4*>(a.norm_w);
-      float4 y[MAXK];
+    const bool wx = a.x_out != nullptr && blockIdx.x == 0;
+    float ss = 0.0f;
 #pragma unroll
-      for (int k = 0; k < MAXK; ++k) {
-        const int i = tid + k * NW * 32;
-        y[k] = (a.y_in && i < nv) ? y4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        w[k] = i < nv ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < VK; ++k) {
+      const int i = tid + k * NW * 32;
+      if (a.y_in) {
+        v[k].x = __fadd_rn(v[k].x, y[k].x);
+        v[k].y = __fadd_rn(v[k].y, y[k].y);
+        v[k].z = __fadd_rn(v[k].z, y[k].z);
+        v[k].w = __fadd_rn(v[k].w, y[k].w);
       }
-      const bool wx = a.x_out != nullptr && blockIdx.x == 0;
-      float ss = 0.0f;
-#pragma unroll
-      for (int k = 0; k < MAXK; ++k) {
-        const int i = tid + k * NW * 32;
-        if (a.y_in) {
-          v[k].x = __fadd_rn(v[k].x, y[k].x);
-          v[k].y = __fadd_rn(v[k].y, y[k].y);
-          v[k].z = __fadd_rn(v[k].z, y[k].z);
-          v[k].w = __fadd_rn(v[k].w, y[k].w);
-        }
-        if (wx && i < nv) reinterpret_cast<float4*>(a.x_out)[i] = v[k];
-        ss = fmaf(v[k].x, v[k].x, ss);
-        ss = fmaf(v[k].y, v[k].y, ss);
-        ss = fmaf(v[k].z, v[k].z, ss);
-        ss = fmaf(v[k].w, v[k].w, ss);
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) sh->ssred[warp] = ss;
-      consumer_sync();
-      float tot = 0.0f;
-#pragma unroll
-      for (int q = 0; q < NW; ++q) tot += sh->ssred[q];
-      scale = (float)(1.0 / sqrt((double)__fadd_rn(__fdiv_rn(tot, (float)C), a.eps)));
+      if (wx && i < nv) reinterpret_cast<float4*>(a.x_out)[i] = v[k];
+      ss = fmaf(v[k].x, v[k].x, ss);
+      ss = fmaf(v[k].y, v[k].y, ss);
+      ss = fmaf(v[k].z, v[k].z, ss);
+      ss = fmaf(v[k].w, v[k].w, ss);
     }
+    trace_mark(a.trace, a.trace_seq, 5);  // inputs loaded
+    ss = warp_sum(ss);
+    if (lane == 0) sh->ssred[warp] = ss;
+    consumer_sync();
+    float tot = 0.0f;
 #pragma unroll
-    for (int k = 0; k < MAXK; ++k) {
+    for (int q = 0; q < NW; ++q) tot += sh->ssred[q];
+    const float scale = (float)(1.0 / sqrt((double)__fadd_rn(__fdiv_rn(tot, (float)C), a.eps)));
+    trace_mark(a.trace, a.trace_seq, 6);  // scale known
+#pragma unroll
+    for (int k = 0; k < VK; ++k) {
       const int i = tid + k * NW * 32;
       if (k * NW * 32 >= nv) break;  // uniform: nv is a multiple of 8
       float4 u = v[k];
-      if constexpr (PRO == PRO_RMS) {
-        u.x = __fmul_rn(__fmul_rn(u.x, scale), w[k].x);
-        u.y = __fmul_rn(__fmul_rn(u.y, scale), w[k].y);
-        u.z = __fmul_rn(__fmul_rn(u.z, scale), w[k].z);
-        u.w = __fmul_rn(__fmul_rn(u.w, scale), w[k].w);
-      }
+      u.x = __fmul_rn(__fmul_rn(u.x, scale), w[k].x);
+      u.y = __fmul_rn(__fmul_rn(u.y, scale), w[k].y);
+      u.z = __fmul_rn(__fmul_rn(u.z, scale), w[k].z);
+      u.w = __fmul_rn(__fmul_rn(u.w, scale), w[k].w);
       quant_quad(u, i < nv, i >> 3, lane & 7, xd, xqs);
     }
+    trace_mark(a.trace, a.trace_seq, 7);  // quantized
   }
 }
 
@@ -189,8 +215,8 @@ __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int n
         // KV append at this position, infer.go:122-127
         const int r2 = is_k ? row - a.nq : row - a.nq - a.nkv;
         const int kvh = r2 / hd, d = r2 % hd;
-        const size_t off = ((size_t)kvh * a.ctx + pos) * hd + d;
-        void* base = is_k ? a.kc : a.vc;
+        const size_t off = (((size_t)kvh * a.ctx + pos) * 2 + (is_k ? 0 : 1)) * hd + d;
+        void* base = a.kv;
         if (a.kv_f16)
           *reinterpret_cast<__half2*>(static_cast<__half*>(base) + off) =
               __floats2half2_rn(x0, x1);
@@ -235,7 +261,7 @@ __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int n
 // finishes those rows itself; with RPW == 1 the pairs of the RoPE and SwiGLU
 // epilogues span two warps, so the last warp to post its row of a group runs
 // the epilogue of the whole group (fixed order, no CTA barrier).
-template <int PRO, int EPI, int RPW>
+template <int PRO, int EPI, int RPW, int VK>
 __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     k_matvec(const __grid_constant__ MatvecArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -267,6 +293,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
   }
   __syncthreads();
   pdl_launch_dependents();
+  trace_mark(a.trace, a.trace_seq, TR_ENTRY);
 
   if (warp == NW) {  // producer: weights never depend on the previous kernel
     if (lane == 0) {
@@ -285,9 +312,19 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     return;
   }
 
+  // the norm weights are constants: fetch them before the dependency wait
+  float4 nw[VK];
+#pragma unroll
+  for (int k = 0; k < VK; ++k) {
+    const int i = threadIdx.x + k * NW * 32;
+    nw[k] = (PRO == PRO_RMS && i < C / 4) ? reinterpret_cast<const float4*>(a.norm_w)[i]
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   pdl_wait();  // activations come from the previous kernel
-  mv_prologue<PRO>(a, xd, xqs, sh);
+  trace_mark(a.trace, a.trace_seq, TR_WAITED);
+  mv_prologue<PRO, VK>(a, xd, xqs, sh, nw);
   consumer_sync();
+  trace_mark(a.trace, a.trace_seq, TR_PROLOGUE);
 
   const int nchunks = ck >> 4;
   const int nbk = ck >> 5;
@@ -356,6 +393,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
       }
     }
   }
+  trace_mark(a.trace, a.trace_seq, TR_LOOP);
 
   if constexpr (EPI == EPI_LOGITS) {
     // per-warp best -> per-CTA best -> the last CTA merges in a fixed order
@@ -422,5 +460,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
       mbar_wait(&sh->full[t % ns], (t / ns) & 1, &dummy, a.res, 3, 100000000ull);
     }
   }
+  trace_mark(a.trace, a.trace_seq, TR_EXIT);
 }
 

@@ -16,6 +16,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -128,25 +129,49 @@ static int sm_count(int dev) {
   return n > 0 ? n : 1;
 }
 
+// Dynamic shared memory may take what static shared memory leaves of the
+// per-block opt-in limit.
+template <typename K>
+static cudaError_t set_max_shared(K k, int limit) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, k);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             limit - (int)fa.sharedSizeBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
+  return e;
+}
+
 static int setup_kernels() {
   static int rc = -100;
   static std::once_flag once;
   std::call_once(once, [] {
     const int big = 227 * 1024;
     cudaError_t e = cudaSuccess;
+    // Every kernel asks for the largest shared-memory carveout: the SM's
+    // split is fixed while CTAs are resident, and the next kernel's CTA
+    // (programmatic dependent launch) only fits beside the current one when
+    // the SM already runs with the maximum shared memory.
 #define SETK(k) \
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, big)
-#define SETMV(P, E)                  \
-  SETK((k_matvec<P, E, 1>));         \
-  SETK((k_matvec<P, E, 2>));         \
-  SETK((k_matvec<P, E, 4>));         \
-  SETK((k_matvec<P, E, 8>))
-    SETMV(PRO_PREQ, EPI_STORE);
-    SETMV(PRO_QUANT, EPI_STORE);
-    SETMV(PRO_RMS, EPI_QKV);
-    SETMV(PRO_RMS, EPI_SWIGLU);
-    SETMV(PRO_RMS, EPI_LOGITS);
-#undef SETMV
+  if (e == cudaSuccess) e = set_max_shared(k, big)
+#define SETMV4(P, E, VK)             \
+  SETK((k_matvec<P, E, 1, VK>));     \
+  SETK((k_matvec<P, E, 2, VK>));     \
+  SETK((k_matvec<P, E, 4, VK>));     \
+  SETK((k_matvec<P, E, 8, VK>))
+#define SETRMS(E)      \
+  SETMV4(PRO_RMS, E, 2); \
+  SETMV4(PRO_RMS, E, 4); \
+  SETMV4(PRO_RMS, E, 8)
+    SETMV4(PRO_PREQ, EPI_STORE, 1);
+    SETMV4(PRO_QUANT, EPI_STORE, 1);
+    SETRMS(EPI_QKV);
+    SETRMS(EPI_SWIGLU);
+    SETRMS(EPI_LOGITS);
+#undef SETRMS
+#undef SETMV4
 #define SETAT(D, T)                  \
   SETK((k_attention<D, T, 1>));      \
   SETK((k_attention<D, T, 2>));      \
@@ -159,6 +184,9 @@ static int setup_kernels() {
     SETAT(4, __half);
 #undef SETAT
     SETK(k_topk_final);
+    SETK(k_embed);
+    SETK(k_advance);
+    SETK(k_topk_partial);
 #undef SETK
     rc = e == cudaSuccess ? 0 : (int)e;
   });
@@ -220,6 +248,11 @@ static Q8Tiles make_tiles(int rows, int cols, int rpw) {
 // first under tile_cost_ns, bounded below by the HBM time of the matrix;
 // ties go to fewer rows per warp.
 static Q8Tiles plan_tiles(int rows, int cols, int nsm) {
+  // L3G_RPW=1|2|4|8 pins the rows per warp (a tuning knob for experiments)
+  if (const char* env = getenv("L3G_RPW")) {
+    const int rpw = atoi(env);
+    if (rpw == 1 || rpw == 2 || rpw == 4 || rpw == 8) return make_tiles(rows, cols, rpw);
+  }
   Q8Tiles best{};
   double best_t = 1e300;
   for (int rpw : {1, 2, 4, 8}) {
@@ -607,9 +640,8 @@ extern "C" int l3g_model_hparams(const l3g_model* m, l3g_hparams* out) {
 struct l3g_state {
   l3g_model* m = nullptr;
   int ctx = 0, pos = 0;
-  void* kc = nullptr;
-  void* vc = nullptr;
-  size_t layer_elems = 0;  // per layer: local kv heads * ctx * hd
+  void* kv = nullptr;      // [layer][local kv head][ctx][K hd | V hd]
+  size_t layer_elems = 0;  // per layer: local kv heads * ctx * 2 * hd
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
   uint64_t serial = 0;
@@ -625,8 +657,7 @@ static uint64_t next_serial() {
 extern "C" void l3g_state_free(l3g_state* s) {
   if (!s) return;
   cudaSetDevice(s->m->device);
-  if (s->kc) cudaFree(s->kc);
-  if (s->vc) cudaFree(s->vc);
+  if (s->kv) cudaFree(s->kv);
   if (s->rope_cos) cudaFree(s->rope_cos);
   if (s->rope_sin) cudaFree(s->rope_sin);
   delete s;
@@ -642,13 +673,11 @@ extern "C" int l3g_state_new(l3g_model* m, int32_t ctx, l3g_state** out) {
   s->m = m;
   s->ctx = ctx;
   s->serial = next_serial();
-  s->layer_elems = (size_t)m->hkv_l * ctx * m->hd;
+  s->layer_elems = (size_t)m->hkv_l * ctx * 2 * m->hd;
   const size_t es = m->kv_f16 ? 2 : 4;
   const size_t kvb = s->layer_elems * m->hp.n_layers * es;
-  cudaError_t e = cudaMalloc(&s->kc, kvb);
-  if (e == cudaSuccess) e = cudaMalloc(&s->vc, kvb);
-  if (e == cudaSuccess) e = cudaMemset(s->kc, 0, kvb);
-  if (e == cudaSuccess) e = cudaMemset(s->vc, 0, kvb);
+  cudaError_t e = cudaMalloc(&s->kv, kvb);
+  if (e == cudaSuccess) e = cudaMemset(s->kv, 0, kvb);
   // RoPE tables, NewRopeCache rope.go:27-34 (f64 angles, f32 tables)
   const int half = m->rope_half;
   std::vector<float> c((size_t)ctx * half), sn((size_t)ctx * half);
@@ -699,22 +728,22 @@ extern "C" int l3g_state_read_kv(const l3g_state* s, int32_t layer, int32_t pos0
   CUDA_TRY(cudaSetDevice(m->device));
   const int hd = m->hd, nh = m->hkv_l;
   const size_t es = m->kv_f16 ? 2 : 4;
-  std::vector<uint8_t> kb((size_t)npos * hd * es), vb(kb.size());
+  std::vector<uint8_t> buf((size_t)npos * 2 * hd * es);
   for (int h = 0; h < nh; ++h) {
-    const size_t off = ((size_t)layer * s->layer_elems + ((size_t)h * s->ctx + pos0) * hd) * es;
-    CUDA_TRY(cudaMemcpy(kb.data(), static_cast<uint8_t*>(s->kc) + off, kb.size(),
-                        cudaMemcpyDeviceToHost));
-    CUDA_TRY(cudaMemcpy(vb.data(), static_cast<uint8_t*>(s->vc) + off, vb.size(),
+    const size_t off =
+        ((size_t)layer * s->layer_elems + ((size_t)h * s->ctx + pos0) * 2 * hd) * es;
+    CUDA_TRY(cudaMemcpy(buf.data(), static_cast<uint8_t*>(s->kv) + off, buf.size(),
                         cudaMemcpyDeviceToHost));
     for (int p = 0; p < npos; ++p)
       for (int d = 0; d < hd; ++d) {
-        const size_t src = (size_t)p * hd + d, dst = ((size_t)p * nh + h) * hd + d;
+        const size_t ks = (size_t)p * 2 * hd + d, vs = ks + hd;
+        const size_t dst = ((size_t)p * nh + h) * hd + d;
         if (es == 4) {
-          k_out[dst] = reinterpret_cast<float*>(kb.data())[src];
-          v_out[dst] = reinterpret_cast<float*>(vb.data())[src];
+          k_out[dst] = reinterpret_cast<float*>(buf.data())[ks];
+          v_out[dst] = reinterpret_cast<float*>(buf.data())[vs];
         } else {
-          k_out[dst] = l3g_f16_to_f32(reinterpret_cast<uint16_t*>(kb.data())[src]);
-          v_out[dst] = l3g_f16_to_f32(reinterpret_cast<uint16_t*>(vb.data())[src]);
+          k_out[dst] = l3g_f16_to_f32(reinterpret_cast<uint16_t*>(buf.data())[ks]);
+          v_out[dst] = l3g_f16_to_f32(reinterpret_cast<uint16_t*>(buf.data())[vs]);
         }
       }
   }
@@ -726,8 +755,11 @@ extern "C" int l3g_state_read_kv(const l3g_state* s, int32_t layer, int32_t pos0
 // ---------------------------------------------------------------------------
 // V_GREEDY_DEV: the token and position come from the previous replay's
 // argmax on the device (k_advance), no host copies inside the graph.
-enum Variant { V_PREFILL = 0, V_ARGMAX = 1, V_LOGITS = 2, V_TOPK = 3, V_GREEDY_DEV = 4 };
+// V_TRACE: V_GREEDY_DEV with the device timeline recorded.
+enum Variant { V_PREFILL = 0, V_ARGMAX = 1, V_LOGITS = 2, V_TOPK = 3, V_GREEDY_DEV = 4, V_TRACE = 5 };
 constexpr int MAX_TOPK = 64;
+constexpr int kTraceCap = 256;  // traced launches per step
+constexpr size_t kTraceBytes = (size_t)kTraceCap * TRACE_CTAS * 8 * 8;
 
 struct StepGraph {
   int variant, k;
@@ -771,6 +803,9 @@ struct l3g_workspace {
   bool profiling = false;      // record an event after every kernel
   std::vector<int> prof_kind;
   std::vector<cudaEvent_t> prof_ev;
+  unsigned long long* d_trace = nullptr;  // [kernels][2][8] timeline stamps
+  std::vector<int> trace_kinds;            // kind of each traced launch
+  std::vector<int> trace_kinds_graph;      // ... as captured in the V_TRACE graph
   std::vector<StepGraph> graphs;
   bool logits_valid = false;
 };
@@ -781,7 +816,7 @@ static void ws_release(l3g_workspace* ws) {
   void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
                    ws->attn, ws->act, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
                    ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
-                   ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens};
+                   ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens, ws->d_trace};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   void* hptrs[] = {ws->h_io, ws->h_res, ws->h_logits, ws->h_tk_ids, ws->h_tk_logits};
@@ -812,9 +847,9 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   const int ne = m->hp.n_emb, hd = m->hd;
   const int G = m->group;
   const size_t es = m->kv_f16 ? 2 : 4;
-  // attention geometry: splits fill the SMs; a stage holds P positions, the
-  // K and V halves each one ~16 KB bulk copy; three stages in flight
-  ws->att_P = std::max(NW, (int)(16384 / (hd * es)));
+  // attention geometry: splits fill the SMs; a stage holds the interleaved
+  // K|V rows of P positions, one ~32 KB bulk copy; three stages in flight
+  ws->att_P = std::max(NW, (int)(32768 / (2 * hd * es)));
   ws->att_stage = 2 * ws->att_P * hd * (int)es;
   ws->att_ns = 3;
   ws->att_gp = 1;
@@ -851,6 +886,7 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   DM(ws->am_cnt, 4);
   DM(ws->tk_part, (size_t)ws->tk_chunks * MAX_TOPK * 8);
   DM(ws->d_tokens, (size_t)ctx * 4);
+  DM(ws->d_trace, kTraceBytes);
   DM(ws->d_tk_ids, MAX_TOPK * 4);
   DM(ws->d_tk_logits, MAX_TOPK * 4);
   HM(ws->h_tk_ids, MAX_TOPK * 4);
@@ -888,16 +924,37 @@ static MatvecArgs mv_args(const DevMat& w) {
   return a;
 }
 
+// float4 per thread of a PRO_RMS input row of `cols` values (a power of two)
+static int rms_vk(int cols) {
+  int vk = 2;
+  while (vk * 1024 < cols) vk <<= 1;
+  return vk;
+}
+
+template <int PRO, int EPI, int RPW>
+static cudaError_t launch_mv_r(const DevMat& w, const MatvecArgs& a, dim3 grid, cudaStream_t st) {
+  if constexpr (PRO == PRO_RMS) {
+    switch (rms_vk(w.t.cols)) {
+      case 2: return launch(k_matvec<PRO, EPI, RPW, 2>, grid, dim3(NTHREADS), (size_t)w.smem, st, a);
+      case 4: return launch(k_matvec<PRO, EPI, RPW, 4>, grid, dim3(NTHREADS), (size_t)w.smem, st, a);
+      case 8: return launch(k_matvec<PRO, EPI, RPW, 8>, grid, dim3(NTHREADS), (size_t)w.smem, st, a);
+      default: return cudaErrorInvalidValue;
+    }
+  } else {
+    return launch(k_matvec<PRO, EPI, RPW, 1>, grid, dim3(NTHREADS), (size_t)w.smem, st, a);
+  }
+}
+
 template <int PRO, int EPI>
 static cudaError_t launch_mv(const DevMat& w, const MatvecArgs& a, int nsm, cudaStream_t st) {
   const int gl = a.row_lo / w.t.wr;
   const int ng = (a.row_hi + w.t.wr - 1) / w.t.wr - gl;
-  const int grid = std::max(1, std::min(ng, nsm));
+  const dim3 grid(std::max(1, std::min(ng, nsm)));
   switch (w.t.wr / NW) {
-    case 1: return launch(k_matvec<PRO, EPI, 1>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
-    case 2: return launch(k_matvec<PRO, EPI, 2>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
-    case 4: return launch(k_matvec<PRO, EPI, 4>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
-    case 8: return launch(k_matvec<PRO, EPI, 8>, dim3(grid), dim3(NTHREADS), (size_t)w.smem, st, a);
+    case 1: return launch_mv_r<PRO, EPI, 1>(w, a, grid, st);
+    case 2: return launch_mv_r<PRO, EPI, 2>(w, a, grid, st);
+    case 4: return launch_mv_r<PRO, EPI, 4>(w, a, grid, st);
+    case 8: return launch_mv_r<PRO, EPI, 8>(w, a, grid, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -953,6 +1010,10 @@ __global__ void k_merge_argmax(const Result* g, int world, Result* out) {
 
 // Enqueues one decode step on ws->stream (captured into a graph).
 static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int k) {
+  const bool traced = variant == V_TRACE;
+  if (traced) variant = V_GREEDY_DEV;
+  unsigned long long* tr = traced ? ws->d_trace : nullptr;
+  if (traced) ws->trace_kinds.clear();
   l3g_model* m = ws->m;
   const l3g_hparams& hp = m->hp;
   cudaStream_t st = ws->stream;
@@ -963,6 +1024,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
   do {                                                 \
     CUDA_TRY(expr);                                    \
     ++ws->kernels;                                     \
+    if (tr) ws->trace_kinds.push_back(kind);           \
     if (ws->profiling) {                               \
       cudaEvent_t ev_;                                 \
       CUDA_TRY(cudaEventCreate(&ev_));                 \
@@ -977,8 +1039,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
                   hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res));
   for (int l = 0; l < hp.n_layers; ++l) {
     const LayerW& L = m->layers[l];
-    uint8_t* kc = static_cast<uint8_t*>(s->kc) + (size_t)l * s->layer_elems * es;
-    uint8_t* vc = static_cast<uint8_t*>(s->vc) + (size_t)l * s->layer_elems * es;
+    uint8_t* kv = static_cast<uint8_t*>(s->kv) + (size_t)l * s->layer_elems * es;
     {  // RMSNorm -> act-quant -> QKV -> RoPE -> KV append, infer.go:67-127
       MatvecArgs a = mv_args(L.qkv);
       a.x_in = ws->x[0];
@@ -996,16 +1057,16 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.rope_cos = s->rope_cos;
       a.rope_sin = s->rope_sin;
       a.io = ws->d_io;
-      a.kc = kc;
-      a.vc = vc;
+      a.kv = kv;
       a.res = ws->d_res;
+      a.trace = ws->kernels < kTraceCap ? tr : nullptr;
+      a.trace_seq = ws->kernels;
       KL(L3G_K_QKV, (launch_mv<PRO_RMS, EPI_QKV>(L.qkv, a, m->nsm, st)));
     }
     {  // attention, infer.go:130-175
       AttnArgs a{};
       a.q = ws->q;
-      a.kc = kc;
-      a.vc = vc;
+      a.kv = kv;
       a.ctx = s->ctx;
       a.hd = hd;
       a.group = m->group;
@@ -1020,6 +1081,8 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.counters = ws->att_cnt;
       a.out = ws->attn;
       a.res = ws->d_res;
+      a.trace = ws->kernels < kTraceCap ? tr : nullptr;
+      a.trace_seq = ws->kernels;
       KL(L3G_K_ATTN, launch_attention(ws, a, st));
     }
     {  // act-quant -> Wo, infer.go:178-187 (residual add fused downstream)
@@ -1027,6 +1090,8 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.x_in = ws->attn;
       a.out = ws->y;
       a.res = ws->d_res;
+      a.trace = ws->kernels < kTraceCap ? tr : nullptr;
+      a.trace_seq = ws->kernels;
       KL(L3G_K_WO, (launch_mv<PRO_QUANT, EPI_STORE>(L.wo, a, m->nsm, st)));
     }
     if (m->world > 1)
@@ -1040,6 +1105,8 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.eps = hp.rms_eps;
       a.out = ws->act;
       a.res = ws->d_res;
+      a.trace = ws->kernels < kTraceCap ? tr : nullptr;
+      a.trace_seq = ws->kernels;
       KL(L3G_K_UPGATE, (launch_mv<PRO_RMS, EPI_SWIGLU>(L.upgate, a, m->nsm, st)));
     }
     {  // act-quant -> down, infer.go:233-242
@@ -1047,6 +1114,8 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.x_in = ws->act;
       a.out = ws->y;
       a.res = ws->d_res;
+      a.trace = ws->kernels < kTraceCap ? tr : nullptr;
+      a.trace_seq = ws->kernels;
       KL(L3G_K_DOWN, (launch_mv<PRO_QUANT, EPI_STORE>(L.down, a, m->nsm, st)));
     }
     if (m->world > 1)
@@ -1066,6 +1135,8 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     a.am_idx = ws->am_idx;
     a.am_counter = ws->am_cnt;
     a.res = ws->d_res;
+    a.trace = ws->kernels < kTraceCap ? tr : nullptr;
+    a.trace_seq = ws->kernels;
     KL(L3G_K_LOGITS, (launch_mv<PRO_RMS, EPI_LOGITS>(m->logits, a, m->nsm, st)));
     const float* full = ws->logits;
     if (m->world > 1) {
@@ -1133,6 +1204,7 @@ static int get_graph(l3g_workspace* ws, const l3g_state* s, int variant, int k,
   if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
   ws->graphs.push_back({variant, k, s->serial, exec});
   if (variant == V_GREEDY_DEV) ws->kernels_greedy = ws->kernels;
+  if (variant == V_TRACE) ws->trace_kinds_graph = ws->trace_kinds;
   *out = exec;
   return L3G_OK;
 }
@@ -1312,6 +1384,43 @@ extern "C" int l3g_profile_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
     return l3g_fail(L3G_E_DEVICE, "device check failed during profiling");
   }
   *n = std::min(cnt, *n);
+  s->pos++;
+  return L3G_OK;
+}
+
+extern "C" int l3g_trace_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token,
+                              uint64_t* stamps, int32_t* kinds, int32_t* n) {
+  if (!m || !s || !ws || !stamps || !kinds || !n) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (s->m != m || ws->m != m)
+    return l3g_fail(L3G_E_INVALID, "state or workspace belongs to another model");
+  if (s->pos >= s->ctx) return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+  if (ws->ctx < s->ctx)
+    return l3g_fail(L3G_E_INVALID, "workspace ctxLen=%d < state ctxLen=%d", ws->ctx, s->ctx);
+  if (token < 0 || token >= m->hp.vocab_size)
+    return l3g_fail(L3G_E_TOKEN, "token out of range: %d", token);
+  CUDA_TRY(cudaSetDevice(m->device));
+  cudaGraphExec_t exec;
+  int rc = get_graph(ws, s, V_TRACE, 0, &exec);
+  if (rc) return rc;
+  const int cnt = std::min<int>((int)ws->trace_kinds_graph.size(), kTraceCap);
+  ws->h_io[0] = token;
+  ws->h_io[1] = s->pos;
+  ws->h_io[2] = 0;
+  ws->h_io[3] = 0;
+  CUDA_TRY(cudaMemsetAsync(ws->d_trace, 0, kTraceBytes, ws->stream));
+  CUDA_TRY(cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, ws->stream));
+  CUDA_TRY(cudaGraphLaunch(exec, ws->stream));
+  CUDA_TRY(cudaMemcpyAsync(ws->h_res, ws->d_res, sizeof(Result), cudaMemcpyDeviceToHost, ws->stream));
+  CUDA_TRY(cudaStreamSynchronize(ws->stream));
+  if (ws->h_res->err) {
+    cudaMemset(ws->d_res, 0, sizeof(Result));
+    return l3g_fail(L3G_E_DEVICE, "device check failed during trace");
+  }
+  const int out_n = std::min(cnt, *n);
+  CUDA_TRY(cudaMemcpy(stamps, ws->d_trace, (size_t)out_n * TRACE_CTAS * 8 * 8,
+                      cudaMemcpyDeviceToHost));
+  for (int i = 0; i < out_n; ++i) kinds[i] = ws->trace_kinds_graph[i];
+  *n = out_n;
   s->pos++;
   return L3G_OK;
 }

@@ -111,6 +111,8 @@ def lib():
         "l3g_workspace_kernels_per_step": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_profile_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_float),
                                        C.POINTER(C.c_int32)]),
+        "l3g_trace_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_uint64), C.POINTER(C.c_int32),
+                                     C.POINTER(C.c_int32)]),
         "l3g_matrix_upload": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_P)]),
         "l3g_matvec_q8": (C.c_int, [_P, _P, _P, _P, C.c_int32, C.c_int32, _P]),
         "l3g_matrix_free": (None, [_P]),
@@ -262,6 +264,20 @@ class Model:
         n = C.c_int32(cap)
         _check(lib().l3g_profile_step(self._h, s._h, _ws(ws), int(token), kinds, us, C.byref(n)))
         return [(self.KERNEL_KINDS[kinds[i]], float(us[i])) for i in range(n.value)]
+
+    TRACE_CTAS = 256
+
+    def TraceStep(self, s: "State", token: int, ws: "Workspace", cap: int = 256):
+        """One greedy step replayed as its graph with the device timeline:
+        [(kind, stamps[TRACE_CTAS][8] in ns)] per launch (zeros: untraced)."""
+        per = self.TRACE_CTAS * 8
+        stamps = np.zeros(cap * per, np.uint64)
+        kinds = (C.c_int32 * cap)()
+        n = C.c_int32(cap)
+        _check(lib().l3g_trace_step(self._h, s._h, _ws(ws), int(token),
+                                    stamps.ctypes.data_as(C.POINTER(C.c_uint64)), kinds, C.byref(n)))
+        arr = stamps[: n.value * per].reshape(n.value, self.TRACE_CTAS, 8).astype(np.int64)
+        return [(self.KERNEL_KINDS[kinds[i]], arr[i]) for i in range(n.value)]
 
     def DecodeGreedy(self, s: "State", first_token: int, n: int, ws: "Workspace"):
         """n greedy steps fed on the device; returns (tokens, device_ms)."""

@@ -64,6 +64,9 @@ CONFIGS = {
     "llama3.2-3b": Config("llama3.2-3b", 3072, 28, 24, 8, 8192, 128256, tied=True, ctx_len=4096),
     "llama3.1-8b": Config("llama3.1-8b", 4096, 32, 32, 8, 14336, 128256, tied=False,
                           rope_scaling=(8.0, 1.0, 4.0, 8192), ctx_len=8320),
+    # the 8B layer shapes with two layers (~1.1 GB): kernel-level profiling
+    "llama3.1-8b-2l": Config("llama3.1-8b-2l", 4096, 2, 32, 8, 14336, 128256, tied=False,
+                             rope_scaling=(8.0, 1.0, 4.0, 8192), ctx_len=8320),
     # small shapes for parity tests (same structure, seconds on the CPU oracle)
     "tiny": Config("tiny", 64, 2, 2, 1, 128, 97, tied=True, ctx_len=64),
     "tiny-gqa": Config("tiny-gqa", 128, 2, 4, 2, 256, 300, tied=False, ctx_len=128),
