@@ -72,6 +72,40 @@ def test_matvec_vs_reference_simd(gpu_lib, oracle_mod, rows, cols):
     M.Close()
 
 
+@pytest.mark.parametrize("rpw", [1, 2, 4, 8])
+def test_every_rows_per_warp_layout(gpu_lib, oracle_mod, monkeypatch, rpw):
+    """Each tile layout (1, 2, 4 or 8 rows per warp; L3G_RPW pins the
+    planner) gives the reference's matvec and the same forward logits."""
+    import synthetic
+    import torch
+    monkeypatch.setenv("L3G_RPW", str(rpw))
+    for rows, cols in ((2050, 1792), (513, 512), (64, 4096)):
+        g = torch.Generator().manual_seed(rows + cols)
+        w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g) * 0.02, torch).numpy()
+        x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
+        d0, q0 = oracle_mod.quantize_q8_0(x)
+        ref = oracle_mod.ref_matvec_q8(w, d0, q0, rows, cols)
+        M = gpu_lib.Matrix(w, rows, cols)
+        xd, xq = torch.from_numpy(d0).cuda(), torch.from_numpy(q0).cuda()
+        out = torch.full((rows,), 12345.0, device="cuda")
+        M.matvec(xd.data_ptr(), xq.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_l2(out.cpu().numpy(), ref) < 1e-5
+        M.Close()
+    cfg, T = synthetic_model("mid")
+    ids = synthetic.prompt_ids(cfg, 8, seed=11)
+    R = ReferenceRuns(oracle_mod, cfg, T, ids, 64, with_f64=False)
+    m = _load_gpu(gpu_lib, cfg, T)
+    s = m.NewState(64)
+    ws = m.NewWorkspace(64, 40)
+    logits = np.empty(cfg.vocab, np.float32)
+    errs = []
+    for i, t in enumerate(ids):
+        m.ForwardIntoWorkspace(s, int(t), logits, ws)
+        errs.append(rel_l2(logits, R.cgo[i]))
+    assert max(errs) < R.tol(), (errs, R.band())
+
+
 def _load_gpu(gpu_lib, cfg, T, **kw):
     return gpu_lib.LoadModelFromTensors(gpu_lib.hparams_for(cfg), T, gpu_lib.default_options(**kw))
 
