@@ -66,6 +66,17 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def profiled_traffic(summary: str):
+    """DRAM bytes (read + write) per launch that an ncu capture of the kernel
+    measured, from the summary committed under profiles/ (None if absent)."""
+    import re
+    p = os.path.join(ROOT, "profiles", summary)
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", open(p).read())
+    return int(m.group(1)) if m else None
+
+
 # ---------------------------------------------------------------------------
 # clocks during the timed region
 # ---------------------------------------------------------------------------
@@ -422,7 +433,10 @@ def run_l3g(args):
                    "l2": "inputs larger than L2: every step streams %.2f GB of weights" % (cfg.weight_bytes() / 1e9),
                    "weights": "seeded N(0,0.02) quantized to Q8_0, norms 1.0; random-init synthetic"},
         "roofline": {"bound": "hbm", "achieved": round(mv["achieved_gbs"], 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(mv["achieved_gbs"] / hbm, 4), "traffic": None,
+                     "frac": round(mv["achieved_gbs"] / hbm, 4),
+                     "traffic": profiled_traffic("k_matvec_q8_upgate_28672x4096.md"),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                       "(profiles/k_matvec_q8_upgate_28672x4096.md)",
                      "kernel": mv["kernel"], "bytes_per_launch": mv["bytes_per_launch"],
                      "ms_per_launch": round(mv["ms_per_launch"], 5), "peak_kind": hbm_kind},
         "decode_roofline": {"bytes_per_token": int(step_bytes), "weight_bytes": cfg.weight_bytes(),
