@@ -233,6 +233,46 @@ int l3g_matvec_q8(const l3g_matrix *w, const float *x_scales,
 void l3g_matrix_free(l3g_matrix *w);
 int l3g_matrix_device_bytes(const l3g_matrix *w, uint64_t *bytes);
 
+/* ---- matvec + argmax without allocation ---------------------------------- */
+/* No counterpart in the reference: its greedy step runs the logits matvec
+ * (infer.go:250-260) and then scans the logits on the host (Sampler.Sample,
+ * sampling.go:37-65).  This entry fuses the two on the device: the same
+ * Q8_0 matvec as l3g_matvec_q8 over all rows, and the argmax over the rows
+ * (ties to the lowest row).  It allocates nothing, at any call: the
+ * cross-CTA reduction uses a fixed static device array of
+ * L3G_ARGMAX_STATIC_MAX_CTAS per-CTA slots plus one arrival counter, so a
+ * caller holding no workspace (the matrix handle is all it has, as with
+ * matvec_q8_c) and unable to allocate (device memory fully committed to
+ * weights and KV cache, or a stream that must not be stalled by
+ * cudaMalloc/cudaFree, which synchronize the device) can still get a greedy
+ * token without a host round trip over the logits.
+ *  - x_scales, x_qs, out, result are DEVICE pointers; out may be NULL (the
+ *    logits are then not stored); *result is cleared on the stream and then
+ *    receives {index, value, status, detail}, status 0 unless a bounded wait
+ *    of the kernel gave up (then an internal code, detail = wait site).
+ *  - max_ctas caps the CTAs of the launch (0: one per SM); values above
+ *    L3G_ARGMAX_STATIC_MAX_CTAS, or an SM count above it, are rejected with
+ *    L3G_E_INVALID.
+ *  - The first call on a device does the set-up (looks up the static array's
+ *    device address with that device current); make that first call before
+ *    any stream capture on the device.
+ *  - The arrival counter must be zero when a launch starts: it is zero when
+ *    the library loads and every launch's last CTA resets it; the slots need
+ *    no initial value.  The array is shared by every call on the device, so
+ *    calls that overlap in time (other streams, other threads) race and give
+ *    wrong results: issue them on one stream, or serialize them. */
+#define L3G_ARGMAX_STATIC_MAX_CTAS 1024
+typedef struct l3g_argmax_result {
+  int32_t index;  /* row of the largest value                        */
+  float value;    /* out[index]                                      */
+  int32_t status; /* 0, or the device error of a bounded wait        */
+  int32_t detail; /* wait site when status != 0                      */
+} l3g_argmax_result;
+int l3g_matvec_q8_argmax_static(const l3g_matrix *w, const float *x_scales,
+                                const int8_t *x_qs, float *out,
+                                l3g_argmax_result *result, int32_t max_ctas,
+                                void *stream);
+
 /* QuantizeQ8_0Into, q8_0.go:22-79, on the device (DEVICE pointers): d has
  * ceil(n/32) floats, qs ceil(n/32)*32 bytes. */
 int l3g_quantize_q8_0(const float *x, int32_t n, float *d, int8_t *qs,

@@ -1526,6 +1526,94 @@ extern "C" int l3g_matvec_q8(const l3g_matrix* w, const float* x_scales, const i
   return L3G_OK;
 }
 
+// ---------------------------------------------------------------------------
+// matvec + argmax out of static device scratch (allocates nothing)
+// ---------------------------------------------------------------------------
+// Layout of the array: [0, S) per-CTA best value (float bits), [S, 2S) its
+// row, [2S] the arrival counter, S = L3G_ARGMAX_STATIC_MAX_CTAS (8 KB + 256
+// bytes).  The counter must be zero when a launch starts: static device
+// storage is zero-initialized when the module loads, and the launch's last
+// CTA writes it back to zero after reading the slots.  The slots need no
+// initial value: a CTA writes its own before it increments the counter.
+constexpr int kArgmaxSlots = L3G_ARGMAX_STATIC_MAX_CTAS;
+static __device__ __align__(256) uint32_t g_argmax_scratch[2 * kArgmaxSlots + 64];
+
+struct ArgmaxStatic {   // per device, filled by the first call on it
+  std::once_flag once;
+  int rc = L3G_OK;
+  uint32_t* scratch = nullptr;
+};
+static ArgmaxStatic g_argmax_static[64];
+
+// Once per device, with that device current: the array's device address and
+// the kernels' attributes.  Neither allocates.
+static int argmax_static_setup(int dev, uint32_t** scratch) {
+  if (dev < 0 || dev >= 64) return l3g_fail(L3G_E_INVALID, "device %d out of range", dev);
+  ArgmaxStatic& st = g_argmax_static[dev];
+  std::call_once(st.once, [&st] {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
+    if (e == cudaSuccess) e = set_max_shared(k_matvec<PRO_PREQ, EPI_LOGITS, 1, 1>, 227 * 1024);
+    if (e == cudaSuccess) e = set_max_shared(k_matvec<PRO_PREQ, EPI_LOGITS, 2, 1>, 227 * 1024);
+    if (e == cudaSuccess) e = set_max_shared(k_matvec<PRO_PREQ, EPI_LOGITS, 4, 1>, 227 * 1024);
+    if (e == cudaSuccess) e = set_max_shared(k_matvec<PRO_PREQ, EPI_LOGITS, 8, 1>, 227 * 1024);
+    if (e != cudaSuccess) {
+      st.rc = l3g_fail(L3G_E_CUDA, "static argmax scratch set-up: %s", cudaGetErrorString(e));
+      return;
+    }
+    st.scratch = static_cast<uint32_t*>(p);
+  });
+  if (st.rc) return l3g_fail(L3G_E_CUDA, "static argmax scratch set-up failed on device %d", dev);
+  *scratch = st.scratch;
+  return L3G_OK;
+}
+
+extern "C" int l3g_matvec_q8_argmax_static(const l3g_matrix* w, const float* x_scales,
+                                           const int8_t* x_qs, float* out,
+                                           l3g_argmax_result* result, int32_t max_ctas,
+                                           void* stream) {
+  static_assert(sizeof(l3g_argmax_result) == sizeof(Result), "result layout");
+  if (!w || !x_scales || !x_qs || !result) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (((uintptr_t)x_qs & 15) || ((uintptr_t)x_scales & 3) || ((uintptr_t)out & 3) ||
+      ((uintptr_t)result & 15))
+    return l3g_fail(L3G_E_INVALID, "x_qs and result must be 16-byte aligned, x_scales/out 4-byte");
+  if (max_ctas < 0 || max_ctas > kArgmaxSlots)
+    return l3g_fail(L3G_E_INVALID,
+                    "max_ctas=%d outside [0, %d]: the static argmax scratch holds %d CTA slots",
+                    max_ctas, kArgmaxSlots, kArgmaxSlots);
+  const int ng = w->w.t.n_groups;
+  const int grid = std::max(1, std::min(ng, max_ctas ? max_ctas : w->nsm));
+  if (grid > kArgmaxSlots)
+    return l3g_fail(L3G_E_INVALID,
+                    "launch needs %d CTA slots, the static argmax scratch holds %d", grid,
+                    kArgmaxSlots);
+  CUDA_TRY(cudaSetDevice(w->device));
+  uint32_t* scratch = nullptr;
+  if (int rc = argmax_static_setup(w->device, &scratch)) return rc;
+  const cudaStream_t st = (cudaStream_t)stream;
+  CUDA_TRY(cudaMemsetAsync(result, 0, sizeof(*result), st));
+  MatvecArgs a = mv_args(w->w);
+  a.xd_in = x_scales;
+  a.xqs_in = x_qs;
+  a.out = out;
+  a.row_offset = 0;
+  a.am_val = reinterpret_cast<float*>(scratch);
+  a.am_idx = reinterpret_cast<int*>(scratch + kArgmaxSlots);
+  a.am_counter = scratch + 2 * kArgmaxSlots;
+  a.res = reinterpret_cast<Result*>(result);
+  const dim3 g(grid);
+  cudaError_t e;
+  switch (w->w.t.wr / NW) {
+    case 1: e = launch_mv_r<PRO_PREQ, EPI_LOGITS, 1>(w->w, a, g, st); break;
+    case 2: e = launch_mv_r<PRO_PREQ, EPI_LOGITS, 2>(w->w, a, g, st); break;
+    case 4: e = launch_mv_r<PRO_PREQ, EPI_LOGITS, 4>(w->w, a, g, st); break;
+    case 8: e = launch_mv_r<PRO_PREQ, EPI_LOGITS, 8>(w->w, a, g, st); break;
+    default: e = cudaErrorInvalidValue;
+  }
+  CUDA_TRY(e);
+  return L3G_OK;
+}
+
 extern "C" int l3g_quantize_q8_0(const float* x, int32_t n, float* d, int8_t* qs, void* stream) {
   if (!x || !d || !qs || n <= 0) return l3g_fail(L3G_E_INVALID, "bad argument");
   const int nb = (n + 31) / 32;

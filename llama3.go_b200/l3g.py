@@ -27,6 +27,7 @@ L3G_OK, L3G_E_INVALID, L3G_E_CUDA, L3G_E_NCCL, L3G_E_CTX, L3G_E_TOKEN, \
     L3G_E_FORMAT, L3G_E_DEVICE = 0, -1, -2, -3, -4, -5, -6, -7
 L3G_KV_F32, L3G_KV_F16 = 0, 1
 BUF_HIDDEN, BUF_Q, BUF_ATTN, BUF_FFN_ACT, BUF_LOGITS = range(5)
+ARGMAX_STATIC_MAX_CTAS = 1024  # L3G_ARGMAX_STATIC_MAX_CTAS
 
 
 class L3GError(RuntimeError):
@@ -115,6 +116,7 @@ def lib():
                                      C.POINTER(C.c_int32)]),
         "l3g_matrix_upload": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_P)]),
         "l3g_matvec_q8": (C.c_int, [_P, _P, _P, _P, C.c_int32, C.c_int32, _P]),
+        "l3g_matvec_q8_argmax_static": (C.c_int, [_P, _P, _P, _P, _P, C.c_int32, _P]),
         "l3g_matrix_free": (None, [_P]),
         "l3g_matrix_device_bytes": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
         "l3g_quantize_q8_0": (C.c_int, [_P, C.c_int32, _P, _P, _P]),
@@ -447,6 +449,15 @@ class Matrix:
         """matvec_q8_c(w, x_scales, x_qs, out, start, end, cols) on device pointers."""
         end = self.rows if end is None else end
         _check(lib().l3g_matvec_q8(self._h, x_scales_ptr, x_qs_ptr, out_ptr, start, end, stream or None))
+
+    def matvec_argmax_static(self, x_scales_ptr: int, x_qs_ptr: int, out_ptr: int,
+                             result_ptr: int, max_ctas: int = 0, stream: int = 0):
+        """The same matvec over all rows fused with the argmax of its output,
+        using the library's static device scratch (no allocation).  out_ptr
+        may be 0; result_ptr points at 16 device bytes that receive
+        (int32 index, float32 value, int32 status, int32 detail)."""
+        _check(lib().l3g_matvec_q8_argmax_static(self._h, x_scales_ptr, x_qs_ptr, out_ptr or None,
+                                                 result_ptr, max_ctas, stream or None))
 
     def Close(self):
         if self._h:
