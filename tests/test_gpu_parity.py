@@ -72,6 +72,31 @@ def test_matvec_vs_reference_simd(gpu_lib, oracle_mod, rows, cols):
     M.Close()
 
 
+def test_matvec_vs_golden_fixture(gpu_lib):
+    """l3g_matvec_q8 against the committed outputs of the reference's own
+    matvec_q8_c (tests/golden/ref_simd_matvec.npz), with the recorded
+    quantized activations: no oracle in the loop."""
+    import os
+    import sys
+    import torch
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, golden)
+    import make_golden
+    z = np.load(os.path.join(golden, "ref_simd_matvec.npz"))
+    for i in range(len(make_golden.MATVEC_CASES)):
+        rows, cols, seed = z[f"c{i}_shape"].tolist()
+        w = make_golden.q8_matrix(rows, cols, seed)
+        assert make_golden.sha(w) == str(z[f"c{i}_w_sha256"])
+        M = gpu_lib.Matrix(w, rows, cols)
+        xd = torch.from_numpy(z[f"c{i}_xd"]).cuda()
+        xq = torch.from_numpy(z[f"c{i}_xq"]).cuda()
+        out = torch.full((rows,), 12345.0, device="cuda")
+        M.matvec(xd.data_ptr(), xq.data_ptr(), out.data_ptr())
+        torch.cuda.synchronize()
+        assert rel_l2(out.cpu().numpy(), z[f"c{i}_out"]) < 1e-5, (rows, cols)
+        M.Close()
+
+
 @pytest.mark.parametrize("rpw", [1, 2, 4, 8])
 def test_every_rows_per_warp_layout(gpu_lib, oracle_mod, monkeypatch, rpw):
     """Each tile layout (1, 2, 4 or 8 rows per warp; L3G_RPW pins the
