@@ -207,6 +207,7 @@ int l3g_workspace_kernels_per_step(l3g_workspace *ws, int32_t *n);
 #define L3G_K_DOWN 5
 #define L3G_K_LOGITS 6
 #define L3G_K_OTHER 7
+#define L3G_K_ACT_QUANT 8 /* act-quant of the SwiGLU output for down     */
 int l3g_profile_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                      int32_t token, int32_t *kinds, float *us, int32_t *n);
 /* Device timeline of one greedy step replayed as its CUDA graph (kernels

@@ -27,6 +27,8 @@ struct AttnArgs {
   float* part_ml;     // [kv heads][splits][group][2]
   unsigned* counters; // [kv heads], zero between launches
   float* out;         // [local q heads][hd]
+  float* out_d;       // out quantized (QuantizeQ8_0Into) for the Wo matvec:
+  int8_t* out_q;      //   [local q heads * hd / 32] scales, int8 values
   Result* res;
   unsigned long long* trace;  // device timeline (nullptr: off)
   int trace_seq;
@@ -147,6 +149,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     return;
   }
 
+  // warm the translations of q and of the merge buffers before the wait
+  if (lane == 0) {
+    if (warp == 0) touch_page(a.q + (size_t)kvh * G * hd);
+    if (warp == 1) touch_page(a.part_o + ((size_t)kvh * S + split) * G * hd);
+    if (warp == 2) touch_page(a.part_ml + ((size_t)kvh * S + split) * G * 2);
+    if (warp == 3) touch_page(a.counters + kvh);
+    if (warp == 4) touch_page(a.out + (size_t)kvh * G * hd);
+  }
   pdl_wait();  // q comes from the previous kernel
   trace_mark(a.trace, a.trace_seq, TR_WAITED);
   float q[GP][DPL];
@@ -360,11 +370,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   }
   trace_mark(a.trace, a.trace_seq, 7);  // merged
+  // normalize, store, and quantize: a warp holds 32 consecutive outputs,
+  // one Q8_0 block (hd is a multiple of 32, so no block spans two kv heads)
   for (int k = 0; k < 4; ++k) {
     const int idx = threadIdx.x + k * NW * 32;
-    if (idx >= gh) break;
+    if (idx >= gh) break;  // uniform per warp: gh is a multiple of 32
     const int h = idx / hd;
-    a.out[(size_t)kvh * gh + idx] = __fmul_rn(acc2[k], __fdiv_rn(1.0f, sm_tot[h]));
+    const float v = __fmul_rn(acc2[k], __fdiv_rn(1.0f, sm_tot[h]));
+    a.out[(size_t)kvh * gh + idx] = v;
+    quant_block(v, (kvh * gh + idx) >> 5, lane, a.out_d, a.out_q);
   }
   if (threadIdx.x == 0) a.counters[kvh] = 0u;
   trace_mark(a.trace, a.trace_seq, TR_EXIT);

@@ -93,6 +93,15 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void pdl_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
+// An L2-only load whose value is discarded, issued before the dependency wait
+// on a buffer the previous kernel is still writing: it warms the address
+// translation of that buffer's page so the real loads after the wait do not
+// pay for it.  `.cg` keeps the (stale) line out of L1, so nothing read after
+// the wait can come from it.
+__device__ __forceinline__ void touch_page(const void* p) {
+  unsigned v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+}
 // barrier 1: the NW consumer warps only (the producer warp never joins)
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
@@ -246,7 +255,12 @@ __global__ void k_advance(int* io, const Result* res, int* tokens) {
 }
 
 // Standalone activation quantization (QuantizeQ8_0Into), one warp per block.
+// QuantizeQ8_0Into (q8_0.go:22-79): one warp per 32-value block.  In the
+// decode step it quantizes the SwiGLU output once for every CTA of the down
+// matvec (which then only copies the int8 vector), as a dependent launch.
 __global__ void k_quantize(const float* x, int n, float* d, int8_t* qs) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (b >= (n + 31) / 32) return;

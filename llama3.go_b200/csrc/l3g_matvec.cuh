@@ -14,7 +14,7 @@ struct Q8Tiles {
   int rows, cols, wr, ck, nslices, tile_bytes, n_groups;
 };
 
-enum Pro { PRO_PREQ = 0, PRO_QUANT = 1, PRO_RMS = 2 };
+enum Pro { PRO_PREQ = 0, PRO_RMS = 2 };
 enum Epi { EPI_STORE = 0, EPI_QKV = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
 
 struct MatvecArgs {
@@ -22,7 +22,7 @@ struct MatvecArgs {
   int nstages;
   int row_lo, row_hi;  // rows this launch covers / writes
   // prologue
-  const float* x_in;    // PRO_QUANT: vector to quantize; PRO_RMS: residual
+  const float* x_in;    // PRO_RMS: residual
   const float* y_in;    // PRO_RMS: delta added to x_in first (or null)
   const float* norm_w;  // PRO_RMS
   float* x_out;         // PRO_RMS: x_in + y_in written by CTA 0 (or null)
@@ -77,51 +77,39 @@ __host__ __device__ __forceinline__ int mv_smem_bytes(int cols, int nstages,
 template <int PRO, int VK>
 __device__ __forceinline__ void mv_prologue(const MatvecArgs& a, float* xd,
                                             int8_t* xqs, MatvecSmem* sh,
-                                            const float4 (&w)[VK]) {
+                                            const float4* w) {
   const int C = a.w.cols;
   const int nb = C >> 5;
   const int tid = threadIdx.x;  // < NW*32
   const int warp = tid >> 5, lane = tid & 31;
   if constexpr (PRO == PRO_PREQ) {
-    for (int i = tid; i < nb; i += NW * 32) xd[i] = a.xd_in[i];
-    for (int i = tid * 16; i < C; i += NW * 32 * 16)
-      *reinterpret_cast<int4*>(xqs + i) =
-          *reinterpret_cast<const int4*>(a.xqs_in + i);
-  } else if constexpr (PRO == PRO_QUANT) {
-    // Element i of float4 k of thread t is x[4 * (t + 256 k) + i]; eight
-    // consecutive threads cover one 32-value block.  Loads run one chunk of
-    // four float4 ahead of the quantization (a register double buffer), so
-    // the L2 round trips overlap instead of serializing.
-    const int nv = C >> 2;
-    const int nk = (nv + NW * 32 - 1) / (NW * 32);
-    const float4* x4 = reinterpret_cast<const float4*>(a.x_in);
-    auto ld = [&](int k) {
-      const int i = tid + k * NW * 32;
-      return (k < nk && i < nv) ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    };
-    auto qz = [&](const float4& u, int k) {
-      if (k < nk) {  // uniform over the CTA
-        const int i = tid + k * NW * 32;
-        quant_quad(u, i < nv, i >> 3, lane & 7, xd, xqs);
+    // copy the quantized activation, 16 KB of int8 and 512 scales per
+    // round: each thread's loads of a round are issued before its stores
+    for (int base = 0; base < C; base += 4 * NW * 32 * 16) {
+      int4 q[4];
+      float dv[2];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = base + (tid + k * NW * 32) * 16;
+        q[k] = i < C ? *reinterpret_cast<const int4*>(a.xqs_in + i) : make_int4(0, 0, 0, 0);
       }
-    };
-    float4 a0 = ld(0), a1 = ld(1), a2 = ld(2), a3 = ld(3);
-    for (int c = 0; c < nk; c += 8) {
-      const float4 b0 = ld(c + 4), b1 = ld(c + 5), b2 = ld(c + 6), b3 = ld(c + 7);
-      qz(a0, c);
-      qz(a1, c + 1);
-      qz(a2, c + 2);
-      qz(a3, c + 3);
-      a0 = ld(c + 8);
-      a1 = ld(c + 9);
-      a2 = ld(c + 10);
-      a3 = ld(c + 11);
-      qz(b0, c + 4);
-      qz(b1, c + 5);
-      qz(b2, c + 6);
-      qz(b3, c + 7);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int i = base / 32 + tid + k * NW * 32;
+        dv[k] = i < nb ? a.xd_in[i] : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = base + (tid + k * NW * 32) * 16;
+        if (i < C) *reinterpret_cast<int4*>(xqs + i) = q[k];
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int i = base / 32 + tid + k * NW * 32;
+        if (i < nb) xd[i] = dv[k];
+      }
     }
-    trace_mark(a.trace, a.trace_seq, 7);  // quantized
+    trace_mark(a.trace, a.trace_seq, 7);  // copied
   } else {
     // residual add (infer.go:189-191 / :244-246), rmsNorm (math.go:5-14),
     // then the block quantization; w (the norm weights, loaded before the
@@ -313,12 +301,23 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
   }
 
   // the norm weights are constants: fetch them before the dependency wait
-  float4 nw[VK];
+  float4 nw[PRO == PRO_RMS ? VK : 1];
 #pragma unroll
-  for (int k = 0; k < VK; ++k) {
+  for (int k = 0; k < (PRO == PRO_RMS ? VK : 1); ++k) {
     const int i = threadIdx.x + k * NW * 32;
     nw[k] = (PRO == PRO_RMS && i < C / 4) ? reinterpret_cast<const float4*>(a.norm_w)[i]
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // warm the translations of the activation inputs (one line per warp
+  // spread over each vector) while the previous kernel still runs
+  if (lane == 0) {
+    if constexpr (PRO == PRO_PREQ) {
+      touch_page(a.xqs_in + (size_t)warp * (C / NW));
+      touch_page(a.xd_in + (size_t)warp * (C / 32 / NW));
+    } else {
+      touch_page(a.x_in + (size_t)warp * (C / NW));
+      if (PRO == PRO_RMS && a.y_in) touch_page(a.y_in + (size_t)warp * (C / NW));
+    }
   }
   pdl_wait();  // activations come from the previous kernel
   trace_mark(a.trace, a.trace_seq, TR_WAITED);

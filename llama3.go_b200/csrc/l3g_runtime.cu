@@ -166,7 +166,6 @@ static int setup_kernels() {
   SETMV4(PRO_RMS, E, 4); \
   SETMV4(PRO_RMS, E, 8)
     SETMV4(PRO_PREQ, EPI_STORE, 1);
-    SETMV4(PRO_QUANT, EPI_STORE, 1);
     SETRMS(EPI_QKV);
     SETRMS(EPI_SWIGLU);
     SETRMS(EPI_LOGITS);
@@ -783,6 +782,10 @@ struct l3g_workspace {
   float* q = nullptr;
   float* attn = nullptr;
   float* act = nullptr;
+  float* attn_d = nullptr;     // attention output, Q8_0-quantized by the merge
+  int8_t* attn_q = nullptr;
+  float* act_d = nullptr;      // SwiGLU output, Q8_0-quantized once per step
+  int8_t* act_q = nullptr;
   float* logits = nullptr;     // [world * v_l]: local shard first, gathered when TP
   float* logits_full = nullptr;
   float* h_logits = nullptr;   // pinned [vocab]
@@ -816,7 +819,7 @@ static void ws_release(l3g_workspace* ws) {
   for (auto& g : ws->graphs) cudaGraphExecDestroy(g.exec);
   ws->graphs.clear();
   void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
-                   ws->attn, ws->act, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
+                   ws->attn, ws->act, ws->attn_d, ws->attn_q, ws->act_d, ws->act_q, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
                    ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
                    ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens, ws->d_trace};
   for (void* p : dptrs)
@@ -877,6 +880,10 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   DM(ws->q, (size_t)m->hq_l * hd * 4);
   DM(ws->attn, (size_t)m->hq_l * hd * 4);
   DM(ws->act, (size_t)m->ff_l * 4);
+  DM(ws->attn_d, (size_t)m->hq_l * hd / 32 * 4);
+  DM(ws->attn_q, (size_t)m->hq_l * hd);
+  DM(ws->act_d, (size_t)m->ff_l / 32 * 4);
+  DM(ws->act_q, (size_t)m->ff_l);
   DM(ws->logits, (size_t)vloc * 4);
   DM(ws->logits_full, (size_t)vloc * m->world * 4);
   HM(ws->h_logits, (size_t)vloc * m->world * 4);
@@ -1082,19 +1089,23 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.part_ml = ws->part_ml;
       a.counters = ws->att_cnt;
       a.out = ws->attn;
+      a.out_d = ws->attn_d;
+      a.out_q = ws->attn_q;
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
       KL(L3G_K_ATTN, launch_attention(ws, a, st));
     }
-    {  // act-quant -> Wo, infer.go:178-187 (residual add fused downstream)
+    {  // Wo on the attention output the merge quantized, infer.go:178-187
+       // (residual add fused downstream)
       MatvecArgs a = mv_args(L.wo);
-      a.x_in = ws->attn;
+      a.xd_in = ws->attn_d;
+      a.xqs_in = ws->attn_q;
       a.out = ws->y;
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      KL(L3G_K_WO, (launch_mv<PRO_QUANT, EPI_STORE>(L.wo, a, m->nsm, st)));
+      KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_STORE>(L.wo, a, m->nsm, st)));
     }
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));
@@ -1111,14 +1122,20 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.trace_seq = ws->kernels;
       KL(L3G_K_UPGATE, (launch_mv<PRO_RMS, EPI_SWIGLU>(L.upgate, a, m->nsm, st)));
     }
-    {  // act-quant -> down, infer.go:233-242
+    {  // act-quant of the SwiGLU output (once, not per CTA), infer.go:233-234
+      const int nb = m->ff_l / 32;
+      KL(L3G_K_ACT_QUANT, launch(k_quantize, dim3((nb + NW - 1) / NW), dim3(NW * 32), 0, st,
+                                 (const float*)ws->act, m->ff_l, ws->act_d, ws->act_q));
+    }
+    {  // down, infer.go:235-242
       MatvecArgs a = mv_args(L.down);
-      a.x_in = ws->act;
+      a.xd_in = ws->act_d;
+      a.xqs_in = ws->act_q;
       a.out = ws->y;
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      KL(L3G_K_DOWN, (launch_mv<PRO_QUANT, EPI_STORE>(L.down, a, m->nsm, st)));
+      KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_STORE>(L.down, a, m->nsm, st)));
     }
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));

@@ -257,7 +257,7 @@ class Model:
                                  arr.size))
 
     KERNEL_KINDS = ("embed", "qkv_rope_kv", "attention", "wo", "upgate_swiglu", "down", "logits_argmax",
-                    "other")
+                    "other", "act_quant")
 
     def ProfileStep(self, s: "State", token: int, ws: "Workspace", cap: int = 4096):
         """One step run eagerly with every kernel timed alone: [(kind, us)]."""
