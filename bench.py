@@ -332,6 +332,13 @@ def trace_summary(m, s, ws, tok, pos, reps=3):
     return out
 
 
+def progress(world, rank, msg):
+    """Rank-tagged progress on stderr for multi-GPU runs (stdout keeps the
+    single JSON line)."""
+    if world > 1:
+        print(f"[rank {rank} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def run_l3g(args):
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -347,8 +354,10 @@ def run_l3g(args):
     hbm, hbm_kind = peaks()
     cfg = synthetic.CONFIGS[args.config]
 
+    progress(world, rank, "generating the synthetic model")
     T = make_host_model(cfg, args.seed, f"cuda:{local}")
     torch.cuda.empty_cache()
+    progress(world, rank, "loading the model")
     nid = D.bcast_bytes(l3g.nccl_unique_id() if (world > 1 and rank == 0) else None) if world > 1 else None
     kv = l3g.L3G_KV_F16 if args.kv == "f16" else l3g.L3G_KV_F32
     opts = l3g.default_options(world, rank, local, kv, nid)
@@ -359,12 +368,14 @@ def run_l3g(args):
     s = m.NewState(ctx)
     ws = m.NewWorkspace(ctx, 40)
     prompt = synthetic.prompt_ids(cfg, args.prefill, seed=args.seed)
+    progress(world, rank, "prefill")
     t0 = time.perf_counter()
     m.Prefill(s, prompt[:-1], ws)
     prefill_s = time.perf_counter() - t0
     p0 = s.Pos
 
     # value: device-resident greedy loop
+    progress(world, rank, "decode warm-up")
     warm, _ = m.DecodeGreedy(s, int(prompt[-1]), max(1, args.warmup), ws)
     D.barrier()
     clk = Clocks(physical_index(local))
@@ -377,6 +388,7 @@ def run_l3g(args):
     value = args.steps / (dev_ms / 1000.0)
     kernels = ws.kernels_per_step()
 
+    progress(world, rank, "e2e")
     # e2e: the public per-step call, host token in / host token out
     s.Pos = p0
     tok = int(prompt[-1])
@@ -393,6 +405,7 @@ def run_l3g(args):
     e2e = args.steps / e2e_s
     same = bool(np.array_equal(np.array(e2e_toks, np.int32), toks))
 
+    progress(world, rank, "per-kernel profile")
     # per-kernel device time of one step at this context (eager, serialized)
     s.Pos = p0 + max(1, args.warmup)
     prof = {}
@@ -401,7 +414,9 @@ def run_l3g(args):
             prof[kind] = prof.get(kind, 0.0) + us / 3
         s.Pos = p0 + max(1, args.warmup)
     prof = {k: round(v, 1) for k, v in sorted(prof.items(), key=lambda kv: -kv[1])}
+    progress(world, rank, "device timeline")
     timeline = trace_summary(m, s, ws, tok, p0 + max(1, args.warmup))
+    progress(world, rank, "matvec timing and wrap-up")
 
     # roofline of the whole decode step (weights + KV read per token)
     es = 2 if args.kv == "f16" else 4
@@ -418,6 +433,10 @@ def run_l3g(args):
                "sample": f"{n} greedy decode steps of the {cfg.name} shape at position {args.prefill} "
                          f"(KV of earlier positions seeded), ForwardTopK path, topK 40; C restatement "
                          f"of infer.go + the reference's own simd.c"}
+    # workspace and state first: the workspace's step graphs hold NCCL calls
+    # on the model's communicator
+    ws.Close()
+    s.Close()
     m.Close()
     D.close()
     if rank != 0:

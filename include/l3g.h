@@ -193,6 +193,12 @@ int l3g_decode_greedy(l3g_model *m, l3g_state *s, l3g_workspace *ws,
 /* Kernels of this library one step launches (greedy variant), for launch
  * accounting. */
 int l3g_workspace_kernels_per_step(l3g_workspace *ws, int32_t *n);
+/* Attention layout the workspace chose: splits per kv head, and the cluster
+ * size when the splits of a kv head merge as one thread-block cluster (0:
+ * they merge through global memory).  Inspection only; no reference
+ * counterpart (the reference attends on one goroutine, infer.go:130-175). */
+int l3g_workspace_attention_layout(const l3g_workspace *ws, int32_t *splits,
+                                   int32_t *cluster);
 
 /* Profiling (the device counterpart of the chat CLI's -cpuprofile,
  * cmd/go-llama-chat/main.go:35-54): runs one greedy step eagerly, each kernel

@@ -13,8 +13,14 @@
 //     them so lane i ends with complete score i (31 shuffles per sub-batch);
 //   - probabilities are broadcast through a warp-private buffer for the V
 //     accumulation.
-// The per-warp states merge in the CTA, the CTAs of one kv head merge in
-// split order in whichever CTA finishes last (deterministic).
+// The per-warp states merge in the CTA.  The CTAs (splits) of one kv head
+// then merge in split order (deterministic) either
+//   - CL: as one thread-block cluster, each CTA leaving its (m, l, o) in its
+//     own shared memory; after a cluster barrier CTA r merges output slice r
+//     (one or more Q8_0 blocks) reading the others' partials over
+//     distributed shared memory, then a second barrier keeps every CTA's
+//     shared memory alive until all reads are done;
+//   - otherwise through global partials, in whichever CTA finishes last.
 #pragma once
 
 struct AttnArgs {
@@ -39,6 +45,7 @@ struct AttnSmem {
   uint64_t empty[MAX_STAGES];
   int abort_flag;
   int issued;
+  int producer_done;
   int last;
 };
 constexpr int AT_HEAD = 512;
@@ -90,7 +97,14 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
   return v[0];
 }
 
-template <int DPL, typename KT, int GP>
+// Shared-memory merge scratch in the ring after the loop (floats):
+// [NW][MAXG][2] per-warp (m, l), [NW][G][hd] per-warp o, then (CL) the CTA's
+// combined [MAXG][2] (m, l) and [G][hd] o read by the cluster's other CTAs.
+__host__ __device__ __forceinline__ int at_scratch_floats(int G, int hd) {
+  return NW * MAXG * 2 + NW * G * hd + MAXG * 2 + G * hd;
+}
+
+template <int DPL, typename KT, int GP, bool CL>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ AttnArgs a) {
   constexpr int SB = 32 / GP;  // positions per sub-batch
@@ -109,14 +123,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int nst = (t1 - t0 + P - 1) / P;
   const size_t head_off = (size_t)kvh * a.ctx * 2 * hd;
   const int row = 2 * hd;  // elements per position: K then V
+  // Stage groups: when a stage holds fewer than NW sub-batches, the warps
+  // split into two groups of NW/2 that take alternate stages, so a warp's
+  // share of a stage (nbw positions) still fills whole sub-batches.  Two
+  // groups never outrun a ring of >= 2 stages, which keeps every mbarrier
+  // wait within one phase of the barrier's state.
+  const int wsz = (P / SB >= NW) ? NW : NW / 2;  // warps per stage
+  const int ngrp = NW / wsz;
+  const int nbw = P / wsz;                        // positions per warp and stage
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&sh->full[s], 1);
-      mbar_init(&sh->empty[s], NW);
+      mbar_init(&sh->empty[s], wsz);
     }
     sh->abort_flag = 0;
     sh->issued = 0;
+    sh->producer_done = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -145,6 +168,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                  static_cast<const uint8_t*>(a.kv) + off, bytes, &sh->full[s]);
         *(volatile int*)&sh->issued = st + 1;
       }
+      *(volatile int*)&sh->producer_done = 1;
+    }
+    if constexpr (CL) {  // the cluster barriers count every thread
+      __syncwarp();
+      cluster_sync_all();
+      cluster_sync_all();
     }
     return;
   }
@@ -175,21 +204,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   float* pbuf = pbuf_all + warp * 32;
   float* hbuf = hbuf_all + warp * MAXG * 4;
-  const int nbw = P / NW;          // positions of a stage this warp takes
   const int my_h = lane % GP;      // after the transpose-reduce: lane -> (pos, head)
   const int my_p = lane / GP;
+  const int grp = warp / wsz, wj = warp % wsz;
 
-  int consumed = 0;
-  for (int st = 0; st < nst; ++st) {
+  for (int st = grp; st < nst; st += ngrp) {
     const int s = st % ns;
-    const bool ok = mbar_wait(&sh->full[s], (st / ns) & 1, &sh->abort_flag, a.res, 5);
-    if (ok) {
-      consumed = st + 1;
+    // warp-uniform: a stage is either consumed by the whole warp or, after
+    // an abort, not at all (and then not released: no copy can be issued
+    // into a slot whose previous copy may still be in flight)
+    const bool ok = __all_sync(0xffffffffu,
+                               mbar_wait(&sh->full[s], (st / ns) & 1, &sh->abort_flag, a.res, 5));
+    if (!ok) break;
+    {
       const int cnt = min(t1, t0 + st * P + P) - (t0 + st * P);
       const KT* Ks = reinterpret_cast<const KT*>(ring + (size_t)s * a.stage_bytes);
       const KT* Vs = Ks + hd;
       for (int sb = 0; sb < nbw; sb += SB) {
-        const int p0 = warp * nbw + sb;      // first position of the sub-batch
+        const int p0 = wj * nbw + sb;        // first position of the sub-batch
         const int np = min(SB, nbw - sb);    // positions of this warp in it
         // partial dots of (position, head), then the transpose-reduce
         float v[32];
@@ -245,11 +277,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int p = 0; p < np && p0 + p < cnt; ++p) {
           float vv[DPL];
           load_row<DPL, KT>(Vs + (size_t)(p0 + p) * row + lane * DPL, vv);
+          float w[GP];
+          if constexpr (GP % 4 == 0) {
+#pragma unroll
+            for (int k = 0; k < GP / 4; ++k) {
+              const float4 t = reinterpret_cast<const float4*>(pbuf + p * GP)[k];
+              w[4 * k] = t.x; w[4 * k + 1] = t.y; w[4 * k + 2] = t.z; w[4 * k + 3] = t.w;
+            }
+          } else {
+#pragma unroll
+            for (int h = 0; h < GP; ++h) w[h] = pbuf[p * GP + h];
+          }
 #pragma unroll
           for (int h = 0; h < GP; ++h) {
-            const float w = pbuf[p * GP + h];
 #pragma unroll
-            for (int j = 0; j < DPL; ++j) o[h][j] = fmaf(w, vv[j], o[h][j]);
+            for (int j = 0; j < DPL; ++j) o[h][j] = fmaf(w[h], vv[j], o[h][j]);
           }
         }
         __syncwarp();
@@ -260,12 +302,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 
   trace_mark(a.trace, a.trace_seq, TR_LOOP);
-  // drain after an abort, then reuse the ring as merge scratch
+  // After an abort: wait (bounded) until the producer has stopped issuing,
+  // then for the last copy issued to each ring slot (earlier copies to a
+  // slot were consumed before it was refilled).  Then the ring is free to
+  // reuse as merge scratch.
+  consumer_sync();
   if (*(volatile int*)&sh->abort_flag && threadIdx.x == 0) {
+    const uint64_t t_start = gtime();
+    while (!*(volatile int*)&sh->producer_done && gtime() - t_start < 100000000ull) {
+    }
     const int issued = *(volatile int*)&sh->issued;
-    for (int t = consumed; t < issued; ++t) {
+    for (int s2 = 0; s2 < ns && s2 < issued; ++s2) {
+      const int t = s2 + ((issued - 1 - s2) / ns) * ns;
       int dummy = 0;
-      mbar_wait(&sh->full[t % ns], (t / ns) & 1, &dummy, a.res, 6, 100000000ull);
+      mbar_wait(&sh->full[s2], (t / ns) & 1, &dummy, a.res, 6, 100000000ull);
     }
   }
   consumer_sync();
@@ -284,89 +334,185 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   }
   consumer_sync();
+  float* cta_ml = sm_o + NW * G * hd;  // CL: this CTA's combined state
+  float* cta_o = cta_ml + MAXG * 2;
   const size_t pbase = ((size_t)kvh * S + split) * G;
   for (int idx = threadIdx.x; idx < G * hd; idx += NW * 32) {
     const int h = idx / hd, d = idx % hd;
+    // all NW warps' values loaded up front (independent), then combined
+    float mw[NW], lw[NW], ow[NW];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      mw[w] = sm_ml[(w * MAXG + h) * 2];
+      lw[w] = sm_ml[(w * MAXG + h) * 2 + 1];
+      ow[w] = sm_o[((size_t)w * G + h) * hd + d];
+    }
     float M = -INFINITY;
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_ml[(w * MAXG + h) * 2]);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, mw[w]);
     float L = 0.0f, O = 0.0f;
     if (M != -INFINITY) {
+#pragma unroll
       for (int w = 0; w < NW; ++w) {
-        const float mw = sm_ml[(w * MAXG + h) * 2];
-        if (mw == -INFINITY) continue;
-        const float e = expf(mw - M);
-        L = fmaf(sm_ml[(w * MAXG + h) * 2 + 1], e, L);
-        O = fmaf(sm_o[((size_t)w * G + h) * hd + d], e, O);
+        const float e = mw[w] == -INFINITY ? 0.0f : expf(mw[w] - M);
+        L = fmaf(lw[w], e, L);
+        O = fmaf(ow[w], e, O);
       }
     }
-    a.part_o[(pbase + h) * hd + d] = O;
-    if (d == 0) {
-      a.part_ml[(pbase + h) * 2] = M;
-      a.part_ml[(pbase + h) * 2 + 1] = L;
+    if constexpr (CL) {
+      cta_o[idx] = O;
+      if (d == 0) {
+        cta_ml[h * 2] = M;
+        cta_ml[h * 2 + 1] = L;
+      }
+    } else {
+      a.part_o[(pbase + h) * hd + d] = O;
+      if (d == 0) {
+        a.part_ml[(pbase + h) * 2] = M;
+        a.part_ml[(pbase + h) * 2 + 1] = L;
+      }
     }
   }
-  // publish: the CTA barrier orders every thread's partial stores before
-  // thread 0's device-scope fence and count (release); the CTA that brings
-  // the count to S fences again before reading the others' partials (acquire)
-  consumer_sync();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(a.counters + kvh, 1u);
-    const bool last = prev == (unsigned)S - 1;
-    if (last) __threadfence();
-    sh->last = last;
+  if constexpr (CL) {
+    cluster_sync_all();
+    trace_mark(a.trace, a.trace_seq, 5);  // partials visible to the cluster
+    // merge slice `rank` of the G*hd outputs: whole warps, whole blocks
+    const int gh = G * hd;
+    const uint32_t rank = cluster_ctarank();
+    const int chunk = align_up((gh + S - 1) / S, 32);
+    for (int j = threadIdx.x; j < chunk; j += NW * 32) {
+      const int idx = (int)rank * chunk + j;
+      if (idx >= gh) break;  // uniform per warp
+      const int h = idx / hd;
+      float ms[16], ls[16], os[16];
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2) {
+        if (s2 < S) {
+          ms[s2] = ld_cluster_f32(cta_ml + h * 2, s2);
+          ls[s2] = ld_cluster_f32(cta_ml + h * 2 + 1, s2);
+          os[s2] = ld_cluster_f32(cta_o + idx, s2);
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2)
+        if (s2 < S) M = fmaxf(M, ms[s2]);
+      float L = 0.0f, O = 0.0f;
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2) {
+        if (s2 < S) {
+          const float e = ms[s2] == -INFINITY ? 0.0f : expf(ms[s2] - M);
+          L = fmaf(ls[s2], e, L);
+          O = fmaf(os[s2], e, O);
+        }
+      }
+      const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
+      a.out[(size_t)kvh * gh + idx] = v;
+      quant_block(v, (kvh * gh + idx) >> 5, lane, a.out_d, a.out_q);
+    }
+    trace_mark(a.trace, a.trace_seq, 7);  // merged
+    cluster_sync_all();  // the others' reads of this CTA's shared memory are done
+    trace_mark(a.trace, a.trace_seq, TR_EXIT);
+    return;
   }
+  // publish: the CTA barrier orders every thread's partial stores before
+  // thread 0's acquire-release count at device scope; in the CTA that brings
+  // the count to S the same operation acquires the other CTAs' partials, and
+  // the CTA barrier after it extends that to every thread's reads.
+  consumer_sync();
+  if (threadIdx.x == 0) sh->last = atom_add_acq_rel_gpu(a.counters + kvh, 1u) == (unsigned)S - 1;
   consumer_sync();
   trace_mark(a.trace, a.trace_seq, 5);  // partial published
   if (!*(volatile int*)&sh->last) {
     trace_mark(a.trace, a.trace_seq, TR_EXIT);
     return;
   }
-  // Merge the splits of this kv head.  Their (m, l) pairs, then the split
-  // weights e_s = exp(m_s - M) per head, go to shared memory; the partial
-  // outputs are staged through the ring in chunks of splits with every
-  // thread's 16-byte loads in flight at once, and accumulated in split order.
+  // Merge the splits of this kv head in split order.  One round trip stages
+  // every split's (m, l) and the first chunk of partial outputs (all loads of
+  // a thread in flight at once); then the split weights e_s = exp(m_s - M)
+  // per head and their sums, then the weighted partial outputs.
   const int gh = G * hd;
-  float* sm_split = reinterpret_cast<float*>(ring);             // [S][G][2]
-  float* sm_w = sm_split + align_up(S * G * 2, 4);              // [S][G] weights
-  float* sm_tot = sm_w + align_up(S * G, 4);                    // [G] sum of l_s e_s
-  float* sm_part = sm_tot + align_up(MAXG, 4);                  // [chunk][G][hd]
-  for (int i = threadIdx.x; i < S * G * 2; i += NW * 32)
-    sm_split[i] = __ldcg(a.part_ml + (size_t)kvh * S * G * 2 + i);
-  consumer_sync();
-  if (threadIdx.x < G) {
-    const int h = threadIdx.x;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, sm_split[(s2 * G + h) * 2]);
-    float L = 0.0f;
-    for (int s2 = 0; s2 < S; ++s2) {
-      const float ms = sm_split[(s2 * G + h) * 2];
-      const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
-      sm_w[s2 * G + h] = e;
-      L = fmaf(sm_split[(s2 * G + h) * 2 + 1], e, L);
-    }
-    sm_tot[h] = L;
-  }
-  const int ring_bytes = a.nstages * a.stage_bytes;
-  const int used = (int)((reinterpret_cast<uint8_t*>(sm_part) - ring));
-  const int chunk_s = max(1, (ring_bytes - used) / (gh * 4));
-  float acc2[4] = {0.f, 0.f, 0.f, 0.f};  // outputs idx = threadIdx.x + k * 256
-  for (int c0 = 0; c0 < S; c0 += chunk_s) {
+  const int nml = S * G * 2;                              // <= 12 * 256
+  float* sm_split = reinterpret_cast<float*>(ring);       // [S][G][2]
+  float* sm_w = sm_split + align_up(nml, 4);              // [S][G] weights
+  float* sm_tot = sm_w + align_up(S * G, 4);              // [G] sum of l_s e_s
+  float* sm_part = sm_tot + align_up(MAXG, 4);            // [chunk][G][hd]
+  const int used = (int)(reinterpret_cast<uint8_t*>(sm_part) - ring);
+  const int chunk_s = max(1, (a.nstages * a.stage_bytes - used) / (gh * 4));
+  const float* ml_src = a.part_ml + (size_t)kvh * nml;
+  auto stage_chunk = [&](int c0, bool with_ml) {
+    constexpr int R = 12;
     const int cs = min(chunk_s, S - c0);
-    consumer_sync();  // previous chunk consumed (and sm_w ready)
     const float4* src = reinterpret_cast<const float4*>(a.part_o + ((size_t)kvh * S + c0) * gh);
     float4* dst = reinterpret_cast<float4*>(sm_part);
     const int n4 = cs * gh / 4;
-    for (int i = threadIdx.x; i < n4; i += NW * 32) dst[i] = __ldcg(src + i);
-    consumer_sync();
-    trace_mark(a.trace, a.trace_seq, 6);  // split partials staged
+    for (int base = 0; base < n4 || (with_ml && base == 0); base += R * NW * 32) {
+      float mr[R];
+      float4 r[R];
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const int i = threadIdx.x + k * NW * 32;
+        mr[k] = (with_ml && base == 0 && i < nml) ? __ldcg(ml_src + i) : 0.0f;
+        r[k] = base + i < n4 ? __ldcg(src + base + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const int i = threadIdx.x + k * NW * 32;
+        if (with_ml && base == 0 && i < nml) sm_split[i] = mr[k];
+        if (base + i < n4) dst[base + i] = r[k];
+      }
+    }
+  };
+  stage_chunk(0, true);
+  consumer_sync();
+  trace_mark(a.trace, a.trace_seq, 6);  // split partials staged
+  // warp h: the maximum M_h of the splits' m, their weights and
+  // L_h = sum l_s e_s (butterfly reductions: a fixed order)
+  for (int h = warp; h < G; h += NW) {
+    float M = -INFINITY;
+    for (int s0 = 0; s0 < S; s0 += 32) {
+      const int s2 = s0 + lane;
+      M = fmaxf(M, warp_max(s2 < S ? sm_split[(s2 * G + h) * 2] : -INFINITY));
+    }
+    float L = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 32) {
+      const int s2 = s0 + lane;
+      float le = 0.0f;
+      if (s2 < S) {
+        const float ms = sm_split[(s2 * G + h) * 2];
+        const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
+        sm_w[s2 * G + h] = e;
+        le = sm_split[(s2 * G + h) * 2 + 1] * e;
+      }
+      L += warp_sum(le);
+    }
+    if (lane == 0) sm_tot[h] = L;
+  }
+  consumer_sync();
+  float acc2[4] = {0.f, 0.f, 0.f, 0.f};  // outputs idx = threadIdx.x + k * 256
+  for (int c0 = 0; c0 < S; c0 += chunk_s) {
+    if (c0) {
+      consumer_sync();  // previous chunk consumed
+      stage_chunk(c0, false);
+      consumer_sync();
+    }
+    const int cs = min(chunk_s, S - c0);
+#pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int idx = threadIdx.x + k * NW * 32;
-      if (idx >= gh) break;
-      const int h = idx / hd;
-      float O = acc2[k];
-      for (int s2 = 0; s2 < cs; ++s2) O = fmaf(sm_part[s2 * gh + idx], sm_w[(c0 + s2) * G + h], O);
-      acc2[k] = O;
+      if (idx < gh) {
+        const int h = idx / hd;
+        // four independent partial sums, combined in a fixed order
+        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+        int s2 = 0;
+        for (; s2 + 4 <= cs; s2 += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            o4[u] = fmaf(sm_part[(s2 + u) * gh + idx], sm_w[(c0 + s2 + u) * G + h], o4[u]);
+        }
+        for (; s2 < cs; ++s2) o4[0] = fmaf(sm_part[s2 * gh + idx], sm_w[(c0 + s2) * G + h], o4[0]);
+        acc2[k] += (o4[0] + o4[1]) + (o4[2] + o4[3]);
+      }
     }
   }
   trace_mark(a.trace, a.trace_seq, 7);  // merged

@@ -102,6 +102,33 @@ __device__ __forceinline__ void touch_page(const void* p) {
   unsigned v;
   asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
 }
+// Device-scope atomic add with acquire-release semantics; returns the old value.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+// Thread-block cluster helpers (distributed shared memory).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster: release this CTA's shared-memory
+// writes, acquire the others'.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The float at the same shared-memory offset as p in CTA `rank` of the cluster.
+__device__ __forceinline__ float ld_cluster_f32(const float* p, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
+  return v;
+}
 // barrier 1: the NW consumer warps only (the producer warp never joins)
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");

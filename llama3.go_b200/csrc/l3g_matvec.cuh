@@ -62,6 +62,7 @@ struct MatvecSmem {
   int best_i[NW];
   int abort_flag;
   int issued;
+  int producer_done;
   int last;
 };
 constexpr int MV_HEAD = 1024;
@@ -277,6 +278,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     for (int s = 0; s < RED_SLOTS; ++s) sh->cnt[s] = 0;
     sh->abort_flag = 0;
     sh->issued = 0;
+    sh->producer_done = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -296,6 +298,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
         bulk_g2s(ring + (size_t)s * tb, src, tb, &sh->full[s]);
         *(volatile int*)&sh->issued = t + 1;
       }
+      *(volatile int*)&sh->producer_done = 1;
     }
     return;
   }
@@ -332,13 +335,15 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
   for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
-  int consumed = 0;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % ns;
-    const bool ok = mbar_wait(&sh->full[s], (t / ns) & 1, &sh->abort_flag, a.res, 2);
+    // warp-uniform; after an abort the tile is neither used nor released (no
+    // copy can then be issued into a slot whose previous copy may be in flight)
+    const bool ok = __all_sync(0xffffffffu,
+                               mbar_wait(&sh->full[s], (t / ns) & 1, &sh->abort_flag, a.res, 2));
+    if (!ok) break;
     const int slice = t % nsl;
-    if (ok) {
-      consumed = t + 1;
+    {
       const uint8_t* tile = ring + (size_t)s * tb;
       const uint8_t* wq = tile + (size_t)warp * RPW * ck;
       const __half* wd = reinterpret_cast<const __half*>(tile + (size_t)wr * ck) + warp * RPW * nbk;
@@ -451,12 +456,18 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     }
   }
 
-  // after an abort, wait (bounded) for copies still in flight to this ring
+  // After an abort: wait (bounded) until the producer has stopped issuing,
+  // then for the last copy issued to each ring slot (earlier copies to a
+  // slot were consumed before it was refilled).
   if (*(volatile int*)&sh->abort_flag && threadIdx.x == 0) {
+    const uint64_t t_start = gtime();
+    while (!*(volatile int*)&sh->producer_done && gtime() - t_start < 100000000ull) {
+    }
     const int issued = *(volatile int*)&sh->issued;
-    for (int t = consumed; t < issued; ++t) {
+    for (int s2 = 0; s2 < ns && s2 < issued; ++s2) {
+      const int t = s2 + ((issued - 1 - s2) / ns) * ns;
       int dummy = 0;
-      mbar_wait(&sh->full[t % ns], (t / ns) & 1, &dummy, a.res, 3, 100000000ull);
+      mbar_wait(&sh->full[s2], (t / ns) & 1, &dummy, a.res, 3, 100000000ull);
     }
   }
   trace_mark(a.trace, a.trace_seq, TR_EXIT);

@@ -171,17 +171,25 @@ static int setup_kernels() {
     SETRMS(EPI_LOGITS);
 #undef SETRMS
 #undef SETMV4
-#define SETAT(D, T)                  \
-  SETK((k_attention<D, T, 1>));      \
-  SETK((k_attention<D, T, 2>));      \
-  SETK((k_attention<D, T, 4>));      \
-  SETK((k_attention<D, T, 8>))
+#define SETCL(k)                                                                   \
+  SETK(k);                                                                         \
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1)
+#define SETAT(D, T)                      \
+  SETK((k_attention<D, T, 1, false>));   \
+  SETK((k_attention<D, T, 2, false>));   \
+  SETK((k_attention<D, T, 4, false>));   \
+  SETK((k_attention<D, T, 8, false>));   \
+  SETCL((k_attention<D, T, 1, true>));   \
+  SETCL((k_attention<D, T, 2, true>));   \
+  SETCL((k_attention<D, T, 4, true>));   \
+  SETCL((k_attention<D, T, 8, true>))
     SETAT(1, float);
     SETAT(2, float);
     SETAT(4, float);
     SETAT(2, __half);
     SETAT(4, __half);
 #undef SETAT
+#undef SETCL
     SETK(k_topk_final);
     SETK(k_embed);
     SETK(k_advance);
@@ -334,6 +342,10 @@ struct LayerW {
 struct l3g_model {
   l3g_hparams hp{};
   int world = 1, rank = 0, device = 0, kv_f16 = 0, nsm = 1;
+  // live workspaces: their captured step graphs hold NCCL calls on `comm`,
+  // so they are released before the communicator is destroyed
+  std::mutex ws_mu;
+  std::vector<l3g_workspace*> workspaces;
   int hd = 0, hq_l = 0, hkv_l = 0, group = 1, ff_l = 0, v_l = 0, v_off = 0;
   int rope_half = 0;
   std::vector<double> inv_freq;
@@ -393,11 +405,18 @@ static void free_mat(DevMat& m) {
   m.buf = nullptr;
 }
 
+static void ws_detach(l3g_workspace* ws);  // releases its graphs, forgets the model
+
 extern "C" void l3g_model_free(l3g_model* m) {
   if (!m) return;
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(m->device);
+  {
+    std::lock_guard<std::mutex> lk(m->ws_mu);
+    for (l3g_workspace* ws : m->workspaces) ws_detach(ws);
+    m->workspaces.clear();
+  }
   for (auto& L : m->layers) {
     free_mat(L.qkv);
     free_mat(L.wo);
@@ -640,6 +659,7 @@ extern "C" int l3g_model_hparams(const l3g_model* m, l3g_hparams* out) {
 // ---------------------------------------------------------------------------
 struct l3g_state {
   l3g_model* m = nullptr;
+  int device = 0;
   int ctx = 0, pos = 0;
   void* kv = nullptr;      // [layer][local kv head][ctx][K hd | V hd]
   size_t layer_elems = 0;  // per layer: local kv heads * ctx * 2 * hd
@@ -657,7 +677,7 @@ static uint64_t next_serial() {
 
 extern "C" void l3g_state_free(l3g_state* s) {
   if (!s) return;
-  cudaSetDevice(s->m->device);
+  cudaSetDevice(s->device);
   if (s->kv) cudaFree(s->kv);
   if (s->rope_cos) cudaFree(s->rope_cos);
   if (s->rope_sin) cudaFree(s->rope_sin);
@@ -672,6 +692,7 @@ extern "C" int l3g_state_new(l3g_model* m, int32_t ctx, l3g_state** out) {
   CUDA_TRY(cudaSetDevice(m->device));
   auto* s = new l3g_state();
   s->m = m;
+  s->device = m->device;
   s->ctx = ctx;
   s->serial = next_serial();
   s->layer_elems = (size_t)m->hkv_l * ctx * 2 * m->hd;
@@ -770,6 +791,7 @@ struct StepGraph {
 
 struct l3g_workspace {
   l3g_model* m = nullptr;
+  int device = 0;
   int ctx = 0, topk = 40;
   cudaStream_t stream = nullptr;
   int* d_io = nullptr;
@@ -801,6 +823,7 @@ struct l3g_workspace {
   int* h_tk_ids = nullptr;
   float* h_tk_logits = nullptr;
   int n_splits = 1, att_P = 16, att_ns = 3, att_stage = 0, att_smem = 0, att_gp = 1;
+  int att_cluster = 0;         // > 0: the splits of a kv head form one cluster
   int tk_chunks = 0;
   int* d_tokens = nullptr;     // [ctx] tokens of a device-fed greedy run
   int kernels = 0;             // kernel launches counted during a capture
@@ -830,11 +853,80 @@ static void ws_release(l3g_workspace* ws) {
   if (ws->stream) cudaStreamDestroy(ws->stream);
 }
 
+static void ws_detach(l3g_workspace* ws) {
+  for (auto& g : ws->graphs) cudaGraphExecDestroy(g.exec);
+  ws->graphs.clear();
+  ws->m = nullptr;
+}
+
 extern "C" void l3g_workspace_free(l3g_workspace* ws) {
   if (!ws) return;
-  cudaSetDevice(ws->m->device);
+  if (ws->m) {
+    std::lock_guard<std::mutex> lk(ws->m->ws_mu);
+    auto& v = ws->m->workspaces;
+    v.erase(std::remove(v.begin(), v.end(), ws), v.end());
+  }
+  cudaSetDevice(ws->device);
   ws_release(ws);
   delete ws;
+}
+
+// Cluster merge of the attention splits: 16 splits per kv head as one
+// (non-portable) cluster, used when clusters for every local kv head can be
+// resident at once and they give at least half the SMs a CTA.
+// L3G_ATT_CLUSTER=0 forces the global-memory merge, =1 the 16-CTA cluster
+// merge whenever the clusters fit, =N (2..16) clusters of N CTAs (N splits)
+// whenever they fit (knobs for tests and experiments).
+template <int DPL, typename KT>
+static void max_attention_clusters(const l3g_workspace* ws, int cs, int* n) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ws->m->hkv_l, cs);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = ws->att_smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = cs;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+  switch (ws->att_gp) {
+    case 1: e = cudaOccupancyMaxActiveClusters(n, k_attention<DPL, KT, 1, true>, &cfg); break;
+    case 2: e = cudaOccupancyMaxActiveClusters(n, k_attention<DPL, KT, 2, true>, &cfg); break;
+    case 4: e = cudaOccupancyMaxActiveClusters(n, k_attention<DPL, KT, 4, true>, &cfg); break;
+    case 8: e = cudaOccupancyMaxActiveClusters(n, k_attention<DPL, KT, 8, true>, &cfg); break;
+    default: e = cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *n = 0;
+  }
+}
+
+static void choose_attention_cluster(l3g_workspace* ws) {
+  const l3g_model* m = ws->m;
+  ws->att_cluster = 0;
+  const char* env = getenv("L3G_ATT_CLUSTER");
+  if (env && atoi(env) == 0) return;
+  const int knob = env ? atoi(env) : -1;
+  const bool force = knob >= 1;
+  const int cs = knob >= 2 && knob <= 16 ? knob : 16;
+  if (!force && m->hkv_l * cs * 2 < m->nsm) return;  // too few CTAs: keep the splits
+  int n = 0;
+  const int dpl = m->hd / 32;
+  if (m->kv_f16) {
+    if (dpl == 2) max_attention_clusters<2, __half>(ws, cs, &n);
+    if (dpl == 4) max_attention_clusters<4, __half>(ws, cs, &n);
+  } else {
+    if (dpl == 1) max_attention_clusters<1, float>(ws, cs, &n);
+    if (dpl == 2) max_attention_clusters<2, float>(ws, cs, &n);
+    if (dpl == 4) max_attention_clusters<4, float>(ws, cs, &n);
+  }
+  if (n < m->hkv_l) return;
+  ws->att_cluster = cs;
+  ws->n_splits = cs;
+  return;
 }
 
 extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_workspace** out) {
@@ -860,8 +952,9 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   ws->att_gp = 1;
   while (ws->att_gp < G) ws->att_gp <<= 1;
   ws->n_splits = std::max(1, std::min(m->nsm / m->hkv_l, (ctx + ws->att_P - 1) / ws->att_P));
-  const int scratch = std::max((NW * MAXG * 2 + NW * G * hd) * 4, ws->n_splits * G * 2 * 4);
+  const int scratch = std::max(at_scratch_floats(G, hd) * 4, ws->n_splits * G * 2 * 4);
   ws->att_smem = at_ring_offset() + std::max(ws->att_ns * ws->att_stage, scratch);
+  choose_attention_cluster(ws);
   const int vloc = m->v_l;
   ws->tk_chunks = (m->v_l * m->world + TOPK_CHUNK - 1) / TOPK_CHUNK;
   cudaError_t e = cudaStreamCreateWithFlags(&ws->stream, cudaStreamNonBlocking);
@@ -919,6 +1012,11 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
     delete ws;
     return l3g_fail(L3G_E_CUDA, "workspace allocation: %s", cudaGetErrorString(e));
   }
+  ws->device = m->device;
+  {
+    std::lock_guard<std::mutex> lk(m->ws_mu);
+    m->workspaces.push_back(ws);
+  }
   *out = ws;
   return L3G_OK;
 }
@@ -968,16 +1066,53 @@ static cudaError_t launch_mv(const DevMat& w, const MatvecArgs& a, int nsm, cuda
   }
 }
 
+// Launch with programmatic dependent launch and, when cluster_y > 0, thread
+// block clusters of (1, cluster_y, 1).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_cl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, int cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (!g_serialize) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <int DPL, typename KT, bool CL>
+static cudaError_t launch_attention_c(int gp, const AttnArgs& a, cudaStream_t st, dim3 grid,
+                                      size_t smem, int cluster_y) {
+  switch (gp) {
+    case 1: return launch_cl(k_attention<DPL, KT, 1, CL>, grid, dim3(NTHREADS), smem, st, cluster_y, a);
+    case 2: return launch_cl(k_attention<DPL, KT, 2, CL>, grid, dim3(NTHREADS), smem, st, cluster_y, a);
+    case 4: return launch_cl(k_attention<DPL, KT, 4, CL>, grid, dim3(NTHREADS), smem, st, cluster_y, a);
+    case 8: return launch_cl(k_attention<DPL, KT, 8, CL>, grid, dim3(NTHREADS), smem, st, cluster_y, a);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <int DPL, typename KT>
 static cudaError_t launch_attention_g(const l3g_workspace* ws, const AttnArgs& a, cudaStream_t st,
                                       dim3 grid, size_t smem) {
-  switch (ws->att_gp) {
-    case 1: return launch(k_attention<DPL, KT, 1>, grid, dim3(NTHREADS), smem, st, a);
-    case 2: return launch(k_attention<DPL, KT, 2>, grid, dim3(NTHREADS), smem, st, a);
-    case 4: return launch(k_attention<DPL, KT, 4>, grid, dim3(NTHREADS), smem, st, a);
-    case 8: return launch(k_attention<DPL, KT, 8>, grid, dim3(NTHREADS), smem, st, a);
-    default: return cudaErrorInvalidValue;
-  }
+  if (ws->att_cluster)
+    return launch_attention_c<DPL, KT, true>(ws->att_gp, a, st, grid, smem, ws->att_cluster);
+  return launch_attention_c<DPL, KT, false>(ws->att_gp, a, st, grid, smem, 0);
 }
 
 static cudaError_t launch_attention(const l3g_workspace* ws, const AttnArgs& a, cudaStream_t st) {
@@ -1447,6 +1582,14 @@ extern "C" int l3g_trace_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int
 extern "C" int l3g_workspace_kernels_per_step(l3g_workspace* ws, int32_t* n) {
   if (!ws || !n) return l3g_fail(L3G_E_INVALID, "null argument");
   *n = ws->kernels_greedy;
+  return L3G_OK;
+}
+
+extern "C" int l3g_workspace_attention_layout(const l3g_workspace* ws, int32_t* splits,
+                                              int32_t* cluster) {
+  if (!ws || !splits || !cluster) return l3g_fail(L3G_E_INVALID, "null argument");
+  *splits = ws->n_splits;
+  *cluster = ws->att_cluster;
   return L3G_OK;
 }
 

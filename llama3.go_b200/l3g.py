@@ -110,6 +110,7 @@ def lib():
         "l3g_decode_greedy": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.POINTER(C.c_int32),
                                         C.POINTER(C.c_float)]),
         "l3g_workspace_kernels_per_step": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+        "l3g_workspace_attention_layout": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
         "l3g_profile_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_float),
                                        C.POINTER(C.c_int32)]),
         "l3g_trace_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_uint64), C.POINTER(C.c_int32),
@@ -364,6 +365,12 @@ class Workspace:
         v = C.c_int32()
         _check(lib().l3g_workspace_kernels_per_step(self._h, C.byref(v)))
         return v.value
+
+    def attention_layout(self) -> tuple[int, int]:
+        """(splits per kv head, cluster size or 0)."""
+        sp, cl = C.c_int32(), C.c_int32()
+        _check(lib().l3g_workspace_attention_layout(self._h, C.byref(sp), C.byref(cl)))
+        return sp.value, cl.value
 
     def Close(self):
         if self._h:

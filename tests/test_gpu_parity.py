@@ -253,6 +253,54 @@ def test_long_context_split_attention(gpu_lib, oracle_mod):
     assert rel_l2(K, K0) < tol and rel_l2(V, V0) < tol
 
 
+@pytest.mark.parametrize("mode", ["0", "1"])
+def test_attention_merge_modes(gpu_lib, oracle_mod, monkeypatch, mode):
+    """The splits of a kv head merge through global partials (0) or as one
+    thread-block cluster over distributed shared memory (1); both match the
+    reference at a long context (every split busy) and a short one (most
+    splits empty)."""
+    import synthetic
+    monkeypatch.setenv("L3G_ATT_CLUSTER", mode)
+    for name, n, tail in (("small-hd128", 1500, 3), ("tiny-gqa", 5, 3)):
+        cfg, T = synthetic_model(name)
+        ids = synthetic.prompt_ids(cfg, n, seed=5)
+        R = ReferenceRuns(oracle_mod, cfg, T, ids[-tail:], n + 8, with_f64=False, prefix_ids=ids[:-tail])
+        m = _load_gpu(gpu_lib, cfg, T)
+        s = m.NewState(n + 8)
+        ws = m.NewWorkspace(n + 8, 40)
+        splits, cluster = ws.attention_layout()
+        assert (cluster == 16 and splits == 16) if mode == "1" else cluster == 0
+        m.Prefill(s, ids[:-tail], ws)
+        logits = np.empty(cfg.vocab, np.float32)
+        errs = []
+        for i, t in enumerate(ids[-tail:]):
+            m.ForwardIntoWorkspace(s, int(t), logits, ws)
+            errs.append(rel_l2(logits, R.cgo[i]))
+        assert max(errs) < R.tol(), (name, errs, R.band())
+        attn = ws.read(gpu_lib.BUF_ATTN, cfg.n_heads * cfg.head_dim)
+        assert rel_l2(attn, R.cgo_model.buffer("attn")) < R.tol()
+
+
+def test_free_order_does_not_matter(gpu_lib):
+    """Model freed before its state and workspace (whose captured graphs the
+    model releases first): no fault, and the later frees are harmless."""
+    import synthetic
+    cfg, T = synthetic_model("tiny")
+    m = _load_gpu(gpu_lib, cfg, T)
+    s = m.NewState(16)
+    ws = m.NewWorkspace(16, 40)
+    m.ForwardArgmax(s, 1, ws)
+    m.Close()
+    ws.Close()
+    s.Close()
+    m2 = _load_gpu(gpu_lib, cfg, T)  # the device is still usable
+    s2, ws2 = m2.NewState(16), m2.NewWorkspace(16, 40)
+    m2.ForwardArgmax(s2, 1, ws2)
+    ws2.Close()
+    s2.Close()
+    m2.Close()
+
+
 def test_fp16_kv_cache(gpu_lib, oracle_mod):
     import synthetic
     cfg, T = synthetic_model("small")

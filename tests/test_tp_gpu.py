@@ -1,0 +1,102 @@
+"""Tensor parallel on 2 GPUs: one process per GPU, the library's own NCCL
+communicator (the unique id travels through a file), the shard split of
+l3g_shard_plan.  Rank 0's logits must match the reference within the same
+band as the single-GPU path, and both ranks must agree on every greedy id.
+Skipped on a machine with fewer than two GPUs.
+"""
+import os
+import time
+
+import numpy as np
+import pytest
+
+from conftest import synthetic_model
+from refspread import ReferenceRuns, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+CONFIG, N_TOK, CTX = "mid", 12, 64
+
+
+def _rank_main(rank, world, id_path, out_dir):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for sub in ("llama3.go_b200", "oracle", "tests"):
+        sys.path.insert(0, os.path.join(root, sub))
+    import l3g
+    import synthetic
+    from conftest import synthetic_model as sm
+    cfg, T = sm(CONFIG)
+    if rank == 0:
+        nid = l3g.nccl_unique_id()
+        with open(id_path + ".tmp", "wb") as f:
+            f.write(nid)
+        os.replace(id_path + ".tmp", id_path)
+    else:
+        t0 = time.time()
+        while not os.path.exists(id_path):
+            if time.time() - t0 > 120:
+                raise TimeoutError("no NCCL id from rank 0")
+            time.sleep(0.05)
+        nid = open(id_path, "rb").read()
+    opts = l3g.default_options(world, rank, rank, l3g.L3G_KV_F32, nid)
+    m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, opts)
+    s = m.NewState(CTX)
+    ws = m.NewWorkspace(CTX, 40)
+    ids = synthetic.prompt_ids(cfg, N_TOK, seed=17)
+    logits = np.empty(cfg.vocab, np.float32)
+    out = []
+    for t in ids:
+        m.ForwardIntoWorkspace(s, int(t), logits, ws)
+        out.append(logits.copy())
+    # greedy continuation through the device argmax (allgathered per rank)
+    tok, greedy = int(ids[-1]), []
+    for _ in range(8):
+        tok, _ = m.ForwardArgmax(s, tok, ws)
+        greedy.append(tok)
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=np.stack(out),
+             greedy=np.array(greedy, np.int32))
+    ws.Close()
+    s.Close()
+    m.Close()
+
+
+def test_tp2_matches_reference_and_single_gpu(gpu_lib, oracle_mod, tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    import synthetic
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    id_path = str(tmp_path / "nccl_id")
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, id_path, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    deadline = time.time() + 600
+    for p in procs:
+        p.join(timeout=max(1.0, deadline - time.time()))
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+        p.join(10)
+    assert not alive, "a tensor-parallel rank did not finish"
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    r0 = np.load(tmp_path / "rank0.npz")
+    r1 = np.load(tmp_path / "rank1.npz")
+    assert np.array_equal(r0["greedy"], r1["greedy"])
+    assert np.array_equal(r0["logits"], r1["logits"])  # allgathered: identical on every rank
+
+    cfg, T = synthetic_model(CONFIG)
+    ids = synthetic.prompt_ids(cfg, N_TOK, seed=17)
+    R = ReferenceRuns(oracle_mod, cfg, T, ids, CTX, with_f64=False)
+    errs = [rel_l2(r0["logits"][i], R.cgo[i]) for i in range(N_TOK)]
+    assert max(errs) < R.tol(), (errs, R.band())
+    # the single-GPU library on the same inputs
+    m = gpu_lib.LoadModelFromTensors(gpu_lib.hparams_for(cfg), T, gpu_lib.default_options(device=0))
+    s = m.NewState(CTX)
+    ws = m.NewWorkspace(CTX, 40)
+    logits = np.empty(cfg.vocab, np.float32)
+    for i, t in enumerate(ids):
+        m.ForwardIntoWorkspace(s, int(t), logits, ws)
+        assert rel_l2(r0["logits"][i], logits) < R.tol()
