@@ -299,8 +299,9 @@ def time_matvec_kernel(l3g, cfg, seed, hbm):
 def trace_summary(m, s, ws, tok, pos, reps=3):
     """Device timeline of one step replayed as its graph (kernels overlapping
     as in the timed loop): per kind, the time between consecutive kernel
-    completions (sums to the step), the span from entry to exit, and the
-    time from dependency release to the end of the prologue."""
+    completions (sums to the step), the span from entry to exit, the time
+    from dependency release to the end of the prologue, and the tail from
+    the last CTA's end of tile loop to the last exit."""
     import numpy as np
     acc = {}
     step_us = []
@@ -314,18 +315,23 @@ def trace_summary(m, s, ws, tok, pos, reps=3):
             ent = st[live, 0].min()
             ext = st[live, 4].max()
             released = st[live, 1].min()
-            d = acc.setdefault(kind, {"critical": 0.0, "span": 0.0, "prologue": 0.0, "wake": 0.0, "n": 0})
+            d = acc.setdefault(kind, {"critical": 0.0, "span": 0.0, "prologue": 0.0, "wake": 0.0,
+                                      "tail": 0.0, "n": 0})
             d["critical"] += (ext - prev_exit) / 1e3
             d["span"] += (ext - ent) / 1e3
             d["wake"] += max(0, released - prev_exit) / 1e3
             pro = st[live, 2]
             if (pro > 0).all():
                 d["prologue"] += (pro.max() - released) / 1e3
+            loop = st[live, 3]
+            if (loop > 0).all():
+                d["tail"] += max(0, ext - loop.max()) / 1e3
             d["n"] += 1
             prev_exit = max(prev_exit, ext)
         step_us.append((prev_exit - first) / 1e3)
     out = {k: {"critical_us": round(v["critical"] / reps, 1), "avg_span_us": round(v["span"] / v["n"], 2),
                "avg_wake_us": round(v["wake"] / v["n"], 2), "avg_prologue_us": round(v["prologue"] / v["n"], 2),
+               "avg_tail_us": round(v["tail"] / v["n"], 2),
                "launches": v["n"] // reps}
            for k, v in sorted(acc.items(), key=lambda kv: -kv[1]["critical"])}
     out["traced_step_us"] = round(float(np.mean(step_us)), 1)

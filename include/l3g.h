@@ -199,6 +199,12 @@ int l3g_workspace_kernels_per_step(l3g_workspace *ws, int32_t *n);
  * counterpart (the reference attends on one goroutine, infer.go:130-175). */
 int l3g_workspace_attention_layout(const l3g_workspace *ws, int32_t *splits,
                                    int32_t *cluster);
+/* Tensor-parallel reduction the workspace uses: 1 when the Wo / down partial
+ * sums travel over peer memory (CUDA IPC mappings, pushed by the producing
+ * matvec and summed by the next kernel), 0 for NCCL allreduces (or a single
+ * GPU).  Inspection only; no reference counterpart (the reference is one
+ * process on one CPU). */
+int l3g_workspace_tp_p2p(const l3g_workspace *ws, int32_t *p2p);
 
 /* Profiling (the device counterpart of the chat CLI's -cpuprofile,
  * cmd/go-llama-chat/main.go:35-54): runs one greedy step eagerly, each kernel

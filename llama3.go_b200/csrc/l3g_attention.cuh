@@ -38,6 +38,7 @@ struct AttnArgs {
   Result* res;
   unsigned long long* trace;  // device timeline (nullptr: off)
   int trace_seq;
+  unsigned long long wait_ns;  // bound of every wait (WAIT_TIMEOUT_NS or _PEER_NS)
 };
 
 struct AttnSmem {
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int st = 0; st < nst; ++st) {
         const int s = st % ns;
         if (st >= ns &&
-            !mbar_wait(&sh->empty[s], ((st / ns) - 1) & 1, &sh->abort_flag, a.res, 4))
+            !mbar_wait(&sh->empty[s], ((st / ns) - 1) & 1, &sh->abort_flag, a.res, 4, a.wait_ns))
           break;
         const int ta = t0 + st * P, tb = min(t1, ta + P);
         // past positions are immutable: only the stage holding this step's
@@ -214,7 +215,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // an abort, not at all (and then not released: no copy can be issued
     // into a slot whose previous copy may still be in flight)
     const bool ok = __all_sync(0xffffffffu,
-                               mbar_wait(&sh->full[s], (st / ns) & 1, &sh->abort_flag, a.res, 5));
+                               mbar_wait(&sh->full[s], (st / ns) & 1, &sh->abort_flag, a.res, 5, a.wait_ns));
     if (!ok) break;
     {
       const int cnt = min(t1, t0 + st * P + P) - (t0 + st * P);

@@ -29,6 +29,10 @@ constexpr int CTA_SMEM_SHARE = 112 * 1024;
 constexpr int TILE_TARGET = 32 * 1024;
 constexpr int MAXG = 8;                 // max query heads per kv head
 constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s
+// Waits of a tensor-parallel step: a wait can depend, directly or through the
+// kernels launched early behind it, on another GPU's progress, which host
+// skew between the ranks' processes can delay by more than the local bound.
+constexpr unsigned long long WAIT_TIMEOUT_PEER_NS = 30000000000ull;  // 30 s
 
 // device error codes (Result::err); Result::where names the wait site
 enum { ERR_NONE = 0, ERR_TIMEOUT = 1, ERR_TOKEN = 2 };
@@ -101,12 +105,32 @@ __device__ __forceinline__ void pdl_wait() {
 __device__ __forceinline__ void touch_page(const void* p) {
   unsigned v;
   asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  (void)v;
 }
 // Device-scope atomic add with acquire-release semantics; returns the old value.
 __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
   unsigned old;
   asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
+}
+// System-scope acquire load / release store (flags shared across GPUs).
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// System-scope relaxed 64-bit accesses: single-copy atomic, so a {value,
+// epoch} word written by another GPU is seen whole or not at all.
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 // Thread-block cluster helpers (distributed shared memory).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -247,13 +271,54 @@ __device__ __forceinline__ void quant_quad(float4 u, bool live, int blk, int sub
 #include "l3g_attention.cuh"
 
 // ---------------------------------------------------------------------------
+// Tensor-parallel reduction, the receiving half of the exchange (the pushing
+// half is the EPI_PUSH epilogue of the Wo / down matvecs): thread i waits for
+// elements 4i..4i+3 of every rank's slot of this phase (their epoch words,
+// bounded wait) and writes their sum, in rank order, to y.  It replaces the
+// reference's single-process residual input (infer.go:189-191, :244-246) in
+// a sharded step: y is the full Wo / down output on every rank.
+// ---------------------------------------------------------------------------
+__global__ void k_tp_reduce(const TpExchange t, float* y, Result* res,
+                            unsigned long long wait_ns) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (4 * i >= t.n) return;
+  const unsigned e = tp_epoch(t);
+  const unsigned long long* rb = t.my_recv + (size_t)(e & 1u) * t.world * t.n + 4 * i;
+  const uint64_t t_start = gtime();
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int r = 0; r < MAX_WORLD; ++r) {
+    if (r >= t.world) break;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      unsigned long long w = ld_relaxed_sys_u64(rb + (size_t)r * t.n + j);
+      while ((unsigned)(w >> 32) != e) {
+        if (gtime() - t_start > wait_ns) {
+          report(res, ERR_TIMEOUT, 8);
+          break;
+        }
+        w = ld_relaxed_sys_u64(rb + (size_t)r * t.n + j);
+      }
+      const float v = __uint_as_float((unsigned)w);
+      acc[j] = r == 0 ? v : __fadd_rn(acc[j], v);
+    }
+  }
+  reinterpret_cast<float4*>(y)[i] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// ---------------------------------------------------------------------------
 // Embedding row dequant (infer.go:513-518, tensor_read.go:128-147) from the
 // raw GGUF Q8_0 rows: x[i] = f16(d) * q[i].
 // ---------------------------------------------------------------------------
+// It also advances the workspace's step counter (the epoch base of the
+// tensor-parallel exchange), once per step on every rank.
 __global__ void k_embed(const uint8_t* emb, int vocab, int cols, const int* io,
-                        float* x, Result* res) {
+                        float* x, Result* res, unsigned* step) {
   pdl_launch_dependents();
   pdl_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *step += 1u;
   const int token = io[0];
   if (token < 0 || token >= vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) report(res, ERR_TOKEN, token);

@@ -15,7 +15,31 @@ struct Q8Tiles {
 };
 
 enum Pro { PRO_PREQ = 0, PRO_RMS = 2 };
-enum Epi { EPI_STORE = 0, EPI_QKV = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
+enum Epi { EPI_STORE = 0, EPI_QKV = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3, EPI_PUSH = 4 };
+
+// Tensor-parallel reduction over peer memory (one process per GPU, receive
+// buffers mapped with CUDA IPC).  The producer (EPI_PUSH: the Wo and down
+// matvecs, whose rows are partial sums over this rank's columns) stores each
+// row into slot `rank` of every rank's receive buffer as one 64-bit word
+// {float bits, epoch}; a naturally aligned 64-bit access is single-copy
+// atomic, so the consumer (k_tp_reduce, launched right after the producer)
+// knows an element has arrived when its epoch matches, with no fence or
+// flag.  It sums the ranks' values in rank order into this rank's y, so
+// every rank gets bit-identical sums.  Receive
+// buffers alternate between two parities by epoch: a rank cannot get two
+// phases ahead of a reader, since its next-but-one push depends on the
+// reader's push of the phase in between.
+constexpr int MAX_WORLD = 8;
+struct TpExchange {
+  int world, rank, n;                    // ranks, this rank, vector length
+  int nphase, phase;                     // epoch = *step * nphase + phase
+  const unsigned* step;                  // device step counter (k_embed)
+  unsigned long long* recv[MAX_WORLD];   // producer: rank r's buffer [2][world][n]
+  const unsigned long long* my_recv;     // consumer: this rank's buffer
+};
+__device__ __forceinline__ unsigned tp_epoch(const TpExchange& t) {
+  return *t.step * (unsigned)t.nphase + (unsigned)t.phase;
+}
 
 struct MatvecArgs {
   Q8Tiles w;
@@ -45,6 +69,8 @@ struct MatvecArgs {
   Result* res;            // error word, argmax result
   unsigned long long* trace;  // device timeline (nullptr: off)
   int trace_seq;
+  TpExchange tp_out;      // EPI_PUSH
+  unsigned long long wait_ns;  // bound of every wait (WAIT_TIMEOUT_NS or _PEER_NS)
 };
 
 // Row-group partial sums: a ring of slots, one per group in flight.  Warps
@@ -118,24 +144,26 @@ __device__ __forceinline__ void mv_prologue(const MatvecArgs& a, float* xd,
     const int nv = C >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(a.x_in);
     const float4* y4 = reinterpret_cast<const float4*>(a.y_in);
-    float4 v[VK], y[VK];
+    const bool has_y = a.y_in != nullptr;
+    // v = x + delta, one float4 of each at a time
+    float4 v[VK];
 #pragma unroll
     for (int k = 0; k < VK; ++k) {
       const int i = tid + k * NW * 32;
       v[k] = i < nv ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      y[k] = (a.y_in && i < nv) ? y4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (has_y && i < nv) {
+        const float4 y = y4[i];
+        v[k].x = __fadd_rn(v[k].x, y.x);
+        v[k].y = __fadd_rn(v[k].y, y.y);
+        v[k].z = __fadd_rn(v[k].z, y.z);
+        v[k].w = __fadd_rn(v[k].w, y.w);
+      }
     }
     const bool wx = a.x_out != nullptr && blockIdx.x == 0;
     float ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < VK; ++k) {
       const int i = tid + k * NW * 32;
-      if (a.y_in) {
-        v[k].x = __fadd_rn(v[k].x, y[k].x);
-        v[k].y = __fadd_rn(v[k].y, y[k].y);
-        v[k].z = __fadd_rn(v[k].z, y[k].z);
-        v[k].w = __fadd_rn(v[k].w, y[k].w);
-      }
       if (wx && i < nv) reinterpret_cast<float4*>(a.x_out)[i] = v[k];
       ss = fmaf(v[k].x, v[k].x, ss);
       ss = fmaf(v[k].y, v[k].y, ss);
@@ -172,10 +200,22 @@ __device__ __forceinline__ void mv_prologue(const MatvecArgs& a, float* xd,
 template <int EPI>
 __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int nrows,
                                             float v, int lane, float& best_v,
-                                            int& best_i) {
+                                            int& best_i, size_t push_off,
+                                            unsigned push_e) {
   const int row = row0 + lane;
   const bool live = lane < nrows && row < a.w.rows;
-  if constexpr (EPI == EPI_STORE) {
+  if constexpr (EPI == EPI_PUSH) {
+    // push_off: this rank's slot of this phase's parity in every receive
+    // buffer, push_e: the phase's epoch (both computed once per thread)
+    if (live && row >= a.row_lo && row < a.row_hi) {
+      const TpExchange& t = a.tp_out;
+      const unsigned long long word = ((unsigned long long)push_e << 32) | __float_as_uint(v);
+      const size_t off = push_off + row;
+#pragma unroll
+      for (int r = 0; r < MAX_WORLD; ++r)
+        if (r < t.world) st_relaxed_sys_u64(t.recv[r] + off, word);
+    }
+  } else if constexpr (EPI == EPI_STORE) {
     if (live && row >= a.row_lo && row < a.row_hi) a.out[row] = v;
   } else if constexpr (EPI == EPI_QKV) {
     const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
@@ -290,7 +330,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % ns;
         if (t >= ns &&
-            !mbar_wait(&sh->empty[s], ((t / ns) - 1) & 1, &sh->abort_flag, a.res, 1))
+            !mbar_wait(&sh->empty[s], ((t / ns) - 1) & 1, &sh->abort_flag, a.res, 1, a.wait_ns))
           break;
         const int g = gl + b + (t / nsl) * G;
         const uint8_t* src = a.w.data + ((size_t)g * nsl + (t % nsl)) * tb;
@@ -324,6 +364,13 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
   }
   pdl_wait();  // activations come from the previous kernel
   trace_mark(a.trace, a.trace_seq, TR_WAITED);
+  // EPI_PUSH: the phase's epoch and this rank's slot of its parity
+  size_t push_off = 0;
+  unsigned push_e = 0;
+  if constexpr (EPI == EPI_PUSH) {
+    push_e = tp_epoch(a.tp_out);
+    push_off = (size_t)((push_e & 1u) * a.tp_out.world + a.tp_out.rank) * a.tp_out.n;
+  }
   mv_prologue<PRO, VK>(a, xd, xqs, sh, nw);
   consumer_sync();
   trace_mark(a.trace, a.trace_seq, TR_PROLOGUE);
@@ -340,7 +387,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     // warp-uniform; after an abort the tile is neither used nor released (no
     // copy can then be issued into a slot whose previous copy may be in flight)
     const bool ok = __all_sync(0xffffffffu,
-                               mbar_wait(&sh->full[s], (t / ns) & 1, &sh->abort_flag, a.res, 2));
+                               mbar_wait(&sh->full[s], (t / ns) & 1, &sh->abort_flag, a.res, 2, a.wait_ns));
     if (!ok) break;
     const int slice = t % nsl;
     {
@@ -377,7 +424,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
         acc[r] = 0.0f;
       }
       if constexpr (RPW >= 2) {
-        mv_epilogue<EPI>(a, g * wr + warp * RPW, RPW, v, lane, best_v, best_i);
+        mv_epilogue<EPI>(a, g * wr + warp * RPW, RPW, v, lane, best_v, best_i, push_off, push_e);
       } else {
         const int slot = k % RED_SLOTS;
         int old = 0;
@@ -392,7 +439,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
           const float vv = lane < NW ? sh->red[slot][lane] : 0.0f;
           __syncwarp();
           if (lane == 0) sh->cnt[slot] = 0;
-          mv_epilogue<EPI>(a, g * wr, NW, vv, lane, best_v, best_i);
+          mv_epilogue<EPI>(a, g * wr, NW, vv, lane, best_v, best_i, push_off, push_e);
         }
       }
     }

@@ -166,6 +166,7 @@ static int setup_kernels() {
   SETMV4(PRO_RMS, E, 4); \
   SETMV4(PRO_RMS, E, 8)
     SETMV4(PRO_PREQ, EPI_STORE, 1);
+    SETMV4(PRO_PREQ, EPI_PUSH, 1);
     SETRMS(EPI_QKV);
     SETRMS(EPI_SWIGLU);
     SETRMS(EPI_LOGITS);
@@ -193,6 +194,7 @@ static int setup_kernels() {
     SETK(k_topk_final);
     SETK(k_embed);
     SETK(k_advance);
+    SETK(k_tp_reduce);
     SETK(k_topk_partial);
 #undef SETK
     rc = e == cudaSuccess ? 0 : (int)e;
@@ -824,6 +826,12 @@ struct l3g_workspace {
   float* h_tk_logits = nullptr;
   int n_splits = 1, att_P = 16, att_ns = 3, att_stage = 0, att_smem = 0, att_gp = 1;
   int att_cluster = 0;         // > 0: the splits of a kv head form one cluster
+  unsigned* d_step = nullptr;  // steps run (advanced by k_embed)
+  int* d_sync = nullptr;       // operand of the ranks' line-up after a capture
+  // tensor parallel exchange over peer memory (world > 1 and IPC available)
+  bool tp_p2p = false;
+  unsigned long long* tp_recv = nullptr;               // [2][world][n_emb] {value, epoch}
+  unsigned long long* tp_peer_recv[MAX_WORLD] = {};    // every rank's (self: own)
   int tk_chunks = 0;
   int* d_tokens = nullptr;     // [ctx] tokens of a device-fed greedy run
   int kernels = 0;             // kernel launches counted during a capture
@@ -841,6 +849,13 @@ struct l3g_workspace {
 static void ws_release(l3g_workspace* ws) {
   for (auto& g : ws->graphs) cudaGraphExecDestroy(g.exec);
   ws->graphs.clear();
+  for (int r = 0; r < MAX_WORLD; ++r) {
+    if (ws->tp_peer_recv[r] && ws->tp_peer_recv[r] != ws->tp_recv) cudaIpcCloseMemHandle(ws->tp_peer_recv[r]);
+    ws->tp_peer_recv[r] = nullptr;
+  }
+  void* tp_ptrs[] = {ws->d_step, ws->d_sync, ws->tp_recv};
+  for (void* p : tp_ptrs)
+    if (p) cudaFree(p);
   void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
                    ws->attn, ws->act, ws->attn_d, ws->attn_q, ws->act_d, ws->act_q, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
                    ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
@@ -869,6 +884,94 @@ extern "C" void l3g_workspace_free(l3g_workspace* ws) {
   cudaSetDevice(ws->device);
   ws_release(ws);
   delete ws;
+}
+
+// Tensor-parallel exchange buffer: a receive buffer [2][world][n_emb] of
+// {value, epoch} words per rank (zero: no epoch yet), mapped into every other
+// rank's address space with CUDA IPC; the handles travel over the model's
+// NCCL communicator.  All ranks agree (an NCCL min) on whether every mapping
+// succeeded; otherwise the step uses NCCL allreduces instead.  L3G_TP_NCCL=1
+// forces the NCCL path.  Collective: every rank creates its workspaces in
+// the same order.
+static int tp_setup(l3g_workspace* ws) {
+  l3g_model* m = ws->m;
+  const int W = m->world, R = m->rank, ne = m->hp.n_emb;
+  const NcclApi* api = nccl();
+  if (!api->ok) return l3g_fail(L3G_E_NCCL, "NCCL unavailable");
+  const size_t bytes = (size_t)2 * W * ne * 8;
+  int ok = W <= MAX_WORLD && !getenv("L3G_TP_NCCL");
+  if (ok && (cudaMalloc(&ws->tp_recv, bytes) != cudaSuccess ||
+             cudaMemset(ws->tp_recv, 0, bytes) != cudaSuccess))
+    ok = 0;
+  constexpr int HB = (int)sizeof(cudaIpcMemHandle_t);
+  std::vector<uint8_t> h((size_t)W * HB, 0);
+  if (ok) {
+    cudaIpcMemHandle_t a;
+    if (cudaIpcGetMemHandle(&a, ws->tp_recv) != cudaSuccess)
+      ok = 0;
+    else
+      memcpy(&h[(size_t)R * HB], &a, HB);
+  }
+  cudaGetLastError();
+  // exchange the handles and agree on `ok`, then on the mappings
+  auto agree = [&](int* v) -> int {
+    int* d_v = nullptr;
+    CUDA_TRY(cudaMalloc(&d_v, 4));
+    cudaError_t e = cudaMemcpy(d_v, v, 4, cudaMemcpyHostToDevice);
+    ncclResult_t r = ncclSuccess;
+    if (e == cudaSuccess) {
+      r = api->AllReduce(d_v, d_v, 1, ncclInt32, ncclMin, m->comm, ws->stream);
+      e = cudaStreamSynchronize(ws->stream);
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(v, d_v, 4, cudaMemcpyDeviceToHost);
+    cudaFree(d_v);
+    if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "tp exchange: %s", cudaGetErrorString(e));
+    if (r != ncclSuccess) return l3g_fail(L3G_E_NCCL, "tp exchange: %s", api->GetErrorString(r));
+    return L3G_OK;
+  };
+  {
+    uint8_t* d = nullptr;
+    CUDA_TRY(cudaMalloc(&d, h.size()));
+    cudaError_t e = cudaMemcpy(d, h.data(), h.size(), cudaMemcpyHostToDevice);
+    ncclResult_t r = ncclSuccess;
+    if (e == cudaSuccess) {
+      r = api->AllGather(d + (size_t)R * HB, d, HB, ncclUint8, m->comm, ws->stream);
+      e = cudaStreamSynchronize(ws->stream);
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), d, h.size(), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "tp exchange: %s", cudaGetErrorString(e));
+    if (r != ncclSuccess) return l3g_fail(L3G_E_NCCL, "tp exchange: %s", api->GetErrorString(r));
+  }
+  if (int rc = agree(&ok)) return rc;
+  int mapped = ok;
+  for (int r = 0; r < W && mapped; ++r) {
+    if (r == R) {
+      ws->tp_peer_recv[r] = ws->tp_recv;
+      continue;
+    }
+    cudaIpcMemHandle_t a;
+    memcpy(&a, &h[(size_t)r * HB], HB);
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, a, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      mapped = 0;
+      break;
+    }
+    ws->tp_peer_recv[r] = static_cast<unsigned long long*>(p);
+  }
+  cudaGetLastError();
+  if (ok)
+    if (int rc = agree(&mapped)) return rc;
+  ws->tp_p2p = ok && mapped;
+  if (!ws->tp_p2p) {  // the NCCL path: drop whatever was set up
+    for (int r = 0; r < MAX_WORLD; ++r) {
+      if (ws->tp_peer_recv[r] && ws->tp_peer_recv[r] != ws->tp_recv) cudaIpcCloseMemHandle(ws->tp_peer_recv[r]);
+      ws->tp_peer_recv[r] = nullptr;
+    }
+    if (ws->tp_recv) cudaFree(ws->tp_recv);
+    ws->tp_recv = nullptr;
+  }
+  return L3G_OK;
 }
 
 // Cluster merge of the attention splits: 16 splits per kv head as one
@@ -989,6 +1092,10 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   DM(ws->tk_part, (size_t)ws->tk_chunks * MAX_TOPK * 8);
   DM(ws->d_tokens, (size_t)ctx * 4);
   DM(ws->d_trace, kTraceBytes);
+  DM(ws->d_step, 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->d_step, 0, 4);
+  DM(ws->d_sync, 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->d_sync, 0, 4);
   DM(ws->d_tk_ids, MAX_TOPK * 4);
   DM(ws->d_tk_logits, MAX_TOPK * 4);
   HM(ws->h_tk_ids, MAX_TOPK * 4);
@@ -1013,6 +1120,14 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
     return l3g_fail(L3G_E_CUDA, "workspace allocation: %s", cudaGetErrorString(e));
   }
   ws->device = m->device;
+  if (m->world > 1) {
+    const int rc = tp_setup(ws);
+    if (rc) {
+      ws_release(ws);
+      delete ws;
+      return rc;
+    }
+  }
   {
     std::lock_guard<std::mutex> lk(m->ws_mu);
     m->workspaces.push_back(ws);
@@ -1025,6 +1140,7 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
 static MatvecArgs mv_args(const DevMat& w) {
   MatvecArgs a{};
   a.w = w.t;
+  a.wait_ns = WAIT_TIMEOUT_NS;
   a.nstages = w.nstages;
   a.row_lo = 0;
   a.row_hi = w.t.rows;
@@ -1153,6 +1269,22 @@ __global__ void k_merge_argmax(const Result* g, int world, Result* out) {
 }
 
 // Enqueues one decode step on ws->stream (captured into a graph).
+// Exchange descriptor of reduction phase `phase` (2 * layer + 0 after Wo,
+// + 1 after down) for this rank.
+static TpExchange tp_exchange(const l3g_workspace* ws, int phase) {
+  const l3g_model* m = ws->m;
+  TpExchange t{};
+  t.world = m->world;
+  t.rank = m->rank;
+  t.n = m->hp.n_emb;
+  t.nphase = 2 * m->hp.n_layers;
+  t.phase = phase;
+  t.step = ws->d_step;
+  for (int r = 0; r < m->world && r < MAX_WORLD; ++r) t.recv[r] = ws->tp_peer_recv[r];
+  t.my_recv = ws->tp_recv;
+  return t;
+}
+
 static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int k) {
   const bool traced = variant == V_TRACE;
   if (traced) variant = V_GREEDY_DEV;
@@ -1163,6 +1295,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
   cudaStream_t st = ws->stream;
   const int ne = hp.n_emb, hd = m->hd;
   const size_t es = m->kv_f16 ? 2 : 4;
+  const unsigned long long wait_ns = m->world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS;
   ws->kernels = 0;
 #define KL(kind, expr)                                 \
   do {                                                 \
@@ -1180,12 +1313,13 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
   if (variant != V_GREEDY_DEV)
     CUDA_TRY(cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, st));
   KL(L3G_K_EMBED, launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
-                  hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res));
+                  hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res, ws->d_step));
   for (int l = 0; l < hp.n_layers; ++l) {
     const LayerW& L = m->layers[l];
     uint8_t* kv = static_cast<uint8_t*>(s->kv) + (size_t)l * s->layer_elems * es;
     {  // RMSNorm -> act-quant -> QKV -> RoPE -> KV append, infer.go:67-127
       MatvecArgs a = mv_args(L.qkv);
+      a.wait_ns = wait_ns;
       a.x_in = ws->x[0];
       a.y_in = l ? ws->y : nullptr;
       a.norm_w = L.attn_norm;
@@ -1209,6 +1343,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     }
     {  // attention, infer.go:130-175
       AttnArgs a{};
+      a.wait_ns = wait_ns;
       a.q = ws->q;
       a.kv = kv;
       a.ctx = s->ctx;
@@ -1234,18 +1369,28 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     {  // Wo on the attention output the merge quantized, infer.go:178-187
        // (residual add fused downstream)
       MatvecArgs a = mv_args(L.wo);
+      a.wait_ns = wait_ns;
       a.xd_in = ws->attn_d;
       a.xqs_in = ws->attn_q;
       a.out = ws->y;
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_STORE>(L.wo, a, m->nsm, st)));
+      if (ws->tp_p2p) {  // partial rows pushed to every rank (phase 2l)
+        a.tp_out = tp_exchange(ws, 2 * l);
+        KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_PUSH>(L.wo, a, m->nsm, st)));
+      } else {
+        KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_STORE>(L.wo, a, m->nsm, st)));
+      }
     }
-    if (m->world > 1)
+    if (ws->tp_p2p)
+      KL(L3G_K_OTHER, launch(k_tp_reduce, dim3((ne / 4 + 255) / 256), dim3(256), 0, st,
+                             tp_exchange(ws, 2 * l), ws->y, ws->d_res, wait_ns));
+    else if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));
     {  // residual -> RMSNorm -> act-quant -> up/gate -> SwiGLU, infer.go:189-230
       MatvecArgs a = mv_args(L.upgate);
+      a.wait_ns = wait_ns;
       a.x_in = ws->x[1];
       a.y_in = ws->y;
       a.norm_w = L.ffn_norm;
@@ -1264,20 +1409,30 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     }
     {  // down, infer.go:235-242
       MatvecArgs a = mv_args(L.down);
+      a.wait_ns = wait_ns;
       a.xd_in = ws->act_d;
       a.xqs_in = ws->act_q;
       a.out = ws->y;
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_STORE>(L.down, a, m->nsm, st)));
+      if (ws->tp_p2p) {  // phase 2l + 1
+        a.tp_out = tp_exchange(ws, 2 * l + 1);
+        KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_PUSH>(L.down, a, m->nsm, st)));
+      } else {
+        KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_STORE>(L.down, a, m->nsm, st)));
+      }
     }
-    if (m->world > 1)
+    if (ws->tp_p2p)
+      KL(L3G_K_OTHER, launch(k_tp_reduce, dim3((ne / 4 + 255) / 256), dim3(256), 0, st,
+                             tp_exchange(ws, 2 * l + 1), ws->y, ws->d_res, wait_ns));
+    else if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->y, ws->y, ne, ncclFloat, ncclSum, m->comm, st));
   }
   if (variant != V_PREFILL) {
     // residual -> final RMSNorm -> act-quant -> logits + argmax, infer.go:250-262
     MatvecArgs a = mv_args(m->logits);
+      a.wait_ns = wait_ns;
     a.x_in = ws->x[0];
     a.y_in = ws->y;
     a.norm_w = m->out_norm;
@@ -1357,6 +1512,13 @@ static int get_graph(l3g_workspace* ws, const l3g_state* s, int variant, int k,
   cudaGraphDestroy(g);
   if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
   ws->graphs.push_back({variant, k, s->serial, exec});
+  if (ws->m->world > 1) {
+    // ranks capture at their own pace; line them up before the first launch
+    // so that none waits on a peer that is still capturing
+    NCCL_TRY(nccl()->AllReduce(ws->d_sync, ws->d_sync, 1, ncclInt32, ncclMax, ws->m->comm,
+                               ws->stream));
+    CUDA_TRY(cudaStreamSynchronize(ws->stream));
+  }
   if (variant == V_GREEDY_DEV) ws->kernels_greedy = ws->kernels;
   if (variant == V_TRACE) ws->trace_kinds_graph = ws->trace_kinds;
   *out = exec;
@@ -1590,6 +1752,12 @@ extern "C" int l3g_workspace_attention_layout(const l3g_workspace* ws, int32_t* 
   if (!ws || !splits || !cluster) return l3g_fail(L3G_E_INVALID, "null argument");
   *splits = ws->n_splits;
   *cluster = ws->att_cluster;
+  return L3G_OK;
+}
+
+extern "C" int l3g_workspace_tp_p2p(const l3g_workspace* ws, int32_t* p2p) {
+  if (!ws || !p2p) return l3g_fail(L3G_E_INVALID, "null argument");
+  *p2p = ws->tp_p2p ? 1 : 0;
   return L3G_OK;
 }
 

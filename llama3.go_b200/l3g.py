@@ -111,6 +111,7 @@ def lib():
                                         C.POINTER(C.c_float)]),
         "l3g_workspace_kernels_per_step": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_workspace_attention_layout": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+        "l3g_workspace_tp_p2p": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_profile_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_float),
                                        C.POINTER(C.c_int32)]),
         "l3g_trace_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_uint64), C.POINTER(C.c_int32),
@@ -365,6 +366,12 @@ class Workspace:
         v = C.c_int32()
         _check(lib().l3g_workspace_kernels_per_step(self._h, C.byref(v)))
         return v.value
+
+    def tp_p2p(self) -> bool:
+        """True when the tensor-parallel reductions go over peer memory."""
+        v = C.c_int32()
+        _check(lib().l3g_workspace_tp_p2p(self._h, C.byref(v)))
+        return bool(v.value)
 
     def attention_layout(self) -> tuple[int, int]:
         """(splits per kv head, cluster size or 0)."""

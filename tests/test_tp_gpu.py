@@ -18,12 +18,14 @@ pytestmark = pytest.mark.gpu
 CONFIG, N_TOK, CTX = "mid", 12, 64
 
 
-def _rank_main(rank, world, id_path, out_dir):
+def _rank_main(rank, world, id_path, out_dir, path):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     for sub in ("llama3.go_b200", "oracle", "tests"):
         sys.path.insert(0, os.path.join(root, sub))
+    if path == "nccl":
+        os.environ["L3G_TP_NCCL"] = "1"
     import l3g
     import synthetic
     from conftest import synthetic_model as sm
@@ -44,6 +46,8 @@ def _rank_main(rank, world, id_path, out_dir):
     m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, opts)
     s = m.NewState(CTX)
     ws = m.NewWorkspace(CTX, 40)
+    if ws.tp_p2p() != (path == "p2p"):
+        raise RuntimeError(f"workspace reduction path is not {path}")
     ids = synthetic.prompt_ids(cfg, N_TOK, seed=17)
     logits = np.empty(cfg.vocab, np.float32)
     out = []
@@ -62,7 +66,10 @@ def _rank_main(rank, world, id_path, out_dir):
     m.Close()
 
 
-def test_tp2_matches_reference_and_single_gpu(gpu_lib, oracle_mod, tmp_path):
+@pytest.mark.parametrize("path", ["p2p", "nccl"])
+def test_tp2_matches_reference_and_single_gpu(gpu_lib, oracle_mod, tmp_path, path):
+    """Both reductions: partial sums pushed over peer memory by the Wo / down
+    matvecs and summed by the next kernel (p2p), and NCCL allreduces."""
     import torch
     import torch.multiprocessing as mp
     import synthetic
@@ -70,7 +77,7 @@ def test_tp2_matches_reference_and_single_gpu(gpu_lib, oracle_mod, tmp_path):
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     id_path = str(tmp_path / "nccl_id")
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, id_path, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, id_path, str(tmp_path), path)) for r in range(2)]
     for p in procs:
         p.start()
     deadline = time.time() + 600
