@@ -976,10 +976,12 @@ static int tp_setup(l3g_workspace* ws) {
 
 // Cluster merge of the attention splits: 16 splits per kv head as one
 // (non-portable) cluster, used when clusters for every local kv head can be
-// resident at once and they give at least half the SMs a CTA.
-// L3G_ATT_CLUSTER=0 forces the global-memory merge, =1 the 16-CTA cluster
-// merge whenever the clusters fit, =N (2..16) clusters of N CTAs (N splits)
-// whenever they fit (knobs for tests and experiments).
+// resident at once (on a 148-SM B200 at most 7 such clusters fit, so a
+// single-GPU 8-kv-head model keeps the global merge; tensor-parallel ranks
+// with 4 or fewer kv heads use the cluster merge, whose tail is a fraction of
+// the global one).
+// L3G_ATT_CLUSTER=0 forces the global-memory merge, =N (2..16) clusters of N
+// CTAs (N splits) whenever they fit (knobs for tests and experiments).
 template <int DPL, typename KT>
 static void max_attention_clusters(const l3g_workspace* ws, int cs, int* n) {
   cudaLaunchConfig_t cfg = {};
@@ -1013,9 +1015,7 @@ static void choose_attention_cluster(l3g_workspace* ws) {
   const char* env = getenv("L3G_ATT_CLUSTER");
   if (env && atoi(env) == 0) return;
   const int knob = env ? atoi(env) : -1;
-  const bool force = knob >= 1;
   const int cs = knob >= 2 && knob <= 16 ? knob : 16;
-  if (!force && m->hkv_l * cs * 2 < m->nsm) return;  // too few CTAs: keep the splits
   int n = 0;
   const int dpl = m->hd / 32;
   if (m->kv_f16) {
