@@ -20,7 +20,9 @@
 //     (one or more Q8_0 blocks) reading the others' partials over
 //     distributed shared memory, then a second barrier keeps every CTA's
 //     shared memory alive until all reads are done;
-//   - otherwise through global partials, in whichever CTA finishes last.
+//   - otherwise through global partials: every CTA publishes its own, waits
+//     until all splits of its kv head have (they are all resident), and
+//     merges one slice of the outputs.
 #pragma once
 
 struct AttnArgs {
@@ -31,7 +33,7 @@ struct AttnArgs {
   const int* io;      // io[1] = position of this token
   float* part_o;      // [kv heads][splits][group][hd]
   float* part_ml;     // [kv heads][splits][group][2]
-  unsigned* counters; // [kv heads], zero between launches
+  unsigned* counters; // [2][kv heads]: arrivals, departures; zero between launches
   float* out;         // [local q heads][hd]
   float* out_d;       // out quantized (QuantizeQ8_0Into) for the Wo matvec:
   int8_t* out_q;      //   [local q heads * hd / 32] scales, int8 values
@@ -416,117 +418,74 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     trace_mark(a.trace, a.trace_seq, TR_EXIT);
     return;
   }
-  // publish: the CTA barrier orders every thread's partial stores before
-  // thread 0's acquire-release count at device scope; in the CTA that brings
-  // the count to S the same operation acquires the other CTAs' partials, and
-  // the CTA barrier after it extends that to every thread's reads.
+  // Publish this split's partial, then wait (bounded) until every split of
+  // this kv head has published: the grid has at most one CTA per SM, so all
+  // of them are resident.  Then each CTA merges its own slice of the G*hd
+  // outputs (whole Q8_0 blocks), reading every split's (m, l) and that
+  // slice of their partial outputs: one small gather per CTA instead of one
+  // CTA gathering everything.  counters[kvh] counts arrivals,
+  // counters[gridDim.x + kvh] departures; the last to depart resets both.
   consumer_sync();
-  if (threadIdx.x == 0) sh->last = atom_add_acq_rel_gpu(a.counters + kvh, 1u) == (unsigned)S - 1;
-  consumer_sync();
-  trace_mark(a.trace, a.trace_seq, 5);  // partial published
-  if (!*(volatile int*)&sh->last) {
-    trace_mark(a.trace, a.trace_seq, TR_EXIT);
-    return;
+  unsigned* arrived = a.counters + kvh;
+  unsigned* departed = a.counters + gridDim.x + kvh;
+  if (threadIdx.x == 0) {
+    atom_add_acq_rel_gpu(arrived, 1u);
+    const uint64_t t0 = gtime();
+    while (ld_acquire_gpu_u32(arrived) < (unsigned)S) {
+      if (gtime() - t0 > a.wait_ns) {
+        report(a.res, ERR_TIMEOUT, 9);
+        break;
+      }
+    }
   }
-  // Merge the splits of this kv head in split order.  One round trip stages
-  // every split's (m, l) and the first chunk of partial outputs (all loads of
-  // a thread in flight at once); then the split weights e_s = exp(m_s - M)
-  // per head and their sums, then the weighted partial outputs.
-  const int gh = G * hd;
-  const int nml = S * G * 2;                              // <= 12 * 256
-  float* sm_split = reinterpret_cast<float*>(ring);       // [S][G][2]
-  float* sm_w = sm_split + align_up(nml, 4);              // [S][G] weights
-  float* sm_tot = sm_w + align_up(S * G, 4);              // [G] sum of l_s e_s
-  float* sm_part = sm_tot + align_up(MAXG, 4);            // [chunk][G][hd]
-  const int used = (int)(reinterpret_cast<uint8_t*>(sm_part) - ring);
-  const int chunk_s = max(1, (a.nstages * a.stage_bytes - used) / (gh * 4));
-  const float* ml_src = a.part_ml + (size_t)kvh * nml;
-  auto stage_chunk = [&](int c0, bool with_ml) {
-    constexpr int R = 12;
-    const int cs = min(chunk_s, S - c0);
-    const float4* src = reinterpret_cast<const float4*>(a.part_o + ((size_t)kvh * S + c0) * gh);
-    float4* dst = reinterpret_cast<float4*>(sm_part);
-    const int n4 = cs * gh / 4;
-    for (int base = 0; base < n4 || (with_ml && base == 0); base += R * NW * 32) {
-      float mr[R];
-      float4 r[R];
-#pragma unroll
-      for (int k = 0; k < R; ++k) {
-        const int i = threadIdx.x + k * NW * 32;
-        mr[k] = (with_ml && base == 0 && i < nml) ? __ldcg(ml_src + i) : 0.0f;
-        r[k] = base + i < n4 ? __ldcg(src + base + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int k = 0; k < R; ++k) {
-        const int i = threadIdx.x + k * NW * 32;
-        if (with_ml && base == 0 && i < nml) sm_split[i] = mr[k];
-        if (base + i < n4) dst[base + i] = r[k];
-      }
-    }
-  };
-  stage_chunk(0, true);
   consumer_sync();
-  trace_mark(a.trace, a.trace_seq, 6);  // split partials staged
-  // warp h: the maximum M_h of the splits' m, their weights and
-  // L_h = sum l_s e_s (butterfly reductions: a fixed order)
-  for (int h = warp; h < G; h += NW) {
+  trace_mark(a.trace, a.trace_seq, 5);  // every split published
+  const int gh = G * hd;
+  const int slice = align_up((gh + S - 1) / S, 32);  // outputs merged per CTA
+  const int b0 = min(gh, split * slice) / 32, b1 = min(gh, (split + 1) * slice) / 32;
+  float* wbuf = reinterpret_cast<float*>(ring) + warp * align_up(S, 32);  // e_s per warp
+  const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
+  const float* po = a.part_o + (size_t)kvh * S * gh;
+  for (int blk = b0 + warp; blk < b1; blk += NW) {  // one warp per block of 32 outputs
+    const int h = blk * 32 / hd;
     float M = -INFINITY;
-    for (int s0 = 0; s0 < S; s0 += 32) {
-      const int s2 = s0 + lane;
-      M = fmaxf(M, warp_max(s2 < S ? sm_split[(s2 * G + h) * 2] : -INFINITY));
-    }
+    for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
+    M = warp_max(M);
     float L = 0.0f;
     for (int s0 = 0; s0 < S; s0 += 32) {
       const int s2 = s0 + lane;
       float le = 0.0f;
       if (s2 < S) {
-        const float ms = sm_split[(s2 * G + h) * 2];
+        const float ms = __ldcg(ml + ((size_t)s2 * G + h) * 2);
         const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
-        sm_w[s2 * G + h] = e;
-        le = sm_split[(s2 * G + h) * 2 + 1] * e;
+        wbuf[s2] = e;
+        le = __ldcg(ml + ((size_t)s2 * G + h) * 2 + 1) * e;
       }
       L += warp_sum(le);
     }
-    if (lane == 0) sm_tot[h] = L;
+    __syncwarp();
+    // O = sum over splits in split order of o_s * e_s, loads batched by 8
+    const float* col = po + (size_t)blk * 32 + lane;
+    float O = 0.0f;
+    int s2 = 0;
+    for (; s2 + 8 <= S; s2 += 8) {
+      float ov[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ov[u] = __ldcg(col + (size_t)(s2 + u) * gh);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) O = fmaf(ov[u], wbuf[s2 + u], O);
+    }
+    for (; s2 < S; ++s2) O = fmaf(__ldcg(col + (size_t)s2 * gh), wbuf[s2], O);
+    __syncwarp();
+    const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
+    a.out[(size_t)kvh * gh + blk * 32 + lane] = v;
+    quant_block(v, kvh * gh / 32 + blk, lane, a.out_d, a.out_q);
   }
+  trace_mark(a.trace, a.trace_seq, 7);  // slice merged
   consumer_sync();
-  float acc2[4] = {0.f, 0.f, 0.f, 0.f};  // outputs idx = threadIdx.x + k * 256
-  for (int c0 = 0; c0 < S; c0 += chunk_s) {
-    if (c0) {
-      consumer_sync();  // previous chunk consumed
-      stage_chunk(c0, false);
-      consumer_sync();
-    }
-    const int cs = min(chunk_s, S - c0);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int idx = threadIdx.x + k * NW * 32;
-      if (idx < gh) {
-        const int h = idx / hd;
-        // four independent partial sums, combined in a fixed order
-        float o4[4] = {0.f, 0.f, 0.f, 0.f};
-        int s2 = 0;
-        for (; s2 + 4 <= cs; s2 += 4) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            o4[u] = fmaf(sm_part[(s2 + u) * gh + idx], sm_w[(c0 + s2 + u) * G + h], o4[u]);
-        }
-        for (; s2 < cs; ++s2) o4[0] = fmaf(sm_part[s2 * gh + idx], sm_w[(c0 + s2) * G + h], o4[0]);
-        acc2[k] += (o4[0] + o4[1]) + (o4[2] + o4[3]);
-      }
-    }
+  if (threadIdx.x == 0 && atom_add_acq_rel_gpu(departed, 1u) == (unsigned)S - 1) {
+    *arrived = 0u;
+    *departed = 0u;
   }
-  trace_mark(a.trace, a.trace_seq, 7);  // merged
-  // normalize, store, and quantize: a warp holds 32 consecutive outputs,
-  // one Q8_0 block (hd is a multiple of 32, so no block spans two kv heads)
-  for (int k = 0; k < 4; ++k) {
-    const int idx = threadIdx.x + k * NW * 32;
-    if (idx >= gh) break;  // uniform per warp: gh is a multiple of 32
-    const int h = idx / hd;
-    const float v = __fmul_rn(acc2[k], __fdiv_rn(1.0f, sm_tot[h]));
-    a.out[(size_t)kvh * gh + idx] = v;
-    quant_block(v, (kvh * gh + idx) >> 5, lane, a.out_d, a.out_q);
-  }
-  if (threadIdx.x == 0) a.counters[kvh] = 0u;
   trace_mark(a.trace, a.trace_seq, TR_EXIT);
 }

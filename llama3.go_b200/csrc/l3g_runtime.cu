@@ -1055,7 +1055,7 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   ws->att_gp = 1;
   while (ws->att_gp < G) ws->att_gp <<= 1;
   ws->n_splits = std::max(1, std::min(m->nsm / m->hkv_l, (ctx + ws->att_P - 1) / ws->att_P));
-  const int scratch = std::max(at_scratch_floats(G, hd) * 4, ws->n_splits * G * 2 * 4);
+  const int scratch = std::max(at_scratch_floats(G, hd) * 4, NW * align_up(ws->n_splits, 32) * 4);
   ws->att_smem = at_ring_offset() + std::max(ws->att_ns * ws->att_stage, scratch);
   choose_attention_cluster(ws);
   const int vloc = m->v_l;
@@ -1085,7 +1085,7 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   HM(ws->h_logits, (size_t)vloc * m->world * 4);
   DM(ws->part_o, (size_t)m->hkv_l * ws->n_splits * G * hd * 4);
   DM(ws->part_ml, (size_t)m->hkv_l * ws->n_splits * G * 2 * 4);
-  DM(ws->att_cnt, (size_t)m->hkv_l * 4);
+  DM(ws->att_cnt, (size_t)m->hkv_l * 2 * 4);  // arrivals, departures
   DM(ws->am_val, (size_t)m->nsm * 4);
   DM(ws->am_idx, (size_t)m->nsm * 4);
   DM(ws->am_cnt, 4);
@@ -1103,7 +1103,7 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
 #undef DM
 #undef HM
   if (e == cudaSuccess) e = cudaMemset(ws->d_res, 0, sizeof(Result));
-  if (e == cudaSuccess) e = cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 2 * 4);
   if (e == cudaSuccess) e = cudaMemset(ws->am_cnt, 0, 4);
   if (e == cudaSuccess) e = cudaMemset(ws->x[0], 0, ne * 4);
   if (e == cudaSuccess) e = cudaMemset(ws->x[1], 0, ne * 4);
@@ -1550,7 +1550,7 @@ static int run_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token
     const int code = ws->h_res->err, where = ws->h_res->where;
     cudaMemset(ws->d_res, 0, sizeof(Result));
     // an aborted kernel may have left its last-CTA counters mid-count
-    cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 4);
+    cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 2 * 4);
     cudaMemset(ws->am_cnt, 0, 4);
     ws->logits_valid = false;
     return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d (%s)", code, where,

@@ -5,7 +5,6 @@ columns for Wo / down, vocab rows for the logits), and exchange partial sums
 with all_reduce / all_gather exactly where the GPU path calls NCCL.  The
 result must equal the unsharded forward."""
 import os
-import socket
 
 import numpy as np
 import pytest
@@ -13,13 +12,7 @@ import pytest
 from conftest import ROOT, synthetic_model
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _tp_worker(rank, world, port, name, ntok, out_dir):
+def _tp_worker(rank, world, store_path, name, ntok, out_dir):
     import sys
     for sub in ("llama3.go_b200", "oracle", "tests"):
         sys.path.insert(0, os.path.join(ROOT, sub))
@@ -31,9 +24,8 @@ def _tp_worker(rank, world, port, name, ntok, out_dir):
     import l3g
     import npref
     import synthetic
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # file rendezvous: no TCP port to race for
+    dist.init_process_group("gloo", init_method=f"file://{store_path}", rank=rank, world_size=world)
     cfg = synthetic.CONFIGS[name]
     T = synthetic.make_model(cfg, seed=0)
     sh = l3g.shard_plan(l3g.hparams_for(cfg), world, rank)
@@ -102,7 +94,7 @@ def test_tp2_decomposition_matches_single_rank(tmp_path, name):
     import synthetic
     cfg, T = synthetic_model(name)
     ntok = 4
-    mp.start_processes(_tp_worker, args=(2, _free_port(), name, ntok, str(tmp_path)), nprocs=2,
+    mp.start_processes(_tp_worker, args=(2, str(tmp_path / "store"), name, ntok, str(tmp_path)), nprocs=2,
                        join=True, start_method="spawn")
     ref_model = npref.NpModel(cfg, T, 16)
     ref = np.stack([ref_model.forward(int(t)) for t in synthetic.prompt_ids(cfg, ntok, seed=3)])
