@@ -9,6 +9,7 @@
 // programmatic stream serialization so each one's weight prefetch overlaps
 // the tail of its predecessor.
 #include <dlfcn.h>
+#include <unistd.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -144,10 +145,16 @@ static cudaError_t set_max_shared(K k, int limit) {
   return e;
 }
 
+// Kernel attributes belong to the device (context) they were set on: once
+// per device, with that device current.
 static int setup_kernels() {
-  static int rc = -100;
-  static std::once_flag once;
-  std::call_once(once, [] {
+  static int rcs[64];
+  static std::once_flag onces[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return l3g_fail(L3G_E_CUDA, "kernel attribute set-up: no current device");
+  int& rc = rcs[dev];
+  std::call_once(onces[dev], [&rc] {
     const int big = 227 * 1024;
     cudaError_t e = cudaSuccess;
     // Every kernel asks for the largest shared-memory carveout: the SM's
@@ -832,6 +839,7 @@ struct l3g_workspace {
   bool tp_p2p = false;
   unsigned long long* tp_recv = nullptr;               // [2][world][n_emb] {value, epoch}
   unsigned long long* tp_peer_recv[MAX_WORLD] = {};    // every rank's (self: own)
+  bool tp_peer_same_process[MAX_WORLD] = {};            // mapped without IPC
   int tk_chunks = 0;
   int* d_tokens = nullptr;     // [ctx] tokens of a device-fed greedy run
   int kernels = 0;             // kernel launches counted during a capture
@@ -850,7 +858,8 @@ static void ws_release(l3g_workspace* ws) {
   for (auto& g : ws->graphs) cudaGraphExecDestroy(g.exec);
   ws->graphs.clear();
   for (int r = 0; r < MAX_WORLD; ++r) {
-    if (ws->tp_peer_recv[r] && ws->tp_peer_recv[r] != ws->tp_recv) cudaIpcCloseMemHandle(ws->tp_peer_recv[r]);
+    if (ws->tp_peer_recv[r] && ws->tp_peer_recv[r] != ws->tp_recv && !ws->tp_peer_same_process[r])
+      cudaIpcCloseMemHandle(ws->tp_peer_recv[r]);
     ws->tp_peer_recv[r] = nullptr;
   }
   void* tp_ptrs[] = {ws->d_step, ws->d_sync, ws->tp_recv};
@@ -888,8 +897,10 @@ extern "C" void l3g_workspace_free(l3g_workspace* ws) {
 
 // Tensor-parallel exchange buffer: a receive buffer [2][world][n_emb] of
 // {value, epoch} words per rank (zero: no epoch yet), mapped into every other
-// rank's address space with CUDA IPC; the handles travel over the model's
-// NCCL communicator.  All ranks agree (an NCCL min) on whether every mapping
+// rank's address space with CUDA IPC (ranks in other processes) or reached
+// through unified addressing with peer access (ranks that are threads of the
+// same process); the handles and pointers travel over the model's NCCL
+// communicator.  All ranks agree (an NCCL min) on whether every mapping
 // succeeded; otherwise the step uses NCCL allreduces instead.  L3G_TP_NCCL=1
 // forces the NCCL path.  Collective: every rank creates its workspaces in
 // the same order.
@@ -903,14 +914,23 @@ static int tp_setup(l3g_workspace* ws) {
   if (ok && (cudaMalloc(&ws->tp_recv, bytes) != cudaSuccess ||
              cudaMemset(ws->tp_recv, 0, bytes) != cudaSuccess))
     ok = 0;
-  constexpr int HB = (int)sizeof(cudaIpcMemHandle_t);
+  // per rank: the IPC handle, then its process id and raw device pointer
+  // (ranks that are threads of one process use the pointer directly: an
+  // IPC handle cannot be opened in the process that exported it)
+  constexpr int HI = (int)sizeof(cudaIpcMemHandle_t);
+  constexpr int HB = HI + 16;
   std::vector<uint8_t> h((size_t)W * HB, 0);
   if (ok) {
     cudaIpcMemHandle_t a;
-    if (cudaIpcGetMemHandle(&a, ws->tp_recv) != cudaSuccess)
+    if (cudaIpcGetMemHandle(&a, ws->tp_recv) != cudaSuccess) {
       ok = 0;
-    else
-      memcpy(&h[(size_t)R * HB], &a, HB);
+    } else {
+      const int64_t pid = (int64_t)getpid();
+      const uint64_t ptr = (uint64_t)(uintptr_t)ws->tp_recv;
+      memcpy(&h[(size_t)R * HB], &a, HI);
+      memcpy(&h[(size_t)R * HB + HI], &pid, 8);
+      memcpy(&h[(size_t)R * HB + HI + 8], &ptr, 8);
+    }
   }
   cudaGetLastError();
   // exchange the handles and agree on `ok`, then on the mappings
@@ -950,8 +970,32 @@ static int tp_setup(l3g_workspace* ws) {
       ws->tp_peer_recv[r] = ws->tp_recv;
       continue;
     }
+    int64_t pid = 0;
+    uint64_t ptr = 0;
+    memcpy(&pid, &h[(size_t)r * HB + HI], 8);
+    memcpy(&ptr, &h[(size_t)r * HB + HI + 8], 8);
+    if (pid == (int64_t)getpid()) {  // same process: unified addressing
+      int peer_dev = -1;
+      cudaPointerAttributes pa{};
+      if (cudaPointerGetAttributes(&pa, (void*)(uintptr_t)ptr) == cudaSuccess) peer_dev = pa.device;
+      int can = 0;
+      if (peer_dev >= 0 && peer_dev != m->device)
+        cudaDeviceCanAccessPeer(&can, m->device, peer_dev);
+      if (!can) {
+        mapped = 0;
+        break;
+      }
+      const cudaError_t pe = cudaDeviceEnablePeerAccess(peer_dev, 0);
+      if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled) {
+        mapped = 0;
+        break;
+      }
+      ws->tp_peer_same_process[r] = true;
+      ws->tp_peer_recv[r] = reinterpret_cast<unsigned long long*>((uintptr_t)ptr);
+      continue;
+    }
     cudaIpcMemHandle_t a;
-    memcpy(&a, &h[(size_t)r * HB], HB);
+    memcpy(&a, &h[(size_t)r * HB], HI);
     void* p = nullptr;
     if (cudaIpcOpenMemHandle(&p, a, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
       mapped = 0;
@@ -965,8 +1009,10 @@ static int tp_setup(l3g_workspace* ws) {
   ws->tp_p2p = ok && mapped;
   if (!ws->tp_p2p) {  // the NCCL path: drop whatever was set up
     for (int r = 0; r < MAX_WORLD; ++r) {
-      if (ws->tp_peer_recv[r] && ws->tp_peer_recv[r] != ws->tp_recv) cudaIpcCloseMemHandle(ws->tp_peer_recv[r]);
+      if (ws->tp_peer_recv[r] && ws->tp_peer_recv[r] != ws->tp_recv && !ws->tp_peer_same_process[r])
+        cudaIpcCloseMemHandle(ws->tp_peer_recv[r]);
       ws->tp_peer_recv[r] = nullptr;
+      ws->tp_peer_same_process[r] = false;
     }
     if (ws->tp_recv) cudaFree(ws->tp_recv);
     ws->tp_recv = nullptr;

@@ -66,6 +66,81 @@ def _rank_main(rank, world, id_path, out_dir, path):
     m.Close()
 
 
+def _threads_main(out_dir):
+    """Both ranks as threads of this (spawned) process."""
+    import sys
+    import threading
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for sub in ("llama3.go_b200", "oracle", "tests"):
+        sys.path.insert(0, os.path.join(root, sub))
+    import l3g
+    import synthetic
+    from conftest import synthetic_model as sm
+    cfg, T = sm(CONFIG)
+    ids = synthetic.prompt_ids(cfg, N_TOK, seed=17)
+    nid = l3g.nccl_unique_id()
+    out, errors = {}, []
+
+    def run(rank):
+        try:
+            opts = l3g.default_options(2, rank, rank, l3g.L3G_KV_F32, nid)
+            m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, opts)
+            s, ws = m.NewState(CTX), m.NewWorkspace(CTX, 40)
+            p2p = ws.tp_p2p()
+            logits = np.empty(cfg.vocab, np.float32)
+            rows = []
+            for t in ids:
+                m.ForwardIntoWorkspace(s, int(t), logits, ws)
+                rows.append(logits.copy())
+            out[rank] = (p2p, np.stack(rows))
+            ws.Close()
+            s.Close()
+            m.Close()
+        except Exception as ex:
+            errors.append(f"rank {rank}: {ex!r}")
+
+    th = [threading.Thread(target=run, args=(r,), daemon=True) for r in range(2)]
+    for x in th:
+        x.start()
+    for x in th:
+        x.join(240)
+    if any(x.is_alive() for x in th) or errors or len(out) != 2:
+        with open(os.path.join(out_dir, "errors.txt"), "w") as f:
+            f.write("\n".join(errors) or "a rank thread did not finish")
+        os._exit(1)
+    np.savez(os.path.join(out_dir, "threads.npz"), p2p=np.array([out[0][0], out[1][0]]),
+             l0=out[0][1], l1=out[1][1])
+
+
+def test_tp2_ranks_as_threads_of_one_process(gpu_lib, oracle_mod, tmp_path):
+    """Two ranks driven by two threads of one process (the layout of a Go
+    caller with one OS thread per GPU): the peer buffers are reached through
+    unified addressing instead of IPC, and the results match the reference."""
+    import torch
+    import torch.multiprocessing as mp
+    import synthetic
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    p = mp.get_context("spawn").Process(target=_threads_main, args=(str(tmp_path),))
+    p.start()
+    p.join(300)
+    if p.is_alive():
+        p.kill()
+        p.join(10)
+        pytest.fail("the two-thread run did not finish")
+    err = tmp_path / "errors.txt"
+    assert p.exitcode == 0, err.read_text() if err.exists() else p.exitcode
+    z = np.load(tmp_path / "threads.npz")
+    assert z["p2p"].all(), "same-process peers should use peer memory"
+    assert np.array_equal(z["l0"], z["l1"])
+    cfg, T = synthetic_model(CONFIG)
+    ids = synthetic.prompt_ids(cfg, N_TOK, seed=17)
+    R = ReferenceRuns(oracle_mod, cfg, T, ids, CTX, with_f64=False)
+    errs = [rel_l2(z["l0"][i], R.cgo[i]) for i in range(N_TOK)]
+    assert max(errs) < R.tol(), (errs, R.band())
+
+
 @pytest.mark.parametrize("path", ["p2p", "nccl"])
 def test_tp2_matches_reference_and_single_gpu(gpu_lib, oracle_mod, tmp_path, path):
     """Both reductions: partial sums pushed over peer memory by the Wo / down
