@@ -1020,14 +1020,13 @@ static int tp_setup(l3g_workspace* ws) {
   return L3G_OK;
 }
 
-// Cluster merge of the attention splits: 16 splits per kv head as one
-// (non-portable) cluster, used when clusters for every local kv head can be
-// resident at once (on a 148-SM B200 at most 7 such clusters fit, so a
-// single-GPU 8-kv-head model keeps the global merge; tensor-parallel ranks
-// with 4 or fewer kv heads use the cluster merge, whose tail is a fraction of
-// the global one).
-// L3G_ATT_CLUSTER=0 forces the global-memory merge, =N (2..16) clusters of N
-// CTAs (N splits) whenever they fit (knobs for tests and experiments).
+// Cluster merge of the attention splits: N splits per kv head as one
+// thread-block cluster (L3G_ATT_CLUSTER=N, 2..16, when clusters for every
+// local kv head can be resident at once; a 148-SM B200 holds at most 7
+// clusters of 16).  Off by default: the distributed global merge keeps one
+// CTA per SM streaming, and its tail (~6 us) is close to the cluster's
+// (~5 us), while a cluster of 16 per kv head leaves most SMs idle when a
+// rank has few kv heads.
 template <int DPL, typename KT>
 static void max_attention_clusters(const l3g_workspace* ws, int cs, int* n) {
   cudaLaunchConfig_t cfg = {};
@@ -1059,8 +1058,8 @@ static void choose_attention_cluster(l3g_workspace* ws) {
   const l3g_model* m = ws->m;
   ws->att_cluster = 0;
   const char* env = getenv("L3G_ATT_CLUSTER");
-  if (env && atoi(env) == 0) return;
-  const int knob = env ? atoi(env) : -1;
+  const int knob = env ? atoi(env) : 0;
+  if (knob <= 0) return;
   const int cs = knob >= 2 && knob <= 16 ? knob : 16;
   int n = 0;
   const int dpl = m->hd / 32;
