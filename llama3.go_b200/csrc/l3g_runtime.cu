@@ -1020,13 +1020,14 @@ static int tp_setup(l3g_workspace* ws) {
   return L3G_OK;
 }
 
-// Cluster merge of the attention splits: N splits per kv head as one
-// thread-block cluster (L3G_ATT_CLUSTER=N, 2..16, when clusters for every
-// local kv head can be resident at once; a 148-SM B200 holds at most 7
-// clusters of 16).  Off by default: the distributed global merge keeps one
-// CTA per SM streaming, and its tail (~6 us) is close to the cluster's
-// (~5 us), while a cluster of 16 per kv head leaves most SMs idle when a
-// rank has few kv heads.
+// Cluster merge of the attention splits: 16 splits per kv head as one
+// thread-block cluster, used when clusters for every local kv head can be
+// resident at once (a 148-SM B200 holds at most 7) and the global merge
+// would need 64 or more splits per kv head (1-2 kv heads per rank: TP4,
+// TP8), where its wait and merge over that many partials grow (TP8 tail 11.8
+// vs 5.2 us).  With more kv heads the distributed global merge keeps one CTA
+// per SM streaming and wins.  L3G_ATT_CLUSTER=0 forces the global merge, =N
+// (2..16) clusters of N whenever they fit.
 template <int DPL, typename KT>
 static void max_attention_clusters(const l3g_workspace* ws, int cs, int* n) {
   cudaLaunchConfig_t cfg = {};
@@ -1058,7 +1059,7 @@ static void choose_attention_cluster(l3g_workspace* ws) {
   const l3g_model* m = ws->m;
   ws->att_cluster = 0;
   const char* env = getenv("L3G_ATT_CLUSTER");
-  const int knob = env ? atoi(env) : 0;
+  const int knob = env ? atoi(env) : (m->nsm / m->hkv_l >= 64 ? 16 : 0);
   if (knob <= 0) return;
   const int cs = knob >= 2 && knob <= 16 ? knob : 16;
   int n = 0;
