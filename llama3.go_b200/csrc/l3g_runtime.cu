@@ -1023,10 +1023,10 @@ static int tp_setup(l3g_workspace* ws) {
 // Cluster merge of the attention splits: 16 splits per kv head as one
 // thread-block cluster, used when clusters for every local kv head can be
 // resident at once (a 148-SM B200 holds at most 7) and the global merge
-// would need 64 or more splits per kv head (1-2 kv heads per rank: TP4,
-// TP8), where its wait and merge over that many partials grow (TP8 tail 11.8
-// vs 5.2 us).  With more kv heads the distributed global merge keeps one CTA
-// per SM streaming and wins.  L3G_ATT_CLUSTER=0 forces the global merge, =N
+// would need 32 or more splits per kv head (4 or fewer kv heads per rank:
+// TP2 and up), where its wait and merge over that many partials grow (TP8
+// tail 11.8 vs 5.2 us).  With 8 kv heads the distributed global merge keeps
+// one CTA per SM streaming.  L3G_ATT_CLUSTER=0 forces the global merge, =N
 // (2..16) clusters of N whenever they fit.
 template <int DPL, typename KT>
 static void max_attention_clusters(const l3g_workspace* ws, int cs, int* n) {
@@ -1059,7 +1059,7 @@ static void choose_attention_cluster(l3g_workspace* ws) {
   const l3g_model* m = ws->m;
   ws->att_cluster = 0;
   const char* env = getenv("L3G_ATT_CLUSTER");
-  const int knob = env ? atoi(env) : (m->nsm / m->hkv_l >= 64 ? 16 : 0);
+  const int knob = env ? atoi(env) : (m->nsm / m->hkv_l >= 32 ? 16 : 0);
   if (knob <= 0) return;
   const int cs = knob >= 2 && knob <= 16 ? knob : 16;
   int n = 0;
