@@ -151,6 +151,16 @@ int l3g_state_ctx_len(const l3g_state *s, int32_t *ctx_len);
 /* Moves the write position (0 <= pos <= ctx): rewinds a session for reuse
  * (the REPL's /reset, main.go:120-122) without reallocating. */
 int l3g_state_set_pos(l3g_state *s, int32_t pos);
+/* Session snapshot (a KV-cache checkpoint; no counterpart in the reference,
+ * whose State lives in Go memory and is rebuilt by ingesting the prompt
+ * again, main.go:120-122 and :276-286).  A snapshot holds the position and
+ * this rank's KV rows of positions [0, pos) plus a header (model shape,
+ * shard, KV element type), in host memory.  _bytes gives its size; restore
+ * loads it into a state of the same model shape and shard whose context
+ * length is at least the snapshot's position, and sets that position. */
+int l3g_state_snapshot_bytes(const l3g_state *s, uint64_t *bytes);
+int l3g_state_snapshot(const l3g_state *s, void *dst, uint64_t bytes);
+int l3g_state_restore(l3g_state *s, const void *src, uint64_t bytes);
 void l3g_state_free(l3g_state *s);
 
 /* ---- workspace: NewWorkspace (workspace.go:35-69) ------------------------ */
@@ -189,6 +199,29 @@ int l3g_prefill(l3g_model *m, l3g_state *s, l3g_workspace *ws,
  * stream).  Advances the position by n. */
 int l3g_decode_greedy(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                       int32_t first_token, int32_t n, int32_t *out_tokens,
+                      float *device_ms);
+/* ForwardTopKIntoWorkspace (infer.go:269-511) followed by Sampler.SampleTopK
+ * (sampling.go:103-143) on the device: float64 temperature softmax over the
+ * top-K items, cumulative pick with a uniform draw from Philox4x32-10 keyed
+ * by `seed` and counted by the workspace's draw index (the reference draws
+ * from Go's math/rand, whose stream is not reproduced).  temperature <= 0
+ * means 0.8 and top_k <= 0 the workspace's top-K, as NewSampler
+ * (sampling.go:19-30).  Advances the position. */
+int l3g_forward_sample(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                       int32_t token, int32_t top_k, float temperature,
+                       uint64_t seed, int32_t *next);
+/* The sampled decode loop on the device (n steps: step i ingests a token and
+ * samples out_tokens[i], which step i+1 ingests; one host synchronization),
+ * then the chat loop's stop rule (cmd/go-llama-chat/main.go:146-150):
+ * *n_out counts the samples up to and including the first of stop_ids (n if
+ * none).  The position covers the ingested tokens through the stop token's
+ * own ingestion when the loop ran it (*n_out + 1 steps), else all n steps
+ * (a stop token sampled last is not yet ingested: the caller ingests it, as
+ * main.go:148 does). */
+int l3g_decode_sample(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                      int32_t first_token, int32_t n, int32_t top_k,
+                      float temperature, uint64_t seed, const int32_t *stop_ids,
+                      int32_t n_stop, int32_t *out_tokens, int32_t *n_out,
                       float *device_ms);
 /* Kernels of this library one step launches (greedy variant), for launch
  * accounting. */

@@ -29,6 +29,7 @@ constexpr int CTA_SMEM_SHARE = 112 * 1024;
 constexpr int TILE_TARGET = 32 * 1024;
 constexpr int MAXG = 8;                 // max query heads per kv head
 constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s
+constexpr int MAX_TOPK = 64;  // largest top-K a workspace serves
 // Waits of a tensor-parallel step: a wait can depend, directly or through the
 // kernels launched early behind it, on another GPU's progress, which host
 // skew between the ranks' processes can delay by more than the local bound.
@@ -337,6 +338,70 @@ __global__ void k_embed(const uint8_t* emb, int vocab, int cols, const int* io,
     const float d = __half2float(__ushort_as_half(bits));
     x[i] = __fmul_rn(d, (float)(int8_t)blk[2 + (i & 31)]);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Sampler.SampleTopK (sampling.go:103-143) on the device, after the top-K
+// kernels: maxLogit over the items, e_i = exp(float64(l_i - maxLogit) / T)
+// in float64, r = U * sum e_i, the first item (in the list's order) whose
+// running sum reaches r.  U is a uniform double in [0, 1) from Philox4x32-10
+// (Salmon, Moraes, Dror, Shaw, SC 2011) keyed by the caller's seed and
+// counted by the draw index (the reference draws from Go's math/rand, whose
+// stream is not reproduced).
+// ---------------------------------------------------------------------------
+struct SampleParams {      // copied from the host before a step
+  float temperature;       // > 0
+  int32_t pad;
+  uint64_t seed;
+  uint64_t counter;        // draw index of this step (device-fed: + io[2])
+  uint64_t pad2;
+};
+
+__host__ __device__ inline void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = (uint32_t)p1;
+    c[2] = n2;
+    c[3] = (uint32_t)p0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
+__global__ void k_sample(const int* ids, const float* logits, int k, const SampleParams* sp,
+                         const int* io, Result* res) {
+  __shared__ double e[MAX_TOPK];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x;
+  float mx = logits[0];
+  for (int i = 1; i < k; ++i) mx = fmaxf(mx, logits[i]);
+  const double invT = 1.0 / (double)sp->temperature;
+  for (int i = lane; i < k; i += 32) e[i] = exp((double)(logits[i] - mx) * invT);
+  __syncwarp();
+  if (lane != 0) return;
+  double sum = 0.0;
+  for (int i = 0; i < k; ++i) sum += e[i];
+  const uint64_t ctr = sp->counter + (io ? (uint64_t)io[2] : 0ull);
+  uint32_t c[4] = {(uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u};
+  philox4x32_10(c, (uint32_t)sp->seed, (uint32_t)(sp->seed >> 32));
+  const uint64_t x = ((uint64_t)c[0] << 32) | c[1];
+  const double r = (double)(x >> 11) * 0x1.0p-53 * sum;
+  double acc = 0.0;
+  int pick = k - 1;
+  for (int i = 0; i < k; ++i) {
+    acc += e[i];
+    if (r <= acc) {
+      pick = i;
+      break;
+    }
+  }
+  res->token = ids[pick];
+  res->logit = logits[pick];
 }
 
 // End of a device-fed greedy step: record the argmax and make it the next

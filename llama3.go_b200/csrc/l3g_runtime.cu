@@ -202,6 +202,7 @@ static int setup_kernels() {
     SETK(k_embed);
     SETK(k_advance);
     SETK(k_tp_reduce);
+    SETK(k_sample);
     SETK(k_topk_partial);
 #undef SETK
     rc = e == cudaSuccess ? 0 : (int)e;
@@ -750,6 +751,85 @@ extern "C" int l3g_state_set_pos(l3g_state* s, int32_t pos) {
   return L3G_OK;
 }
 
+// Snapshot layout: SnapHeader, then for each layer and local kv head the
+// interleaved K|V rows of positions [0, pos) (the device layout's prefix).
+struct SnapHeader {
+  char magic[8];  // "L3GKV1\0\0"
+  int32_t n_layers, n_emb, n_heads, n_heads_kv, world, rank, hkv_l, hd, elem_bytes, pos;
+};
+
+static bool snap_header(const l3g_state* s, SnapHeader* h) {
+  const l3g_model* m = s->m;
+  memset(h, 0, sizeof *h);
+  memcpy(h->magic, "L3GKV1", 6);
+  h->n_layers = m->hp.n_layers;
+  h->n_emb = m->hp.n_emb;
+  h->n_heads = m->hp.n_heads;
+  h->n_heads_kv = m->hp.n_heads_kv;
+  h->world = m->world;
+  h->rank = m->rank;
+  h->hkv_l = m->hkv_l;
+  h->hd = m->hd;
+  h->elem_bytes = m->kv_f16 ? 2 : 4;
+  h->pos = s->pos;
+  return true;
+}
+
+static size_t snap_bytes(const SnapHeader& h) {
+  return sizeof(SnapHeader) +
+         (size_t)h.n_layers * h.hkv_l * h.pos * 2 * h.hd * (size_t)h.elem_bytes;
+}
+
+extern "C" int l3g_state_snapshot_bytes(const l3g_state* s, uint64_t* bytes) {
+  if (!s || !bytes) return l3g_fail(L3G_E_INVALID, "null argument");
+  SnapHeader h;
+  snap_header(s, &h);
+  *bytes = snap_bytes(h);
+  return L3G_OK;
+}
+
+extern "C" int l3g_state_snapshot(const l3g_state* s, void* dst, uint64_t bytes) {
+  if (!s || !dst) return l3g_fail(L3G_E_INVALID, "null argument");
+  SnapHeader h;
+  snap_header(s, &h);
+  if (bytes < snap_bytes(h))
+    return l3g_fail(L3G_E_INVALID, "snapshot buffer of %llu bytes, need %llu",
+                    (unsigned long long)bytes, (unsigned long long)snap_bytes(h));
+  memcpy(dst, &h, sizeof h);
+  if (h.pos == 0) return L3G_OK;
+  CUDA_TRY(cudaSetDevice(s->device));
+  const size_t row = (size_t)h.pos * 2 * h.hd * h.elem_bytes;     // one (layer, kv head)
+  const size_t pitch = (size_t)s->ctx * 2 * h.hd * h.elem_bytes;  // its slot in the cache
+  CUDA_TRY(cudaMemcpy2D(static_cast<uint8_t*>(dst) + sizeof h, row, s->kv, pitch, row,
+                        (size_t)h.n_layers * h.hkv_l, cudaMemcpyDeviceToHost));
+  return L3G_OK;
+}
+
+extern "C" int l3g_state_restore(l3g_state* s, const void* src, uint64_t bytes) {
+  if (!s || !src) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (bytes < sizeof(SnapHeader)) return l3g_fail(L3G_E_FORMAT, "snapshot too short");
+  SnapHeader h, mine;
+  memcpy(&h, src, sizeof h);
+  snap_header(s, &mine);
+  if (memcmp(h.magic, mine.magic, 8) != 0) return l3g_fail(L3G_E_FORMAT, "not a KV snapshot");
+  if (h.n_layers != mine.n_layers || h.n_emb != mine.n_emb || h.n_heads != mine.n_heads ||
+      h.n_heads_kv != mine.n_heads_kv || h.world != mine.world || h.rank != mine.rank ||
+      h.hkv_l != mine.hkv_l || h.hd != mine.hd || h.elem_bytes != mine.elem_bytes)
+    return l3g_fail(L3G_E_INVALID, "snapshot of another model shape, shard or KV type");
+  if (h.pos < 0 || h.pos > s->ctx)
+    return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+  if (bytes < snap_bytes(h)) return l3g_fail(L3G_E_FORMAT, "snapshot truncated");
+  if (h.pos > 0) {
+    CUDA_TRY(cudaSetDevice(s->device));
+    const size_t row = (size_t)h.pos * 2 * h.hd * h.elem_bytes;
+    const size_t pitch = (size_t)s->ctx * 2 * h.hd * h.elem_bytes;
+    CUDA_TRY(cudaMemcpy2D(s->kv, pitch, static_cast<const uint8_t*>(src) + sizeof h, row, row,
+                          (size_t)h.n_layers * h.hkv_l, cudaMemcpyHostToDevice));
+  }
+  s->pos = h.pos;
+  return L3G_OK;
+}
+
 extern "C" int l3g_state_read_kv(const l3g_state* s, int32_t layer, int32_t pos0, int32_t npos,
                                  float* k_out, float* v_out) {
   if (!s || !k_out || !v_out) return l3g_fail(L3G_E_INVALID, "null argument");
@@ -787,8 +867,11 @@ extern "C" int l3g_state_read_kv(const l3g_state* s, int32_t layer, int32_t pos0
 // V_GREEDY_DEV: the token and position come from the previous replay's
 // argmax on the device (k_advance), no host copies inside the graph.
 // V_TRACE: V_GREEDY_DEV with the device timeline recorded.
-enum Variant { V_PREFILL = 0, V_ARGMAX = 1, V_LOGITS = 2, V_TOPK = 3, V_GREEDY_DEV = 4, V_TRACE = 5 };
-constexpr int MAX_TOPK = 64;
+enum Variant {
+  V_PREFILL = 0, V_ARGMAX = 1, V_LOGITS = 2, V_TOPK = 3, V_GREEDY_DEV = 4, V_TRACE = 5,
+  V_SAMPLE = 6,      // top-K + device sampler, token to the host
+  V_SAMPLE_DEV = 7   // top-K + device sampler, token fed to the next step
+};
 constexpr int kTraceCap = 256;  // traced launches per step
 constexpr size_t kTraceBytes = (size_t)kTraceCap * TRACE_CTAS * 8 * 8;
 
@@ -834,6 +917,9 @@ struct l3g_workspace {
   int n_splits = 1, att_P = 16, att_ns = 3, att_stage = 0, att_smem = 0, att_gp = 1;
   int att_cluster = 0;         // > 0: the splits of a kv head form one cluster
   unsigned* d_step = nullptr;  // steps run (advanced by k_embed)
+  SampleParams* h_samp = nullptr;  // pinned: the sampler's temperature, seed, draw index
+  SampleParams* d_samp = nullptr;
+  uint64_t draws = 0;              // sampler draws made with this workspace
   int* d_sync = nullptr;       // operand of the ranks' line-up after a capture
   // tensor parallel exchange over peer memory (world > 1 and IPC available)
   bool tp_p2p = false;
@@ -868,10 +954,10 @@ static void ws_release(l3g_workspace* ws) {
   void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
                    ws->attn, ws->act, ws->attn_d, ws->attn_q, ws->act_d, ws->act_q, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
                    ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
-                   ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens, ws->d_trace};
+                   ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens, ws->d_trace, ws->d_samp};
   for (void* p : dptrs)
     if (p) cudaFree(p);
-  void* hptrs[] = {ws->h_io, ws->h_res, ws->h_logits, ws->h_tk_ids, ws->h_tk_logits};
+  void* hptrs[] = {ws->h_io, ws->h_res, ws->h_logits, ws->h_tk_ids, ws->h_tk_logits, ws->h_samp};
   for (void* p : hptrs)
     if (p) cudaFreeHost(p);
   if (ws->stream) cudaStreamDestroy(ws->stream);
@@ -1138,6 +1224,8 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   DM(ws->tk_part, (size_t)ws->tk_chunks * MAX_TOPK * 8);
   DM(ws->d_tokens, (size_t)ctx * 4);
   DM(ws->d_trace, kTraceBytes);
+  HM(ws->h_samp, sizeof(SampleParams));
+  DM(ws->d_samp, sizeof(SampleParams));
   DM(ws->d_step, 4);
   if (e == cudaSuccess) e = cudaMemset(ws->d_step, 0, 4);
   DM(ws->d_sync, 4);
@@ -1356,8 +1444,12 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       ws->prof_ev.push_back(ev_);                      \
     }                                                  \
   } while (0)
-  if (variant != V_GREEDY_DEV)
+  const bool device_fed = variant == V_GREEDY_DEV || variant == V_SAMPLE_DEV;
+  const bool sampled = variant == V_SAMPLE || variant == V_SAMPLE_DEV;
+  if (!device_fed)
     CUDA_TRY(cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, st));
+  if (variant == V_SAMPLE)
+    CUDA_TRY(cudaMemcpyAsync(ws->d_samp, ws->h_samp, sizeof(SampleParams), cudaMemcpyHostToDevice, st));
   KL(L3G_K_EMBED, launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
                   hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res, ws->d_step));
   for (int l = 0; l < hp.n_layers; ++l) {
@@ -1498,7 +1590,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       NCCL_TRY(nccl()->AllGather(ws->d_res, ws->d_gather, sizeof(Result) / 4, ncclInt32, m->comm, st));
       KL(L3G_K_OTHER, launch(k_merge_argmax, dim3(1), dim3(32), 0, st, (const Result*)ws->d_gather,
                       m->world, ws->d_res));
-      if (variant == V_LOGITS || variant == V_TOPK) {
+      if (variant == V_LOGITS || variant == V_TOPK || sampled) {
         NCCL_TRY(nccl()->AllGather(ws->logits, ws->logits_full, m->v_l, ncclFloat, m->comm, st));
         full = ws->logits_full;
       }
@@ -1506,7 +1598,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     if (variant == V_LOGITS)
       CUDA_TRY(cudaMemcpyAsync(ws->h_logits, full, (size_t)hp.vocab_size * 4,
                                cudaMemcpyDeviceToHost, st));
-    if (variant == V_TOPK) {
+    if (variant == V_TOPK || sampled) {
       const int nv = hp.vocab_size;
       const int chunks = (nv + TOPK_CHUNK - 1) / TOPK_CHUNK;
       KL(L3G_K_OTHER, launch(k_topk_partial, dim3(chunks), dim3(512), 0, st, full, nv, k, 0, ws->tk_part));
@@ -1515,11 +1607,17 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       KL(L3G_K_OTHER, launch(k_topk_final, dim3(1), dim3(1024), (size_t)cap * 8, st,
                       (const uint64_t*)ws->tk_part, chunks * k, cap, k, ws->d_tk_ids,
                       ws->d_tk_logits));
-      CUDA_TRY(cudaMemcpyAsync(ws->h_tk_ids, ws->d_tk_ids, k * 4, cudaMemcpyDeviceToHost, st));
-      CUDA_TRY(cudaMemcpyAsync(ws->h_tk_logits, ws->d_tk_logits, k * 4, cudaMemcpyDeviceToHost, st));
+      if (sampled) {
+        KL(L3G_K_OTHER, launch(k_sample, dim3(1), dim3(32), 0, st, (const int*)ws->d_tk_ids,
+                               (const float*)ws->d_tk_logits, k, (const SampleParams*)ws->d_samp,
+                               (const int*)ws->d_io, ws->d_res));
+      } else {
+        CUDA_TRY(cudaMemcpyAsync(ws->h_tk_ids, ws->d_tk_ids, k * 4, cudaMemcpyDeviceToHost, st));
+        CUDA_TRY(cudaMemcpyAsync(ws->h_tk_logits, ws->d_tk_logits, k * 4, cudaMemcpyDeviceToHost, st));
+      }
     }
   }
-  if (variant == V_GREEDY_DEV)
+  if (device_fed)
     KL(L3G_K_OTHER, launch(k_advance, dim3(1), dim3(32), 0, st, ws->d_io, (const Result*)ws->d_res,
               ws->d_tokens));
   else
@@ -1698,6 +1796,101 @@ extern "C" int l3g_decode_greedy(l3g_model* m, l3g_state* s, l3g_workspace* ws,
   if (device_ms) *device_ms = ms;
   ws->logits_valid = true;
   s->pos += n;
+  return L3G_OK;
+}
+
+// Sampler defaults of NewSampler (sampling.go:19-30) for the device sampler.
+static int sample_setup(l3g_workspace* ws, int32_t* top_k, float* temperature, uint64_t seed) {
+  if (*temperature <= 0.0f) *temperature = 0.8f;
+  if (*top_k <= 0) *top_k = ws->topk;
+  if (*top_k > MAX_TOPK) return l3g_fail(L3G_E_INVALID, "top_k %d above %d", *top_k, MAX_TOPK);
+  ws->h_samp->temperature = *temperature;
+  ws->h_samp->seed = seed;
+  ws->h_samp->counter = ws->draws;
+  return L3G_OK;
+}
+
+extern "C" int l3g_forward_sample(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token,
+                                  int32_t top_k, float temperature, uint64_t seed, int32_t* next) {
+  if (!next) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (!ws) return l3g_fail(L3G_E_INVALID, "workspace is nil");
+  int rc = sample_setup(ws, &top_k, &temperature, seed);
+  if (rc) return rc;
+  rc = run_step(m, s, ws, token, V_SAMPLE, top_k);
+  if (rc) return rc;
+  *next = ws->h_res->token;
+  ws->draws += 1;
+  return L3G_OK;
+}
+
+extern "C" int l3g_decode_sample(l3g_model* m, l3g_state* s, l3g_workspace* ws,
+                                 int32_t first_token, int32_t n, int32_t top_k,
+                                 float temperature, uint64_t seed, const int32_t* stop_ids,
+                                 int32_t n_stop, int32_t* out_tokens, int32_t* n_out,
+                                 float* device_ms) {
+  if (!m || !s || !out_tokens || !n_out || (n_stop > 0 && !stop_ids))
+    return l3g_fail(L3G_E_INVALID, "null argument");
+  if (!ws) return l3g_fail(L3G_E_INVALID, "workspace is nil");
+  if (s->m != m || ws->m != m)
+    return l3g_fail(L3G_E_INVALID, "state or workspace belongs to another model");
+  *n_out = 0;
+  if (n <= 0) return L3G_OK;
+  if (ws->ctx < s->ctx)
+    return l3g_fail(L3G_E_INVALID, "workspace ctxLen=%d < state ctxLen=%d", ws->ctx, s->ctx);
+  if (s->pos + n > s->ctx) return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+  if (first_token < 0 || first_token >= m->hp.vocab_size)
+    return l3g_fail(L3G_E_TOKEN, "token out of range: %d", first_token);
+  int rc = sample_setup(ws, &top_k, &temperature, seed);
+  if (rc) return rc;
+  CUDA_TRY(cudaSetDevice(m->device));
+  cudaGraphExec_t exec;
+  rc = get_graph(ws, s, V_SAMPLE_DEV, top_k, &exec);
+  if (rc) return rc;
+  cudaEvent_t e0, e1;
+  CUDA_TRY(cudaEventCreate(&e0));
+  CUDA_TRY(cudaEventCreate(&e1));
+  ws->h_io[0] = first_token;
+  ws->h_io[1] = s->pos;
+  ws->h_io[2] = 0;
+  ws->h_io[3] = 0;
+  cudaError_t e = cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, ws->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(ws->d_samp, ws->h_samp, sizeof(SampleParams), cudaMemcpyHostToDevice,
+                        ws->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(e0, ws->stream);
+  for (int i = 0; i < n && e == cudaSuccess; ++i) e = cudaGraphLaunch(exec, ws->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(e1, ws->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(ws->h_res, ws->d_res, sizeof(Result), cudaMemcpyDeviceToHost, ws->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ws->stream);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(out_tokens, ws->d_tokens, (size_t)n * 4, cudaMemcpyDeviceToHost);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "sampled decode: %s", cudaGetErrorString(e));
+  if (ws->h_res->err) {
+    const int code = ws->h_res->err, where = ws->h_res->where;
+    cudaMemset(ws->d_res, 0, sizeof(Result));
+    return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d", code, where);
+  }
+  ws->draws += (uint64_t)n;
+  // the chat loop's stop rule (cmd/go-llama-chat/main.go:146-150): the
+  // samples up to and including the first stop id count; the position
+  // covers the tokens ingested up to the stop token's own ingestion (the
+  // step after it was sampled), which the loop ran unless it was the last
+  int kept = n;
+  for (int i = 0; i < n && kept == n; ++i)
+    for (int j = 0; j < n_stop; ++j)
+      if (out_tokens[i] == stop_ids[j]) {
+        kept = i + 1;
+        break;
+      }
+  *n_out = kept;
+  if (device_ms) *device_ms = ms;
+  ws->logits_valid = kept == n;
+  s->pos += kept < n ? kept + 1 : n;
   return L3G_OK;
 }
 

@@ -98,6 +98,9 @@ def lib():
         "l3g_state_pos": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_state_ctx_len": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_state_set_pos": (C.c_int, [_P, C.c_int32]),
+        "l3g_state_snapshot_bytes": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
+        "l3g_state_snapshot": (C.c_int, [_P, _P, C.c_uint64]),
+        "l3g_state_restore": (C.c_int, [_P, _P, C.c_uint64]),
         "l3g_state_free": (None, [_P]),
         "l3g_workspace_new": (C.c_int, [_P, C.c_int32, C.c_int32, C.POINTER(_P)]),
         "l3g_workspace_free": (None, [_P]),
@@ -107,6 +110,12 @@ def lib():
         "l3g_forward_argmax": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32),
                                          C.POINTER(C.c_float)]),
         "l3g_prefill": (C.c_int, [_P, _P, _P, C.POINTER(C.c_int32), C.c_int32]),
+        "l3g_forward_sample": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_float, C.c_uint64,
+                                         C.POINTER(C.c_int32)]),
+        "l3g_decode_sample": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_float,
+                                        C.c_uint64, C.POINTER(C.c_int32), C.c_int32,
+                                        C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                        C.POINTER(C.c_float)]),
         "l3g_decode_greedy": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.POINTER(C.c_int32),
                                         C.POINTER(C.c_float)]),
         "l3g_workspace_kernels_per_step": (C.c_int, [_P, C.POINTER(C.c_int32)]),
@@ -291,6 +300,30 @@ class Model:
                                        out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(ms)))
         return out, ms.value
 
+    def ForwardSample(self, s: "State", token: int, ws: "Workspace", top_k: int = 0,
+                      temperature: float = 0.8, seed: int = 1) -> int:
+        """ForwardTopKIntoWorkspace + SampleTopK on the device (Philox draw
+        `seed`, counted per workspace); returns the sampled id."""
+        nxt = C.c_int32()
+        _check(lib().l3g_forward_sample(self._h, s._h, _ws(ws), int(token), int(top_k),
+                                        float(temperature), int(seed) & (2**64 - 1), C.byref(nxt)))
+        return nxt.value
+
+    def DecodeSample(self, s: "State", first_token: int, n: int, ws: "Workspace", top_k: int = 0,
+                     temperature: float = 0.8, seed: int = 1, stop_ids=()):
+        """n sampled steps fed on the device; returns (tokens up to and
+        including the first stop id, device_ms)."""
+        out = np.empty(n, np.int32)
+        stops = np.ascontiguousarray(np.asarray(stop_ids, np.int32))
+        n_out = C.c_int32()
+        ms = C.c_float()
+        _check(lib().l3g_decode_sample(self._h, s._h, _ws(ws), int(first_token), n, int(top_k),
+                                       float(temperature), int(seed) & (2**64 - 1),
+                                       stops.ctypes.data_as(C.POINTER(C.c_int32)) if stops.size else None,
+                                       stops.size, out.ctypes.data_as(C.POINTER(C.c_int32)),
+                                       C.byref(n_out), C.byref(ms)))
+        return out[:n_out.value], ms.value
+
 
 def _ws(ws):
     return ws._h if ws is not None else None
@@ -331,6 +364,20 @@ class State:
         return k.reshape(shape), v.reshape(shape)
 
     local_kv_heads = property(lambda self: self.model.HP.NHeadsKV // getattr(self.model, "world_size", 1))
+
+    def Snapshot(self) -> np.ndarray:
+        """The position and KV rows [0, Pos) of this rank, as host bytes."""
+        n = C.c_uint64()
+        _check(lib().l3g_state_snapshot_bytes(self._h, C.byref(n)))
+        buf = np.empty(n.value, np.uint8)
+        _check(lib().l3g_state_snapshot(self._h, buf.ctypes.data, n.value))
+        return buf
+
+    def Restore(self, snap: np.ndarray):
+        """Loads a Snapshot of a state of the same model (any context length
+        at least its position) and moves to its position."""
+        snap = np.ascontiguousarray(snap, dtype=np.uint8)
+        _check(lib().l3g_state_restore(self._h, snap.ctypes.data, snap.size))
 
     def Close(self):
         if self._h:

@@ -281,6 +281,46 @@ def test_attention_merge_modes(gpu_lib, oracle_mod, monkeypatch, mode):
         assert rel_l2(attn, R.cgo_model.buffer("attn")) < R.tol()
 
 
+def test_snapshot_restore_resumes_bit_for_bit(gpu_lib):
+    """A state restored from a snapshot (into a state with a longer context)
+    continues exactly like the original; mismatched shapes and buffers are
+    rejected."""
+    import synthetic
+    cfg, T = synthetic_model("tiny-gqa")
+    m = _load_gpu(gpu_lib, cfg, T)
+    ids = synthetic.prompt_ids(cfg, 20, seed=31)
+    a = m.NewState(48)
+    ws = m.NewWorkspace(96, 40)
+    m.Prefill(a, ids[:-1], ws)
+    snap = a.Snapshot()
+    b = m.NewState(96)
+    b.Restore(snap)
+    assert b.Pos == a.Pos == len(ids) - 1
+    la, lb = np.empty(cfg.vocab, np.float32), np.empty(cfg.vocab, np.float32)
+    ta = tb = int(ids[-1])
+    for _ in range(6):
+        m.ForwardIntoWorkspace(a, ta, la, ws)
+        m.ForwardIntoWorkspace(b, tb, lb, ws)
+        assert np.array_equal(la, lb)
+        ta = tb = int(np.argmax(la))
+    Ka, Va = a.read_kv(1, 0, a.Pos)
+    Kb, Vb = b.read_kv(1, 0, b.Pos)
+    assert np.array_equal(Ka, Kb) and np.array_equal(Va, Vb)
+    small = m.NewState(8)  # too short for the snapshot's position
+    with pytest.raises(gpu_lib.L3GError, match="context length exceeded"):
+        small.Restore(snap)
+    with pytest.raises(gpu_lib.L3GError, match="truncated"):
+        b.Restore(snap[:-4])
+    cfg2, T2 = synthetic_model("tiny")
+    m2 = _load_gpu(gpu_lib, cfg2, T2)
+    with pytest.raises(gpu_lib.L3GError, match="another model shape"):
+        m2.NewState(96).Restore(snap)
+    m2.Close()
+    for x in (small, b, a, ws):
+        x.Close()
+    m.Close()
+
+
 def test_free_order_does_not_matter(gpu_lib):
     """Model freed before its state and workspace (whose captured graphs the
     model releases first): no fault, and the later frees are harmless."""

@@ -133,3 +133,34 @@ def test_header_cites_reference_for_each_entry():
     for ref in ("simd.h:7-9", "workers.go", "infer.go:21-267", "infer.go:269-511",
                 "model.go:55-156", "state.go:51-64", "workspace.go:35-69", "q8_0.go:22-79"):
         assert ref in hdr, ref
+
+
+def test_philox_known_answers():
+    """The test-side Philox4x32-10 reproduces the published known-answer
+    values (counter, key) -> output of the algorithm."""
+    from sampler_ref import philox4x32_10
+    kat = [
+        ([0, 0, 0, 0], [0, 0], [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]),
+        ([0xFFFFFFFF] * 4, [0xFFFFFFFF] * 2, [0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]),
+        ([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], [0xA4093822, 0x299F31D0],
+         [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]),
+    ]
+    for ctr, key, want in kat:
+        assert philox4x32_10(ctr, key) == want
+
+
+def test_sampler_restatement_is_a_distribution():
+    """Over many draw indices the restated sampler picks each item with its
+    softmax probability (chi-square-free check: every frequency within 4
+    standard deviations)."""
+    import math
+    from sampler_ref import sample_topk
+    ids = [10, 11, 12, 13]
+    logits = [2.0, 1.0, 0.5, -1.0]
+    T, n = 0.8, 20000
+    counts = {i: 0 for i in ids}
+    for c in range(n):
+        counts[sample_topk(ids, logits, T, 1234, c)] += 1
+    e = [math.exp((l - 2.0) / T) for l in logits]
+    for i, p in zip(ids, [v / sum(e) for v in e]):
+        assert abs(counts[i] - n * p) < 4 * math.sqrt(n * p * (1 - p)), (i, counts[i], n * p)
