@@ -7,10 +7,12 @@
 // K|V rows of P positions per stage through a shared-memory ring (one ~32 KB
 // bulk copy per stage), and keeps an online softmax per warp:
 //   - lanes split the head dimension (DPL = hd / 32 values each);
-//   - a warp takes NBW = P / 8 positions of each stage in sub-batches of
-//     32 / GP positions (GP = group rounded up to a power of two), computes
-//     the partial dots of every (position, head) pair and transpose-reduces
-//     them so lane i ends with complete score i (31 shuffles per sub-batch);
+//   - a warp takes nbw positions of a stage in sub-batches of 32 / GP
+//     positions (GP = group rounded up to a power of two), computes the
+//     partial dots of every (position, head) pair and transpose-reduces them
+//     so lane i ends with complete score i (31 shuffles per sub-batch); when
+//     a stage holds fewer than 8 sub-batches the warps form two groups that
+//     take alternate stages, so every sub-batch is full;
 //   - probabilities are broadcast through a warp-private buffer for the V
 //     accumulation.
 // The per-warp states merge in the CTA.  The CTAs (splits) of one kv head
