@@ -353,7 +353,7 @@ struct SampleParams {      // copied from the host before a step
   float temperature;       // > 0
   int32_t pad;
   uint64_t seed;
-  uint64_t counter;        // draw index of this step (device-fed: + io[2])
+  uint64_t counter;        // draw index of this step (device-fed loop: + io[2])
   uint64_t pad2;
 };
 

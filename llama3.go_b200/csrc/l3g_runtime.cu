@@ -1610,7 +1610,9 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       if (sampled) {
         KL(L3G_K_OTHER, launch(k_sample, dim3(1), dim3(32), 0, st, (const int*)ws->d_tk_ids,
                                (const float*)ws->d_tk_logits, k, (const SampleParams*)ws->d_samp,
-                               (const int*)ws->d_io, ws->d_res));
+                               // the device-fed loop's step index offsets the draw
+                               (const int*)(variant == V_SAMPLE_DEV ? ws->d_io : nullptr),
+                               ws->d_res));
       } else {
         CUDA_TRY(cudaMemcpyAsync(ws->h_tk_ids, ws->d_tk_ids, k * 4, cudaMemcpyDeviceToHost, st));
         CUDA_TRY(cudaMemcpyAsync(ws->h_tk_logits, ws->d_tk_logits, k * 4, cudaMemcpyDeviceToHost, st));
@@ -1688,6 +1690,8 @@ static int run_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token
   if (rc) return rc;
   ws->h_io[0] = token;
   ws->h_io[1] = s->pos;
+  ws->h_io[2] = 0;
+  ws->h_io[3] = 0;
   CUDA_TRY(cudaGraphLaunch(exec, ws->stream));
   CUDA_TRY(cudaStreamSynchronize(ws->stream));
   if (ws->h_res->err) {

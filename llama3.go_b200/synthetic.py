@@ -74,6 +74,10 @@ CONFIGS = {
     "small-hd128": Config("small-hd128", 512, 2, 4, 1, 1024, 2048, tied=False,
                           rope_scaling=(8.0, 1.0, 4.0, 8192), ctx_len=4608),
     "mid": Config("mid", 1024, 4, 8, 2, 2816, 8000, tied=True, ctx_len=1024),
+    # a GQA group of 3 (the 3B shape's 24 / 8), padded to 4 in attention
+    "tiny-g3": Config("tiny-g3", 192, 2, 6, 2, 384, 500, tied=True, ctx_len=128),
+    # the 1B layer shapes (head_dim 64, the full vocabulary) with two layers
+    "llama3.2-1b-2l": Config("llama3.2-1b-2l", 2048, 2, 32, 8, 8192, 128256, tied=True, ctx_len=2048),
 }
 
 

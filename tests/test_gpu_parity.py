@@ -146,13 +146,15 @@ def _log(record):
 
 
 @pytest.mark.parametrize("name,n_tok", [("tiny", 24), ("tiny-gqa", 24), ("small", 40),
-                                        ("small-hd128", 24), ("mid", 16)])
+                                        ("small-hd128", 24), ("mid", 16), ("tiny-g3", 24),
+                                        ("llama3.2-1b-2l", 16)])
 def test_forward_logits_and_kv_parity(gpu_lib, oracle_mod, name, n_tok):
     import synthetic
     cfg, T = synthetic_model(name)
     ctx = min(cfg.ctx_len, 256)
     ids = synthetic.prompt_ids(cfg, n_tok, seed=11)
-    R = ReferenceRuns(oracle_mod, cfg, T, ids, ctx)
+    # the float64 numpy forward dequantizes everything: small vocabularies only
+    R = ReferenceRuns(oracle_mod, cfg, T, ids, ctx, with_f64=cfg.vocab * cfg.n_emb < 50_000_000)
     tol = R.tol()
     m = _load_gpu(gpu_lib, cfg, T)
     s = m.NewState(ctx)
@@ -163,11 +165,12 @@ def test_forward_logits_and_kv_parity(gpu_lib, oracle_mod, name, n_tok):
         m.ForwardIntoWorkspace(s, int(t), logits, ws)
         errs.append(rel_l2(logits, R.cgo[i]))
         vs_pure.append(rel_l2(logits, R.pure[i]))
-        vs_f64.append(rel_l2(logits, R.f64[i]))
+        if R.f64:
+            vs_f64.append(rel_l2(logits, R.f64[i]))
     worst = max(errs)
     _log({"test": "forward_logits", "config": name, "steps": n_tok, "gpu_vs_cgo_worst": worst,
           "gpu_vs_cgo_first": errs[0], "gpu_vs_pure_worst": max(vs_pure),
-          "gpu_vs_f64_worst": max(vs_f64), "reference_band": R.band(), "tol": tol})
+          "gpu_vs_f64_worst": max(vs_f64) if vs_f64 else None, "reference_band": R.band(), "tol": tol})
     assert worst < tol, (worst, R.band())
     assert s.Pos == n_tok
     # every layer's KV cache: roped K and V at every position
