@@ -85,14 +85,31 @@ class Clocks:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int):
-        self.idx = device_index
+    def __init__(self, device: str):
+        """device: what nvidia-smi -i accepts (an index or a UUID)."""
+        self.dev = device
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+            self.p = subprocess.Popen(["nvidia-smi", "-i", device, f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+
+    def wait_first_sample(self, timeout_s: float = 5.0):
+        """Blocks (bounded) until the sampler has written a row, so the timed
+        region that follows is covered from its start."""
+        if self.p is None:
+            return
+        t0 = time.time()
+        while time.time() - t0 < timeout_s and self.p.poll() is None:
+            try:
+                with open(self.f.name) as g:
+                    if any(len(r.split(",")) >= 9 for r in g.read().splitlines()):
+                        return
+            except OSError:
+                pass
+            time.sleep(0.02)
 
     def stop(self):
         if self.p is None:
@@ -102,7 +119,7 @@ class Clocks:
         self.f.seek(0)
         rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
         os.unlink(self.f.name)
-        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9 and r[0].strip() == str(self.idx)]
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -114,13 +131,14 @@ class Clocks:
                 "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
 
 
-def physical_index(local: int) -> int:
+def physical_index(local: int) -> str:
+    """The nvidia-smi identifier (index or UUID) of CUDA device `local`."""
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
-        parts = [p for p in vis.split(",") if p.strip()]
-        if local < len(parts) and parts[local].strip().isdigit():
-            return int(parts[local])
-    return local
+        parts = [p.strip() for p in vis.split(",") if p.strip()]
+        if local < len(parts):
+            return parts[local]
+    return str(local)
 
 
 # ---------------------------------------------------------------------------
@@ -383,8 +401,11 @@ def run_l3g(args):
     # value: device-resident greedy loop
     progress(world, rank, "decode warm-up")
     warm, _ = m.DecodeGreedy(s, int(prompt[-1]), max(1, args.warmup), ws)
-    D.barrier()
     clk = Clocks(physical_index(local))
+    clk.wait_first_sample()
+    # ranks enter the timed loop together (its steps wait on each other's
+    # exchanges, so a late rank's start would count in an early rank's time)
+    D.barrier()
     torch.cuda.nvtx.range_push("l3g_decode")
     toks, dev_ms = m.DecodeGreedy(s, int(warm[-1]), args.steps, ws)
     torch.cuda.nvtx.range_pop()
