@@ -106,7 +106,8 @@ def test_tp2_decomposition_matches_single_rank(tmp_path, name):
 def test_shard_plan_covers_every_row_once():
     import l3g
     import synthetic
-    for name, world in (("llama3.1-8b", 8), ("llama3.1-8b", 2), ("llama3.2-3b", 2), ("tiny-gqa", 2)):
+    for name, world in (("llama3.1-8b", 8), ("llama3.1-8b", 4), ("llama3.1-8b", 2), ("llama3.2-3b", 2),
+                        ("llama3.2-3b", 4), ("llama3.2-3b", 8), ("llama3.2-1b", 8), ("tiny-gqa", 2)):
         cfg = synthetic.CONFIGS[name]
         hp = l3g.hparams_for(cfg)
         plans = [l3g.shard_plan(hp, world, r) for r in range(world)]
