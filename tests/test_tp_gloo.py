@@ -124,3 +124,48 @@ def test_shard_plan_covers_every_row_once():
         l3g.shard_plan(l3g.hparams_for(synthetic.CONFIGS["llama3.2-3b"]), 16, 0)
     with pytest.raises(l3g.L3GError, match="rank"):
         l3g.shard_plan(l3g.hparams_for(synthetic.CONFIGS["tiny-gqa"]), 2, 2)
+
+
+def test_exchange_protocol_never_reads_overwritten_words():
+    """Model of the tensor-parallel exchange under random interleavings of
+    the ranks: rank r's program is push(1), reduce(1), push(2), reduce(2),
+    ... (Wo / down push their partials for epoch e into slot r of parity
+    e % 2 of every rank's buffer; the reduce kernel of epoch e waits until
+    its buffer holds epoch e in every slot of that parity).  A rank's next
+    kernel runs only after its previous one completed (stream order), so a
+    push can never overwrite words a slower rank has not read yet: every
+    reduce sees exactly its epoch, and no schedule deadlocks."""
+    import random
+    for world in (2, 3, 8):
+        for trial in range(200):
+            rng = random.Random(world * 1000 + trial)
+            phases = 12
+            buf = [[[0] * world for _ in range(2)] for _ in range(world)]  # [rank][parity][src]
+            nxt = [0] * world  # index into the program: 2e = push(e+1), 2e+1 = reduce(e+1)
+            done = 0
+            while done < world:
+                ready = []
+                for r in range(world):
+                    i = nxt[r]
+                    if i >= 2 * phases:
+                        continue
+                    e = i // 2 + 1
+                    if i % 2 == 0:
+                        ready.append(r)  # a push depends only on the rank's own stream
+                    elif all(buf[r][e % 2][s] == e for s in range(world)):
+                        ready.append(r)  # a reduce waits for every rank's epoch e
+                assert ready, "deadlock"
+                r = rng.choice(ready)
+                i = nxt[r]
+                e = i // 2 + 1
+                if i % 2 == 0:
+                    for p in range(world):
+                        # the words it replaces are from epoch e - 2, already read by p
+                        assert buf[p][e % 2][r] in (0, e - 2)
+                        assert buf[p][e % 2][r] == 0 or nxt[p] > 2 * (e - 2) - 1
+                        buf[p][e % 2][r] = e
+                else:
+                    assert all(buf[r][e % 2][s] == e for s in range(world))
+                nxt[r] += 1
+                if nxt[r] == 2 * phases:
+                    done += 1
