@@ -59,6 +59,7 @@ typedef struct l3g_model l3g_model;
 typedef struct l3g_state l3g_state;
 typedef struct l3g_workspace l3g_workspace;
 typedef struct l3g_matrix l3g_matrix;
+typedef struct l3g_gemm_matrix l3g_gemm_matrix;
 
 /* HyperParams, internal/llama/model.go:10-21.  llama3 RoPE frequency scaling,
  * absent from the reference (rope.go:15-37), is taken from an optional f32
@@ -323,6 +324,41 @@ int l3g_matvec_q8_argmax_static(const l3g_matrix *w, const float *x_scales,
  * ceil(n/32) floats, qs ceil(n/32)*32 bytes. */
 int l3g_quantize_q8_0(const float *x, int32_t n, float *d, int8_t *qs,
                       void *stream);
+
+/* ---- batched Q8_0 product on the tensor cores (tcgen05 kind::i8) --------- */
+/* n_tok independent Q8_0 matvecs over one weight matrix, as one GEMM:
+ * out[n][r] = sum_b (fp16(w.d[r,b]) * x.d[n,b]) * (sum_i w.q[r,b,i] *
+ * x.q[n,b*32+i]), i.e. matvec_q8_c (simd.h:8, simd.c:33-110; matVecQ8_0,
+ * matvec_cgo.go:14-30) of every token's activation quantized by
+ * QuantizeQ8_0Into (q8_0.go:22-79).  One int8 MMA per Q8_0 block (K = 32)
+ * and the fp32 rescale by w.d * x.d per block, so each block's integer sum
+ * is exact as in the reference.  The reference has no batched call: it runs
+ * prompt tokens one ForwardIntoWorkspace at a time
+ * (cmd/go-llama-chat/main.go:276-286); this is the building block of batched
+ * prefill and batched decode.
+ *  - l3g_gemm_matrix_upload repacks GGUF Q8_0 rows (host bytes, values
+ *    unchanged) into 128-row x 128-column chunks on the device;
+ *    l3g_gemm_repack is the same repack into a host buffer of
+ *    l3g_gemm_matrix_bytes bytes (no device needed).
+ *  - l3g_gemm_quantize quantizes x [n_tok][cols] (DEVICE f32) into the
+ *    product's activation buffer act (DEVICE, l3g_gemm_act_bytes bytes,
+ *    16-byte aligned), bit-identical to QuantizeQ8_0Into per row.
+ *  - l3g_gemm_q8 writes out [n_tok][rows] (DEVICE f32); asynchronous on
+ *    stream.  l3g_gemm_status synchronizes the device and returns (and
+ *    clears) the error word of the kernel's bounded waits: err 0, or 1 with
+ *    `where` naming the wait that gave up. */
+int l3g_gemm_matrix_bytes(int32_t rows, int32_t cols, uint64_t *bytes);
+int l3g_gemm_repack(const void *q8_0_rows, int32_t rows, int32_t cols, void *dst,
+                    uint64_t dst_bytes);
+int l3g_gemm_matrix_upload(const void *q8_0_rows, int32_t rows, int32_t cols,
+                           int32_t device, l3g_gemm_matrix **out);
+void l3g_gemm_matrix_free(l3g_gemm_matrix *w);
+int l3g_gemm_act_bytes(int32_t n_tok, int32_t cols, uint64_t *bytes);
+int l3g_gemm_quantize(const float *x, int32_t n_tok, int32_t cols, void *act,
+                      void *stream);
+int l3g_gemm_q8(const l3g_gemm_matrix *w, const void *act, int32_t n_tok,
+                float *out, void *stream);
+int l3g_gemm_status(const l3g_gemm_matrix *w, int32_t *err, int32_t *where);
 
 /* ---- inspection (tests, debugging) --------------------------------------- */
 /* KV entries of one layer for positions [pos0, pos0+npos) in the reference

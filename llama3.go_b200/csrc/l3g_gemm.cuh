@@ -1,0 +1,313 @@
+// Batched Q8_0 product on the tcgen05 tensor cores (included by
+// l3g_kernels.cuh, inside namespace l3g, after l3g_gemm_layout.h).
+#pragma once
+
+// ---------------------------------------------------------------------------
+// tcgen05 helpers (tensor memory, MMA issue and completion)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// whole warp: allocate ncols columns (power of two >= 32) of tensor memory,
+// base address written to *dst (shared memory)
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// one thread: D[tmem] = A * B (accumulate = 0) or D += A * B
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// one thread: arrive once on *bar when every tcgen05 operation this thread
+// issued before has completed
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+// whole warp: 8 consecutive 32-bit columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                 "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmArgs {
+  const uint8_t* a;   // weight chunks [row tiles][nk] (gemm::A_CHUNK bytes each)
+  const uint8_t* b;   // activation chunks [token tiles][nk] (gemm::b_chunk(NT) each)
+  float* out;         // [n_tok][rows]
+  int rows, n_tok, nk, n_rt, n_tt;
+  int nstages;
+  Result* res;
+  unsigned long long wait_ns;
+};
+
+constexpr int GEMM_EPI_WARPS = 8;                      // two warpgroups
+constexpr int GEMM_THREADS = 32 * (2 + GEMM_EPI_WARPS);  // producer, MMA, rescale
+
+struct GemmSmem {
+  uint64_t full[gemm::MAX_STAGES_G];   // stage landed (A and B copies)
+  uint64_t empty[gemm::MAX_STAGES_G];  // stage consumed: 1 MMA commit + 8 rescale warps
+  uint64_t tfull[8];                   // TMEM buffer holds a finished block product
+  uint64_t tempty[8];                  // TMEM buffer read by all 8 rescale warps
+  uint64_t drain;                      // every MMA issued has completed
+  uint32_t tmem_base;
+  int abort_flag;
+  int issued;
+  int producer_done;
+};
+static_assert(sizeof(GemmSmem) <= gemm::SMEM_HEAD, "gemm smem head");
+
+// out[n][r] = sum over Q8_0 blocks b of fp16(d_w[r,b]) * d_x[n,b] * I_b[r,n]
+// for every token n < n_tok and row r < rows: n_tok matvec_q8_c products
+// (simd.c:33-110) sharing one pass over the weights.
+//
+// Roles: warp 0 lane 0 streams (weight chunk, activation chunk) pairs into a
+// ring of shared-memory stages with 1-D bulk copies (the weight copies of the
+// first stages are issued before griddepcontrol.wait: weights never depend on
+// the previous kernel); warp 1 lane 0 issues one kind::i8 MMA per Q8_0 block
+// (M = 128 weight rows, N = NT tokens, K = 32) into one of NB tensor-memory
+// buffers and commits its completion to that buffer's barrier; warps 2-9 read
+// each block's int32 products back (warp w reads TMEM lanes 32*(w%4).., i.e.
+// weight rows, and columns of its half of the token tile), rescale them by
+// d_w * d_x and accumulate in fp32 registers, then release the buffer.  A
+// stage is refilled once its four MMAs have completed and all eight rescale
+// warps have read its scales.  Tiles (row tile, token tile) are dealt
+// round-robin over the grid; after the last chunk of a tile the rescale warps
+// store its outputs.
+template <int NT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_q8(const __grid_constant__ GemmArgs g) {
+  using namespace gemm;
+  constexpr int NB = tmem_buffers(NT);
+  constexpr uint32_t TCOLS = tmem_cols(NT);
+  constexpr int CPT = NT / 2;  // token columns per rescale thread
+  constexpr uint32_t IDESC = idesc_i8(TILE_M, NT);
+  constexpr int SB = stage_bytes(NT);
+  static_assert(NB * NT <= (int)TCOLS && TCOLS <= 512, "tensor memory budget");
+  static_assert(CPT % 8 == 0, "tcgen05.ld granularity");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  GemmSmem* sh = reinterpret_cast<GemmSmem*>(smem);
+  uint8_t* ring = smem + SMEM_HEAD;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ns = g.nstages;
+  const int n_tiles = g.n_rt * g.n_tt;
+  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+  const int my_tiles = cta < n_tiles ? (n_tiles - cta + G - 1) / G : 0;
+  const int nchunks = my_tiles * g.nk;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&sh->full[s], 1);
+      mbar_init(&sh->empty[s], 1 + GEMM_EPI_WARPS);
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&sh->tfull[i], 1);
+      mbar_init(&sh->tempty[i], GEMM_EPI_WARPS);
+    }
+    mbar_init(&sh->drain, 1);
+    sh->abort_flag = 0;
+    sh->issued = 0;
+    sh->producer_done = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&sh->tmem_base, TCOLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---- producer -------------------------------------------------------
+    if (lane == 0) {
+      auto a_src = [&](int c) {
+        const int tile = cta + (c / g.nk) * G;
+        return g.a + ((size_t)(tile % g.n_rt) * g.nk + (c % g.nk)) * A_CHUNK;
+      };
+      auto b_src = [&](int c) {
+        const int tile = cta + (c / g.nk) * G;
+        return g.b + ((size_t)(tile / g.n_rt) * g.nk + (c % g.nk)) * b_chunk(NT);
+      };
+      const int pre = nchunks < ns ? nchunks : ns;
+      for (int c = 0; c < pre; ++c) {
+        mbar_arrive_expect_tx(&sh->full[c], SB);
+        bulk_g2s(ring + (size_t)c * SB, a_src(c), A_CHUNK, &sh->full[c]);
+      }
+      pdl_wait();  // the activations come from the previous kernel
+      for (int c = 0; c < pre; ++c)
+        bulk_g2s(ring + (size_t)c * SB + A_CHUNK, b_src(c), b_chunk(NT), &sh->full[c]);
+      *(volatile int*)&sh->issued = pre;
+      for (int c = pre; c < nchunks; ++c) {
+        const int s = c % ns;
+        if (!mbar_wait(&sh->empty[s], ((c / ns) - 1) & 1, &sh->abort_flag, g.res, 20, g.wait_ns))
+          break;
+        mbar_arrive_expect_tx(&sh->full[s], SB);
+        bulk_g2s(ring + (size_t)s * SB, a_src(c), A_CHUNK, &sh->full[s]);
+        bulk_g2s(ring + (size_t)s * SB + A_CHUNK, b_src(c), b_chunk(NT), &sh->full[s]);
+        *(volatile int*)&sh->issued = c + 1;
+      }
+      *(volatile int*)&sh->producer_done = 1;
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer -----------------------------------------------------
+    if (lane == 0) {
+      int blk = 0;
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int s = c % ns;
+        if (!mbar_wait(&sh->full[s], (c / ns) & 1, &sh->abort_flag, g.res, 21, g.wait_ns)) break;
+        const uint32_t a0 = smem_u32(ring + (size_t)s * SB);
+        const uint32_t b0 = a0 + A_CHUNK;
+#pragma unroll
+        for (int j = 0; j < BPC; ++j, ++blk) {
+          const int buf = blk % NB, use = blk / NB;
+          if (use > 0 &&
+              !mbar_wait(&sh->tempty[buf], (use - 1) & 1, &sh->abort_flag, g.res, 22, g.wait_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          mma_i8(tmem + (uint32_t)(buf * NT), a_desc(a0, j), b_desc(b0, j, NT), IDESC, 0u);
+          mma_commit(&sh->tfull[buf]);
+        }
+        if (ok) mma_commit(&sh->empty[s]);
+      }
+      // every MMA issued has completed before the tensor memory is released
+      if (blk > 0) {
+        mma_commit(&sh->drain);
+        int dummy = 0;
+        mbar_wait(&sh->drain, 0, &dummy, g.res, 23, g.wait_ns);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- rescale warps --------------------------------------------------
+    const int ep = warp - 2;
+    const int quarter = warp & 3;      // TMEM lanes this warp may read
+    const int half = ep >> 2;          // token columns [half*CPT, half*CPT+CPT)
+    const int m = quarter * 32 + lane; // weight row within the tile
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * CPT);
+    int c = 0, blk = 0;
+    bool ok = true;
+    for (int ti = 0; ti < my_tiles && ok; ++ti) {
+      const int tile = cta + ti * G;
+      const int rt = tile % g.n_rt, tt = tile / g.n_rt;
+      float acc[CPT];
+#pragma unroll
+      for (int i = 0; i < CPT; ++i) acc[i] = 0.0f;
+      for (int kc = 0; kc < g.nk; ++kc, ++c) {
+        const int s = c % ns;
+        ok = __all_sync(0xffffffffu, mbar_wait(&sh->full[s], (c / ns) & 1, &sh->abort_flag,
+                                               g.res, 24, g.wait_ns));
+        if (!ok) break;
+        const uint8_t* st = ring + (size_t)s * SB;
+        const __half* dw = reinterpret_cast<const __half*>(st + A_Q_BYTES);
+        const float* dx = reinterpret_cast<const float*>(st + A_CHUNK + b_q_bytes(NT));
+#pragma unroll 1
+        for (int j = 0; j < BPC; ++j, ++blk) {
+          const int buf = blk % NB, use = blk / NB;
+          ok = __all_sync(0xffffffffu, mbar_wait(&sh->tfull[buf], use & 1, &sh->abort_flag,
+                                                 g.res, 25, g.wait_ns));
+          if (!ok) break;
+          tc_fence_after();
+          uint32_t v[CPT];
+#pragma unroll
+          for (int i = 0; i < CPT / 8; ++i)
+            tmem_ld8(t_lane + (uint32_t)(buf * NT + i * 8), v + i * 8);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh->tempty[buf]);
+          const float w = __half2float(dw[j * TILE_M + m]);
+          const float* dxj = dx + j * NT + half * CPT;
+#pragma unroll
+          for (int i = 0; i < CPT; ++i)
+            acc[i] = fmaf((float)(int)v[i], __fmul_rn(w, dxj[i]), acc[i]);
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->empty[s]);
+      }
+      if (!ok) break;
+      const int row = rt * TILE_M + m;
+      if (row < g.rows) {
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+          const int n = tt * NT + half * CPT + i;
+          if (n < g.n_tok) g.out[(size_t)n * g.rows + row] = acc[i];
+        }
+      }
+    }
+  }
+
+  // After an abort: wait (bounded) until the producer has stopped issuing,
+  // then for the last copy issued to each stage.
+  if (*(volatile int*)&sh->abort_flag && threadIdx.x == 0) {
+    const uint64_t t_start = gtime();
+    while (!*(volatile int*)&sh->producer_done && gtime() - t_start < 100000000ull) {
+    }
+    const int issued = *(volatile int*)&sh->issued;
+    for (int s2 = 0; s2 < ns && s2 < issued; ++s2) {
+      const int t = s2 + ((issued - 1 - s2) / ns) * ns;
+      int dummy = 0;
+      mbar_wait(&sh->full[s2], (t / ns) & 1, &dummy, g.res, 26, 100000000ull);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, TCOLS);
+  }
+}
+
+// QuantizeQ8_0Into (q8_0.go:22-79) of n_tok rows of x [n_tok][cols] into the
+// activation chunks of the batched product: one warp per (token, 32-column
+// block), one value per lane; tokens n_tok..n_pad-1 and the columns past
+// cols up to the chunk boundary are written as zero blocks.  Bit-identical
+// to the reference's quantization of each row.
+__global__ void k_gemm_quantize(const float* x, int n_tok, int cols, int nt, int nk,
+                                int n_pad, uint8_t* act) {
+  using namespace gemm;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  const int nbk = nk * BPC;
+  if (gw >= n_pad * nbk) return;
+  const int n = gw / nbk, bk = gw % nbk;
+  const int k = bk * QBLK + lane;
+  const bool live = n < n_tok && bk * QBLK < cols;
+  const float v = live ? x[(size_t)n * cols + k] : 0.0f;
+  const float mx = warp_max(fabsf(v));
+  float scale = __fdiv_rn(mx, 127.0f);
+  if (scale == 0.0f) scale = 1e-8f;
+  const float inv = __fdiv_rn(1.0f, scale);
+  const int8_t q = live ? quant_one(v, inv) : (int8_t)0;
+  const int ti = n / nt, nn = n % nt, c = bk / BPC, j = bk % BPC;
+  uint8_t* ch = act + ((size_t)ti * nk + c) * b_chunk(nt);
+  ch[q_offset(nt, nn, j * QBLK + lane)] = (uint8_t)q;
+  if (lane == 0) reinterpret_cast<float*>(ch + b_q_bytes(nt))[j * nt + nn] = live ? scale : 0.0f;
+}

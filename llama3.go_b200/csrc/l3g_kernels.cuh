@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "l3g_gemm_layout.h"
+
 namespace l3g {
 
 constexpr int NW = 8;                   // consumer warps
@@ -276,6 +278,8 @@ __device__ __forceinline__ void quant_quad(float4 u, bool live, int blk, int sub
 #include "l3g_matvec.cuh"
 
 #include "l3g_attention.cuh"
+
+#include "l3g_gemm.cuh"
 
 // ---------------------------------------------------------------------------
 // Tensor-parallel reduction, the receiving half of the exchange (the pushing

@@ -2196,6 +2196,203 @@ extern "C" int l3g_quantize_q8_0(const float* x, int32_t n, float* d, int8_t* qs
 }
 
 // ---------------------------------------------------------------------------
+// batched Q8_0 product on the tensor cores (tcgen05 kind::i8)
+// ---------------------------------------------------------------------------
+struct l3g_gemm_matrix {
+  uint8_t* data = nullptr;  // weight chunks, gemm::A_CHUNK bytes each
+  int rows = 0, cols = 0, nk = 0, n_rt = 0;
+  size_t bytes = 0;
+  int device = 0, nsm = 1;
+  Result* d_res = nullptr;  // device error word of the kernel's bounded waits
+};
+
+// Kernel attributes of the batched product, once per device (kept apart from
+// the decode kernels' set-up).
+static int gemm_setup() {
+  static int rcs[64];
+  static std::once_flag onces[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return l3g_fail(L3G_E_CUDA, "gemm set-up: no current device");
+  int& rc = rcs[dev];
+  std::call_once(onces[dev], [&rc] {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_q8<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemm::smem_bytes(16));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_gemm_q8<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               gemm::smem_bytes(32));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_gemm_q8<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               gemm::smem_bytes(64));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_gemm_q8<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               gemm::smem_bytes(128));
+    rc = e == cudaSuccess ? L3G_OK
+                          : l3g_fail(L3G_E_CUDA, "gemm kernel attributes: %s", cudaGetErrorString(e));
+  });
+  return rc ? l3g_fail(L3G_E_CUDA, "gemm kernel set-up failed on device %d", dev) : L3G_OK;
+}
+
+extern "C" int l3g_gemm_matrix_bytes(int32_t rows, int32_t cols, uint64_t* bytes) {
+  if (!bytes) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (rows <= 0 || cols <= 0 || cols % 32)
+    return l3g_fail(L3G_E_INVALID, "gemm: %d x %d is not a Q8_0 matrix (cols multiple of 32)",
+                    rows, cols);
+  *bytes = (uint64_t)gemm::row_tiles(rows) * gemm::chunks(cols) * gemm::A_CHUNK;
+  return L3G_OK;
+}
+
+// Host-side repack of GGUF Q8_0 rows (34-byte blocks: fp16 d, 32 int8) into
+// weight chunks; values unchanged, padding rows and blocks zero.
+extern "C" int l3g_gemm_repack(const void* q8, int32_t rows, int32_t cols, void* dst,
+                               uint64_t dst_bytes) {
+  if (!q8 || !dst) return l3g_fail(L3G_E_INVALID, "null argument");
+  uint64_t need = 0;
+  if (int rc = l3g_gemm_matrix_bytes(rows, cols, &need)) return rc;
+  if (dst_bytes < need)
+    return l3g_fail(L3G_E_INVALID, "gemm repack needs %llu bytes, got %llu",
+                    (unsigned long long)need, (unsigned long long)dst_bytes);
+  using namespace gemm;
+  const uint8_t* src = static_cast<const uint8_t*>(q8);
+  uint8_t* out = static_cast<uint8_t*>(dst);
+  std::memset(out, 0, need);
+  const size_t row_bytes = (size_t)cols / QBLK * 34;
+  const int nk = chunks(cols), nrt = row_tiles(rows), nblk = cols / QBLK;
+  for (int rt = 0; rt < nrt; ++rt)
+    for (int c = 0; c < nk; ++c) {
+      uint8_t* ch = out + ((size_t)rt * nk + c) * A_CHUNK;
+      for (int m = 0; m < TILE_M; ++m) {
+        const int row = rt * TILE_M + m;
+        if (row >= rows) break;
+        for (int j = 0; j < BPC; ++j) {
+          const int b = c * BPC + j;
+          if (b >= nblk) break;
+          const uint8_t* blk = src + (size_t)row * row_bytes + (size_t)b * 34;
+          std::memcpy(ch + A_Q_BYTES + (j * TILE_M + m) * 2, blk, 2);
+          std::memcpy(ch + q_offset(TILE_M, m, j * QBLK), blk + 2, 16);
+          std::memcpy(ch + q_offset(TILE_M, m, j * QBLK + 16), blk + 18, 16);
+        }
+      }
+    }
+  return L3G_OK;
+}
+
+extern "C" void l3g_gemm_matrix_free(l3g_gemm_matrix* w) {
+  if (!w) return;
+  cudaSetDevice(w->device);
+  if (w->data) cudaFree(w->data);
+  if (w->d_res) cudaFree(w->d_res);
+  delete w;
+}
+
+extern "C" int l3g_gemm_matrix_upload(const void* q8, int32_t rows, int32_t cols, int32_t device,
+                                      l3g_gemm_matrix** out) {
+  if (!q8 || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  *out = nullptr;
+  uint64_t bytes = 0;
+  if (int rc = l3g_gemm_matrix_bytes(rows, cols, &bytes)) return rc;
+  int dev = device;
+  if (dev < 0) CUDA_TRY(cudaGetDevice(&dev));
+  CUDA_TRY(cudaSetDevice(dev));
+  if (int rc = gemm_setup()) return rc;
+  std::vector<uint8_t> host(bytes);
+  if (int rc = l3g_gemm_repack(q8, rows, cols, host.data(), bytes)) return rc;
+  auto* w = new l3g_gemm_matrix();
+  w->rows = rows;
+  w->cols = cols;
+  w->nk = gemm::chunks(cols);
+  w->n_rt = gemm::row_tiles(rows);
+  w->bytes = bytes;
+  w->device = dev;
+  w->nsm = sm_count(dev);
+  cudaError_t e = cudaMalloc(&w->data, bytes);
+  if (e == cudaSuccess) e = cudaMemcpy(w->data, host.data(), bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&w->d_res, sizeof(Result));
+  if (e == cudaSuccess) e = cudaMemset(w->d_res, 0, sizeof(Result));
+  if (e != cudaSuccess) {
+    l3g_gemm_matrix_free(w);
+    return l3g_fail(L3G_E_CUDA, "gemm matrix upload: %s", cudaGetErrorString(e));
+  }
+  *out = w;
+  return L3G_OK;
+}
+
+extern "C" int l3g_gemm_act_bytes(int32_t n_tok, int32_t cols, uint64_t* bytes) {
+  if (!bytes) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (n_tok <= 0 || cols <= 0 || cols % 32)
+    return l3g_fail(L3G_E_INVALID, "gemm activations: n_tok=%d cols=%d", n_tok, cols);
+  const int nt = gemm::token_tile(n_tok);
+  *bytes = (uint64_t)((n_tok + nt - 1) / nt) * gemm::chunks(cols) * gemm::b_chunk(nt);
+  return L3G_OK;
+}
+
+extern "C" int l3g_gemm_quantize(const float* x, int32_t n_tok, int32_t cols, void* act,
+                                 void* stream) {
+  if (!x || !act) return l3g_fail(L3G_E_INVALID, "null argument");
+  uint64_t bytes = 0;
+  if (int rc = l3g_gemm_act_bytes(n_tok, cols, &bytes)) return rc;
+  if (((uintptr_t)x & 3) || ((uintptr_t)act & 15))
+    return l3g_fail(L3G_E_INVALID, "x must be 4-byte aligned, act 16-byte");
+  const int nt = gemm::token_tile(n_tok);
+  const int n_pad = (n_tok + nt - 1) / nt * nt;
+  const int nk = gemm::chunks(cols);
+  const long long warps = (long long)n_pad * nk * gemm::BPC;
+  const int threads = 256;
+  const long long blocks = (warps * 32 + threads - 1) / threads;
+  if (blocks > INT_MAX) return l3g_fail(L3G_E_INVALID, "gemm activations too large");
+  k_gemm_quantize<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(
+      x, n_tok, cols, nt, nk, n_pad, static_cast<uint8_t*>(act));
+  CUDA_TRY(cudaGetLastError());
+  return L3G_OK;
+}
+
+extern "C" int l3g_gemm_q8(const l3g_gemm_matrix* w, const void* act, int32_t n_tok, float* out,
+                           void* stream) {
+  if (!w || !act || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (n_tok <= 0) return l3g_fail(L3G_E_INVALID, "n_tok=%d", n_tok);
+  if (((uintptr_t)act & 15) || ((uintptr_t)out & 3))
+    return l3g_fail(L3G_E_INVALID, "act must be 16-byte aligned, out 4-byte");
+  CUDA_TRY(cudaSetDevice(w->device));
+  if (int rc = gemm_setup()) return rc;
+  const int nt = gemm::token_tile(n_tok);
+  GemmArgs g{};
+  g.a = w->data;
+  g.b = static_cast<const uint8_t*>(act);
+  g.out = out;
+  g.rows = w->rows;
+  g.n_tok = n_tok;
+  g.nk = w->nk;
+  g.n_rt = w->n_rt;
+  g.n_tt = (n_tok + nt - 1) / nt;
+  g.nstages = gemm::stages(nt);
+  g.res = w->d_res;
+  g.wait_ns = WAIT_TIMEOUT_NS;
+  const long long tiles = (long long)g.n_rt * g.n_tt;
+  const int grid = (int)std::min<long long>(w->nsm, tiles);
+  const cudaStream_t st = (cudaStream_t)stream;
+  switch (nt) {
+    case 16: k_gemm_q8<16><<<grid, GEMM_THREADS, gemm::smem_bytes(16), st>>>(g); break;
+    case 32: k_gemm_q8<32><<<grid, GEMM_THREADS, gemm::smem_bytes(32), st>>>(g); break;
+    case 64: k_gemm_q8<64><<<grid, GEMM_THREADS, gemm::smem_bytes(64), st>>>(g); break;
+    default: k_gemm_q8<128><<<grid, GEMM_THREADS, gemm::smem_bytes(128), st>>>(g); break;
+  }
+  CUDA_TRY(cudaGetLastError());
+  return L3G_OK;
+}
+
+extern "C" int l3g_gemm_status(const l3g_gemm_matrix* w, int32_t* err, int32_t* where) {
+  if (!w || !err || !where) return l3g_fail(L3G_E_INVALID, "null argument");
+  CUDA_TRY(cudaSetDevice(w->device));
+  CUDA_TRY(cudaDeviceSynchronize());
+  Result h{};
+  CUDA_TRY(cudaMemcpy(&h, w->d_res, sizeof h, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemset(w->d_res, 0, sizeof(Result)));
+  *err = h.err;
+  *where = h.where;
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
 // failure-detection self test
 // ---------------------------------------------------------------------------
 extern "C" int l3g_selftest_bounded_wait(int32_t device, int32_t timeout_us, int32_t* status) {

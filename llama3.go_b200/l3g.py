@@ -131,6 +131,14 @@ def lib():
         "l3g_matrix_free": (None, [_P]),
         "l3g_matrix_device_bytes": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
         "l3g_quantize_q8_0": (C.c_int, [_P, C.c_int32, _P, _P, _P]),
+        "l3g_gemm_matrix_bytes": (C.c_int, [C.c_int32, C.c_int32, C.POINTER(C.c_uint64)]),
+        "l3g_gemm_repack": (C.c_int, [_P, C.c_int32, C.c_int32, _P, C.c_uint64]),
+        "l3g_gemm_matrix_upload": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_P)]),
+        "l3g_gemm_matrix_free": (None, [_P]),
+        "l3g_gemm_act_bytes": (C.c_int, [C.c_int32, C.c_int32, C.POINTER(C.c_uint64)]),
+        "l3g_gemm_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, _P, _P]),
+        "l3g_gemm_q8": (C.c_int, [_P, _P, C.c_int32, _P, _P]),
+        "l3g_gemm_status": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
         "l3g_state_read_kv": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32,
                                         C.POINTER(C.c_float), C.POINTER(C.c_float)]),
         "l3g_workspace_read": (C.c_int, [_P, C.c_int32, C.POINTER(C.c_float), C.c_int32]),
@@ -523,6 +531,74 @@ class Matrix:
     def Close(self):
         if self._h:
             lib().l3g_matrix_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.Close()
+        except Exception:
+            pass
+
+
+def gemm_matrix_bytes(rows: int, cols: int) -> int:
+    v = C.c_uint64()
+    _check(lib().l3g_gemm_matrix_bytes(rows, cols, C.byref(v)))
+    return v.value
+
+
+def gemm_repack(q8_rows: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Host-side repack of GGUF Q8_0 rows into the batched product's weight
+    chunks (no device needed)."""
+    q8_rows = np.ascontiguousarray(q8_rows, dtype=np.uint8)
+    if q8_rows.size != rows * cols // 32 * 34:
+        raise L3GError(L3G_E_INVALID, "matrix bytes do not match rows x cols")
+    out = np.empty(gemm_matrix_bytes(rows, cols), np.uint8)
+    _check(lib().l3g_gemm_repack(q8_rows.ctypes.data, rows, cols, out.ctypes.data, out.size))
+    return out
+
+
+def gemm_act_bytes(n_tok: int, cols: int) -> int:
+    v = C.c_uint64()
+    _check(lib().l3g_gemm_act_bytes(n_tok, cols, C.byref(v)))
+    return v.value
+
+
+def gemm_quantize(x_ptr: int, n_tok: int, cols: int, act_ptr: int, stream: int = 0):
+    """QuantizeQ8_0Into of n_tok device rows of cols floats into the batched
+    product's activation chunks (act: gemm_act_bytes(n_tok, cols) bytes)."""
+    _check(lib().l3g_gemm_quantize(x_ptr, n_tok, cols, act_ptr, stream or None))
+
+
+class GemmMatrix:
+    """A Q8_0 matrix resident on the device for the batched product (n_tok
+    matvec_q8_c products in one pass over the weights, on the tensor cores)."""
+
+    def __init__(self, q8_rows: np.ndarray, rows: int, cols: int, device: int = -1):
+        q8_rows = np.ascontiguousarray(q8_rows, dtype=np.uint8)
+        if q8_rows.size != rows * cols // 32 * 34:
+            raise L3GError(L3G_E_INVALID, "matrix bytes do not match rows x cols")
+        h = C.c_void_p()
+        _check(lib().l3g_gemm_matrix_upload(q8_rows.ctypes.data, rows, cols, device, C.byref(h)))
+        self._h = h
+        self.rows, self.cols = rows, cols
+
+    def quantize(self, x_ptr: int, n_tok: int, act_ptr: int, stream: int = 0):
+        """gemm_quantize with this matrix's column count."""
+        gemm_quantize(x_ptr, n_tok, self.cols, act_ptr, stream)
+
+    def gemm(self, act_ptr: int, n_tok: int, out_ptr: int, stream: int = 0):
+        """out[n][r] for n < n_tok, r < rows (device pointers)."""
+        _check(lib().l3g_gemm_q8(self._h, act_ptr, n_tok, out_ptr, stream or None))
+
+    def status(self):
+        """(err, where) of the kernel's bounded waits since the last call."""
+        e, w = C.c_int32(), C.c_int32()
+        _check(lib().l3g_gemm_status(self._h, C.byref(e), C.byref(w)))
+        return e.value, w.value
+
+    def Close(self):
+        if self._h:
+            lib().l3g_gemm_matrix_free(self._h)
             self._h = C.c_void_p()
 
     def __del__(self):
