@@ -192,6 +192,17 @@ int l3g_forward_argmax(l3g_model *m, l3g_state *s, l3g_workspace *ws,
  * each token in turn. */
 int l3g_prefill(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                 const int32_t *tokens, int32_t n);
+/* The same ingest as l3g_prefill (KV entries of positions pos..pos+n-1,
+ * position advanced by n, no logits), computed up to 512 tokens at a time:
+ * every projection as one batched Q8_0 product on the tensor cores
+ * (l3g_gemm_q8) over the tokens of the pass, causal attention of the pass's
+ * positions over the cache, and the last layer cut after its K/V append
+ * (its attention and FFN outputs feed only the logits).  The reference
+ * ingests one token per ForwardIntoWorkspace (main.go:276-286); per token the
+ * arithmetic is the same (quantized activations, int32 block sums), with
+ * fp32 sums in another order. */
+int l3g_prefill_batched(l3g_model *m, l3g_state *s, l3g_workspace *ws,
+                        const int32_t *tokens, int32_t n);
 /* The decode loop of cmd/go-llama-chat/main.go:141-165 with a greedy
  * sampler: n steps, each fed the previous step's argmax, replayed back to
  * back on the device with no host round trip in between.  out_tokens[i]

@@ -281,6 +281,8 @@ __device__ __forceinline__ void quant_quad(float4 u, bool live, int blk, int sub
 
 #include "l3g_gemm.cuh"
 
+#include "l3g_prefill.cuh"
+
 // ---------------------------------------------------------------------------
 // Tensor-parallel reduction, the receiving half of the exchange (the pushing
 // half is the EPI_PUSH epilogue of the Wo / down matvecs): thread i waits for

@@ -343,10 +343,25 @@ static int upload_tiled(DevMat& out, const RowSrc* segs, int nseg,
 // ---------------------------------------------------------------------------
 // model
 // ---------------------------------------------------------------------------
+// A matrix in the batched product's weight chunks (l3g_gemm_layout.h).
+struct GemmMat {
+  uint8_t* data = nullptr;
+  int rows = 0, cols = 0, nk = 0, n_rt = 0;
+  size_t bytes = 0;
+};
+
+static void free_gemm(GemmMat& g) {
+  if (g.data) cudaFree(g.data);
+  g = GemmMat{};
+}
+
 struct LayerW {
   DevMat qkv, wo, upgate, down;
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
+  // the same matrices as weight chunks of the batched product (built on
+  // the first batched prefill)
+  GemmMat gqkv, gwo, gupgate, gdown;
 };
 
 struct l3g_model {
@@ -365,6 +380,8 @@ struct l3g_model {
   uint8_t* emb = nullptr;  // raw GGUF Q8_0 token_embd (all rows)
   ncclComm_t comm = nullptr;
   size_t dev_bytes = 0;
+  std::mutex gemm_mu;       // guards the lazy build of the layers' GemmMat
+  bool gemm_ready = false;
 };
 
 static const l3g_tensor* find_tensor(const l3g_tensor* ts, int n, const char* name) {
@@ -432,6 +449,10 @@ extern "C" void l3g_model_free(l3g_model* m) {
     free_mat(L.wo);
     free_mat(L.upgate);
     free_mat(L.down);
+    free_gemm(L.gqkv);
+    free_gemm(L.gwo);
+    free_gemm(L.gupgate);
+    free_gemm(L.gdown);
     if (L.attn_norm) cudaFree(L.attn_norm);
     if (L.ffn_norm) cudaFree(L.ffn_norm);
   }
@@ -938,6 +959,16 @@ struct l3g_workspace {
   std::vector<int> trace_kinds_graph;      // ... as captured in the V_TRACE graph
   std::vector<StepGraph> graphs;
   bool logits_valid = false;
+  // batched prefill buffers for up to pf_cap tokens (allocated on first use)
+  int pf_cap = 0;
+  int* pf_ids = nullptr;
+  float* pf_x = nullptr;    // [pf_cap][n_emb] residual stream
+  float* pf_y = nullptr;    // [pf_cap][n_emb] Wo / down output
+  float* pf_qkv = nullptr;  // [pf_cap][qkv rows]
+  float* pf_q = nullptr;    // [pf_cap][local q heads * hd] roped queries
+  float* pf_att = nullptr;  // [pf_cap][local q heads * hd] attention output
+  float* pf_ug = nullptr;   // [pf_cap][2 * local n_ff] interleaved up/gate
+  uint8_t* pf_act = nullptr;  // activation chunks of the batched product
 };
 
 static void ws_release(l3g_workspace* ws) {
@@ -956,6 +987,10 @@ static void ws_release(l3g_workspace* ws) {
                    ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
                    ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens, ws->d_trace, ws->d_samp};
   for (void* p : dptrs)
+    if (p) cudaFree(p);
+  void* pf[] = {ws->pf_ids, ws->pf_x, ws->pf_y, ws->pf_qkv, ws->pf_q, ws->pf_att, ws->pf_ug,
+                ws->pf_act};
+  for (void* p : pf)
     if (p) cudaFree(p);
   void* hptrs[] = {ws->h_io, ws->h_res, ws->h_logits, ws->h_tk_ids, ws->h_tk_logits, ws->h_samp};
   for (void* p : hptrs)
@@ -2198,10 +2233,37 @@ extern "C" int l3g_quantize_q8_0(const float* x, int32_t n, float* d, int8_t* qs
 // ---------------------------------------------------------------------------
 // batched Q8_0 product on the tensor cores (tcgen05 kind::i8)
 // ---------------------------------------------------------------------------
+// One batched product out[n][r] (n < n_tok) on stream st: one CTA per SM at
+// most, tiles dealt round-robin.
+static cudaError_t launch_gemm(const GemmMat& w, const uint8_t* act, int n_tok, float* out,
+                               Result* res, unsigned long long wait_ns, int nsm,
+                               cudaStream_t st) {
+  const int nt = gemm::token_tile(n_tok);
+  GemmArgs g{};
+  g.a = w.data;
+  g.b = act;
+  g.out = out;
+  g.rows = w.rows;
+  g.n_tok = n_tok;
+  g.nk = w.nk;
+  g.n_rt = w.n_rt;
+  g.n_tt = (n_tok + nt - 1) / nt;
+  g.nstages = gemm::stages(nt);
+  g.res = res;
+  g.wait_ns = wait_ns;
+  const long long tiles = (long long)g.n_rt * g.n_tt;
+  const int grid = (int)std::max<long long>(1, std::min<long long>(nsm, tiles));
+  switch (nt) {
+    case 16: k_gemm_q8<16><<<grid, GEMM_THREADS, gemm::smem_bytes(16), st>>>(g); break;
+    case 32: k_gemm_q8<32><<<grid, GEMM_THREADS, gemm::smem_bytes(32), st>>>(g); break;
+    case 64: k_gemm_q8<64><<<grid, GEMM_THREADS, gemm::smem_bytes(64), st>>>(g); break;
+    default: k_gemm_q8<128><<<grid, GEMM_THREADS, gemm::smem_bytes(128), st>>>(g); break;
+  }
+  return cudaGetLastError();
+}
+
 struct l3g_gemm_matrix {
-  uint8_t* data = nullptr;  // weight chunks, gemm::A_CHUNK bytes each
-  int rows = 0, cols = 0, nk = 0, n_rt = 0;
-  size_t bytes = 0;
+  GemmMat w;                // weight chunks, gemm::A_CHUNK bytes each
   int device = 0, nsm = 1;
   Result* d_res = nullptr;  // device error word of the kernel's bounded waits
 };
@@ -2227,6 +2289,17 @@ static int gemm_setup() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k_gemm_q8<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                gemm::smem_bytes(128));
+#define SETPF(HD, KT)                                                                       \
+  if (e == cudaSuccess)                                                                    \
+  e = cudaFuncSetAttribute(k_pf_attention<HD, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                           pf_attention_smem(HD))
+    SETPF(32, float);
+    SETPF(64, float);
+    SETPF(128, float);
+    SETPF(32, __half);
+    SETPF(64, __half);
+    SETPF(128, __half);
+#undef SETPF
     rc = e == cudaSuccess ? L3G_OK
                           : l3g_fail(L3G_E_CUDA, "gemm kernel attributes: %s", cudaGetErrorString(e));
   });
@@ -2280,7 +2353,7 @@ extern "C" int l3g_gemm_repack(const void* q8, int32_t rows, int32_t cols, void*
 extern "C" void l3g_gemm_matrix_free(l3g_gemm_matrix* w) {
   if (!w) return;
   cudaSetDevice(w->device);
-  if (w->data) cudaFree(w->data);
+  free_gemm(w->w);
   if (w->d_res) cudaFree(w->d_res);
   delete w;
 }
@@ -2298,15 +2371,15 @@ extern "C" int l3g_gemm_matrix_upload(const void* q8, int32_t rows, int32_t cols
   std::vector<uint8_t> host(bytes);
   if (int rc = l3g_gemm_repack(q8, rows, cols, host.data(), bytes)) return rc;
   auto* w = new l3g_gemm_matrix();
-  w->rows = rows;
-  w->cols = cols;
-  w->nk = gemm::chunks(cols);
-  w->n_rt = gemm::row_tiles(rows);
-  w->bytes = bytes;
+  w->w.rows = rows;
+  w->w.cols = cols;
+  w->w.nk = gemm::chunks(cols);
+  w->w.n_rt = gemm::row_tiles(rows);
+  w->w.bytes = bytes;
   w->device = dev;
   w->nsm = sm_count(dev);
-  cudaError_t e = cudaMalloc(&w->data, bytes);
-  if (e == cudaSuccess) e = cudaMemcpy(w->data, host.data(), bytes, cudaMemcpyHostToDevice);
+  cudaError_t e = cudaMalloc(&w->w.data, bytes);
+  if (e == cudaSuccess) e = cudaMemcpy(w->w.data, host.data(), bytes, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMalloc(&w->d_res, sizeof(Result));
   if (e == cudaSuccess) e = cudaMemset(w->d_res, 0, sizeof(Result));
   if (e != cudaSuccess) {
@@ -2354,29 +2427,8 @@ extern "C" int l3g_gemm_q8(const l3g_gemm_matrix* w, const void* act, int32_t n_
     return l3g_fail(L3G_E_INVALID, "act must be 16-byte aligned, out 4-byte");
   CUDA_TRY(cudaSetDevice(w->device));
   if (int rc = gemm_setup()) return rc;
-  const int nt = gemm::token_tile(n_tok);
-  GemmArgs g{};
-  g.a = w->data;
-  g.b = static_cast<const uint8_t*>(act);
-  g.out = out;
-  g.rows = w->rows;
-  g.n_tok = n_tok;
-  g.nk = w->nk;
-  g.n_rt = w->n_rt;
-  g.n_tt = (n_tok + nt - 1) / nt;
-  g.nstages = gemm::stages(nt);
-  g.res = w->d_res;
-  g.wait_ns = WAIT_TIMEOUT_NS;
-  const long long tiles = (long long)g.n_rt * g.n_tt;
-  const int grid = (int)std::min<long long>(w->nsm, tiles);
-  const cudaStream_t st = (cudaStream_t)stream;
-  switch (nt) {
-    case 16: k_gemm_q8<16><<<grid, GEMM_THREADS, gemm::smem_bytes(16), st>>>(g); break;
-    case 32: k_gemm_q8<32><<<grid, GEMM_THREADS, gemm::smem_bytes(32), st>>>(g); break;
-    case 64: k_gemm_q8<64><<<grid, GEMM_THREADS, gemm::smem_bytes(64), st>>>(g); break;
-    default: k_gemm_q8<128><<<grid, GEMM_THREADS, gemm::smem_bytes(128), st>>>(g); break;
-  }
-  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(launch_gemm(w->w, static_cast<const uint8_t*>(act), n_tok, out, w->d_res,
+                       WAIT_TIMEOUT_NS, w->nsm, (cudaStream_t)stream));
   return L3G_OK;
 }
 
@@ -2389,6 +2441,196 @@ extern "C" int l3g_gemm_status(const l3g_gemm_matrix* w, int32_t* err, int32_t* 
   CUDA_TRY(cudaMemset(w->d_res, 0, sizeof(Result)));
   *err = h.err;
   *where = h.where;
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// batched prefill
+// ---------------------------------------------------------------------------
+// Tokens per pass over the weights (a pass streams every layer's matrices
+// once); the last pass takes the remainder.
+constexpr int PF_CHUNK = 512;
+
+static int gemm_from_tiles(const DevMat& src, GemmMat& dst, size_t* dev_bytes) {
+  dst.rows = src.t.rows;
+  dst.cols = src.t.cols;
+  dst.nk = gemm::chunks(dst.cols);
+  dst.n_rt = gemm::row_tiles(dst.rows);
+  dst.bytes = (size_t)dst.n_rt * dst.nk * gemm::A_CHUNK;
+  CUDA_TRY(cudaMalloc(&dst.data, dst.bytes));
+  CUDA_TRY(cudaMemset(dst.data, 0, dst.bytes));
+  k_gemm_from_tiles<<<2048, 256>>>(src.t, dst.data);
+  CUDA_TRY(cudaGetLastError());
+  *dev_bytes += dst.bytes;
+  return L3G_OK;
+}
+
+// The layers' matrices as weight chunks of the batched product, built once
+// per model from the resident tiles (same shard, same fused row orders).
+static int ensure_gemm_weights(l3g_model* m) {
+  std::lock_guard<std::mutex> lk(m->gemm_mu);
+  if (m->gemm_ready) return L3G_OK;
+  for (auto& L : m->layers) {
+    int rc = gemm_from_tiles(L.qkv, L.gqkv, &m->dev_bytes);
+    if (!rc) rc = gemm_from_tiles(L.wo, L.gwo, &m->dev_bytes);
+    if (!rc) rc = gemm_from_tiles(L.upgate, L.gupgate, &m->dev_bytes);
+    if (!rc) rc = gemm_from_tiles(L.down, L.gdown, &m->dev_bytes);
+    if (rc) return rc;
+  }
+  CUDA_TRY(cudaDeviceSynchronize());
+  m->gemm_ready = true;
+  return L3G_OK;
+}
+
+static int ensure_prefill_buffers(l3g_workspace* ws) {
+  if (ws->pf_cap) return L3G_OK;
+  const l3g_model* m = ws->m;
+  const int cap = PF_CHUNK;
+  const int ne = m->hp.n_emb, nq = m->hq_l * m->hd, nkv = m->hkv_l * m->hd;
+  const int max_cols = std::max(std::max(ne, nq), m->ff_l);
+  uint64_t act_bytes = 0;
+  if (int rc = l3g_gemm_act_bytes(cap, max_cols, &act_bytes)) return rc;
+  cudaError_t e = cudaMalloc(&ws->pf_ids, (size_t)cap * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->pf_x, (size_t)cap * ne * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->pf_y, (size_t)cap * ne * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->pf_qkv, (size_t)cap * (nq + 2 * nkv) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->pf_q, (size_t)cap * nq * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->pf_att, (size_t)cap * nq * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->pf_ug, (size_t)cap * 2 * m->ff_l * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->pf_act, act_bytes);
+  // padding tokens and columns of the activation chunks are never written
+  if (e == cudaSuccess) e = cudaMemset(ws->pf_act, 0, act_bytes);
+  if (e != cudaSuccess)
+    return l3g_fail(L3G_E_CUDA, "prefill buffers: %s", cudaGetErrorString(e));
+  ws->pf_cap = cap;
+  return L3G_OK;
+}
+
+template <int HD>
+static cudaError_t launch_pf_attention(const l3g_model* m, const l3g_workspace* ws,
+                                       const void* kv, int P, int pos0, int ctx,
+                                       cudaStream_t st) {
+  const int bq = std::max(1, 64 / m->group);
+  const dim3 grid((P + bq - 1) / bq, m->hkv_l);
+  const float scale = (float)(1.0 / sqrt((double)m->hd));
+  if (m->kv_f16)
+    k_pf_attention<HD, __half><<<grid, 256, pf_attention_smem(HD), st>>>(
+        ws->pf_q, kv, ws->pf_att, P, pos0, ctx, m->group, bq, m->hq_l, scale);
+  else
+    k_pf_attention<HD, float><<<grid, 256, pf_attention_smem(HD), st>>>(
+        ws->pf_q, kv, ws->pf_att, P, pos0, ctx, m->group, bq, m->hq_l, scale);
+  return cudaGetLastError();
+}
+
+// One pass of P <= pf_cap tokens at positions pos0..pos0+P-1 over every
+// layer.  The last layer stops after its K/V append: its attention and FFN
+// outputs only feed the logits, which prefill does not compute (infer.go:250).
+static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, int P,
+                                int pos0) {
+  const l3g_hparams& hp = m->hp;
+  const cudaStream_t st = ws->stream;
+  const int ne = hp.n_emb, hd = m->hd;
+  const int nq = m->hq_l * hd, nkv = m->hkv_l * hd;
+  const size_t es = m->kv_f16 ? 2 : 4;
+  const unsigned long long wait_ns = WAIT_TIMEOUT_NS;
+  const int nt = gemm::token_tile(P);
+  uint8_t* act = ws->pf_act;
+  k_pf_embed<<<dim3((ne + 255) / 256, P), 256, 0, st>>>(m->emb, hp.vocab_size, ne, ws->pf_ids,
+                                                        ws->pf_x, ws->d_res);
+  CUDA_TRY(cudaGetLastError());
+  for (int l = 0; l < hp.n_layers; ++l) {
+    const LayerW& L = m->layers[l];
+    uint8_t* kv = static_cast<uint8_t*>(s->kv) + (size_t)l * s->layer_elems * es;
+    // residual (from layer l-1's down) -> RMSNorm -> act-quant, infer.go:67-73
+    k_pf_rms_quant<<<P, PF_THREADS, 0, st>>>(ws->pf_x, l ? ws->pf_y : nullptr, L.attn_norm,
+                                            hp.rms_eps, ne, nt, gemm::chunks(ne), act);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_gemm(L.gqkv, act, P, ws->pf_qkv, ws->d_res, wait_ns, m->nsm, st));
+    {  // RoPE + KV append, infer.go:76-127
+      const long long pairs = (long long)P * ((nq + 2 * nkv) / 2);
+      k_pf_qkv_rope<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
+          ws->pf_qkv, P, pos0, nq, nkv, hd, m->rope_half, s->rope_cos, s->rope_sin, ws->pf_q, kv,
+          s->ctx, m->kv_f16);
+      CUDA_TRY(cudaGetLastError());
+    }
+    if (l == hp.n_layers - 1) break;
+    // attention, infer.go:130-175
+    switch (hd) {
+      case 32: CUDA_TRY(launch_pf_attention<32>(m, ws, kv, P, pos0, s->ctx, st)); break;
+      case 64: CUDA_TRY(launch_pf_attention<64>(m, ws, kv, P, pos0, s->ctx, st)); break;
+      case 128: CUDA_TRY(launch_pf_attention<128>(m, ws, kv, P, pos0, s->ctx, st)); break;
+      default: return l3g_fail(L3G_E_INVALID, "batched prefill: head_dim %d", hd);
+    }
+    // act-quant of the attention output -> Wo, infer.go:178-187
+    {
+      const long long warps = (long long)((P + nt - 1) / nt * nt) * gemm::chunks(nq) * gemm::BPC;
+      k_gemm_quantize<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+          ws->pf_att, P, nq, nt, gemm::chunks(nq), (P + nt - 1) / nt * nt, act);
+      CUDA_TRY(cudaGetLastError());
+    }
+    CUDA_TRY(launch_gemm(L.gwo, act, P, ws->pf_y, ws->d_res, wait_ns, m->nsm, st));
+    if (m->world > 1)
+      NCCL_TRY(nccl()->AllReduce(ws->pf_y, ws->pf_y, (size_t)P * ne, ncclFloat, ncclSum, m->comm,
+                                 st));
+    // residual -> RMSNorm -> act-quant -> up/gate -> SwiGLU -> act-quant,
+    // infer.go:189-234
+    k_pf_rms_quant<<<P, PF_THREADS, 0, st>>>(ws->pf_x, ws->pf_y, L.ffn_norm, hp.rms_eps, ne, nt,
+                                            gemm::chunks(ne), act);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_gemm(L.gupgate, act, P, ws->pf_ug, ws->d_res, wait_ns, m->nsm, st));
+    {
+      const long long warps = (long long)P * (m->ff_l / 32);
+      k_pf_swiglu_quant<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+          ws->pf_ug, P, m->ff_l, nt, gemm::chunks(m->ff_l), act);
+      CUDA_TRY(cudaGetLastError());
+    }
+    // down, infer.go:235-246 (its residual add opens the next layer)
+    CUDA_TRY(launch_gemm(L.gdown, act, P, ws->pf_y, ws->d_res, wait_ns, m->nsm, st));
+    if (m->world > 1)
+      NCCL_TRY(nccl()->AllReduce(ws->pf_y, ws->pf_y, (size_t)P * ne, ncclFloat, ncclSum, m->comm,
+                                 st));
+  }
+  return L3G_OK;
+}
+
+extern "C" int l3g_prefill_batched(l3g_model* m, l3g_state* s, l3g_workspace* ws,
+                                   const int32_t* tokens, int32_t n) {
+  if (!m || !s) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (!ws) return l3g_fail(L3G_E_INVALID, "workspace is nil");
+  if (n > 0 && !tokens) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (s->m != m || ws->m != m)
+    return l3g_fail(L3G_E_INVALID, "state or workspace belongs to another model");
+  if (n <= 0) return L3G_OK;
+  if (ws->ctx < s->ctx)
+    return l3g_fail(L3G_E_INVALID, "workspace ctxLen=%d < state ctxLen=%d", ws->ctx, s->ctx);
+  if ((long long)s->pos + n > s->ctx)
+    return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= m->hp.vocab_size)
+      return l3g_fail(L3G_E_TOKEN, "token out of range: %d", tokens[i]);
+  if (m->hp.n_emb > PF_THREADS * 4 * PF_VK || m->hp.n_emb % 32)
+    return l3g_fail(L3G_E_INVALID, "batched prefill: n_emb %d", m->hp.n_emb);
+  CUDA_TRY(cudaSetDevice(m->device));
+  if (int rc = gemm_setup()) return rc;
+  if (int rc = ensure_gemm_weights(m)) return rc;
+  if (int rc = ensure_prefill_buffers(ws)) return rc;
+  ws->logits_valid = false;
+  for (int c0 = 0; c0 < n; c0 += ws->pf_cap) {
+    const int P = std::min(ws->pf_cap, n - c0);
+    CUDA_TRY(cudaMemcpyAsync(ws->pf_ids, tokens + c0, (size_t)P * 4, cudaMemcpyHostToDevice,
+                             ws->stream));
+    if (int rc = enqueue_prefill_pass(m, s, ws, P, s->pos)) return rc;
+    CUDA_TRY(cudaMemcpyAsync(ws->h_res, ws->d_res, sizeof(Result), cudaMemcpyDeviceToHost,
+                             ws->stream));
+    CUDA_TRY(cudaStreamSynchronize(ws->stream));
+    if (ws->h_res->err) {
+      const int code = ws->h_res->err, where = ws->h_res->where;
+      cudaMemset(ws->d_res, 0, sizeof(Result));
+      return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d (%s)", code, where,
+                      code == ERR_TIMEOUT ? "bounded wait ran out" : "bad input");
+    }
+    s->pos += P;
+  }
   return L3G_OK;
 }
 

@@ -110,6 +110,7 @@ def lib():
         "l3g_forward_argmax": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32),
                                          C.POINTER(C.c_float)]),
         "l3g_prefill": (C.c_int, [_P, _P, _P, C.POINTER(C.c_int32), C.c_int32]),
+        "l3g_prefill_batched": (C.c_int, [_P, _P, _P, C.POINTER(C.c_int32), C.c_int32]),
         "l3g_forward_sample": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_float, C.c_uint64,
                                          C.POINTER(C.c_int32)]),
         "l3g_decode_sample": (C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_float,
@@ -274,6 +275,13 @@ class Model:
         arr = np.ascontiguousarray(tokens, dtype=np.int32)
         _check(lib().l3g_prefill(self._h, s._h, _ws(ws), arr.ctypes.data_as(C.POINTER(C.c_int32)),
                                  arr.size))
+
+    def PrefillBatched(self, s: "State", tokens, ws: "Workspace") -> None:
+        """The same ingest, up to 512 tokens per pass through the batched
+        tensor-core product (l3g_prefill_batched)."""
+        arr = np.ascontiguousarray(tokens, dtype=np.int32)
+        _check(lib().l3g_prefill_batched(self._h, s._h, _ws(ws),
+                                         arr.ctypes.data_as(C.POINTER(C.c_int32)), arr.size))
 
     KERNEL_KINDS = ("embed", "qkv_rope_kv", "attention", "wo", "upgate_swiglu", "down", "logits_argmax",
                     "other", "act_quant")
