@@ -60,6 +60,7 @@ typedef struct l3g_state l3g_state;
 typedef struct l3g_workspace l3g_workspace;
 typedef struct l3g_matrix l3g_matrix;
 typedef struct l3g_gemm_matrix l3g_gemm_matrix;
+typedef struct l3g_batch l3g_batch;
 
 /* HyperParams, internal/llama/model.go:10-21.  llama3 RoPE frequency scaling,
  * absent from the reference (rope.go:15-37), is taken from an optional f32
@@ -335,6 +336,31 @@ int l3g_matvec_q8_argmax_static(const l3g_matrix *w, const float *x_scales,
  * ceil(n/32) floats, qs ceil(n/32)*32 bytes. */
 int l3g_quantize_q8_0(const float *x, int32_t n, float *d, int8_t *qs,
                       void *stream);
+
+/* ---- batched decode: many sessions, one step ----------------------------- */
+/* One decode step for n independent sessions of one model, each an
+ * l3g_state (its own KV cache, context length and position; no two entries
+ * the same state).  Per session the step is ForwardTopKIntoWorkspace
+ * (infer.go:269-511, with the exact exp of the full path, :130-175) followed
+ * by Sampler.SampleTopK (sampling.go:103-143): state i ingests tokens[i] at
+ * its position and advances by one, and next_tokens[i] receives a sample
+ * from its top_k largest logits (top_k <= 0: 40, at most 64; ties to the
+ * lower id) at temperature (<= 0: 0.8), drawn from Philox4x32-10 keyed by
+ * seeds[i] with the state's position before the step as the draw index
+ * (Go's math/rand stream is not reproduced).  logits_out (nullable, host
+ * [n][vocab]) receives the logits.  The projections run as batched Q8_0
+ * products over the n tokens on the tensor cores (l3g_gemm_q8); attention
+ * is per session over its own cache.  The reference serves one session
+ * (cmd/go-llama-chat/main.go:139-176); this has no counterpart there.
+ * Tensor parallel: every rank calls with its own states of the same
+ * sessions and the same tokens and seeds, and gets the same samples. */
+#define L3G_BATCH_MAX 256
+int l3g_batch_new(l3g_model *m, int32_t max_seqs, l3g_batch **out);
+void l3g_batch_free(l3g_batch *b);
+int l3g_batch_step(l3g_batch *b, l3g_state *const *states, int32_t n,
+                   const int32_t *tokens, int32_t top_k, float temperature,
+                   const uint64_t *seeds, int32_t *next_tokens,
+                   float *logits_out);
 
 /* ---- batched Q8_0 product on the tensor cores (tcgen05 kind::i8) --------- */
 /* n_tok independent Q8_0 matvecs over one weight matrix, as one GEMM:

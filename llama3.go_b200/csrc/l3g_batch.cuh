@@ -1,0 +1,282 @@
+// Batched decode kernels (included by l3g_kernels.cuh after l3g_prefill.cuh).
+//
+// One step advances n independent sequences (each an l3g_state: its own KV
+// cache, context length and position) by one token: per sequence exactly
+// ForwardTopKIntoWorkspace (internal/llama/infer.go:269-511, here with the
+// exact exp of the full path, :130-175) followed by Sampler.SampleTopK
+// (sampling.go:103-143).  The projections run as batched Q8_0 products over
+// the n tokens (k_gemm_q8) and the row-wise kernels of batched prefill; the
+// kernels here are the per-sequence parts: KV append at each sequence's
+// position, decode attention over each sequence's own cache, and top-K plus
+// sampling per sequence.
+#pragma once
+
+// Per-sequence inputs of a step (host-filled, copied once per step).
+struct SeqInfo {
+  void* kv;                // the sequence's KV cache, all layers
+  const float* rope_cos;   // its RoPE tables [ctx][rope_half]
+  const float* rope_sin;
+  long long layer_bytes;   // bytes of one layer of that cache
+  int ctx;                 // its context length
+  int pos;                 // position this step writes
+  int token;               // token this step ingests
+  int pad;
+  uint64_t seed;           // sampler seed
+  float temperature;       // sampler temperature (> 0)
+  int pad2;
+};
+static_assert(sizeof(SeqInfo) == 64, "SeqInfo layout");
+
+// x[b] = embedding row of seqs[b].token (infer.go:513-518).  grid (ceil(cols/256), n).
+__global__ void k_bd_embed(const uint8_t* emb, int vocab, int cols, const SeqInfo* seqs,
+                           float* X, Result* res) {
+  const int b = blockIdx.y;
+  const int token = seqs[b].token;
+  if (token < 0 || token >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) report(res, ERR_TOKEN, token);
+    return;
+  }
+  const uint8_t* row = emb + (size_t)token * (cols / 32) * 34;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= cols) return;
+  const uint8_t* blk = row + (size_t)(i >> 5) * 34;
+  const unsigned short bits = (unsigned short)(blk[0] | (blk[1] << 8));
+  const float d = __half2float(__ushort_as_half(bits));
+  X[(size_t)b * cols + i] = __fmul_rn(d, (float)(int8_t)blk[2 + (i & 31)]);
+}
+
+// RoPE + KV append of row b at seqs[b].pos into layer `layer` of seqs[b]'s
+// cache (as k_pf_qkv_rope, with a cache and position per row).
+__global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seqs, int layer, int nq,
+                              int nkv, int hd, int rope_half, float* Q, int kv_f16) {
+  const int rows = nq + 2 * nkv;
+  const int half_rows = rows >> 1;
+  const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (long long)n * half_rows) return;
+  const int b = (int)(e / half_rows);
+  const int row = (int)(e % half_rows) * 2;
+  const SeqInfo& sq = seqs[b];
+  const int pos = sq.pos;
+  const float2 xv = *reinterpret_cast<const float2*>(QKV + (size_t)b * rows + row);
+  float x0 = xv.x, x1 = xv.y;
+  const bool is_q = row < nq;
+  const bool is_k = !is_q && row < nq + nkv;
+  if (is_q || is_k) {
+    const int d = (is_q ? row : row - nq) % hd;
+    const int i = d >> 1;
+    if (i < rope_half) {
+      const float c = sq.rope_cos[(size_t)pos * rope_half + i];
+      const float s = sq.rope_sin[(size_t)pos * rope_half + i];
+      const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+      const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+      x0 = y0;
+      x1 = y1;
+    }
+  }
+  if (is_q) {
+    *reinterpret_cast<float2*>(Q + (size_t)b * nq + row) = make_float2(x0, x1);
+  } else {
+    const int r2 = is_k ? row - nq : row - nq - nkv;
+    const int kvh = r2 / hd, d = r2 % hd;
+    uint8_t* kvl = static_cast<uint8_t*>(sq.kv) + (size_t)layer * sq.layer_bytes;
+    const size_t off = (((size_t)kvh * sq.ctx + pos) * 2 + (is_k ? 0 : 1)) * hd + d;
+    if (kv_f16)
+      *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(kvl) + off) = __floats2half2_rn(x0, x1);
+    else
+      *reinterpret_cast<float2*>(reinterpret_cast<float*>(kvl) + off) = make_float2(x0, x1);
+  }
+}
+
+// Split-K decode attention (infer.go:130-175) of every sequence: CTA (split,
+// kv head, sequence) covers positions [split * BD_SPLIT, ...) up to the
+// sequence's own position; warp w takes every 8th position from the split's
+// start (neighbouring warps read neighbouring cache rows), lane = dims j*32 +
+// lane.  Per query row of the kv head's group it keeps an online softmax (max,
+// sum, weighted V); the 8 warps merge in shared memory and the CTA writes one
+// partial (max, sum, o[HD]) per query head, merged across splits by
+// k_bd_merge.
+constexpr int BD_SPLIT = 256;
+template <int HD, typename KT>
+__global__ void __launch_bounds__(256) k_bd_attention(const float* Q, const SeqInfo* seqs,
+                                                      int layer, int group, int nq_heads,
+                                                      float scale, float* part_o,
+                                                      float* part_ml, int max_splits) {
+  constexpr int DPL = HD / 32;
+  __shared__ float sm_m[8][MAXG], sm_l[8][MAXG];
+  __shared__ __align__(16) float sm_o[8][MAXG][HD];
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const SeqInfo& sq = seqs[b];
+  const int p0 = split * BD_SPLIT;
+  const int p1 = min(sq.pos + 1, p0 + BD_SPLIT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float q[MAXG][DPL], o[MAXG][DPL], m[MAXG], l[MAXG];
+#pragma unroll
+  for (int g = 0; g < MAXG; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) {
+      o[g][j] = 0.0f;
+      q[g][j] = g < group
+                    ? Q[(size_t)b * nq_heads * HD + (size_t)(kvh * group + g) * HD + j * 32 + lane]
+                    : 0.0f;
+    }
+  }
+  const KT* base = reinterpret_cast<const KT*>(static_cast<const uint8_t*>(sq.kv) +
+                                               (size_t)layer * sq.layer_bytes) +
+                   (size_t)kvh * sq.ctx * 2 * HD;
+  for (int p = p0 + warp; p < p1; p += 8) {
+    const KT* kr = base + (size_t)p * 2 * HD;
+    float kf[DPL], vf[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) {
+      kf[j] = (float)kr[j * 32 + lane];
+      vf[j] = (float)kr[HD + j * 32 + lane];
+    }
+#pragma unroll
+    for (int g = 0; g < MAXG; ++g) {
+      if (g >= group) break;  // uniform
+      float d = 0.0f;
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) d = fmaf(q[g][j], kf[j], d);
+      d = warp_sum(d);
+      const float s = __fmul_rn(d, scale);
+      const float mn = fmaxf(m[g], s);
+      const float corr = expf(m[g] - mn);  // 0 while m is -inf
+      const float pe = expf(s - mn);
+      l[g] = fmaf(l[g], corr, pe);
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) o[g][j] = fmaf(pe, vf[j], o[g][j] * corr);
+      m[g] = mn;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < MAXG; ++g) {
+    if (g >= group) break;
+    if (lane == 0) {
+      sm_m[warp][g] = m[g];
+      sm_l[warp][g] = l[g];
+    }
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) sm_o[warp][g][j * 32 + lane] = o[g][j];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < group * HD; e += 256) {
+    const int g = e / HD, d = e % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, sm_m[w][g]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float f = sm_m[w][g] == -INFINITY ? 0.0f : expf(sm_m[w][g] - M);
+        L = fmaf(sm_l[w][g], f, L);
+        O = fmaf(sm_o[w][g][d], f, O);
+      }
+    }
+    const size_t slot = ((size_t)b * nq_heads + kvh * group + g) * max_splits + split;
+    part_o[slot * HD + d] = O;
+    if (d == 0) {
+      part_ml[slot * 2] = M;
+      part_ml[slot * 2 + 1] = L;
+    }
+  }
+}
+
+// out[b][head] = sum over splits of o_s * exp(m_s - M) / sum of l_s * exp(m_s - M).
+// grid (query heads, n), HD threads.
+__global__ void k_bd_merge(const float* part_o, const float* part_ml, const SeqInfo* seqs,
+                           int nq_heads, int hd, int max_splits, float* out) {
+  const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  if (d >= hd) return;
+  const int ns = (seqs[b].pos + 1 + BD_SPLIT - 1) / BD_SPLIT;
+  const size_t slot0 = ((size_t)b * nq_heads + head) * max_splits;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, part_ml[(slot0 + s) * 2]);
+  float L = 0.0f, O = 0.0f;
+  for (int s = 0; s < ns; ++s) {
+    const float ms = part_ml[(slot0 + s) * 2];
+    const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+    L = fmaf(part_ml[(slot0 + s) * 2 + 1], f, L);
+    O = fmaf(part_o[(slot0 + s) * hd + d], f, O);
+  }
+  out[(size_t)b * nq_heads * hd + (size_t)head * hd + d] = O / L;
+}
+
+// Top-K of each sequence's logits (keys as k_topk_partial: ordered float
+// bits, lower id first on ties).  The logits of rank r's vocabulary shard
+// for sequence b sit at L[(r * n + b) * v_l + v] (the allgather layout; one
+// rank: r = 0), global id r * v_l + v; ids at or past vocab are padding.
+// Phase 1: grid (chunks of TOPK_CHUNK ids, n).
+__global__ void k_bd_topk_partial(const float* L, int n, int v_l, int vocab, int k,
+                                  uint64_t* part) {
+  __shared__ uint64_t keys[TOPK_CHUNK];
+  const int b = blockIdx.y, nchunks = gridDim.x;
+  const int base = blockIdx.x * TOPK_CHUNK;
+  for (int i = threadIdx.x; i < TOPK_CHUNK; i += blockDim.x) {
+    const int id = base + i;
+    uint64_t key = 0ull;
+    if (id < vocab) {
+      const int r = id / v_l, v = id % v_l;
+      key = topk_key(L[((size_t)r * n + b) * v_l + v], id);
+    }
+    keys[i] = key;
+  }
+  __syncthreads();
+  bitonic_desc(keys, TOPK_CHUNK);
+  for (int i = threadIdx.x; i < k; i += blockDim.x)
+    part[((size_t)b * nchunks + blockIdx.x) * k + i] = keys[i];
+}
+// Phase 2: grid n; cap (a power of two >= count) keys of dynamic shared memory.
+__global__ void k_bd_topk_final(const uint64_t* part, int count, int cap, int k, int* ids,
+                                float* logits) {
+  extern __shared__ uint64_t keys3[];
+  const int b = blockIdx.x;
+  for (int i = threadIdx.x; i < cap; i += blockDim.x)
+    keys3[i] = i < count ? part[(size_t)b * count + i] : 0ull;
+  __syncthreads();
+  bitonic_desc(keys3, cap);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    ids[(size_t)b * k + i] = key_index(keys3[i]);
+    logits[(size_t)b * k + i] = key_value(keys3[i]);
+  }
+}
+
+// SampleTopK (sampling.go:103-143) per sequence, as k_sample: float64
+// softmax with 1/T over the items in order, r = uniform * sum from
+// Philox4x32-10 keyed by the sequence's seed, counted by its position, then
+// the cumulative pick.  grid n, one warp.
+__global__ void k_bd_sample(const int* ids, const float* logits, int k, const SeqInfo* seqs,
+                            Result* out) {
+  __shared__ double e[MAX_TOPK];
+  const int b = blockIdx.x, lane = threadIdx.x;
+  const int* id = ids + (size_t)b * k;
+  const float* lg = logits + (size_t)b * k;
+  float mx = lg[0];
+  for (int i = 1; i < k; ++i) mx = fmaxf(mx, lg[i]);
+  const double invT = 1.0 / (double)seqs[b].temperature;
+  for (int i = lane; i < k; i += 32) e[i] = exp((double)(lg[i] - mx) * invT);
+  __syncwarp();
+  if (lane != 0) return;
+  double sum = 0.0;
+  for (int i = 0; i < k; ++i) sum += e[i];
+  const uint64_t ctr = (uint64_t)seqs[b].pos;
+  uint32_t c[4] = {(uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u};
+  philox4x32_10(c, (uint32_t)seqs[b].seed, (uint32_t)(seqs[b].seed >> 32));
+  const uint64_t x = ((uint64_t)c[0] << 32) | c[1];
+  const double r = (double)(x >> 11) * 0x1.0p-53 * sum;
+  double acc = 0.0;
+  int pick = k - 1;
+  for (int i = 0; i < k; ++i) {
+    acc += e[i];
+    if (r <= acc) {
+      pick = i;
+      break;
+    }
+  }
+  out[b].token = id[pick];
+  out[b].logit = lg[pick];
+  out[b].err = 0;
+  out[b].where = 0;
+}

@@ -55,8 +55,8 @@ __device__ __forceinline__ void tmem_wait_ld() {
 struct GemmArgs {
   const uint8_t* a;   // weight chunks [row tiles][nk] (gemm::A_CHUNK bytes each)
   const uint8_t* b;   // activation chunks [token tiles][nk] (gemm::b_chunk(NT) each)
-  float* out;         // [n_tok][rows]
-  int rows, n_tok, nk, n_rt, n_tt;
+  float* out;         // [n_tok][ldo], columns [0, rows) written
+  int rows, ldo, n_tok, nk, n_rt, n_tt;
   int nstages;
   Result* res;
   unsigned long long wait_ns;
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < CPT; ++i) {
           const int n = tt * NT + half * CPT + i;
-          if (n < g.n_tok) g.out[(size_t)n * g.rows + row] = acc[i];
+          if (n < g.n_tok) g.out[(size_t)n * g.ldo + row] = acc[i];
         }
       }
     }

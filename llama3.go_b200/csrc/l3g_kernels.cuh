@@ -574,4 +574,7 @@ __global__ void k_selftest_wait(Result* res, unsigned long long timeout_ns) {
   if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, res, 99, timeout_ns);
 }
 
+// batched decode (uses the top-K keys and the sampler's Philox above)
+#include "l3g_batch.cuh"
+
 }  // namespace l3g

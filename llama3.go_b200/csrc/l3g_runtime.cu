@@ -382,6 +382,7 @@ struct l3g_model {
   size_t dev_bytes = 0;
   std::mutex gemm_mu;       // guards the lazy build of the layers' GemmMat
   bool gemm_ready = false;
+  GemmMat glogits;          // logits shard as weight chunks (batched decode)
 };
 
 static const l3g_tensor* find_tensor(const l3g_tensor* ts, int n, const char* name) {
@@ -457,6 +458,7 @@ extern "C" void l3g_model_free(l3g_model* m) {
     if (L.ffn_norm) cudaFree(L.ffn_norm);
   }
   free_mat(m->logits);
+  free_gemm(m->glogits);
   if (m->out_norm) cudaFree(m->out_norm);
   if (m->emb) cudaFree(m->emb);
   if (m->comm) nccl()->CommDestroy(m->comm);
@@ -2237,13 +2239,14 @@ extern "C" int l3g_quantize_q8_0(const float* x, int32_t n, float* d, int8_t* qs
 // most, tiles dealt round-robin.
 static cudaError_t launch_gemm(const GemmMat& w, const uint8_t* act, int n_tok, float* out,
                                Result* res, unsigned long long wait_ns, int nsm,
-                               cudaStream_t st) {
+                               cudaStream_t st, int ldo = 0) {
   const int nt = gemm::token_tile(n_tok);
   GemmArgs g{};
   g.a = w.data;
   g.b = act;
   g.out = out;
   g.rows = w.rows;
+  g.ldo = ldo > 0 ? ldo : w.rows;
   g.n_tok = n_tok;
   g.nk = w.nk;
   g.n_rt = w.n_rt;
@@ -2630,6 +2633,281 @@ extern "C" int l3g_prefill_batched(l3g_model* m, l3g_state* s, l3g_workspace* ws
                       code == ERR_TIMEOUT ? "bounded wait ran out" : "bad input");
     }
     s->pos += P;
+  }
+  return L3G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// batched decode
+// ---------------------------------------------------------------------------
+struct l3g_batch {
+  l3g_model* m = nullptr;
+  int device = 0, cap = 0, max_splits = 0, tk_chunks = 0;
+  cudaStream_t stream = nullptr;
+  SeqInfo* h_seq = nullptr;  // pinned [cap]
+  SeqInfo* d_seq = nullptr;
+  Result* h_out = nullptr;   // pinned [cap]: sampled token and its logit
+  Result* d_out = nullptr;
+  Result* h_res = nullptr;   // pinned: error word
+  Result* d_res = nullptr;
+  float* x = nullptr;        // [cap][n_emb]
+  float* y = nullptr;        // [cap][n_emb]
+  float* qkv = nullptr;      // [cap][qkv rows]
+  float* q = nullptr;        // [cap][local q heads * hd]
+  float* att = nullptr;      // [cap][local q heads * hd]
+  float* ug = nullptr;       // [cap][2 * local n_ff]
+  float* logits = nullptr;   // [cap][v_l], columns past the shard's rows -inf
+  float* logits_full = nullptr;  // [world][cap][v_l] (world > 1)
+  float* part_o = nullptr;   // [cap][local q heads][max_splits][hd]
+  float* part_ml = nullptr;  // [cap][local q heads][max_splits][2]
+  uint8_t* act = nullptr;
+  uint64_t* tk_part = nullptr;  // [cap][tk_chunks][MAX_TOPK]
+  int* tk_ids = nullptr;        // [cap][MAX_TOPK]
+  float* tk_logits = nullptr;
+};
+
+extern "C" void l3g_batch_free(l3g_batch* b) {
+  if (!b) return;
+  cudaSetDevice(b->device);
+  void* d[] = {b->d_seq, b->d_out, b->d_res, b->x, b->y, b->qkv, b->q, b->att, b->ug,
+               b->logits, b->logits_full, b->part_o, b->part_ml, b->act, b->tk_part,
+               b->tk_ids, b->tk_logits};
+  for (void* p : d)
+    if (p) cudaFree(p);
+  void* h[] = {b->h_seq, b->h_out, b->h_res};
+  for (void* p : h)
+    if (p) cudaFreeHost(p);
+  if (b->stream) cudaStreamDestroy(b->stream);
+  delete b;
+}
+
+extern "C" int l3g_batch_new(l3g_model* m, int32_t max_seqs, l3g_batch** out) {
+  if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  *out = nullptr;
+  if (max_seqs <= 0 || max_seqs > L3G_BATCH_MAX)
+    return l3g_fail(L3G_E_INVALID, "max_seqs=%d outside [1, %d]", max_seqs, L3G_BATCH_MAX);
+  if (m->hp.n_emb > PF_THREADS * 4 * PF_VK || m->hd > 128 || (m->hd != 32 && m->hd != 64 &&
+                                                              m->hd != 128))
+    return l3g_fail(L3G_E_INVALID, "batched decode: n_emb %d, head_dim %d", m->hp.n_emb, m->hd);
+  CUDA_TRY(cudaSetDevice(m->device));
+  if (int rc = gemm_setup()) return rc;
+  if (int rc = ensure_gemm_weights(m)) return rc;
+  {
+    std::lock_guard<std::mutex> lk(m->gemm_mu);
+    if (!m->glogits.data) {
+      size_t bytes = 0;
+      if (int rc = gemm_from_tiles(m->logits, m->glogits, &bytes)) return rc;
+      CUDA_TRY(cudaDeviceSynchronize());
+      m->dev_bytes += bytes;
+    }
+  }
+  auto* b = new l3g_batch();
+  b->m = m;
+  b->device = m->device;
+  b->cap = max_seqs;
+  b->max_splits = (m->hp.ctx_len + BD_SPLIT - 1) / BD_SPLIT;
+  b->tk_chunks = (m->hp.vocab_size + TOPK_CHUNK - 1) / TOPK_CHUNK;
+  const size_t cap = (size_t)max_seqs;
+  const int ne = m->hp.n_emb, nq = m->hq_l * m->hd, nkv = m->hkv_l * m->hd;
+  const int max_cols = std::max(std::max(ne, nq), m->ff_l);
+  uint64_t act_bytes = 0;
+  if (int rc = l3g_gemm_act_bytes(max_seqs, max_cols, &act_bytes)) {
+    l3g_batch_free(b);
+    return rc;
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMallocHost(&b->h_seq, cap * sizeof(SeqInfo));
+  if (e == cudaSuccess) e = cudaMallocHost(&b->h_out, cap * sizeof(Result));
+  if (e == cudaSuccess) e = cudaMallocHost(&b->h_res, sizeof(Result));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_seq, cap * sizeof(SeqInfo));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_out, cap * sizeof(Result));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_res, sizeof(Result));
+  if (e == cudaSuccess) e = cudaMemset(b->d_res, 0, sizeof(Result));
+  if (e == cudaSuccess) e = cudaMalloc(&b->x, cap * ne * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->y, cap * ne * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->qkv, cap * (nq + 2 * nkv) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->q, cap * nq * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->att, cap * nq * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->ug, cap * 2 * m->ff_l * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->logits, cap * m->v_l * 4);
+  if (e == cudaSuccess && m->world > 1)
+    e = cudaMalloc(&b->logits_full, cap * m->v_l * m->world * 4);
+  if (e == cudaSuccess)
+    e = cudaMalloc(&b->part_o, cap * m->hq_l * b->max_splits * m->hd * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->part_ml, cap * m->hq_l * b->max_splits * 2 * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->act, act_bytes);
+  if (e == cudaSuccess) e = cudaMemset(b->act, 0, act_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&b->tk_part, cap * b->tk_chunks * MAX_TOPK * 8);
+  if (e == cudaSuccess) e = cudaMalloc(&b->tk_ids, cap * MAX_TOPK * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->tk_logits, cap * MAX_TOPK * 4);
+  if (e == cudaSuccess) {  // the shard's padding columns (past its vocabulary rows) stay -inf
+    std::vector<float> ninf(cap * m->v_l, -INFINITY);
+    e = cudaMemcpy(b->logits, ninf.data(), ninf.size() * 4, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess) {
+    l3g_batch_free(b);
+    return l3g_fail(L3G_E_CUDA, "batch allocation: %s", cudaGetErrorString(e));
+  }
+  *out = b;
+  return L3G_OK;
+}
+
+extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
+                              const int32_t* tokens, int32_t top_k, float temperature,
+                              const uint64_t* seeds, int32_t* next_tokens, float* logits_out) {
+  if (!b || !states || !tokens || !seeds || !next_tokens)
+    return l3g_fail(L3G_E_INVALID, "null argument");
+  l3g_model* m = b->m;
+  if (n <= 0 || n > b->cap) return l3g_fail(L3G_E_INVALID, "n=%d outside [1, %d]", n, b->cap);
+  if (top_k <= 0) top_k = 40;  // infer.go:279-281
+  if (top_k > MAX_TOPK) return l3g_fail(L3G_E_INVALID, "top_k %d above %d", top_k, MAX_TOPK);
+  if (top_k > m->hp.vocab_size) top_k = m->hp.vocab_size;
+  if (temperature <= 0.0f) temperature = 0.8f;  // sampling.go:20-22
+  const size_t es = m->kv_f16 ? 2 : 4;
+  int max_pos = 0;
+  for (int i = 0; i < n; ++i) {
+    const l3g_state* s = states[i];
+    if (!s) return l3g_fail(L3G_E_INVALID, "null state %d", i);
+    if (s->m != m) return l3g_fail(L3G_E_INVALID, "state %d belongs to another model", i);
+    for (int j = 0; j < i; ++j)
+      if (states[j] == s) return l3g_fail(L3G_E_INVALID, "state %d appears twice", i);
+    if (s->pos >= s->ctx) return l3g_fail(L3G_E_CTX, "context length exceeded (%d)", s->ctx);
+    if (tokens[i] < 0 || tokens[i] >= m->hp.vocab_size)
+      return l3g_fail(L3G_E_TOKEN, "token out of range: %d", tokens[i]);
+    SeqInfo& q = b->h_seq[i];
+    q = SeqInfo{};
+    q.kv = s->kv;
+    q.rope_cos = s->rope_cos;
+    q.rope_sin = s->rope_sin;
+    q.layer_bytes = (long long)(s->layer_elems * es);
+    q.ctx = s->ctx;
+    q.pos = s->pos;
+    q.token = tokens[i];
+    q.seed = seeds[i];
+    q.temperature = temperature;
+    max_pos = std::max(max_pos, s->pos);
+  }
+  CUDA_TRY(cudaSetDevice(m->device));
+  const l3g_hparams& hp = m->hp;
+  const cudaStream_t st = b->stream;
+  const int ne = hp.n_emb, hd = m->hd;
+  const int nq = m->hq_l * hd, nkv = m->hkv_l * hd;
+  const unsigned long long wait_ns = m->world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS;
+  const int nt = gemm::token_tile(n);
+  const int n_pad = (n + nt - 1) / nt * nt;
+  const int splits = (max_pos + 1 + BD_SPLIT - 1) / BD_SPLIT;
+  const float scale = (float)(1.0 / sqrt((double)hd));
+  CUDA_TRY(cudaMemcpyAsync(b->d_seq, b->h_seq, (size_t)n * sizeof(SeqInfo),
+                           cudaMemcpyHostToDevice, st));
+  k_bd_embed<<<dim3((ne + 255) / 256, n), 256, 0, st>>>(m->emb, hp.vocab_size, ne, b->d_seq, b->x,
+                                                        b->d_res);
+  CUDA_TRY(cudaGetLastError());
+  for (int l = 0; l < hp.n_layers; ++l) {
+    const LayerW& L = m->layers[l];
+    k_pf_rms_quant<<<n, PF_THREADS, 0, st>>>(b->x, l ? b->y : nullptr, L.attn_norm, hp.rms_eps,
+                                            ne, nt, gemm::chunks(ne), b->act);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_gemm(L.gqkv, b->act, n, b->qkv, b->d_res, wait_ns, m->nsm, st));
+    {
+      const long long pairs = (long long)n * ((nq + 2 * nkv) / 2);
+      k_bd_qkv_rope<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
+          b->qkv, n, b->d_seq, l, nq, nkv, hd, m->rope_half, b->q, m->kv_f16);
+      CUDA_TRY(cudaGetLastError());
+    }
+    {
+      const dim3 grid(splits, m->hkv_l, n);
+#define BDATT(HD)                                                                           \
+  if (m->kv_f16)                                                                           \
+    k_bd_attention<HD, __half><<<grid, 256, 0, st>>>(b->q, b->d_seq, l, m->group, m->hq_l, \
+                                                      scale, b->part_o, b->part_ml,        \
+                                                      b->max_splits);                      \
+  else                                                                                     \
+    k_bd_attention<HD, float><<<grid, 256, 0, st>>>(b->q, b->d_seq, l, m->group, m->hq_l,  \
+                                                     scale, b->part_o, b->part_ml,         \
+                                                     b->max_splits)
+      if (hd == 32) {
+        BDATT(32);
+      } else if (hd == 64) {
+        BDATT(64);
+      } else {
+        BDATT(128);
+      }
+#undef BDATT
+      CUDA_TRY(cudaGetLastError());
+      k_bd_merge<<<dim3(m->hq_l, n), 128, 0, st>>>(b->part_o, b->part_ml, b->d_seq, m->hq_l, hd,
+                                                   b->max_splits, b->att);
+      CUDA_TRY(cudaGetLastError());
+    }
+    {
+      const long long warps = (long long)n_pad * gemm::chunks(nq) * gemm::BPC;
+      k_gemm_quantize<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+          b->att, n, nq, nt, gemm::chunks(nq), n_pad, b->act);
+      CUDA_TRY(cudaGetLastError());
+    }
+    CUDA_TRY(launch_gemm(L.gwo, b->act, n, b->y, b->d_res, wait_ns, m->nsm, st));
+    if (m->world > 1)
+      NCCL_TRY(nccl()->AllReduce(b->y, b->y, (size_t)n * ne, ncclFloat, ncclSum, m->comm, st));
+    k_pf_rms_quant<<<n, PF_THREADS, 0, st>>>(b->x, b->y, L.ffn_norm, hp.rms_eps, ne, nt,
+                                            gemm::chunks(ne), b->act);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(launch_gemm(L.gupgate, b->act, n, b->ug, b->d_res, wait_ns, m->nsm, st));
+    {
+      const long long warps = (long long)n * (m->ff_l / 32);
+      k_pf_swiglu_quant<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+          b->ug, n, m->ff_l, nt, gemm::chunks(m->ff_l), b->act);
+      CUDA_TRY(cudaGetLastError());
+    }
+    CUDA_TRY(launch_gemm(L.gdown, b->act, n, b->y, b->d_res, wait_ns, m->nsm, st));
+    if (m->world > 1)
+      NCCL_TRY(nccl()->AllReduce(b->y, b->y, (size_t)n * ne, ncclFloat, ncclSum, m->comm, st));
+  }
+  // residual -> final RMSNorm -> act-quant -> logits shard, infer.go:250-260
+  k_pf_rms_quant<<<n, PF_THREADS, 0, st>>>(b->x, b->y, m->out_norm, hp.rms_eps, ne, nt,
+                                          gemm::chunks(ne), b->act);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(launch_gemm(m->glogits, b->act, n, b->logits, b->d_res, wait_ns, m->nsm, st, m->v_l));
+  const float* lg = b->logits;
+  if (m->world > 1) {
+    NCCL_TRY(nccl()->AllGather(b->logits, b->logits_full, (size_t)n * m->v_l, ncclFloat, m->comm,
+                               st));
+    lg = b->logits_full;
+  }
+  // top-K and SampleTopK per sequence
+  k_bd_topk_partial<<<dim3(b->tk_chunks, n), 256, 0, st>>>(lg, n, m->v_l, hp.vocab_size, top_k,
+                                                          b->tk_part);
+  CUDA_TRY(cudaGetLastError());
+  {
+    const int count = b->tk_chunks * top_k;
+    int cap2 = 1;
+    while (cap2 < count) cap2 <<= 1;
+    k_bd_topk_final<<<n, 256, (size_t)cap2 * 8, st>>>(b->tk_part, count, cap2, top_k, b->tk_ids,
+                                                     b->tk_logits);
+    CUDA_TRY(cudaGetLastError());
+  }
+  k_bd_sample<<<n, 32, 0, st>>>(b->tk_ids, b->tk_logits, top_k, b->d_seq, b->d_out);
+  CUDA_TRY(cudaGetLastError());
+  CUDA_TRY(cudaMemcpyAsync(b->h_out, b->d_out, (size_t)n * sizeof(Result), cudaMemcpyDeviceToHost,
+                           st));
+  CUDA_TRY(cudaMemcpyAsync(b->h_res, b->d_res, sizeof(Result), cudaMemcpyDeviceToHost, st));
+  if (logits_out) {  // [n][vocab]: the shards side by side
+    for (int r = 0; r < m->world; ++r) {
+      const int rows = std::min(m->v_l, hp.vocab_size - r * m->v_l);
+      if (rows <= 0) break;
+      CUDA_TRY(cudaMemcpy2DAsync(logits_out + (size_t)r * m->v_l, (size_t)hp.vocab_size * 4,
+                                 lg + (size_t)r * n * m->v_l, (size_t)m->v_l * 4,
+                                 (size_t)rows * 4, n, cudaMemcpyDeviceToHost, st));
+    }
+  }
+  CUDA_TRY(cudaStreamSynchronize(st));
+  if (b->h_res->err) {
+    const int code = b->h_res->err, where = b->h_res->where;
+    cudaMemset(b->d_res, 0, sizeof(Result));
+    return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d (%s)", code, where,
+                    code == ERR_TIMEOUT ? "bounded wait ran out" : "bad input");
+  }
+  for (int i = 0; i < n; ++i) {
+    next_tokens[i] = b->h_out[i].token;
+    states[i]->pos++;
   }
   return L3G_OK;
 }

@@ -132,6 +132,11 @@ def lib():
         "l3g_matrix_free": (None, [_P]),
         "l3g_matrix_device_bytes": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
         "l3g_quantize_q8_0": (C.c_int, [_P, C.c_int32, _P, _P, _P]),
+        "l3g_batch_new": (C.c_int, [_P, C.c_int32, C.POINTER(_P)]),
+        "l3g_batch_free": (None, [_P]),
+        "l3g_batch_step": (C.c_int, [_P, C.POINTER(_P), C.c_int32, C.POINTER(C.c_int32), C.c_int32,
+                                     C.c_float, C.POINTER(C.c_uint64), C.POINTER(C.c_int32),
+                                     C.POINTER(C.c_float)]),
         "l3g_gemm_matrix_bytes": (C.c_int, [C.c_int32, C.c_int32, C.POINTER(C.c_uint64)]),
         "l3g_gemm_repack": (C.c_int, [_P, C.c_int32, C.c_int32, _P, C.c_uint64]),
         "l3g_gemm_matrix_upload": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_P)]),
@@ -539,6 +544,46 @@ class Matrix:
     def Close(self):
         if self._h:
             lib().l3g_matrix_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.Close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """Batched decode over many sessions (l3g_state) of one model: one step
+    ingests a token per session and samples its next token on the device."""
+
+    def __init__(self, model: "Model", max_seqs: int):
+        h = C.c_void_p()
+        _check(lib().l3g_batch_new(model._h, max_seqs, C.byref(h)))
+        self._h = h
+        self.model = model
+        self.max_seqs = max_seqs
+
+    def step(self, states, tokens, seeds, top_k: int = 40, temperature: float = 0.8,
+             want_logits: bool = False):
+        """Returns next tokens [n] (and logits [n][vocab] when asked)."""
+        n = len(states)
+        arr = (C.c_void_p * n)(*[s._h.value if isinstance(s._h, C.c_void_p) else s._h
+                                for s in states])
+        tok = np.ascontiguousarray(tokens, dtype=np.int32)
+        sd = np.ascontiguousarray(seeds, dtype=np.uint64)
+        nxt = np.empty(n, np.int32)
+        logits = np.empty((n, self.model.HP.VocabSize), np.float32) if want_logits else None
+        _check(lib().l3g_batch_step(self._h, C.cast(arr, C.POINTER(C.c_void_p)), n,
+                                    tok.ctypes.data_as(C.POINTER(C.c_int32)), top_k, temperature,
+                                    sd.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                    nxt.ctypes.data_as(C.POINTER(C.c_int32)),
+                                    _fptr(logits) if logits is not None else None))
+        return (nxt, logits) if want_logits else nxt
+
+    def Close(self):
+        if self._h:
+            lib().l3g_batch_free(self._h)
             self._h = C.c_void_p()
 
     def __del__(self):
