@@ -339,8 +339,8 @@ int l3g_quantize_q8_0(const float *x, int32_t n, float *d, int8_t *qs,
 
 /* ---- batched decode: many sessions, one step ----------------------------- */
 /* One decode step for n independent sessions of one model, each an
- * l3g_state (its own KV cache, context length and position; no two entries
- * the same state).  Per session the step is ForwardTopKIntoWorkspace
+ * l3g_state with its own KV cache, context length and position (no two
+ * entries the same state).  Per session the step is ForwardTopKIntoWorkspace
  * (infer.go:269-511, with the exact exp of the full path, :130-175) followed
  * by Sampler.SampleTopK (sampling.go:103-143): state i ingests tokens[i] at
  * its position and advances by one, and next_tokens[i] receives a sample
