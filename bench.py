@@ -19,7 +19,10 @@ Prints one JSON line:
                  the host cores, on a bounded sample of the same workload.
 
 --impl reference times only the reference's CPU path (the oracle) on this
-workload.  --workload matvec runs the Q8_0 matvec microbench instead.
+workload.  --workload matvec runs the Q8_0 matvec microbench instead;
+--workload gemm the batched tensor-core product microbench, --workload
+prefill batched prefill against token-by-token ingest, --workload batched the
+64-session batched decode (tensor parallel under torchrun).
 """
 from __future__ import annotations
 
@@ -45,7 +48,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="l3g", choices=["l3g", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "matvec"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "matvec", "gemm", "prefill", "batched"])
     ap.add_argument("--config", default="llama3.1-8b")
     ap.add_argument("--prefill", type=int, default=4096)
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"])
@@ -53,6 +57,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--iters", type=int, default=1000, help="matvec microbench iterations")
+    ap.add_argument("--tokens", default="16,64,128", help="gemm microbench token counts")
+    ap.add_argument("--seqs", type=int, default=64, help="batched decode sessions")
+    ap.add_argument("--ctx-min", type=int, default=512, help="batched decode shortest context")
+    ap.add_argument("--ctx-max", type=int, default=8192, help="batched decode longest context")
     ap.add_argument("--shapes", default="4096x4096,1024x4096,14336x4096,4096x14336,128256x4096",
                     help="matvec microbench shapes, rows x cols")
     return ap.parse_args()
@@ -548,12 +556,184 @@ def run_matvec(args):
     return 0
 
 
+def run_gemm(args):
+    """Batched Q8_0 product (tcgen05 int8) microbench over the 8B shapes and
+    token counts: GB/s of weights + activations + out, and int8 TOP/s."""
+    import torch
+    import build
+    build.build(quiet=True)
+    import l3g
+    import synthetic
+    hbm, kind = peaks()
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s]
+    for rows, cols in shapes:
+        g = torch.Generator(device="cuda").manual_seed(rows + cols)
+        w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g, device="cuda") * 0.02, torch)
+        host = w.cpu().numpy()
+        del w
+        wbytes = rows * cols // 32 * 34
+        ncopy = max(1, -(-4 * l2 // wbytes))
+        mats = [l3g.GemmMatrix(host, rows, cols, device=0) for _ in range(ncopy)]
+        for n in [int(v) for v in args.tokens.split(",") if v]:
+            x = torch.randn(n, cols, device="cuda")
+            act = torch.empty(l3g.gemm_act_bytes(n, cols), dtype=torch.uint8, device="cuda")
+            out = torch.empty(n, rows, device="cuda")
+            st = torch.cuda.current_stream().cuda_stream
+            l3g.gemm_quantize(x.data_ptr(), n, cols, act.data_ptr(), stream=st)
+            for i in range(5):
+                mats[i % ncopy].gemm(act.data_ptr(), n, out.data_ptr(), stream=st)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(args.iters):
+                mats[i % ncopy].gemm(act.data_ptr(), n, out.data_ptr(), stream=st)
+            e1.record()
+            torch.cuda.synchronize()
+            err = mats[0].status()
+            ms = e0.elapsed_time(e1) / args.iters
+            alg = wbytes + n * cols * 34 // 32 + n * rows * 4
+            print(json.dumps({"workload": "q8_0 batched product (tcgen05 kind::i8) microbench",
+                              "shape": [rows, cols], "tokens": n, "iters": args.iters,
+                              "copies_rotated": ncopy, "bytes_per_launch": alg,
+                              "us_per_launch": round(ms * 1e3, 3),
+                              "achieved_gbs": round(alg / ms / 1e6, 1), "peak_gbs": hbm,
+                              "frac": round(alg / ms / 1e6 / hbm, 4), "peak_kind": kind,
+                              "int8_tops": round(2.0 * rows * cols * n / ms / 1e9, 2),
+                              "device_status": list(err)}), flush=True)
+        for mtx in mats:
+            mtx.Close()
+    return 0
+
+
+def run_prefill(args):
+    """Batched prefill of --prefill tokens against the token-by-token ingest
+    (timed on a bounded sample), on one GPU."""
+    import torch
+    import build
+    build.build(quiet=True)
+    import l3g
+    import synthetic
+    cfg = synthetic.CONFIGS[args.config]
+    T = make_host_model(cfg, args.seed, "cuda:0")
+    torch.cuda.empty_cache()
+    kv = l3g.L3G_KV_F16 if args.kv == "f16" else l3g.L3G_KV_F32
+    m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, l3g.default_options(1, 0, 0, kv))
+    ctx = args.prefill + 1
+    s = m.NewState(ctx)
+    ws = m.NewWorkspace(ctx, 40)
+    prompt = synthetic.prompt_ids(cfg, args.prefill, seed=args.seed)
+    m.PrefillBatched(s, prompt[:64], ws)  # first call builds the product's weight copies
+    s.Pos = 0
+    t0 = time.perf_counter()
+    m.PrefillBatched(s, prompt, ws)
+    batched_s = time.perf_counter() - t0
+    sample = min(256, args.prefill)
+    s.Pos = 0
+    t0 = time.perf_counter()
+    m.Prefill(s, prompt[:sample], ws)
+    tbt_s = time.perf_counter() - t0
+    ws.Close()
+    s.Close()
+    m.Close()
+    print(json.dumps({"workload": f"{cfg.name}-shape batched prefill", "tokens": args.prefill,
+                      "kv_dtype": args.kv, "seconds": round(batched_s, 4),
+                      "tok_per_s": round(args.prefill / batched_s, 1),
+                      "token_by_token_tok_per_s": round(sample / tbt_s, 1),
+                      "token_by_token_sample": f"first {sample} positions"}), flush=True)
+    return 0
+
+
+def run_batched(args):
+    """Batched decode: --seqs sessions with seeded context lengths uniform in
+    [--ctx-min, --ctx-max], prefilled in batches, then --steps steps of top-k
+    40 / temperature 0.8 sampling with a seed per session, tensor parallel
+    over the ranks.  value: sampled tokens per second over all sessions,
+    each step a host call (tokens in, samples out)."""
+    world, rank, local = dist_env()
+    import numpy as np
+    import torch
+    import build
+    build.build(quiet=True)
+    import l3g
+    import synthetic
+    D = Dist(world, rank, local)
+    torch.cuda.set_device(local)
+    hbm, hbm_kind = peaks()
+    cfg = synthetic.CONFIGS[args.config]
+    T = make_host_model(cfg, args.seed, f"cuda:{local}")
+    torch.cuda.empty_cache()
+    nid = D.bcast_bytes(l3g.nccl_unique_id() if (world > 1 and rank == 0) else None) if world > 1 else None
+    kv = l3g.L3G_KV_F16 if args.kv == "f16" else l3g.L3G_KV_F32
+    m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, l3g.default_options(world, rank, local, kv, nid))
+    rng = np.random.default_rng(args.seed)
+    lens = rng.integers(args.ctx_min, args.ctx_max + 1, args.seqs)
+    seeds = rng.integers(1, 2**62, args.seqs).astype(np.uint64)
+    ws = m.NewWorkspace(int(lens.max()) + args.warmup + args.steps + 1, 40)
+    states = []
+    progress(world, rank, "batched prefill of the sessions")
+    t0 = time.perf_counter()
+    for i, L in enumerate(lens):
+        s = m.NewState(int(L) + args.warmup + args.steps + 1)
+        m.PrefillBatched(s, synthetic.prompt_ids(cfg, int(L), seed=args.seed + 1 + i), ws)
+        states.append(s)
+    prefill_s = time.perf_counter() - t0
+    batch = l3g.Batch(m, args.seqs)
+    tokens = rng.integers(0, cfg.vocab, args.seqs)
+    for _ in range(max(1, args.warmup)):
+        tokens = batch.step(states, tokens, seeds)
+    pos0 = np.array([s.Pos for s in states])
+    clk = Clocks(physical_index(local))
+    clk.wait_first_sample()
+    D.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tokens = batch.step(states, tokens, seeds)
+    D.barrier()
+    clocks = clk.stop()
+    wall = D.max(time.perf_counter() - t0)
+    value = args.seqs * args.steps / wall
+    es = 2 if args.kv == "f16" else 4
+    kv_step = sum(cfg.kv_bytes(int(p) + i + 1, es) for p in pos0 for i in range(args.steps)) / args.steps
+    step_bytes = cfg.weight_bytes() + kv_step
+    gbs = step_bytes * args.steps / wall / 1e9
+    batch.Close()
+    for s in states:
+        s.Close()
+    ws.Close()
+    m.Close()
+    D.close()
+    if rank != 0:
+        return 0
+    print(json.dumps({"metric": "batched decode tok/s (all sessions)", "value": round(value, 1),
+                      "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(wall * 1e3 / args.steps, 3), "higher_is_better": True,
+                      "dtype": "int8", "data": "synthetic",
+                      "config": {"workload": f"{cfg.name}-shape Q8_0 batched decode, {args.seqs} sessions, "
+                                             f"contexts uniform in [{args.ctx_min}, {args.ctx_max}], "
+                                             "top-k 40, temperature 0.8, a seed per session",
+                                 "parallelism": f"tp{world}", "kv_dtype": args.kv},
+                      "timing": "host wall clock per step call (tokens in, samples out), max over ranks",
+                      "roofline": {"bound": "hbm", "bytes_per_step": int(step_bytes),
+                                   "kv_bytes_per_step": int(kv_step), "achieved_gbs": round(gbs, 1),
+                                   "peak_gbs_aggregate": hbm * world,
+                                   "frac": round(gbs / (hbm * world), 4), "peak_kind": hbm_kind},
+                      "prefill_s": round(prefill_s, 2), "clocks": clocks}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "matvec":
         return run_matvec(args)
+    if args.workload == "gemm":
+        return run_gemm(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
+    if args.workload == "batched":
+        return run_batched(args)
     return run_l3g(args)
 
 
