@@ -89,89 +89,173 @@ __global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seqs, int 
 
 // Split-K decode attention (infer.go:130-175) of every sequence: CTA (split,
 // kv head, sequence) covers positions [split * BD_SPLIT, ...) up to the
-// sequence's own position; warp w takes every 8th position from the split's
-// start (neighbouring warps read neighbouring cache rows), lane = dims j*32 +
-// lane.  Per query row of the kv head's group it keeps an online softmax (max,
-// sum, weighted V); the 8 warps merge in shared memory and the CTA writes one
+// sequence's own position.  A producer warp streams the split's cache rows
+// (K | V of 32 positions, contiguous in the cache) into a ring of BD_STAGES
+// shared-memory stages with 1-D bulk copies; compute warp w takes positions
+// w, w + 8, w + 16, w + 24 of every 32-position tile (so across the split it
+// visits split start + w + 8i in order), lane = dims j*32 + lane.  Per query
+// row of the kv head's group a warp keeps an online softmax (max, sum,
+// weighted V); the 8 warps merge in shared memory and the CTA writes one
 // partial (max, sum, o[HD]) per query head, merged across splits by
-// k_bd_merge.
+// k_bd_merge.  Every wait is bounded; after an abort the CTA drains its
+// copies and writes nothing.
 constexpr int BD_SPLIT = 256;
-template <int HD, typename KT>
-__global__ void __launch_bounds__(256) k_bd_attention(const float* Q, const SeqInfo* seqs,
-                                                      int layer, int group, int nq_heads,
-                                                      float scale, float* part_o,
-                                                      float* part_ml, int max_splits) {
+constexpr int BD_TILE = 32;    // positions per ring stage
+constexpr int BD_STAGES = 3;
+constexpr int BD_THREADS = 288;  // 8 compute warps + 1 producer warp
+struct BdSmem {
+  uint64_t full[BD_STAGES];
+  uint64_t empty[BD_STAGES];
+  int abort_flag, issued, producer_done;
+  float m[8][MAXG], l[8][MAXG];
+};
+__host__ __device__ constexpr int bd_stage_bytes(int hd, int es) { return BD_TILE * 2 * hd * es; }
+// the merge buffer (8 warps x GP rows x hd floats) reuses the ring
+__host__ __device__ constexpr int bd_smem_bytes(int hd, int es, int gp) {
+  return 1024 + (BD_STAGES * bd_stage_bytes(hd, es) > 8 * gp * hd * 4
+                     ? BD_STAGES * bd_stage_bytes(hd, es)
+                     : 8 * gp * hd * 4);
+}
+// GP: the group size rounded up to 1, 2, 4 or 8 (register arrays per row)
+template <int HD, int GP, typename KT>
+__global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
+    const float* Q, const SeqInfo* seqs, int layer, int group, int nq_heads, float scale,
+    float* part_o, float* part_ml, int max_splits, Result* res, unsigned long long wait_ns) {
   constexpr int DPL = HD / 32;
-  __shared__ float sm_m[8][MAXG], sm_l[8][MAXG];
-  __shared__ __align__(16) float sm_o[8][MAXG][HD];
+  constexpr int SB = bd_stage_bytes(HD, (int)sizeof(KT));
+  static_assert(sizeof(BdSmem) <= 1024, "smem head");
+  extern __shared__ __align__(1024) uint8_t bd_smem[];
+  BdSmem* sh = reinterpret_cast<BdSmem*>(bd_smem);
+  uint8_t* ring = bd_smem + 1024;
+  float(*sm_o)[GP][HD] = reinterpret_cast<float(*)[GP][HD]>(ring);  // after the ring drains
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const SeqInfo& sq = seqs[b];
   const int p0 = split * BD_SPLIT;
   const int p1 = min(sq.pos + 1, p0 + BD_SPLIT);
+  const int ntiles = p1 > p0 ? (p1 - p0 + BD_TILE - 1) / BD_TILE : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float q[MAXG][DPL], o[MAXG][DPL], m[MAXG], l[MAXG];
-#pragma unroll
-  for (int g = 0; g < MAXG; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) {
-      o[g][j] = 0.0f;
-      q[g][j] = g < group
-                    ? Q[(size_t)b * nq_heads * HD + (size_t)(kvh * group + g) * HD + j * 32 + lane]
-                    : 0.0f;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BD_STAGES; ++s) {
+      mbar_init(&sh->full[s], 1);
+      mbar_init(&sh->empty[s], 8);
     }
+    sh->abort_flag = 0;
+    sh->issued = 0;
+    sh->producer_done = 0;
+    fence_mbar_init();
   }
+  __syncthreads();
   const KT* base = reinterpret_cast<const KT*>(static_cast<const uint8_t*>(sq.kv) +
                                                (size_t)layer * sq.layer_bytes) +
                    (size_t)kvh * sq.ctx * 2 * HD;
-  for (int p = p0 + warp; p < p1; p += 8) {
-    const KT* kr = base + (size_t)p * 2 * HD;
-    float kf[DPL], vf[DPL];
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) {
-      kf[j] = (float)kr[j * 32 + lane];
-      vf[j] = (float)kr[HD + j * 32 + lane];
+  float q[GP][DPL], o[GP][DPL], m[GP], l[GP];  // compute warps' online softmax
+  if (warp == 8) {  // producer
+    if (lane == 0) {
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % BD_STAGES;
+        if (t >= BD_STAGES &&
+            !mbar_wait(&sh->empty[s], ((t / BD_STAGES) - 1) & 1, &sh->abort_flag, res, 30, wait_ns))
+          break;
+        const int q0 = p0 + t * BD_TILE;
+        const int np = min(BD_TILE, p1 - q0);
+        const uint32_t bytes = (uint32_t)(np * 2 * HD * sizeof(KT));
+        mbar_arrive_expect_tx(&sh->full[s], bytes);
+        bulk_g2s(ring + (size_t)s * SB, base + (size_t)q0 * 2 * HD, bytes, &sh->full[s]);
+        *(volatile int*)&sh->issued = t + 1;
+      }
+      *(volatile int*)&sh->producer_done = 1;
     }
+  } else {
 #pragma unroll
-    for (int g = 0; g < MAXG; ++g) {
-      if (g >= group) break;  // uniform
-      float d = 0.0f;
+    for (int g = 0; g < GP; ++g) {
+      m[g] = -INFINITY;
+      l[g] = 0.0f;
 #pragma unroll
-      for (int j = 0; j < DPL; ++j) d = fmaf(q[g][j], kf[j], d);
-      d = warp_sum(d);
-      const float s = __fmul_rn(d, scale);
-      const float mn = fmaxf(m[g], s);
-      const float corr = expf(m[g] - mn);  // 0 while m is -inf
-      const float pe = expf(s - mn);
-      l[g] = fmaf(l[g], corr, pe);
+      for (int j = 0; j < DPL; ++j) {
+        o[g][j] = 0.0f;
+        q[g][j] = g < group ? Q[(size_t)b * nq_heads * HD + (size_t)(kvh * group + g) * HD +
+                                j * 32 + lane]
+                            : 0.0f;
+      }
+    }
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % BD_STAGES;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&sh->full[s], (t / BD_STAGES) & 1,
+                                                        &sh->abort_flag, res, 31, wait_ns));
+      if (!ok) break;
+      const KT* tile = reinterpret_cast<const KT*>(ring + (size_t)s * SB);
+      const int q0 = p0 + t * BD_TILE;
 #pragma unroll
-      for (int j = 0; j < DPL; ++j) o[g][j] = fmaf(pe, vf[j], o[g][j] * corr);
-      m[g] = mn;
+      for (int i = 0; i < BD_TILE / 8; ++i) {
+        const int pi = warp + 8 * i;  // position within the tile
+        if (q0 + pi >= p1) break;     // warp-uniform
+        const KT* kr = tile + (size_t)pi * 2 * HD;
+        float kf[DPL], vf[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+          kf[j] = (float)kr[j * 32 + lane];
+          vf[j] = (float)kr[HD + j * 32 + lane];
+        }
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+          if (g >= group) break;  // uniform
+          float d = 0.0f;
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) d = fmaf(q[g][j], kf[j], d);
+          d = warp_sum(d);
+          const float sc = __fmul_rn(d, scale);
+          const float mn = fmaxf(m[g], sc);
+          const float corr = expf(m[g] - mn);  // 0 while m is -inf
+          const float pe = expf(sc - mn);
+          l[g] = fmaf(l[g], corr, pe);
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) o[g][j] = fmaf(pe, vf[j], o[g][j] * corr);
+          m[g] = mn;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty[s]);
     }
   }
-#pragma unroll
-  for (int g = 0; g < MAXG; ++g) {
-    if (g >= group) break;
-    if (lane == 0) {
-      sm_m[warp][g] = m[g];
-      sm_l[warp][g] = l[g];
+  // after an abort: the producer has stopped, then the last copy issued to
+  // each stage has landed (earlier ones were consumed before the refill)
+  if (*(volatile int*)&sh->abort_flag && threadIdx.x == 0) {
+    const uint64_t t_start = gtime();
+    while (!*(volatile int*)&sh->producer_done && gtime() - t_start < 100000000ull) {
     }
+    const int issued = *(volatile int*)&sh->issued;
+    for (int s2 = 0; s2 < BD_STAGES && s2 < issued; ++s2) {
+      const int t = s2 + ((issued - 1 - s2) / BD_STAGES) * BD_STAGES;
+      int dummy = 0;
+      mbar_wait(&sh->full[s2], (t / BD_STAGES) & 1, &dummy, res, 32, 100000000ull);
+    }
+  }
+  __syncthreads();  // every copy consumed (or drained): the ring is free
+  if (*(volatile int*)&sh->abort_flag) return;
+  if (warp < 8) {
 #pragma unroll
-    for (int j = 0; j < DPL; ++j) sm_o[warp][g][j * 32 + lane] = o[g][j];
+    for (int g = 0; g < GP; ++g) {
+      if (g >= group) break;
+      if (lane == 0) {
+        sh->m[warp][g] = m[g];
+        sh->l[warp][g] = l[g];
+      }
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) sm_o[warp][g][j * 32 + lane] = o[g][j];
+    }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < group * HD; e += 256) {
+  for (int e = threadIdx.x; e < group * HD; e += BD_THREADS) {
     const int g = e / HD, d = e % HD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) M = fmaxf(M, sm_m[w][g]);
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, sh->m[w][g]);
     float L = 0.0f, O = 0.0f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
-        const float f = sm_m[w][g] == -INFINITY ? 0.0f : expf(sm_m[w][g] - M);
-        L = fmaf(sm_l[w][g], f, L);
+        const float f = sh->m[w][g] == -INFINITY ? 0.0f : expf(sh->m[w][g] - M);
+        L = fmaf(sh->l[w][g], f, L);
         O = fmaf(sm_o[w][g][d], f, O);
       }
     }

@@ -2303,6 +2303,24 @@ static int gemm_setup() {
     SETPF(64, __half);
     SETPF(128, __half);
 #undef SETPF
+#define SETBD(HD, GP, KT)                                                                  \
+  if (e == cudaSuccess)                                                                    \
+  e = cudaFuncSetAttribute(k_bd_attention<HD, GP, KT>,                                     \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
+                           bd_smem_bytes(HD, (int)sizeof(KT), GP))
+#define SETBD_G(HD, KT) \
+  SETBD(HD, 1, KT);     \
+  SETBD(HD, 2, KT);     \
+  SETBD(HD, 4, KT);     \
+  SETBD(HD, 8, KT)
+    SETBD_G(32, float);
+    SETBD_G(64, float);
+    SETBD_G(128, float);
+    SETBD_G(32, __half);
+    SETBD_G(64, __half);
+    SETBD_G(128, __half);
+#undef SETBD_G
+#undef SETBD
     rc = e == cudaSuccess ? L3G_OK
                           : l3g_fail(L3G_E_CUDA, "gemm kernel attributes: %s", cudaGetErrorString(e));
   });
@@ -2816,22 +2834,34 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
     }
     {
       const dim3 grid(splits, m->hkv_l, n);
-#define BDATT(HD)                                                                           \
-  if (m->kv_f16)                                                                           \
-    k_bd_attention<HD, __half><<<grid, 256, 0, st>>>(b->q, b->d_seq, l, m->group, m->hq_l, \
-                                                      scale, b->part_o, b->part_ml,        \
-                                                      b->max_splits);                      \
-  else                                                                                     \
-    k_bd_attention<HD, float><<<grid, 256, 0, st>>>(b->q, b->d_seq, l, m->group, m->hq_l,  \
-                                                     scale, b->part_o, b->part_ml,         \
-                                                     b->max_splits)
+      const int gp = m->group <= 1 ? 1 : m->group <= 2 ? 2 : m->group <= 4 ? 4 : 8;
+#define BDATT(HD, GP)                                                                         \
+  if (m->kv_f16)                                                                             \
+    k_bd_attention<HD, GP, __half><<<grid, BD_THREADS, bd_smem_bytes(HD, 2, GP), st>>>(      \
+        b->q, b->d_seq, l, m->group, m->hq_l, scale, b->part_o, b->part_ml, b->max_splits,     \
+        b->d_res, wait_ns);                                                                   \
+  else                                                                                       \
+    k_bd_attention<HD, GP, float><<<grid, BD_THREADS, bd_smem_bytes(HD, 4, GP), st>>>(       \
+        b->q, b->d_seq, l, m->group, m->hq_l, scale, b->part_o, b->part_ml, b->max_splits,     \
+        b->d_res, wait_ns)
+#define BDATT_G(HD)          \
+  if (gp == 1) {             \
+    BDATT(HD, 1);            \
+  } else if (gp == 2) {      \
+    BDATT(HD, 2);            \
+  } else if (gp == 4) {      \
+    BDATT(HD, 4);            \
+  } else {                   \
+    BDATT(HD, 8);            \
+  }
       if (hd == 32) {
-        BDATT(32);
+        BDATT_G(32)
       } else if (hd == 64) {
-        BDATT(64);
+        BDATT_G(64)
       } else {
-        BDATT(128);
+        BDATT_G(128)
       }
+#undef BDATT_G
 #undef BDATT
       CUDA_TRY(cudaGetLastError());
       k_bd_merge<<<dim3(m->hq_l, n), 128, 0, st>>>(b->part_o, b->part_ml, b->d_seq, m->hq_l, hd,
