@@ -55,8 +55,10 @@ __device__ __forceinline__ void tmem_wait_ld() {
 struct GemmArgs {
   const uint8_t* a;   // weight chunks [row tiles][nk] (gemm::A_CHUNK bytes each)
   const uint8_t* b;   // activation chunks [token tiles][nk] (gemm::b_chunk(NT) each)
-  float* out;         // [n_tok][ldo], columns [0, rows) written
+  float* out;         // [n_tok][ldo], columns [0, rows) written (ksplit == 1)
   int rows, ldo, n_tok, nk, n_rt, n_tt;
+  int ksplit;         // K split into ksplit equal ranges of nk / ksplit chunks
+  float* part;        // ksplit > 1: partial sums [ksplit][n_tok][rows]
   int nstages;
   Result* res;
   unsigned long long wait_ns;
@@ -92,9 +94,10 @@ static_assert(sizeof(GemmSmem) <= gemm::SMEM_HEAD, "gemm smem head");
 // weight rows, and columns of its half of the token tile), rescale them by
 // d_w * d_x and accumulate in fp32 registers, then release the buffer.  A
 // stage is refilled once its four MMAs have completed and all eight rescale
-// warps have read its scales.  Tiles (row tile, token tile) are dealt
-// round-robin over the grid; after the last chunk of a tile the rescale warps
-// store its outputs.
+// warps have read its scales.  Work units (row tile, token tile, K range)
+// are dealt round-robin over the grid; after the last chunk of a unit the
+// rescale warps store its outputs, or with a split K its partial sums
+// (k_gemm_reduce adds them in split order).
 template <int NT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_q8(const __grid_constant__ GemmArgs g) {
@@ -111,10 +114,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* ring = smem + SMEM_HEAD;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ns = g.nstages;
-  const int n_tiles = g.n_rt * g.n_tt;
+  const int nku = g.nk / g.ksplit;  // chunks per unit
+  const int n_units = g.n_rt * g.n_tt * g.ksplit;
   const int G = (int)gridDim.x, cta = (int)blockIdx.x;
-  const int my_tiles = cta < n_tiles ? (n_tiles - cta + G - 1) / G : 0;
-  const int nchunks = my_tiles * g.nk;
+  const int my_units = cta < n_units ? (n_units - cta + G - 1) / G : 0;
+  const int nchunks = my_units * nku;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
@@ -141,13 +145,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 0) {
     // ---- producer -------------------------------------------------------
     if (lane == 0) {
+      // the CTA's c-th chunk: unit cta + (c / nku) * G, chunk (c % nku) of its range
       auto a_src = [&](int c) {
-        const int tile = cta + (c / g.nk) * G;
-        return g.a + ((size_t)(tile % g.n_rt) * g.nk + (c % g.nk)) * A_CHUNK;
+        const int u = cta + (c / nku) * G;
+        const int tile = u / g.ksplit, kc = (u % g.ksplit) * nku + c % nku;
+        return g.a + ((size_t)(tile % g.n_rt) * g.nk + kc) * A_CHUNK;
       };
       auto b_src = [&](int c) {
-        const int tile = cta + (c / g.nk) * G;
-        return g.b + ((size_t)(tile / g.n_rt) * g.nk + (c % g.nk)) * b_chunk(NT);
+        const int u = cta + (c / nku) * G;
+        const int tile = u / g.ksplit, kc = (u % g.ksplit) * nku + c % nku;
+        return g.b + ((size_t)(tile / g.n_rt) * g.nk + kc) * b_chunk(NT);
       };
       const int pre = nchunks < ns ? nchunks : ns;
       for (int c = 0; c < pre; ++c) {
@@ -210,13 +217,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * CPT);
     int c = 0, blk = 0;
     bool ok = true;
-    for (int ti = 0; ti < my_tiles && ok; ++ti) {
-      const int tile = cta + ti * G;
+    for (int ui = 0; ui < my_units && ok; ++ui) {
+      const int u = cta + ui * G;
+      const int tile = u / g.ksplit, ks = u % g.ksplit;
       const int rt = tile % g.n_rt, tt = tile / g.n_rt;
       float acc[CPT];
 #pragma unroll
       for (int i = 0; i < CPT; ++i) acc[i] = 0.0f;
-      for (int kc = 0; kc < g.nk; ++kc, ++c) {
+      for (int kc = 0; kc < nku; ++kc, ++c) {
         const int s = c % ns;
         ok = __all_sync(0xffffffffu, mbar_wait(&sh->full[s], (c / ns) & 1, &sh->abort_flag,
                                                g.res, 24, g.wait_ns));
@@ -252,10 +260,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!ok) break;
       const int row = rt * TILE_M + m;
       if (row < g.rows) {
+        float* dst = g.ksplit > 1 ? g.part + (size_t)ks * g.n_tok * g.rows : g.out;
+        const int ld = g.ksplit > 1 ? g.rows : g.ldo;
 #pragma unroll
         for (int i = 0; i < CPT; ++i) {
           const int n = tt * NT + half * CPT + i;
-          if (n < g.n_tok) g.out[(size_t)n * g.ldo + row] = acc[i];
+          if (n < g.n_tok) dst[(size_t)n * ld + row] = acc[i];
         }
       }
     }
@@ -281,6 +291,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __syncwarp();
     tmem_dealloc(tmem, TCOLS);
   }
+}
+
+// out[n][r] = sum over k of part[k][n][r], k in order (deterministic).
+__global__ void k_gemm_reduce(const float* part, int ksplit, int n_tok, int rows, int ldo,
+                              float* out) {
+  const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (long long)n_tok * rows) return;
+  const int n = (int)(e / rows), r = (int)(e % rows);
+  float v = part[e];
+  for (int k = 1; k < ksplit; ++k) v += part[(size_t)k * n_tok * rows + e];
+  out[(size_t)n * ldo + r] = v;
 }
 
 // QuantizeQ8_0Into (q8_0.go:22-79) of n_tok rows of x [n_tok][cols] into the

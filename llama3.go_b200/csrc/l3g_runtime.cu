@@ -971,6 +971,8 @@ struct l3g_workspace {
   float* pf_att = nullptr;  // [pf_cap][local q heads * hd] attention output
   float* pf_ug = nullptr;   // [pf_cap][2 * local n_ff] interleaved up/gate
   uint8_t* pf_act = nullptr;  // activation chunks of the batched product
+  float* pf_part = nullptr;   // split-K partial sums of the product
+  size_t pf_part_floats = 0;
 };
 
 static void ws_release(l3g_workspace* ws) {
@@ -991,7 +993,7 @@ static void ws_release(l3g_workspace* ws) {
   for (void* p : dptrs)
     if (p) cudaFree(p);
   void* pf[] = {ws->pf_ids, ws->pf_x, ws->pf_y, ws->pf_qkv, ws->pf_q, ws->pf_att, ws->pf_ug,
-                ws->pf_act};
+                ws->pf_act, ws->pf_part};
   for (void* p : pf)
     if (p) cudaFree(p);
   void* hptrs[] = {ws->h_io, ws->h_res, ws->h_logits, ws->h_tk_ids, ws->h_tk_logits, ws->h_samp};
@@ -2237,9 +2239,33 @@ extern "C" int l3g_quantize_q8_0(const float* x, int32_t n, float* d, int8_t* qs
 // ---------------------------------------------------------------------------
 // One batched product out[n][r] (n < n_tok) on stream st: one CTA per SM at
 // most, tiles dealt round-robin.
+// K split of a product with few (row tile, token tile) tiles: the largest
+// divisor of the chunk count that keeps the units within the SM count and
+// the partial sums within part_floats (1: no split).
+static int gemm_ksplit(const GemmMat& w, int n_tok, int nsm, size_t part_floats) {
+  const int nt = gemm::token_tile(n_tok);
+  const long long tiles = (long long)w.n_rt * ((n_tok + nt - 1) / nt);
+  if (part_floats == 0 || tiles >= nsm) return 1;
+  const long long want = nsm / tiles;
+  int best = 1;
+  for (int d = 2; d <= w.nk && d <= want; ++d)
+    if (w.nk % d == 0 && (size_t)d * n_tok * w.rows <= part_floats) best = d;
+  return best;
+}
+// Partial-sum floats that gemm_ksplit can ask of matrix w for up to cap tokens.
+static size_t gemm_part_bound(const GemmMat& w, int cap, int nsm) {
+  if (!w.data) return 0;
+  const long long d = std::min<long long>(w.nk, std::max(1, nsm / std::max(1, w.n_rt)));
+  return d > 1 ? (size_t)d * cap * w.rows : 0;
+}
+
+// One batched product out[n][r] (n < n_tok) on stream st: one CTA per SM at
+// most, work units dealt round-robin; with few tiles the K range is split
+// over more CTAs (partial sums in part, then k_gemm_reduce).
 static cudaError_t launch_gemm(const GemmMat& w, const uint8_t* act, int n_tok, float* out,
                                Result* res, unsigned long long wait_ns, int nsm,
-                               cudaStream_t st, int ldo = 0) {
+                               cudaStream_t st, int ldo = 0, float* part = nullptr,
+                               size_t part_floats = 0) {
   const int nt = gemm::token_tile(n_tok);
   GemmArgs g{};
   g.a = w.data;
@@ -2251,18 +2277,27 @@ static cudaError_t launch_gemm(const GemmMat& w, const uint8_t* act, int n_tok, 
   g.nk = w.nk;
   g.n_rt = w.n_rt;
   g.n_tt = (n_tok + nt - 1) / nt;
+  g.ksplit = part ? gemm_ksplit(w, n_tok, nsm, part_floats) : 1;
+  g.part = part;
   g.nstages = gemm::stages(nt);
   g.res = res;
   g.wait_ns = wait_ns;
-  const long long tiles = (long long)g.n_rt * g.n_tt;
-  const int grid = (int)std::max<long long>(1, std::min<long long>(nsm, tiles));
+  const long long units = (long long)g.n_rt * g.n_tt * g.ksplit;
+  const int grid = (int)std::max<long long>(1, std::min<long long>(nsm, units));
   switch (nt) {
     case 16: k_gemm_q8<16><<<grid, GEMM_THREADS, gemm::smem_bytes(16), st>>>(g); break;
     case 32: k_gemm_q8<32><<<grid, GEMM_THREADS, gemm::smem_bytes(32), st>>>(g); break;
     case 64: k_gemm_q8<64><<<grid, GEMM_THREADS, gemm::smem_bytes(64), st>>>(g); break;
     default: k_gemm_q8<128><<<grid, GEMM_THREADS, gemm::smem_bytes(128), st>>>(g); break;
   }
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && g.ksplit > 1) {
+    const long long n = (long long)n_tok * w.rows;
+    k_gemm_reduce<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, g.ksplit, n_tok, w.rows,
+                                                               g.ldo, out);
+    e = cudaGetLastError();
+  }
+  return e;
 }
 
 struct l3g_gemm_matrix {
@@ -2521,6 +2556,12 @@ static int ensure_prefill_buffers(l3g_workspace* ws) {
   if (e == cudaSuccess) e = cudaMalloc(&ws->pf_act, act_bytes);
   // padding tokens and columns of the activation chunks are never written
   if (e == cudaSuccess) e = cudaMemset(ws->pf_act, 0, act_bytes);
+  size_t part = 0;
+  for (const auto& L : m->layers)
+    for (const GemmMat* g : {&L.gqkv, &L.gwo, &L.gupgate, &L.gdown})
+      part = std::max(part, gemm_part_bound(*g, cap, m->nsm));
+  if (e == cudaSuccess && part) e = cudaMalloc(&ws->pf_part, part * 4);
+  ws->pf_part_floats = e == cudaSuccess ? part : 0;
   if (e != cudaSuccess)
     return l3g_fail(L3G_E_CUDA, "prefill buffers: %s", cudaGetErrorString(e));
   ws->pf_cap = cap;
@@ -2566,7 +2607,8 @@ static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
     k_pf_rms_quant<<<P, PF_THREADS, 0, st>>>(ws->pf_x, l ? ws->pf_y : nullptr, L.attn_norm,
                                             hp.rms_eps, ne, nt, gemm::chunks(ne), act);
     CUDA_TRY(cudaGetLastError());
-    CUDA_TRY(launch_gemm(L.gqkv, act, P, ws->pf_qkv, ws->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gqkv, act, P, ws->pf_qkv, ws->d_res, wait_ns, m->nsm, st, 0,
+                         ws->pf_part, ws->pf_part_floats));
     {  // RoPE + KV append, infer.go:76-127
       const long long pairs = (long long)P * ((nq + 2 * nkv) / 2);
       k_pf_qkv_rope<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
@@ -2589,7 +2631,8 @@ static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
           ws->pf_att, P, nq, nt, gemm::chunks(nq), (P + nt - 1) / nt * nt, act);
       CUDA_TRY(cudaGetLastError());
     }
-    CUDA_TRY(launch_gemm(L.gwo, act, P, ws->pf_y, ws->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gwo, act, P, ws->pf_y, ws->d_res, wait_ns, m->nsm, st, 0, ws->pf_part,
+                         ws->pf_part_floats));
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->pf_y, ws->pf_y, (size_t)P * ne, ncclFloat, ncclSum, m->comm,
                                  st));
@@ -2598,7 +2641,8 @@ static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
     k_pf_rms_quant<<<P, PF_THREADS, 0, st>>>(ws->pf_x, ws->pf_y, L.ffn_norm, hp.rms_eps, ne, nt,
                                             gemm::chunks(ne), act);
     CUDA_TRY(cudaGetLastError());
-    CUDA_TRY(launch_gemm(L.gupgate, act, P, ws->pf_ug, ws->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gupgate, act, P, ws->pf_ug, ws->d_res, wait_ns, m->nsm, st, 0,
+                         ws->pf_part, ws->pf_part_floats));
     {
       const long long warps = (long long)P * (m->ff_l / 32);
       k_pf_swiglu_quant<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
@@ -2606,7 +2650,8 @@ static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
       CUDA_TRY(cudaGetLastError());
     }
     // down, infer.go:235-246 (its residual add opens the next layer)
-    CUDA_TRY(launch_gemm(L.gdown, act, P, ws->pf_y, ws->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gdown, act, P, ws->pf_y, ws->d_res, wait_ns, m->nsm, st, 0, ws->pf_part,
+                         ws->pf_part_floats));
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(ws->pf_y, ws->pf_y, (size_t)P * ne, ncclFloat, ncclSum, m->comm,
                                  st));
@@ -2679,6 +2724,8 @@ struct l3g_batch {
   float* part_o = nullptr;   // [cap][local q heads][max_splits][hd]
   float* part_ml = nullptr;  // [cap][local q heads][max_splits][2]
   uint8_t* act = nullptr;
+  float* part = nullptr;         // split-K partial sums of the product
+  size_t part_floats = 0;
   uint64_t* tk_part = nullptr;  // [cap][tk_chunks][MAX_TOPK]
   int* tk_ids = nullptr;        // [cap][MAX_TOPK]
   float* tk_logits = nullptr;
@@ -2689,7 +2736,7 @@ extern "C" void l3g_batch_free(l3g_batch* b) {
   cudaSetDevice(b->device);
   void* d[] = {b->d_seq, b->d_out, b->d_res, b->x, b->y, b->qkv, b->q, b->att, b->ug,
                b->logits, b->logits_full, b->part_o, b->part_ml, b->act, b->tk_part,
-               b->tk_ids, b->tk_logits};
+               b->tk_ids, b->tk_logits, b->part};
   for (void* p : d)
     if (p) cudaFree(p);
   void* h[] = {b->h_seq, b->h_out, b->h_res};
@@ -2758,6 +2805,14 @@ extern "C" int l3g_batch_new(l3g_model* m, int32_t max_seqs, l3g_batch** out) {
   if (e == cudaSuccess) e = cudaMalloc(&b->tk_part, cap * b->tk_chunks * MAX_TOPK * 8);
   if (e == cudaSuccess) e = cudaMalloc(&b->tk_ids, cap * MAX_TOPK * 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->tk_logits, cap * MAX_TOPK * 4);
+  if (e == cudaSuccess) {
+    size_t part = gemm_part_bound(m->glogits, max_seqs, m->nsm);
+    for (const auto& L : m->layers)
+      for (const GemmMat* g : {&L.gqkv, &L.gwo, &L.gupgate, &L.gdown})
+        part = std::max(part, gemm_part_bound(*g, max_seqs, m->nsm));
+    if (part) e = cudaMalloc(&b->part, part * 4);
+    b->part_floats = e == cudaSuccess ? part : 0;
+  }
   if (e == cudaSuccess) {  // the shard's padding columns (past its vocabulary rows) stay -inf
     std::vector<float> ninf(cap * m->v_l, -INFINITY);
     e = cudaMemcpy(b->logits, ninf.data(), ninf.size() * 4, cudaMemcpyHostToDevice);
@@ -2825,7 +2880,8 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
     k_pf_rms_quant<<<n, PF_THREADS, 0, st>>>(b->x, l ? b->y : nullptr, L.attn_norm, hp.rms_eps,
                                             ne, nt, gemm::chunks(ne), b->act);
     CUDA_TRY(cudaGetLastError());
-    CUDA_TRY(launch_gemm(L.gqkv, b->act, n, b->qkv, b->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gqkv, b->act, n, b->qkv, b->d_res, wait_ns, m->nsm, st, 0, b->part,
+                         b->part_floats));
     {
       const long long pairs = (long long)n * ((nq + 2 * nkv) / 2);
       k_bd_qkv_rope<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
@@ -2874,20 +2930,23 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
           b->att, n, nq, nt, gemm::chunks(nq), n_pad, b->act);
       CUDA_TRY(cudaGetLastError());
     }
-    CUDA_TRY(launch_gemm(L.gwo, b->act, n, b->y, b->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gwo, b->act, n, b->y, b->d_res, wait_ns, m->nsm, st, 0, b->part,
+                         b->part_floats));
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(b->y, b->y, (size_t)n * ne, ncclFloat, ncclSum, m->comm, st));
     k_pf_rms_quant<<<n, PF_THREADS, 0, st>>>(b->x, b->y, L.ffn_norm, hp.rms_eps, ne, nt,
                                             gemm::chunks(ne), b->act);
     CUDA_TRY(cudaGetLastError());
-    CUDA_TRY(launch_gemm(L.gupgate, b->act, n, b->ug, b->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gupgate, b->act, n, b->ug, b->d_res, wait_ns, m->nsm, st, 0, b->part,
+                         b->part_floats));
     {
       const long long warps = (long long)n * (m->ff_l / 32);
       k_pf_swiglu_quant<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
           b->ug, n, m->ff_l, nt, gemm::chunks(m->ff_l), b->act);
       CUDA_TRY(cudaGetLastError());
     }
-    CUDA_TRY(launch_gemm(L.gdown, b->act, n, b->y, b->d_res, wait_ns, m->nsm, st));
+    CUDA_TRY(launch_gemm(L.gdown, b->act, n, b->y, b->d_res, wait_ns, m->nsm, st, 0, b->part,
+                         b->part_floats));
     if (m->world > 1)
       NCCL_TRY(nccl()->AllReduce(b->y, b->y, (size_t)n * ne, ncclFloat, ncclSum, m->comm, st));
   }
@@ -2895,7 +2954,8 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
   k_pf_rms_quant<<<n, PF_THREADS, 0, st>>>(b->x, b->y, m->out_norm, hp.rms_eps, ne, nt,
                                           gemm::chunks(ne), b->act);
   CUDA_TRY(cudaGetLastError());
-  CUDA_TRY(launch_gemm(m->glogits, b->act, n, b->logits, b->d_res, wait_ns, m->nsm, st, m->v_l));
+  CUDA_TRY(launch_gemm(m->glogits, b->act, n, b->logits, b->d_res, wait_ns, m->nsm, st, m->v_l,
+                         b->part, b->part_floats));
   const float* lg = b->logits;
   if (m->world > 1) {
     NCCL_TRY(nccl()->AllGather(b->logits, b->logits_full, (size_t)n * m->v_l, ncclFloat, m->comm,

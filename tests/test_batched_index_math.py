@@ -13,7 +13,11 @@ it must compute:
   0..pos (float64 restatement of infer.go:130-175) within 1e-5;
 - k_pf_attention (csrc/l3g_prefill.cuh): query blocks of 64 / group
   positions, key tiles of 32 with the causal limit of each row, online
-  softmax, for a pass starting above position zero.
+  softmax, for a pass starting above position zero;
+- k_gemm_q8's work units with a split K (gemm_ksplit, the producer's and the
+  rescale warps' chunk sequences): every (row tile, token tile, chunk) is
+  visited exactly once, both roles walk the same sequence per CTA, and each
+  unit owns one partial-sum slot.
 """
 import numpy as np
 import pytest
@@ -205,3 +209,65 @@ def test_causal_prefill_attention_replay(P, pos0, group, hd):
             lim = pos0 + p + 1
             want = _attention_f64(Q[p, g], K[:lim], V[:lim], scale)
             assert np.abs(got[p, g] - want).max() < 1e-5 * max(1.0, np.abs(want).max()), (p, g)
+
+
+def gemm_ksplit(n_rt, nk, n_tok, rows, nsm, part_floats):
+    """gemm_ksplit (l3g_runtime.cu), transcribed."""
+    nt = 16 if n_tok <= 16 else 32 if n_tok <= 32 else 64 if n_tok <= 64 else 128
+    tiles = n_rt * (-(-n_tok // nt))
+    if part_floats == 0 or tiles >= nsm:
+        return 1
+    want = nsm // tiles
+    best = 1
+    for d in range(2, nk + 1):
+        if d > want:
+            break
+        if nk % d == 0 and d * n_tok * rows <= part_floats:
+            best = d
+    return best
+
+
+@pytest.mark.parametrize("rows,cols,n_tok,nsm", [(768, 4096, 64, 148), (4096, 1792, 64, 148),
+                                                 (4096, 512, 5, 148), (3584, 4096, 64, 148),
+                                                 (6144, 4096, 512, 148), (200, 288, 17, 8)])
+def test_split_k_units_cover_every_chunk_once(rows, cols, n_tok, nsm):
+    """k_gemm_q8's work units: the producer's and the rescale warps' chunk
+    sequences (transcribed) visit every (row tile, token tile, chunk) exactly
+    once, in the same order per CTA, and each unit's partial sums go to its
+    own K range slot."""
+    nt = 16 if n_tok <= 16 else 32 if n_tok <= 32 else 64 if n_tok <= 64 else 128
+    n_rt, n_tt, nk = -(-rows // 128), -(-n_tok // nt), -(-cols // 128)
+    ks = gemm_ksplit(n_rt, nk, n_tok, rows, nsm, part_floats=10**9)
+    assert nk % ks == 0
+    nku = nk // ks
+    n_units = n_rt * n_tt * ks
+    G = max(1, min(nsm, n_units))
+    seen = {}
+    for cta in range(G):
+        my_units = -(-(n_units - cta) // G) if cta < n_units else 0
+        prod = []
+        for c in range(my_units * nku):  # producer (a_src / b_src)
+            u = cta + (c // nku) * G
+            tile, kc = u // ks, (u % ks) * nku + c % nku
+            prod.append((tile % n_rt, tile // n_rt, kc))
+        epi = []
+        for ui in range(my_units):       # rescale warps
+            u = cta + ui * G
+            tile, k = u // ks, u % ks
+            for kc in range(nku):
+                epi.append((tile % n_rt, tile // n_rt, k * nku + kc))
+            slot = (tile, k)
+            assert slot not in seen
+            seen[slot] = cta
+        assert prod == epi
+    cover = {}
+    for cta in range(G):
+        my_units = -(-(n_units - cta) // G) if cta < n_units else 0
+        for c in range(my_units * nku):
+            u = cta + (c // nku) * G
+            tile, kc = u // ks, (u % ks) * nku + c % nku
+            cover[(tile, kc)] = cover.get((tile, kc), 0) + 1
+    assert len(cover) == n_rt * n_tt * nk and set(cover.values()) == {1}
+    want = nsm // (n_rt * n_tt)
+    if any(nk % d == 0 for d in range(2, min(nk, want) + 1)):
+        assert ks > 1  # few tiles: the K range is split when a divisor fits
