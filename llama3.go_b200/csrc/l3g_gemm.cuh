@@ -52,6 +52,40 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic: two IEEE round-to-nearest
+// operations per instruction, the same results as two scalar ones).
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(unsigned long long r) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+  return make_float2(a, b);
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
+                                                   unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// An int32 block sum (|v| < 2^22: at most 32 * 128 * 128) as fp32, exactly,
+// without the conversion unit: the bits of 1.5 * 2^23 + v, minus 1.5 * 2^23
+// (the second step is the caller's packed add of -1.5 * 2^23).
+constexpr int GEMM_BIAS_BITS = 0x4B400000;
+constexpr float GEMM_BIAS = 12582912.0f;
+
 struct GemmArgs {
   const uint8_t* a;   // weight chunks [row tiles][nk] (gemm::A_CHUNK bytes each)
   const uint8_t* b;   // activation chunks [token tiles][nk] (gemm::b_chunk(NT) each)
@@ -221,9 +255,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int u = cta + ui * G;
       const int tile = u / g.ksplit, ks = u % g.ksplit;
       const int rt = tile % g.n_rt, tt = tile / g.n_rt;
-      float acc[CPT];
+      unsigned long long acc2[CPT / 2];  // fp32 pairs (columns 2i, 2i + 1)
 #pragma unroll
-      for (int i = 0; i < CPT; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < CPT / 2; ++i) acc2[i] = 0ull;
       for (int kc = 0; kc < nku; ++kc, ++c) {
         const int s = c % ns;
         ok = __all_sync(0xffffffffu, mbar_wait(&sh->full[s], (c / ns) & 1, &sh->abort_flag,
@@ -247,11 +281,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sh->tempty[buf]);
+          // acc += float(I) * (d_w * d_x), per column, as fmaf(I, d_w * d_x, acc)
           const float w = __half2float(dw[j * TILE_M + m]);
-          const float* dxj = dx + j * NT + half * CPT;
+          const unsigned long long w2 = pk2(w, w);
+          const unsigned long long nbias2 = pk2(-GEMM_BIAS, -GEMM_BIAS);
+          const float2* dxj = reinterpret_cast<const float2*>(dx + j * NT + half * CPT);
 #pragma unroll
-          for (int i = 0; i < CPT; ++i)
-            acc[i] = fmaf((float)(int)v[i], __fmul_rn(w, dxj[i]), acc[i]);
+          for (int i = 0; i < CPT / 2; ++i) {
+            const float2 d2 = dxj[i];
+            const unsigned long long s2 = mul2(w2, pk2(d2.x, d2.y));
+            const unsigned long long f2 =
+                add2(pk2(__int_as_float((int)v[2 * i] + GEMM_BIAS_BITS),
+                         __int_as_float((int)v[2 * i + 1] + GEMM_BIAS_BITS)),
+                     nbias2);
+            acc2[i] = fma2(f2, s2, acc2[i]);
+          }
         }
         if (!ok) break;
         __syncwarp();
@@ -263,9 +307,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         float* dst = g.ksplit > 1 ? g.part + (size_t)ks * g.n_tok * g.rows : g.out;
         const int ld = g.ksplit > 1 ? g.rows : g.ldo;
 #pragma unroll
-        for (int i = 0; i < CPT; ++i) {
-          const int n = tt * NT + half * CPT + i;
-          if (n < g.n_tok) dst[(size_t)n * ld + row] = acc[i];
+        for (int i = 0; i < CPT / 2; ++i) {
+          const float2 a2 = upk2(acc2[i]);
+          const int n = tt * NT + half * CPT + 2 * i;
+          if (n < g.n_tok) dst[(size_t)n * ld + row] = a2.x;
+          if (n + 1 < g.n_tok) dst[(size_t)(n + 1) * ld + row] = a2.y;
         }
       }
     }

@@ -213,3 +213,13 @@ def test_repack_and_size_errors():
         l3g.gemm_act_bytes(0, 128)
     with pytest.raises(l3g.L3GError, match="do not match"):
         l3g.gemm_repack(np.zeros(10, np.uint8), 1, 32)
+
+
+def test_bias_conversion_is_exact():
+    """k_gemm_q8 turns each int32 block sum v into fp32 as the bits of
+    1.5 * 2^23 + v minus 1.5 * 2^23; every |v| < 2^22 (a Q8_0 block sum is at
+    most 32 * 128 * 128 = 2^19) comes back exactly."""
+    v = np.arange(-(1 << 22) + 1, 1 << 22, dtype=np.int32)
+    f = (v + np.int32(0x4B400000)).view(np.float32) - np.float32(12582912.0)
+    assert np.array_equal(f, v.astype(np.float32))
+    assert 32 * 128 * 128 < (1 << 22)
