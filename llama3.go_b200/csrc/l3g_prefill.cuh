@@ -237,29 +237,60 @@ __global__ void __launch_bounds__(256) k_pf_attention(const float* Q, const void
       vs[key][d] = vval;
     }
     __syncthreads();
+    // this warp's rows r0 .. r0 + nr - 1 (warp-uniform); every key and value
+    // element read from shared memory serves all of them
+    const int r0 = warp * RW;
+    const int nr = min(RW, R - r0);
+    if (nr > 0) {
+      float sdot[RW];
 #pragma unroll
-    for (int i = 0; i < RW; ++i) {
-      const int r = warp * RW + i;
-      if (r >= R) break;  // warp-uniform
-      const int limit = pos0 + tok0 + r / group;  // causal: keys <= own position
-      float sdot = 0.0f;
-#pragma unroll 8
-      for (int d = 0; d < HD; ++d) sdot = fmaf(qs[r][d], kt[d][lane], sdot);
+      for (int i = 0; i < RW; ++i) sdot[i] = 0.0f;
+#pragma unroll 2
+      for (int d = 0; d < HD; d += 4) {
+        const float k0 = kt[d][lane], k1 = kt[d + 1][lane], k2 = kt[d + 2][lane],
+                    k3 = kt[d + 3][lane];
+#pragma unroll
+        for (int i = 0; i < RW; ++i) {
+          if (i < nr) {
+            const float4 q4 = *reinterpret_cast<const float4*>(&qs[r0 + i][d]);
+            sdot[i] = fmaf(q4.x, k0, sdot[i]);
+            sdot[i] = fmaf(q4.y, k1, sdot[i]);
+            sdot[i] = fmaf(q4.z, k2, sdot[i]);
+            sdot[i] = fmaf(q4.w, k3, sdot[i]);
+          }
+        }
+      }
       const int kp = kb + lane;
-      const bool valid = kp <= limit;
-      const float sc = valid ? __fmul_rn(sdot, scale) : -INFINITY;
-      const float mn = fmaxf(mrow[i], warp_max(sc));
-      const float pe = valid ? expf(sc - mn) : 0.0f;
-      const float corr = mrow[i] == -INFINITY ? 0.0f : expf(mrow[i] - mn);
-      lrow[i] = fmaf(lrow[i], corr, warp_sum(pe));
-      mrow[i] = mn;
+      float pe[RW];
 #pragma unroll
-      for (int j = 0; j < DPL; ++j) o[i][j] *= corr;
+      for (int i = 0; i < RW; ++i) {
+        pe[i] = 0.0f;
+        if (i < nr) {
+          const int limit = pos0 + tok0 + (r0 + i) / group;  // causal: keys <= own position
+          const bool valid = kp <= limit;
+          const float sc = valid ? __fmul_rn(sdot[i], scale) : -INFINITY;
+          const float mn = fmaxf(mrow[i], warp_max(sc));
+          pe[i] = valid ? expf(sc - mn) : 0.0f;
+          const float corr = mrow[i] == -INFINITY ? 0.0f : expf(mrow[i] - mn);
+          lrow[i] = fmaf(lrow[i], corr, warp_sum(pe[i]));
+          mrow[i] = mn;
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) o[i][j] *= corr;
+        }
+      }
 #pragma unroll 4
       for (int key = 0; key < 32; ++key) {
-        const float pk = __shfl_sync(0xffffffffu, pe, key);
+        float vv[DPL];
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) o[i][j] = fmaf(pk, vs[key][j * 32 + lane], o[i][j]);
+        for (int j = 0; j < DPL; ++j) vv[j] = vs[key][j * 32 + lane];
+#pragma unroll
+        for (int i = 0; i < RW; ++i) {
+          if (i < nr) {
+            const float pk = __shfl_sync(0xffffffffu, pe[i], key);
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) o[i][j] = fmaf(pk, vv[j], o[i][j]);
+          }
+        }
       }
     }
   }
