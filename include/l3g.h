@@ -266,6 +266,7 @@ int l3g_workspace_tp_p2p(const l3g_workspace *ws, int32_t *p2p);
 #define L3G_K_LOGITS 6
 #define L3G_K_OTHER 7
 #define L3G_K_ACT_QUANT 8 /* act-quant of the SwiGLU output for down     */
+#define L3G_K_LAYERS 9    /* every layer in one persistent launch         */
 int l3g_profile_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                      int32_t token, int32_t *kinds, float *us, int32_t *n);
 /* Device timeline of one greedy step replayed as its CUDA graph (kernels
@@ -278,6 +279,22 @@ int l3g_profile_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
 int l3g_trace_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                    int32_t token, uint64_t *stamps, int32_t *kinds,
                    int32_t *n);
+
+/* Persistent layer kernel (opt-in: L3G_PERSIST=1 in the environment when the
+ * model is loaded).  It replaces the per-layer launches of a step, i.e. the
+ * per-row-chunk matvec calls and the goroutine fork-join of
+ * ForwardIntoWorkspace's layer loop (infer.go:56-246, workers.go:98-112),
+ * with one launch of one CTA per SM whose layer phases are separated by grid
+ * barriers.  *on = 1 when this workspace's steps use it.  Inspection only. */
+int l3g_workspace_persistent(const l3g_workspace *ws, int32_t *on);
+/* After l3g_trace_step on a workspace that runs the persistent kernel: the
+ * %globaltimer (ns) at which each CTA arrived at and left each grid barrier
+ * of the traced step, out[(b * grid + cta) * 2 + {0, 1}] for barrier b (7 per
+ * layer: after QKV, attention, merge, Wo, up/gate, quantize, down; the last
+ * layer's down has none, so its slots stay 0).  cap is out's length in
+ * 64-bit words.  No reference counterpart (tracing). */
+int l3g_persist_stamps(const l3g_workspace *ws, uint64_t *out, int64_t cap,
+                       int32_t *n_barriers, int32_t *grid);
 
 /* ---- Q8_0 matvec drop-in: matvec_q8_c (simd.h:8) / matVecQ8_0 ------------ */
 /* Uploads a GGUF Q8_0 matrix (rows x cols, 34-byte blocks, host bytes). */

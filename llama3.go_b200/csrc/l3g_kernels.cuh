@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "l3g_gemm_layout.h"
+#include "l3g_persist_plan.h"
 
 namespace l3g {
 
@@ -279,6 +280,8 @@ __device__ __forceinline__ void quant_quad(float4 u, bool live, int blk, int sub
 
 #include "l3g_attention.cuh"
 
+#include "l3g_persist.cuh"
+
 #include "l3g_gemm.cuh"
 
 #include "l3g_prefill.cuh"
@@ -326,12 +329,20 @@ __global__ void k_tp_reduce(const TpExchange t, float* y, Result* res,
 // raw GGUF Q8_0 rows: x[i] = f16(d) * q[i].
 // ---------------------------------------------------------------------------
 // It also advances the workspace's step counter (the epoch base of the
-// tensor-parallel exchange), once per step on every rank.
+// tensor-parallel exchange), once per step on every rank, and, when the step
+// runs the persistent layer kernel, zeroes that kernel's barrier and abort
+// words (bar, nullable): every earlier kernel has completed by then.
 __global__ void k_embed(const uint8_t* emb, int vocab, int cols, const int* io,
-                        float* x, Result* res, unsigned* step) {
+                        float* x, Result* res, unsigned* step, unsigned* bar) {
   pdl_launch_dependents();
   pdl_wait();
-  if (blockIdx.x == 0 && threadIdx.x == 0) *step += 1u;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *step += 1u;
+    if (bar) {
+      bar[0] = 0u;
+      bar[1] = 0u;
+    }
+  }
   const int token = io[0];
   if (token < 0 || token >= vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) report(res, ERR_TOKEN, token);

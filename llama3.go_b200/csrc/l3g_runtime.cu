@@ -198,6 +198,17 @@ static int setup_kernels() {
     SETAT(4, __half);
 #undef SETAT
 #undef SETCL
+#define SETPS(D, T)              \
+  SETK((k_layers<D, T, 1>));     \
+  SETK((k_layers<D, T, 2>));     \
+  SETK((k_layers<D, T, 4>));     \
+  SETK((k_layers<D, T, 8>))
+    SETPS(1, float);
+    SETPS(2, float);
+    SETPS(4, float);
+    SETPS(2, __half);
+    SETPS(4, __half);
+#undef SETPS
     SETK(k_topk_final);
     SETK(k_embed);
     SETK(k_advance);
@@ -247,17 +258,15 @@ struct DevMat {
 static double tile_cost_ns(int tile_bytes) { return 250.0 + tile_bytes / 100.0; }
 
 static Q8Tiles make_tiles(int rows, int cols, int rpw) {
+  const TileGeom g = tile_geometry(rows, cols, rpw, NW, TILE_TARGET);
   Q8Tiles t{};
   t.rows = rows;
   t.cols = cols;
-  t.wr = NW * rpw;
-  const int nb = cols / 32;
-  int nsl = std::max(1, (int)(((long long)cols * t.wr + TILE_TARGET - 1) / TILE_TARGET));
-  while (nb % nsl) ++nsl;
-  t.nslices = nsl;
-  t.ck = cols / nsl;
-  t.tile_bytes = align_up(t.wr * t.ck + t.wr * (t.ck / 32) * 2, 16);
-  t.n_groups = (rows + t.wr - 1) / t.wr;
+  t.wr = g.wr;
+  t.nslices = g.nslices;
+  t.ck = g.ck;
+  t.tile_bytes = g.tile_bytes;
+  t.n_groups = g.n_groups;
   return t;
 }
 
@@ -303,12 +312,13 @@ struct RowSrc {         // rows [row0, row0+n) of a host GGUF Q8_0 tensor
 };
 
 // Uploads the needed source rows, repacks them into tiles on the device.
+// rpw > 0 fixes the rows per warp (the persistent kernel's layout); 0 plans.
 static int upload_tiled(DevMat& out, const RowSrc* segs, int nseg,
                         bool interleave2, int src_cols, int blk0, int cols,
-                        int nsm, size_t* dev_bytes) {
+                        int nsm, size_t* dev_bytes, int rpw = 0) {
   int rows = 0;
   for (int i = 0; i < nseg; ++i) rows += segs[i].n;
-  out.t = plan_tiles(rows, cols, nsm);
+  out.t = rpw > 0 ? make_tiles(rows, cols, rpw) : plan_tiles(rows, cols, nsm);
   finish_plan(out);
   out.bytes = (size_t)out.t.n_groups * out.t.nslices * out.t.tile_bytes;
   CUDA_TRY(cudaMalloc(&out.buf, out.bytes));
@@ -383,6 +393,10 @@ struct l3g_model {
   std::mutex gemm_mu;       // guards the lazy build of the layers' GemmMat
   bool gemm_ready = false;
   GemmMat glogits;          // logits shard as weight chunks (batched decode)
+  // persistent layer kernel (L3G_PERSIST=1 at load): layer matrices tiled
+  // with four rows per warp, and their pointers in a device table
+  bool persist = false;
+  PersistLayer* d_layers = nullptr;
 };
 
 static const l3g_tensor* find_tensor(const l3g_tensor* ts, int n, const char* name) {
@@ -459,6 +473,7 @@ extern "C" void l3g_model_free(l3g_model* m) {
   }
   free_mat(m->logits);
   free_gemm(m->glogits);
+  if (m->d_layers) cudaFree(m->d_layers);
   if (m->out_norm) cudaFree(m->out_norm);
   if (m->emb) cudaFree(m->emb);
   if (m->comm) nccl()->CommDestroy(m->comm);
@@ -577,6 +592,11 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
   m->v_l = sh.vocab_stride;
   m->v_off = sh.vocab_row0;
   m->rope_half = hp.rope_dim / 2;
+  {
+    const char* env = getenv("L3G_PERSIST");
+    m->persist = env && atoi(env) == 1;
+  }
+  const int layer_rpw = m->persist ? 4 : 0;
   auto bail = [&](int code) {
     l3g_model_free(m);
     return code;
@@ -644,21 +664,21 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
     RowSrc qkv[3] = {{wq, sh.q_row0, sh.q_rows},
                      {wk, sh.kv_row0, sh.kv_rows},
                      {wv, sh.kv_row0, sh.kv_rows}};
-    if ((rc = upload_tiled(L.qkv, qkv, 3, false, ne, 0, ne, m->nsm, &m->dev_bytes)))
+    if ((rc = upload_tiled(L.qkv, qkv, 3, false, ne, 0, ne, m->nsm, &m->dev_bytes, layer_rpw)))
       return bail(rc);
     // Wo: all rows, this rank's head columns
     RowSrc wos{wo, 0, ne};
     if ((rc = upload_tiled(L.wo, &wos, 1, false, ne, sh.o_col0 / 32, sh.o_cols, m->nsm,
-                           &m->dev_bytes)))
+                           &m->dev_bytes, layer_rpw)))
       return bail(rc);
     // up/gate interleaved (up_i, gate_i) for this rank's FFN rows
     RowSrc ug[2] = {{wu, sh.ff_row0, sh.ff_rows}, {wg, sh.ff_row0, sh.ff_rows}};
-    if ((rc = upload_tiled(L.upgate, ug, 2, true, ne, 0, ne, m->nsm, &m->dev_bytes)))
+    if ((rc = upload_tiled(L.upgate, ug, 2, true, ne, 0, ne, m->nsm, &m->dev_bytes, layer_rpw)))
       return bail(rc);
     // down: all rows, this rank's FFN columns
     RowSrc ds{wd, 0, ne};
     if ((rc = upload_tiled(L.down, &ds, 1, false, hp.n_ff, sh.down_col0 / 32, sh.down_cols,
-                           m->nsm, &m->dev_bytes)))
+                           m->nsm, &m->dev_bytes, layer_rpw)))
       return bail(rc);
     snprintf(name, sizeof name, "blk.%d.attn_norm.weight", l);
     if ((rc = upload_vector(find_tensor(ts, nt, name), name, ne, &L.attn_norm, &m->dev_bytes)))
@@ -666,6 +686,23 @@ extern "C" int l3g_model_load(const l3g_hparams* hp_in, const l3g_tensor* ts, in
     snprintf(name, sizeof name, "blk.%d.ffn_norm.weight", l);
     if ((rc = upload_vector(find_tensor(ts, nt, name), name, ne, &L.ffn_norm, &m->dev_bytes)))
       return bail(rc);
+  }
+
+  if (m->persist) {  // the persistent kernel's table of layer pointers
+    std::vector<PersistLayer> tab(hp.n_layers);
+    for (int l = 0; l < hp.n_layers; ++l) {
+      const LayerW& L = m->layers[l];
+      tab[l].w[persist::M_QKV] = L.qkv.buf;
+      tab[l].w[persist::M_WO] = L.wo.buf;
+      tab[l].w[persist::M_UPGATE] = L.upgate.buf;
+      tab[l].w[persist::M_DOWN] = L.down.buf;
+      tab[l].attn_norm = L.attn_norm;
+      tab[l].ffn_norm = L.ffn_norm;
+    }
+    const size_t nb = tab.size() * sizeof(PersistLayer);
+    if (cudaMalloc(&m->d_layers, nb) != cudaSuccess ||
+        cudaMemcpy(m->d_layers, tab.data(), nb, cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(l3g_fail(L3G_E_CUDA, "layer table upload failed"));
   }
 
   if (m->world > 1) {
@@ -973,6 +1010,11 @@ struct l3g_workspace {
   uint8_t* pf_act = nullptr;  // activation chunks of the batched product
   float* pf_part = nullptr;   // split-K partial sums of the product
   size_t pf_part_floats = 0;
+  // persistent layer kernel (model->persist, see persist_setup)
+  bool ps_on = false;
+  persist::Plan ps_plan{};     // ctx is the state's, filled per capture
+  int ps_ns = 0, ps_slot = 0, ps_union = 0, ps_xq_off = 0, ps_smem = 0;
+  unsigned* d_bar = nullptr;   // [0] grid-barrier arrivals, [1] abort word
 };
 
 static void ws_release(l3g_workspace* ws) {
@@ -983,7 +1025,7 @@ static void ws_release(l3g_workspace* ws) {
       cudaIpcCloseMemHandle(ws->tp_peer_recv[r]);
     ws->tp_peer_recv[r] = nullptr;
   }
-  void* tp_ptrs[] = {ws->d_step, ws->d_sync, ws->tp_recv};
+  void* tp_ptrs[] = {ws->d_step, ws->d_sync, ws->tp_recv, ws->d_bar};
   for (void* p : tp_ptrs)
     if (p) cudaFree(p);
   void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
@@ -1203,6 +1245,85 @@ static void choose_attention_cluster(l3g_workspace* ws) {
   return;
 }
 
+template <int DPL, typename KT>
+static void* layers_kernel_t(int gp) {
+  switch (gp) {
+    case 1: return (void*)k_layers<DPL, KT, 1>;
+    case 2: return (void*)k_layers<DPL, KT, 2>;
+    case 4: return (void*)k_layers<DPL, KT, 4>;
+    case 8: return (void*)k_layers<DPL, KT, 8>;
+    default: return nullptr;
+  }
+}
+// The instantiation of k_layers for this model's head size, KV element type
+// and query heads per kv head (rounded up to a power of two).
+static void* layers_kernel(const l3g_model* m, int gp) {
+  const int dpl = m->hd / 32;
+  if (m->kv_f16) {
+    if (dpl == 2) return layers_kernel_t<2, __half>(gp);
+    if (dpl == 4) return layers_kernel_t<4, __half>(gp);
+  } else {
+    if (dpl == 1) return layers_kernel_t<1, float>(gp);
+    if (dpl == 2) return layers_kernel_t<2, float>(gp);
+    if (dpl == 4) return layers_kernel_t<4, float>(gp);
+  }
+  return nullptr;
+}
+
+// The persistent layer kernel's plan for this workspace, when the model was
+// loaded for it: the four layer matrices' tile geometry (four rows per
+// warp), the attention split (the per-kernel step's count, so both give the
+// same partials), and a ring of as many slots as fit beside the phase
+// scratch.  It stays off (the per-kernel step runs) when a tensor-parallel
+// workspace has no peer-memory exchange, or the kernel cannot be resident
+// on every SM.
+static int persist_setup(l3g_workspace* ws) {
+  l3g_model* m = ws->m;
+  ws->ps_on = false;
+  if (!m->persist || (m->world > 1 && !ws->tp_p2p) || m->hkv_l > m->nsm) return L3G_OK;
+  const LayerW& L0 = m->layers[0];
+  const DevMat* mats[persist::N_MAT] = {&L0.qkv, &L0.wo, &L0.upgate, &L0.down};
+  int rows[persist::N_MAT], cols[persist::N_MAT];
+  for (int i = 0; i < persist::N_MAT; ++i) {
+    rows[i] = mats[i]->t.rows;
+    cols[i] = mats[i]->t.cols;
+  }
+  const size_t es = m->kv_f16 ? 2 : 4;
+  persist::Plan& p = ws->ps_plan;
+  p = persist::make_plan(m->nsm, m->hp.n_layers, rows, cols, m->hkv_l, ws->att_P,
+                         2 * m->hd * (int)es, ws->ctx, NW, TILE_TARGET);
+  int slot = p.P * p.row_bytes, max_cols = 0;
+  for (int i = 0; i < persist::N_MAT; ++i) {
+    const Q8Tiles& t = mats[i]->t;  // the uploaded layout must be the plan's
+    if (t.wr != p.wr[i] || t.ck != p.ck[i] || t.nslices != p.nsl[i] ||
+        t.tile_bytes != p.tile_bytes[i] || t.n_groups != p.ng[i])
+      return L3G_OK;
+    slot = std::max(slot, t.tile_bytes);
+    max_cols = std::max(max_cols, t.cols);
+  }
+  if (m->hp.n_emb > 8 * NW * 32 * 4) return L3G_OK;  // ps_rms holds 8 float4 per thread
+  ws->ps_slot = align_up(slot, 128);
+  ws->ps_xq_off = ps_xq_off(max_cols);
+  ws->ps_union = ps_union_bytes(max_cols, m->group, m->hd, p.splits);
+  const int limit = 227 * 1024;
+  ws->ps_ns = std::min(MAX_STAGES, (limit - PS_HEAD - ws->ps_union) / ws->ps_slot);
+  if (ws->ps_ns < 2) return L3G_OK;
+  ws->ps_smem = PS_HEAD + ws->ps_union + ws->ps_ns * ws->ps_slot;
+  int gp = 1;
+  while (gp < m->group) gp <<= 1;
+  void* k = layers_kernel(m, gp);
+  int per_sm = 0;
+  if (!k || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, NTHREADS, ws->ps_smem) !=
+                cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    return L3G_OK;
+  }
+  CUDA_TRY(cudaMalloc(&ws->d_bar, 2 * sizeof(unsigned)));
+  CUDA_TRY(cudaMemset(ws->d_bar, 0, 2 * sizeof(unsigned)));
+  ws->ps_on = true;
+  return L3G_OK;
+}
+
 extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_workspace** out) {
   if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
   *out = nullptr;
@@ -1254,8 +1375,11 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   DM(ws->logits, (size_t)vloc * 4);
   DM(ws->logits_full, (size_t)vloc * m->world * 4);
   HM(ws->h_logits, (size_t)vloc * m->world * 4);
-  DM(ws->part_o, (size_t)m->hkv_l * ws->n_splits * G * hd * 4);
-  DM(ws->part_ml, (size_t)m->hkv_l * ws->n_splits * G * 2 * 4);
+  // partials for the per-kernel step's splits or the persistent kernel's
+  // (at most one CTA per SM each)
+  const int part_splits = std::max(ws->n_splits, std::max(1, m->nsm / m->hkv_l));
+  DM(ws->part_o, (size_t)m->hkv_l * part_splits * G * hd * 4);
+  DM(ws->part_ml, (size_t)m->hkv_l * part_splits * G * 2 * 4);
   DM(ws->att_cnt, (size_t)m->hkv_l * 2 * 4);  // arrivals, departures
   DM(ws->am_val, (size_t)m->nsm * 4);
   DM(ws->am_idx, (size_t)m->nsm * 4);
@@ -1295,6 +1419,14 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   ws->device = m->device;
   if (m->world > 1) {
     const int rc = tp_setup(ws);
+    if (rc) {
+      ws_release(ws);
+      delete ws;
+      return rc;
+    }
+  }
+  {
+    const int rc = persist_setup(ws);  // after tp_setup: needs the exchange's state
     if (rc) {
       ws_release(ws);
       delete ws;
@@ -1458,6 +1590,66 @@ static TpExchange tp_exchange(const l3g_workspace* ws, int phase) {
   return t;
 }
 
+// Arguments of the persistent layer kernel for state s (its cache, RoPE
+// tables and context length are captured into the step's graph).
+static PersistArgs persist_args(const l3g_workspace* ws, const l3g_state* s,
+                                unsigned long long* stamps) {
+  const l3g_model* m = ws->m;
+  PersistArgs a{};
+  a.plan = ws->ps_plan;
+  a.plan.ctx = s->ctx;
+  a.layers = m->d_layers;
+  a.nstages = ws->ps_ns;
+  a.slot_bytes = ws->ps_slot;
+  a.union_bytes = ws->ps_union;
+  a.xq_off = ws->ps_xq_off;
+  a.eps = m->hp.rms_eps;
+  a.scale = (float)(1.0 / sqrt((double)m->hd));
+  a.n_emb = m->hp.n_emb;
+  a.n_ff = m->ff_l;
+  a.hq = m->hq_l;
+  a.head_dim = m->hd;
+  a.group = m->group;
+  a.rope_half = m->rope_half;
+  a.xa = ws->x[0];
+  a.xb = ws->x[1];
+  a.y = ws->y;
+  a.q = ws->q;
+  a.attn = ws->attn;
+  a.attn_d = ws->attn_d;
+  a.attn_q = ws->attn_q;
+  a.act = ws->act;
+  a.act_d = ws->act_d;
+  a.act_q = ws->act_q;
+  a.part_o = ws->part_o;
+  a.part_ml = ws->part_ml;
+  a.rope_cos = s->rope_cos;
+  a.rope_sin = s->rope_sin;
+  a.io = ws->d_io;
+  a.kv = static_cast<uint8_t*>(s->kv);
+  a.kv_layer_bytes = s->layer_elems * (m->kv_f16 ? 2 : 4);
+  a.bar = ws->d_bar;
+  a.res = ws->d_res;
+  a.wait_ns = m->world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS;
+  if (ws->tp_p2p) {
+    a.tp = tp_exchange(ws, 0);
+  } else {
+    a.tp = TpExchange{};
+    a.tp.world = 1;
+  }
+  a.stamps = stamps;
+  return a;
+}
+
+// The persistent kernel's barrier stamps of a traced step live in the trace
+// buffer after the first kPersistStampSlot launches' per-CTA stamps (the
+// step's other kernels stamp there), [barrier][cta]{arrival, release}.
+constexpr size_t kPersistStampSlot = 16;
+constexpr size_t kPersistStampOff = kPersistStampSlot * TRACE_CTAS * 8;  // in 64-bit words
+static size_t persist_stamp_bytes(const l3g_workspace* ws) {
+  return (size_t)persist::BARRIERS_PER_LAYER * ws->ps_plan.n_layers * ws->ps_plan.grid * 2 * 8;
+}
+
 static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int k) {
   const bool traced = variant == V_TRACE;
   if (traced) variant = V_GREEDY_DEV;
@@ -1490,8 +1682,33 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
   if (variant == V_SAMPLE)
     CUDA_TRY(cudaMemcpyAsync(ws->d_samp, ws->h_samp, sizeof(SampleParams), cudaMemcpyHostToDevice, st));
   KL(L3G_K_EMBED, launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
-                  hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res, ws->d_step));
-  for (int l = 0; l < hp.n_layers; ++l) {
+                  hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res, ws->d_step,
+                  ws->ps_on ? ws->d_bar : nullptr));
+  if (ws->ps_on) {  // every layer in one persistent launch
+    unsigned long long* stamps =
+        tr && kPersistStampOff * 8 + persist_stamp_bytes(ws) <= kTraceBytes
+            ? ws->d_trace + kPersistStampOff
+            : nullptr;
+    const PersistArgs a = persist_args(ws, s, stamps);
+    int gp = 1;
+    while (gp < m->group) gp <<= 1;
+    void* kfn = layers_kernel(m, gp);
+    if (!kfn) return l3g_fail(L3G_E_INVALID, "no persistent layer kernel for this shape");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ws->ps_plan.grid);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = ws->ps_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_serialize ? 0 : 1;
+    void* kargs[] = {(void*)&a};
+    KL(L3G_K_LAYERS, cudaLaunchKernelExC(&cfg, kfn, kargs));
+  }
+  // the per-kernel step (skipped when the persistent kernel ran the layers)
+  for (int l = 0; !ws->ps_on && l < hp.n_layers; ++l) {
     const LayerW& L = m->layers[l];
     uint8_t* kv = static_cast<uint8_t*>(s->kv) + (size_t)l * s->layer_elems * es;
     {  // RMSNorm -> act-quant -> QKV -> RoPE -> KV append, infer.go:67-127
@@ -2020,6 +2237,27 @@ extern "C" int l3g_trace_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int
   for (int i = 0; i < out_n; ++i) kinds[i] = ws->trace_kinds_graph[i];
   *n = out_n;
   s->pos++;
+  return L3G_OK;
+}
+
+extern "C" int l3g_workspace_persistent(const l3g_workspace* ws, int32_t* on) {
+  if (!ws || !on) return l3g_fail(L3G_E_INVALID, "null argument");
+  *on = ws->ps_on ? 1 : 0;
+  return L3G_OK;
+}
+
+extern "C" int l3g_persist_stamps(const l3g_workspace* ws, uint64_t* out, int64_t cap,
+                                  int32_t* n_barriers, int32_t* grid) {
+  if (!ws || !out || !n_barriers || !grid) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (!ws->ps_on) return l3g_fail(L3G_E_INVALID, "the workspace does not run the persistent kernel");
+  const size_t bytes = persist_stamp_bytes(ws);
+  if (kPersistStampOff * 8 + bytes > kTraceBytes)
+    return l3g_fail(L3G_E_INVALID, "too many layers to stamp");
+  if (cap < (int64_t)(bytes / 8)) return l3g_fail(L3G_E_INVALID, "capacity %lld < %zu", (long long)cap, bytes / 8);
+  CUDA_TRY(cudaSetDevice(ws->device));
+  CUDA_TRY(cudaMemcpy(out, ws->d_trace + kPersistStampOff, bytes, cudaMemcpyDeviceToHost));
+  *n_barriers = persist::BARRIERS_PER_LAYER * ws->ps_plan.n_layers;
+  *grid = ws->ps_plan.grid;
   return L3G_OK;
 }
 

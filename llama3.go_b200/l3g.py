@@ -122,6 +122,9 @@ def lib():
         "l3g_workspace_kernels_per_step": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_workspace_attention_layout": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
         "l3g_workspace_tp_p2p": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+        "l3g_workspace_persistent": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+        "l3g_persist_stamps": (C.c_int, [_P, C.POINTER(C.c_uint64), C.c_int64, C.POINTER(C.c_int32),
+                                         C.POINTER(C.c_int32)]),
         "l3g_profile_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_float),
                                        C.POINTER(C.c_int32)]),
         "l3g_trace_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_uint64), C.POINTER(C.c_int32),
@@ -289,7 +292,7 @@ class Model:
                                          arr.ctypes.data_as(C.POINTER(C.c_int32)), arr.size))
 
     KERNEL_KINDS = ("embed", "qkv_rope_kv", "attention", "wo", "upgate_swiglu", "down", "logits_argmax",
-                    "other", "act_quant")
+                    "other", "act_quant", "layers")
 
     def ProfileStep(self, s: "State", token: int, ws: "Workspace", cap: int = 4096):
         """One step run eagerly with every kernel timed alone: [(kind, us)]."""
@@ -440,6 +443,24 @@ class Workspace:
         v = C.c_int32()
         _check(lib().l3g_workspace_tp_p2p(self._h, C.byref(v)))
         return bool(v.value)
+
+    def persistent(self) -> bool:
+        """True when this workspace's steps run every layer in one persistent
+        launch (model loaded with L3G_PERSIST=1 in the environment)."""
+        v = C.c_int32()
+        _check(lib().l3g_workspace_persistent(self._h, C.byref(v)))
+        return bool(v.value)
+
+    def persist_stamps(self) -> np.ndarray:
+        """After Model.TraceStep on a persistent workspace: [barrier][cta][2]
+        %globaltimer ns of each CTA's arrival at and release from each grid
+        barrier (7 per layer; zeros where none ran)."""
+        cap = 7 * self.model.HP.NLayers * 1024 * 2
+        out = np.zeros(cap, np.uint64)
+        nb, grid = C.c_int32(), C.c_int32()
+        _check(lib().l3g_persist_stamps(self._h, out.ctypes.data_as(C.POINTER(C.c_uint64)), cap,
+                                        C.byref(nb), C.byref(grid)))
+        return out[: nb.value * grid.value * 2].reshape(nb.value, grid.value, 2).astype(np.int64)
 
     def attention_layout(self) -> tuple[int, int]:
         """(splits per kv head, cluster size or 0)."""
