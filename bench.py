@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--config", default="llama3.1-8b")
     ap.add_argument("--prefill", type=int, default=4096)
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"])
+    ap.add_argument("--persistent", action="store_true",
+                    help="decode with the persistent layer kernel (every layer in one launch)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -364,6 +366,36 @@ def trace_summary(m, s, ws, tok, pos, reps=3):
     return out
 
 
+PERSIST_PHASES = ("qkv", "attention", "merge", "wo", "upgate", "act_quant", "down")
+
+
+def persist_summary(m, s, ws, tok, pos, reps=3):
+    """Barrier timeline of the persistent layer kernel (one traced step
+    replayed as its graph): per phase, the mean time per layer from the
+    last CTA's release at the previous barrier to the last CTA's arrival at
+    this one (the phase's critical path), and the mean barrier latency (last
+    arrival to last release)."""
+    import numpy as np
+    acc = {n: [] for n in PERSIST_PHASES}
+    lat = []
+    for _ in range(reps):
+        s.Pos = pos
+        m.TraceStep(s, tok, ws)
+        st = ws.persist_stamps()
+        arr, rel = st[..., 0], st[..., 1]
+        prev = None
+        for b in range(st.shape[0]):
+            if (arr[b] == 0).all():
+                continue
+            if prev is not None:
+                acc[PERSIST_PHASES[b % 7]].append((arr[b].max() - prev) / 1e3)
+            lat.append((rel[b].max() - arr[b].max()) / 1e3)
+            prev = rel[b].max()
+    out = {k: round(float(np.mean(v)), 2) for k, v in acc.items() if v}
+    out["barrier_latency_us"] = round(float(np.mean(lat)), 2)
+    return out
+
+
 def progress(world, rank, msg):
     """Rank-tagged progress on stderr for multi-GPU runs (stdout keeps the
     single JSON line)."""
@@ -393,12 +425,17 @@ def run_l3g(args):
     nid = D.bcast_bytes(l3g.nccl_unique_id() if (world > 1 and rank == 0) else None) if world > 1 else None
     kv = l3g.L3G_KV_F16 if args.kv == "f16" else l3g.L3G_KV_F32
     opts = l3g.default_options(world, rank, local, kv, nid)
+    if args.persistent:
+        os.environ["L3G_PERSIST"] = "1"
     m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, opts)
+    os.environ.pop("L3G_PERSIST", None)
     ctx = args.prefill + args.warmup + args.steps + 2
     if ctx > cfg.ctx_len:
         raise SystemExit(f"prefill+warmup+steps exceeds the model context {cfg.ctx_len}")
     s = m.NewState(ctx)
     ws = m.NewWorkspace(ctx, 40)
+    if args.persistent and not ws.persistent():
+        raise SystemExit("--persistent: the workspace did not enable the persistent layer kernel")
     prompt = synthetic.prompt_ids(cfg, args.prefill, seed=args.seed)
     progress(world, rank, "prefill")
     t0 = time.perf_counter()
@@ -449,8 +486,10 @@ def run_l3g(args):
             prof[kind] = prof.get(kind, 0.0) + us / 3
         s.Pos = p0 + max(1, args.warmup)
     prof = {k: round(v, 1) for k, v in sorted(prof.items(), key=lambda kv: -kv[1])}
+    ws_grid = torch.cuda.get_device_properties(local).multi_processor_count
     progress(world, rank, "device timeline")
     timeline = trace_summary(m, s, ws, tok, p0 + max(1, args.warmup))
+    phases = persist_summary(m, s, ws, tok, p0 + max(1, args.warmup)) if args.persistent else None
     progress(world, rank, "matvec timing and wrap-up")
 
     # roofline of the whole decode step (weights + KV read per token)
@@ -459,7 +498,17 @@ def run_l3g(args):
     kv_bytes = sum(cfg.kv_bytes(first_pos + i + 1, es) for i in range(args.steps)) / args.steps
     step_bytes = cfg.weight_bytes() + kv_bytes
     decode_gbs = step_bytes * value / 1e9
-    mv = time_matvec_kernel(l3g, cfg, args.seed, hbm) if rank == 0 else None
+    if args.persistent:
+        # the dominant kernel is the persistent launch itself: every layer's
+        # weights plus the KV cache at the profiled position, over its
+        # CUDA-event time in the eager profile
+        layer_bytes = cfg.weight_bytes() - cfg.vocab * cfg.n_emb // 32 * 34 - cfg.n_emb // 32 * 34
+        alg = (layer_bytes + cfg.kv_bytes(first_pos + 1, es)) // world
+        ms = prof["layers"] / 1e3
+        mv = {"kernel": "k_layers (persistent: every layer of the step, %d CTAs)" % ws_grid,
+              "bytes_per_launch": alg, "ms_per_launch": ms, "achieved_gbs": alg / ms / 1e6}
+    else:
+        mv = time_matvec_kernel(l3g, cfg, args.seed, hbm) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -484,12 +533,14 @@ def run_l3g(args):
         "config": {"workload": f"{cfg.name}-shape Q8_0 bs1 greedy decode after {args.prefill}-token prefill",
                    "model": cfg.name, "global_batch": 1, "seq_len": args.prefill,
                    "parallelism": f"tp{world}", "kv_dtype": args.kv,
+                   "step_kernels": "persistent" if args.persistent else "per-kernel",
                    "l2": "inputs larger than L2: every step streams %.2f GB of weights" % (cfg.weight_bytes() / 1e9),
                    "weights": "seeded N(0,0.02) quantized to Q8_0, norms 1.0; random-init synthetic"},
         "roofline": {"bound": "hbm", "achieved": round(mv["achieved_gbs"], 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(mv["achieved_gbs"] / hbm, 4),
-                     "traffic": profiled_traffic("k_matvec_q8_upgate_28672x4096.md"),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                     "traffic": None if args.persistent else profiled_traffic("k_matvec_q8_upgate_28672x4096.md"),
+                     "traffic_source": "not captured for the persistent kernel" if args.persistent else
+                                       "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
                                        "(profiles/k_matvec_q8_upgate_28672x4096.md)",
                      "kernel": mv["kernel"], "bytes_per_launch": mv["bytes_per_launch"],
                      "ms_per_launch": round(mv["ms_per_launch"], 5), "peak_kind": hbm_kind},
@@ -503,6 +554,7 @@ def run_l3g(args):
         "kernels_per_step": kernels,
         "step_profile_us": prof,
         "step_timeline_us": timeline,
+        **({"persistent_phase_us": phases} if phases else {}),
         "clocks": clocks,
         "prefill_s": round(prefill_s, 3),
     }
