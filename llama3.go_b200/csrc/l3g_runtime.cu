@@ -198,17 +198,6 @@ static int setup_kernels() {
     SETAT(4, __half);
 #undef SETAT
 #undef SETCL
-#define SETPS(D, T)              \
-  SETK((k_layers<D, T, 1>));     \
-  SETK((k_layers<D, T, 2>));     \
-  SETK((k_layers<D, T, 4>));     \
-  SETK((k_layers<D, T, 8>))
-    SETPS(1, float);
-    SETPS(2, float);
-    SETPS(4, float);
-    SETPS(2, __half);
-    SETPS(4, __half);
-#undef SETPS
     SETK(k_topk_final);
     SETK(k_embed);
     SETK(k_advance);
@@ -1312,9 +1301,13 @@ static int persist_setup(l3g_workspace* ws) {
   int gp = 1;
   while (gp < m->group) gp <<= 1;
   void* k = layers_kernel(m, gp);
+  // attributes of this instantiation only, here rather than at load, so the
+  // per-kernel step never depends on the persistent kernel's set-up
   int per_sm = 0;
-  if (!k || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, NTHREADS, ws->ps_smem) !=
-                cudaSuccess || per_sm < 1) {
+  if (!k || set_max_shared(k, limit) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, NTHREADS, ws->ps_smem) !=
+          cudaSuccess ||
+      per_sm < 1) {
     cudaGetLastError();
     return L3G_OK;
   }
