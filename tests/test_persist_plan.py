@@ -78,3 +78,35 @@ int main() {
         subprocess.run([gxx, "-std=c++17", "-I", CSRC, cpp, "-o", exe], check=True)
         out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
     assert [int(v) for v in out] == [32, 1024, 4, 34816, 896, 32, 1024, 14, 34816, 128]
+
+
+def test_tile_geometry_matches_the_python_statement(tmp_path):
+    """The shared tile_geometry (used by make_tiles for every decode matrix)
+    equals the independent statement of the layout in
+    test_batched_index_math.make_tiles for 480 shapes and every rows-per-warp
+    choice."""
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("g++ not found")
+    from test_batched_index_math import make_tiles
+    rows_l = [1, 7, 32, 100, 513, 1024, 2050, 4096, 6144, 14336, 28672, 128256]
+    cols_l = [32, 96, 288, 512, 1792, 2048, 3072, 4096, 8192, 14336]
+    src = tmp_path / "g.cpp"
+    src.write_text("#include <cstdio>\n#include \"l3g_persist_plan.h\"\nint main() {\n"
+                   + "".join(f"  {{ l3g::TileGeom g = l3g::tile_geometry({r}, {c}, {k}, 8, 32768);"
+                             f" std::printf(\"%d %d %d %d %d\\n\", g.wr, g.ck, g.nslices, g.tile_bytes,"
+                             f" g.n_groups); }}\n"
+                             for r in rows_l for c in cols_l for k in (1, 2, 4, 8))
+                   + "}\n")
+    exe = str(tmp_path / "g")
+    subprocess.run([gxx, "-std=c++17", "-I", CSRC, str(src), "-o", exe], check=True)
+    out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.splitlines()
+    i = 0
+    for r in rows_l:
+        for c in cols_l:
+            for k in (1, 2, 4, 8):
+                t = make_tiles(r, c, k)
+                want = [t["wr"], t["ck"], t["nslices"], t["tile_bytes"], t["n_groups"]]
+                assert [int(v) for v in out[i].split()] == want, (r, c, k)
+                i += 1
+
