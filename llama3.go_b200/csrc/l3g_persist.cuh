@@ -59,7 +59,8 @@ struct PersistArgs {
   const int* io;          // io[1] = position of this token
   uint8_t* kv;            // layer 0 of the cache; layer l at + l * kv_layer_bytes
   size_t kv_layer_bytes;
-  unsigned* bar;          // [0] barrier arrivals this step, [1] abort (k_embed zeroes both)
+  unsigned* bar;          // barrier counters and abort word (persist::BAR_*), zeroed by k_embed
+  int nsub;               // barrier counters in use (1 .. BAR_MAX_SUB)
   Result* res;
   unsigned long long wait_ns;
   TpExchange tp;          // tp.world > 1: Wo / down rows pushed to every rank
@@ -95,20 +96,28 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Bounded wait until the barrier counter reaches `target` (producer side).
-__device__ __forceinline__ bool ps_wait_count(const PersistArgs& a, unsigned target, PSmem* sh,
-                                              int where) {
+__device__ __forceinline__ unsigned* ps_abort_word(const PersistArgs& a) {
+  return a.bar + persist::BAR_ABORT;
+}
+
+// Bounded wait until barrier `idx` is complete (producer side, one thread:
+// every counter, in order).
+__device__ __forceinline__ bool ps_wait_barrier(const PersistArgs& a, int idx, PSmem* sh,
+                                                int where) {
   const uint64_t t0 = gtime();
-  while (ld_acquire_gpu_u32(a.bar) < target) {
-    if (*(volatile int*)&sh->abort_flag || *(volatile unsigned*)(a.bar + 1)) {
-      sh->abort_flag = 1;
-      return false;
-    }
-    if (gtime() - t0 > a.wait_ns) {
-      sh->abort_flag = 1;
-      report(a.res, ERR_TIMEOUT, where);
-      atomicExch(a.bar + 1, 1u);
-      return false;
+  for (int i = 0; i < a.nsub; ++i) {
+    const unsigned target = (unsigned)(idx + 1) * persist::sub_count(gridDim.x, a.nsub, i);
+    while (ld_acquire_gpu_u32(a.bar + i * persist::BAR_STRIDE) < target) {
+      if (*(volatile int*)&sh->abort_flag || *(volatile unsigned*)ps_abort_word(a)) {
+        sh->abort_flag = 1;
+        return false;
+      }
+      if (gtime() - t0 > a.wait_ns) {
+        sh->abort_flag = 1;
+        report(a.res, ERR_TIMEOUT, where);
+        atomicExch(ps_abort_word(a), 1u);
+        return false;
+      }
     }
   }
   return true;
@@ -119,37 +128,57 @@ __device__ __forceinline__ bool ps_wait_count(const PersistArgs& a, unsigned tar
 // wait inside a phase only skips work (every warp still runs the phase's
 // CTA barriers), so the warps always reach the same barriers.  Returns false
 // when the step is aborting (this CTA's flag or the step's abort word).
+// Warp 0 polls: lane i < nsub watches counter i (acquire), and the CTA
+// barrier after it passes what those lanes acquired to every thread.
 __device__ __forceinline__ bool ps_barrier(const PersistArgs& a, int idx, PSmem* sh) {
   consumer_sync();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     const uint64_t t_arr = gtime();
-    int stop = *(volatile int*)&sh->abort_flag;
-    if (stop) {
-      atomicExch(a.bar + 1, 1u);  // the other CTAs stop waiting for this one
-    } else {
-      __threadfence();  // this CTA's writes of the phase, ordered by the CTA barrier above
-      atomicAdd(a.bar, 1u);
-      const unsigned target = (unsigned)(idx + 1) * gridDim.x;
-      while (ld_acquire_gpu_u32(a.bar) < target) {
-        if (*(volatile int*)&sh->abort_flag || *(volatile unsigned*)(a.bar + 1)) {
-          stop = 1;
-          break;
+    int stop = 0;
+    if (lane == 0) {
+      stop = *(volatile int*)&sh->abort_flag;
+      if (stop) {
+        atomicExch(ps_abort_word(a), 1u);  // the other CTAs stop waiting for this one
+      } else {
+        __threadfence();  // this CTA's writes of the phase, ordered by the CTA barrier above
+        atomicAdd(a.bar + (blockIdx.x % a.nsub) * persist::BAR_STRIDE, 1u);
+      }
+    }
+    stop = __shfl_sync(0xffffffffu, stop, 0);
+    if (!stop) {
+      const bool mine = lane < a.nsub;
+      const unsigned* ctr = a.bar + (mine ? lane : 0) * persist::BAR_STRIDE;
+      const unsigned target =
+          mine ? (unsigned)(idx + 1) * persist::sub_count(gridDim.x, a.nsub, lane) : 0u;
+      for (;;) {
+        const bool ready = !mine || ld_acquire_gpu_u32(ctr) >= target;
+        if (__all_sync(0xffffffffu, ready)) break;
+        int s = 0;
+        if (lane == 0) {
+          if (*(volatile int*)&sh->abort_flag || *(volatile unsigned*)ps_abort_word(a)) {
+            s = 1;
+          } else if (gtime() - t_arr > a.wait_ns) {
+            report(a.res, ERR_TIMEOUT, 50);
+            atomicExch(ps_abort_word(a), 1u);
+            s = 1;
+          }
         }
-        if (gtime() - t_arr > a.wait_ns) {
-          report(a.res, ERR_TIMEOUT, 50);
-          atomicExch(a.bar + 1, 1u);
+        if (__shfl_sync(0xffffffffu, s, 0)) {
           stop = 1;
           break;
         }
       }
       __threadfence();
     }
-    if (stop) sh->abort_flag = 1;  // the producer stops too
-    sh->stop = stop;
-    if (a.stamps) {
-      unsigned long long* s = a.stamps + ((size_t)idx * gridDim.x + blockIdx.x) * 2;
-      s[0] = t_arr;
-      s[1] = gtime();
+    if (lane == 0) {
+      if (stop) sh->abort_flag = 1;  // the producer stops too
+      sh->stop = stop;
+      if (a.stamps) {
+        unsigned long long* st = a.stamps + ((size_t)idx * gridDim.x + blockIdx.x) * 2;
+        st[0] = t_arr;
+        st[1] = gtime();
+      }
     }
   }
   consumer_sync();
@@ -197,7 +226,7 @@ __device__ void ps_produce(const PersistArgs& a, PSmem* sh, uint8_t* ring) {
             const int tb = min(t1, ta + p.P);
             if (!waited && tb > pos) {
               // this step's own K/V row is appended in the QKV phase
-              ok = ps_wait_count(a, (unsigned)(barrier_index(l, 0) + 1) * gridDim.x, sh, 42);
+              ok = ps_wait_barrier(a, barrier_index(l, 0), sh, 42);
               fence_proxy_async_global();
               waited = true;
               if (!ok) break;
@@ -662,9 +691,9 @@ __device__ void ps_reduce(const PersistArgs& a, unsigned e) {
     for (int j = 0; j < 4; ++j) {
       unsigned long long w = ld_relaxed_sys_u64(rb + (size_t)r * t.n + j);
       while (!late && (unsigned)(w >> 32) != e) {
-        if (*(volatile unsigned*)(a.bar + 1) || gtime() - t_start > a.wait_ns) {
-          if (!*(volatile unsigned*)(a.bar + 1)) report(a.res, ERR_TIMEOUT, 51);
-          atomicExch(a.bar + 1, 1u);
+        if (*(volatile unsigned*)ps_abort_word(a) || gtime() - t_start > a.wait_ns) {
+          if (!*(volatile unsigned*)ps_abort_word(a)) report(a.res, ERR_TIMEOUT, 51);
+          atomicExch(ps_abort_word(a), 1u);
           late = true;
           break;
         }

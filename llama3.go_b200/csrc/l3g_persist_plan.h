@@ -155,9 +155,20 @@ L3G_HD inline long long stage_offset(const Plan& p, int kvh, int t0, int st) {
   return ((long long)kvh * p.ctx + t0 + (long long)st * p.P) * p.row_bytes;
 }
 
-// Global index of barrier j (0..6) of layer l; it completes when the
-// arrival counter reaches (index + 1) * grid.
+// Global index of barrier j (0..6) of layer l.  Arrivals are spread over
+// nsub counters (1 to BAR_MAX_SUB, each on its own 128-byte line): CTA b adds
+// one to counter b % nsub, and barrier k is complete when every counter i
+// holds (k + 1) * sub_count(grid, nsub, i).  One counter makes every
+// arrival an atomic on the same address; several let the arrivals proceed
+// in parallel at the cost of one load per counter when polling.
 L3G_HD inline int barrier_index(int l, int j) { return l * BARRIERS_PER_LAYER + j; }
+constexpr int BAR_STRIDE = 32;                      // 32-bit words between counters
+constexpr int BAR_MAX_SUB = 16;
+constexpr int BAR_ABORT = BAR_MAX_SUB * BAR_STRIDE;  // the step's abort word
+constexpr int BAR_WORDS = BAR_ABORT + 1;
+L3G_HD inline int sub_count(int grid, int nsub, int i) {
+  return grid / nsub + (i < grid % nsub ? 1 : 0);
+}
 
 // Tiles CTA b consumes in layer l (weights and attention stages) when n
 // positions are live; the producer and the consumers walk the same list.

@@ -1002,8 +1002,8 @@ struct l3g_workspace {
   // persistent layer kernel (model->persist, see persist_setup)
   bool ps_on = false;
   persist::Plan ps_plan{};     // ctx is the state's, filled per capture
-  int ps_ns = 0, ps_slot = 0, ps_union = 0, ps_xq_off = 0, ps_smem = 0;
-  unsigned* d_bar = nullptr;   // [0] grid-barrier arrivals, [1] abort word
+  int ps_ns = 0, ps_slot = 0, ps_union = 0, ps_xq_off = 0, ps_smem = 0, ps_nsub = 1;
+  unsigned* d_bar = nullptr;   // grid-barrier counters and abort word (persist::BAR_*)
 };
 
 static void ws_release(l3g_workspace* ws) {
@@ -1311,8 +1311,12 @@ static int persist_setup(l3g_workspace* ws) {
     cudaGetLastError();
     return L3G_OK;
   }
-  CUDA_TRY(cudaMalloc(&ws->d_bar, 2 * sizeof(unsigned)));
-  CUDA_TRY(cudaMemset(ws->d_bar, 0, 2 * sizeof(unsigned)));
+  CUDA_TRY(cudaMalloc(&ws->d_bar, persist::BAR_WORDS * sizeof(unsigned)));
+  CUDA_TRY(cudaMemset(ws->d_bar, 0, persist::BAR_WORDS * sizeof(unsigned)));
+  // barrier counters: L3G_PERSIST_BAR_SPREAD=n spreads the arrivals over n
+  ws->ps_nsub = 1;
+  if (const char* env = getenv("L3G_PERSIST_BAR_SPREAD"))
+    ws->ps_nsub = std::max(1, std::min({atoi(env), (int)persist::BAR_MAX_SUB, p.grid}));
   ws->ps_on = true;
   return L3G_OK;
 }
@@ -1622,6 +1626,7 @@ static PersistArgs persist_args(const l3g_workspace* ws, const l3g_state* s,
   a.kv = static_cast<uint8_t*>(s->kv);
   a.kv_layer_bytes = s->layer_elems * (m->kv_f16 ? 2 : 4);
   a.bar = ws->d_bar;
+  a.nsub = ws->ps_nsub;
   a.res = ws->d_res;
   a.wait_ns = m->world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS;
   if (ws->tp_p2p) {

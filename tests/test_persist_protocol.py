@@ -8,14 +8,14 @@ tile counts per phase (the round-robin deal gives CTAs unequal shares):
   layer by layer (QKV tiles, attention stages, Wo, up/gate and down tiles);
   before tile t >= ns it waits empty[t % ns] (parity ((t / ns) - 1) & 1);
   before the attention stage holding this step's own K/V it waits until the
-  step's barrier counter shows the layer's QKV barrier complete; it stops
+  step's barrier counters show the layer's QKV barrier complete; it stops
   when its CTA aborts or, in that wait, when the step's abort word is set;
 - consumer warps (NW per CTA): per phase, per tile wait full[t % ns]
   (parity (t / ns) & 1), read, arrive empty; after a failed wait (abort)
   the warp skips its remaining waits and arrivals but keeps walking the
-  phases; at each grid barrier: CTA sync, thread 0 adds one arrival to the
-  step counter (unless aborting: it sets the abort word) and spins until
-  (index + 1) * grid arrivals or abort, CTA sync, and every warp reads the
+  phases; at each grid barrier: CTA sync, thread 0 adds one arrival to
+  counter b % nsub (unless aborting: it sets the abort word) and spins until
+  every counter i holds (index + 1) * its CTAs, or abort, CTA sync, and every warp reads the
   CTA's decision; after the loop thread 0 waits for the producer to stop and
   for the last copy into each slot.
 mbarrier model as in test_gemm_protocol.  Checked: no deadlock (with and
@@ -36,7 +36,12 @@ PHASES = 7  # QKV, ATT, MERGE, WO, UPGATE, QUANT, DOWN
 TILED = {0: "qkv", 1: "att", 3: "wo", 4: "upgate", 6: "down"}  # phases with ring tiles
 
 
-def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False):
+def sub_count(grid, nsub, i):
+    """CTAs that arrive on counter i (l3g_persist_plan.h sub_count)."""
+    return grid // nsub + (1 if i < grid % nsub else 0)
+
+
+def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1):
     rng = random.Random(seed)
     mdl = Model()
     # per CTA, per layer, per tiled phase: its tile count; the attention
@@ -54,8 +59,12 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False):
                     s.append((l, ph, i, ph == 1 and holds_pos[b][l] and i == n - 1))
         seq.append(s)
 
-    counter = [0]
+    counter = [0] * nsub  # CTA b arrives on counter b % nsub
     abort_word = [0]
+
+    def complete(k):
+        """Barrier k is complete: every counter holds (k + 1) * its CTAs."""
+        return all(counter[i] >= (k + 1) * sub_count(G, nsub, i) for i in range(nsub))
     qkv_done = [[False] * G for _ in range(layers)]  # CTA b appended its K/V rows of layer l
     done_phase = [-1] * G  # highest (layer * PHASES + phase) every warp of CTA b finished
     warp_done = [[-1] * NW for _ in range(G)]
@@ -84,8 +93,7 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False):
             if c.abort:
                 break
             if pos and not skip_pos_wait:
-                target = (l * PHASES + 0 + 1) * G
-                while counter[0] < target:
+                while not complete(l * PHASES + 0):
                     if c.abort or abort_word[0]:
                         c.abort = True
                         break
@@ -170,10 +178,9 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False):
                         abort_word[0] = 1
                         mdl.bump()
                     else:
-                        counter[0] += 1
+                        counter[b % nsub] += 1
                         mdl.bump()
-                        target = (lin + 1) * G
-                        while counter[0] < target:
+                        while not complete(lin):
                             if c.abort or abort_word[0]:
                                 stop = True
                                 break
@@ -226,21 +233,24 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False):
     assert all(exited)
     if not inject_abort:
         assert abort_word[0] == 0
-        assert counter[0] == (layers * PHASES - 1) * G
+        assert sum(counter) == (layers * PHASES - 1) * G
     return abort_word[0]
 
 
-@pytest.mark.parametrize("G,NW,ns", [(1, 2, 2), (3, 2, 2), (4, 3, 3), (5, 2, 6), (2, 4, 1)])
-def test_persistent_protocol(G, NW, ns):
+@pytest.mark.parametrize("G,NW,ns,nsub", [(1, 2, 2, 1), (3, 2, 2, 1), (4, 3, 3, 1), (5, 2, 6, 1),
+                                          (2, 4, 1, 1), (5, 2, 3, 2), (7, 2, 2, 3), (4, 2, 3, 4)])
+def test_persistent_protocol(G, NW, ns, nsub):
+    """One barrier counter, or arrivals spread over nsub counters
+    (L3G_PERSIST_BAR_SPREAD), including grids that do not divide evenly."""
     for trial in range(25):
-        run(G, NW, ns, layers=2, seed=G * 1000 + NW * 100 + ns * 10 + trial)
+        run(G, NW, ns, layers=2, seed=G * 1000 + NW * 100 + ns * 10 + trial, nsub=nsub)
 
 
-@pytest.mark.parametrize("G,NW,ns", [(3, 2, 2), (4, 3, 3)])
-def test_persistent_protocol_with_a_timeout(G, NW, ns):
+@pytest.mark.parametrize("G,NW,ns,nsub", [(3, 2, 2, 1), (4, 3, 3, 1), (5, 2, 3, 2)])
+def test_persistent_protocol_with_a_timeout(G, NW, ns, nsub):
     """One consumer wait gives up (a bounded wait running out): every CTA
     still reaches its exit, with no copy in flight."""
-    aborted = sum(run(G, NW, ns, layers=2, seed=7 * trial + G, inject_abort=True)
+    aborted = sum(run(G, NW, ns, layers=2, seed=7 * trial + G, inject_abort=True, nsub=nsub)
                   for trial in range(40))
     assert aborted >= 10  # the abort path ran, not just clean steps
 
