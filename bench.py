@@ -436,6 +436,7 @@ def run_l3g(args):
     ws = m.NewWorkspace(ctx, 40)
     if args.persistent and not ws.persistent():
         raise SystemExit("--persistent: the workspace did not enable the persistent layer kernel")
+    ps_layout = ws.persist_layout() if args.persistent else None
     prompt = synthetic.prompt_ids(cfg, args.prefill, seed=args.seed)
     progress(world, rank, "prefill")
     t0 = time.perf_counter()
@@ -534,6 +535,7 @@ def run_l3g(args):
                    "model": cfg.name, "global_batch": 1, "seq_len": args.prefill,
                    "parallelism": f"tp{world}", "kv_dtype": args.kv,
                    "step_kernels": "persistent" if args.persistent else "per-kernel",
+                   **({"persistent_layout": ps_layout} if ps_layout else {}),
                    "l2": "inputs larger than L2: every step streams %.2f GB of weights" % (cfg.weight_bytes() / 1e9),
                    "weights": "seeded N(0,0.02) quantized to Q8_0, norms 1.0; random-init synthetic"},
         "roofline": {"bound": "hbm", "achieved": round(mv["achieved_gbs"], 1), "peak": hbm, "unit": "GB/s",

@@ -287,6 +287,12 @@ int l3g_trace_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
  * with one launch of one CTA per SM whose layer phases are separated by grid
  * barriers.  *on = 1 when this workspace's steps use it.  Inspection only. */
 int l3g_workspace_persistent(const l3g_workspace *ws, int32_t *on);
+/* The persistent kernel's layout on this workspace: ring slots and their
+ * bytes, attention splits per kv head, grid-barrier counters, shared memory
+ * per CTA.  Inspection only (L3G_PERSIST_STAGES, L3G_PERSIST_SPLITS and
+ * L3G_PERSIST_BAR_SPREAD, read at workspace creation, cap or set them). */
+int l3g_persist_layout(const l3g_workspace *ws, int32_t *stages, int32_t *slot_bytes,
+                       int32_t *splits, int32_t *counters, int32_t *smem_bytes);
 /* After l3g_trace_step on a workspace that runs the persistent kernel: the
  * %globaltimer (ns) at which each CTA arrived at and left each grid barrier
  * of the traced step, out[(b * grid + cta) * 2 + {0, 1}] for barrier b (7 per

@@ -1281,6 +1281,10 @@ static int persist_setup(l3g_workspace* ws) {
   persist::Plan& p = ws->ps_plan;
   p = persist::make_plan(m->nsm, m->hp.n_layers, rows, cols, m->hkv_l, ws->att_P,
                          2 * m->hd * (int)es, ws->ctx, NW, TILE_TARGET);
+  // L3G_PERSIST_SPLITS=n caps the attention splits per kv head (fewer,
+  // longer items: less merge work, more stages per item)
+  if (const char* env = getenv("L3G_PERSIST_SPLITS"))
+    if (atoi(env) >= 1) p.splits = std::min(p.splits, atoi(env));
   int slot = p.P * p.row_bytes, max_cols = 0;
   for (int i = 0; i < persist::N_MAT; ++i) {
     const Q8Tiles& t = mats[i]->t;  // the uploaded layout must be the plan's
@@ -1296,6 +1300,9 @@ static int persist_setup(l3g_workspace* ws) {
   ws->ps_union = ps_union_bytes(max_cols, m->group, m->hd, p.splits);
   const int limit = 227 * 1024;
   ws->ps_ns = std::min(MAX_STAGES, (limit - PS_HEAD - ws->ps_union) / ws->ps_slot);
+  // L3G_PERSIST_STAGES=n caps the ring slots (a tuning knob for experiments)
+  if (const char* env = getenv("L3G_PERSIST_STAGES"))
+    if (atoi(env) >= 2) ws->ps_ns = std::min(ws->ps_ns, atoi(env));
   if (ws->ps_ns < 2) return L3G_OK;
   ws->ps_smem = PS_HEAD + ws->ps_union + ws->ps_ns * ws->ps_slot;
   int gp = 1;
@@ -2241,6 +2248,19 @@ extern "C" int l3g_trace_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int
 extern "C" int l3g_workspace_persistent(const l3g_workspace* ws, int32_t* on) {
   if (!ws || !on) return l3g_fail(L3G_E_INVALID, "null argument");
   *on = ws->ps_on ? 1 : 0;
+  return L3G_OK;
+}
+
+extern "C" int l3g_persist_layout(const l3g_workspace* ws, int32_t* stages, int32_t* slot_bytes,
+                                  int32_t* splits, int32_t* counters, int32_t* smem_bytes) {
+  if (!ws || !stages || !slot_bytes || !splits || !counters || !smem_bytes)
+    return l3g_fail(L3G_E_INVALID, "null argument");
+  if (!ws->ps_on) return l3g_fail(L3G_E_INVALID, "the workspace does not run the persistent kernel");
+  *stages = ws->ps_ns;
+  *slot_bytes = ws->ps_slot;
+  *splits = ws->ps_plan.splits;
+  *counters = ws->ps_nsub;
+  *smem_bytes = ws->ps_smem;
   return L3G_OK;
 }
 

@@ -123,6 +123,7 @@ def lib():
         "l3g_workspace_attention_layout": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
         "l3g_workspace_tp_p2p": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_workspace_persistent": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+        "l3g_persist_layout": (C.c_int, [_P] + [C.POINTER(C.c_int32)] * 5),
         "l3g_persist_stamps": (C.c_int, [_P, C.POINTER(C.c_uint64), C.c_int64, C.POINTER(C.c_int32),
                                          C.POINTER(C.c_int32)]),
         "l3g_profile_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_float),
@@ -450,6 +451,14 @@ class Workspace:
         v = C.c_int32()
         _check(lib().l3g_workspace_persistent(self._h, C.byref(v)))
         return bool(v.value)
+
+    def persist_layout(self) -> dict:
+        """The persistent kernel's ring slots, slot bytes, attention splits,
+        barrier counters and shared memory per CTA."""
+        v = [C.c_int32() for _ in range(5)]
+        _check(lib().l3g_persist_layout(self._h, *[C.byref(x) for x in v]))
+        return dict(zip(("stages", "slot_bytes", "splits", "barrier_counters", "smem_bytes"),
+                        (x.value for x in v)))
 
     def persist_stamps(self) -> np.ndarray:
         """After Model.TraceStep on a persistent workspace: [barrier][cta][2]
