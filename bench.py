@@ -366,7 +366,8 @@ def trace_summary(m, s, ws, tok, pos, reps=3):
     return out
 
 
-PERSIST_PHASES = ("qkv", "attention", "merge", "wo", "upgate", "act_quant", "down")
+PERSIST_PHASES = {7: ("qkv", "attention", "merge", "wo", "upgate", "act_quant", "down"),
+                  6: ("qkv", "attention", "merge", "wo", "upgate_act_quant", "down")}
 
 
 def persist_summary(m, s, ws, tok, pos, reps=3):
@@ -376,7 +377,9 @@ def persist_summary(m, s, ws, tok, pos, reps=3):
     this one (the phase's critical path), and the mean barrier latency (last
     arrival to last release)."""
     import numpy as np
-    acc = {n: [] for n in PERSIST_PHASES}
+    bpl = ws.persist_layout()["barriers_per_layer"]
+    names = PERSIST_PHASES[bpl]
+    acc = {n: [] for n in names}
     lat = []
     for _ in range(reps):
         s.Pos = pos
@@ -388,7 +391,7 @@ def persist_summary(m, s, ws, tok, pos, reps=3):
             if (arr[b] == 0).all():
                 continue
             if prev is not None:
-                acc[PERSIST_PHASES[b % 7]].append((arr[b].max() - prev) / 1e3)
+                acc[names[b % bpl]].append((arr[b].max() - prev) / 1e3)
             lat.append((rel[b].max() - arr[b].max()) / 1e3)
             prev = rel[b].max()
     out = {k: round(float(np.mean(v)), 2) for k, v in acc.items() if v}

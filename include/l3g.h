@@ -289,16 +289,20 @@ int l3g_trace_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
 int l3g_workspace_persistent(const l3g_workspace *ws, int32_t *on);
 /* The persistent kernel's layout on this workspace: ring slots and their
  * bytes, attention splits per kv head, grid-barrier counters, shared memory
- * per CTA.  Inspection only (L3G_PERSIST_STAGES, L3G_PERSIST_SPLITS and
- * L3G_PERSIST_BAR_SPREAD, read at workspace creation, cap or set them). */
+ * per CTA, grid barriers per layer (6 when the SwiGLU act-quant is fused into
+ * the up/gate phase, else 7).  Inspection only (L3G_PERSIST_STAGES,
+ * L3G_PERSIST_SPLITS, L3G_PERSIST_BAR_SPREAD and L3G_PERSIST_FUSE_QUANT, read
+ * at workspace creation, cap or set them). */
 int l3g_persist_layout(const l3g_workspace *ws, int32_t *stages, int32_t *slot_bytes,
-                       int32_t *splits, int32_t *counters, int32_t *smem_bytes);
+                       int32_t *splits, int32_t *counters, int32_t *smem_bytes,
+                       int32_t *barriers_per_layer);
 /* After l3g_trace_step on a workspace that runs the persistent kernel: the
  * %globaltimer (ns) at which each CTA arrived at and left each grid barrier
- * of the traced step, out[(b * grid + cta) * 2 + {0, 1}] for barrier b (7 per
- * layer: after QKV, attention, merge, Wo, up/gate, quantize, down; the last
- * layer's down has none, so its slots stay 0).  cap is out's length in
- * 64-bit words.  No reference counterpart (tracing). */
+ * of the traced step, out[(b * grid + cta) * 2 + {0, 1}] for barrier b (per
+ * layer: after QKV, attention, merge, Wo, up/gate, [quantize,] down; the
+ * last layer's down has none, so its slots stay 0).  *n_barriers = barriers
+ * per layer x layers.  cap is out's length in 64-bit words.  No reference
+ * counterpart (tracing). */
 int l3g_persist_stamps(const l3g_workspace *ws, uint64_t *out, int64_t cap,
                        int32_t *n_barriers, int32_t *grid);
 

@@ -330,15 +330,17 @@ __global__ void k_tp_reduce(const TpExchange t, float* y, Result* res,
 // ---------------------------------------------------------------------------
 // It also advances the workspace's step counter (the epoch base of the
 // tensor-parallel exchange), once per step on every rank, and, when the step
-// runs the persistent layer kernel, zeroes that kernel's barrier counters
-// and abort word (bar, nullable): every earlier kernel has completed by then.
+// runs the persistent layer kernel, zeroes that kernel's nbar barrier,
+// abort and handshake words (bar, nullable): every earlier kernel has
+// completed by then, so an aborted step leaves no stale count behind.
 __global__ void k_embed(const uint8_t* emb, int vocab, int cols, const int* io,
-                        float* x, Result* res, unsigned* step, unsigned* bar) {
+                        float* x, Result* res, unsigned* step, unsigned* bar, int nbar) {
   pdl_launch_dependents();
   pdl_wait();
   if (blockIdx.x == 0 && threadIdx.x == 0) *step += 1u;
-  if (bar && blockIdx.x == 0 && threadIdx.x <= persist::BAR_MAX_SUB)
-    bar[threadIdx.x * persist::BAR_STRIDE] = 0u;  // counters 0..15, then the abort word
+  if (bar)
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nbar; i += gridDim.x * blockDim.x)
+      bar[i] = 0u;
   const int token = io[0];
   if (token < 0 || token >= vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) report(res, ERR_TOKEN, token);

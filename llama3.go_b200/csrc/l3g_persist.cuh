@@ -59,8 +59,10 @@ struct PersistArgs {
   const int* io;          // io[1] = position of this token
   uint8_t* kv;            // layer 0 of the cache; layer l at + l * kv_layer_bytes
   size_t kv_layer_bytes;
-  unsigned* bar;          // barrier counters and abort word (persist::BAR_*), zeroed by k_embed
+  unsigned* bar;          // barrier counters, abort word, handshakes (persist::BAR_*), zeroed by k_embed
   int nsub;               // barrier counters in use (1 .. BAR_MAX_SUB)
+  int fuse_quant;         // the SwiGLU act-quant runs in the up/gate phase (no QUANT phase)
+  int bpl;                // grid barriers per layer (6 fused, else 7)
   Result* res;
   unsigned long long wait_ns;
   TpExchange tp;          // tp.world > 1: Wo / down rows pushed to every rank
@@ -75,7 +77,12 @@ struct PSmem {
   int issued;
   int producer_done;
   int stop;  // the CTA's decision at a grid barrier (written by thread 0)
+  // fused act-quant: warps done with the CTA's k-th up/gate group, slot
+  // k % GSLOTS (warps drift apart by at most the ring's depth in tiles, so at
+  // most MAX_STAGES groups: slots never alias)
+  int gcnt[MAX_STAGES + 2];
 };
+constexpr int GSLOTS = MAX_STAGES + 2;
 constexpr int PS_HEAD = 512;
 static_assert(sizeof(PSmem) <= PS_HEAD, "persistent kernel smem head");
 
@@ -226,7 +233,7 @@ __device__ void ps_produce(const PersistArgs& a, PSmem* sh, uint8_t* ring) {
             const int tb = min(t1, ta + p.P);
             if (!waited && tb > pos) {
               // this step's own K/V row is appended in the QKV phase
-              ok = ps_wait_barrier(a, barrier_index(l, 0), sh, 42);
+              ok = ps_wait_barrier(a, barrier_index(l, 0, a.bpl), sh, 42);
               fence_proxy_async_global();
               waited = true;
               if (!ok) break;
@@ -377,6 +384,40 @@ __device__ __forceinline__ void ps_epilogue(const PersistArgs& a, int m, int l, 
   }
 }
 
+// Fused act-quant of the SwiGLU output (QuantizeQ8_0Into, infer.go:233-234),
+// run by a warp right after its epilogue of up/gate row group g (the CTA's
+// k-th): group g holds act values [16g, 16g + 16), half of Q8_0 block g / 2.
+// The last of the CTA's warps to finish the group (a shared-memory count)
+// adds one to the block's counter in global memory; whoever brings it to 2,
+// in this CTA or another, reads the block's 32 values back and quantizes
+// them (quant_block, as ps_quant would), then zeroes the counter for the
+// next layer.  Fences: every warp orders its act stores (its lanes' stores,
+// via __syncwarp) before its count; the counting warps fence again before
+// the next count, so the quantizing warp sees both halves.
+__device__ __forceinline__ void ps_swiglu_quant(const PersistArgs& a, PSmem* sh, int k, int g,
+                                                int lane) {
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    __threadfence();
+    last = atomicAdd(&sh->gcnt[k % GSLOTS], 1) == NW - 1;
+  }
+  if (!__shfl_sync(0xffffffffu, last, 0)) return;
+  const int blk = g >> 1;
+  unsigned* cnt = a.bar + persist::BAR_QCNT + blk;
+  int second = 0;
+  if (lane == 0) {
+    sh->gcnt[k % GSLOTS] = 0;  // its next use is GSLOTS groups later
+    __threadfence();
+    second = atomicAdd(cnt, 1u) == 1u;
+  }
+  if (!__shfl_sync(0xffffffffu, second, 0)) return;
+  __threadfence();
+  const int i = blk * 32 + lane;
+  quant_block(i < a.n_ff ? __ldcg(a.act + i) : 0.0f, blk, lane, a.act_d, a.act_q);
+  if (lane == 0) *cnt = 0u;
+}
+
 // This CTA's row groups of matrix m: four rows per warp, dp4a against the
 // int8 activation in shared memory, fp16(d_w) * d_x per 32-block.  After a
 // failed wait the warp neither uses nor releases its tiles (no copy can then
@@ -432,6 +473,8 @@ __device__ void ps_matvec(const PersistArgs& a, int m, int l, uint32_t& t, const
       if (lane == r) v = sr;
     }
     ps_epilogue<EPI>(a, m, l, g * wr + warp * 4, v, lane, out, pos, push_off, push_e);
+    if constexpr (EPI == PE_SWIGLU)
+      if (a.fuse_quant) ps_swiglu_quant(a, sh, k, g, lane);
   }
 }
 
@@ -728,6 +771,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_layers(const __grid_constant__ 
     sh->abort_flag = 0;
     sh->issued = 0;
     sh->producer_done = 0;
+    for (int i = 0; i < GSLOTS; ++i) sh->gcnt[i] = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -744,18 +788,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_layers(const __grid_constant__ 
   const unsigned e0 = a.tp.world > 1 ? *a.tp.step * (unsigned)a.tp.nphase : 0u;
   const bool tp = a.tp.world > 1;
   uint32_t t = 0;
+  int bi = 0;  // grid barriers passed (barrier_index order)
   for (int l = 0; l < p.n_layers; ++l) {
     const PersistLayer& L = a.layers[l];
     const bool last = l + 1 == p.n_layers;
     // QKV: RMSNorm -> act-quant -> QKV -> RoPE -> KV append, infer.go:67-127
     ps_rms(a, a.xa, l ? a.y : nullptr, L.attn_norm, a.xb, xd, xqs, sh);
     ps_matvec<PE_QKV>(a, M_QKV, l, t, xd, xqs, sh, ring, a.q, pos, 0, 0);
-    if (!ps_barrier(a, barrier_index(l, 0), sh)) break;
+    if (!ps_barrier(a, bi++, sh)) break;
     // attention, infer.go:130-175
     ps_attention<DPL, KT, GP>(a, l, pos + 1, t, uni, ring, sh);
-    if (!ps_barrier(a, barrier_index(l, 1), sh)) break;
+    if (!ps_barrier(a, bi++, sh)) break;
     ps_merge(a, uni);
-    if (!ps_barrier(a, barrier_index(l, 2), sh)) break;
+    if (!ps_barrier(a, bi++, sh)) break;
     // Wo, infer.go:178-187 (the residual add is fused into the next norm)
     ps_preq(a.attn_d, a.attn_q, p.cols[M_WO], xd, xqs);
     if (tp) {
@@ -766,13 +811,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_layers(const __grid_constant__ 
     } else {
       ps_matvec<PE_STORE>(a, M_WO, l, t, xd, xqs, sh, ring, a.y, pos, 0, 0);
     }
-    if (!ps_barrier(a, barrier_index(l, 3), sh)) break;
+    if (!ps_barrier(a, bi++, sh)) break;
     // residual -> RMSNorm -> act-quant -> up/gate -> SwiGLU, infer.go:189-230
+    // (and its act-quant, infer.go:233-234, when fused)
     ps_rms(a, a.xb, a.y, L.ffn_norm, a.xa, xd, xqs, sh);
     ps_matvec<PE_SWIGLU>(a, M_UPGATE, l, t, xd, xqs, sh, ring, a.act, pos, 0, 0);
-    if (!ps_barrier(a, barrier_index(l, 4), sh)) break;
-    ps_quant(a);
-    if (!ps_barrier(a, barrier_index(l, 5), sh)) break;
+    if (!ps_barrier(a, bi++, sh)) break;
+    if (!a.fuse_quant) {
+      ps_quant(a);
+      if (!ps_barrier(a, bi++, sh)) break;
+    }
     // down, infer.go:233-242
     if (last) pdl_launch_dependents();  // the logits kernel may take SMs as CTAs finish
     ps_preq(a.act_d, a.act_q, p.cols[M_DOWN], xd, xqs);
@@ -784,7 +832,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_layers(const __grid_constant__ 
     } else {
       ps_matvec<PE_STORE>(a, M_DOWN, l, t, xd, xqs, sh, ring, a.y, pos, 0, 0);
     }
-    if (!last && !ps_barrier(a, barrier_index(l, 6), sh)) break;
+    if (!last && !ps_barrier(a, bi++, sh)) break;
   }
 
   // After an abort: wait (bounded) until the producer has stopped issuing,

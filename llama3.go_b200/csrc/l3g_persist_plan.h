@@ -69,6 +69,9 @@ enum Mat { M_QKV = 0, M_WO = 1, M_UPGATE = 2, M_DOWN = 3, N_MAT = 4 };
 // Wo groups, up/gate groups, down groups.
 enum Deal { D_QKV = 0, D_ATT = 1, D_WO = 2, D_UPGATE = 3, D_DOWN = 4, N_DEAL = 5 };
 constexpr int BARRIERS_PER_LAYER = 7;  // after QKV, ATT, MERGE, WO, UPGATE, QUANT, DOWN
+// With the SwiGLU act-quant fused into the up/gate phase the QUANT phase and
+// its barrier go: 6 barriers per layer.
+L3G_HD inline int barriers_per_layer(bool fuse_quant) { return fuse_quant ? 6 : 7; }
 
 struct Plan {
   int grid;       // CTAs (one per SM)
@@ -155,17 +158,21 @@ L3G_HD inline long long stage_offset(const Plan& p, int kvh, int t0, int st) {
   return ((long long)kvh * p.ctx + t0 + (long long)st * p.P) * p.row_bytes;
 }
 
-// Global index of barrier j (0..6) of layer l.  Arrivals are spread over
+// Global index of barrier j of layer l, bpl barriers per layer (the last
+// layer's last barrier is never run: the kernel ends).  Arrivals are spread over
 // nsub counters (1 to BAR_MAX_SUB, each on its own 128-byte line): CTA b adds
 // one to counter b % nsub, and barrier k is complete when every counter i
 // holds (k + 1) * sub_count(grid, nsub, i).  One counter makes every
 // arrival an atomic on the same address; several let the arrivals proceed
 // in parallel at the cost of one load per counter when polling.
-L3G_HD inline int barrier_index(int l, int j) { return l * BARRIERS_PER_LAYER + j; }
+L3G_HD inline int barrier_index(int l, int j, int bpl) { return l * bpl + j; }
 constexpr int BAR_STRIDE = 32;                      // 32-bit words between counters
 constexpr int BAR_MAX_SUB = 16;
 constexpr int BAR_ABORT = BAR_MAX_SUB * BAR_STRIDE;  // the step's abort word
 constexpr int BAR_WORDS = BAR_ABORT + 1;
+// After them: one arrival counter per Q8_0 block of the SwiGLU output (the
+// fused act-quant's handshake between the two 32-row groups of a block).
+constexpr int BAR_QCNT = BAR_WORDS;
 L3G_HD inline int sub_count(int grid, int nsub, int i) {
   return grid / nsub + (i < grid % nsub ? 1 : 0);
 }

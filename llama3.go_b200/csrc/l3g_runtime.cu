@@ -1003,6 +1003,8 @@ struct l3g_workspace {
   bool ps_on = false;
   persist::Plan ps_plan{};     // ctx is the state's, filled per capture
   int ps_ns = 0, ps_slot = 0, ps_union = 0, ps_xq_off = 0, ps_smem = 0, ps_nsub = 1;
+  bool ps_fuse = false;        // SwiGLU act-quant fused into the up/gate phase
+  int ps_bar_words = 0;        // words of d_bar that k_embed zeroes
   unsigned* d_bar = nullptr;   // grid-barrier counters and abort word (persist::BAR_*)
 };
 
@@ -1318,8 +1320,15 @@ static int persist_setup(l3g_workspace* ws) {
     cudaGetLastError();
     return L3G_OK;
   }
-  CUDA_TRY(cudaMalloc(&ws->d_bar, persist::BAR_WORDS * sizeof(unsigned)));
-  CUDA_TRY(cudaMemset(ws->d_bar, 0, persist::BAR_WORDS * sizeof(unsigned)));
+  // L3G_PERSIST_FUSE_QUANT=1: the SwiGLU act-quant runs in the up/gate phase
+  {
+    const char* env = getenv("L3G_PERSIST_FUSE_QUANT");
+    ws->ps_fuse = env && atoi(env) == 1 && p.wr[persist::M_UPGATE] == 32 &&
+                  p.rows[persist::M_UPGATE] % 64 == 0;
+  }
+  ws->ps_bar_words = persist::BAR_QCNT + m->ff_l / 32;
+  CUDA_TRY(cudaMalloc(&ws->d_bar, ws->ps_bar_words * sizeof(unsigned)));
+  CUDA_TRY(cudaMemset(ws->d_bar, 0, ws->ps_bar_words * sizeof(unsigned)));
   // barrier counters: L3G_PERSIST_BAR_SPREAD=n spreads the arrivals over n
   ws->ps_nsub = 1;
   if (const char* env = getenv("L3G_PERSIST_BAR_SPREAD"))
@@ -1634,6 +1643,8 @@ static PersistArgs persist_args(const l3g_workspace* ws, const l3g_state* s,
   a.kv_layer_bytes = s->layer_elems * (m->kv_f16 ? 2 : 4);
   a.bar = ws->d_bar;
   a.nsub = ws->ps_nsub;
+  a.fuse_quant = ws->ps_fuse ? 1 : 0;
+  a.bpl = persist::barriers_per_layer(ws->ps_fuse);
   a.res = ws->d_res;
   a.wait_ns = m->world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS;
   if (ws->tp_p2p) {
@@ -1688,7 +1699,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     CUDA_TRY(cudaMemcpyAsync(ws->d_samp, ws->h_samp, sizeof(SampleParams), cudaMemcpyHostToDevice, st));
   KL(L3G_K_EMBED, launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
                   hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res, ws->d_step,
-                  ws->ps_on ? ws->d_bar : nullptr));
+                  ws->ps_on ? ws->d_bar : nullptr, ws->ps_bar_words));
   if (ws->ps_on) {  // every layer in one persistent launch
     unsigned long long* stamps =
         tr && kPersistStampOff * 8 + persist_stamp_bytes(ws) <= kTraceBytes
@@ -2252,8 +2263,9 @@ extern "C" int l3g_workspace_persistent(const l3g_workspace* ws, int32_t* on) {
 }
 
 extern "C" int l3g_persist_layout(const l3g_workspace* ws, int32_t* stages, int32_t* slot_bytes,
-                                  int32_t* splits, int32_t* counters, int32_t* smem_bytes) {
-  if (!ws || !stages || !slot_bytes || !splits || !counters || !smem_bytes)
+                                  int32_t* splits, int32_t* counters, int32_t* smem_bytes,
+                                  int32_t* barriers_per_layer) {
+  if (!ws || !stages || !slot_bytes || !splits || !counters || !smem_bytes || !barriers_per_layer)
     return l3g_fail(L3G_E_INVALID, "null argument");
   if (!ws->ps_on) return l3g_fail(L3G_E_INVALID, "the workspace does not run the persistent kernel");
   *stages = ws->ps_ns;
@@ -2261,6 +2273,7 @@ extern "C" int l3g_persist_layout(const l3g_workspace* ws, int32_t* stages, int3
   *splits = ws->ps_plan.splits;
   *counters = ws->ps_nsub;
   *smem_bytes = ws->ps_smem;
+  *barriers_per_layer = persist::barriers_per_layer(ws->ps_fuse);
   return L3G_OK;
 }
 
@@ -2274,7 +2287,7 @@ extern "C" int l3g_persist_stamps(const l3g_workspace* ws, uint64_t* out, int64_
   if (cap < (int64_t)(bytes / 8)) return l3g_fail(L3G_E_INVALID, "capacity %lld < %zu", (long long)cap, bytes / 8);
   CUDA_TRY(cudaSetDevice(ws->device));
   CUDA_TRY(cudaMemcpy(out, ws->d_trace + kPersistStampOff, bytes, cudaMemcpyDeviceToHost));
-  *n_barriers = persist::BARRIERS_PER_LAYER * ws->ps_plan.n_layers;
+  *n_barriers = persist::barriers_per_layer(ws->ps_fuse) * ws->ps_plan.n_layers;
   *grid = ws->ps_plan.grid;
   return L3G_OK;
 }

@@ -123,7 +123,7 @@ def lib():
         "l3g_workspace_attention_layout": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
         "l3g_workspace_tp_p2p": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_workspace_persistent": (C.c_int, [_P, C.POINTER(C.c_int32)]),
-        "l3g_persist_layout": (C.c_int, [_P] + [C.POINTER(C.c_int32)] * 5),
+        "l3g_persist_layout": (C.c_int, [_P] + [C.POINTER(C.c_int32)] * 6),
         "l3g_persist_stamps": (C.c_int, [_P, C.POINTER(C.c_uint64), C.c_int64, C.POINTER(C.c_int32),
                                          C.POINTER(C.c_int32)]),
         "l3g_profile_step": (C.c_int, [_P, _P, _P, C.c_int32, C.POINTER(C.c_int32), C.POINTER(C.c_float),
@@ -454,16 +454,16 @@ class Workspace:
 
     def persist_layout(self) -> dict:
         """The persistent kernel's ring slots, slot bytes, attention splits,
-        barrier counters and shared memory per CTA."""
-        v = [C.c_int32() for _ in range(5)]
+        barrier counters, shared memory per CTA and grid barriers per layer."""
+        v = [C.c_int32() for _ in range(6)]
         _check(lib().l3g_persist_layout(self._h, *[C.byref(x) for x in v]))
-        return dict(zip(("stages", "slot_bytes", "splits", "barrier_counters", "smem_bytes"),
-                        (x.value for x in v)))
+        return dict(zip(("stages", "slot_bytes", "splits", "barrier_counters", "smem_bytes",
+                         "barriers_per_layer"), (x.value for x in v)))
 
     def persist_stamps(self) -> np.ndarray:
         """After Model.TraceStep on a persistent workspace: [barrier][cta][2]
         %globaltimer ns of each CTA's arrival at and release from each grid
-        barrier (7 per layer; zeros where none ran)."""
+        barrier (barriers_per_layer per layer; zeros where none ran)."""
         cap = 7 * self.model.HP.NLayers * 1024 * 2
         out = np.zeros(cap, np.uint64)
         nb, grid = C.c_int32(), C.c_int32()

@@ -46,6 +46,8 @@ bool check_plan(const Plan& p, const char* tag) {
   const int G = p.grid;
   CHECK(p.hkv * p.splits <= G, "%s: %d items on %d CTAs", tag, p.hkv * p.splits, G);
   CHECK((long long)(BARRIERS_PER_LAYER * p.n_layers + 1) * G < (1ll << 32), "%s: barrier count", tag);
+  CHECK(barrier_index(p.n_layers - 1, barriers_per_layer(false) - 1, barriers_per_layer(false)) <
+            BARRIERS_PER_LAYER * p.n_layers, "%s: barrier index", tag);
   const int layers[3] = {0, p.n_layers > 1 ? 1 : 0, p.n_layers - 1};
   const int ns[5] = {1, p.P, p.P + 1, p.ctx / 2 + 3, p.ctx};
   for (int li = 0; li < 3; ++li) {

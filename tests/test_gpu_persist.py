@@ -33,9 +33,11 @@ pytestmark = [
 ]
 
 
-def _load(gpu_lib, monkeypatch, cfg, T, persistent, **kw):
+def _load(gpu_lib, monkeypatch, cfg, T, persistent, fuse="0", spread="1", **kw):
     monkeypatch.setenv("L3G_RPW", "4")
     monkeypatch.setenv("L3G_ATT_CLUSTER", "0")
+    monkeypatch.setenv("L3G_PERSIST_FUSE_QUANT", fuse)
+    monkeypatch.setenv("L3G_PERSIST_BAR_SPREAD", spread)
     if persistent:
         monkeypatch.setenv("L3G_PERSIST", "1")
     else:
@@ -60,12 +62,18 @@ def _run(gpu_lib, m, cfg, ids, ctx, prefill=0):
     return ws, out, kv, hidden
 
 
-@pytest.mark.parametrize("name,n_tok,prefill,kv", [
-    ("tiny", 24, 0, "f32"), ("tiny-gqa", 24, 0, "f32"), ("small", 40, 0, "f32"),
-    ("small-hd128", 24, 0, "f32"), ("small-hd128", 24, 0, "f16"), ("tiny-g3", 24, 0, "f32"),
-    ("mid", 16, 0, "f32"), ("llama3.2-1b-2l", 12, 0, "f32"), ("small-hd128", 1500, 1496, "f32"),
+@pytest.mark.parametrize("name,n_tok,prefill,kv,fuse,spread", [
+    ("tiny", 24, 0, "f32", "0", "1"), ("tiny-gqa", 24, 0, "f32", "0", "1"),
+    ("small", 40, 0, "f32", "0", "1"), ("small-hd128", 24, 0, "f32", "0", "1"),
+    ("small-hd128", 24, 0, "f16", "0", "1"), ("tiny-g3", 24, 0, "f32", "0", "1"),
+    ("mid", 16, 0, "f32", "0", "1"), ("llama3.2-1b-2l", 12, 0, "f32", "0", "1"),
+    ("small-hd128", 1500, 1496, "f32", "0", "1"),
+    # the SwiGLU act-quant fused into up/gate, barrier arrivals spread over counters
+    ("tiny", 24, 0, "f32", "1", "3"), ("mid", 16, 0, "f32", "1", "16"),
+    ("llama3.2-1b-2l", 12, 0, "f32", "1", "1"), ("small", 40, 0, "f32", "0", "16"),
 ])
-def test_bit_identical_to_per_kernel_step(gpu_lib, monkeypatch, name, n_tok, prefill, kv):
+def test_bit_identical_to_per_kernel_step(gpu_lib, monkeypatch, name, n_tok, prefill, kv, fuse,
+                                          spread):
     import synthetic
     cfg, T = synthetic_model(name)
     ctx = max(64, n_tok + 8)
@@ -74,9 +82,12 @@ def test_bit_identical_to_per_kernel_step(gpu_lib, monkeypatch, name, n_tok, pre
     base = _load(gpu_lib, monkeypatch, cfg, T, False, **kw)
     ws0, l0, kv0, h0 = _run(gpu_lib, base, cfg, ids, ctx, prefill)
     assert not ws0.persistent()
-    pers = _load(gpu_lib, monkeypatch, cfg, T, True, **kw)
+    pers = _load(gpu_lib, monkeypatch, cfg, T, True, fuse, spread, **kw)
     ws1, l1, kv1, h1 = _run(gpu_lib, pers, cfg, ids, ctx, prefill)
     assert ws1.persistent()
+    lay = ws1.persist_layout()
+    assert lay["barriers_per_layer"] == (6 if fuse == "1" else 7)
+    assert lay["barrier_counters"] == int(spread)
     for i, (a, b) in enumerate(zip(l0, l1)):
         assert np.array_equal(a, b), (i, rel_l2(b, a))
     for layer, ((k0, v0), (k1, v1)) in enumerate(zip(kv0, kv1)):
@@ -84,14 +95,15 @@ def test_bit_identical_to_per_kernel_step(gpu_lib, monkeypatch, name, n_tok, pre
     assert np.array_equal(h0, h1)
 
 
-@pytest.mark.parametrize("name,n_tok", [("mid", 16), ("llama3.2-1b-2l", 12)])
-def test_logits_vs_reference(gpu_lib, oracle_mod, monkeypatch, name, n_tok):
+@pytest.mark.parametrize("name,n_tok,fuse", [("mid", 16, "0"), ("llama3.2-1b-2l", 12, "0"),
+                                            ("mid", 16, "1")])
+def test_logits_vs_reference(gpu_lib, oracle_mod, monkeypatch, name, n_tok, fuse):
     import synthetic
     cfg, T = synthetic_model(name)
     ctx = min(cfg.ctx_len, 256)
     ids = synthetic.prompt_ids(cfg, n_tok, seed=11)
     R = ReferenceRuns(oracle_mod, cfg, T, ids, ctx, with_f64=False)
-    m = _load(gpu_lib, monkeypatch, cfg, T, True)
+    m = _load(gpu_lib, monkeypatch, cfg, T, True, fuse)
     s = m.NewState(ctx)
     ws = m.NewWorkspace(ctx, 40)
     assert ws.persistent()
@@ -153,7 +165,7 @@ def test_device_loop_and_barrier_stamps(gpu_lib, monkeypatch):
     assert list(toks_dev) == toks
     m.TraceStep(s2, tok, ws)
     st = ws.persist_stamps()
-    nb = 7 * cfg.n_layers - 1  # the last layer's down phase ends the kernel
+    nb = ws.persist_layout()["barriers_per_layer"] * cfg.n_layers - 1  # the last down ends the kernel
     arr, rel = st[:nb, :, 0], st[:nb, :, 1]
     assert (arr > 0).all() and (rel >= arr).all()
     assert (rel.min(axis=1) >= arr.max(axis=1)).all()

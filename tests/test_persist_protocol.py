@@ -41,13 +41,24 @@ def sub_count(grid, nsub, i):
     return grid // nsub + (1 if i < grid % nsub else 0)
 
 
-def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1):
+def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1, fuse=False):
     rng = random.Random(seed)
     mdl = Model()
+    # phases run per layer (the fused act-quant drops QUANT) and barriers per layer
+    phs = [0, 1, 2, 3, 4, 6] if fuse else list(range(PHASES))
+    bpl = len(phs)
     # per CTA, per layer, per tiled phase: its tile count; the attention
     # phase's last stage of a CTA with stages is the one holding the step's K/V
     # (only some CTAs hold it: the last split of each kv head)
     tiles = [[{ph: rng.randint(0, 3) for ph in TILED} for _ in range(layers)] for _ in range(G)]
+    # up/gate: 2 * nblk row groups of nsl tiles, dealt round-robin; groups 2j
+    # and 2j + 1 hold the two halves of SwiGLU block j
+    nblk = [rng.randint(1, 4) for _ in range(layers)]
+    nsl_up = [rng.randint(1, 2) for _ in range(layers)]
+    ups = [[list(range(b, 2 * nblk[l], G)) for l in range(layers)] for b in range(G)]
+    for b in range(G):
+        for l in range(layers):
+            tiles[b][l][4] = len(ups[b][l]) * nsl_up[l]
     holds_pos = [[tiles[b][l][1] > 0 and rng.random() < 0.5 for l in range(layers)] for b in range(G)]
     seq = []  # per CTA: [(layer, phase, index, is_pos_stage)]
     for b in range(G):
@@ -65,6 +76,13 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
     def complete(k):
         """Barrier k is complete: every counter holds (k + 1) * its CTAs."""
         return all(counter[i] >= (k + 1) * sub_count(G, nsub, i) for i in range(nsub))
+    # fused act-quant state
+    GSL = ns + 2                                   # the kernel's MAX_STAGES + 2 for ns <= MAX_STAGES
+    act_written = [[[False] * NW for _ in range(2 * nblk[l])] for l in range(layers)]
+    gcnt = [[0] * GSL for _ in range(G)]           # shared-memory group counts per CTA
+    gown = [[None] * GSL for _ in range(G)]        # (layer, group) a slot counts
+    qcnt = [[0] * nblk[l] for l in range(layers)]  # global per-block counts
+    quantized = [[False] * nblk[l] for l in range(layers)]
     qkv_done = [[False] * G for _ in range(layers)]  # CTA b appended its K/V rows of layer l
     done_phase = [-1] * G  # highest (layer * PHASES + phase) every warp of CTA b finished
     warp_done = [[-1] * NW for _ in range(G)]
@@ -93,7 +111,7 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
             if c.abort:
                 break
             if pos and not skip_pos_wait:
-                while not complete(l * PHASES + 0):
+                while not complete(l * bpl + 0):
                     if c.abort or abort_word[0]:
                         c.abort = True
                         break
@@ -137,11 +155,14 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
         t = 0
         alive = True
         k = 0  # waits so far (for the injected timeout)
+        bi = 0  # barriers passed
         for l in range(layers):
-            for ph in range(PHASES):
+            for j, ph in enumerate(phs):
                 # every CTA finished the previous phase (what the barrier orders)
-                lin = l * PHASES + ph
+                lin = l * bpl + j
                 assert min(done_phase) >= lin - 1 or c.stop, ("phase started early", b, lin, done_phase)
+                if fuse and ph == 6:
+                    assert all(quantized[l]) or c.stop, "down phase before every block was quantized"
                 n = tiles[b][l][ph] if ph in TILED else 0
                 for i in range(n):
                     if alive:
@@ -164,8 +185,36 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
                             c.readers[s].discard(w)
                             c.empty[s].arrive()
                     t += 1
+                    if fuse and ph == 4 and alive and (i + 1) % nsl_up[l] == 0:
+                        # the group's epilogue, then ps_swiglu_quant
+                        kk = i // nsl_up[l]
+                        g = ups[b][l][kk]
+                        act_written[l][g][w] = True
+                        mdl.bump()
+                        yield
+                        slot = kk % GSL
+                        assert gown[b][slot] in (None, (l, g)), ("group count slot aliased", gown[b][slot], g)
+                        gown[b][slot] = (l, g)
+                        gcnt[b][slot] += 1
+                        mdl.bump()
+                        if gcnt[b][slot] == NW:
+                            gcnt[b][slot] = 0
+                            gown[b][slot] = None
+                            yield
+                            blk = g // 2
+                            old = qcnt[l][blk]
+                            qcnt[l][blk] += 1
+                            mdl.bump()
+                            if old == 1:
+                                yield
+                                assert all(act_written[l][2 * blk]) and all(act_written[l][2 * blk + 1]), \
+                                    "block quantized before both halves were written"
+                                quantized[l][blk] = True
+                                qcnt[l][blk] = 0
+                                mdl.bump()
+                        yield
                 warp_done[b][w] = lin
-                if l == layers - 1 and ph == PHASES - 1:
+                if l == layers - 1 and j == bpl - 1:
                     break  # the last layer's down phase has no barrier
                 # grid barrier
                 yield from cta_sync(c)
@@ -180,7 +229,7 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
                     else:
                         counter[b % nsub] += 1
                         mdl.bump()
-                        while not complete(lin):
+                        while not complete(bi):
                             if c.abort or abort_word[0]:
                                 stop = True
                                 break
@@ -188,6 +237,7 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
                     if stop:
                         c.abort = True
                     c.stop = stop
+                bi += 1
                 yield from cta_sync(c)
                 if c.stop:
                     break
@@ -233,7 +283,9 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
     assert all(exited)
     if not inject_abort:
         assert abort_word[0] == 0
-        assert sum(counter) == (layers * PHASES - 1) * G
+        assert sum(counter) == (layers * bpl - 1) * G
+        if fuse:
+            assert all(all(q) for q in quantized) and not any(any(q) for q in qcnt)
     return abort_word[0]
 
 
@@ -241,16 +293,19 @@ def run(G, NW, ns, layers, seed, inject_abort=False, skip_pos_wait=False, nsub=1
                                           (2, 4, 1, 1), (5, 2, 3, 2), (7, 2, 2, 3), (4, 2, 3, 4)])
 def test_persistent_protocol(G, NW, ns, nsub):
     """One barrier counter, or arrivals spread over nsub counters
-    (L3G_PERSIST_BAR_SPREAD), including grids that do not divide evenly."""
+    (L3G_PERSIST_BAR_SPREAD), including grids that do not divide evenly;
+    with and without the fused SwiGLU act-quant (L3G_PERSIST_FUSE_QUANT)."""
     for trial in range(25):
-        run(G, NW, ns, layers=2, seed=G * 1000 + NW * 100 + ns * 10 + trial, nsub=nsub)
+        for fuse in (False, True):
+            run(G, NW, ns, layers=2, seed=G * 1000 + NW * 100 + ns * 10 + trial, nsub=nsub, fuse=fuse)
 
 
 @pytest.mark.parametrize("G,NW,ns,nsub", [(3, 2, 2, 1), (4, 3, 3, 1), (5, 2, 3, 2)])
 def test_persistent_protocol_with_a_timeout(G, NW, ns, nsub):
     """One consumer wait gives up (a bounded wait running out): every CTA
     still reaches its exit, with no copy in flight."""
-    aborted = sum(run(G, NW, ns, layers=2, seed=7 * trial + G, inject_abort=True, nsub=nsub)
+    aborted = sum(run(G, NW, ns, layers=2, seed=7 * trial + G, inject_abort=True, nsub=nsub,
+                      fuse=trial % 2 == 1)
                   for trial in range(40))
     assert aborted >= 10  # the abort path ran, not just clean steps
 
@@ -266,3 +321,28 @@ def test_model_catches_a_missing_kv_wait():
             assert "K/V stage" in str(e), e
             caught += 1
     assert caught > 0
+
+
+def test_model_catches_a_small_group_count_ring():
+    """The replay is not vacuous for the fused act-quant either: with fewer
+    shared-memory count slots than the warps' drift (one slot), a fast warp
+    reuses a slot another group still counts, and the replay reports it."""
+    caught = 0
+    for trial in range(60):
+        try:
+            _run_with_gsl(trial)
+        except AssertionError as e:
+            assert "aliased" in str(e) or "before both halves" in str(e), e
+            caught += 1
+    assert caught > 0
+
+
+def _run_with_gsl(trial):
+    """run() with the count ring cut to one slot (a planted bug, in the model)."""
+    import inspect
+    import test_persist_protocol as mod
+    code = inspect.getsource(mod.run).replace("GSL = ns + 2", "GSL = 1")
+    ns_ = {}
+    exec(compile(code, "<planted>", "exec"), mod.__dict__, ns_)
+    ns_["run"](3, 3, 4, layers=2, seed=trial, fuse=True)
+
