@@ -21,260 +21,11 @@
 
 namespace l3g {
 
-constexpr int NW = 8;                   // consumer warps
-constexpr int NTHREADS = 32 * (NW + 1); // + one producer warp
-constexpr int MAX_STAGES = 16;
-// Shared memory per CTA kept under half an SM's 228 KB, so the next kernel's
-// CTA (programmatic dependent launch) can be resident and prefetching.
-constexpr int CTA_SMEM_SHARE = 112 * 1024;
-// Weight tile target: a 1-D bulk copy costs about 0.25 us per copy per CTA
-// on top of its bytes, so copies of ~32 KB are needed to approach HBM speed.
-constexpr int TILE_TARGET = 32 * 1024;
-constexpr int MAXG = 8;                 // max query heads per kv head
-constexpr unsigned long long WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s
-constexpr int MAX_TOPK = 64;  // largest top-K a workspace serves
-// Waits of a tensor-parallel step: a wait can depend, directly or through the
-// kernels launched early behind it, on another GPU's progress, which host
-// skew between the ranks' processes can delay by more than the local bound.
-constexpr unsigned long long WAIT_TIMEOUT_PEER_NS = 30000000000ull;  // 30 s
+#include "l3g_base.cuh"
 
-// device error codes (Result::err); Result::where names the wait site
-enum { ERR_NONE = 0, ERR_TIMEOUT = 1, ERR_TOKEN = 2 };
+#include "l3g_ptx.cuh"
 
-struct Result {        // copied to the host at the end of every step
-  int32_t token;       // argmax id (greedy)
-  float logit;         // its logit
-  int32_t err;         // ERR_*
-  int32_t where;       // wait site / detail
-};
-
-// ---------------------------------------------------------------------------
-// PTX helpers
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)),
-               "r"(count)
-               : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b,
-                                                      uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
-                   smem_u32(b)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b))
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// 1-D bulk copy global -> this CTA's shared memory; completion is signalled
-// as transaction bytes on the mbarrier.  src, dst 16-byte aligned, bytes a
-// multiple of 16.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src,
-                                         uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
-      "[%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void pdl_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void pdl_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-// An L2-only load whose value is discarded, issued before the dependency wait
-// on a buffer the previous kernel is still writing: it warms the address
-// translation of that buffer's page so the real loads after the wait do not
-// pay for it.  `.cg` keeps the (stale) line out of L1, so nothing read after
-// the wait can come from it.
-__device__ __forceinline__ void touch_page(const void* p) {
-  unsigned v;
-  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  (void)v;
-}
-// Device-scope atomic add with acquire-release semantics; returns the old value.
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-// Device-scope acquire load (counters shared by the CTAs of a grid).
-__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// System-scope acquire load / release store (flags shared across GPUs).
-__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// System-scope relaxed 64-bit accesses: single-copy atomic, so a {value,
-// epoch} word written by another GPU is seen whole or not at all.
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-// Thread-block cluster helpers (distributed shared memory).
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Every thread of every CTA of the cluster: release this CTA's shared-memory
-// writes, acquire the others'.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// The float at the same shared-memory offset as p in CTA `rank` of the cluster.
-__device__ __forceinline__ float ld_cluster_f32(const float* p, uint32_t rank) {
-  const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
-  return v;
-}
-// barrier 1: the NW consumer warps only (the producer warp never joins)
-__device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
-}
-__device__ __forceinline__ uint64_t gtime() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Device timeline (off when tr == nullptr): thread 0 of every CTA (up to
-// TRACE_CTAS per launch) stamps %globaltimer at a few points; launch `seq` of
-// the step owns tr[(seq * TRACE_CTAS + cta) * 8 + event].
-enum { TR_ENTRY = 0, TR_WAITED = 1, TR_PROLOGUE = 2, TR_LOOP = 3, TR_EXIT = 4 };
-constexpr int TRACE_CTAS = 256;
-__device__ __forceinline__ void trace_mark(unsigned long long* tr, int seq, int ev) {
-  if (tr == nullptr || threadIdx.x != 0) return;
-  const unsigned lin = blockIdx.x + blockIdx.y * gridDim.x;
-  if (lin >= (unsigned)TRACE_CTAS) return;
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  tr[((size_t)seq * TRACE_CTAS + lin) * 8 + ev] = t;
-}
-
-__device__ __forceinline__ void report(Result* res, int code, int where) {
-  if (atomicCAS(&res->err, 0, code) == 0) atomicExch(&res->where, where);
-}
-
-// Bounded wait for the phase of parity `parity` of mbarrier b.  Returns false
-// when the CTA's abort flag is set or when timeout_ns pass; the latter sets
-// the abort flag and reports ERR_TIMEOUT at `where`.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity,
-                                          volatile int* abort_flag,
-                                          Result* res, int where,
-                                          unsigned long long timeout_ns =
-                                              WAIT_TIMEOUT_NS) {
-  if (mbar_test(b, parity)) return true;
-  const uint64_t t0 = gtime();
-  for (;;) {
-    if (mbar_test(b, parity)) return true;
-    if (*abort_flag) return false;
-    if (gtime() - t0 > timeout_ns) {
-      *abort_flag = 1;
-      report(res, ERR_TIMEOUT, where);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-__host__ __device__ __forceinline__ int align_up(int x, int a) {
-  return (x + a - 1) / a * a;
-}
-
-// silu, internal/llama/math.go:16-19 (f64 exp, f32 divide)
-__device__ __forceinline__ float silu_ref(float x) {
-  return __fdiv_rn(x, __fadd_rn(1.0f, (float)exp(-(double)x)));
-}
-
-// One 32-element block of QuantizeQ8_0Into (q8_0.go:36-77), one value per
-// lane: scale = maxabs/127 (1e-8 when 0), q = trunc(v/scale +- 0.5) clamped.
-// Bit-identical to the reference for identical inputs.
-__device__ __forceinline__ void quant_block(float v, int b, int lane,
-                                            float* xd, int8_t* xqs) {
-  const float m = warp_max(fabsf(v));
-  float scale = __fdiv_rn(m, 127.0f);
-  if (scale == 0.0f) scale = 1e-8f;
-  const float inv = __fdiv_rn(1.0f, scale);
-  const float f = __fmul_rn(v, inv);
-  int q = f >= 0.0f ? (int)__fadd_rn(f, 0.5f) : (int)__fsub_rn(f, 0.5f);
-  q = min(127, max(-128, q));
-  xqs[b * 32 + lane] = (int8_t)q;
-  if (lane == 0) xd[b] = scale;
-}
-
-// The same block quantization with four consecutive values per lane and the
-// eight lanes (lane & 7) of an aligned lane group sharing one 32-value block
-// `blk`.  Every lane of the warp must call it (shuffles); lanes with
-// live == false only join the shuffles.
-__device__ __forceinline__ int8_t quant_one(float v, float inv) {
-  const float f = __fmul_rn(v, inv);
-  const int q = f >= 0.0f ? (int)__fadd_rn(f, 0.5f) : (int)__fsub_rn(f, 0.5f);
-  return (int8_t)min(127, max(-128, q));
-}
-__device__ __forceinline__ void quant_quad(float4 u, bool live, int blk, int sub, float* xd,
-                                           int8_t* xqs) {
-  float m = fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w)));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-  if (!live) return;
-  float scale = __fdiv_rn(m, 127.0f);
-  if (scale == 0.0f) scale = 1e-8f;
-  const float inv = __fdiv_rn(1.0f, scale);
-  char4 q;
-  q.x = quant_one(u.x, inv);
-  q.y = quant_one(u.y, inv);
-  q.z = quant_one(u.z, inv);
-  q.w = quant_one(u.w, inv);
-  *reinterpret_cast<char4*>(xqs + blk * 32 + sub * 4) = q;
-  if (sub == 0) xd[blk] = scale;
-}
+#include "l3g_helpers.cuh"
 
 #include "l3g_matvec.cuh"
 
@@ -513,59 +264,8 @@ __global__ void k_topk_final(const uint64_t* part, int count, int cap, int k,
   }
 }
 
-// ---------------------------------------------------------------------------
-// Load-time repack: GGUF Q8_0 rows (34-byte blocks, already on the device)
-// into the tiled layout.  Destination row r takes source row map(r):
-// concatenation of up to three row ranges, or the interleave (a_i, b_i).
-// Values are copied unchanged.
-// ---------------------------------------------------------------------------
-struct RepackArgs {
-  const uint8_t* src[3];
-  int src_row0[3];
-  int seg_rows[3];
-  int nseg;
-  int interleave2;        // dst 2i <- seg0 row i, dst 2i+1 <- seg1 row i
-  int src_blocks;         // blocks per source row
-  int blk0;               // first source block of the column slice
-  Q8Tiles dst;            // rows/cols of the destination
-  uint8_t* out;
-};
+#include "l3g_repack.cuh"
 
-__global__ void k_repack(const __grid_constant__ RepackArgs a) {
-  const int nbc = a.dst.cols / 32;
-  const long long total = (long long)a.dst.n_groups * a.dst.wr * nbc;
-  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const int r = (int)(e / nbc), b = (int)(e % nbc);
-    const int g = r / a.dst.wr, i = r % a.dst.wr;
-    const int bpt = a.dst.ck / 32;
-    const int s = b / bpt, bb = b % bpt;
-    uint8_t* tile = a.out + ((size_t)g * a.dst.nslices + s) * a.dst.tile_bytes;
-    uint8_t* qd = tile + (size_t)i * a.dst.ck + bb * 32;
-    uint8_t* dd = tile + (size_t)a.dst.wr * a.dst.ck + ((size_t)i * bpt + bb) * 2;
-    const uint8_t* blk = nullptr;
-    if (r < a.dst.rows) {
-      int seg = 0, sr = r;
-      if (a.interleave2) {
-        seg = r & 1;
-        sr = r >> 1;
-      } else {
-        while (seg < a.nseg - 1 && sr >= a.seg_rows[seg]) sr -= a.seg_rows[seg++];
-      }
-      blk = a.src[seg] + ((size_t)(a.src_row0[seg] + sr) * a.src_blocks + a.blk0 + b) * 34;
-    }
-    if (blk) {
-      dd[0] = blk[0];
-      dd[1] = blk[1];
-#pragma unroll 8
-      for (int j = 0; j < 32; ++j) qd[j] = blk[2 + j];
-    } else {
-      dd[0] = 0;
-      dd[1] = 0;
-      for (int j = 0; j < 32; ++j) qd[j] = 0;
-    }
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Failure-detection self test: a bounded wait on an mbarrier that nothing

@@ -99,10 +99,6 @@ __host__ __device__ inline int ps_union_bytes(int max_cols, int group, int hd, i
   return align_up(u, 1024);
 }
 
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 __device__ __forceinline__ unsigned* ps_abort_word(const PersistArgs& a) {
   return a.bar + persist::BAR_ABORT;
 }
@@ -755,7 +751,7 @@ __device__ void ps_reduce(const PersistArgs& a, unsigned e) {
 template <int DPL, typename KT, int GP>
 __global__ void __launch_bounds__(NTHREADS, 1) k_layers(const __grid_constant__ PersistArgs a) {
   using namespace persist;
-  extern __shared__ __align__(1024) uint8_t smem[];
+  L3G_DYNAMIC_SMEM(smem);
   PSmem* sh = reinterpret_cast<PSmem*>(smem);
   uint8_t* uni = smem + PS_HEAD;
   uint8_t* ring = uni + a.union_bytes;
