@@ -8,7 +8,7 @@
  *     (WorkerPool.Run / ParallelFor), held as Model.Pool (model.go:52);
  *   - the per-token forward  internal/llama/infer.go:21-267 and :269-511.
  * The Go Model / State / Workspace / Sampler API stays; each of its calls maps
- * onto one entry point below (see INTEGRATION.md).
+ * onto one entry point below.
  *
  * Conventions
  *   - Every function returns an int status: L3G_OK (0) or a negative code;

@@ -128,6 +128,21 @@ def test_library_fails_loudly_without_a_gpu():
         l3g.Matrix(np.zeros(34, np.uint8), 1, 32)
 
 
+def test_c_abi_from_plain_c(tmp_path):
+    """The header and the library as a cgo preamble sees them: tests/c_abi_check.c
+    compiled as strict C99 (no C++), linked against libl3g.so and run without
+    a GPU (host-only entries, error codes and messages, null handles)."""
+    l3g = _lib()
+    exe = str(tmp_path / "c_abi_check")
+    libdir = os.path.dirname(l3g.LIB_PATH)
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                    "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "c_abi_check.c"),
+                    "-L", libdir, "-ll3g", f"-Wl,-rpath,{libdir}", "-o", exe], check=True)
+    out = subprocess.run([exe, str(tmp_path)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0 and out.stdout.strip() == "ok", out.stderr
+
+
 def test_header_cites_reference_for_each_entry():
     hdr = open(os.path.join(ROOT, "include", "l3g.h")).read()
     for ref in ("simd.h:7-9", "workers.go", "infer.go:21-267", "infer.go:269-511",
