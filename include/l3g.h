@@ -185,6 +185,18 @@ int l3g_forward(l3g_model *m, l3g_state *s, l3g_workspace *ws, int32_t token,
 int l3g_forward_topk(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                      int32_t token, int32_t top_k, l3g_topk_item *items,
                      int32_t *n_items);
+/* The attention softmax of ForwardTopKIntoWorkspace exactly as the reference
+ * computes it (infer.go:376-423): weights fastExp(score - max) with max over
+ * all positions (infer.go:404,520-525) instead of the exact exp of
+ * ForwardIntoWorkspace (infer.go:130-175).  With on = 1 the top-K and sampled
+ * calls of this workspace (l3g_forward_topk, l3g_forward_sample,
+ * l3g_decode_sample) run that attention, so their items are the reference
+ * top-K path's; l3g_forward, l3g_forward_argmax, l3g_decode_greedy and
+ * l3g_prefill keep the exact exp, as the reference's full path does.  Off
+ * (the exact exp everywhere) by default.  The first call with on = 1
+ * allocates the pass's scratch (scores of every local query head over the
+ * workspace's context), so make it before any stream capture. */
+int l3g_workspace_set_topk_fast_exp(l3g_workspace *ws, int32_t on);
 /* Greedy decode step: argmax (lowest id on ties) of the logits that
  * l3g_forward would return, computed on the device. */
 int l3g_forward_argmax(l3g_model *m, l3g_state *s, l3g_workspace *ws,

@@ -31,6 +31,8 @@ namespace l3g {
 
 #include "l3g_attention.cuh"
 
+#include "l3g_attention_fast.cuh"
+
 #include "l3g_persist.cuh"
 
 #include "l3g_gemm.cuh"

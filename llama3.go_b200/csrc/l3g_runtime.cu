@@ -1006,6 +1006,15 @@ struct l3g_workspace {
   bool ps_fuse = false;        // SwiGLU act-quant fused into the up/gate phase
   int ps_bar_words = 0;        // words of d_bar that k_embed zeroes
   unsigned* d_bar = nullptr;   // grid-barrier counters and abort word (persist::BAR_*)
+  // the top-K path's fastExp attention (l3g_workspace_set_topk_fast_exp):
+  // scores [local q heads][ctx], per-split max / sum [kv heads][splits][group],
+  // per-split sum of e * V [kv heads][splits][group][hd]
+  bool topk_fast = false;
+  int attf_splits = 0;
+  float* attf_scores = nullptr;
+  float* attf_pmax = nullptr;
+  float* attf_psum = nullptr;
+  float* attf_po = nullptr;
 };
 
 static void ws_release(l3g_workspace* ws) {
@@ -1026,7 +1035,8 @@ static void ws_release(l3g_workspace* ws) {
   for (void* p : dptrs)
     if (p) cudaFree(p);
   void* pf[] = {ws->pf_ids, ws->pf_x, ws->pf_y, ws->pf_qkv, ws->pf_q, ws->pf_att, ws->pf_ug,
-                ws->pf_act, ws->pf_part};
+                ws->pf_act, ws->pf_part, ws->attf_scores, ws->attf_pmax, ws->attf_psum,
+                ws->attf_po};
   for (void* p : pf)
     if (p) cudaFree(p);
   void* hptrs[] = {ws->h_io, ws->h_res, ws->h_logits, ws->h_tk_ids, ws->h_tk_logits, ws->h_samp};
@@ -1565,6 +1575,43 @@ static cudaError_t launch_attention(const l3g_workspace* ws, const AttnArgs& a, 
   return cudaErrorInvalidValue;
 }
 
+// The top-K path's attention (fastExp of score - max over all positions,
+// infer.go:376-423) in three passes: 0 scores, 1 values, 2 merge + act-quant.
+template <int DPL, typename KT>
+static cudaError_t launch_attf_g(const AttfArgs& a, dim3 grid, cudaStream_t st, int pass) {
+  if (pass == 0) return launch(k_attf_scores<DPL, KT>, grid, dim3(ATTF_THREADS), 0, st, a);
+  return launch(k_attf_values<DPL, KT>, grid, dim3(ATTF_THREADS), 0, st, a);
+}
+
+static cudaError_t launch_attention_fast(const l3g_workspace* ws, const AttfArgs& a,
+                                         cudaStream_t st, int pass) {
+  const l3g_model* m = ws->m;
+  if (pass == 2)
+    return launch(k_attf_merge, dim3((a.n_blocks + NW - 1) / NW), dim3(ATTF_THREADS), 0, st, a);
+  const dim3 grid(m->hkv_l, ws->attf_splits);
+  const int dpl = m->hd / 32;
+  if (m->kv_f16) {
+    if (dpl == 2) return launch_attf_g<2, __half>(a, grid, st, pass);
+    if (dpl == 4) return launch_attf_g<4, __half>(a, grid, st, pass);
+    return cudaErrorInvalidValue;
+  }
+  if (dpl == 1) return launch_attf_g<1, float>(a, grid, st, pass);
+  if (dpl == 2) return launch_attf_g<2, float>(a, grid, st, pass);
+  if (dpl == 4) return launch_attf_g<4, float>(a, grid, st, pass);
+  return cudaErrorInvalidValue;
+}
+
+// Whether a step of this variant runs the top-K path's fastExp attention:
+// the top-K and sampled calls (ForwardTopKIntoWorkspace, infer.go:269-511)
+// once the workspace asked for it; the logits, argmax, greedy and prefill
+// calls (ForwardIntoWorkspace, infer.go:21-267) always use the exact exp.
+static bool uses_fast_attention(const l3g_workspace* ws, int variant) {
+  return ws->topk_fast && (variant == V_TOPK || variant == V_SAMPLE || variant == V_SAMPLE_DEV);
+}
+// Graphs of a variant captured with the fastExp attention are cached under
+// this bit added to the variant.
+constexpr int kFastGraphKey = 0x100;
+
 // merges the per-rank argmax results gathered by NCCL (largest logit, lowest
 // id on ties; first error wins)
 __global__ void k_merge_argmax(const Result* g, int world, Result* out) {
@@ -1693,14 +1740,16 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
   } while (0)
   const bool device_fed = variant == V_GREEDY_DEV || variant == V_SAMPLE_DEV;
   const bool sampled = variant == V_SAMPLE || variant == V_SAMPLE_DEV;
+  const bool fast_att = uses_fast_attention(ws, variant);
+  const bool persistent = ws->ps_on && !fast_att;  // k_layers has the exact-exp attention only
   if (!device_fed)
     CUDA_TRY(cudaMemcpyAsync(ws->d_io, ws->h_io, 16, cudaMemcpyHostToDevice, st));
   if (variant == V_SAMPLE)
     CUDA_TRY(cudaMemcpyAsync(ws->d_samp, ws->h_samp, sizeof(SampleParams), cudaMemcpyHostToDevice, st));
   KL(L3G_K_EMBED, launch(k_embed, dim3((ne + 255) / 256), dim3(256), 0, st, (const uint8_t*)m->emb,
                   hp.vocab_size, ne, (const int*)ws->d_io, ws->x[0], ws->d_res, ws->d_step,
-                  ws->ps_on ? ws->d_bar : nullptr, ws->ps_bar_words));
-  if (ws->ps_on) {  // every layer in one persistent launch
+                  persistent ? ws->d_bar : nullptr, ws->ps_bar_words));
+  if (persistent) {  // every layer in one persistent launch
     unsigned long long* stamps =
         tr && kPersistStampOff * 8 + persist_stamp_bytes(ws) <= kTraceBytes
             ? ws->d_trace + kPersistStampOff
@@ -1724,7 +1773,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     KL(L3G_K_LAYERS, cudaLaunchKernelExC(&cfg, kfn, kargs));
   }
   // the per-kernel step (skipped when the persistent kernel ran the layers)
-  for (int l = 0; !ws->ps_on && l < hp.n_layers; ++l) {
+  for (int l = 0; !persistent && l < hp.n_layers; ++l) {
     const LayerW& L = m->layers[l];
     uint8_t* kv = static_cast<uint8_t*>(s->kv) + (size_t)l * s->layer_elems * es;
     {  // RMSNorm -> act-quant -> QKV -> RoPE -> KV append, infer.go:67-127
@@ -1774,7 +1823,28 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      KL(L3G_K_ATTN, launch_attention(ws, a, st));
+      if (fast_att) {  // the top-K path's fastExp softmax, infer.go:376-423
+        AttfArgs f{};
+        f.q = ws->q;
+        f.kv = kv;
+        f.ctx = s->ctx;
+        f.hd = hd;
+        f.group = m->group;
+        f.splits = ws->attf_splits;
+        f.n_blocks = m->hq_l * hd / 32;
+        f.scale = a.scale;
+        f.io = ws->d_io;
+        f.scores = ws->attf_scores;
+        f.pmax = ws->attf_pmax;
+        f.psum = ws->attf_psum;
+        f.po = ws->attf_po;
+        f.out = ws->attn;
+        f.out_d = ws->attn_d;
+        f.out_q = ws->attn_q;
+        for (int pass = 0; pass < 3; ++pass) KL(L3G_K_ATTN, launch_attention_fast(ws, f, st, pass));
+      } else {
+        KL(L3G_K_ATTN, launch_attention(ws, a, st));
+      }
     }
     {  // Wo on the attention output the merge quantized, infer.go:178-187
        // (residual add fused downstream)
@@ -1902,8 +1972,9 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
 
 static int get_graph(l3g_workspace* ws, const l3g_state* s, int variant, int k,
                      cudaGraphExec_t* out) {
+  const int key = variant | (uses_fast_attention(ws, variant) ? kFastGraphKey : 0);
   for (auto& g : ws->graphs)
-    if (g.variant == variant && g.k == k && g.state_serial == s->serial) {
+    if (g.variant == key && g.k == k && g.state_serial == s->serial) {
       *out = g.exec;
       return L3G_OK;
     }
@@ -1929,7 +2000,7 @@ static int get_graph(l3g_workspace* ws, const l3g_state* s, int variant, int k,
   e = cudaGraphInstantiate(&exec, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
-  ws->graphs.push_back({variant, k, s->serial, exec});
+  ws->graphs.push_back({key, k, s->serial, exec});
   if (ws->m->world > 1) {
     // ranks capture at their own pace; line them up before the first launch
     // so that none waits on a peer that is still capturing
@@ -2253,6 +2324,38 @@ extern "C" int l3g_trace_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int
   for (int i = 0; i < out_n; ++i) kinds[i] = ws->trace_kinds_graph[i];
   *n = out_n;
   s->pos++;
+  return L3G_OK;
+}
+
+extern "C" int l3g_workspace_set_topk_fast_exp(l3g_workspace* ws, int32_t on) {
+  if (!ws) return l3g_fail(L3G_E_INVALID, "null argument");
+  if (on != 0 && on != 1) return l3g_fail(L3G_E_INVALID, "on must be 0 or 1, got %d", on);
+  const l3g_model* m = ws->m;
+  if (on && !ws->attf_scores) {
+    const int hd = m->hd, G = m->group;
+    if (hd % 32 || hd > ATTF_MAX_HD || G > MAXG)
+      return l3g_fail(L3G_E_INVALID, "fastExp attention: head dim %d, group %d unsupported", hd, G);
+    // about two CTAs per SM over the kv heads, at least NW positions a split
+    const int S = std::max(1, std::min({(2 * m->nsm + m->hkv_l - 1) / m->hkv_l,
+                                        (ws->ctx + NW - 1) / NW, 64}));
+    CUDA_TRY(cudaSetDevice(ws->device));
+    const size_t parts = (size_t)m->hkv_l * S * G;
+    float* p[4] = {nullptr, nullptr, nullptr, nullptr};
+    const size_t floats[4] = {(size_t)m->hq_l * ws->ctx, parts, parts, parts * hd};
+    for (int i = 0; i < 4; ++i) {
+      if (cudaMalloc(&p[i], floats[i] * 4) != cudaSuccess) {
+        cudaGetLastError();
+        for (int j = 0; j < i; ++j) cudaFree(p[j]);
+        return l3g_fail(L3G_E_CUDA, "fastExp attention scratch: out of device memory");
+      }
+    }
+    ws->attf_scores = p[0];
+    ws->attf_pmax = p[1];
+    ws->attf_psum = p[2];
+    ws->attf_po = p[3];
+    ws->attf_splits = S;
+  }
+  ws->topk_fast = on == 1;
   return L3G_OK;
 }
 

@@ -123,6 +123,7 @@ def lib():
         "l3g_workspace_attention_layout": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
         "l3g_workspace_tp_p2p": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_workspace_persistent": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+        "l3g_workspace_set_topk_fast_exp": (C.c_int, [_P, C.c_int32]),
         "l3g_persist_layout": (C.c_int, [_P] + [C.POINTER(C.c_int32)] * 6),
         "l3g_persist_stamps": (C.c_int, [_P, C.POINTER(C.c_uint64), C.c_int64, C.POINTER(C.c_int32),
                                          C.POINTER(C.c_int32)]),
@@ -433,6 +434,14 @@ class Workspace:
         out = np.empty(n, np.float32)
         _check(lib().l3g_workspace_read(self._h, which, _fptr(out), n))
         return out
+
+    def SetTopKFastExp(self, on: bool = True):
+        """ForwardTopKIntoWorkspace's attention softmax as the reference
+        computes it (fastExp of score - max over all positions,
+        infer.go:376-423, 520-525) for this workspace's top-K and sampled
+        calls; the full-logits, argmax and greedy calls keep the exact exp
+        of ForwardIntoWorkspace.  Off by default."""
+        _check(lib().l3g_workspace_set_topk_fast_exp(self._h, 1 if on else 0))
 
     def kernels_per_step(self) -> int:
         v = C.c_int32()
