@@ -117,6 +117,7 @@ int main(int argc, char **argv) {
   CHECK(l3g_model_load(NULL, NULL, 0, &opt, &m) == L3G_E_INVALID);
   CHECK(l3g_forward(NULL, NULL, NULL, 0, NULL) == L3G_E_INVALID);
   CHECK(l3g_state_new(NULL, 16, NULL) == L3G_E_INVALID);
+  CHECK(l3g_workspace_set_topk_fast_exp(NULL, 1) == L3G_E_INVALID);
   l3g_model_free(NULL);
   l3g_state_free(NULL);
   l3g_workspace_free(NULL);

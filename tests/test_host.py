@@ -143,6 +143,59 @@ def test_c_abi_from_plain_c(tmp_path):
     assert out.returncode == 0 and out.stdout.strip() == "ok", out.stderr
 
 
+def _split_args(text, open_at):
+    """Top-level comma-separated arguments of the call whose '(' is at
+    text[open_at]; returns (args, index after the closing ')')."""
+    depth, cur, args, i = 0, "", [], open_at
+    while True:
+        ch = text[i]
+        if ch in "([{":
+            depth += 1
+            if depth > 1:
+                cur += ch
+        elif ch in ")]}":
+            depth -= 1
+            if depth == 0:
+                break
+            cur += ch
+        elif ch == "," and depth == 1:
+            args.append(cur.strip())
+            cur = ""
+        else:
+            cur += ch
+        i += 1
+    if cur.strip():
+        args.append(cur.strip())
+    return args, i + 1
+
+
+def test_go_shim_calls_match_the_header():
+    """Every C.l3g_* call of the Go shim (the cgo code a maintainer adds)
+    names a function the header declares, with as many arguments as the
+    declaration; every C.l3g_* type and C.L3G_* constant it uses exists."""
+    import re
+    hdr = open(os.path.join(ROOT, "include", "l3g.h")).read()
+    nparams = {}
+    for mt in re.finditer(r"\b(l3g_[a-z0-9_]+)\s*\(", hdr):
+        args, _ = _split_args(hdr, mt.end() - 1)
+        nparams[mt.group(1)] = 0 if args == ["void"] else len(args)
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    go = "\n".join(re.findall(r"```go\n(.*?)```", doc, re.S))
+    assert "C.l3g_forward" in go
+    calls = 0
+    for mt in re.finditer(r"\bC\.(l3g_[a-z0-9_]+)\s*\(", go):
+        name = mt.group(1)
+        assert name in nparams, name
+        args, _ = _split_args(go, mt.end() - 1)
+        assert len(args) == nparams[name], (name, args, nparams[name])
+        calls += 1
+    assert calls >= 8
+    for name in set(re.findall(r"\bC\.(l3g_[a-z0-9_]+)\b(?!\s*\()", go)):
+        assert re.search(r"\b%s\s*;" % name, hdr), name  # a typedef name
+    for name in set(re.findall(r"\bC\.(L3G_[A-Z0-9_]+)", go)):
+        assert re.search(r"#define\s+%s\b" % name, hdr), name
+
+
 def test_header_cites_reference_for_each_entry():
     hdr = open(os.path.join(ROOT, "include", "l3g.h")).read()
     for ref in ("simd.h:7-9", "workers.go", "infer.go:21-267", "infer.go:269-511",
