@@ -9,7 +9,7 @@ a pair) eventually round some value on opposite sides of a quantization
 boundary; that flip perturbs the next stage's inputs, which flips more values,
 and the difference saturates at the quantization noise level (about 1% of the
 logits) within a few steps.  A float64 implementation of the same algorithm
-shows the same band.  The north-star bar (logits within 1e-2 relative L2,
+shows the same band.  The parity bar (logits within 1e-2 relative L2,
 greedy ids equal except where the top-2 gap is below 1e-3) is therefore
 applied together with this measured band: the GPU may differ from the cgo
 reference by no more than the reference's other builds do on the same inputs.

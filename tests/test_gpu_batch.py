@@ -5,7 +5,7 @@ Sessions with different prompt lengths (so different positions and, across
 256-position splits, different attention split counts) step together.  Per
 session:
 - the logits equal the single-session l3g_forward logits on a clone of the
-  state within the north-star tolerance (1e-2 relative L2; both compute the
+  state within the parity tolerance (1e-2 relative L2; both compute the
   same quantized arithmetic, the batched path with fp32 sums in another
   order), and the K/V rows the step appends match within 1e-4;
 - the sampled id equals SampleTopK restated on the host (tests/sampler_ref)

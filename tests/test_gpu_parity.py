@@ -361,7 +361,7 @@ def test_fp16_kv_cache(gpu_lib, oracle_mod):
     # fp16 storage rounds every K/V value (about 5e-4 relative), which starts
     # the same quantization-flip cascade as a summation-order change; it is a
     # precision option outside the reference's f32 layout, bounded at twice
-    # the north-star tolerance
+    # the parity tolerance
     assert max(errs) < max(2 * R.tol(), 2e-2), (max(errs), R.band())
 
 
