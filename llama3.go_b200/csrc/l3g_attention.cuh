@@ -113,7 +113,7 @@ template <int DPL, typename KT, int GP, bool CL>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ AttnArgs a) {
   constexpr int SB = 32 / GP;  // positions per sub-batch
-  extern __shared__ __align__(1024) uint8_t smem[];
+  L3G_DYNAMIC_SMEM(smem);
   AttnSmem* sh = reinterpret_cast<AttnSmem*>(smem);
   float* pbuf_all = reinterpret_cast<float*>(smem + AT_HEAD);
   float* hbuf_all = pbuf_all + NW * 32;

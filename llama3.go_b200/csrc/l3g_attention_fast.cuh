@@ -60,10 +60,22 @@ __device__ __forceinline__ void attf_range(int n, int splits, int s, int* t0, in
 constexpr int ATTF_THREADS = NW * 32;
 constexpr int ATTF_MAX_HD = 128;
 
+// Dynamic shared memory of the two passes.
+struct AttfScoresSmem {
+  float qs[MAXG * ATTF_MAX_HD];  // the kv head's query heads
+  float wmax[NW][MAXG];          // per-warp maxima
+};
+struct AttfValuesSmem {
+  float hmax[MAXG];                   // the heads' maxima over all splits
+  float wsum[NW][MAXG];               // per-warp sums of e
+  float wo[NW * MAXG * ATTF_MAX_HD];  // per-warp sums of e * V [warp][h][hd]
+};
+
 template <int DPL, typename KT>
 __global__ void __launch_bounds__(ATTF_THREADS) k_attf_scores(const __grid_constant__ AttfArgs a) {
-  __shared__ __align__(16) float qs[MAXG * ATTF_MAX_HD];
-  __shared__ float wmax[NW][MAXG];
+  L3G_DYNAMIC_SMEM(smem);
+  AttfScoresSmem& sm = *reinterpret_cast<AttfScoresSmem*>(smem);
+  float* qs = sm.qs;
   pdl_launch_dependents();
   pdl_wait();  // q, the appended K row and the position come from the QKV kernel
   const int g = blockIdx.x, s = blockIdx.y;
@@ -95,21 +107,22 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attf_scores(const __grid_const
   }
   if (lane == 0)
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h) wmax[warp][h] = mx[h];
+    for (int h = 0; h < MAXG; ++h) sm.wmax[warp][h] = mx[h];
   __syncthreads();
   if (threadIdx.x < G) {
     float m = -1e30f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) m = fmaxf(m, wmax[w][threadIdx.x]);
+    for (int w = 0; w < NW; ++w) m = fmaxf(m, sm.wmax[w][threadIdx.x]);
     a.pmax[((size_t)g * a.splits + s) * G + threadIdx.x] = m;
   }
 }
 
 template <int DPL, typename KT>
 __global__ void __launch_bounds__(ATTF_THREADS) k_attf_values(const __grid_constant__ AttfArgs a) {
-  __shared__ float hmax[MAXG];
-  __shared__ float wsum[NW][MAXG];
-  __shared__ __align__(16) float wo[NW * MAXG * ATTF_MAX_HD];  // [warp][h][hd]
+  L3G_DYNAMIC_SMEM(smem);
+  AttfValuesSmem& sm = *reinterpret_cast<AttfValuesSmem*>(smem);
+  float* hmax = sm.hmax;
+  float* wo = sm.wo;
   pdl_launch_dependents();
   pdl_wait();  // the scores and split maxima of k_attf_scores
   const int g = blockIdx.x, s = blockIdx.y;
@@ -151,7 +164,7 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attf_values(const __grid_const
     if (h < G) {
 #pragma unroll
       for (int j = 0; j < DPL; ++j) wo[((size_t)warp * MAXG + h) * hd + lane * DPL + j] = o[h][j];
-      if (lane == 0) wsum[warp][h] = l[h];
+      if (lane == 0) sm.wsum[warp][h] = l[h];
     }
   }
   __syncthreads();
@@ -165,7 +178,7 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attf_values(const __grid_const
     if (d == 0) {
       float ls = 0.0f;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) ls = __fadd_rn(ls, wsum[w][h]);
+      for (int w = 0; w < NW; ++w) ls = __fadd_rn(ls, sm.wsum[w][h]);
       a.psum[pb + h] = ls;
     }
   }

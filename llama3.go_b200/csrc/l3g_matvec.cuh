@@ -293,7 +293,7 @@ __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int n
 template <int PRO, int EPI, int RPW, int VK>
 __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     k_matvec(const __grid_constant__ MatvecArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  L3G_DYNAMIC_SMEM(smem);
   MatvecSmem* sh = reinterpret_cast<MatvecSmem*>(smem);
   const int C = a.w.cols;
   float* xd = reinterpret_cast<float*>(smem + MV_HEAD);

@@ -1579,8 +1579,9 @@ static cudaError_t launch_attention(const l3g_workspace* ws, const AttnArgs& a, 
 // infer.go:376-423) in three passes: 0 scores, 1 values, 2 merge + act-quant.
 template <int DPL, typename KT>
 static cudaError_t launch_attf_g(const AttfArgs& a, dim3 grid, cudaStream_t st, int pass) {
-  if (pass == 0) return launch(k_attf_scores<DPL, KT>, grid, dim3(ATTF_THREADS), 0, st, a);
-  return launch(k_attf_values<DPL, KT>, grid, dim3(ATTF_THREADS), 0, st, a);
+  if (pass == 0)
+    return launch(k_attf_scores<DPL, KT>, grid, dim3(ATTF_THREADS), sizeof(AttfScoresSmem), st, a);
+  return launch(k_attf_values<DPL, KT>, grid, dim3(ATTF_THREADS), sizeof(AttfValuesSmem), st, a);
 }
 
 static cudaError_t launch_attention_fast(const l3g_workspace* ws, const AttfArgs& a,

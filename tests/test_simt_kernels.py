@@ -1,0 +1,224 @@
+"""Device kernels run on the CPU under the SIMT emulator (tests/simt/): the
+kernels' own source, built for the host with software versions of the
+inline-PTX helpers, every CUDA thread a coroutine (tests/simt/simt.h).
+
+Covered here, against the oracle and the reference's loops:
+- the persistent decode step (k_layers: every layer of a token in one
+  launch, grid barriers between the phases, one producer warp per CTA
+  streaming weight tiles and K|V stages through a bulk-copy ring): hidden
+  state, last-layer attention output and the appended K/V of every layer
+  against the oracle (the reference's Go forward restated, linked to its
+  simd.c), for head sizes 32, 64 and 128, query heads per kv head 2 and 3,
+  1 to 4 attention splits with several stages each, f32 and f16 caches;
+  bit-identical across random schedules and copy delays, with and without
+  the fused SwiGLU act-quant, with spread barrier counters and a two-slot
+  ring; and the abort path when a CTA never arrives;
+- the top-K path's fastExp attention (k_attf_scores / values / merge)
+  against the reference's loop (infer.go:376-423).
+
+What the emulator does not check: the hardware memory model (one OS thread
+runs every coroutine, so memory is sequentially consistent), timing, and
+anything of the tensor cores.
+"""
+import dataclasses
+
+import numpy as np
+import pytest
+
+from conftest import synthetic_model
+from refspread import rel_l2
+
+
+@pytest.fixture(scope="module")
+def S():
+    import simt_lib
+    simt_lib.lib()
+    simt_lib.lib().emu_schedule(0, 0, 0)
+    return simt_lib
+
+
+def _model(name, ctx):
+    cfg, T = synthetic_model(name)
+    if ctx > cfg.ctx_len:
+        cfg = dataclasses.replace(cfg, ctx_len=ctx)
+    return cfg, T
+
+
+def _oracle_after(oracle_mod, cfg, T, ids, ctx):
+    om = oracle_mod.OracleModel(cfg, T)
+    om.new_state(ctx)
+    for t in ids:
+        om.forward(int(t), logits=False)
+    return om
+
+
+# (config, prefix positions, tokens stepped, grid, kv f16, step options)
+CASES = [
+    ("tiny-gqa", 0, 3, 4, False, {}),                       # hd 32, G 2, one split
+    ("tiny-gqa", 600, 2, 8, False, {}),                     # 4 splits x 2 stages
+    ("tiny-g3", 300, 2, 5, False, {}),                      # G 3 (padded to 4)
+    ("small", 200, 2, 6, False, {"fuse_quant": 1}),         # hd 64, fused act-quant
+    ("small-hd128", 100, 2, 3, False, {}),                  # hd 128, one kv head
+    ("tiny-gqa", 260, 2, 7, False, {"max_stages": 2, "nsub": 4}),
+    ("small", 100, 2, 6, True, {}),                         # f16 cache
+]
+
+
+@pytest.mark.parametrize("name,prefix,n,grid,f16,kw", CASES)
+def test_persistent_step_matches_oracle(S, oracle_mod, name, prefix, n, grid, f16, kw):
+    import synthetic
+    ctx = prefix + n + 3
+    cfg, T = _model(name, ctx)
+    ids = synthetic.prompt_ids(cfg, prefix + n, seed=3)
+    om = _oracle_after(oracle_mod, cfg, T, ids[:prefix], ctx)
+    pm = S.PersistentModel(cfg, T, ctx, grid, kv_f16=f16)
+    if prefix:
+        K, V = om.kv_arrays()
+        pm.load_kv(K, V, prefix)
+    # f16 storage rounds every K/V value: the bar of the GPU tests for it
+    tol = 2e-2 if f16 else 1e-5
+    for pos in range(prefix, prefix + n):
+        hidden, rec = pm.step(ids[pos], pos, **kw)
+        assert rec.err == 0, (rec.err, rec.where)
+        om.forward(int(ids[pos]), logits=False)
+        assert rel_l2(hidden, om.buffer("hidden")) < tol
+        assert rel_l2(pm.attn.read(np.float32), om.buffer("attn")) < max(tol, 2e-3 if f16 else 0)
+        K, V = om.kv_arrays()
+        K = K.reshape(cfg.n_layers, ctx, cfg.n_heads_kv, cfg.head_dim)[:, pos]
+        V = V.reshape(cfg.n_layers, ctx, cfg.n_heads_kv, cfg.head_dim)[:, pos]
+        kv = pm.read_kv()[:, :, pos]
+        assert rel_l2(kv[:, :, 0], K) < tol
+        assert rel_l2(kv[:, :, 1], V) < tol
+    if "max_splits" not in kw and prefix >= 200:
+        assert rec.splits > 1  # the split merge is exercised
+    pm.close()
+    om.close()
+
+
+def _run_steps(S, cfg, T, ctx, grid, ids, prefix_kv, **kw):
+    pm = S.PersistentModel(cfg, T, ctx, grid)
+    pm.load_kv(*prefix_kv)
+    out = [pm.step(ids[p], p, **kw)[0] for p in range(prefix_kv[2], len(ids))]
+    kv = pm.read_kv()
+    pm.close()
+    return np.array(out), kv
+
+
+def test_persistent_step_is_bit_identical_across_schedules(S, oracle_mod):
+    """Random thread orders and bulk-copy delays, the fused act-quant, spread
+    barrier counters and a short ring change no bit of the result."""
+    import synthetic
+    cfg, T = _model("tiny-g3", 160)
+    ctx = 160
+    ids = synthetic.prompt_ids(cfg, 152, seed=9)
+    om = _oracle_after(oracle_mod, cfg, T, ids[:150], ctx)
+    K, V = om.kv_arrays()
+    prefix_kv = (K.copy(), V.copy(), 150)
+    om.close()
+    try:
+        S.lib().emu_schedule(0, 0, 0)
+        base_h, base_kv = _run_steps(S, cfg, T, ctx, 5, ids, prefix_kv)
+        variants = [(1, {"fuse_quant": 1}), (2, {"nsub": 3, "max_stages": 3}),
+                    (3, {"fuse_quant": 1, "nsub": 2, "max_stages": 2})]
+        for seed, kw in variants:
+            S.lib().emu_schedule(1, seed, 64)
+            h, kv = _run_steps(S, cfg, T, ctx, 5, ids, prefix_kv, **kw)
+            assert np.array_equal(h, base_h), (seed, kw)
+            assert np.array_equal(kv, base_kv), (seed, kw)
+    finally:
+        S.lib().emu_schedule(0, 0, 0)
+
+
+def test_persistent_step_abort_when_a_cta_never_arrives(S):
+    """One CTA of the plan's grid is not launched: the others' bounded grid
+    barrier waits give up, the step reports a timeout, and every CTA exits
+    with no bulk copy in flight (the emulator fails the launch otherwise)."""
+    import synthetic
+    cfg, T = _model("tiny-gqa", 40)
+    pm = S.PersistentModel(cfg, T, 40, 4)
+    ids = synthetic.prompt_ids(cfg, 2, seed=1)
+    _, rec = pm.step(ids[0], 0, launch_grid=3, wait_ns=200000)
+    assert rec.err == 1  # ERR_TIMEOUT
+    # the next step, with every CTA present, is unaffected by the aborted one
+    # (the barrier words start from zero each step, as k_embed leaves them)
+    _, rec = pm.step(ids[0], 0)
+    assert rec.err == 0
+    pm.close()
+
+
+@pytest.mark.parametrize("G,hd,hkv,n,splits,f16", [(4, 64, 2, 37, 5, False), (1, 32, 3, 100, 7, False),
+                                                   (3, 128, 1, 260, 4, False), (8, 64, 1, 9, 3, True),
+                                                   (2, 128, 2, 1, 6, False)])
+def test_fast_exp_attention_kernels(S, G, hd, hkv, n, splits, f16):
+    from test_topk_fast_attention import fast_exp_kernel, reference_head
+    rng = np.random.default_rng(G * 1000 + n)
+    ctx = n + 4
+    q = rng.standard_normal((hkv * G, hd)).astype(np.float32)
+    kv = rng.standard_normal((hkv, ctx, 2, hd)).astype(np.float32)
+    if f16:
+        kv = kv.astype(np.float16).astype(np.float32)
+    dq = S.Dev(q)
+    dkv = S.Dev(kv.astype(np.float16) if f16 else kv)
+    io = S.Dev(np.array([0, n - 1, 0, 0], np.int32))
+    bufs = [S.Dev(hkv * G * ctx * 4), S.Dev(hkv * splits * G * 4), S.Dev(hkv * splits * G * 4),
+            S.Dev(hkv * splits * G * hd * 4), S.Dev(hkv * G * hd * 4), S.Dev(hkv * G * hd // 32 * 4),
+            S.Dev(hkv * G * hd)]
+    S.check(S.lib().emu_attf(dq.ptr, dkv.ptr, ctx, hd, G, hkv, splits, 1 if f16 else 0, io.ptr,
+                             *[b.ptr for b in bufs]))
+    got = bufs[4].read(np.float32).reshape(hkv * G, hd)
+    scale = np.float32(1.0 / np.sqrt(hd))
+    for h in range(hkv * G):
+        g = h // G
+        want = reference_head(q[h], kv[g, :n, 0], kv[g, :n, 1], scale, fast_exp_kernel)
+        assert rel_l2(got[h], want) < 2e-6, h
+    # the act-quant for Wo is QuantizeQ8_0Into of the output, bit for bit
+    import oracle
+    d0, q0 = oracle.quantize_q8_0(bufs[4].read(np.float32))
+    assert np.array_equal(bufs[5].read(np.float32), d0)
+    assert np.array_equal(bufs[6].read(np.int8), q0)
+    for b in [dq, dkv, io] + bufs:
+        b.free()
+
+
+@pytest.mark.parametrize("world,grid,prefix", [(2, 4, 0), (4, 5, 150)])
+def test_persistent_step_tensor_parallel(S, oracle_mod, world, grid, prefix):
+    """`world` ranks of the persistent step in one emulated launch: each holds
+    its shard as the library's shard plan cuts it, pushes its Wo / down rows
+    into every rank's receive buffer with the step's epochs and sums the
+    ranks' rows in rank order.  Every rank ends with the same hidden state,
+    within 1e-5 of the oracle; a random schedule gives the same bits."""
+    import synthetic
+    ctx = prefix + 2 + 3
+    # 8 query heads over 4 kv heads, so that 4 ranks hold one kv head each
+    cfg = synthetic.Config("tp-4kv", 256, 2, 8, 4, 512, 300, tied=True, ctx_len=max(64, ctx))
+    T = synthetic.make_model(cfg, seed=0)
+    ids = synthetic.prompt_ids(cfg, prefix + 2, seed=4)
+    om = _oracle_after(oracle_mod, cfg, T, ids[:prefix], ctx)
+    K, V = om.kv_arrays()
+    K, V = K.copy(), V.copy()
+
+    def run():
+        ms = [S.PersistentModel(cfg, T, ctx, grid, world=world, rank=r) for r in range(world)]
+        for m in ms:
+            m.load_kv(K, V, prefix)
+        out = []
+        for i, pos in enumerate(range(prefix, prefix + 2)):
+            hs, recs = S.step_tp(ms, ids[pos], pos, step_count=i + 1)
+            assert all(r.err == 0 for r in recs), [(r.err, r.where) for r in recs]
+            assert all(np.array_equal(hs[0], h) for h in hs)
+            out.append(hs[0])
+        for m in ms:
+            m.close()
+        return np.array(out)
+
+    try:
+        S.lib().emu_schedule(0, 0, 0)
+        got = run()
+        for i, pos in enumerate(range(prefix, prefix + 2)):
+            om.forward(int(ids[pos]), logits=False)
+            assert rel_l2(got[i], om.buffer("hidden")) < 1e-5, i
+        S.lib().emu_schedule(1, 11, 64)
+        assert np.array_equal(run(), got)
+    finally:
+        S.lib().emu_schedule(0, 0, 0)
+        om.close()
