@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
   constexpr int DPL = HD / 32;
   constexpr int SB = bd_stage_bytes(HD, (int)sizeof(KT));
   static_assert(sizeof(BdSmem) <= 1024, "smem head");
-  extern __shared__ __align__(1024) uint8_t bd_smem[];
+  L3G_DYNAMIC_SMEM(bd_smem);
   BdSmem* sh = reinterpret_cast<BdSmem*>(bd_smem);
   uint8_t* ring = bd_smem + 1024;
   float(*sm_o)[GP][HD] = reinterpret_cast<float(*)[GP][HD]>(ring);  // after the ring drains
@@ -315,7 +315,8 @@ __global__ void k_bd_topk_partial(const float* L, int n, int v_l, int vocab, int
 // Phase 2: grid n; cap (a power of two >= count) keys of dynamic shared memory.
 __global__ void k_bd_topk_final(const uint64_t* part, int count, int cap, int k, int* ids,
                                 float* logits) {
-  extern __shared__ uint64_t keys3[];
+  L3G_DYNAMIC_SMEM(keys3_raw);
+  uint64_t* keys3 = reinterpret_cast<uint64_t*>(keys3_raw);
   const int b = blockIdx.x;
   for (int i = threadIdx.x; i < cap; i += blockDim.x)
     keys3[i] = i < count ? part[(size_t)b * count + i] : 0ull;

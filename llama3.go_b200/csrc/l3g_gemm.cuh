@@ -1,85 +1,8 @@
 // Batched Q8_0 product on the tcgen05 tensor cores (included by
-// l3g_kernels.cuh, inside namespace l3g, after l3g_gemm_layout.h).
+// l3g_kernels.cuh, inside namespace l3g, after l3g_gemm_layout.h and the
+// tensor-core helpers of l3g_tcgen05.cuh).
 #pragma once
 
-// ---------------------------------------------------------------------------
-// tcgen05 helpers (tensor memory, MMA issue and completion)
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// whole warp: allocate ncols columns (power of two >= 32) of tensor memory,
-// base address written to *dst (shared memory)
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   smem_u32(dst)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-// one thread: D[tmem] = A * B (accumulate = 0) or D += A * B
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// one thread: arrive once on *bar when every tcgen05 operation this thread
-// issued before has completed
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-// whole warp: 8 consecutive 32-bit columns of this warp's 32 lanes
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* v) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-                 "=r"(v[6]), "=r"(v[7])
-               : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Packed pairs of fp32 (sm_100 f32x2 arithmetic: two IEEE round-to-nearest
-// operations per instruction, the same results as two scalar ones).
-__device__ __forceinline__ unsigned long long pk2(float a, float b) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ float2 upk2(unsigned long long r) {
-  float a, b;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-  return make_float2(a, b);
-}
-__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
-  unsigned long long r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b,
-                                                   unsigned long long c) {
-  unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
 // An int32 block sum (|v| < 2^22: at most 32 * 128 * 128) as fp32, exactly,
 // without the conversion unit: the bits of 1.5 * 2^23 + v, minus 1.5 * 2^23
 // (the second step is the caller's packed add of -1.5 * 2^23).
@@ -143,7 +66,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   constexpr int SB = stage_bytes(NT);
   static_assert(NB * NT <= (int)TCOLS && TCOLS <= 512, "tensor memory budget");
   static_assert(CPT % 8 == 0, "tcgen05.ld granularity");
-  extern __shared__ __align__(1024) uint8_t smem[];
+  L3G_DYNAMIC_SMEM(smem);
   GemmSmem* sh = reinterpret_cast<GemmSmem*>(smem);
   uint8_t* ring = smem + SMEM_HEAD;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

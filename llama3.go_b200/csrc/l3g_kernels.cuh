@@ -23,7 +23,15 @@ namespace l3g {
 
 #include "l3g_base.cuh"
 
+// The inline-PTX layer (the kernels above it are plain CUDA C++); a host
+// build of the kernels for the CPU checks names its own in L3G_PTX_HEADER.
+#ifndef L3G_PTX_HEADER
 #include "l3g_ptx.cuh"
+
+#include "l3g_tcgen05.cuh"
+#else
+#include L3G_PTX_HEADER
+#endif
 
 #include "l3g_helpers.cuh"
 
@@ -254,7 +262,8 @@ __global__ void k_topk_partial(const float* logits, int n, int k, int id_offset,
 // Phase 2: one CTA merges all partial keys (count <= cap, cap a power of 2).
 __global__ void k_topk_final(const uint64_t* part, int count, int cap, int k,
                              int* out_ids, float* out_logits) {
-  extern __shared__ uint64_t keys2[];
+  L3G_DYNAMIC_SMEM(keys2_raw);
+  uint64_t* keys2 = reinterpret_cast<uint64_t*>(keys2_raw);
   pdl_wait();
   for (int i = threadIdx.x; i < cap; i += blockDim.x)
     keys2[i] = i < count ? part[i] : 0ull;

@@ -197,7 +197,8 @@ __global__ void __launch_bounds__(256) k_pf_attention(const float* Q, const void
                                                       int bq, int nq_heads, float scale) {
   constexpr int DPL = HD / 32;  // output dims per lane: lane + 32 j
   constexpr int RW = 8;         // rows per warp
-  extern __shared__ __align__(16) float pf_smem[];
+  L3G_DYNAMIC_SMEM(pf_smem_raw);
+  float* pf_smem = reinterpret_cast<float*>(pf_smem_raw);
   float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(pf_smem);
   float(*kt)[33] = reinterpret_cast<float(*)[33]>(pf_smem + 64 * HD);
   float(*vs)[HD] = reinterpret_cast<float(*)[HD]>(pf_smem + 64 * HD + HD * 33);

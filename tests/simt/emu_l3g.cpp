@@ -2,25 +2,11 @@
 // entry point per kernel for the CPU tests (ctypes).  Test infrastructure.
 #include "simt.h"
 
-#include "l3g_persist_plan.h"
+#include "simt_tcgen05.h"
 
-namespace l3g {
-#include "l3g_base.cuh"
-
-#include "simt_ptx.h"
-
-#include "l3g_helpers.cuh"
-
-#include "l3g_matvec.cuh"
-
-#include "l3g_attention.cuh"
-
-#include "l3g_attention_fast.cuh"
-
-#include "l3g_persist.cuh"
-
-#include "l3g_repack.cuh"
-}  // namespace l3g
+// every device kernel of the library, on the emulator's PTX layer
+#define L3G_PTX_HEADER "simt_l3g_ptx.h"
+#include "l3g_kernels.cuh"
 
 // ---------------------------------------------------------------------------
 // C entry points (ctypes).  Pointers named "device" come from emu_malloc.
@@ -341,5 +327,385 @@ int emu_layers_tp(EmuLayers* ranks, int world) {
 }
 
 int emu_layers(EmuLayers* e) { return emu_layers_tp(e, 1); }
+
+// The runtime's gemm_ksplit: with fewer (row tile, token tile) tiles than
+// SMs, split K over a divisor of the chunk count that fits `part_floats`.
+static int emu_ksplit(int rows, int cols, int n_tok, int nsm, size_t part_floats) {
+  using namespace l3g;
+  const int nt = gemm::token_tile(n_tok), nk = gemm::chunks(cols);
+  const long long tiles = (long long)gemm::row_tiles(rows) * ((n_tok + nt - 1) / nt);
+  if (part_floats == 0 || tiles >= nsm) return 1;
+  const long long want = nsm / tiles;
+  int best = 1;
+  for (int d = 2; d <= nk && d <= want; ++d)
+    if (nk % d == 0 && (size_t)d * n_tok * rows <= part_floats) best = d;
+  return best;
+}
+
+// One product as the runtime's launch_gemm issues it (ldo = rows).
+static void run_gemm(const uint8_t* w, int rows, int cols, const uint8_t* act, int n_tok,
+                     float* out, int ksplit, float* part, int grid, int nstages, l3g::Result* res,
+                     int nsm = 148) {
+  using namespace l3g;
+  const int nt = gemm::token_tile(n_tok);
+  GemmArgs g{};
+  g.a = w;
+  g.b = act;
+  g.out = out;
+  g.rows = rows;
+  g.ldo = rows;
+  g.n_tok = n_tok;
+  g.nk = gemm::chunks(cols);
+  g.n_rt = gemm::row_tiles(rows);
+  g.n_tt = (n_tok + nt - 1) / nt;
+  g.ksplit = ksplit > 1 ? ksplit : 1;
+  if (g.nk % g.ksplit) simt::fail("ksplit must divide the chunk count");
+  g.part = part;
+  g.nstages = nstages > 0 ? std::min(nstages, gemm::stages(nt)) : gemm::stages(nt);
+  g.res = res;
+  g.wait_ns = WAIT_TIMEOUT_NS;
+  const long long units = (long long)g.n_rt * g.n_tt * g.ksplit;
+  const int G = grid > 0 ? grid : (int)std::max<long long>(1, std::min<long long>(nsm, units));
+  const size_t smem = gemm::SMEM_HEAD + (size_t)g.nstages * gemm::stage_bytes(nt);
+  auto go = [&](auto nt_c) {
+    constexpr int NT = decltype(nt_c)::value;
+    simt::launch(dim3(G), dim3(GEMM_THREADS), smem, [&] { k_gemm_q8<NT>(g); });
+  };
+  switch (nt) {
+    case 16: go(std::integral_constant<int, 16>{}); break;
+    case 32: go(std::integral_constant<int, 32>{}); break;
+    case 64: go(std::integral_constant<int, 64>{}); break;
+    default: go(std::integral_constant<int, 128>{}); break;
+  }
+  if (g.ksplit > 1) {
+    const long long n = (long long)n_tok * rows;
+    simt::launch(dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                 [&] { k_gemm_reduce(part, g.ksplit, n_tok, rows, rows, out); });
+  }
+}
+
+// k_gemm_quantize of x [n_tok][cols] (device) into activation chunks for a
+// token tile of token_tile(n_tok) (device `act`, l3g_gemm_act_bytes bytes).
+int emu_gemm_quantize(const float* x, int n_tok, int cols, uint8_t* act) {
+  return guarded_call([&] {
+    using namespace l3g;
+    const int nt = gemm::token_tile(n_tok), nk = gemm::chunks(cols);
+    const int n_pad = (n_tok + nt - 1) / nt * nt;
+    const long long warps = (long long)n_pad * nk * gemm::BPC;
+    simt::launch(dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
+                 [&] { k_gemm_quantize(x, n_tok, cols, nt, nk, n_pad, act); });
+  });
+}
+
+// The batched Q8_0 product as the runtime's launch_gemm issues it: weight
+// chunks w (device, rows x cols repacked), activation chunks act, out
+// [n_tok][rows]; ksplit > 1 splits K over CTAs into `part` and reduces.
+// grid 0 takes min(148, units); nstages 0 the layout's ring depth.
+int emu_gemm(const uint8_t* w, int rows, int cols, const uint8_t* act, int n_tok, float* out,
+             int ksplit, float* part, int grid, int nstages, int* err, int* where) {
+  return guarded_call([&] {
+    auto* res = static_cast<l3g::Result*>(simt::dmalloc(sizeof(l3g::Result)));
+    try {
+      run_gemm(w, rows, cols, act, n_tok, out, ksplit, part, grid, nstages, res);
+    } catch (...) {
+      simt::dfree(res);
+      throw;
+    }
+    *err = res->err;
+    *where = res->where;
+    simt::dfree(res);
+  });
+}
+
+// k_gemm_from_tiles: weight chunks (device dst, zeroed) of a matrix held in
+// the decode kernels' tile layout with rpw rows per warp (device src).
+int emu_gemm_from_tiles(const uint8_t* src, int rows, int cols, int rpw, uint8_t* dst) {
+  return guarded_call([&] {
+    const l3g::TileGeom g = l3g::tile_geometry(rows, cols, rpw, l3g::NW, l3g::TILE_TARGET);
+    const l3g::Q8Tiles t{src, rows, cols, g.wr, g.ck, g.nslices, g.tile_bytes, g.n_groups};
+    simt::launch(dim3(8), dim3(256), 0, [&] { l3g::k_gemm_from_tiles(t, dst); });
+  });
+}
+
+// One batched prefill pass of P tokens at positions pos0.. as the runtime's
+// enqueue_prefill_pass issues it on one GPU.
+struct EmuPrefillLayer {
+  const uint8_t* g[4];  // weight chunks of QKV, Wo, up/gate (interleaved), down (device)
+  const float* attn_norm;
+  const float* ffn_norm;
+};
+struct EmuPrefill {
+  int n_layers, n_emb, n_ff, hq, hkv, hd, rope_half, ctx, kv_f16, vocab;
+  float eps;
+  const EmuPrefillLayer* layers;  // host array of n_layers
+  const uint8_t* emb;             // raw GGUF token_embd (device)
+  void* kv;                       // cache [n_layers][hkv][ctx][2][hd] (device)
+  const float* rope_cos;          // [ctx][rope_half] (device)
+  const float* rope_sin;
+  const int* ids;                 // P token ids (device)
+  int P, pos0, nsm;
+  int err, where;
+};
+
+int emu_prefill(EmuPrefill* e) {
+  return guarded_call([&] {
+    using namespace l3g;
+    const int ne = e->n_emb, hd = e->hd, P = e->P;
+    const int nq = e->hq * hd, nkv = e->hkv * hd, ff = e->n_ff, G = e->hq / e->hkv;
+    const int es = e->kv_f16 ? 2 : 4;
+    const int nt = gemm::token_tile(P);
+    const int rows[4] = {nq + 2 * nkv, ne, 2 * ff, ne}, cols[4] = {ne, nq, ne, ff};
+    std::vector<void*> scratch;
+    auto dm = [&](size_t bytes) {
+      void* q = simt::dmalloc(bytes);
+      scratch.push_back(q);
+      return q;
+    };
+    try {
+      const int cap = P;
+      const int max_cols = std::max(std::max(ne, nq), ff);
+      const int ntc = gemm::token_tile(cap);
+      const size_t act_bytes =
+          (size_t)((cap + ntc - 1) / ntc) * gemm::chunks(max_cols) * gemm::b_chunk(ntc);
+      auto* X = static_cast<float*>(dm((size_t)cap * ne * 4));
+      auto* Y = static_cast<float*>(dm((size_t)cap * ne * 4));
+      auto* QKV = static_cast<float*>(dm((size_t)cap * (nq + 2 * nkv) * 4));
+      auto* Q = static_cast<float*>(dm((size_t)cap * nq * 4));
+      auto* ATT = static_cast<float*>(dm((size_t)cap * nq * 4));
+      auto* UG = static_cast<float*>(dm((size_t)cap * 2 * ff * 4));
+      auto* act = static_cast<uint8_t*>(dm(act_bytes));
+      size_t part_floats = 0;  // gemm_part_bound over the matrices
+      for (int m = 0; m < 4; ++m) {
+        const long long d = std::min<long long>(
+            gemm::chunks(cols[m]), std::max(1, e->nsm / std::max(1, gemm::row_tiles(rows[m]))));
+        if (d > 1) part_floats = std::max(part_floats, (size_t)d * cap * rows[m]);
+      }
+      auto* part = static_cast<float*>(dm(std::max<size_t>(1, part_floats) * 4));
+      auto* res = static_cast<Result*>(dm(sizeof(Result)));
+      auto gemm = [&](int l, int m, float* out) {
+        const int ks = emu_ksplit(rows[m], cols[m], P, e->nsm, part_floats);
+        run_gemm(e->layers[l].g[m], rows[m], cols[m], act, P, out, ks, part, 0, 0, res, e->nsm);
+      };
+      simt::launch(dim3((ne + 255) / 256, P), dim3(256), 0,
+                   [&] { k_pf_embed(e->emb, e->vocab, ne, e->ids, X, res); });
+      for (int l = 0; l < e->n_layers; ++l) {
+        const EmuPrefillLayer& L = e->layers[l];
+        uint8_t* kv = static_cast<uint8_t*>(e->kv) + (size_t)l * e->hkv * e->ctx * 2 * hd * es;
+        simt::launch(dim3(P), dim3(PF_THREADS), 0, [&] {
+          k_pf_rms_quant(X, l ? Y : nullptr, L.attn_norm, e->eps, ne, nt, gemm::chunks(ne), act);
+        }, true);
+        gemm(l, 0, QKV);
+        const long long pairs = (long long)P * ((nq + 2 * nkv) / 2);
+        simt::launch(dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, [&] {
+          k_pf_qkv_rope(QKV, P, e->pos0, nq, nkv, hd, e->rope_half, e->rope_cos, e->rope_sin, Q,
+                        kv, e->ctx, e->kv_f16);
+        });
+        if (l == e->n_layers - 1) break;
+        {
+          const int bq = std::max(1, 64 / G);
+          const dim3 grid((P + bq - 1) / bq, e->hkv);
+          const float scale = (float)(1.0 / sqrt((double)hd));
+          auto att = [&](auto hd_c) {
+            constexpr int HD = decltype(hd_c)::value;
+            if (e->kv_f16)
+              simt::launch(grid, dim3(256), pf_attention_smem(HD), [&] {
+                k_pf_attention<HD, __half>(Q, kv, ATT, P, e->pos0, e->ctx, G, bq, e->hq, scale);
+              });
+            else
+              simt::launch(grid, dim3(256), pf_attention_smem(HD), [&] {
+                k_pf_attention<HD, float>(Q, kv, ATT, P, e->pos0, e->ctx, G, bq, e->hq, scale);
+              });
+          };
+          switch (hd) {
+            case 32: att(std::integral_constant<int, 32>{}); break;
+            case 64: att(std::integral_constant<int, 64>{}); break;
+            case 128: att(std::integral_constant<int, 128>{}); break;
+            default: simt::fail("head dim");
+          }
+        }
+        {
+          const int n_pad = (P + nt - 1) / nt * nt;
+          const long long warps = (long long)n_pad * gemm::chunks(nq) * gemm::BPC;
+          simt::launch(dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, [&] {
+            k_gemm_quantize(ATT, P, nq, nt, gemm::chunks(nq), n_pad, act);
+          });
+        }
+        gemm(l, 1, Y);
+        simt::launch(dim3(P), dim3(PF_THREADS), 0, [&] {
+          k_pf_rms_quant(X, Y, L.ffn_norm, e->eps, ne, nt, gemm::chunks(ne), act);
+        }, true);
+        gemm(l, 2, UG);
+        {
+          const long long warps = (long long)P * (ff / 32);
+          simt::launch(dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
+                       [&] { k_pf_swiglu_quant(UG, P, ff, nt, gemm::chunks(ff), act); });
+        }
+        gemm(l, 3, Y);
+      }
+      e->err = res->err;
+      e->where = res->where;
+    } catch (...) {
+      for (void* q : scratch) simt::dfree(q);
+      throw;
+    }
+    for (void* q : scratch) simt::dfree(q);
+  });
+}
+
+// One batched decode step of n sessions as the runtime's l3g_batch_step
+// issues it on one GPU (embedding, per layer RMSNorm + act-quant, QKV
+// product, RoPE + KV append per session, split-K attention over each
+// session's cache and its merge, Wo, FFN; final norm, logits product,
+// top-K and SampleTopK per session).
+struct EmuBatch {
+  int n_layers, n_emb, n_ff, hq, hkv, hd, rope_half, kv_f16, vocab;
+  float eps;
+  const EmuPrefillLayer* layers;  // host array of n_layers (weight chunks)
+  const uint8_t* glogits;         // logits matrix as weight chunks (device)
+  const float* out_norm;          // (device)
+  const uint8_t* emb;             // raw GGUF token_embd (device)
+  l3g::SeqInfo* seqs;             // [n] (device)
+  int n, max_splits, top_k, nsm;
+  float* logits;                  // out: [n][vocab] (device)
+  l3g::Result* out;               // out: [n] sampled token and its logit (device)
+  int err, where;
+};
+
+int emu_batch_step(EmuBatch* e) {
+  return guarded_call([&] {
+    using namespace l3g;
+    const int ne = e->n_emb, hd = e->hd, n = e->n;
+    const int nq = e->hq * hd, nkv = e->hkv * hd, ff = e->n_ff, G = e->hq / e->hkv;
+    const int nt = gemm::token_tile(n), n_pad = (n + nt - 1) / nt * nt;
+    const int rows[5] = {nq + 2 * nkv, ne, 2 * ff, ne, e->vocab};
+    const int cols[5] = {ne, nq, ne, ff, ne};
+    std::vector<void*> scratch;
+    auto dm = [&](size_t bytes) {
+      void* q = simt::dmalloc(bytes);
+      scratch.push_back(q);
+      return q;
+    };
+    try {
+      int max_pos = 0;
+      for (int i = 0; i < n; ++i) max_pos = std::max(max_pos, e->seqs[i].pos);
+      const int splits = (max_pos + 1 + BD_SPLIT - 1) / BD_SPLIT;
+      if (splits > e->max_splits) simt::fail("max_splits too small");
+      const int max_cols = std::max(std::max(ne, nq), ff);
+      const size_t act_bytes = (size_t)(n_pad / nt) * gemm::chunks(max_cols) * gemm::b_chunk(nt);
+      auto* X = static_cast<float*>(dm((size_t)n * ne * 4));
+      auto* Y = static_cast<float*>(dm((size_t)n * ne * 4));
+      auto* QKV = static_cast<float*>(dm((size_t)n * (nq + 2 * nkv) * 4));
+      auto* Q = static_cast<float*>(dm((size_t)n * nq * 4));
+      auto* ATT = static_cast<float*>(dm((size_t)n * nq * 4));
+      auto* UG = static_cast<float*>(dm((size_t)n * 2 * ff * 4));
+      auto* part_o = static_cast<float*>(dm((size_t)n * e->hq * e->max_splits * hd * 4));
+      auto* part_ml = static_cast<float*>(dm((size_t)n * e->hq * e->max_splits * 2 * 4));
+      auto* act = static_cast<uint8_t*>(dm(act_bytes));
+      size_t part_floats = 0;
+      for (int m = 0; m < 5; ++m) {
+        const long long d = std::min<long long>(
+            gemm::chunks(cols[m]), std::max(1, e->nsm / std::max(1, gemm::row_tiles(rows[m]))));
+        if (d > 1) part_floats = std::max(part_floats, (size_t)d * n * rows[m]);
+      }
+      auto* part = static_cast<float*>(dm(std::max<size_t>(1, part_floats) * 4));
+      const int tk_chunks = (e->vocab + TOPK_CHUNK - 1) / TOPK_CHUNK;
+      auto* tk_part = static_cast<uint64_t*>(dm((size_t)n * tk_chunks * MAX_TOPK * 8));
+      auto* tk_ids = static_cast<int*>(dm((size_t)n * MAX_TOPK * 4));
+      auto* tk_logits = static_cast<float*>(dm((size_t)n * MAX_TOPK * 4));
+      auto* res = static_cast<Result*>(dm(sizeof(Result)));
+      auto gemm = [&](const uint8_t* w, int m, float* out) {
+        const int ks = emu_ksplit(rows[m], cols[m], n, e->nsm, part_floats);
+        run_gemm(w, rows[m], cols[m], act, n, out, ks, part, 0, 0, res, e->nsm);
+      };
+      const float scale = (float)(1.0 / sqrt((double)hd));
+      simt::launch(dim3((ne + 255) / 256, n), dim3(256), 0,
+                   [&] { k_bd_embed(e->emb, e->vocab, ne, e->seqs, X, res); });
+      for (int l = 0; l < e->n_layers; ++l) {
+        const EmuPrefillLayer& L = e->layers[l];
+        simt::launch(dim3(n), dim3(PF_THREADS), 0, [&] {
+          k_pf_rms_quant(X, l ? Y : nullptr, L.attn_norm, e->eps, ne, nt, gemm::chunks(ne), act);
+        }, true);
+        gemm(L.g[0], 0, QKV);
+        const long long pairs = (long long)n * ((nq + 2 * nkv) / 2);
+        simt::launch(dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, [&] {
+          k_bd_qkv_rope(QKV, n, e->seqs, l, nq, nkv, hd, e->rope_half, Q, e->kv_f16);
+        });
+        {
+          const dim3 grid(splits, e->hkv, n);
+          const int gp = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+          auto att = [&](auto hd_c, auto gp_c, auto kt) {
+            constexpr int HD = decltype(hd_c)::value, GPc = decltype(gp_c)::value;
+            using KT = decltype(kt);
+            simt::launch(grid, dim3(BD_THREADS), bd_smem_bytes(HD, (int)sizeof(KT), GPc), [&] {
+              k_bd_attention<HD, GPc, KT>(Q, e->seqs, l, G, e->hq, scale, part_o, part_ml,
+                                          e->max_splits, res, WAIT_TIMEOUT_NS);
+            });
+          };
+          auto by_gp = [&](auto hd_c, auto kt) {
+            switch (gp) {
+              case 1: att(hd_c, std::integral_constant<int, 1>{}, kt); break;
+              case 2: att(hd_c, std::integral_constant<int, 2>{}, kt); break;
+              case 4: att(hd_c, std::integral_constant<int, 4>{}, kt); break;
+              default: att(hd_c, std::integral_constant<int, 8>{}, kt); break;
+            }
+          };
+          auto by_kt = [&](auto hd_c) {
+            if (e->kv_f16) by_gp(hd_c, __half{});
+            else by_gp(hd_c, float{});
+          };
+          switch (hd) {
+            case 32: by_kt(std::integral_constant<int, 32>{}); break;
+            case 64: by_kt(std::integral_constant<int, 64>{}); break;
+            case 128: by_kt(std::integral_constant<int, 128>{}); break;
+            default: simt::fail("head dim");
+          }
+          simt::launch(dim3(e->hq, n), dim3(128), 0, [&] {
+            k_bd_merge(part_o, part_ml, e->seqs, e->hq, hd, e->max_splits, ATT);
+          });
+        }
+        {
+          const long long warps = (long long)n_pad * gemm::chunks(nq) * gemm::BPC;
+          simt::launch(dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, [&] {
+            k_gemm_quantize(ATT, n, nq, nt, gemm::chunks(nq), n_pad, act);
+          });
+        }
+        gemm(L.g[1], 1, Y);
+        simt::launch(dim3(n), dim3(PF_THREADS), 0, [&] {
+          k_pf_rms_quant(X, Y, L.ffn_norm, e->eps, ne, nt, gemm::chunks(ne), act);
+        }, true);
+        gemm(L.g[2], 2, UG);
+        {
+          const long long warps = (long long)n * (ff / 32);
+          simt::launch(dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
+                       [&] { k_pf_swiglu_quant(UG, n, ff, nt, gemm::chunks(ff), act); });
+        }
+        gemm(L.g[3], 3, Y);
+      }
+      simt::launch(dim3(n), dim3(PF_THREADS), 0, [&] {
+        k_pf_rms_quant(X, Y, e->out_norm, e->eps, ne, nt, gemm::chunks(ne), act);
+      }, true);
+      gemm(e->glogits, 4, e->logits);
+      simt::launch(dim3(tk_chunks, n), dim3(256), 0, [&] {
+        k_bd_topk_partial(e->logits, n, e->vocab, e->vocab, e->top_k, tk_part);
+      }, true);
+      {
+        const int count = tk_chunks * e->top_k;
+        int cap2 = 1;
+        while (cap2 < count) cap2 <<= 1;
+        simt::launch(dim3(n), dim3(256), (size_t)cap2 * 8, [&] {
+          k_bd_topk_final(tk_part, count, cap2, e->top_k, tk_ids, tk_logits);
+        });
+      }
+      simt::launch(dim3(n), dim3(32), 0,
+                   [&] { k_bd_sample(tk_ids, tk_logits, e->top_k, e->seqs, e->out); }, true);
+      e->err = res->err;
+      e->where = res->where;
+    } catch (...) {
+      for (void* q : scratch) simt::dfree(q);
+      throw;
+    }
+    for (void* q : scratch) simt::dfree(q);
+  });
+}
 
 }  // extern "C"

@@ -86,6 +86,24 @@ struct Block {
   std::vector<Thread*> threads;
   std::vector<WarpColl> warps;
   Bar bars[16];
+  // tensor memory: 128 lanes x 512 columns of 32 bits, allocated in
+  // power-of-two column ranges of at least 32
+  std::vector<uint32_t> tmem;
+  uint32_t tmem_used = 0;  // bit i: columns [32i, 32i + 32) allocated
+  bool tmem_relinquished = false;
+};
+
+// An asynchronous tensor-core operation (tcgen05.mma or tcgen05.commit),
+// executed in issue order per issuing thread after a delay.
+struct TensorOp {
+  bool commit;
+  Block* blk;
+  Thread* issuer;
+  uint64_t due;
+  uint32_t d_tmem;
+  uint64_t adesc, bdesc;
+  uint32_t idesc, accumulate;
+  uint64_t* bar;
 };
 
 struct MBar {
@@ -117,6 +135,7 @@ struct Runtime {
   uint64_t clock = 0;      // fake %globaltimer, ns
   uint64_t progress = 0;   // bumped whenever some thread gets past a wait
   std::vector<Copy> copies;
+  std::vector<TensorOp> tensor_ops;
   std::map<uint64_t*, MBar> mbars;
   std::map<uintptr_t, Alloc> allocs;  // base -> allocation
   std::mt19937_64 rng{1};
@@ -133,6 +152,20 @@ inline Runtime& rt() {
 inline Thread* cur() { return rt().cur; }
 
 inline size_t page() { return (size_t)sysconf(_SC_PAGESIZE); }
+
+// block index and grid size seen by the kernel in a sequential launch
+inline bool& seq_override() {
+  static bool v = false;
+  return v;
+}
+inline uint3& seq_bidx() {
+  static uint3 v{};
+  return v;
+}
+inline dim3& seq_grid() {
+  static dim3 v;
+  return v;
+}
 
 // ---------------------------------------------------------------------------
 // memory
@@ -209,6 +242,38 @@ inline void deliver_copies(bool all) {
   }
 }
 
+inline void execute_mma(const TensorOp& op);  // simt_tcgen05.h
+
+inline void deliver_tensor_ops(bool all) {
+  Runtime& r = rt();
+  std::vector<Thread*> blocked;
+  for (size_t i = 0; i < r.tensor_ops.size();) {
+    TensorOp& op = r.tensor_ops[i];
+    const bool waits = std::find(blocked.begin(), blocked.end(), op.issuer) != blocked.end();
+    if (!waits && (all || op.due <= r.clock)) {
+      const TensorOp o = op;
+      r.tensor_ops.erase(r.tensor_ops.begin() + i);
+      if (o.commit) {
+        auto it = r.mbars.find(o.bar);
+        if (it == r.mbars.end()) fail("tcgen05.commit to an uninitialised mbarrier");
+        MBar& m = it->second;
+        if (m.pending == 0) fail("tcgen05.commit arrives on a completed phase");
+        --m.pending;
+        if (m.pending == 0 && m.tx == 0) {
+          ++m.phase;
+          m.pending = m.count;
+        }
+      } else {
+        execute_mma(o);
+      }
+      made_progress();
+    } else {
+      blocked.push_back(op.issuer);
+      ++i;
+    }
+  }
+}
+
 inline void trampoline() {
   Thread* t = cur();
   try {
@@ -225,7 +290,29 @@ inline void trampoline() {
 // dynamic shared memory per block, to completion.  Throws simt::Error on a
 // deadlock or on a failed check inside the emulated code.
 inline void launch(dim3 grid, dim3 block, size_t smem, std::function<void()> body,
-                   size_t stack_bytes = 256 * 1024) {
+                   bool sequential = false, size_t stack_bytes = 256 * 1024);
+
+// With sequential = true the blocks run one after another (each to
+// completion), as kernels with static shared arrays need here.
+inline void launch(dim3 grid, dim3 block, size_t smem, std::function<void()> body,
+                   bool sequential, size_t stack_bytes) {
+  if (sequential && grid.x * grid.y * grid.z > 1) {
+    const std::function<void()> b = body;
+    for (unsigned z = 0; z < grid.z; ++z)
+      for (unsigned y = 0; y < grid.y; ++y)
+        for (unsigned x = 0; x < grid.x; ++x) {
+          // a one-block launch whose block index and grid size read as the
+          // full launch's
+          launch(dim3(1), block, smem, [&, x, y, z] {
+            seq_override() = true;
+            seq_bidx() = uint3{x, y, z};
+            seq_grid() = grid;
+            b();
+          });
+          seq_override() = false;
+        }
+    return;
+  }
   Runtime& r = rt();
   r.grid = grid;
   r.block = block;
@@ -233,6 +320,7 @@ inline void launch(dim3 grid, dim3 block, size_t smem, std::function<void()> bod
   r.error.clear();
   r.mbars.clear();
   r.copies.clear();
+  r.tensor_ops.clear();
   const int nb = (int)(grid.x * grid.y * grid.z);
   const int nt = (int)(block.x * block.y * block.z);
   for (int b = 0; b < nb; ++b) {
@@ -284,14 +372,25 @@ inline void launch(dim3 grid, dim3 block, size_t smem, std::function<void()> bod
       if (t->done) --alive;
       if (!r.error.empty()) break;
     }
-    deliver_copies(false);
+    try {
+      deliver_copies(false);
+      deliver_tensor_ops(false);
+    } catch (const Error& e) {
+      if (r.error.empty()) r.error = e.what();
+    }
     if (!r.error.empty()) break;
     if (r.progress != last_progress) {
       last_progress = r.progress;
       idle_rounds = 0;
     } else if (++idle_rounds > 20000) {
-      if (!r.copies.empty()) {
-        deliver_copies(true);
+      if (!r.copies.empty() || !r.tensor_ops.empty()) {
+        try {
+          deliver_copies(true);
+          deliver_tensor_ops(true);
+        } catch (const Error& e) {
+          if (r.error.empty()) r.error = e.what();
+          break;
+        }
         continue;
       }
       std::string msg = "deadlock: no thread progressed; waits:";
@@ -306,6 +405,11 @@ inline void launch(dim3 grid, dim3 block, size_t smem, std::function<void()> bod
   }
   const std::string err = r.error;
   if (err.empty() && !r.copies.empty()) r.error = "bulk copies still in flight at kernel exit";
+  if (r.error.empty() && !r.tensor_ops.empty())
+    r.error = "tensor-core operations still in flight at kernel exit";
+  for (Block* B : r.blocks)
+    if (r.error.empty() && B->tmem_used)
+      r.error = "tensor memory still allocated at kernel exit";
   const std::string err2 = r.error;
   for (Thread* t : r.threads) {
     munmap(t->stack, t->stack_bytes);
@@ -318,6 +422,7 @@ inline void launch(dim3 grid, dim3 block, size_t smem, std::function<void()> bod
   r.threads.clear();
   r.blocks.clear();
   r.copies.clear();
+  r.tensor_ops.clear();
   if (!err2.empty()) fail(err2);
 }
 
@@ -325,9 +430,9 @@ inline void launch(dim3 grid, dim3 block, size_t smem, std::function<void()> bod
 // built-in variables
 // ---------------------------------------------------------------------------
 inline const uint3& thread_idx() { return cur()->tid; }
-inline const uint3& block_idx() { return cur()->blk->bidx; }
+inline const uint3& block_idx() { return seq_override() ? seq_bidx() : cur()->blk->bidx; }
 inline const dim3& block_dim() { return rt().block; }
-inline const dim3& grid_dim() { return rt().grid; }
+inline const dim3& grid_dim() { return seq_override() ? seq_grid() : rt().grid; }
 inline uint8_t* dyn_smem() { return cur()->blk->smem; }
 
 // ---------------------------------------------------------------------------
@@ -479,6 +584,11 @@ inline uint64_t now() { return rt().clock; }
 #define blockDim (::simt::block_dim())
 #define gridDim (::simt::grid_dim())
 #define L3G_DYNAMIC_SMEM(name) uint8_t* name = ::simt::dyn_smem()
+// Static shared arrays become function statics: one copy for the whole
+// launch, so kernels that declare them run with simt::launch(...,
+// sequential = true), one block after another.
+#undef __shared__
+#define __shared__ static
 
 template <typename T>
 inline T simt_shfl(uint32_t mask, T v, int src, const char* what) {

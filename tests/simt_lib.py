@@ -64,6 +64,12 @@ def lib():
                                _P, _P, _P, _P, _P, _P, _P]
         L.emu_layers.argtypes = [C.POINTER(EmuLayers)]
         L.emu_layers_tp.argtypes = [C.POINTER(EmuLayers), C.c_int]
+        L.emu_gemm_quantize.argtypes = [_P, C.c_int, C.c_int, _P]
+        L.emu_gemm_from_tiles.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P]
+        L.emu_prefill.argtypes = [C.c_void_p]
+        L.emu_batch_step.argtypes = [C.c_void_p]
+        L.emu_gemm.argtypes = [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, _P, C.c_int,
+                               C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
         _lib = L
     return _lib
 
@@ -255,3 +261,170 @@ def step_tp(models, token, pos, step_count, **kw):
     recs = (EmuLayers * len(models))(*[m.record(token, pos, step_count, **kw) for m in models])
     check(lib().emu_layers_tp(recs, len(models)))
     return [m.hidden() for m in models], list(recs)
+
+
+class EmuPrefillLayer(C.Structure):
+    _fields_ = [("g", _P * 4), ("attn_norm", _P), ("ffn_norm", _P)]
+
+
+class EmuPrefill(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "n_emb", "n_ff", "hq", "hkv", "hd", "rope_half",
+                                       "ctx", "kv_f16", "vocab")] + [
+        ("eps", C.c_float), ("layers", C.POINTER(EmuPrefillLayer)), ("emb", _P), ("kv", _P),
+        ("rope_cos", _P), ("rope_sin", _P), ("ids", _P), ("P", C.c_int), ("pos0", C.c_int),
+        ("nsm", C.c_int), ("err", C.c_int), ("where", C.c_int)]
+
+
+def _gemm_chunks_bytes(rows, cols):
+    return ((rows + 127) // 128) * ((cols + 127) // 128) * 17408
+
+
+class PrefillModel:
+    """A synthetic model laid out for batched prefill as the library builds it:
+    decode tiles (k_repack, `rpw` rows per warp) turned into the batched
+    product's weight chunks by k_gemm_from_tiles; a KV cache
+    [layer][kv head][ctx][K | V][hd]; prefill() runs one pass."""
+
+    def __init__(self, cfg, T, ctx, rpw=4, kv_f16=False):
+        import synthetic
+        self.cfg, self.ctx, self.kv_f16 = cfg, ctx, kv_f16
+        e, f, hd, hkv = cfg.n_emb, cfg.n_ff, cfg.head_dim, cfg.n_heads_kv
+        self._keep = []
+        raw = {k: Dev(v[2]) for k, v in T.items() if v[1] == synthetic.GGML_Q8_0}
+        self._keep += raw.values()
+        layers = []
+        for l in range(cfg.n_layers):
+            p = f"blk.{l}."
+            specs = [
+                ([(raw[p + "attn_q.weight"], 0, e), (raw[p + "attn_k.weight"], 0, hkv * hd),
+                  (raw[p + "attn_v.weight"], 0, hkv * hd)], e, e + 2 * hkv * hd, False),
+                ([(raw[p + "attn_output.weight"], 0, e)], e, e, False),
+                ([(raw[p + "ffn_up.weight"], 0, f), (raw[p + "ffn_gate.weight"], 0, f)], e, 2 * f, True),
+                ([(raw[p + "ffn_down.weight"], 0, e)], f, e, False),
+            ]
+            chunks = []
+            for segs, cols, rows, il in specs:
+                tiles = repack(segs, cols, rows, interleave2=il, rpw=rpw)
+                g = Dev(_gemm_chunks_bytes(rows, cols))
+                check(lib().emu_gemm_from_tiles(tiles.ptr, rows, cols, rpw, g.ptr))
+                tiles.free()
+                chunks.append(g)
+            nv = [Dev(T[p + "attn_norm.weight"][2]), Dev(T[p + "ffn_norm.weight"][2])]
+            self._keep += chunks + nv
+            L = EmuPrefillLayer()
+            for i, g in enumerate(chunks):
+                L.g[i] = g.ptr
+            L.attn_norm, L.ffn_norm = nv[0].ptr, nv[1].ptr
+            layers.append(L)
+        self.layers = (EmuPrefillLayer * len(layers))(*layers)
+        self.emb = Dev(T["token_embd.weight"][2])
+        cos, sin = rope_tables(cfg, ctx)
+        self.cos, self.sin = Dev(cos), Dev(sin)
+        self.kv = Dev(cfg.n_layers * hkv * ctx * 2 * hd * (2 if kv_f16 else 4))
+        self._keep += [self.emb, self.cos, self.sin, self.kv]
+
+    def prefill(self, ids, pos0, nsm=148):
+        cfg = self.cfg
+        d_ids = Dev(np.ascontiguousarray(ids, dtype=np.int32))
+        a = EmuPrefill(n_layers=cfg.n_layers, n_emb=cfg.n_emb, n_ff=cfg.n_ff, hq=cfg.n_heads,
+                       hkv=cfg.n_heads_kv, hd=cfg.head_dim, rope_half=cfg.head_dim // 2,
+                       ctx=self.ctx, kv_f16=1 if self.kv_f16 else 0, vocab=cfg.vocab,
+                       eps=cfg.rms_eps, layers=self.layers, emb=self.emb.ptr, kv=self.kv.ptr,
+                       rope_cos=self.cos.ptr, rope_sin=self.sin.ptr, ids=d_ids.ptr, P=len(ids),
+                       pos0=pos0, nsm=nsm)
+        try:
+            check(lib().emu_prefill(C.byref(a)))
+        finally:
+            d_ids.free()
+        return a
+
+    def read_kv(self):
+        cfg = self.cfg
+        a = self.kv.read(np.float16 if self.kv_f16 else np.float32).astype(np.float32)
+        return a.reshape(cfg.n_layers, cfg.n_heads_kv, self.ctx, 2, cfg.head_dim)
+
+    def close(self):
+        for d in self._keep:
+            d.free()
+        self._keep = []
+
+
+class SeqInfo(C.Structure):
+    _fields_ = [("kv", _P), ("rope_cos", _P), ("rope_sin", _P), ("layer_bytes", C.c_longlong),
+                ("ctx", C.c_int), ("pos", C.c_int), ("token", C.c_int), ("pad", C.c_int),
+                ("seed", C.c_uint64), ("temperature", C.c_float), ("pad2", C.c_int)]
+
+
+class Result(C.Structure):
+    _fields_ = [("token", C.c_int32), ("logit", C.c_float), ("err", C.c_int32), ("where", C.c_int32)]
+
+
+class EmuBatch(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "n_emb", "n_ff", "hq", "hkv", "hd", "rope_half",
+                                       "kv_f16", "vocab")] + [
+        ("eps", C.c_float), ("layers", C.POINTER(EmuPrefillLayer)), ("glogits", _P),
+        ("out_norm", _P), ("emb", _P), ("seqs", _P), ("n", C.c_int), ("max_splits", C.c_int),
+        ("top_k", C.c_int), ("nsm", C.c_int), ("logits", _P), ("out", _P), ("err", C.c_int),
+        ("where", C.c_int)]
+
+
+class BatchModel(PrefillModel):
+    """PrefillModel plus the logits matrix as weight chunks (output.weight, or
+    the tied token_embd) and the final norm; step() runs one batched decode
+    step over sessions given as (KV cache Dev, position, token, seed)."""
+
+    def __init__(self, cfg, T, ctx, rpw=4, kv_f16=False):
+        super().__init__(cfg, T, ctx, rpw=rpw, kv_f16=kv_f16)
+        name = "token_embd.weight" if cfg.tied else "output.weight"
+        raw = Dev(T[name][2])
+        tiles = repack([(raw, 0, cfg.vocab)], cfg.n_emb, cfg.vocab, rpw=rpw)
+        self.glogits = Dev(_gemm_chunks_bytes(cfg.vocab, cfg.n_emb))
+        check(lib().emu_gemm_from_tiles(tiles.ptr, cfg.vocab, cfg.n_emb, rpw, self.glogits.ptr))
+        tiles.free()
+        raw.free()
+        self.out_norm = Dev(T["output_norm.weight"][2])
+        self._keep += [self.glogits, self.out_norm]
+
+    def new_cache(self):
+        cfg = self.cfg
+        d = Dev(cfg.n_layers * cfg.n_heads_kv * self.ctx * 2 * cfg.head_dim * (2 if self.kv_f16 else 4))
+        self._keep.append(d)
+        return d
+
+    def step(self, caches, positions, tokens, seeds, top_k=40, temperature=0.8, nsm=148):
+        cfg = self.cfg
+        n = len(caches)
+        es = 2 if self.kv_f16 else 4
+        seqs = (SeqInfo * n)(*[SeqInfo(kv=c.ptr, rope_cos=self.cos.ptr, rope_sin=self.sin.ptr,
+                                       layer_bytes=cfg.n_heads_kv * self.ctx * 2 * cfg.head_dim * es,
+                                       ctx=self.ctx, pos=int(p), token=int(t), seed=int(s),
+                                       temperature=temperature)
+                               for c, p, t, s in zip(caches, positions, tokens, seeds)])
+        d_seqs = Dev(np.frombuffer(bytes(seqs), np.uint8))
+        logits = Dev(n * cfg.vocab * 4)
+        out = Dev(n * C.sizeof(Result))
+        a = EmuBatch(n_layers=cfg.n_layers, n_emb=cfg.n_emb, n_ff=cfg.n_ff, hq=cfg.n_heads,
+                     hkv=cfg.n_heads_kv, hd=cfg.head_dim, rope_half=cfg.head_dim // 2,
+                     kv_f16=1 if self.kv_f16 else 0, vocab=cfg.vocab, eps=cfg.rms_eps,
+                     layers=self.layers, glogits=self.glogits.ptr, out_norm=self.out_norm.ptr,
+                     emb=self.emb.ptr, seqs=d_seqs.ptr, n=n, max_splits=(self.ctx + 255) // 256,
+                     top_k=top_k, nsm=nsm, logits=logits.ptr, out=out.ptr)
+        try:
+            check(lib().emu_batch_step(C.byref(a)))
+            lg = logits.read(np.float32).reshape(n, cfg.vocab)
+            res = (Result * n).from_buffer_copy(out.read(np.uint8).tobytes())
+            return lg, [r.token for r in res], a
+        finally:
+            for d in (d_seqs, logits, out):
+                d.free()
+
+
+def load_session_kv(dev, cfg, ctx, K, V, npos, f16=False):
+    """Positions [0, npos) of a session's cache from the oracle's K, V."""
+    hkv, hd = cfg.n_heads_kv, cfg.head_dim
+    K = K.reshape(cfg.n_layers, ctx, hkv, hd)
+    V = V.reshape(cfg.n_layers, ctx, hkv, hd)
+    ours = np.zeros((cfg.n_layers, hkv, ctx, 2, hd), np.float32)
+    ours[:, :, :npos, 0] = K[:, :npos].transpose(0, 2, 1, 3)
+    ours[:, :, :npos, 1] = V[:, :npos].transpose(0, 2, 1, 3)
+    dev.write(ours.astype(np.float16) if f16 else ours)

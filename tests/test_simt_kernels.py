@@ -14,11 +14,23 @@ Covered here, against the oracle and the reference's loops:
   the fused SwiGLU act-quant, with spread barrier counters and a two-slot
   ring; and the abort path when a CTA never arrives;
 - the top-K path's fastExp attention (k_attf_scores / values / merge)
-  against the reference's loop (infer.go:376-423).
+  against the reference's loop (infer.go:376-423);
+- the batched Q8_0 product on the tensor cores (k_gemm_quantize, k_gemm_q8,
+  k_gemm_reduce) on a software model of tcgen05 (tests/simt/simt_tcgen05.h:
+  tensor memory, asynchronous kind::i8 MMAs reading canonical K-major
+  shared-memory operands through their descriptors, commits to mbarriers,
+  32x32b loads): every token's row against the reference's own matvec_q8_c
+  (simd.c), for ragged rows and columns, one to two token tiles of 16 to
+  128, K split over 2 to 4 CTAs, short rings and random schedules;
+- batched prefill (every kernel of a pass, launched in the runtime's order)
+  against the oracle's token-by-token ingest, and batched decode of
+  sessions at different positions against the oracle's forward per session
+  and the host restatement of SampleTopK.
 
 What the emulator does not check: the hardware memory model (one OS thread
 runs every coroutine, so memory is sequentially consistent), timing, and
-anything of the tensor cores.
+whether the hardware reads the tensor-core descriptors as the model does
+(the encodings themselves are checked against CUTLASS in test_gemm_layout).
 """
 import dataclasses
 
@@ -222,3 +234,150 @@ def test_persistent_step_tensor_parallel(S, oracle_mod, world, grid, prefix):
     finally:
         S.lib().emu_schedule(0, 0, 0)
         om.close()
+
+
+GEMM_CASES = [  # rows, cols, tokens, K split, grid (0: one CTA per unit), ring stages (0: full)
+    (200, 96, 1, 1, 0, 0), (384, 160, 17, 1, 0, 0), (130, 512, 40, 2, 0, 0),
+    (256, 1024, 64, 4, 3, 0), (129, 256, 65, 1, 0, 0), (256, 384, 100, 3, 0, 0),
+    (128, 128, 128, 1, 0, 0), (300, 256, 130, 2, 2, 2),
+]
+
+
+def _gemm(S, w, x, rows, cols, ksplit, grid, nstages):
+    import ctypes as C
+    import l3g
+    n_tok = x.shape[0]
+    A = S.Dev(l3g.gemm_repack(w, rows, cols))
+    X = S.Dev(x)
+    act = S.Dev(l3g.gemm_act_bytes(n_tok, cols))
+    out = S.Dev(n_tok * rows * 4)
+    part = S.Dev(max(1, ksplit) * n_tok * rows * 4)
+    S.check(S.lib().emu_gemm_quantize(X.ptr, n_tok, cols, act.ptr))
+    err, where = C.c_int(), C.c_int()
+    S.check(S.lib().emu_gemm(A.ptr, rows, cols, act.ptr, n_tok, out.ptr, ksplit, part.ptr, grid,
+                             nstages, C.byref(err), C.byref(where)))
+    got = out.read(np.float32).reshape(n_tok, rows)
+    for d in (A, X, act, out, part):
+        d.free()
+    return got, err.value
+
+
+@pytest.mark.parametrize("rows,cols,n_tok,ksplit,grid,nstages", GEMM_CASES)
+def test_tensor_core_product_matches_reference_simd(S, oracle_mod, rows, cols, n_tok, ksplit, grid,
+                                                    nstages):
+    import synthetic
+    import torch
+    if not oracle_mod.have_ref_simd():
+        pytest.fail("oracle/_ref/libref_simd.so (the reference's simd.c) is missing")
+    g = torch.Generator().manual_seed(rows * 7 + cols)
+    w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g) * 0.02, torch).numpy()
+    x = np.random.default_rng(n_tok).standard_normal((n_tok, cols)).astype(np.float32)
+    got, err = _gemm(S, w, x, rows, cols, ksplit, grid, nstages)
+    assert err == 0
+    for n in range(n_tok):
+        d0, q0 = oracle_mod.quantize_q8_0(x[n])
+        ref = oracle_mod.ref_matvec_q8(w, d0, q0, rows, cols)
+        assert rel_l2(got[n], ref) < 1e-6, n
+
+
+def test_tensor_core_product_is_bit_identical_across_schedules(S):
+    import synthetic
+    import torch
+    rows, cols = 256, 512
+    g = torch.Generator().manual_seed(3)
+    w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g) * 0.02, torch).numpy()
+    x = np.random.default_rng(4).standard_normal((33, cols)).astype(np.float32)
+    try:
+        S.lib().emu_schedule(0, 0, 0)
+        base, _ = _gemm(S, w, x, rows, cols, 2, 0, 2)
+        for seed in (5, 6):
+            S.lib().emu_schedule(1, seed, 64)
+            assert np.array_equal(_gemm(S, w, x, rows, cols, 2, 0, 2)[0], base)
+    finally:
+        S.lib().emu_schedule(0, 0, 0)
+
+
+
+PREFILL_CASES = [  # config, first pass, second pass, rows per warp of the decode tiles, f16 cache
+    ("tiny-gqa", 40, 25, 1, False),
+    ("tiny-g3", 130, 0, 2, False),   # two token tiles of 128
+    ("small", 70, 30, 8, False),
+    ("small-hd128", 33, 20, 4, True),
+]
+
+
+@pytest.mark.parametrize("name,p1,p2,rpw,f16", PREFILL_CASES)
+def test_batched_prefill_matches_token_by_token_ingest(S, oracle_mod, name, p1, p2, rpw, f16):
+    """Batched prefill (one or two passes, launched as the runtime's
+    enqueue_prefill_pass launches them: embedding, RMSNorm + act-quant rows,
+    tensor-core products on weight chunks built by k_gemm_from_tiles from the
+    decode tiles, RoPE + KV append, causal attention over the cache, SwiGLU
+    + act-quant) leaves the KV cache the oracle's token-by-token ingest
+    leaves: layer 0 within 1e-6 (the same quantization and exact block
+    sums; fp32 sums in another order), deeper layers within the band of
+    int8 rounding flips."""
+    import synthetic
+    ctx = p1 + p2 + 4
+    cfg, T = _model(name, ctx)
+    ids = synthetic.prompt_ids(cfg, p1 + p2, seed=5)
+    om = _oracle_after(oracle_mod, cfg, T, ids, ctx)
+    K, V = om.kv_arrays()
+    K = K.reshape(cfg.n_layers, ctx, cfg.n_heads_kv, cfg.head_dim).copy()
+    V = V.reshape(cfg.n_layers, ctx, cfg.n_heads_kv, cfg.head_dim).copy()
+    om.close()  # its K, V views die with it: copied above
+    pm = S.PrefillModel(cfg, T, ctx, rpw=rpw, kv_f16=f16)
+    assert pm.prefill(ids[:p1], 0).err == 0
+    if p2:
+        assert pm.prefill(ids[p1:], p1).err == 0
+    kv = pm.read_kv()
+    pm.close()
+    n = p1 + p2
+    for l in range(cfg.n_layers):
+        tol = (2e-3 if l == 0 else 3e-2) if f16 else (1e-6 if l == 0 else 5e-3)
+        assert rel_l2(kv[l, :, :n, 0].transpose(1, 0, 2), K[l, :n]) < tol, l
+        assert rel_l2(kv[l, :, :n, 1].transpose(1, 0, 2), V[l, :n]) < tol, l
+
+
+BATCH_CASES = [  # config, session prompt lengths, context, f16 cache
+    ("tiny-g3", [1, 5, 40, 90], 128, False),
+    ("small", [3, 17, 100, 300, 507], 512, False),   # 1 and 2 attention splits of 256
+    ("small", [7, 120, 260], 512, True),
+]
+
+
+@pytest.mark.parametrize("name,lens,ctx,f16", BATCH_CASES)
+def test_batched_decode_step_matches_oracle_and_sampler(S, oracle_mod, name, lens, ctx, f16):
+    """Batched decode of sessions at different positions (launched as the
+    runtime's l3g_batch_step launches it): each session's logits equal the
+    oracle's ForwardIntoWorkspace on that session's cache, and each sampled id
+    is SampleTopK restated on the host (tests/sampler_ref.py) over the top-K
+    of those logits with the Philox draw keyed by the session's seed and
+    counted by its position; two steps, the second fed the first's picks."""
+    import synthetic
+    from sampler_ref import sample_topk
+    cfg, T = _model(name, ctx)
+    bm = S.BatchModel(cfg, T, ctx, kv_f16=f16)
+    oms, caches = [], []
+    for i, L in enumerate(lens):
+        om = _oracle_after(oracle_mod, cfg, T, synthetic.prompt_ids(cfg, L, seed=100 + i), ctx)
+        K, V = om.kv_arrays()
+        c = bm.new_cache()
+        S.load_session_kv(c, cfg, ctx, K, V, L, f16)
+        oms.append(om)
+        caches.append(c)
+    rng = np.random.default_rng(7)
+    seeds = [int(x) for x in rng.integers(1, 2**62, len(lens))]
+    tokens = [int(t) for t in rng.integers(0, cfg.vocab, len(lens))]
+    pos = list(lens)
+    tol = 3e-2 if f16 else 1e-3
+    for _ in range(2):
+        lg, nxt, rec = bm.step(caches, pos, tokens, seeds, top_k=40, temperature=1.3)
+        assert rec.err == 0
+        for i in range(len(lens)):
+            assert rel_l2(lg[i], oms[i].forward(tokens[i])) < tol, i
+            order = np.lexsort((np.arange(cfg.vocab), -lg[i].astype(np.float64)))[:40]
+            assert nxt[i] == sample_topk(order, lg[i][order], 1.3, seeds[i], pos[i]), i
+        tokens, pos = nxt, [p + 1 for p in pos]
+    for om in oms:
+        om.close()
+    bm.close()
