@@ -33,6 +33,7 @@ whether the hardware reads the tensor-core descriptors as the model does
 (the encodings themselves are checked against CUTLASS in test_gemm_layout).
 """
 import dataclasses
+import os
 
 import numpy as np
 import pytest
@@ -381,3 +382,44 @@ def test_batched_decode_step_matches_oracle_and_sampler(S, oracle_mod, name, len
     for om in oms:
         om.close()
     bm.close()
+
+
+@pytest.mark.skipif(os.environ.get("L3G_SIMT_SLOW") != "1",
+                    reason="about 3 minutes and 6 GB of host memory (set L3G_SIMT_SLOW=1)")
+@pytest.mark.parametrize("fuse", [0, 1])
+def test_persistent_step_at_the_8b_layer_shapes(S, oracle_mod, fuse):
+    """The persistent step at the Llama-3.1-8B layer shapes (two layers),
+    planned for 148 SMs as on a B200: multi-slice tiles, 8 kv heads of 4
+    query heads, 10 attention splits of 32-position stages over 300 cached
+    positions.  The hidden state and the appended K/V lie within the band by
+    which the reference's own builds (cgo simd.c and pure Go) differ on the
+    same step."""
+    import synthetic
+    cfg, T = synthetic_model("llama3.1-8b-2l")
+    prefix, ctx = 300, 304
+    ids = synthetic.prompt_ids(cfg, prefix + 1, seed=3)
+    cgo = _oracle_after(oracle_mod, cfg, T, ids[:prefix], ctx)
+    K, V = cgo.kv_arrays()
+    K, V = K.copy(), V.copy()
+    pure = oracle_mod.OracleModel(cfg, T)
+    pure.new_state(ctx)
+    Kp, Vp = pure.kv_arrays()
+    Kp[:], Vp[:] = K, V
+    pure.pos = prefix
+    pm = S.PersistentModel(cfg, T, ctx, 148)
+    pm.load_kv(K, V, prefix)
+    hidden, rec = pm.step(ids[prefix], prefix, fuse_quant=fuse)
+    assert rec.err == 0 and rec.splits == 10
+    cgo.forward(int(ids[prefix]), logits=False)
+    pure.forward(int(ids[prefix]), logits=False, use_ref=False)
+    band = rel_l2(pure.buffer("hidden"), cgo.buffer("hidden"))
+    assert rel_l2(hidden, cgo.buffer("hidden")) <= max(1e-5, 1.5 * band)
+    kv = pm.read_kv()
+    Kc = cgo.kv_arrays()[0].reshape(cfg.n_layers, ctx, cfg.n_heads_kv, cfg.head_dim)
+    Kq = pure.kv_arrays()[0].reshape(cfg.n_layers, ctx, cfg.n_heads_kv, cfg.head_dim)
+    for l in range(cfg.n_layers):
+        kband = rel_l2(Kq[l, prefix], Kc[l, prefix])
+        assert rel_l2(kv[l, :, prefix, 0], Kc[l, prefix]) <= max(1e-5, 1.5 * kband), l
+    pm.close()
+    cgo.close()
+    pure.close()
