@@ -423,3 +423,40 @@ def test_persistent_step_at_the_8b_layer_shapes(S, oracle_mod, fuse):
     pm.close()
     cgo.close()
     pure.close()
+
+
+def test_persistent_step_multi_slice_tiles(S, oracle_mod):
+    """The 1B layer shapes (two layers): rows of 2048 and 8192 columns are
+    cut into 2 and 8 column slices of 1024 per tile, so every row group
+    takes several tiles of the ring.  On a step where no int8 rounding flips
+    between the builds (checked: the reference's cgo and pure-Go builds
+    agree to 1e-6 there) the hidden state and the appended K/V match the
+    oracle within 1e-5."""
+    import synthetic
+    cfg, T = synthetic_model("llama3.2-1b-2l")
+    assert S.tile_geometry(cfg.n_emb, cfg.n_ff)["nslices"] == 8
+    prefix, ctx = 33, 37
+    ids = synthetic.prompt_ids(cfg, prefix + 1, seed=prefix)
+    cgo = _oracle_after(oracle_mod, cfg, T, ids[:prefix], ctx)
+    K, V = cgo.kv_arrays()
+    K, V = K.copy(), V.copy()
+    pure = oracle_mod.OracleModel(cfg, T)
+    pure.new_state(ctx)
+    Kp, Vp = pure.kv_arrays()
+    Kp[:], Vp[:] = K, V
+    pure.pos = prefix
+    pm = S.PersistentModel(cfg, T, ctx, 12)
+    pm.load_kv(K, V, prefix)
+    hidden, rec = pm.step(ids[prefix], prefix)
+    assert rec.err == 0
+    cgo.forward(int(ids[prefix]), logits=False)
+    pure.forward(int(ids[prefix]), logits=False, use_ref=False)
+    assert rel_l2(pure.buffer("hidden"), cgo.buffer("hidden")) < 1e-6  # a flip-free step
+    assert rel_l2(hidden, cgo.buffer("hidden")) < 1e-5
+    kv = pm.read_kv()
+    Kc = cgo.kv_arrays()[0].reshape(cfg.n_layers, ctx, cfg.n_heads_kv, cfg.head_dim)
+    for l in range(cfg.n_layers):
+        assert rel_l2(kv[l, :, prefix, 0], Kc[l, prefix]) < 1e-5, l
+    pm.close()
+    cgo.close()
+    pure.close()
