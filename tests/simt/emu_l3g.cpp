@@ -708,4 +708,49 @@ int emu_batch_step(EmuBatch* e) {
   });
 }
 
+// The decode step's Q8_0 matvec as the per-op entry l3g_matvec_q8 launches
+// it (k_matvec, pre-quantized activation, plain store of rows [row_lo,
+// row_hi)) on tiles with rpw rows per warp; ring depth as the runtime's
+// finish_plan picks it; grid min(row groups, nsm).
+int emu_matvec(const uint8_t* tiles, int rows, int cols, int rpw, const float* xd,
+               const int8_t* xq, float* out, int row_lo, int row_hi, int nsm) {
+  return guarded_call([&] {
+    using namespace l3g;
+    const TileGeom g = tile_geometry(rows, cols, rpw, NW, TILE_TARGET);
+    MatvecArgs a{};
+    a.w = Q8Tiles{tiles, rows, cols, g.wr, g.ck, g.nslices, g.tile_bytes, g.n_groups};
+    const int fixed = mv_smem_bytes(cols, 0, g.tile_bytes);
+    a.nstages = std::max(2, std::min(MAX_STAGES, (CTA_SMEM_SHARE - fixed) / g.tile_bytes));
+    const size_t smem = mv_smem_bytes(cols, a.nstages, g.tile_bytes);
+    a.row_lo = row_lo;
+    a.row_hi = row_hi;
+    a.xd_in = xd;
+    a.xqs_in = xq;
+    a.out = out;
+    auto* res = static_cast<Result*>(simt::dmalloc(sizeof(Result)));
+    a.res = res;
+    a.wait_ns = WAIT_TIMEOUT_NS;
+    const int gl = row_lo / g.wr, ng = (row_hi + g.wr - 1) / g.wr - gl;
+    const dim3 grid(std::max(1, std::min(ng, nsm)));
+    try {
+      auto go = [&](auto r_c) {
+        constexpr int R = decltype(r_c)::value;
+        simt::launch(grid, dim3(NTHREADS), smem, [&] { k_matvec<PRO_PREQ, EPI_STORE, R, 1>(a); });
+      };
+      switch (rpw) {
+        case 1: go(std::integral_constant<int, 1>{}); break;
+        case 2: go(std::integral_constant<int, 2>{}); break;
+        case 4: go(std::integral_constant<int, 4>{}); break;
+        case 8: go(std::integral_constant<int, 8>{}); break;
+        default: simt::fail("rows per warp");
+      }
+      if (res->err) simt::fail("k_matvec reported an error");
+    } catch (...) {
+      simt::dfree(res);
+      throw;
+    }
+    simt::dfree(res);
+  });
+}
+
 }  // extern "C"

@@ -460,3 +460,30 @@ def test_persistent_step_multi_slice_tiles(S, oracle_mod):
     pm.close()
     cgo.close()
     pure.close()
+
+
+@pytest.mark.parametrize("rows,cols,rpw,lo,hi", [(4096, 512, 4, 0, 4096), (37, 96, 1, 0, 37),
+                                                 (2050, 1792, 2, 0, 2050), (513, 2048, 8, 100, 400)])
+def test_decode_matvec_matches_reference_simd(S, oracle_mod, rows, cols, rpw, lo, hi):
+    """The decode step's k_matvec (the kernel measured on the B200, and
+    tested there against the same reference) under the emulator: rows
+    [lo, hi) equal the reference's matvec_q8_c (simd.c) within 1e-6, the
+    other rows untouched -- a check of the emulator on a kernel whose GPU
+    results are known."""
+    import synthetic
+    import torch
+    g = torch.Generator().manual_seed(rows * 7 + cols)
+    w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g) * 0.02, torch).numpy()
+    x = np.random.default_rng(rows).standard_normal(cols).astype(np.float32)
+    d0, q0 = oracle_mod.quantize_q8_0(x)
+    ref = oracle_mod.ref_matvec_q8(w, d0, q0, rows, cols)
+    raw = S.Dev(w)
+    tiles = S.repack([(raw, 0, rows)], cols, rows, rpw=rpw)
+    xd, xq = S.Dev(d0), S.Dev(q0)
+    out = S.Dev(np.full(rows, 7.0, np.float32))
+    S.check(S.lib().emu_matvec(tiles.ptr, rows, cols, rpw, xd.ptr, xq.ptr, out.ptr, lo, hi, 148))
+    got = out.read(np.float32)
+    assert rel_l2(got[lo:hi], ref[lo:hi]) < 1e-6
+    assert (got[:lo] == 7.0).all() and (got[hi:] == 7.0).all()
+    for d in (raw, tiles, xd, xq, out):
+        d.free()
