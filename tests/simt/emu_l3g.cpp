@@ -753,4 +753,79 @@ int emu_matvec(const uint8_t* tiles, int rows, int cols, int rpw, const float* x
   });
 }
 
+// The decode step's split-K attention (k_attention, global merge through
+// partials in device memory, the CTAs of a kv head waiting on each other's
+// arrival counters) for one layer, set up as l3g_workspace_new and
+// enqueue_step do: P positions per stage, three stages, splits filling nsm.
+int emu_attention(const float* q, const void* kv, int ctx, int hd, int group, int hkv, int kv_f16,
+                  const int* io, float* out, float* out_d, int8_t* out_q, int nsm, int* splits_out) {
+  return guarded_call([&] {
+    using namespace l3g;
+    const int es = kv_f16 ? 2 : 4;
+    AttnArgs a{};
+    a.P = std::max(NW, (int)(32768 / (2 * hd * es)));
+    a.stage_bytes = 2 * a.P * hd * es;
+    a.nstages = 3;
+    a.n_splits = std::max(1, std::min(nsm / hkv, (ctx + a.P - 1) / a.P));
+    *splits_out = a.n_splits;
+    int gp = 1;
+    while (gp < group) gp <<= 1;
+    const int scratch = std::max(at_scratch_floats(group, hd) * 4, NW * align_up(a.n_splits, 32) * 4);
+    const size_t smem = at_ring_offset() + std::max(a.nstages * a.stage_bytes, scratch);
+    std::vector<void*> sc;
+    auto dm = [&](size_t bytes) {
+      void* p = simt::dmalloc(bytes);
+      sc.push_back(p);
+      return p;
+    };
+    a.wait_ns = WAIT_TIMEOUT_NS;
+    a.q = q;
+    a.kv = kv;
+    a.ctx = ctx;
+    a.hd = hd;
+    a.group = group;
+    a.scale = (float)(1.0 / sqrt((double)hd));
+    a.io = io;
+    a.part_o = static_cast<float*>(dm((size_t)hkv * a.n_splits * group * hd * 4));
+    a.part_ml = static_cast<float*>(dm((size_t)hkv * a.n_splits * group * 2 * 4));
+    a.counters = static_cast<unsigned*>(dm((size_t)hkv * 2 * 4));
+    a.out = out;
+    a.out_d = out_d;
+    a.out_q = out_q;
+    a.res = static_cast<Result*>(dm(sizeof(Result)));
+    const dim3 grid(hkv, a.n_splits);
+    try {
+      auto go = [&](auto dpl_c, auto kt, auto gp_c) {
+        constexpr int D = decltype(dpl_c)::value, GPc = decltype(gp_c)::value;
+        using KT = decltype(kt);
+        simt::launch(grid, dim3(NTHREADS), smem, [&] { k_attention<D, KT, GPc, false>(a); });
+      };
+      auto by_gp = [&](auto dpl_c, auto kt) {
+        switch (gp) {
+          case 1: go(dpl_c, kt, std::integral_constant<int, 1>{}); break;
+          case 2: go(dpl_c, kt, std::integral_constant<int, 2>{}); break;
+          case 4: go(dpl_c, kt, std::integral_constant<int, 4>{}); break;
+          default: go(dpl_c, kt, std::integral_constant<int, 8>{}); break;
+        }
+      };
+      const int dpl = hd / 32;
+      if (kv_f16) {
+        if (dpl == 2) by_gp(std::integral_constant<int, 2>{}, __half{});
+        else by_gp(std::integral_constant<int, 4>{}, __half{});
+      } else {
+        if (dpl == 1) by_gp(std::integral_constant<int, 1>{}, float{});
+        else if (dpl == 2) by_gp(std::integral_constant<int, 2>{}, float{});
+        else by_gp(std::integral_constant<int, 4>{}, float{});
+      }
+      if (a.res->err) simt::fail("k_attention reported an error");
+      for (int i = 0; i < 2 * hkv; ++i)
+        if (a.counters[i]) simt::fail("k_attention left its counters non-zero");
+    } catch (...) {
+      for (void* p : sc) simt::dfree(p);
+      throw;
+    }
+    for (void* p : sc) simt::dfree(p);
+  });
+}
+
 }  // extern "C"

@@ -68,6 +68,8 @@ def lib():
         L.emu_gemm_from_tiles.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P]
         L.emu_prefill.argtypes = [C.c_void_p]
         L.emu_batch_step.argtypes = [C.c_void_p]
+        L.emu_attention.argtypes = [_P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P,
+                                    _P, _P, C.c_int, C.POINTER(C.c_int)]
         L.emu_matvec.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int, C.c_int,
                                  C.c_int]
         L.emu_gemm.argtypes = [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, _P, C.c_int,

@@ -487,3 +487,39 @@ def test_decode_matvec_matches_reference_simd(S, oracle_mod, rows, cols, rpw, lo
     assert (got[:lo] == 7.0).all() and (got[hi:] == 7.0).all()
     for d in (raw, tiles, xd, xq, out):
         d.free()
+
+
+@pytest.mark.parametrize("G,hd,hkv,n,f16", [(4, 128, 2, 700, False), (3, 64, 2, 37, False),
+                                            (2, 32, 3, 300, False), (4, 128, 1, 90, True)])
+def test_decode_attention_matches_exact_softmax(S, G, hd, hkv, n, f16):
+    """The decode step's k_attention (measured on the B200) under the
+    emulator: split-K over the cache with the distributed global merge (the
+    CTAs of a kv head wait on each other's arrival counters, which must come
+    back to zero), against the reference's exact-exp loop (infer.go:130-175)
+    in float64, and its act-quant for Wo bit for bit."""
+    import oracle
+    rng = np.random.default_rng(G * 100 + n)
+    ctx = n + 5
+    q = rng.standard_normal((hkv * G, hd)).astype(np.float32)
+    kv = rng.standard_normal((hkv, ctx, 2, hd)).astype(np.float32)
+    if f16:
+        kv = kv.astype(np.float16).astype(np.float32)
+    dq, dkv = S.Dev(q), S.Dev(kv.astype(np.float16) if f16 else kv)
+    io = S.Dev(np.array([0, n - 1, 0, 0], np.int32))
+    out, od, oq = S.Dev(hkv * G * hd * 4), S.Dev(hkv * G * hd // 32 * 4), S.Dev(hkv * G * hd)
+    import ctypes as C
+    splits = C.c_int()
+    S.check(S.lib().emu_attention(dq.ptr, dkv.ptr, ctx, hd, G, hkv, 1 if f16 else 0, io.ptr, out.ptr,
+                                  od.ptr, oq.ptr, 148, C.byref(splits)))
+    got = out.read(np.float32).reshape(hkv * G, hd)
+    scale = np.float32(1.0 / np.sqrt(hd))
+    for h in range(hkv * G):
+        g = h // G
+        s = (kv[g, :n, 0].astype(np.float64) @ q[h].astype(np.float64)) * float(scale)
+        w = np.exp(s - s.max())
+        want = (w / w.sum()) @ kv[g, :n, 1].astype(np.float64)
+        assert rel_l2(got[h], want) < 1e-5, h
+    d0, q0 = oracle.quantize_q8_0(out.read(np.float32))
+    assert np.array_equal(od.read(np.float32), d0) and np.array_equal(oq.read(np.int8), q0)
+    for d in (dq, dkv, io, out, od, oq):
+        d.free()
