@@ -366,8 +366,20 @@ def trace_summary(m, s, ws, tok, pos, reps=3):
     return out
 
 
-PERSIST_PHASES = {7: ("qkv", "attention", "merge", "wo", "upgate", "act_quant", "down"),
-                  6: ("qkv", "attention", "merge", "wo", "upgate_act_quant", "down")}
+def persist_phases(bpl):
+    """Names of a layer's phases, one per grid barrier, for the fusions in
+    effect (7 barriers: none; 5: both; 6: the one whose variable is set)."""
+    fuse_merge = bpl == 5 or (bpl == 6 and os.environ.get("L3G_PERSIST_FUSE_MERGE") == "1")
+    fuse_quant = bpl == 5 or (bpl == 6 and not fuse_merge)
+    names = ["qkv", "attention_merge" if fuse_merge else "attention"]
+    if not fuse_merge:
+        names.append("merge")
+    names += ["wo", "upgate_act_quant" if fuse_quant else "upgate"]
+    if not fuse_quant:
+        names.append("act_quant")
+    names.append("down")
+    assert len(names) == bpl, (names, bpl)
+    return tuple(names)
 
 
 def persist_summary(m, s, ws, tok, pos, reps=3):
@@ -378,7 +390,7 @@ def persist_summary(m, s, ws, tok, pos, reps=3):
     arrival to last release)."""
     import numpy as np
     bpl = ws.persist_layout()["barriers_per_layer"]
-    names = PERSIST_PHASES[bpl]
+    names = persist_phases(bpl)
     acc = {n: [] for n in names}
     lat = []
     for _ in range(reps):

@@ -301,10 +301,11 @@ int l3g_trace_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
 int l3g_workspace_persistent(const l3g_workspace *ws, int32_t *on);
 /* The persistent kernel's layout on this workspace: ring slots and their
  * bytes, attention splits per kv head, grid-barrier counters, shared memory
- * per CTA, grid barriers per layer (6 when the SwiGLU act-quant is fused into
- * the up/gate phase, else 7).  Inspection only (L3G_PERSIST_STAGES,
- * L3G_PERSIST_SPLITS, L3G_PERSIST_BAR_SPREAD and L3G_PERSIST_FUSE_QUANT, read
- * at workspace creation, cap or set them). */
+ * per CTA, grid barriers per layer (7, one less with the SwiGLU act-quant
+ * fused into the up/gate phase, one less with the split merge fused into the
+ * attention phase).  Inspection only (L3G_PERSIST_STAGES, L3G_PERSIST_SPLITS,
+ * L3G_PERSIST_BAR_SPREAD, L3G_PERSIST_FUSE_QUANT and L3G_PERSIST_FUSE_MERGE,
+ * read at workspace creation, cap or set them). */
 int l3g_persist_layout(const l3g_workspace *ws, int32_t *stages, int32_t *slot_bytes,
                        int32_t *splits, int32_t *counters, int32_t *smem_bytes,
                        int32_t *barriers_per_layer);

@@ -62,7 +62,8 @@ struct PersistArgs {
   unsigned* bar;          // barrier counters, abort word, handshakes (persist::BAR_*), zeroed by k_embed
   int nsub;               // barrier counters in use (1 .. BAR_MAX_SUB)
   int fuse_quant;         // the SwiGLU act-quant runs in the up/gate phase (no QUANT phase)
-  int bpl;                // grid barriers per layer (6 fused, else 7)
+  int fuse_merge;         // the split merge runs in the attention phase (k_layers<..., true>)
+  int bpl;                // grid barriers per layer (7, less one per fusion)
   Result* res;
   unsigned long long wait_ns;
   TpExchange tp;          // tp.world > 1: Wo / down rows pushed to every rank
@@ -77,6 +78,7 @@ struct PSmem {
   int issued;
   int producer_done;
   int stop;  // the CTA's decision at a grid barrier (written by thread 0)
+  int merge_last;  // fused merge: this CTA published its kv head's last partial
   // fused act-quant: warps done with the CTA's k-th up/gate group, slot
   // k % GSLOTS (warps drift apart by at most the ring's depth in tiles, so at
   // most MAX_STAGES groups: slots never alias)
@@ -657,50 +659,84 @@ __device__ void ps_attention(const PersistArgs& a, int l, int n, uint32_t& t, ui
   }
 }
 
-// Merge of the splits of every kv head in split order, one warp per block of
-// 32 outputs (k_attention's global merge), and its act-quant for Wo.
-__device__ void ps_merge(const PersistArgs& a, uint8_t* uni) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Merge of the splits of kv head kvh for output block blk (32 outputs of one
+// query head) in split order, k_attention's global merge, and its act-quant
+// for Wo.  One warp; wbuf holds align_up(splits, 32) floats of its own.
+__device__ void ps_merge_block(const PersistArgs& a, float* wbuf, int kvh, int blk, int lane) {
   const int S = a.plan.splits, G = a.group, hd = a.head_dim, gh = G * hd;
-  const int nblk = a.hq * hd / 32;
-  float* wbuf = reinterpret_cast<float*>(uni) + warp * align_up(S, 32);
-  for (int gb = blockIdx.x * NW + warp; gb < nblk; gb += gridDim.x * NW) {
-    const int kvh = gb / (gh / 32), blk = gb % (gh / 32);
-    const int h = blk * 32 / hd;
-    const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
-    const float* po = a.part_o + (size_t)kvh * S * gh;
-    float M = -INFINITY;
-    for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
-    M = warp_max(M);
-    float L = 0.0f;
-    for (int s0 = 0; s0 < S; s0 += 32) {
-      const int s2 = s0 + lane;
-      float le = 0.0f;
-      if (s2 < S) {
-        const float ms = __ldcg(ml + ((size_t)s2 * G + h) * 2);
-        const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
-        wbuf[s2] = e;
-        le = __ldcg(ml + ((size_t)s2 * G + h) * 2 + 1) * e;
-      }
-      L += warp_sum(le);
+  const int h = blk * 32 / hd;
+  const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
+  const float* po = a.part_o + (size_t)kvh * S * gh;
+  float M = -INFINITY;
+  for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
+  M = warp_max(M);
+  float L = 0.0f;
+  for (int s0 = 0; s0 < S; s0 += 32) {
+    const int s2 = s0 + lane;
+    float le = 0.0f;
+    if (s2 < S) {
+      const float ms = __ldcg(ml + ((size_t)s2 * G + h) * 2);
+      const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
+      wbuf[s2] = e;
+      le = __ldcg(ml + ((size_t)s2 * G + h) * 2 + 1) * e;
     }
-    __syncwarp();
-    const float* col = po + (size_t)blk * 32 + lane;
-    float O = 0.0f;
-    int s2 = 0;
-    for (; s2 + 8 <= S; s2 += 8) {
-      float ov[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) ov[u] = __ldcg(col + (size_t)(s2 + u) * gh);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) O = fmaf(ov[u], wbuf[s2 + u], O);
-    }
-    for (; s2 < S; ++s2) O = fmaf(__ldcg(col + (size_t)s2 * gh), wbuf[s2], O);
-    __syncwarp();
-    const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
-    a.attn[(size_t)kvh * gh + blk * 32 + lane] = v;
-    quant_block(v, kvh * gh / 32 + blk, lane, a.attn_d, a.attn_q);
+    L += warp_sum(le);
   }
+  __syncwarp();
+  const float* col = po + (size_t)blk * 32 + lane;
+  float O = 0.0f;
+  int s2 = 0;
+  for (; s2 + 8 <= S; s2 += 8) {
+    float ov[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) ov[u] = __ldcg(col + (size_t)(s2 + u) * gh);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) O = fmaf(ov[u], wbuf[s2 + u], O);
+  }
+  for (; s2 < S; ++s2) O = fmaf(__ldcg(col + (size_t)s2 * gh), wbuf[s2], O);
+  __syncwarp();
+  const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
+  a.attn[(size_t)kvh * gh + blk * 32 + lane] = v;
+  quant_block(v, kvh * gh / 32 + blk, lane, a.attn_d, a.attn_q);
+}
+
+// Merge of output blocks gb0, gb0 + step, ... < gb1 (block gb: kv head
+// gb / (group * hd / 32), its block gb % (group * hd / 32)), one warp each.
+// Unfused, after the attention barrier, the grid's warps share every block;
+// with the fused merge, the warps of the CTA that claimed a kv head take its
+// blocks.  One call site, so the merge is inlined once into k_layers.
+__device__ void ps_merge(const PersistArgs& a, uint8_t* uni, int gb0, int gb1, int step) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per = a.group * a.head_dim / 32;
+  float* wbuf = reinterpret_cast<float*>(uni) + warp * align_up(a.plan.splits, 32);
+  for (int gb = gb0; gb < gb1; gb += step) ps_merge_block(a, wbuf, gb / per, gb % per, lane);
+}
+
+// The merge folded into the attention phase (fuse_merge): after publishing
+// its item's partial, a CTA adds one to its kv head's arrival counter (after
+// the quantization handshake words of the barrier area); the CTA that brings
+// it to the split count claims that kv head -- its warps merge the head's
+// blocks (ps_merge, the same arithmetic, so results are unchanged) -- and
+// returns the counter to 0 for the next layer.  Returns the claimed kv head
+// or -1.  Fences as at a grid barrier: every thread's partial stores, the
+// CTA barrier, then thread 0's release fence and atomic; the claimer's fence
+// after its atomic, then the CTA barrier, before its warps read partials.
+__device__ int ps_merge_claim(const PersistArgs& a, int l, PSmem* sh) {
+  int kvh, split;
+  if (!persist::my_item(a.plan, l, blockIdx.x, &kvh, &split)) return -1;  // uniform over the CTA
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    unsigned* cnt = a.bar + persist::BAR_QCNT + a.n_ff / 32 + kvh;
+    __threadfence();
+    const bool last = atomicAdd(cnt, 1u) == (unsigned)(a.plan.splits - 1);
+    if (last) {
+      __threadfence();
+      *cnt = 0u;
+    }
+    sh->merge_last = last ? 1 : 0;
+  }
+  consumer_sync();
+  return sh->merge_last ? kvh : -1;
 }
 
 // Act-quant of the SwiGLU output (infer.go:233-234), one warp per block.
@@ -748,7 +784,9 @@ __device__ void ps_reduce(const PersistArgs& a, unsigned e) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int DPL, typename KT, int GP>
+// FM: the split merge folded into the attention phase (a.fuse_merge), a
+// separate instantiation so that the unfused kernel's registers are its own.
+template <int DPL, typename KT, int GP, bool FM>
 __global__ void __launch_bounds__(NTHREADS, 1) k_layers(const __grid_constant__ PersistArgs a) {
   using namespace persist;
   L3G_DYNAMIC_SMEM(smem);
@@ -794,8 +832,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_layers(const __grid_constant__ 
     if (!ps_barrier(a, bi++, sh)) break;
     // attention, infer.go:130-175
     ps_attention<DPL, KT, GP>(a, l, pos + 1, t, uni, ring, sh);
-    if (!ps_barrier(a, bi++, sh)) break;
-    ps_merge(a, uni);
+    if constexpr (FM) {  // the merge by the CTA that claims a kv head
+      const int kvh = ps_merge_claim(a, l, sh), per = a.group * a.head_dim / 32;
+      if (kvh >= 0) ps_merge(a, uni, kvh * per + warp, (kvh + 1) * per, NW);
+    } else {  // the merge spread over the grid after a barrier
+      if (!ps_barrier(a, bi++, sh)) break;
+      ps_merge(a, uni, blockIdx.x * NW + warp, a.hq * a.head_dim / 32, gridDim.x * NW);
+    }
     if (!ps_barrier(a, bi++, sh)) break;
     // Wo, infer.go:178-187 (the residual add is fused into the next norm)
     ps_preq(a.attn_d, a.attn_q, p.cols[M_WO], xd, xqs);

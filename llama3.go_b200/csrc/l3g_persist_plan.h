@@ -70,8 +70,11 @@ enum Mat { M_QKV = 0, M_WO = 1, M_UPGATE = 2, M_DOWN = 3, N_MAT = 4 };
 enum Deal { D_QKV = 0, D_ATT = 1, D_WO = 2, D_UPGATE = 3, D_DOWN = 4, N_DEAL = 5 };
 constexpr int BARRIERS_PER_LAYER = 7;  // after QKV, ATT, MERGE, WO, UPGATE, QUANT, DOWN
 // With the SwiGLU act-quant fused into the up/gate phase the QUANT phase and
-// its barrier go: 6 barriers per layer.
-L3G_HD inline int barriers_per_layer(bool fuse_quant) { return fuse_quant ? 6 : 7; }
+// its barrier go; with the split merge fused into the attention phase the
+// barrier between ATT and MERGE goes: 7, 6 or 5 barriers per layer.
+L3G_HD inline int barriers_per_layer(bool fuse_quant, bool fuse_merge = false) {
+  return 7 - (fuse_quant ? 1 : 0) - (fuse_merge ? 1 : 0);
+}
 
 struct Plan {
   int grid;       // CTAs (one per SM)
@@ -171,7 +174,8 @@ constexpr int BAR_MAX_SUB = 16;
 constexpr int BAR_ABORT = BAR_MAX_SUB * BAR_STRIDE;  // the step's abort word
 constexpr int BAR_WORDS = BAR_ABORT + 1;
 // After them: one arrival counter per Q8_0 block of the SwiGLU output (the
-// fused act-quant's handshake between the two 32-row groups of a block).
+// fused act-quant's handshake between the two 32-row groups of a block),
+// then one per kv head of the rank (the fused merge's split arrivals).
 constexpr int BAR_QCNT = BAR_WORDS;
 L3G_HD inline int sub_count(int grid, int nsub, int i) {
   return grid / nsub + (i < grid % nsub ? 1 : 0);

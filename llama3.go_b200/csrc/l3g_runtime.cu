@@ -1004,6 +1004,7 @@ struct l3g_workspace {
   persist::Plan ps_plan{};     // ctx is the state's, filled per capture
   int ps_ns = 0, ps_slot = 0, ps_union = 0, ps_xq_off = 0, ps_smem = 0, ps_nsub = 1;
   bool ps_fuse = false;        // SwiGLU act-quant fused into the up/gate phase
+  bool ps_fuse_merge = false;  // split merge fused into the attention phase
   int ps_bar_words = 0;        // words of d_bar that k_embed zeroes
   unsigned* d_bar = nullptr;   // grid-barrier counters and abort word (persist::BAR_*)
   // the top-K path's fastExp attention (l3g_workspace_set_topk_fast_exp):
@@ -1247,26 +1248,26 @@ static void choose_attention_cluster(l3g_workspace* ws) {
 }
 
 template <int DPL, typename KT>
-static void* layers_kernel_t(int gp) {
+static void* layers_kernel_t(int gp, bool fm) {
   switch (gp) {
-    case 1: return (void*)k_layers<DPL, KT, 1>;
-    case 2: return (void*)k_layers<DPL, KT, 2>;
-    case 4: return (void*)k_layers<DPL, KT, 4>;
-    case 8: return (void*)k_layers<DPL, KT, 8>;
+    case 1: return fm ? (void*)k_layers<DPL, KT, 1, true> : (void*)k_layers<DPL, KT, 1, false>;
+    case 2: return fm ? (void*)k_layers<DPL, KT, 2, true> : (void*)k_layers<DPL, KT, 2, false>;
+    case 4: return fm ? (void*)k_layers<DPL, KT, 4, true> : (void*)k_layers<DPL, KT, 4, false>;
+    case 8: return fm ? (void*)k_layers<DPL, KT, 8, true> : (void*)k_layers<DPL, KT, 8, false>;
     default: return nullptr;
   }
 }
 // The instantiation of k_layers for this model's head size, KV element type
 // and query heads per kv head (rounded up to a power of two).
-static void* layers_kernel(const l3g_model* m, int gp) {
+static void* layers_kernel(const l3g_model* m, int gp, bool fm) {
   const int dpl = m->hd / 32;
   if (m->kv_f16) {
-    if (dpl == 2) return layers_kernel_t<2, __half>(gp);
-    if (dpl == 4) return layers_kernel_t<4, __half>(gp);
+    if (dpl == 2) return layers_kernel_t<2, __half>(gp, fm);
+    if (dpl == 4) return layers_kernel_t<4, __half>(gp, fm);
   } else {
-    if (dpl == 1) return layers_kernel_t<1, float>(gp);
-    if (dpl == 2) return layers_kernel_t<2, float>(gp);
-    if (dpl == 4) return layers_kernel_t<4, float>(gp);
+    if (dpl == 1) return layers_kernel_t<1, float>(gp, fm);
+    if (dpl == 2) return layers_kernel_t<2, float>(gp, fm);
+    if (dpl == 4) return layers_kernel_t<4, float>(gp, fm);
   }
   return nullptr;
 }
@@ -1319,7 +1320,13 @@ static int persist_setup(l3g_workspace* ws) {
   ws->ps_smem = PS_HEAD + ws->ps_union + ws->ps_ns * ws->ps_slot;
   int gp = 1;
   while (gp < m->group) gp <<= 1;
-  void* k = layers_kernel(m, gp);
+  // L3G_PERSIST_FUSE_MERGE=1: the split merge runs in the attention phase
+  // (its own instantiation of the kernel)
+  {
+    const char* env = getenv("L3G_PERSIST_FUSE_MERGE");
+    ws->ps_fuse_merge = env && atoi(env) == 1;
+  }
+  void* k = layers_kernel(m, gp, ws->ps_fuse_merge);
   // attributes of this instantiation only, here rather than at load, so the
   // per-kernel step never depends on the persistent kernel's set-up
   int per_sm = 0;
@@ -1336,7 +1343,7 @@ static int persist_setup(l3g_workspace* ws) {
     ws->ps_fuse = env && atoi(env) == 1 && p.wr[persist::M_UPGATE] == 32 &&
                   p.rows[persist::M_UPGATE] % 64 == 0;
   }
-  ws->ps_bar_words = persist::BAR_QCNT + m->ff_l / 32;
+  ws->ps_bar_words = persist::BAR_QCNT + m->ff_l / 32 + m->hkv_l;
   CUDA_TRY(cudaMalloc(&ws->d_bar, ws->ps_bar_words * sizeof(unsigned)));
   CUDA_TRY(cudaMemset(ws->d_bar, 0, ws->ps_bar_words * sizeof(unsigned)));
   // barrier counters: L3G_PERSIST_BAR_SPREAD=n spreads the arrivals over n
@@ -1692,7 +1699,8 @@ static PersistArgs persist_args(const l3g_workspace* ws, const l3g_state* s,
   a.bar = ws->d_bar;
   a.nsub = ws->ps_nsub;
   a.fuse_quant = ws->ps_fuse ? 1 : 0;
-  a.bpl = persist::barriers_per_layer(ws->ps_fuse);
+  a.fuse_merge = ws->ps_fuse_merge ? 1 : 0;
+  a.bpl = persist::barriers_per_layer(ws->ps_fuse, ws->ps_fuse_merge);
   a.res = ws->d_res;
   a.wait_ns = m->world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS;
   if (ws->tp_p2p) {
@@ -1758,7 +1766,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     const PersistArgs a = persist_args(ws, s, stamps);
     int gp = 1;
     while (gp < m->group) gp <<= 1;
-    void* kfn = layers_kernel(m, gp);
+    void* kfn = layers_kernel(m, gp, ws->ps_fuse_merge);
     if (!kfn) return l3g_fail(L3G_E_INVALID, "no persistent layer kernel for this shape");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ws->ps_plan.grid);
@@ -2377,7 +2385,7 @@ extern "C" int l3g_persist_layout(const l3g_workspace* ws, int32_t* stages, int3
   *splits = ws->ps_plan.splits;
   *counters = ws->ps_nsub;
   *smem_bytes = ws->ps_smem;
-  *barriers_per_layer = persist::barriers_per_layer(ws->ps_fuse);
+  *barriers_per_layer = persist::barriers_per_layer(ws->ps_fuse, ws->ps_fuse_merge);
   return L3G_OK;
 }
 
@@ -2391,7 +2399,7 @@ extern "C" int l3g_persist_stamps(const l3g_workspace* ws, uint64_t* out, int64_
   if (cap < (int64_t)(bytes / 8)) return l3g_fail(L3G_E_INVALID, "capacity %lld < %zu", (long long)cap, bytes / 8);
   CUDA_TRY(cudaSetDevice(ws->device));
   CUDA_TRY(cudaMemcpy(out, ws->d_trace + kPersistStampOff, bytes, cudaMemcpyDeviceToHost));
-  *n_barriers = persist::barriers_per_layer(ws->ps_fuse) * ws->ps_plan.n_layers;
+  *n_barriers = persist::barriers_per_layer(ws->ps_fuse, ws->ps_fuse_merge) * ws->ps_plan.n_layers;
   *grid = ws->ps_plan.grid;
   return L3G_OK;
 }

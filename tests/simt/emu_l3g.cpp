@@ -130,6 +130,7 @@ struct EmuLayers {
   int grid, n_layers, n_emb, n_ff, hq, hkv, hd, rope_half, ctx, kv_f16;
   int fuse_quant, nsub, max_stages, max_splits;
   int launch_grid;           // CTAs actually launched (0: the plan's grid)
+  int fuse_merge;            // the split merge in the attention phase
   unsigned long long wait_ns;  // bound of every wait in emulated ns (0: the library's)
   float eps;
   const void* const* w;      // [n_layers * 4] tiled QKV, Wo, up/gate, down (device)
@@ -200,7 +201,7 @@ void setup_rank(EmuLayers* e, int world, int rank, unsigned* step,
   int* io = static_cast<int*>(dm(16));
   io[0] = e->token;
   io[1] = e->pos;
-  const int bar_words = persist::BAR_QCNT + e->n_ff / 32;
+  const int bar_words = persist::BAR_QCNT + e->n_ff / 32 + e->hkv;
   auto* bar = static_cast<unsigned*>(dm(bar_words * 4));  // zeroed, as k_embed leaves it
   rr.res = static_cast<Result*>(dm(sizeof(Result)));
   a.layers = layers;
@@ -233,7 +234,8 @@ void setup_rank(EmuLayers* e, int world, int rank, unsigned* step,
   a.nsub = std::max(1, std::min({e->nsub, (int)persist::BAR_MAX_SUB, p.grid}));
   a.fuse_quant = e->fuse_quant && p.wr[persist::M_UPGATE] == 32 &&
                  p.rows[persist::M_UPGATE] % 64 == 0;
-  a.bpl = persist::barriers_per_layer(a.fuse_quant != 0);
+  a.fuse_merge = e->fuse_merge ? 1 : 0;
+  a.bpl = persist::barriers_per_layer(a.fuse_quant != 0, a.fuse_merge != 0);
   a.res = rr.res;
   a.wait_ns = e->wait_ns ? e->wait_ns : (world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS);
   a.tp = TpExchange{};
@@ -252,10 +254,15 @@ void setup_rank(EmuLayers* e, int world, int rank, unsigned* step,
 
 template <int D, typename KT>
 void launch_layers(int gp, dim3 grid, size_t smem, std::vector<RankRun>& rr) {
+  const bool fm = rr[0].a.fuse_merge != 0;
   auto go = [&](auto gp_c) {
     constexpr int GPc = decltype(gp_c)::value;
-    simt::launch(grid, dim3(l3g::NTHREADS), smem,
-                 [&] { l3g::k_layers<D, KT, GPc>(rr[simt::block_idx().z].a); });
+    simt::launch(grid, dim3(l3g::NTHREADS), smem, [&] {
+      if (fm)
+        l3g::k_layers<D, KT, GPc, true>(rr[simt::block_idx().z].a);
+      else
+        l3g::k_layers<D, KT, GPc, false>(rr[simt::block_idx().z].a);
+    });
   };
   switch (gp) {
     case 1: go(std::integral_constant<int, 1>{}); break;

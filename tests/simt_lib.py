@@ -41,7 +41,8 @@ def build():
 class EmuLayers(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("grid", "n_layers", "n_emb", "n_ff", "hq", "hkv", "hd",
                                        "rope_half", "ctx", "kv_f16", "fuse_quant", "nsub",
-                                       "max_stages", "max_splits", "launch_grid")] + [
+                                       "max_stages", "max_splits", "launch_grid",
+                                       "fuse_merge")] + [
         ("wait_ns", C.c_ulonglong), ("eps", C.c_float), ("w", C.POINTER(_P)), ("norm", C.POINTER(_P)),
         ("xa", _P), ("xb", _P), ("y", _P), ("attn", _P), ("act", _P), ("kv", _P),
         ("rope_cos", _P), ("rope_sin", _P), ("token", C.c_int), ("pos", C.c_int),
@@ -247,8 +248,8 @@ class PersistentModel:
 
     def step(self, token, pos, **kw):
         """One token's layers; returns (hidden state after the last layer,
-        the EmuLayers record).  kw: fuse_quant, nsub, max_stages, max_splits,
-        launch_grid, wait_ns."""
+        the EmuLayers record).  kw: fuse_quant, fuse_merge, nsub, max_stages,
+        max_splits, launch_grid, wait_ns."""
         a = self.record(token, pos, **kw)
         check(lib().emu_layers(C.byref(a)))
         return self.hidden(), a

@@ -33,10 +33,17 @@ pytestmark = [
 ]
 
 
+def _fusions(fuse):
+    """fuse: "0" none, "1" the SwiGLU act-quant, "m" the split merge, "1m" both."""
+    return "1" in fuse, "m" in fuse
+
+
 def _load(gpu_lib, monkeypatch, cfg, T, persistent, fuse="0", spread="1", **kw):
+    fq, fm = _fusions(fuse)
     monkeypatch.setenv("L3G_RPW", "4")
     monkeypatch.setenv("L3G_ATT_CLUSTER", "0")
-    monkeypatch.setenv("L3G_PERSIST_FUSE_QUANT", fuse)
+    monkeypatch.setenv("L3G_PERSIST_FUSE_QUANT", "1" if fq else "0")
+    monkeypatch.setenv("L3G_PERSIST_FUSE_MERGE", "1" if fm else "0")
     monkeypatch.setenv("L3G_PERSIST_BAR_SPREAD", spread)
     if persistent:
         monkeypatch.setenv("L3G_PERSIST", "1")
@@ -71,6 +78,9 @@ def _run(gpu_lib, m, cfg, ids, ctx, prefill=0):
     # the SwiGLU act-quant fused into up/gate, barrier arrivals spread over counters
     ("tiny", 24, 0, "f32", "1", "3"), ("mid", 16, 0, "f32", "1", "16"),
     ("llama3.2-1b-2l", 12, 0, "f32", "1", "1"), ("small", 40, 0, "f32", "0", "16"),
+    # the split merge in the attention phase, alone and with the act-quant fold
+    ("small-hd128", 1500, 1496, "f32", "m", "1"), ("mid", 16, 0, "f32", "1m", "4"),
+    ("tiny-g3", 24, 0, "f32", "m", "1"),
 ])
 def test_bit_identical_to_per_kernel_step(gpu_lib, monkeypatch, name, n_tok, prefill, kv, fuse,
                                           spread):
@@ -86,7 +96,8 @@ def test_bit_identical_to_per_kernel_step(gpu_lib, monkeypatch, name, n_tok, pre
     ws1, l1, kv1, h1 = _run(gpu_lib, pers, cfg, ids, ctx, prefill)
     assert ws1.persistent()
     lay = ws1.persist_layout()
-    assert lay["barriers_per_layer"] == (6 if fuse == "1" else 7)
+    fq, fm = _fusions(fuse)
+    assert lay["barriers_per_layer"] == 7 - fq - fm
     assert lay["barrier_counters"] == int(spread)
     for i, (a, b) in enumerate(zip(l0, l1)):
         assert np.array_equal(a, b), (i, rel_l2(b, a))

@@ -71,6 +71,8 @@ CASES = [
     ("tiny-gqa", 600, 2, 8, False, {}),                     # 4 splits x 2 stages
     ("tiny-g3", 300, 2, 5, False, {}),                      # G 3 (padded to 4)
     ("small", 200, 2, 6, False, {"fuse_quant": 1}),         # hd 64, fused act-quant
+    ("tiny-gqa", 600, 2, 8, False, {"fuse_merge": 1}),      # merge in the attention phase
+    ("small", 200, 2, 6, False, {"fuse_quant": 1, "fuse_merge": 1}),
     ("small-hd128", 100, 2, 3, False, {}),                  # hd 128, one kv head
     ("tiny-gqa", 260, 2, 7, False, {"max_stages": 2, "nsub": 4}),
     ("small", 100, 2, 6, True, {}),                         # f16 cache
@@ -118,8 +120,9 @@ def _run_steps(S, cfg, T, ctx, grid, ids, prefix_kv, **kw):
 
 
 def test_persistent_step_is_bit_identical_across_schedules(S, oracle_mod):
-    """Random thread orders and bulk-copy delays, the fused act-quant, spread
-    barrier counters and a short ring change no bit of the result."""
+    """Random thread orders and bulk-copy delays, the fused act-quant, the
+    fused merge, spread barrier counters and a short ring change no bit of
+    the result."""
     import synthetic
     cfg, T = _model("tiny-g3", 160)
     ctx = 160
@@ -132,7 +135,8 @@ def test_persistent_step_is_bit_identical_across_schedules(S, oracle_mod):
         S.lib().emu_schedule(0, 0, 0)
         base_h, base_kv = _run_steps(S, cfg, T, ctx, 5, ids, prefix_kv)
         variants = [(1, {"fuse_quant": 1}), (2, {"nsub": 3, "max_stages": 3}),
-                    (3, {"fuse_quant": 1, "nsub": 2, "max_stages": 2})]
+                    (3, {"fuse_quant": 1, "nsub": 2, "max_stages": 2}),
+                    (4, {"fuse_merge": 1}), (5, {"fuse_quant": 1, "fuse_merge": 1, "max_stages": 2})]
         for seed, kw in variants:
             S.lib().emu_schedule(1, seed, 64)
             h, kv = _run_steps(S, cfg, T, ctx, 5, ids, prefix_kv, **kw)
@@ -199,7 +203,8 @@ def test_persistent_step_tensor_parallel(S, oracle_mod, world, grid, prefix):
     its shard as the library's shard plan cuts it, pushes its Wo / down rows
     into every rank's receive buffer with the step's epochs and sums the
     ranks' rows in rank order.  Every rank ends with the same hidden state,
-    within 1e-5 of the oracle; a random schedule gives the same bits."""
+    within 1e-5 of the oracle; a random schedule with both fusions gives the
+    same bits."""
     import synthetic
     ctx = prefix + 2 + 3
     # 8 query heads over 4 kv heads, so that 4 ranks hold one kv head each
@@ -210,13 +215,13 @@ def test_persistent_step_tensor_parallel(S, oracle_mod, world, grid, prefix):
     K, V = om.kv_arrays()
     K, V = K.copy(), V.copy()
 
-    def run():
+    def run(**kw):
         ms = [S.PersistentModel(cfg, T, ctx, grid, world=world, rank=r) for r in range(world)]
         for m in ms:
             m.load_kv(K, V, prefix)
         out = []
         for i, pos in enumerate(range(prefix, prefix + 2)):
-            hs, recs = S.step_tp(ms, ids[pos], pos, step_count=i + 1)
+            hs, recs = S.step_tp(ms, ids[pos], pos, step_count=i + 1, **kw)
             assert all(r.err == 0 for r in recs), [(r.err, r.where) for r in recs]
             assert all(np.array_equal(hs[0], h) for h in hs)
             out.append(hs[0])
@@ -231,7 +236,7 @@ def test_persistent_step_tensor_parallel(S, oracle_mod, world, grid, prefix):
             om.forward(int(ids[pos]), logits=False)
             assert rel_l2(got[i], om.buffer("hidden")) < 1e-5, i
         S.lib().emu_schedule(1, 11, 64)
-        assert np.array_equal(run(), got)
+        assert np.array_equal(run(fuse_merge=1, fuse_quant=1), got)
     finally:
         S.lib().emu_schedule(0, 0, 0)
         om.close()
