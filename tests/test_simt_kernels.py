@@ -413,7 +413,7 @@ def test_persistent_step_at_the_8b_layer_shapes(S, oracle_mod, fuse):
     pure.pos = prefix
     pm = S.PersistentModel(cfg, T, ctx, 148)
     pm.load_kv(K, V, prefix)
-    hidden, rec = pm.step(ids[prefix], prefix, fuse_quant=fuse)
+    hidden, rec = pm.step(ids[prefix], prefix, fuse_quant=fuse, fuse_merge=fuse)  # both folds or none
     assert rec.err == 0 and rec.splits == 10
     cgo.forward(int(ids[prefix]), logits=False)
     pure.forward(int(ids[prefix]), logits=False, use_ref=False)
