@@ -333,11 +333,11 @@ void l3g_matrix_free(l3g_matrix *w);
 int l3g_matrix_device_bytes(const l3g_matrix *w, uint64_t *bytes);
 
 /* ---- matvec + argmax without allocation ---------------------------------- */
-/* No counterpart in the reference: its greedy step runs the logits matvec
- * (infer.go:250-260) and then scans the logits on the host (Sampler.Sample,
- * sampling.go:37-65).  This entry fuses the two on the device: the same
- * Q8_0 matvec as l3g_matvec_q8 over all rows, and the argmax over the rows
- * (ties to the lowest row).  It allocates nothing, at any call: the
+/* No counterpart in the reference: the reference has no greedy or argmax
+ * step at all (its Sampler forces a temperature of 0.8 when given 0,
+ * sampling.go:20-22, and always samples).  This entry runs the same Q8_0
+ * matvec as l3g_matvec_q8 over all rows and the argmax over the rows (ties
+ * to the lowest row) in one launch.  It allocates nothing, at any call: the
  * cross-CTA reduction uses a fixed static device array of
  * L3G_ARGMAX_STATIC_MAX_CTAS per-CTA slots plus one arrival counter, so a
  * caller holding no workspace (the matrix handle is all it has, as with
@@ -346,20 +346,26 @@ int l3g_matrix_device_bytes(const l3g_matrix *w, uint64_t *bytes);
  * cudaMalloc/cudaFree, which synchronize the device) can still get a greedy
  * token without a host round trip over the logits.
  *  - x_scales, x_qs, out, result are DEVICE pointers; out may be NULL (the
- *    logits are then not stored); *result is cleared on the stream and then
- *    receives {index, value, status, detail}, status 0 unless a bounded wait
- *    of the kernel gave up (then an internal code, detail = wait site).
+ *    logits are then not stored).  *result is set on the stream to
+ *    {-1, 0, 0, 0} and then receives {index, value, status, detail} from the
+ *    launch: status 0 unless a bounded wait of the kernel gave up (then an
+ *    internal code, detail = wait site).  An index still -1 after the stream
+ *    completes means the launch's cross-CTA merge never ran (see overlap
+ *    below).
  *  - max_ctas caps the CTAs of the launch (0: one per SM); values above
  *    L3G_ARGMAX_STATIC_MAX_CTAS, or an SM count above it, are rejected with
  *    L3G_E_INVALID.
  *  - The first call on a device does the set-up (looks up the static array's
  *    device address with that device current); make that first call before
- *    any stream capture on the device.
- *  - The arrival counter must be zero when a launch starts: it is zero when
- *    the library loads and every launch's last CTA resets it; the slots need
- *    no initial value.  The array is shared by every call on the device, so
- *    calls that overlap in time (other streams, other threads) race and give
- *    wrong results: issue them on one stream, or serialize them. */
+ *    any stream capture on the device.  A failed set-up is not latched: it
+ *    reports its CUDA error and the next call retries.  The caller's current
+ *    device is the same after the call as before it.
+ *  - The arrival counter must be zero when a launch starts: every call
+ *    clears it on its stream before its launch; the slots need no initial
+ *    value.  The array is shared by every call on the device, so calls that
+ *    overlap in time (other streams, other threads) race and give wrong
+ *    results, possibly index -1: issue them on one stream, or serialize
+ *    them.  The next call after an overlap starts from a cleared counter. */
 #define L3G_ARGMAX_STATIC_MAX_CTAS 1024
 typedef struct l3g_argmax_result {
   int32_t index;  /* row of the largest value                        */

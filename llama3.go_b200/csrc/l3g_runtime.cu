@@ -1773,11 +1773,15 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = ws->ps_smem;
     cfg.stream = st;
+    // A cooperative launch: the driver guarantees every CTA of the grid is
+    // resident at once (the grid barriers between phases depend on it) or
+    // refuses the launch with cudaErrorCooperativeLaunchTooLarge.  No
+    // programmatic early launch for it: k_layers starts after k_embed ends.
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = g_serialize ? 0 : 1;
+    cfg.numAttrs = 1;
     void* kargs[] = {(void*)&a};
     KL(L3G_K_LAYERS, cudaLaunchKernelExC(&cfg, kfn, kargs));
   }
@@ -2522,26 +2526,30 @@ extern "C" int l3g_matvec_q8(const l3g_matrix* w, const float* x_scales, const i
 // ---------------------------------------------------------------------------
 // Layout of the array: [0, S) per-CTA best value (float bits), [S, 2S) its
 // row, [2S] the arrival counter, S = L3G_ARGMAX_STATIC_MAX_CTAS (8 KB + 256
-// bytes).  The counter must be zero when a launch starts: static device
-// storage is zero-initialized when the module loads, and the launch's last
-// CTA writes it back to zero after reading the slots.  The slots need no
-// initial value: a CTA writes its own before it increments the counter.
+// bytes).  The counter must be zero when a launch starts, so every call
+// clears it on its stream before the launch (a 4-byte memset, no
+// allocation); a counter left wrong by overlapping calls is therefore
+// repaired by the next call.  The slots need no initial value: a CTA writes
+// its own before it increments the counter.
 constexpr int kArgmaxSlots = L3G_ARGMAX_STATIC_MAX_CTAS;
 static __device__ __align__(256) uint32_t g_argmax_scratch[2 * kArgmaxSlots + 64];
 
-struct ArgmaxStatic {   // per device, filled by the first call on it
-  std::once_flag once;
-  int rc = L3G_OK;
+struct ArgmaxStatic {   // per device, filled by the first successful set-up on it
+  std::mutex mu;
+  bool ready = false;
   uint32_t* scratch = nullptr;
 };
 static ArgmaxStatic g_argmax_static[64];
 
 // Once per device, with that device current: the array's device address and
-// the kernels' attributes.  Neither allocates.
+// the kernels' attributes.  Neither allocates.  Only success is latched: a
+// failed set-up (for instance a first call made during stream capture)
+// reports its CUDA error and the next call tries again.
 static int argmax_static_setup(int dev, uint32_t** scratch) {
   if (dev < 0 || dev >= 64) return l3g_fail(L3G_E_INVALID, "device %d out of range", dev);
   ArgmaxStatic& st = g_argmax_static[dev];
-  std::call_once(st.once, [&st] {
+  std::lock_guard<std::mutex> lock(st.mu);
+  if (!st.ready) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
     if (e == cudaSuccess) e = set_max_shared(k_matvec<PRO_PREQ, EPI_LOGITS, 1, 1>, 227 * 1024);
@@ -2549,15 +2557,30 @@ static int argmax_static_setup(int dev, uint32_t** scratch) {
     if (e == cudaSuccess) e = set_max_shared(k_matvec<PRO_PREQ, EPI_LOGITS, 4, 1>, 227 * 1024);
     if (e == cudaSuccess) e = set_max_shared(k_matvec<PRO_PREQ, EPI_LOGITS, 8, 1>, 227 * 1024);
     if (e != cudaSuccess) {
-      st.rc = l3g_fail(L3G_E_CUDA, "static argmax scratch set-up: %s", cudaGetErrorString(e));
-      return;
+      cudaGetLastError();
+      return l3g_fail(L3G_E_CUDA, "static argmax scratch set-up on device %d: %s", dev,
+                      cudaGetErrorString(e));
     }
     st.scratch = static_cast<uint32_t*>(p);
-  });
-  if (st.rc) return l3g_fail(L3G_E_CUDA, "static argmax scratch set-up failed on device %d", dev);
+    st.ready = true;
+  }
   *scratch = st.scratch;
   return L3G_OK;
 }
+
+// Makes a device current for the scope and puts the caller's back on exit.
+struct DeviceScope {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceScope(int dev) {
+    err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
 
 extern "C" int l3g_matvec_q8_argmax_static(const l3g_matrix* w, const float* x_scales,
                                            const int8_t* x_qs, float* out,
@@ -2578,11 +2601,17 @@ extern "C" int l3g_matvec_q8_argmax_static(const l3g_matrix* w, const float* x_s
     return l3g_fail(L3G_E_INVALID,
                     "launch needs %d CTA slots, the static argmax scratch holds %d", grid,
                     kArgmaxSlots);
-  CUDA_TRY(cudaSetDevice(w->device));
+  DeviceScope dev(w->device);
+  CUDA_TRY(dev.err);
   uint32_t* scratch = nullptr;
   if (int rc = argmax_static_setup(w->device, &scratch)) return rc;
   const cudaStream_t st = (cudaStream_t)stream;
-  CUDA_TRY(cudaMemsetAsync(result, 0, sizeof(*result), st));
+  // index -1 until the merging CTA writes the result: a launch whose merge
+  // never ran (its counter disturbed by an overlapping call) stays visible
+  CUDA_TRY(cudaMemsetAsync(result, 0xff, sizeof(int32_t), st));
+  CUDA_TRY(cudaMemsetAsync(reinterpret_cast<uint8_t*>(result) + sizeof(int32_t), 0,
+                           sizeof(*result) - sizeof(int32_t), st));
+  CUDA_TRY(cudaMemsetAsync(scratch + 2 * kArgmaxSlots, 0, sizeof(uint32_t), st));
   MatvecArgs a = mv_args(w->w);
   a.xd_in = x_scales;
   a.xqs_in = x_qs;

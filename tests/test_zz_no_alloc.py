@@ -80,3 +80,65 @@ def test_static_argmax_rejects_more_ctas_than_slots(gpu_lib):
         M.matvec_argmax_static(d.data_ptr(), q.data_ptr(), 0, res.data_ptr(),
                                max_ctas=gpu_lib.ARGMAX_STATIC_MAX_CTAS + 1)
     M.Close()
+
+
+def test_static_argmax_against_reference_simd_fixture(gpu_lib):
+    """The entry's logits and argmax against the committed outputs of the
+    reference's own matvec_q8_c (tests/golden/ref_simd_matvec.npz), with
+    the recorded quantized activations."""
+    import os
+    import sys
+    import torch
+    from refspread import rel_l2
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, golden)
+    import make_golden
+    z = np.load(os.path.join(golden, "ref_simd_matvec.npz"))
+    res = torch.zeros(4, dtype=torch.int32, device="cuda")
+    for i in range(len(make_golden.MATVEC_CASES)):
+        rows, cols, seed = z[f"c{i}_shape"].tolist()
+        w = make_golden.q8_matrix(rows, cols, seed)
+        M = gpu_lib.Matrix(w, rows, cols)
+        xd = torch.from_numpy(z[f"c{i}_xd"]).cuda()
+        xq = torch.from_numpy(z[f"c{i}_xq"]).cuda()
+        ref = z[f"c{i}_out"]
+        for _ in range(2):
+            out = torch.full((rows,), 12345.0, device="cuda")
+            M.matvec_argmax_static(xd.data_ptr(), xq.data_ptr(), out.data_ptr(), res.data_ptr())
+            torch.cuda.synchronize()
+            got = out.cpu().numpy()
+            assert rel_l2(got, ref) < 1e-5, (rows, cols)
+            idx = int(res[0])
+            assert int(res[2]) == 0 and idx == int(np.argmax(got))
+            # the reference's own largest row, unless another row is within
+            # the matvec's rounding of it
+            top = float(ref.max())
+            assert idx == int(np.argmax(ref)) or ref[idx] >= top - 1e-5 * float(np.abs(ref).max())
+        M.Close()
+
+
+def test_static_argmax_keeps_callers_device(gpu_lib):
+    """With the matrix on another device, the caller's current device is
+    the same after the call as before it (needs two GPUs)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import synthetic
+    rows, cols = 300, 256
+    g = torch.Generator().manual_seed(3)
+    w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g) * 0.02, torch).numpy()
+    M = gpu_lib.Matrix(w, rows, cols, device=1)
+    with torch.cuda.device(1):
+        x = torch.from_numpy(np.random.default_rng(4).standard_normal(cols).astype(np.float32)).cuda()
+        d = torch.empty(cols // 32, dtype=torch.float32, device="cuda")
+        q = torch.empty(cols, dtype=torch.int8, device="cuda")
+        res = torch.zeros(4, dtype=torch.int32, device="cuda")
+        gpu_lib.quantize_q8_0_device(x.data_ptr(), cols, d.data_ptr(), q.data_ptr())
+        torch.cuda.synchronize()
+    torch.cuda.set_device(0)
+    M.matvec_argmax_static(d.data_ptr(), q.data_ptr(), 0, res.data_ptr())
+    assert torch.cuda.current_device() == 0
+    with torch.cuda.device(1):
+        torch.cuda.synchronize()
+    assert int(res[2].cpu()) == 0 and int(res[0].cpu()) >= 0
+    M.Close()
