@@ -170,8 +170,9 @@ def _split_args(text, open_at):
 
 
 def test_go_shim_calls_match_the_header():
-    """Every C.l3g_* call of the Go shim (the cgo code a maintainer adds)
-    names a function the header declares, with as many arguments as the
+    """Every C.l3g_* call of the Go shim (go/cuda.go, the cgo file a
+    maintainer adds as internal/llama/cuda.go) names a function the header
+    declares, with as many arguments as the
     declaration; every C.l3g_* type and C.L3G_* constant it uses exists."""
     import re
     hdr = open(os.path.join(ROOT, "include", "l3g.h")).read()
@@ -179,8 +180,7 @@ def test_go_shim_calls_match_the_header():
     for mt in re.finditer(r"\b(l3g_[a-z0-9_]+)\s*\(", hdr):
         args, _ = _split_args(hdr, mt.end() - 1)
         nparams[mt.group(1)] = 0 if args == ["void"] else len(args)
-    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    go = "\n".join(re.findall(r"```go\n(.*?)```", doc, re.S))
+    go = open(os.path.join(ROOT, "go", "cuda.go")).read()
     assert "C.l3g_forward" in go
     calls = 0
     for mt in re.finditer(r"\bC\.(l3g_[a-z0-9_]+)\s*\(", go):
