@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attf_values(const __grid_const
   }
 }
 
-__global__ void __launch_bounds__(ATTF_THREADS) k_attf_merge(const __grid_constant__ AttfArgs a) {
+static __global__ void __launch_bounds__(ATTF_THREADS) k_attf_merge(const __grid_constant__ AttfArgs a) {
   pdl_launch_dependents();
   pdl_wait();  // the splits' sums of k_attf_values
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -28,7 +28,7 @@ struct SeqInfo {
 static_assert(sizeof(SeqInfo) == 64, "SeqInfo layout");
 
 // x[b] = embedding row of seqs[b].token (infer.go:513-518).  grid (ceil(cols/256), n).
-__global__ void k_bd_embed(const uint8_t* emb, int vocab, int cols, const SeqInfo* seqs,
+static __global__ void k_bd_embed(const uint8_t* emb, int vocab, int cols, const SeqInfo* seqs,
                            float* X, Result* res) {
   const int b = blockIdx.y;
   const int token = seqs[b].token;
@@ -47,7 +47,7 @@ __global__ void k_bd_embed(const uint8_t* emb, int vocab, int cols, const SeqInf
 
 // RoPE + KV append of row b at seqs[b].pos into layer `layer` of seqs[b]'s
 // cache (as k_pf_qkv_rope, with a cache and position per row).
-__global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seqs, int layer, int nq,
+static __global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seqs, int layer, int nq,
                               int nkv, int hd, int rope_half, float* Q, int kv_f16) {
   const int rows = nq + 2 * nkv;
   const int half_rows = rows >> 1;
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
 
 // out[b][head] = sum over splits of o_s * exp(m_s - M) / sum of l_s * exp(m_s - M).
 // grid (query heads, n), HD threads.
-__global__ void k_bd_merge(const float* part_o, const float* part_ml, const SeqInfo* seqs,
+static __global__ void k_bd_merge(const float* part_o, const float* part_ml, const SeqInfo* seqs,
                            int nq_heads, int hd, int max_splits, float* out) {
   const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   if (d >= hd) return;
@@ -293,7 +293,7 @@ __global__ void k_bd_merge(const float* part_o, const float* part_ml, const SeqI
 // for sequence b sit at L[(r * n + b) * v_l + v] (the allgather layout; one
 // rank: r = 0), global id r * v_l + v; ids at or past vocab are padding.
 // Phase 1: grid (chunks of TOPK_CHUNK ids, n).
-__global__ void k_bd_topk_partial(const float* L, int n, int v_l, int vocab, int k,
+static __global__ void k_bd_topk_partial(const float* L, int n, int v_l, int vocab, int k,
                                   uint64_t* part) {
   __shared__ uint64_t keys[TOPK_CHUNK];
   const int b = blockIdx.y, nchunks = gridDim.x;
@@ -313,7 +313,7 @@ __global__ void k_bd_topk_partial(const float* L, int n, int v_l, int vocab, int
     part[((size_t)b * nchunks + blockIdx.x) * k + i] = keys[i];
 }
 // Phase 2: grid n; cap (a power of two >= count) keys of dynamic shared memory.
-__global__ void k_bd_topk_final(const uint64_t* part, int count, int cap, int k, int* ids,
+static __global__ void k_bd_topk_final(const uint64_t* part, int count, int cap, int k, int* ids,
                                 float* logits) {
   L3G_DYNAMIC_SMEM(keys3_raw);
   uint64_t* keys3 = reinterpret_cast<uint64_t*>(keys3_raw);
@@ -332,7 +332,7 @@ __global__ void k_bd_topk_final(const uint64_t* part, int count, int cap, int k,
 // softmax with 1/T over the items in order, r = uniform * sum from
 // Philox4x32-10 keyed by the sequence's seed, counted by its position, then
 // the cumulative pick.  grid n, one warp.
-__global__ void k_bd_sample(const int* ids, const float* logits, int k, const SeqInfo* seqs,
+static __global__ void k_bd_sample(const int* ids, const float* logits, int k, const SeqInfo* seqs,
                             Result* out) {
   __shared__ double e[MAX_TOPK];
   const int b = blockIdx.x, lane = threadIdx.x;

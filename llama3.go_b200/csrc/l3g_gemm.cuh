@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 }
 
 // out[n][r] = sum over k of part[k][n][r], k in order (deterministic).
-__global__ void k_gemm_reduce(const float* part, int ksplit, int n_tok, int rows, int ldo,
+static __global__ void k_gemm_reduce(const float* part, int ksplit, int n_tok, int rows, int ldo,
                               float* out) {
   const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= (long long)n_tok * rows) return;
@@ -278,7 +278,7 @@ __global__ void k_gemm_reduce(const float* part, int ksplit, int n_tok, int rows
 // block), one value per lane; tokens n_tok..n_pad-1 and the columns past
 // cols up to the chunk boundary are written as zero blocks.  Bit-identical
 // to the reference's quantization of each row.
-__global__ void k_gemm_quantize(const float* x, int n_tok, int cols, int nt, int nk,
+static __global__ void k_gemm_quantize(const float* x, int n_tok, int cols, int nt, int nk,
                                 int n_pad, uint8_t* act) {
   using namespace gemm;
   pdl_launch_dependents();

@@ -55,7 +55,7 @@ namespace l3g {
 // reference's single-process residual input (infer.go:189-191, :244-246) in
 // a sharded step: y is the full Wo / down output on every rank.
 // ---------------------------------------------------------------------------
-__global__ void k_tp_reduce(const TpExchange t, float* y, Result* res,
+static __global__ void k_tp_reduce(const TpExchange t, float* y, Result* res,
                             unsigned long long wait_ns) {
   pdl_launch_dependents();
   pdl_wait();
@@ -94,7 +94,7 @@ __global__ void k_tp_reduce(const TpExchange t, float* y, Result* res,
 // runs the persistent layer kernel, zeroes that kernel's nbar barrier,
 // abort and handshake words (bar, nullable): every earlier kernel has
 // completed by then, so an aborted step leaves no stale count behind.
-__global__ void k_embed(const uint8_t* emb, int vocab, int cols, const int* io,
+static __global__ void k_embed(const uint8_t* emb, int vocab, int cols, const int* io,
                         float* x, Result* res, unsigned* step, unsigned* bar, int nbar) {
   pdl_launch_dependents();
   pdl_wait();
@@ -148,7 +148,7 @@ __host__ __device__ inline void philox4x32_10(uint32_t c[4], uint32_t k0, uint32
   }
 }
 
-__global__ void k_sample(const int* ids, const float* logits, int k, const SampleParams* sp,
+static __global__ void k_sample(const int* ids, const float* logits, int k, const SampleParams* sp,
                          const int* io, Result* res) {
   __shared__ double e[MAX_TOPK];
   pdl_launch_dependents();
@@ -182,7 +182,7 @@ __global__ void k_sample(const int* ids, const float* logits, int k, const Sampl
 
 // End of a device-fed greedy step: record the argmax and make it the next
 // step's token at the next position (io = {token, pos, step}).
-__global__ void k_advance(int* io, const Result* res, int* tokens) {
+static __global__ void k_advance(int* io, const Result* res, int* tokens) {
   pdl_wait();
   if (threadIdx.x == 0) {
     const int t = res->token;
@@ -197,7 +197,7 @@ __global__ void k_advance(int* io, const Result* res, int* tokens) {
 // QuantizeQ8_0Into (q8_0.go:22-79): one warp per 32-value block.  In the
 // decode step it quantizes the SwiGLU output once for every CTA of the down
 // matvec (which then only copies the int8 vector), as a dependent launch.
-__global__ void k_quantize(const float* x, int n, float* d, int8_t* qs) {
+static __global__ void k_quantize(const float* x, int n, float* d, int8_t* qs) {
   pdl_launch_dependents();
   pdl_wait();
   const int lane = threadIdx.x & 31;
@@ -225,7 +225,7 @@ __device__ __forceinline__ int key_index(uint64_t k) {
   return (int)(~(uint32_t)k);
 }
 
-__device__ void bitonic_desc(uint64_t* keys, int n) {
+static __device__ void bitonic_desc(uint64_t* keys, int n) {
   for (int k = 2; k <= n; k <<= 1)
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -245,7 +245,7 @@ __device__ void bitonic_desc(uint64_t* keys, int n) {
 
 constexpr int TOPK_CHUNK = 2048;
 // Phase 1: each CTA sorts one chunk of logits and keeps its best k keys.
-__global__ void k_topk_partial(const float* logits, int n, int k, int id_offset,
+static __global__ void k_topk_partial(const float* logits, int n, int k, int id_offset,
                                uint64_t* part) {
   __shared__ uint64_t keys[TOPK_CHUNK];
   pdl_wait();
@@ -260,7 +260,7 @@ __global__ void k_topk_partial(const float* logits, int n, int k, int id_offset,
     part[(size_t)blockIdx.x * k + i] = keys[i];
 }
 // Phase 2: one CTA merges all partial keys (count <= cap, cap a power of 2).
-__global__ void k_topk_final(const uint64_t* part, int count, int cap, int k,
+static __global__ void k_topk_final(const uint64_t* part, int count, int cap, int k,
                              int* out_ids, float* out_logits) {
   L3G_DYNAMIC_SMEM(keys2_raw);
   uint64_t* keys2 = reinterpret_cast<uint64_t*>(keys2_raw);
@@ -282,7 +282,7 @@ __global__ void k_topk_final(const uint64_t* part, int count, int cap, int k,
 // Failure-detection self test: a bounded wait on an mbarrier that nothing
 // completes must give up and report ERR_TIMEOUT.
 // ---------------------------------------------------------------------------
-__global__ void k_selftest_wait(Result* res, unsigned long long timeout_ns) {
+static __global__ void k_selftest_wait(Result* res, unsigned long long timeout_ns) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {

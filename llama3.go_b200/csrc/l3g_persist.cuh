@@ -193,7 +193,7 @@ __device__ __forceinline__ bool ps_barrier(const PersistArgs& a, int idx, PSmem*
 // ---------------------------------------------------------------------------
 // producer: every tile of this CTA, in consumption order
 // ---------------------------------------------------------------------------
-__device__ void ps_produce(const PersistArgs& a, PSmem* sh, uint8_t* ring) {
+static __device__ void ps_produce(const PersistArgs& a, PSmem* sh, uint8_t* ring) {
   using namespace persist;
   const Plan& p = a.plan;
   const int b = blockIdx.x, ns = a.nstages;
@@ -257,7 +257,7 @@ __device__ void ps_produce(const PersistArgs& a, PSmem* sh, uint8_t* ring) {
 // Residual add (infer.go:189-191 / :244-246), rmsNorm (math.go:5-14), block
 // act-quant into shared memory; CTA 0 stores the new residual.  The same
 // arithmetic as k_matvec's PRO_RMS prologue.
-__device__ void ps_rms(const PersistArgs& a, const float* x_in, const float* y_in,
+static __device__ void ps_rms(const PersistArgs& a, const float* x_in, const float* y_in,
                        const float* norm_w, float* x_out, float* xd, int8_t* xqs, PSmem* sh) {
   constexpr int VKM = 8;  // float4 per thread: n_emb <= 8192
   const int C = a.n_emb, nv = C >> 2;
@@ -313,7 +313,7 @@ __device__ void ps_rms(const PersistArgs& a, const float* x_in, const float* y_i
 
 // Copy of an activation another phase quantized (the attention merge, the
 // SwiGLU quantize phase) into shared memory.
-__device__ void ps_preq(const float* d_in, const int8_t* q_in, int C, float* xd, int8_t* xqs) {
+static __device__ void ps_preq(const float* d_in, const int8_t* q_in, int C, float* xd, int8_t* xqs) {
   const int tid = threadIdx.x;
   for (int i = tid * 16; i < C; i += NW * 32 * 16)
     *reinterpret_cast<int4*>(xqs + i) = __ldcg(reinterpret_cast<const int4*>(q_in + i));
@@ -662,7 +662,7 @@ __device__ void ps_attention(const PersistArgs& a, int l, int n, uint32_t& t, ui
 // Merge of the splits of kv head kvh for output block blk (32 outputs of one
 // query head) in split order, k_attention's global merge, and its act-quant
 // for Wo.  One warp; wbuf holds align_up(splits, 32) floats of its own.
-__device__ void ps_merge_block(const PersistArgs& a, float* wbuf, int kvh, int blk, int lane) {
+static __device__ void ps_merge_block(const PersistArgs& a, float* wbuf, int kvh, int blk, int lane) {
   const int S = a.plan.splits, G = a.group, hd = a.head_dim, gh = G * hd;
   const int h = blk * 32 / hd;
   const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
@@ -705,7 +705,7 @@ __device__ void ps_merge_block(const PersistArgs& a, float* wbuf, int kvh, int b
 // Unfused, after the attention barrier, the grid's warps share every block;
 // with the fused merge, the warps of the CTA that claimed a kv head take its
 // blocks.  One call site, so the merge is inlined once into k_layers.
-__device__ void ps_merge(const PersistArgs& a, uint8_t* uni, int gb0, int gb1, int step) {
+static __device__ void ps_merge(const PersistArgs& a, uint8_t* uni, int gb0, int gb1, int step) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per = a.group * a.head_dim / 32;
   float* wbuf = reinterpret_cast<float*>(uni) + warp * align_up(a.plan.splits, 32);
@@ -721,7 +721,7 @@ __device__ void ps_merge(const PersistArgs& a, uint8_t* uni, int gb0, int gb1, i
 // or -1.  Fences as at a grid barrier: every thread's partial stores, the
 // CTA barrier, then thread 0's release fence and atomic; the claimer's fence
 // after its atomic, then the CTA barrier, before its warps read partials.
-__device__ int ps_merge_claim(const PersistArgs& a, int l, PSmem* sh) {
+static __device__ int ps_merge_claim(const PersistArgs& a, int l, PSmem* sh) {
   int kvh, split;
   if (!persist::my_item(a.plan, l, blockIdx.x, &kvh, &split)) return -1;  // uniform over the CTA
   consumer_sync();
@@ -740,7 +740,7 @@ __device__ int ps_merge_claim(const PersistArgs& a, int l, PSmem* sh) {
 }
 
 // Act-quant of the SwiGLU output (infer.go:233-234), one warp per block.
-__device__ void ps_quant(const PersistArgs& a) {
+static __device__ void ps_quant(const PersistArgs& a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = a.n_ff, nb = (n + 31) / 32;
   for (int blk = blockIdx.x * NW + warp; blk < nb; blk += gridDim.x * NW) {
@@ -751,7 +751,7 @@ __device__ void ps_quant(const PersistArgs& a) {
 
 // Tensor-parallel sum of the phase's pushed rows in rank order (k_tp_reduce
 // spread over the grid's threads).
-__device__ void ps_reduce(const PersistArgs& a, unsigned e) {
+static __device__ void ps_reduce(const PersistArgs& a, unsigned e) {
   const TpExchange& t = a.tp;
   const int i = blockIdx.x * (NW * 32) + threadIdx.x;
   if (4 * i >= t.n) return;

@@ -10,7 +10,7 @@
 
 // x[p][i] = f16(d) * q[i] of embedding row ids[p] (infer.go:513-518,
 // tensor_read.go:128-147), as k_embed.  grid (ceil(cols / 256), P).
-__global__ void k_pf_embed(const uint8_t* emb, int vocab, int cols, const int* ids, float* X,
+static __global__ void k_pf_embed(const uint8_t* emb, int vocab, int cols, const int* ids, float* X,
                            Result* res) {
   const int p = blockIdx.y;
   const int token = ids[p];
@@ -46,7 +46,7 @@ __device__ __forceinline__ void pf_store_quad(uint8_t* act, int nt, int nk, int 
 // most PF_THREADS * 4 * PF_VK.
 constexpr int PF_THREADS = 256;
 constexpr int PF_VK = 8;
-__global__ void __launch_bounds__(PF_THREADS) k_pf_rms_quant(float* X, const float* Y,
+static __global__ void __launch_bounds__(PF_THREADS) k_pf_rms_quant(float* X, const float* Y,
                                                              const float* w, float eps, int cols,
                                                              int nt, int nk, uint8_t* act) {
   __shared__ float red[PF_THREADS / 32];
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_pf_rms_quant(float* X, const flo
 // act_i = silu(gate_i) * up_i (infer.go:228-230) of the interleaved up/gate
 // rows UG[p][2i] = up_i, UG[p][2i+1] = gate_i, quantized (q8_0.go:22-79) into
 // the activation chunks for down.  One warp per (token, 32 outputs).
-__global__ void k_pf_swiglu_quant(const float* UG, int P, int ff, int nt, int nk, uint8_t* act) {
+static __global__ void k_pf_swiglu_quant(const float* UG, int P, int ff, int nt, int nk, uint8_t* act) {
   using namespace gemm;
   const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
@@ -139,7 +139,7 @@ __global__ void k_pf_swiglu_quant(const float* UG, int P, int ff, int nt, int nk
 // position pos0 + p, q to Q[p], k and v appended to this layer's cache
 // [kv heads][ctx][K hd | V hd] (infer.go:122-127), as the EPI_QKV epilogue
 // of the decode step.  One thread per adjacent pair; grid covers P * rows/2.
-__global__ void k_pf_qkv_rope(const float* QKV, int P, int pos0, int nq, int nkv, int hd,
+static __global__ void k_pf_qkv_rope(const float* QKV, int P, int pos0, int nq, int nkv, int hd,
                               int rope_half, const float* rope_cos, const float* rope_sin,
                               float* Q, void* kv, int ctx, int kv_f16) {
   const int rows = nq + 2 * nkv;
@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(256) k_pf_attention(const float* Q, const void
 // fp16 d[wr][ck/32]), so the sharded, fused and interleaved row orders of the
 // decode step carry over unchanged.  One thread per (row, block); dst must
 // be zeroed first (padding rows and blocks stay zero).
-__global__ void k_gemm_from_tiles(const Q8Tiles t, uint8_t* dst) {
+static __global__ void k_gemm_from_tiles(const Q8Tiles t, uint8_t* dst) {
   using namespace gemm;
   const int nbc = t.cols / 32;
   const int nk = chunks(t.cols);

@@ -20,7 +20,7 @@ struct RepackArgs {
   uint8_t* out;
 };
 
-__global__ void k_repack(const __grid_constant__ RepackArgs a) {
+static __global__ void k_repack(const __grid_constant__ RepackArgs a) {
   const int nbc = a.dst.cols / 32;
   const long long total = (long long)a.dst.n_groups * a.dst.wr * nbc;
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;

@@ -27,7 +27,7 @@ NW = 8
 
 
 def make_tiles(rows, cols, rpw):
-    """The decode matrices' tile plan (l3g_runtime.cu make_tiles)."""
+    """The decode matrices' tile plan (l3g_model.cu make_tiles)."""
     wr = NW * rpw
     nb = cols // 32
     nsl = max(1, -(-(cols * wr) // TILE_TARGET))
@@ -212,7 +212,7 @@ def test_causal_prefill_attention_replay(P, pos0, group, hd):
 
 
 def gemm_ksplit(n_rt, nk, n_tok, rows, nsm, part_floats):
-    """gemm_ksplit (l3g_runtime.cu), transcribed."""
+    """gemm_ksplit (l3g_batched.cu), transcribed."""
     nt = 16 if n_tok <= 16 else 32 if n_tok <= 32 else 64 if n_tok <= 64 else 128
     tiles = n_rt * (-(-n_tok // nt))
     if part_floats == 0 or tiles >= nsm:
