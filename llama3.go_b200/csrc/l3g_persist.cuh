@@ -146,8 +146,9 @@ __device__ __forceinline__ bool ps_barrier(const PersistArgs& a, int idx, PSmem*
       if (stop) {
         atomicExch(ps_abort_word(a), 1u);  // the other CTAs stop waiting for this one
       } else {
-        __threadfence();  // this CTA's writes of the phase, ordered by the CTA barrier above
-        atomicAdd(a.bar + (blockIdx.x % a.nsub) * persist::BAR_STRIDE, 1u);
+        // release: this CTA's writes of the phase, ordered before it by the
+        // CTA barrier above
+        red_release_gpu_add(a.bar + (blockIdx.x % a.nsub) * persist::BAR_STRIDE, 1u);
       }
     }
     stop = __shfl_sync(0xffffffffu, stop, 0);
@@ -174,7 +175,8 @@ __device__ __forceinline__ bool ps_barrier(const PersistArgs& a, int idx, PSmem*
           break;
         }
       }
-      __threadfence();
+      // the acquire loads above, then the CTA barrier below, order every
+      // thread's reads of the next phase after the other CTAs' writes
     }
     if (lane == 0) {
       if (stop) sh->abort_flag = 1;  // the producer stops too
@@ -389,28 +391,27 @@ __device__ __forceinline__ void ps_epilogue(const PersistArgs& a, int m, int l, 
 // adds one to the block's counter in global memory; whoever brings it to 2,
 // in this CTA or another, reads the block's 32 values back and quantizes
 // them (quant_block, as ps_quant would), then zeroes the counter for the
-// next layer.  Fences: every warp orders its act stores (its lanes' stores,
-// via __syncwarp) before its count; the counting warps fence again before
-// the next count, so the quantizing warp sees both halves.
+// next layer.  Ordering: each warp's lanes' act stores (via __syncwarp) come
+// before its CTA-scope acquire-release count; the warp that completes the
+// group thus follows every warp's stores, and its device-scope
+// acquire-release add on the block's counter publishes them all (and, for
+// the second arriver, acquires the other half's).
 __device__ __forceinline__ void ps_swiglu_quant(const PersistArgs& a, PSmem* sh, int k, int g,
                                                 int lane) {
   __syncwarp();
   int last = 0;
-  if (lane == 0) {
-    __threadfence();
-    last = atomicAdd(&sh->gcnt[k % GSLOTS], 1) == NW - 1;
-  }
+  if (lane == 0)
+    last = atom_add_acq_rel_cta_shared(reinterpret_cast<unsigned*>(&sh->gcnt[k % GSLOTS]), 1u) ==
+           (unsigned)(NW - 1);
   if (!__shfl_sync(0xffffffffu, last, 0)) return;
   const int blk = g >> 1;
   unsigned* cnt = a.bar + persist::BAR_QCNT + blk;
   int second = 0;
   if (lane == 0) {
     sh->gcnt[k % GSLOTS] = 0;  // its next use is GSLOTS groups later
-    __threadfence();
-    second = atomicAdd(cnt, 1u) == 1u;
+    second = atom_add_acq_rel_gpu(cnt, 1u) == 1u;
   }
   if (!__shfl_sync(0xffffffffu, second, 0)) return;
-  __threadfence();
   const int i = blk * 32 + lane;
   quant_block(i < a.n_ff ? __ldcg(a.act + i) : 0.0f, blk, lane, a.act_d, a.act_q);
   if (lane == 0) *cnt = 0u;
@@ -718,21 +719,18 @@ static __device__ void ps_merge(const PersistArgs& a, uint8_t* uni, int gb0, int
 // it to the split count claims that kv head -- its warps merge the head's
 // blocks (ps_merge, the same arithmetic, so results are unchanged) -- and
 // returns the counter to 0 for the next layer.  Returns the claimed kv head
-// or -1.  Fences as at a grid barrier: every thread's partial stores, the
-// CTA barrier, then thread 0's release fence and atomic; the claimer's fence
-// after its atomic, then the CTA barrier, before its warps read partials.
+// or -1.  Ordering as at a grid barrier: every thread's partial stores, the
+// CTA barrier, then thread 0's acquire-release add (release for this CTA's
+// partials, acquire for the claimer), then the CTA barrier before the
+// claimer's warps read the partials.
 static __device__ int ps_merge_claim(const PersistArgs& a, int l, PSmem* sh) {
   int kvh, split;
   if (!persist::my_item(a.plan, l, blockIdx.x, &kvh, &split)) return -1;  // uniform over the CTA
   consumer_sync();
   if (threadIdx.x == 0) {
     unsigned* cnt = a.bar + persist::BAR_QCNT + a.n_ff / 32 + kvh;
-    __threadfence();
-    const bool last = atomicAdd(cnt, 1u) == (unsigned)(a.plan.splits - 1);
-    if (last) {
-      __threadfence();
-      *cnt = 0u;
-    }
+    const bool last = atom_add_acq_rel_gpu(cnt, 1u) == (unsigned)(a.plan.splits - 1);
+    if (last) *cnt = 0u;  // read again only after the next grid barrier
     sh->merge_last = last ? 1 : 0;
   }
   consumer_sync();

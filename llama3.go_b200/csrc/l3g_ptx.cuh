@@ -72,6 +72,22 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v
   asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
+// Device-scope add with release semantics, no return value: the arrival at
+// a grid barrier (after a CTA barrier, the release covers the writes every
+// thread of the CTA made before it).
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// CTA-scope acquire-release add on a shared-memory word (a count kept by
+// the warps of one CTA); returns the old value.
+__device__ __forceinline__ unsigned atom_add_acq_rel_cta_shared(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "r"(smem_u32(p)), "r"(v)
+               : "memory");
+  return old;
+}
 // Device-scope acquire load (counters shared by the CTAs of a grid).
 __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
   unsigned v;

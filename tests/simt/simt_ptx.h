@@ -24,6 +24,8 @@ inline void pdl_launch_dependents() {}
 inline void pdl_wait() {}
 inline void touch_page(const void*) {}
 inline unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) { return atomicAdd(p, v); }
+inline void red_release_gpu_add(unsigned* p, unsigned v) { atomicAdd(p, v); }
+inline unsigned atom_add_acq_rel_cta_shared(unsigned* p, unsigned v) { return atomicAdd(p, v); }
 inline unsigned ld_acquire_gpu_u32(const unsigned* p) {
   ::simt::cur()->wait = "ld.acquire.gpu (spin)";
   ::simt::yield();

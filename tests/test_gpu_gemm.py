@@ -9,22 +9,14 @@ reference, through the C ABI.
   single-token l3g_matvec_q8 on the same inputs;
 - shapes cover ragged rows, columns that end inside a 128-column chunk, one
   token, every token tile (16 / 32 / 64 / 128) and several token tiles.
-
-Opt-in (L3G_GEMM_GPU=1) until the kernel's first controlled run on a B200:
-the file is then collected like every other GPU test.
 """
-import os
 
 import numpy as np
 import pytest
 
 from test_gemm_layout import _random_q8, act_chunks
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("L3G_GEMM_GPU") != "1",
-                       reason="batched product not yet run on a B200 (set L3G_GEMM_GPU=1)"),
-]
+pytestmark = pytest.mark.gpu
 
 SHAPES = [(200, 288, 5), (4096, 4096, 1), (4096, 4096, 16), (1024, 4096, 17),
           (4096, 4096, 64), (2048, 8192, 100), (130, 512, 40), (256, 128, 300)]
@@ -81,7 +73,7 @@ def test_gemm_matches_reference(gpu_lib, oracle_mod, rows, cols, n_tok):
 
 def test_gemm_rejects_bad_arguments(gpu_lib):
     import torch
-    w = gpu_lib.GemmMatrix(np.zeros(4 * 34, np.uint8), 4, 128, device=0)
+    w = gpu_lib.GemmMatrix(np.zeros(4 * (128 // 32) * 34, np.uint8), 4, 128, device=0)
     buf = torch.empty(1 << 16, dtype=torch.uint8, device="cuda")
     with pytest.raises(gpu_lib.L3GError):
         w.gemm(buf.data_ptr(), 0, buf.data_ptr())
