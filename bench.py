@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the matvec microbench and 1B-shape lines of the default run")
     ap.add_argument("--iters", type=int, default=1000, help="matvec microbench iterations")
     ap.add_argument("--tokens", default="16,64,128", help="gemm microbench token counts")
     ap.add_argument("--seqs", type=int, default=64, help="batched decode sessions")
@@ -210,11 +212,14 @@ def host_cores():
         return os.cpu_count() or 1
 
 
-def cpu_decode_rate(cfg, T, prefill, seconds, max_steps, seed):
+def cpu_decode_rate(cfg, T, prefill, seconds, max_steps, seed, warmup=1):
     """Greedy decode steps of the reference's chat path (ForwardTopK with
-    topK 40, argmax over the items) at position `prefill`, the KV cache of the
-    earlier positions filled with seeded values (the step's cost does not
-    depend on them).  Returns (tok/s, steps, threads)."""
+    topK 40 and its fastExp attention, argmax over the items) at position
+    `prefill`, the KV cache of the earlier positions filled with seeded
+    values (the step's cost does not depend on them).  It reads the same
+    bytes per token as the full-logits greedy path timed on the GPU (every
+    layer's weights, the whole KV prefix, the logits matrix); `warmup` steps
+    run untimed first.  Returns (tok/s, steps, threads)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import oracle
@@ -231,6 +236,9 @@ def cpu_decode_rate(cfg, T, prefill, seconds, max_steps, seed):
             arr[i:i + n] = rng.random(n, dtype=np.float32) - 0.5
     om.pos = prefill - 1
     tok = int(rng.integers(0, cfg.vocab))
+    for _ in range(max(0, warmup - 1)):
+        ids, lg = om.forward_topk(tok, 40)
+        tok = int(ids[int(np.argmax(lg))])
     t0 = time.perf_counter()
     ids, lg = om.forward_topk(tok, 40)
     first = time.perf_counter() - t0
@@ -261,12 +269,16 @@ def run_reference(args):
     T = make_host_model(cfg, args.seed, dev)
     # each step is one decoded token; at most ~90 s of timed CPU work so the
     # whole run ends within a few minutes
-    rate, n, threads = cpu_decode_rate(cfg, T, args.prefill, 90.0, max(1, args.steps), args.seed + 1)
+    rate, n, threads = cpu_decode_rate(cfg, T, args.prefill, 90.0, max(1, args.steps), args.seed + 1,
+                                       warmup=max(1, args.warmup))
     sample = (f"{n} greedy decode steps of the {cfg.name} shape at position {args.prefill} "
-              f"(KV of earlier positions seeded), ForwardTopK path, topK 40")
+              f"(KV of earlier positions seeded), after {max(1, args.warmup)} untimed steps; the "
+              f"reference's ForwardTopKIntoWorkspace path (fastExp attention, topK 40), which reads "
+              f"the same bytes per token as the greedy full-logits path the GPU arm times")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "tok/s",
-        "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": round(1000.0 / rate, 3),
+        "n_gpus": args.gpus, "steps": n, "warmup": max(1, args.warmup),
+        "ms_per_step": round(1000.0 / rate, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
         "config": {"workload": f"{cfg.name}-shape Q8_0 bs1 greedy decode after {args.prefill}-token prefill",
@@ -531,14 +543,25 @@ def run_l3g(args):
         rate, n, threads = cpu_decode_rate(cfg, T, args.prefill, args.cpu_seconds, 64, args.seed + 1)
         cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                "sample": f"{n} greedy decode steps of the {cfg.name} shape at position {args.prefill} "
-                         f"(KV of earlier positions seeded), ForwardTopK path, topK 40; C restatement "
-                         f"of infer.go + the reference's own simd.c"}
+                         f"(KV of earlier positions seeded), the reference's ForwardTopKIntoWorkspace "
+                         f"path (fastExp attention, topK 40: the same bytes per token as the greedy "
+                         f"full-logits path timed on the GPU); C restatement of infer.go + the "
+                         f"reference's own simd.c"}
     # workspace and state first: the workspace's step graphs hold NCCL calls
     # on the model's communicator
     ws.Close()
     s.Close()
     m.Close()
     D.close()
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        # the matvec microbench shapes and the 1B-shape decode, a few seconds
+        progress(world, rank, "matvec microbench and the 1B-shape decode")
+        del T
+        torch.cuda.empty_cache()
+        shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.shapes.split(",") if sh]
+        extras["matvec_microbench"] = matvec_sweep(l3g, shapes, 300, hbm, hbm_kind)
+        extras["other_workloads"] = [small_config_decode(l3g, "llama3.2-1b", 16, 128, args.seed, hbm)]
     if rank != 0:
         return 0
     line = {
@@ -574,6 +597,7 @@ def run_l3g(args):
         **({"persistent_phase_us": phases} if phases else {}),
         "clocks": clocks,
         "prefill_s": round(prefill_s, 3),
+        **extras,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
@@ -581,16 +605,14 @@ def run_l3g(args):
     return 0
 
 
-def run_matvec(args):
-    """Q8_0 matvec microbench over the 8B shapes: GB/s of weights + x + out."""
+def matvec_sweep(l3g, shapes, iters, hbm, kind):
+    """The Q8_0 matvec microbench over (rows, cols) shapes: each shape's
+    weights rotated over copies that together exceed 4 x L2, CUDA events
+    over `iters` launches; GB/s of weights + x + out against the HBM peak."""
     import torch
-    import build
-    build.build(quiet=True)
-    import l3g
     import synthetic
-    hbm, kind = peaks()
-    l2 = torch.cuda.get_device_properties(0).L2_cache_size
-    shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s]
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    rows_out = []
     for rows, cols in shapes:
         alg = rows * cols // 32 * 34 + cols + cols // 32 * 4 + rows * 4
         ncopy = max(1, -(-4 * l2 // alg))
@@ -610,19 +632,65 @@ def run_matvec(args):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record()
-        for i in range(args.iters):
+        for i in range(iters):
             mats[i % ncopy].matvec(d.data_ptr(), q.data_ptr(), out.data_ptr(), stream=st)
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / args.iters
+        ms = e0.elapsed_time(e1) / iters
         gbs = alg / ms / 1e6
-        print(json.dumps({"workload": "q8_0 matvec microbench", "shape": [rows, cols], "iters": args.iters,
-                          "copies_rotated": ncopy, "bytes_per_launch": alg, "us_per_launch": round(ms * 1e3, 3),
-                          "achieved_gbs": round(gbs, 1), "peak_gbs": hbm, "frac": round(gbs / hbm, 4),
-                          "peak_kind": kind}), flush=True)
+        rows_out.append({"shape": [rows, cols], "iters": iters, "copies_rotated": ncopy,
+                         "bytes_per_launch": alg, "us_per_launch": round(ms * 1e3, 3),
+                         "achieved_gbs": round(gbs, 1), "peak_gbs": hbm, "frac": round(gbs / hbm, 4),
+                         "peak_kind": kind})
         for mtx in mats:
             mtx.Close()
+        torch.cuda.empty_cache()
+    return rows_out
+
+
+def run_matvec(args):
+    """Q8_0 matvec microbench over the 8B shapes: GB/s of weights + x + out."""
+    import build
+    build.build(quiet=True)
+    import l3g
+    hbm, kind = peaks()
+    shapes = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",") if s]
+    for r in matvec_sweep(l3g, shapes, args.iters, hbm, kind):
+        print(json.dumps({"workload": "q8_0 matvec microbench", **r}), flush=True)
     return 0
+
+
+def small_config_decode(l3g, name, prefill, steps, seed, hbm):
+    """Greedy decode of another workload shape on this GPU (the 1B shape's
+    16 prompt tokens + 128 greedy tokens by default): tok/s of the
+    device-fed loop (CUDA events) and its decode roofline."""
+    import torch
+    import synthetic
+    cfg = synthetic.CONFIGS[name]
+    T = make_host_model(cfg, seed, "cuda")
+    torch.cuda.empty_cache()
+    m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, l3g.default_options(device=torch.cuda.current_device()))
+    del T
+    ctx = prefill + steps + 8
+    s = m.NewState(ctx)
+    ws = m.NewWorkspace(ctx, 40)
+    prompt = synthetic.prompt_ids(cfg, prefill, seed=seed)
+    m.Prefill(s, prompt[:-1], ws)
+    p0 = s.Pos
+    warm, _ = m.DecodeGreedy(s, int(prompt[-1]), 4, ws)
+    s.Pos = p0
+    toks, dev_ms = m.DecodeGreedy(s, int(prompt[-1]), steps, ws)
+    value = steps / (dev_ms / 1000.0)
+    kv = sum(cfg.kv_bytes(p0 + i + 1, 4) for i in range(steps)) / steps
+    step_bytes = cfg.weight_bytes() + kv
+    ws.Close()
+    s.Close()
+    m.Close()
+    torch.cuda.empty_cache()
+    return {"workload": f"{name}-shape Q8_0 bs1 greedy decode, {prefill} prompt + {steps} greedy tokens",
+            "tok_s": round(value, 1), "ms_per_token": round(dev_ms / steps, 4),
+            "bytes_per_token": int(step_bytes),
+            "decode_roofline_frac": round(step_bytes * value / 1e9 / hbm, 4), "kv_dtype": "f32"}
 
 
 def run_gemm(args):
