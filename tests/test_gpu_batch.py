@@ -7,19 +7,16 @@ session:
 - the logits equal the single-session l3g_forward logits on a clone of the
   state within the parity tolerance (1e-2 relative L2; both compute the
   same quantized arithmetic, the batched path with fp32 sums in another
-  order), and the K/V rows the step appends match within 1e-4;
+  order), and the K/V rows the step appends match within 1e-4 at layer 0
+  (2e-3 with the f16 cache) and within the fixed 1e-2 bar deeper, where an
+  fp32 order difference can flip an int8 activation rounding;
 - the sampled id equals SampleTopK restated on the host (tests/sampler_ref)
   over the top-K of the returned logits, with the Philox draw keyed by the
   session's seed and counted by its position;
 - the position advances by one per step.
 Covered: head dims 32 / 64 / 128, a group of 3, the f16 cache, argument
 errors.
-
-Opt-in (L3G_GEMM_GPU=1) until the batched product's first controlled run on
-a B200: the file is then collected like every other GPU test.
 """
-import os
-
 import numpy as np
 import pytest
 
@@ -27,11 +24,7 @@ from conftest import synthetic_model
 from refspread import LOGIT_TOL, rel_l2
 from sampler_ref import sample_topk
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("L3G_GEMM_GPU") != "1",
-                       reason="batched product not yet run on a B200 (set L3G_GEMM_GPU=1)"),
-]
+pytestmark = pytest.mark.gpu
 
 
 def _topk(logits, k):
@@ -77,6 +70,8 @@ def test_batch_step_matches_single_session(gpu_lib, name, lens, ctx, kv):
                 kb, vb = states[i].read_kv(layer, pos[i], 1)
                 kc, vc = clones[i].read_kv(layer, pos[i], 1)
                 tol = 2e-3 if kv else 1e-4
+                if layer > 0:
+                    tol = LOGIT_TOL
                 assert rel_l2(kb, kc) < tol and rel_l2(vb, vc) < tol, (step, i, layer)
             ids, lg = _topk(logits[i], 40)
             assert nxt[i] == sample_topk(ids, lg, 1.3, seeds[i], pos[i]), (step, i)

@@ -3,39 +3,36 @@ the reference, through the C ABI.
 
 The batched path computes the same per-token arithmetic (same activation
 quantization, exact int32 block sums) with fp32 sums in another order, so:
-- the KV cache it writes matches the token-by-token path's within 1e-4
-  relative L2 per layer;
+- the KV cache it writes for layer 0 matches the token-by-token path's
+  within 1e-4 relative L2; from layer 1 on, an fp32 summation-order
+  difference can round an activation onto the other side of an int8
+  boundary (QuantizeQ8_0Into before every matvec), and the deeper layers'
+  rows are held to the fixed 1e-2 bar instead;
 - the logits of the tokens decoded after it match the token-by-token run's
   and, within the reference's own band, the cgo reference's (the oracle with
   the reference's simd.c, teacher-forced on the same ids).
 Covered: head dims 32 / 64 / 128, a group of 3, several passes (more than
 512 tokens), a start position above zero (two batched calls in a row), and
 the f16 KV cache.
-
-Opt-in (L3G_GEMM_GPU=1) until the batched product's first controlled run on
-a B200: the file is then collected like every other GPU test.
 """
-import os
-
 import numpy as np
 import pytest
 
 from conftest import synthetic_model
-from refspread import ReferenceRuns, rel_l2
+from refspread import LOGIT_TOL, ReferenceRuns, rel_l2
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("L3G_GEMM_GPU") != "1",
-                       reason="batched product not yet run on a B200 (set L3G_GEMM_GPU=1)"),
-]
+pytestmark = pytest.mark.gpu
 
 
 def _kv_close(gpu_lib, cfg, s_a, s_b, npos, tol=1e-4):
+    """Layer 0 within tol; deeper layers (past the first int8 re-quantization
+    of the stream) within the fixed 1e-2 bar."""
     for layer in range(cfg.n_layers):
         ka, va = s_a.read_kv(layer, 0, npos)
         kb, vb = s_b.read_kv(layer, 0, npos)
-        assert rel_l2(ka, kb) < tol, (layer, rel_l2(ka, kb))
-        assert rel_l2(va, vb) < tol, (layer, rel_l2(va, vb))
+        t = tol if layer == 0 else max(tol, LOGIT_TOL)
+        assert rel_l2(ka, kb) < t, (layer, rel_l2(ka, kb))
+        assert rel_l2(va, vb) < t, (layer, rel_l2(va, vb))
 
 
 @pytest.mark.parametrize("name,n_prompt,split,ctx", [
