@@ -147,7 +147,33 @@ int l3g_model_hparams(const l3g_model *m, l3g_hparams *out);
 void l3g_model_free(l3g_model *m);
 
 /* ---- state: NewState (state.go:51-64), KV cache in HBM ------------------ */
+/* The KV cache is paged.  The reference's KVCache (state.go:3-23) is one
+ * contiguous [layer][pos][kv head][hd] block per State.  Here a page holds
+ * L3G_KV_PAGE consecutive positions (K | V rows) of one (layer, kv head),
+ * and each state has a page table from (layer, kv head, position /
+ * L3G_KV_PAGE) to pages of a pool; attention and the KV append go through
+ * that table.  l3g_state_new gives the state a private pool with every page
+ * of its context mapped at once (ctx_len rounded up to L3G_KV_PAGE). */
+#define L3G_KV_PAGE 256
 int l3g_state_new(l3g_model *m, int32_t ctx_len, l3g_state **out);
+/* A pool of n_pages pages shared by many states (a server's sessions):
+ * l3g_state_new_in_pool makes a state that takes pages from it as its
+ * position grows (before each step, for the positions the step writes) and
+ * returns them when freed; a step that finds no free page fails with
+ * L3G_E_CTX ("KV pool exhausted").  l3g_kvpool_page_bytes gives a page's
+ * size for the model, to size the pool; l3g_kvpool_free_pages counts the
+ * free ones; l3g_state_pages counts the pages a pooled state holds (0 for a
+ * private pool).  The pool must be freed after the model's workspaces and
+ * before the model; freeing it while states still hold pages defers its
+ * release to the last of them. */
+typedef struct l3g_kvpool l3g_kvpool;
+int l3g_kvpool_page_bytes(const l3g_model *m, uint64_t *bytes);
+int l3g_kvpool_new(l3g_model *m, int32_t n_pages, l3g_kvpool **out);
+void l3g_kvpool_free(l3g_kvpool *p);
+int l3g_kvpool_free_pages(l3g_kvpool *p, int32_t *n);
+int l3g_state_new_in_pool(l3g_model *m, l3g_kvpool *pool, int32_t ctx_len,
+                          l3g_state **out);
+int l3g_state_pages(const l3g_state *s, int32_t *mapped);
 int l3g_state_pos(const l3g_state *s, int32_t *pos);
 int l3g_state_ctx_len(const l3g_state *s, int32_t *ctx_len);
 /* Moves the write position (0 <= pos <= ctx): rewinds a session for reuse

@@ -29,8 +29,9 @@
 
 struct AttnArgs {
   const float* q;     // [local q heads][hd], roped
-  const void* kv;     // this layer [local kv heads][ctx][2][hd]
-  int ctx, hd, group, n_splits, P, nstages, stage_bytes;
+  KvMap kv;           // the state's KV cache (paged)
+  int layer;          // this layer's rows are read
+  int hd, group, n_splits, P, nstages, stage_bytes;
   float scale;        // float32(1/sqrt(hd)), infer.go:130
   const int* io;      // io[1] = position of this token
   float* part_o;      // [kv heads][splits][group][hd]
@@ -126,7 +127,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int chunk = align_up((n + S - 1) / S, P);
   const int t0 = min(n, split * chunk), t1 = min(n, t0 + chunk);
   const int nst = (t1 - t0 + P - 1) / P;
-  const size_t head_off = (size_t)kvh * a.ctx * 2 * hd;
   const int row = 2 * hd;  // elements per position: K then V
   // Stage groups: when a stage holds fewer than NW sub-batches, the warps
   // split into two groups of NW/2 that take alternate stages, so a warp's
@@ -166,11 +166,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           pdl_wait();
           waited = true;
         }
+        // a stage starts at a multiple of P, which divides KV_PAGE: its
+        // rows are contiguous inside one page
         const uint32_t bytes = (uint32_t)((tb - ta) * row * sizeof(KT));
-        const size_t off = (head_off + (size_t)ta * row) * sizeof(KT);
         mbar_arrive_expect_tx(&sh->full[s], bytes);
-        bulk_g2s(ring + (size_t)s * a.stage_bytes,
-                 static_cast<const uint8_t*>(a.kv) + off, bytes, &sh->full[s]);
+        bulk_g2s(ring + (size_t)s * a.stage_bytes, kv_row(a.kv, a.layer, kvh, ta), bytes,
+                 &sh->full[s]);
         *(volatile int*)&sh->issued = st + 1;
       }
       *(volatile int*)&sh->producer_done = 1;

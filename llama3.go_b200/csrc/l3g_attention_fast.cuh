@@ -26,8 +26,9 @@
 
 struct AttfArgs {
   const float* q;   // [local q heads][hd], roped
-  const void* kv;   // this layer [local kv heads][ctx][2][hd] (K | V per position)
-  int ctx, hd, group, splits;
+  KvMap kv;         // the state's KV cache (paged)
+  int layer;        // this layer's rows are read
+  int ctx, hd, group, splits;  // ctx: the scores buffer's row length
   int n_blocks;     // local q heads * hd / 32 (merge)
   float scale;      // float32(1/sqrt(hd)), infer.go:376
   const int* io;    // io[1] = position of this token
@@ -88,10 +89,9 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attf_scores(const __grid_const
   float mx[MAXG];
 #pragma unroll
   for (int h = 0; h < MAXG; ++h) mx[h] = -1e30f;  // maxScore := float32(-1e30)
-  const KT* kh = reinterpret_cast<const KT*>(a.kv) + (size_t)g * a.ctx * 2 * hd;
   for (int t = t0 + warp; t < t1; t += NW) {
     float k[DPL];
-    load_row<DPL, KT>(kh + (size_t)t * 2 * hd + lane * DPL, k);
+    load_row<DPL, KT>(reinterpret_cast<const KT*>(kv_row(a.kv, a.layer, g, t)) + lane * DPL, k);
 #pragma unroll
     for (int h = 0; h < MAXG; ++h) {
       if (h < G) {  // uniform over the warp
@@ -144,11 +144,10 @@ __global__ void __launch_bounds__(ATTF_THREADS) k_attf_values(const __grid_const
 #pragma unroll
     for (int j = 0; j < DPL; ++j) o[h][j] = 0.0f;
   }
-  const KT* vh = reinterpret_cast<const KT*>(a.kv) + (size_t)g * a.ctx * 2 * hd + hd;
   const float* sc = a.scores + (size_t)g * G * a.ctx;
   for (int t = t0 + warp; t < t1; t += NW) {
     float v[DPL];
-    load_row<DPL, KT>(vh + (size_t)t * 2 * hd + lane * DPL, v);
+    load_row<DPL, KT>(reinterpret_cast<const KT*>(kv_row(a.kv, a.layer, g, t)) + hd + lane * DPL, v);
 #pragma unroll
     for (int h = 0; h < MAXG; ++h) {
       if (h < G) {

@@ -29,6 +29,34 @@ struct Result {        // copied to the host at the end of every step
   int32_t where;       // wait site / detail
 };
 
+// The KV cache in pages.  A page holds KV_PAGE consecutive positions of one
+// (layer, local kv head): [KV_PAGE][K hd | V hd] rows of row_bytes each.  A
+// state's page table maps (layer, kv head, position / KV_PAGE) to a page of
+// a pool: entry (layer * hkv + kv head) * pps + position / KV_PAGE, pps =
+// pages per (layer, kv head) for the state's context.  A state with a pool
+// of its own maps page j of (layer, kv head) to page (layer * hkv + kv head)
+// * pps + j, which is the contiguous layout [layer][kv head][pps *
+// KV_PAGE][K | V]; a state in a shared pool takes pages as its position
+// grows.  Every bulk copy of K|V rows stays inside one page: copies start at
+// multiples of their stage size, which divides KV_PAGE.
+constexpr int KV_PAGE = 256;
+struct KvMap {
+  uint8_t* pool;      // page 0 of the pool
+  const int* pages;   // the state's page table (device)
+  int pps;            // pages per (layer, kv head)
+  int hkv;            // local kv heads
+  int row_bytes;      // 2 * head_dim * element bytes
+  int pad;
+};
+__host__ __device__ __forceinline__ size_t kv_page_byte(const KvMap& m, int page, int pos) {
+  return ((size_t)page * KV_PAGE + (pos & (KV_PAGE - 1))) * (size_t)m.row_bytes;
+}
+// The K|V row of (layer, kv head, pos): K at +0, V at + head_dim elements.
+__device__ __forceinline__ uint8_t* kv_row(const KvMap& m, int layer, int kvh, int pos) {
+  const int page = m.pages[((size_t)layer * m.hkv + kvh) * m.pps + (pos / KV_PAGE)];
+  return m.pool + kv_page_byte(m, page, pos);
+}
+
 // Dynamic shared memory of a kernel (one declaration per kernel body).  A
 // host-side build of the kernels for their CPU checks supplies its own
 // definition before including this file.

@@ -13,19 +13,30 @@
 
 // Per-sequence inputs of a step (host-filled, copied once per step).
 struct SeqInfo {
-  void* kv;                // the sequence's KV cache, all layers
+  uint8_t* kv_pool;        // the sequence's KV cache: its pool (page 0) ...
+  const int* kv_pages;     // ... and its page table
   const float* rope_cos;   // its RoPE tables [ctx][rope_half]
   const float* rope_sin;
-  long long layer_bytes;   // bytes of one layer of that cache
+  int kv_pps;              // its pages per (layer, kv head)
   int ctx;                 // its context length
   int pos;                 // position this step writes
   int token;               // token this step ingests
-  int pad;
   uint64_t seed;           // sampler seed
   float temperature;       // sampler temperature (> 0)
-  int pad2;
+  int pad;
 };
 static_assert(sizeof(SeqInfo) == 64, "SeqInfo layout");
+// The KV map of a sequence (hkv local kv heads, rows of row_bytes).
+__device__ __forceinline__ KvMap seq_kv(const SeqInfo& sq, int hkv, int row_bytes) {
+  KvMap m;
+  m.pool = sq.kv_pool;
+  m.pages = sq.kv_pages;
+  m.pps = sq.kv_pps;
+  m.hkv = hkv;
+  m.row_bytes = row_bytes;
+  m.pad = 0;
+  return m;
+}
 
 // x[b] = embedding row of seqs[b].token (infer.go:513-518).  grid (ceil(cols/256), n).
 static __global__ void k_bd_embed(const uint8_t* emb, int vocab, int cols, const SeqInfo* seqs,
@@ -78,8 +89,8 @@ static __global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seq
   } else {
     const int r2 = is_k ? row - nq : row - nq - nkv;
     const int kvh = r2 / hd, d = r2 % hd;
-    uint8_t* kvl = static_cast<uint8_t*>(sq.kv) + (size_t)layer * sq.layer_bytes;
-    const size_t off = (((size_t)kvh * sq.ctx + pos) * 2 + (is_k ? 0 : 1)) * hd + d;
+    uint8_t* kvl = kv_row(seq_kv(sq, nkv / hd, 2 * hd * (kv_f16 ? 2 : 4)), layer, kvh, pos);
+    const size_t off = (is_k ? 0 : hd) + d;
     if (kv_f16)
       *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(kvl) + off) = __floats2half2_rn(x0, x1);
     else
@@ -145,9 +156,7 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
     fence_mbar_init();
   }
   __syncthreads();
-  const KT* base = reinterpret_cast<const KT*>(static_cast<const uint8_t*>(sq.kv) +
-                                               (size_t)layer * sq.layer_bytes) +
-                   (size_t)kvh * sq.ctx * 2 * HD;
+  const KvMap kvm = seq_kv(sq, (int)gridDim.y, 2 * HD * (int)sizeof(KT));
   float q[GP][DPL], o[GP][DPL], m[GP], l[GP];  // compute warps' online softmax
   if (warp == 8) {  // producer
     if (lane == 0) {
@@ -160,7 +169,8 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
         const int np = min(BD_TILE, p1 - q0);
         const uint32_t bytes = (uint32_t)(np * 2 * HD * sizeof(KT));
         mbar_arrive_expect_tx(&sh->full[s], bytes);
-        bulk_g2s(ring + (size_t)s * SB, base + (size_t)q0 * 2 * HD, bytes, &sh->full[s]);
+        // q0 is a multiple of BD_TILE, which divides KV_PAGE: one page
+        bulk_g2s(ring + (size_t)s * SB, kv_row(kvm, layer, kvh, q0), bytes, &sh->full[s]);
         *(volatile int*)&sh->issued = t + 1;
       }
       *(volatile int*)&sh->producer_done = 1;

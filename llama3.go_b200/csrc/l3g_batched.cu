@@ -338,17 +338,17 @@ static int ensure_prefill_buffers(l3g_workspace* ws) {
 
 template <int HD>
 static cudaError_t launch_pf_attention(const l3g_model* m, const l3g_workspace* ws,
-                                       const void* kv, int P, int pos0, int ctx,
+                                       const KvMap& kv, int layer, int P, int pos0,
                                        cudaStream_t st) {
   const int bq = std::max(1, 64 / m->group);
   const dim3 grid((P + bq - 1) / bq, m->hkv_l);
   const float scale = (float)(1.0 / sqrt((double)m->hd));
   if (m->kv_f16)
     k_pf_attention<HD, __half><<<grid, 256, pf_attention_smem(HD), st>>>(
-        ws->pf_q, kv, ws->pf_att, P, pos0, ctx, m->group, bq, m->hq_l, scale);
+        ws->pf_q, kv, layer, ws->pf_att, P, pos0, m->group, bq, m->hq_l, scale);
   else
     k_pf_attention<HD, float><<<grid, 256, pf_attention_smem(HD), st>>>(
-        ws->pf_q, kv, ws->pf_att, P, pos0, ctx, m->group, bq, m->hq_l, scale);
+        ws->pf_q, kv, layer, ws->pf_att, P, pos0, m->group, bq, m->hq_l, scale);
   return cudaGetLastError();
 }
 
@@ -361,7 +361,6 @@ static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
   const cudaStream_t st = ws->stream;
   const int ne = hp.n_emb, hd = m->hd;
   const int nq = m->hq_l * hd, nkv = m->hkv_l * hd;
-  const size_t es = m->kv_f16 ? 2 : 4;
   const unsigned long long wait_ns = WAIT_TIMEOUT_NS;
   const int nt = gemm::token_tile(P);
   uint8_t* act = ws->pf_act;
@@ -370,7 +369,7 @@ static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
   CUDA_TRY(cudaGetLastError());
   for (int l = 0; l < hp.n_layers; ++l) {
     const LayerW& L = m->layers[l];
-    uint8_t* kv = static_cast<uint8_t*>(s->kv) + (size_t)l * s->layer_elems * es;
+    const KvMap kv = state_kv(s);
     // residual (from layer l-1's down) -> RMSNorm -> act-quant, infer.go:67-73
     k_pf_rms_quant<<<P, PF_THREADS, 0, st>>>(ws->pf_x, l ? ws->pf_y : nullptr, L.attn_norm,
                                             hp.rms_eps, ne, nt, gemm::chunks(ne), act);
@@ -381,15 +380,15 @@ static int enqueue_prefill_pass(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
       const long long pairs = (long long)P * ((nq + 2 * nkv) / 2);
       k_pf_qkv_rope<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(
           ws->pf_qkv, P, pos0, nq, nkv, hd, m->rope_half, s->rope_cos, s->rope_sin, ws->pf_q, kv,
-          s->ctx, m->kv_f16);
+          l, m->kv_f16);
       CUDA_TRY(cudaGetLastError());
     }
     if (l == hp.n_layers - 1) break;
     // attention, infer.go:130-175
     switch (hd) {
-      case 32: CUDA_TRY(launch_pf_attention<32>(m, ws, kv, P, pos0, s->ctx, st)); break;
-      case 64: CUDA_TRY(launch_pf_attention<64>(m, ws, kv, P, pos0, s->ctx, st)); break;
-      case 128: CUDA_TRY(launch_pf_attention<128>(m, ws, kv, P, pos0, s->ctx, st)); break;
+      case 32: CUDA_TRY(launch_pf_attention<32>(m, ws, kv, l, P, pos0, st)); break;
+      case 64: CUDA_TRY(launch_pf_attention<64>(m, ws, kv, l, P, pos0, st)); break;
+      case 128: CUDA_TRY(launch_pf_attention<128>(m, ws, kv, l, P, pos0, st)); break;
       default: return l3g_fail(L3G_E_INVALID, "batched prefill: head_dim %d", hd);
     }
     // act-quant of the attention output -> Wo, infer.go:178-187
@@ -448,6 +447,7 @@ extern "C" int l3g_prefill_batched(l3g_model* m, l3g_state* s, l3g_workspace* ws
   if (int rc = gemm_setup()) return rc;
   if (int rc = ensure_gemm_weights(m)) return rc;
   if (int rc = ensure_prefill_buffers(ws)) return rc;
+  if (int rc = state_map(s, s->pos + n, ws->stream)) return rc;
   ws->logits_valid = false;
   for (int c0 = 0; c0 < n; c0 += ws->pf_cap) {
     const int P = std::min(ws->pf_cap, n - c0);
@@ -604,10 +604,9 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
   if (top_k > MAX_TOPK) return l3g_fail(L3G_E_INVALID, "top_k %d above %d", top_k, MAX_TOPK);
   if (top_k > m->hp.vocab_size) top_k = m->hp.vocab_size;
   if (temperature <= 0.0f) temperature = 0.8f;  // sampling.go:20-22
-  const size_t es = m->kv_f16 ? 2 : 4;
   int max_pos = 0;
   for (int i = 0; i < n; ++i) {
-    const l3g_state* s = states[i];
+    l3g_state* s = states[i];
     if (!s) return l3g_fail(L3G_E_INVALID, "null state %d", i);
     if (s->m != m) return l3g_fail(L3G_E_INVALID, "state %d belongs to another model", i);
     for (int j = 0; j < i; ++j)
@@ -617,10 +616,11 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
       return l3g_fail(L3G_E_TOKEN, "token out of range: %d", tokens[i]);
     SeqInfo& q = b->h_seq[i];
     q = SeqInfo{};
-    q.kv = s->kv;
+    q.kv_pool = s->pool->base;
+    q.kv_pages = s->d_pages;
+    q.kv_pps = s->pps;
     q.rope_cos = s->rope_cos;
     q.rope_sin = s->rope_sin;
-    q.layer_bytes = (long long)(s->layer_elems * es);
     q.ctx = s->ctx;
     q.pos = s->pos;
     q.token = tokens[i];
@@ -638,6 +638,8 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
   const int n_pad = (n + nt - 1) / nt * nt;
   const int splits = (max_pos + 1 + BD_SPLIT - 1) / BD_SPLIT;
   const float scale = (float)(1.0 / sqrt((double)hd));
+  for (int i = 0; i < n; ++i)  // each session's page for this step's position
+    if (int rc = state_map(states[i], states[i]->pos + 1, st)) return rc;
   CUDA_TRY(cudaMemcpyAsync(b->d_seq, b->h_seq, (size_t)n * sizeof(SeqInfo),
                            cudaMemcpyHostToDevice, st));
   k_bd_embed<<<dim3((ne + 255) / 256, n), 256, 0, st>>>(m->emb, hp.vocab_size, ne, b->d_seq, b->x,

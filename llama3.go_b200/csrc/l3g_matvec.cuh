@@ -56,11 +56,11 @@ struct MatvecArgs {
   // epilogue
   float* out;
   // EPI_QKV: rows are [q | k | v] of this rank's heads
-  int nq, nkv, head_dim, rope_half, ctx, kv_f16;
+  int nq, nkv, head_dim, rope_half, layer, kv_f16;
   const float* rope_cos;  // [ctx][rope_half]
   const float* rope_sin;
   const int* io;          // io[0] token, io[1] position
-  void* kv;               // this layer's KV cache [kv heads][ctx][2][hd] (K|V)
+  KvMap kv;               // the state's KV cache; this layer's rows are written
   // EPI_LOGITS: fused argmax
   int row_offset;         // vocab id of local row 0
   float* am_val;          // [gridDim.x] per-CTA best
@@ -244,13 +244,13 @@ __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int n
         // KV append at this position, infer.go:122-127
         const int r2 = is_k ? row - a.nq : row - a.nq - a.nkv;
         const int kvh = r2 / hd, d = r2 % hd;
-        const size_t off = (((size_t)kvh * a.ctx + pos) * 2 + (is_k ? 0 : 1)) * hd + d;
-        void* base = a.kv;
+        const size_t off = (is_k ? 0 : hd) + d;
+        uint8_t* base = kv_row(a.kv, a.layer, kvh, pos);
         if (a.kv_f16)
-          *reinterpret_cast<__half2*>(static_cast<__half*>(base) + off) =
+          *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(base) + off) =
               __floats2half2_rn(x0, x1);
         else
-          *reinterpret_cast<float2*>(static_cast<float*>(base) + off) =
+          *reinterpret_cast<float2*>(reinterpret_cast<float*>(base) + off) =
               make_float2(x0, x1);
       }
     }

@@ -438,18 +438,147 @@ static uint64_t next_serial() {
   return ++s;
 }
 
+// ---------------------------------------------------------------------------
+// paged KV cache: pools of pages, page tables
+// ---------------------------------------------------------------------------
+static_assert(L3G_KV_PAGE == KV_PAGE, "page size of the ABI and the kernels");
+static size_t kv_row_bytes(const l3g_model* m) { return (size_t)2 * m->hd * (m->kv_f16 ? 2 : 4); }
+static size_t kv_page_bytes(const l3g_model* m) { return (size_t)KV_PAGE * kv_row_bytes(m); }
+
+static int pool_create(l3g_model* m, int n_pages, bool priv, l3g_kvpool** out) {
+  *out = nullptr;
+  if (n_pages <= 0) return l3g_fail(L3G_E_INVALID, "a KV pool needs at least one page, got %d", n_pages);
+  auto* p = new l3g_kvpool();
+  p->m = m;
+  p->device = m->device;
+  p->n_pages = n_pages;
+  p->page_bytes = kv_page_bytes(m);
+  p->priv = priv;
+  const size_t bytes = p->page_bytes * (size_t)n_pages;
+  cudaError_t e = cudaMalloc(&p->base, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p->base, 0, bytes);
+  if (e != cudaSuccess) {
+    if (p->base) cudaFree(p->base);
+    delete p;
+    cudaGetLastError();
+    return l3g_fail(L3G_E_CUDA, "KV pool of %d pages (%llu bytes): %s", n_pages,
+                    (unsigned long long)bytes, cudaGetErrorString(e));
+  }
+  if (!priv) {  // a stack: the lowest ids come out first
+    p->free_pages.resize(n_pages);
+    for (int i = 0; i < n_pages; ++i) p->free_pages[i] = n_pages - 1 - i;
+  }
+  *out = p;
+  return L3G_OK;
+}
+
+static void pool_destroy(l3g_kvpool* p) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(p->device);
+  if (p->base) cudaFree(p->base);
+  cudaSetDevice(prev);
+  delete p;
+}
+
+// A state leaves its pool: its pages go back on the free list; a released
+// (or private) pool without states is destroyed.
+static void pool_leave(l3g_kvpool* p, const std::vector<int>& pages) {
+  bool destroy = false;
+  {
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (!p->priv)
+      for (int id : pages)
+        if (id >= 0) p->free_pages.push_back(id);
+    --p->states;
+    destroy = p->priv || (p->released && p->states == 0);
+  }
+  if (destroy) pool_destroy(p);
+}
+
+KvMap state_kv(const l3g_state* s) {
+  KvMap k{};
+  k.pool = s->pool->base;
+  k.pages = s->d_pages;
+  k.pps = s->pps;
+  k.hkv = s->m->hkv_l;
+  k.row_bytes = (int)kv_row_bytes(s->m);
+  return k;
+}
+
+int state_map(l3g_state* s, int n_pos, cudaStream_t st) {
+  const int need = std::min(s->pps, (n_pos + KV_PAGE - 1) / KV_PAGE);
+  if (need <= s->mapped) return L3G_OK;
+  const int heads = s->m->hp.n_layers * s->m->hkv_l;
+  l3g_kvpool* p = s->pool;
+  {
+    std::lock_guard<std::mutex> lk(p->mu);
+    const size_t want = (size_t)heads * (need - s->mapped);
+    if (p->free_pages.size() < want)
+      return l3g_fail(L3G_E_CTX, "KV pool exhausted: %zu free pages, %zu needed for position %d",
+                      p->free_pages.size(), want, n_pos - 1);
+    for (int j = s->mapped; j < need; ++j)
+      for (int h = 0; h < heads; ++h) {
+        s->h_pages[(size_t)h * s->pps + j] = p->free_pages.back();
+        p->free_pages.pop_back();
+      }
+  }
+  // the new entries of every (layer, kv head): one 2-D copy (pageable
+  // source: staged before the call returns)
+  CUDA_TRY(cudaMemcpy2DAsync(s->d_pages + s->mapped, (size_t)s->pps * sizeof(int),
+                             s->h_pages.data() + s->mapped, (size_t)s->pps * sizeof(int),
+                             (size_t)(need - s->mapped) * sizeof(int), (size_t)heads,
+                             cudaMemcpyHostToDevice, st));
+  s->mapped = need;
+  return L3G_OK;
+}
+
+extern "C" int l3g_kvpool_page_bytes(const l3g_model* m, uint64_t* bytes) {
+  if (!m || !bytes) return l3g_fail(L3G_E_INVALID, "null argument");
+  *bytes = kv_page_bytes(m);
+  return L3G_OK;
+}
+
+extern "C" int l3g_kvpool_new(l3g_model* m, int32_t n_pages, l3g_kvpool** out) {
+  if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
+  CUDA_TRY(cudaSetDevice(m->device));
+  return pool_create(m, n_pages, false, out);
+}
+
+extern "C" void l3g_kvpool_free(l3g_kvpool* p) {
+  if (!p) return;
+  bool destroy;
+  {
+    std::lock_guard<std::mutex> lk(p->mu);
+    p->released = true;
+    destroy = p->states == 0;
+  }
+  if (destroy) pool_destroy(p);
+}
+
+extern "C" int l3g_kvpool_free_pages(l3g_kvpool* p, int32_t* n) {
+  if (!p || !n) return l3g_fail(L3G_E_INVALID, "null argument");
+  std::lock_guard<std::mutex> lk(p->mu);
+  *n = (int32_t)p->free_pages.size();
+  return L3G_OK;
+}
+
 extern "C" void l3g_state_free(l3g_state* s) {
   if (!s) return;
   cudaSetDevice(s->device);
-  if (s->kv) cudaFree(s->kv);
+  if (s->d_pages) cudaFree(s->d_pages);
   if (s->rope_cos) cudaFree(s->rope_cos);
   if (s->rope_sin) cudaFree(s->rope_sin);
+  if (s->pool) pool_leave(s->pool, s->h_pages);
   delete s;
 }
 
-extern "C" int l3g_state_new(l3g_model* m, int32_t ctx, l3g_state** out) {
+// A state over `pool` (nullptr: a private pool of exactly its pages, mapped
+// at once, page j of (layer, kv head) h at pool page h * pps + j).
+static int state_create(l3g_model* m, l3g_kvpool* pool, int32_t ctx, l3g_state** out) {
   if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
   *out = nullptr;
+  if (pool && pool->m != m) return l3g_fail(L3G_E_INVALID, "KV pool of another model");
   if (ctx <= 0) ctx = m->hp.ctx_len;  // state.go:52-57
   if (ctx > m->hp.ctx_len) ctx = m->hp.ctx_len;
   CUDA_TRY(cudaSetDevice(m->device));
@@ -458,11 +587,40 @@ extern "C" int l3g_state_new(l3g_model* m, int32_t ctx, l3g_state** out) {
   s->device = m->device;
   s->ctx = ctx;
   s->serial = next_serial();
-  s->layer_elems = (size_t)m->hkv_l * ctx * 2 * m->hd;
-  const size_t es = m->kv_f16 ? 2 : 4;
-  const size_t kvb = s->layer_elems * m->hp.n_layers * es;
-  cudaError_t e = cudaMalloc(&s->kv, kvb);
-  if (e == cudaSuccess) e = cudaMemset(s->kv, 0, kvb);
+  s->pps = (ctx + KV_PAGE - 1) / KV_PAGE;
+  const int heads = m->hp.n_layers * m->hkv_l;
+  s->h_pages.assign((size_t)heads * s->pps, -1);
+  cudaError_t e = cudaMalloc(&s->d_pages, s->h_pages.size() * sizeof(int));
+  if (e != cudaSuccess) {
+    l3g_state_free(s);
+    return l3g_fail(L3G_E_CUDA, "state allocation: %s", cudaGetErrorString(e));
+  }
+  if (pool) {
+    {
+      std::lock_guard<std::mutex> lk(pool->mu);
+      if (pool->released) {
+        l3g_state_free(s);
+        return l3g_fail(L3G_E_INVALID, "KV pool already freed");
+      }
+      ++pool->states;
+    }
+    s->pool = pool;
+    // unmapped entries point at page 0 until mapped: never read, since a
+    // step maps its position's pages before it runs
+    e = cudaMemset(s->d_pages, 0, s->h_pages.size() * sizeof(int));
+  } else {
+    l3g_kvpool* own = nullptr;
+    if (int rc = pool_create(m, heads * s->pps, true, &own)) {
+      l3g_state_free(s);
+      return rc;
+    }
+    own->states = 1;
+    s->pool = own;
+    for (size_t i = 0; i < s->h_pages.size(); ++i) s->h_pages[i] = (int)i;
+    s->mapped = s->pps;
+    e = cudaMemcpy(s->d_pages, s->h_pages.data(), s->h_pages.size() * sizeof(int),
+                   cudaMemcpyHostToDevice);
+  }
   // RoPE tables, NewRopeCache rope.go:27-34 (f64 angles, f32 tables)
   const int half = m->rope_half;
   std::vector<float> c((size_t)ctx * half), sn((size_t)ctx * half);
@@ -484,6 +642,49 @@ extern "C" int l3g_state_new(l3g_model* m, int32_t ctx, l3g_state** out) {
     return l3g_fail(L3G_E_CUDA, "state allocation: %s", cudaGetErrorString(e));
   }
   *out = s;
+  return L3G_OK;
+}
+
+extern "C" int l3g_state_new(l3g_model* m, int32_t ctx, l3g_state** out) {
+  return state_create(m, nullptr, ctx, out);
+}
+
+extern "C" int l3g_state_new_in_pool(l3g_model* m, l3g_kvpool* pool, int32_t ctx,
+                                     l3g_state** out) {
+  if (!pool) return l3g_fail(L3G_E_INVALID, "null argument");
+  return state_create(m, pool, ctx, out);
+}
+
+extern "C" int l3g_state_pages(const l3g_state* s, int32_t* mapped) {
+  if (!s || !mapped) return l3g_fail(L3G_E_INVALID, "null argument");
+  *mapped = s->pool->priv ? 0 : s->mapped * s->m->hp.n_layers * s->m->hkv_l;
+  return L3G_OK;
+}
+
+// Copies rows [pos0, pos0 + n) of (layer, kv head) between the cache and
+// host memory (to_host: cache -> host), one copy per run of pages that are
+// consecutive in the pool.
+static int copy_rows(const l3g_state* s, int layer, int kvh, int pos0, int n, uint8_t* host,
+                     bool to_host) {
+  const size_t rb = kv_row_bytes(s->m);
+  const size_t h = (size_t)layer * s->m->hkv_l + kvh;
+  const KvMap km = state_kv(s);
+  int p = pos0;
+  while (p < pos0 + n) {
+    const int page = s->h_pages[h * s->pps + p / KV_PAGE];
+    if (page < 0) return l3g_fail(L3G_E_INVALID, "position %d of the state is not mapped", p);
+    int q = std::min(pos0 + n, (p / KV_PAGE + 1) * KV_PAGE);
+    while (q < pos0 + n && s->h_pages[h * s->pps + q / KV_PAGE] ==
+                               page + (q / KV_PAGE - p / KV_PAGE))
+      q = std::min(pos0 + n, (q / KV_PAGE + 1) * KV_PAGE);
+    uint8_t* dev = s->pool->base + kv_page_byte(km, page, p);
+    uint8_t* hp = host + (size_t)(p - pos0) * rb;
+    if (to_host)
+      CUDA_TRY(cudaMemcpy(hp, dev, (size_t)(q - p) * rb, cudaMemcpyDeviceToHost));
+    else
+      CUDA_TRY(cudaMemcpy(dev, hp, (size_t)(q - p) * rb, cudaMemcpyHostToDevice));
+    p = q;
+  }
   return L3G_OK;
 }
 
@@ -551,10 +752,13 @@ extern "C" int l3g_state_snapshot(const l3g_state* s, void* dst, uint64_t bytes)
   memcpy(dst, &h, sizeof h);
   if (h.pos == 0) return L3G_OK;
   CUDA_TRY(cudaSetDevice(s->device));
-  const size_t row = (size_t)h.pos * 2 * h.hd * h.elem_bytes;     // one (layer, kv head)
-  const size_t pitch = (size_t)s->ctx * 2 * h.hd * h.elem_bytes;  // its slot in the cache
-  CUDA_TRY(cudaMemcpy2D(static_cast<uint8_t*>(dst) + sizeof h, row, s->kv, pitch, row,
-                        (size_t)h.n_layers * h.hkv_l, cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaDeviceSynchronize());  // steps in flight on any stream
+  const size_t row = (size_t)h.pos * 2 * h.hd * h.elem_bytes;  // one (layer, kv head)
+  uint8_t* out = static_cast<uint8_t*>(dst) + sizeof h;
+  for (int l = 0; l < h.n_layers; ++l)
+    for (int k = 0; k < h.hkv_l; ++k)
+      if (int rc = copy_rows(s, l, k, 0, h.pos, out + ((size_t)l * h.hkv_l + k) * row, true))
+        return rc;
   return L3G_OK;
 }
 
@@ -574,10 +778,14 @@ extern "C" int l3g_state_restore(l3g_state* s, const void* src, uint64_t bytes) 
   if (bytes < snap_bytes(h)) return l3g_fail(L3G_E_FORMAT, "snapshot truncated");
   if (h.pos > 0) {
     CUDA_TRY(cudaSetDevice(s->device));
+    if (int rc = state_map(s, h.pos, 0)) return rc;
+    CUDA_TRY(cudaDeviceSynchronize());  // the table copy and steps in flight
     const size_t row = (size_t)h.pos * 2 * h.hd * h.elem_bytes;
-    const size_t pitch = (size_t)s->ctx * 2 * h.hd * h.elem_bytes;
-    CUDA_TRY(cudaMemcpy2D(s->kv, pitch, static_cast<const uint8_t*>(src) + sizeof h, row, row,
-                          (size_t)h.n_layers * h.hkv_l, cudaMemcpyHostToDevice));
+    uint8_t* in = const_cast<uint8_t*>(static_cast<const uint8_t*>(src)) + sizeof h;
+    for (int l = 0; l < h.n_layers; ++l)
+      for (int k = 0; k < h.hkv_l; ++k)
+        if (int rc = copy_rows(s, l, k, 0, h.pos, in + ((size_t)l * h.hkv_l + k) * row, false))
+          return rc;
   }
   s->pos = h.pos;
   return L3G_OK;
@@ -589,15 +797,15 @@ extern "C" int l3g_state_read_kv(const l3g_state* s, int32_t layer, int32_t pos0
   const l3g_model* m = s->m;
   if (layer < 0 || layer >= m->hp.n_layers || pos0 < 0 || npos < 0 || pos0 + npos > s->ctx)
     return l3g_fail(L3G_E_INVALID, "kv range out of bounds");
+  if ((pos0 + npos + KV_PAGE - 1) / KV_PAGE > s->mapped)
+    return l3g_fail(L3G_E_INVALID, "kv range not mapped (positions up to %d)", s->mapped * KV_PAGE);
   CUDA_TRY(cudaSetDevice(m->device));
+  CUDA_TRY(cudaDeviceSynchronize());  // steps in flight on any stream
   const int hd = m->hd, nh = m->hkv_l;
   const size_t es = m->kv_f16 ? 2 : 4;
   std::vector<uint8_t> buf((size_t)npos * 2 * hd * es);
   for (int h = 0; h < nh; ++h) {
-    const size_t off =
-        ((size_t)layer * s->layer_elems + ((size_t)h * s->ctx + pos0) * 2 * hd) * es;
-    CUDA_TRY(cudaMemcpy(buf.data(), static_cast<uint8_t*>(s->kv) + off, buf.size(),
-                        cudaMemcpyDeviceToHost));
+    if (int rc = copy_rows(s, layer, h, pos0, npos, buf.data(), true)) return rc;
     for (int p = 0; p < npos; ++p)
       for (int d = 0; d < hd; ++d) {
         const size_t ks = (size_t)p * 2 * hd + d, vs = ks + hd;

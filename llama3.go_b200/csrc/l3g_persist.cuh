@@ -57,8 +57,7 @@ struct PersistArgs {
   const float* rope_cos;  // [ctx][rope_half]
   const float* rope_sin;
   const int* io;          // io[1] = position of this token
-  uint8_t* kv;            // layer 0 of the cache; layer l at + l * kv_layer_bytes
-  size_t kv_layer_bytes;
+  KvMap kv;               // the state's KV cache (paged)
   unsigned* bar;          // barrier counters, abort word, handshakes (persist::BAR_*), zeroed by k_embed
   int nsub;               // barrier counters in use (1 .. BAR_MAX_SUB)
   int fuse_quant;         // the SwiGLU act-quant runs in the up/gate phase (no QUANT phase)
@@ -226,7 +225,6 @@ static __device__ void ps_produce(const PersistArgs& a, PSmem* sh, uint8_t* ring
           int t0, t1;
           item_range(p, split, pos + 1, &t0, &t1);
           const int nst = item_stages(p, t0, t1);
-          const uint8_t* base = a.kv + (size_t)l * a.kv_layer_bytes;
           bool waited = false;
           for (int st = 0; st < nst && ok; ++st) {
             const int ta = t0 + st * p.P;
@@ -238,7 +236,8 @@ static __device__ void ps_produce(const PersistArgs& a, PSmem* sh, uint8_t* ring
               waited = true;
               if (!ok) break;
             }
-            ok = issue(base + stage_offset(p, kvh, t0, st), (uint32_t)((tb - ta) * p.row_bytes));
+            // ta is a multiple of P, which divides KV_PAGE: one page
+            ok = issue(kv_row(a.kv, l, kvh, ta), (uint32_t)((tb - ta) * p.row_bytes));
           }
         }
       }
@@ -371,8 +370,8 @@ __device__ __forceinline__ void ps_epilogue(const PersistArgs& a, int m, int l, 
       } else {  // KV append at this position, infer.go:122-127
         const int r2 = is_k ? row - nq : row - nq - nkv;
         const int kvh = r2 / hd, d = r2 % hd;
-        const size_t off = (((size_t)kvh * a.plan.ctx + pos) * 2 + (is_k ? 0 : 1)) * hd + d;
-        uint8_t* base = a.kv + (size_t)l * a.kv_layer_bytes;
+        const size_t off = (is_k ? 0 : hd) + d;
+        uint8_t* base = kv_row(a.kv, l, kvh, pos);
         if (a.plan.row_bytes == 4 * hd)  // f16 cache: 2 * hd elements of 2 bytes
           *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(base) + off) =
               __floats2half2_rn(x0, x1);

@@ -147,8 +147,7 @@ static PersistArgs persist_args(const l3g_workspace* ws, const l3g_state* s,
   a.rope_cos = s->rope_cos;
   a.rope_sin = s->rope_sin;
   a.io = ws->d_io;
-  a.kv = static_cast<uint8_t*>(s->kv);
-  a.kv_layer_bytes = s->layer_elems * (m->kv_f16 ? 2 : 4);
+  a.kv = state_kv(s);
   a.bar = ws->d_bar;
   a.nsub = ws->ps_nsub;
   a.fuse_quant = ws->ps_fuse ? 1 : 0;

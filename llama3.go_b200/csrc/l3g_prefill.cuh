@@ -136,12 +136,12 @@ static __global__ void k_pf_swiglu_quant(const float* UG, int P, int ff, int nt,
 }
 
 // RoPE (rope.go:39-52) on the q and k rows of QKV[p] = [q | k | v] at
-// position pos0 + p, q to Q[p], k and v appended to this layer's cache
-// [kv heads][ctx][K hd | V hd] (infer.go:122-127), as the EPI_QKV epilogue
-// of the decode step.  One thread per adjacent pair; grid covers P * rows/2.
+// position pos0 + p, q to Q[p], k and v appended to layer `layer` of the
+// paged cache (infer.go:122-127), as the EPI_QKV epilogue of the decode
+// step.  One thread per adjacent pair; grid covers P * rows/2.
 static __global__ void k_pf_qkv_rope(const float* QKV, int P, int pos0, int nq, int nkv, int hd,
                               int rope_half, const float* rope_cos, const float* rope_sin,
-                              float* Q, void* kv, int ctx, int kv_f16) {
+                              float* Q, const KvMap kv, int layer, int kv_f16) {
   const int rows = nq + 2 * nkv;
   const int half_rows = rows >> 1;
   const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -170,11 +170,12 @@ static __global__ void k_pf_qkv_rope(const float* QKV, int P, int pos0, int nq, 
   } else {
     const int r2 = is_k ? row - nq : row - nq - nkv;
     const int kvh = r2 / hd, d = r2 % hd;
-    const size_t off = (((size_t)kvh * ctx + pos) * 2 + (is_k ? 0 : 1)) * hd + d;
+    const size_t off = (is_k ? 0 : hd) + d;
+    uint8_t* base = kv_row(kv, layer, kvh, pos);
     if (kv_f16)
-      *reinterpret_cast<__half2*>(static_cast<__half*>(kv) + off) = __floats2half2_rn(x0, x1);
+      *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(base) + off) = __floats2half2_rn(x0, x1);
     else
-      *reinterpret_cast<float2*>(static_cast<float*>(kv) + off) = make_float2(x0, x1);
+      *reinterpret_cast<float2*>(reinterpret_cast<float*>(base) + off) = make_float2(x0, x1);
   }
 }
 
@@ -192,8 +193,8 @@ __host__ __device__ constexpr int pf_attention_smem(int hd) {
   return (64 * hd + hd * 33 + 32 * hd) * 4;
 }
 template <int HD, typename KT>
-__global__ void __launch_bounds__(256) k_pf_attention(const float* Q, const void* kv, float* out,
-                                                      int P, int pos0, int ctx, int group,
+__global__ void __launch_bounds__(256) k_pf_attention(const float* Q, const KvMap kv, int layer,
+                                                      float* out, int P, int pos0, int group,
                                                       int bq, int nq_heads, float scale) {
   constexpr int DPL = HD / 32;  // output dims per lane: lane + 32 j
   constexpr int RW = 8;         // rows per warp
@@ -207,7 +208,6 @@ __global__ void __launch_bounds__(256) k_pf_attention(const float* Q, const void
   const int ntok = min(bq, P - tok0);
   const int R = group * ntok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const KT* kvp = static_cast<const KT*>(kv) + (size_t)kvh * ctx * 2 * HD;
   // query rows of this block
   for (int e = threadIdx.x; e < R * HD; e += 256) {
     const int r = e / HD, d = e % HD;
@@ -226,13 +226,16 @@ __global__ void __launch_bounds__(256) k_pf_attention(const float* Q, const void
   const int last = pos0 + tok0 + ntok - 1;  // last key any row of the block sees
   for (int kb = 0; kb <= last; kb += 32) {
     __syncthreads();  // previous tile consumed (and, first time, qs written)
+    // the tile's 32 keys start at a multiple of 32, which divides KV_PAGE:
+    // they are consecutive rows of one page
+    const KT* kvp = reinterpret_cast<const KT*>(kv_row(kv, layer, kvh, kb));
     for (int e = threadIdx.x; e < 32 * HD; e += 256) {
       const int key = e / HD, d = e % HD;
       const int kp = kb + key;
       float kval = 0.0f, vval = 0.0f;
       if (kp <= last) {
-        kval = (float)kvp[(size_t)kp * 2 * HD + d];
-        vval = (float)kvp[(size_t)kp * 2 * HD + HD + d];
+        kval = (float)kvp[(size_t)key * 2 * HD + d];
+        vval = (float)kvp[(size_t)key * 2 * HD + HD + d];
       }
       kt[d][key] = kval;
       vs[key][d] = vval;

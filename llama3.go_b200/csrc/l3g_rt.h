@@ -138,16 +138,43 @@ struct l3g_model {
 // ---------------------------------------------------------------------------
 // state
 // ---------------------------------------------------------------------------
+// A pool of KV pages: one device allocation of n_pages pages, each KV_PAGE
+// K|V rows of one (layer, kv head) of its model.  States take pages as their
+// position grows and give them back when freed.  A state made by
+// l3g_state_new has a private pool holding exactly its pages (freed with
+// it); l3g_kvpool_new makes a pool several states share.
+struct l3g_kvpool {
+  l3g_model* m = nullptr;
+  int device = 0;
+  uint8_t* base = nullptr;
+  int n_pages = 0;
+  size_t page_bytes = 0;
+  std::mutex mu;
+  std::vector<int> free_pages;  // a stack of free page ids
+  int states = 0;               // states holding pages of it
+  bool released = false;        // its owner freed it: destroyed with its last state
+  bool priv = false;            // a state's private pool
+};
+
 struct l3g_state {
   l3g_model* m = nullptr;
   int device = 0;
   int ctx = 0, pos = 0;
-  void* kv = nullptr;      // [layer][local kv head][ctx][K hd | V hd]
-  size_t layer_elems = 0;  // per layer: local kv heads * ctx * 2 * hd
+  l3g_kvpool* pool = nullptr;  // where its pages live
+  int pps = 0;                 // pages per (layer, kv head): ceil(ctx / KV_PAGE)
+  int* d_pages = nullptr;      // page table [n_layers * local kv heads][pps] (device)
+  std::vector<int> h_pages;    // its host copy; -1: not mapped
+  int mapped = 0;              // logical pages [0, mapped) of every (layer, kv head) mapped
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
   uint64_t serial = 0;
 };
+// The device view of a state's cache.
+KvMap state_kv(const l3g_state* s);  // l3g_model.cu
+// Maps pages for positions [0, n_pos) of every (layer, kv head), taking
+// them from the state's pool, and copies the new table entries to the
+// device on stream st (ordered before the kernels that use them).
+int state_map(l3g_state* s, int n_pos, cudaStream_t st);  // l3g_model.cu
 
 // ---------------------------------------------------------------------------
 // workspace and the step graphs

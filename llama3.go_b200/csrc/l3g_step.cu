@@ -219,7 +219,9 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   const size_t es = m->kv_f16 ? 2 : 4;
   // attention geometry: splits fill the SMs; a stage holds the interleaved
   // K|V rows of P positions, one ~32 KB bulk copy; three stages in flight
-  ws->att_P = std::max(NW, (int)(32768 / (2 * hd * es)));
+  // (a power of two, so stages start at multiples of P that divide KV_PAGE)
+  ws->att_P = NW;
+  while (ws->att_P * 2 <= std::min(KV_PAGE, (int)(32768 / (2 * hd * es)))) ws->att_P *= 2;
   ws->att_stage = 2 * ws->att_P * hd * (int)es;
   ws->att_ns = 3;
   ws->att_gp = 1;
@@ -536,7 +538,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
   // the per-kernel step (skipped when the persistent kernel ran the layers)
   for (int l = 0; !persistent && l < hp.n_layers; ++l) {
     const LayerW& L = m->layers[l];
-    uint8_t* kv = static_cast<uint8_t*>(s->kv) + (size_t)l * s->layer_elems * es;
+    const KvMap kv = state_kv(s);
     {  // RMSNorm -> act-quant -> QKV -> RoPE -> KV append, infer.go:67-127
       MatvecArgs a = mv_args(L.qkv);
       a.wait_ns = wait_ns;
@@ -550,7 +552,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.nkv = m->hkv_l * hd;
       a.head_dim = hd;
       a.rope_half = m->rope_half;
-      a.ctx = s->ctx;
+      a.layer = l;
       a.kv_f16 = m->kv_f16;
       a.rope_cos = s->rope_cos;
       a.rope_sin = s->rope_sin;
@@ -566,7 +568,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.wait_ns = wait_ns;
       a.q = ws->q;
       a.kv = kv;
-      a.ctx = s->ctx;
+      a.layer = l;
       a.hd = hd;
       a.group = m->group;
       a.n_splits = ws->n_splits;
@@ -588,6 +590,7 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
         AttfArgs f{};
         f.q = ws->q;
         f.kv = kv;
+        f.layer = l;
         f.ctx = s->ctx;
         f.hd = hd;
         f.group = m->group;
@@ -792,6 +795,7 @@ static int run_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token
   cudaGraphExec_t exec;
   int rc = get_graph(ws, s, variant, k, &exec);
   if (rc) return rc;
+  if ((rc = state_map(s, s->pos + 1, ws->stream))) return rc;
   ws->h_io[0] = token;
   ws->h_io[1] = s->pos;
   ws->h_io[2] = 0;
@@ -875,6 +879,7 @@ extern "C" int l3g_decode_greedy(l3g_model* m, l3g_state* s, l3g_workspace* ws,
   cudaGraphExec_t exec;
   int rc = get_graph(ws, s, V_GREEDY_DEV, 0, &exec);
   if (rc) return rc;
+  if ((rc = state_map(s, s->pos + n, ws->stream))) return rc;
   cudaEvent_t e0, e1;
   CUDA_TRY(cudaEventCreate(&e0));
   CUDA_TRY(cudaEventCreate(&e1));
@@ -954,6 +959,7 @@ extern "C" int l3g_decode_sample(l3g_model* m, l3g_state* s, l3g_workspace* ws,
   cudaGraphExec_t exec;
   rc = get_graph(ws, s, V_SAMPLE_DEV, top_k, &exec);
   if (rc) return rc;
+  if ((rc = state_map(s, s->pos + n, ws->stream))) return rc;
   cudaEvent_t e0, e1;
   CUDA_TRY(cudaEventCreate(&e0));
   CUDA_TRY(cudaEventCreate(&e1));
@@ -1013,6 +1019,7 @@ extern "C" int l3g_profile_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
   if (token < 0 || token >= m->hp.vocab_size)
     return l3g_fail(L3G_E_TOKEN, "token out of range: %d", token);
   CUDA_TRY(cudaSetDevice(m->device));
+  if (int rc0 = state_map(s, s->pos + 1, ws->stream)) return rc0;
   cudaEvent_t e0;
   CUDA_TRY(cudaEventCreate(&e0));
   ws->h_io[0] = token;
@@ -1065,6 +1072,7 @@ extern "C" int l3g_trace_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int
   cudaGraphExec_t exec;
   int rc = get_graph(ws, s, V_TRACE, 0, &exec);
   if (rc) return rc;
+  if ((rc = state_map(s, s->pos + 1, ws->stream))) return rc;
   const int cnt = std::min<int>((int)ws->trace_kinds_graph.size(), kTraceCap);
   ws->h_io[0] = token;
   ws->h_io[1] = s->pos;

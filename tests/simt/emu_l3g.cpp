@@ -25,6 +25,26 @@ int guarded_call(F&& f) {
     return -1;
   }
 }
+// An identity page table over a contiguous cache [n_layers][hkv][ctx][K|V]
+// (ctx a multiple of KV_PAGE): page j of (layer, kv head) h is pool page
+// h * pps + j, as the library's private pools map them.  The table lives in
+// emulated device memory kept in `keep`.
+l3g::KvMap contiguous_kv(void* kv, int n_layers, int hkv, int ctx, int row_bytes,
+                         std::vector<void*>& keep) {
+  if (ctx % l3g::KV_PAGE) simt::fail("cache length not a multiple of KV_PAGE");
+  const int pps = ctx / l3g::KV_PAGE;
+  const size_t n = (size_t)n_layers * hkv * pps;
+  int* pages = static_cast<int*>(simt::dmalloc(n * sizeof(int)));
+  keep.push_back(pages);
+  for (size_t i = 0; i < n; ++i) pages[i] = (int)i;
+  l3g::KvMap m{};
+  m.pool = static_cast<uint8_t*>(kv);
+  m.pages = pages;
+  m.pps = pps;
+  m.hkv = hkv;
+  m.row_bytes = row_bytes;
+  return m;
+}
 }  // namespace
 
 extern "C" {
@@ -83,10 +103,12 @@ int emu_repack(const void* const* src, const int* src_row0, const int* seg_rows,
 int emu_attf(const float* q, const void* kv, int ctx, int hd, int group, int hkv, int splits,
              int kv_f16, const int* io, float* scores, float* pmax, float* psum, float* po,
              float* out, float* out_d, int8_t* out_q) {
-  return guarded_call([&] {
+  std::vector<void*> keep;
+  const int rc = guarded_call([&] {
     l3g::AttfArgs a{};
     a.q = q;
-    a.kv = kv;
+    a.kv = contiguous_kv(const_cast<void*>(kv), 1, hkv, ctx, 2 * hd * (kv_f16 ? 2 : 4), keep);
+    a.layer = 0;
     a.ctx = ctx;
     a.hd = hd;
     a.group = group;
@@ -121,6 +143,8 @@ int emu_attf(const float* q, const void* kv, int ctx, int hd, int group, int hkv
     }
     simt::launch(dim3((a.n_blocks + l3g::NW - 1) / l3g::NW), blk, 0, [&] { l3g::k_attf_merge(a); });
   });
+  for (void* p : keep) guarded_call([&] { simt::dfree(p); });
+  return rc;
 }
 
 // One decode step's layers through the persistent kernel, set up as the
@@ -166,7 +190,8 @@ void setup_rank(EmuLayers* e, int world, int rank, unsigned* step,
   const int es = e->kv_f16 ? 2 : 4;
   int rows[persist::N_MAT] = {(e->hq + 2 * e->hkv) * e->hd, e->n_emb, 2 * e->n_ff, e->n_emb};
   int cols[persist::N_MAT] = {e->n_emb, e->hq * e->hd, e->n_emb, e->n_ff};
-  const int P = std::max(NW, 32768 / (2 * e->hd * es));
+  int P = NW;  // the runtime's stage size: a power of two dividing KV_PAGE
+  while (P * 2 <= std::min(KV_PAGE, 32768 / (2 * e->hd * es))) P *= 2;
   persist::Plan p = persist::make_plan(e->grid, e->n_layers, rows, cols, e->hkv, P,
                                        2 * e->hd * es, e->ctx, NW, TILE_TARGET);
   if (e->max_splits >= 1) p.splits = std::min(p.splits, e->max_splits);
@@ -228,8 +253,7 @@ void setup_rank(EmuLayers* e, int world, int rank, unsigned* step,
   a.rope_cos = e->rope_cos;
   a.rope_sin = e->rope_sin;
   a.io = io;
-  a.kv = static_cast<uint8_t*>(e->kv);
-  a.kv_layer_bytes = (size_t)e->hkv * e->ctx * 2 * e->hd * es;
+  a.kv = contiguous_kv(e->kv, e->n_layers, e->hkv, e->ctx, 2 * e->hd * es, rr.scratch);
   a.bar = bar;
   a.nsub = std::max(1, std::min({e->nsub, (int)persist::BAR_MAX_SUB, p.grid}));
   a.fuse_quant = e->fuse_quant && p.wr[persist::M_UPGATE] == 32 &&
@@ -489,6 +513,7 @@ int emu_prefill(EmuPrefill* e) {
       }
       auto* part = static_cast<float*>(dm(std::max<size_t>(1, part_floats) * 4));
       auto* res = static_cast<Result*>(dm(sizeof(Result)));
+      const KvMap kvm = contiguous_kv(e->kv, e->n_layers, e->hkv, e->ctx, 2 * hd * es, scratch);
       auto gemm = [&](int l, int m, float* out) {
         const int ks = emu_ksplit(rows[m], cols[m], P, e->nsm, part_floats);
         run_gemm(e->layers[l].g[m], rows[m], cols[m], act, P, out, ks, part, 0, 0, res, e->nsm);
@@ -497,7 +522,7 @@ int emu_prefill(EmuPrefill* e) {
                    [&] { k_pf_embed(e->emb, e->vocab, ne, e->ids, X, res); });
       for (int l = 0; l < e->n_layers; ++l) {
         const EmuPrefillLayer& L = e->layers[l];
-        uint8_t* kv = static_cast<uint8_t*>(e->kv) + (size_t)l * e->hkv * e->ctx * 2 * hd * es;
+        const KvMap kv = kvm;
         simt::launch(dim3(P), dim3(PF_THREADS), 0, [&] {
           k_pf_rms_quant(X, l ? Y : nullptr, L.attn_norm, e->eps, ne, nt, gemm::chunks(ne), act);
         }, true);
@@ -505,7 +530,7 @@ int emu_prefill(EmuPrefill* e) {
         const long long pairs = (long long)P * ((nq + 2 * nkv) / 2);
         simt::launch(dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, [&] {
           k_pf_qkv_rope(QKV, P, e->pos0, nq, nkv, hd, e->rope_half, e->rope_cos, e->rope_sin, Q,
-                        kv, e->ctx, e->kv_f16);
+                        kv, l, e->kv_f16);
         });
         if (l == e->n_layers - 1) break;
         {
@@ -516,11 +541,11 @@ int emu_prefill(EmuPrefill* e) {
             constexpr int HD = decltype(hd_c)::value;
             if (e->kv_f16)
               simt::launch(grid, dim3(256), pf_attention_smem(HD), [&] {
-                k_pf_attention<HD, __half>(Q, kv, ATT, P, e->pos0, e->ctx, G, bq, e->hq, scale);
+                k_pf_attention<HD, __half>(Q, kv, l, ATT, P, e->pos0, G, bq, e->hq, scale);
               });
             else
               simt::launch(grid, dim3(256), pf_attention_smem(HD), [&] {
-                k_pf_attention<HD, float>(Q, kv, ATT, P, e->pos0, e->ctx, G, bq, e->hq, scale);
+                k_pf_attention<HD, float>(Q, kv, l, ATT, P, e->pos0, G, bq, e->hq, scale);
               });
           };
           switch (hd) {
@@ -770,7 +795,8 @@ int emu_attention(const float* q, const void* kv, int ctx, int hd, int group, in
     using namespace l3g;
     const int es = kv_f16 ? 2 : 4;
     AttnArgs a{};
-    a.P = std::max(NW, (int)(32768 / (2 * hd * es)));
+    a.P = NW;  // the runtime's stage size: a power of two dividing KV_PAGE
+    while (a.P * 2 <= std::min(KV_PAGE, (int)(32768 / (2 * hd * es)))) a.P *= 2;
     a.stage_bytes = 2 * a.P * hd * es;
     a.nstages = 3;
     a.n_splits = std::max(1, std::min(nsm / hkv, (ctx + a.P - 1) / a.P));
@@ -787,8 +813,8 @@ int emu_attention(const float* q, const void* kv, int ctx, int hd, int group, in
     };
     a.wait_ns = WAIT_TIMEOUT_NS;
     a.q = q;
-    a.kv = kv;
-    a.ctx = ctx;
+    a.kv = contiguous_kv(const_cast<void*>(kv), 1, hkv, ctx, 2 * hd * es, sc);
+    a.layer = 0;
     a.hd = hd;
     a.group = group;
     a.scale = (float)(1.0 / sqrt((double)hd));

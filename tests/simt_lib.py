@@ -137,6 +137,15 @@ def repack(segments, cols_total, rows, blk0=0, cols=None, interleave2=False, rpw
     return out
 
 
+KV_PAGE = 256  # positions per page of the library's KV cache (L3G_KV_PAGE)
+
+
+def kv_len(ctx):
+    """Positions per (layer, kv head) of a contiguous cache the kernels can
+    reach through an identity page table: ctx rounded up to KV_PAGE."""
+    return -(-ctx // KV_PAGE) * KV_PAGE
+
+
 def rope_tables(cfg, ctx):
     """cos / sin [ctx][head_dim / 2] as the library builds them: inverse
     frequencies 1 / base^(2i / rope_dim) in f64 (rope.go:20-25), divided by
@@ -208,7 +217,8 @@ class PersistentModel:
         cos, sin = rope_tables(cfg, ctx)
         self.cos, self.sin = Dev(cos), Dev(sin)
         self.es = 2 if kv_f16 else 4
-        self.kv = Dev(cfg.n_layers * self.hkv * ctx * 2 * hd * self.es)
+        self.kctx = kv_len(ctx)
+        self.kv = Dev(cfg.n_layers * self.hkv * self.kctx * 2 * hd * self.es)
         self.xa, self.xb, self.y = Dev(e * 4), Dev(e * 4), Dev(e * 4)
         self.attn, self.act = Dev(self.hq * hd * 4), Dev(nf * 4)
         self._keep += [self.cos, self.sin, self.kv, self.xa, self.xb, self.y, self.attn, self.act]
@@ -220,7 +230,7 @@ class PersistentModel:
         hkv, hd, h0 = cfg.n_heads_kv, cfg.head_dim, self.kv_head0
         K = K.reshape(cfg.n_layers, self.ctx, hkv, hd)[:, :, h0:h0 + self.hkv]
         V = V.reshape(cfg.n_layers, self.ctx, hkv, hd)[:, :, h0:h0 + self.hkv]
-        ours = np.zeros((cfg.n_layers, self.hkv, self.ctx, 2, hd), np.float32)
+        ours = np.zeros((cfg.n_layers, self.hkv, self.kctx, 2, hd), np.float32)
         ours[:, :, :npos, 0] = K[:, :npos].transpose(0, 2, 1, 3)
         ours[:, :, :npos, 1] = V[:, :npos].transpose(0, 2, 1, 3)
         self.kv.write(ours.astype(np.float16) if self.kv_f16 else ours)
@@ -229,14 +239,14 @@ class PersistentModel:
         """[layer][local kv head][ctx][2][hd] as f32."""
         cfg = self.cfg
         a = self.kv.read(np.float16 if self.kv_f16 else np.float32).astype(np.float32)
-        return a.reshape(cfg.n_layers, self.hkv, self.ctx, 2, cfg.head_dim)
+        return a.reshape(cfg.n_layers, self.hkv, self.kctx, 2, cfg.head_dim)[:, :, :self.ctx]
 
     def record(self, token, pos, step_count=1, **kw):
         cfg = self.cfg
         self.xa.write(embed_row(cfg, self.T, int(token)))
         return EmuLayers(grid=self.grid, n_layers=cfg.n_layers, n_emb=cfg.n_emb, n_ff=self.ff,
                          hq=self.hq, hkv=self.hkv, hd=cfg.head_dim, rope_half=cfg.head_dim // 2,
-                         ctx=self.ctx, kv_f16=1 if self.kv_f16 else 0, eps=cfg.rms_eps, w=self.W,
+                         ctx=self.kctx, kv_f16=1 if self.kv_f16 else 0, eps=cfg.rms_eps, w=self.W,
                          norm=self.N, xa=self.xa.ptr, xb=self.xb.ptr, y=self.y.ptr,
                          attn=self.attn.ptr, act=self.act.ptr, kv=self.kv.ptr,
                          rope_cos=self.cos.ptr, rope_sin=self.sin.ptr, token=int(token),
@@ -325,7 +335,8 @@ class PrefillModel:
         self.emb = Dev(T["token_embd.weight"][2])
         cos, sin = rope_tables(cfg, ctx)
         self.cos, self.sin = Dev(cos), Dev(sin)
-        self.kv = Dev(cfg.n_layers * hkv * ctx * 2 * hd * (2 if kv_f16 else 4))
+        self.kctx = kv_len(ctx)
+        self.kv = Dev(cfg.n_layers * hkv * self.kctx * 2 * hd * (2 if kv_f16 else 4))
         self._keep += [self.emb, self.cos, self.sin, self.kv]
 
     def prefill(self, ids, pos0, nsm=148):
@@ -333,7 +344,7 @@ class PrefillModel:
         d_ids = Dev(np.ascontiguousarray(ids, dtype=np.int32))
         a = EmuPrefill(n_layers=cfg.n_layers, n_emb=cfg.n_emb, n_ff=cfg.n_ff, hq=cfg.n_heads,
                        hkv=cfg.n_heads_kv, hd=cfg.head_dim, rope_half=cfg.head_dim // 2,
-                       ctx=self.ctx, kv_f16=1 if self.kv_f16 else 0, vocab=cfg.vocab,
+                       ctx=self.kctx, kv_f16=1 if self.kv_f16 else 0, vocab=cfg.vocab,
                        eps=cfg.rms_eps, layers=self.layers, emb=self.emb.ptr, kv=self.kv.ptr,
                        rope_cos=self.cos.ptr, rope_sin=self.sin.ptr, ids=d_ids.ptr, P=len(ids),
                        pos0=pos0, nsm=nsm)
@@ -346,7 +357,7 @@ class PrefillModel:
     def read_kv(self):
         cfg = self.cfg
         a = self.kv.read(np.float16 if self.kv_f16 else np.float32).astype(np.float32)
-        return a.reshape(cfg.n_layers, cfg.n_heads_kv, self.ctx, 2, cfg.head_dim)
+        return a.reshape(cfg.n_layers, cfg.n_heads_kv, self.kctx, 2, cfg.head_dim)[:, :, :self.ctx]
 
     def close(self):
         for d in self._keep:
@@ -355,9 +366,9 @@ class PrefillModel:
 
 
 class SeqInfo(C.Structure):
-    _fields_ = [("kv", _P), ("rope_cos", _P), ("rope_sin", _P), ("layer_bytes", C.c_longlong),
-                ("ctx", C.c_int), ("pos", C.c_int), ("token", C.c_int), ("pad", C.c_int),
-                ("seed", C.c_uint64), ("temperature", C.c_float), ("pad2", C.c_int)]
+    _fields_ = [("kv_pool", _P), ("kv_pages", _P), ("rope_cos", _P), ("rope_sin", _P),
+                ("kv_pps", C.c_int), ("ctx", C.c_int), ("pos", C.c_int), ("token", C.c_int),
+                ("seed", C.c_uint64), ("temperature", C.c_float), ("pad", C.c_int)]
 
 
 class Result(C.Structure):
@@ -388,22 +399,24 @@ class BatchModel(PrefillModel):
         tiles.free()
         raw.free()
         self.out_norm = Dev(T["output_norm.weight"][2])
-        self._keep += [self.glogits, self.out_norm]
+        # every session's cache is contiguous: one identity page table serves all
+        self.pages = Dev(np.arange(cfg.n_layers * cfg.n_heads_kv * (self.kctx // KV_PAGE),
+                                   dtype=np.int32))
+        self._keep += [self.glogits, self.out_norm, self.pages]
 
     def new_cache(self):
         cfg = self.cfg
-        d = Dev(cfg.n_layers * cfg.n_heads_kv * self.ctx * 2 * cfg.head_dim * (2 if self.kv_f16 else 4))
+        d = Dev(cfg.n_layers * cfg.n_heads_kv * self.kctx * 2 * cfg.head_dim * (2 if self.kv_f16 else 4))
         self._keep.append(d)
         return d
 
     def step(self, caches, positions, tokens, seeds, top_k=40, temperature=0.8, nsm=148):
         cfg = self.cfg
         n = len(caches)
-        es = 2 if self.kv_f16 else 4
-        seqs = (SeqInfo * n)(*[SeqInfo(kv=c.ptr, rope_cos=self.cos.ptr, rope_sin=self.sin.ptr,
-                                       layer_bytes=cfg.n_heads_kv * self.ctx * 2 * cfg.head_dim * es,
-                                       ctx=self.ctx, pos=int(p), token=int(t), seed=int(s),
-                                       temperature=temperature)
+        seqs = (SeqInfo * n)(*[SeqInfo(kv_pool=c.ptr, kv_pages=self.pages.ptr,
+                                       kv_pps=self.kctx // KV_PAGE, rope_cos=self.cos.ptr,
+                                       rope_sin=self.sin.ptr, ctx=self.ctx, pos=int(p),
+                                       token=int(t), seed=int(s), temperature=temperature)
                                for c, p, t, s in zip(caches, positions, tokens, seeds)])
         d_seqs = Dev(np.frombuffer(bytes(seqs), np.uint8))
         logits = Dev(n * cfg.vocab * 4)
@@ -429,7 +442,7 @@ def load_session_kv(dev, cfg, ctx, K, V, npos, f16=False):
     hkv, hd = cfg.n_heads_kv, cfg.head_dim
     K = K.reshape(cfg.n_layers, ctx, hkv, hd)
     V = V.reshape(cfg.n_layers, ctx, hkv, hd)
-    ours = np.zeros((cfg.n_layers, hkv, ctx, 2, hd), np.float32)
+    ours = np.zeros((cfg.n_layers, hkv, kv_len(ctx), 2, hd), np.float32)
     ours[:, :, :npos, 0] = K[:, :npos].transpose(0, 2, 1, 3)
     ours[:, :, :npos, 1] = V[:, :npos].transpose(0, 2, 1, 3)
     dev.write(ours.astype(np.float16) if f16 else ours)

@@ -169,7 +169,7 @@ def test_persistent_step_abort_when_a_cta_never_arrives(S):
 def test_fast_exp_attention_kernels(S, G, hd, hkv, n, splits, f16):
     from test_topk_fast_attention import fast_exp_kernel, reference_head
     rng = np.random.default_rng(G * 1000 + n)
-    ctx = n + 4
+    ctx = S.kv_len(n + 4)  # a whole number of KV pages
     q = rng.standard_normal((hkv * G, hd)).astype(np.float32)
     kv = rng.standard_normal((hkv, ctx, 2, hd)).astype(np.float32)
     if f16:
@@ -504,7 +504,7 @@ def test_decode_attention_matches_exact_softmax(S, G, hd, hkv, n, f16):
     in float64, and its act-quant for Wo bit for bit."""
     import oracle
     rng = np.random.default_rng(G * 100 + n)
-    ctx = n + 5
+    ctx = S.kv_len(n + 5)  # a whole number of KV pages
     q = rng.standard_normal((hkv * G, hd)).astype(np.float32)
     kv = rng.standard_normal((hkv, ctx, 2, hd)).astype(np.float32)
     if f16:
