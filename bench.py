@@ -808,10 +808,15 @@ def run_batched(args):
     seeds = rng.integers(1, 2**62, args.seqs).astype(np.uint64)
     ws = m.NewWorkspace(int(lens.max()) + args.warmup + args.steps + 1, 40)
     states = []
+    # every session's KV pages come from one shared pool sized for the run
+    # (pages of KV_PAGE positions per layer and local kv head)
+    heads = cfg.n_layers * (cfg.n_heads_kv // world)
+    need = [-(-(int(L) + args.warmup + args.steps + 1) // l3g.KV_PAGE) for L in lens]
+    pool = m.NewKvPool(heads * sum(need))
     progress(world, rank, "batched prefill of the sessions")
     t0 = time.perf_counter()
     for i, L in enumerate(lens):
-        s = m.NewState(int(L) + args.warmup + args.steps + 1)
+        s = m.NewStateInPool(pool, int(L) + args.warmup + args.steps + 1)
         m.PrefillBatched(s, synthetic.prompt_ids(cfg, int(L), seed=args.seed + 1 + i), ws)
         states.append(s)
     prefill_s = time.perf_counter() - t0
@@ -834,9 +839,12 @@ def run_batched(args):
     kv_step = sum(cfg.kv_bytes(int(p) + i + 1, es) for p in pos0 for i in range(args.steps)) / args.steps
     step_bytes = cfg.weight_bytes() + kv_step
     gbs = step_bytes * args.steps / wall / 1e9
+    kv_pool = {"pages": heads * sum(need), "page_bytes": m.KvPageBytes(),
+               "pages_held": int(sum(s.Pages for s in states)), "page_positions": l3g.KV_PAGE}
     batch.Close()
     for s in states:
         s.Close()
+    pool.Close()
     ws.Close()
     m.Close()
     D.close()
@@ -855,7 +863,8 @@ def run_batched(args):
                                    "kv_bytes_per_step": int(kv_step), "achieved_gbs": round(gbs, 1),
                                    "peak_gbs_aggregate": hbm * world,
                                    "frac": round(gbs / (hbm * world), 4), "peak_kind": hbm_kind},
-                      "prefill_s": round(prefill_s, 2), "clocks": clocks}), flush=True)
+                      "kv_pool": kv_pool, "prefill_s": round(prefill_s, 2), "clocks": clocks}),
+          flush=True)
     return 0
 
 

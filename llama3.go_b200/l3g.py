@@ -95,6 +95,12 @@ def lib():
         "l3g_model_hparams": (C.c_int, [_P, C.POINTER(HyperParams)]),
         "l3g_model_free": (None, [_P]),
         "l3g_state_new": (C.c_int, [_P, C.c_int32, C.POINTER(_P)]),
+        "l3g_kvpool_page_bytes": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
+        "l3g_kvpool_new": (C.c_int, [_P, C.c_int32, C.POINTER(_P)]),
+        "l3g_kvpool_free": (None, [_P]),
+        "l3g_kvpool_free_pages": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+        "l3g_state_new_in_pool": (C.c_int, [_P, _P, C.c_int32, C.POINTER(_P)]),
+        "l3g_state_pages": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_state_pos": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_state_ctx_len": (C.c_int, [_P, C.POINTER(C.c_int32)]),
         "l3g_state_set_pos": (C.c_int, [_P, C.c_int32]),
@@ -201,6 +207,9 @@ def nccl_unique_id() -> bytes:
     return bytes(buf)
 
 
+KV_PAGE = 256  # positions per KV page (L3G_KV_PAGE)
+
+
 class Model:
     """Model (model.go:37-53): weights resident in HBM."""
 
@@ -229,6 +238,24 @@ class Model:
     def NewState(self, ctx_len: int = 0) -> "State":
         h = C.c_void_p()
         _check(lib().l3g_state_new(self._h, ctx_len, C.byref(h)))
+        return State(self, h)
+
+    def NewKvPool(self, n_pages: int) -> "KvPool":
+        """A pool of n_pages KV pages (KV_PAGE positions of one layer and kv
+        head each) that states made with NewState(pool=...) share."""
+        h = C.c_void_p()
+        _check(lib().l3g_kvpool_new(self._h, int(n_pages), C.byref(h)))
+        return KvPool(self, h)
+
+    def KvPageBytes(self) -> int:
+        v = C.c_uint64()
+        _check(lib().l3g_kvpool_page_bytes(self._h, C.byref(v)))
+        return v.value
+
+    def NewStateInPool(self, pool: "KvPool", ctx_len: int = 0) -> "State":
+        """A state whose KV pages come from `pool` as its position grows."""
+        h = C.c_void_p()
+        _check(lib().l3g_state_new_in_pool(self._h, pool._h, ctx_len, C.byref(h)))
         return State(self, h)
 
     def NewWorkspace(self, ctx_len: int = 0, topK: int = 0) -> "Workspace":
@@ -405,9 +432,41 @@ class State:
         snap = np.ascontiguousarray(snap, dtype=np.uint8)
         _check(lib().l3g_state_restore(self._h, snap.ctypes.data, snap.size))
 
+    @property
+    def Pages(self) -> int:
+        """KV pages this state holds from a shared pool (0: a private pool)."""
+        v = C.c_int32()
+        _check(lib().l3g_state_pages(self._h, C.byref(v)))
+        return v.value
+
     def Close(self):
         if self._h:
             lib().l3g_state_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.Close()
+        except Exception:
+            pass
+
+
+class KvPool:
+    """Pages of KV cache shared by the states of one model (l3g_kvpool)."""
+
+    def __init__(self, model: Model, h):
+        self.model = model
+        self._h = h
+
+    @property
+    def FreePages(self) -> int:
+        v = C.c_int32()
+        _check(lib().l3g_kvpool_free_pages(self._h, C.byref(v)))
+        return v.value
+
+    def Close(self):
+        if self._h:
+            lib().l3g_kvpool_free(self._h)
             self._h = C.c_void_p()
 
     def __del__(self):

@@ -117,6 +117,19 @@ int main(int argc, char **argv) {
   CHECK(l3g_model_load(NULL, NULL, 0, &opt, &m) == L3G_E_INVALID);
   CHECK(l3g_forward(NULL, NULL, NULL, 0, NULL) == L3G_E_INVALID);
   CHECK(l3g_state_new(NULL, 16, NULL) == L3G_E_INVALID);
+  {
+    l3g_kvpool *pool = NULL;
+    l3g_state *ps = NULL;
+    int32_t n = 0;
+    uint64_t pb = 0;
+    CHECK(l3g_kvpool_new(NULL, 4, &pool) == L3G_E_INVALID && pool == NULL);
+    CHECK(l3g_kvpool_page_bytes(NULL, &pb) == L3G_E_INVALID);
+    CHECK(l3g_kvpool_free_pages(NULL, &n) == L3G_E_INVALID);
+    CHECK(l3g_state_new_in_pool(NULL, NULL, 16, &ps) == L3G_E_INVALID);
+    CHECK(l3g_state_pages(NULL, &n) == L3G_E_INVALID);
+    CHECK(L3G_KV_PAGE == 256);
+    l3g_kvpool_free(NULL);
+  }
   CHECK(l3g_workspace_set_topk_fast_exp(NULL, 1) == L3G_E_INVALID);
   l3g_model_free(NULL);
   l3g_state_free(NULL);
