@@ -26,6 +26,8 @@ def _rank_main(rank, world, id_path, out_dir, path):
         sys.path.insert(0, os.path.join(root, sub))
     if path == "nccl":
         os.environ["L3G_TP_NCCL"] = "1"
+    if path == "persistent":
+        os.environ["L3G_PERSIST"] = "1"
     import l3g
     import synthetic
     from conftest import synthetic_model as sm
@@ -46,8 +48,10 @@ def _rank_main(rank, world, id_path, out_dir, path):
     m = l3g.LoadModelFromTensors(l3g.hparams_for(cfg), T, opts)
     s = m.NewState(CTX)
     ws = m.NewWorkspace(CTX, 40)
-    if ws.tp_p2p() != (path == "p2p"):
+    if ws.tp_p2p() != (path != "nccl"):
         raise RuntimeError(f"workspace reduction path is not {path}")
+    if ws.persistent() != (path == "persistent"):
+        raise RuntimeError("persistent layer kernel not as requested")
     ids = synthetic.prompt_ids(cfg, N_TOK, seed=17)
     logits = np.empty(cfg.vocab, np.float32)
     out = []
@@ -141,10 +145,12 @@ def test_tp2_ranks_as_threads_of_one_process(gpu_lib, oracle_mod, tmp_path):
     assert max(errs) < R.tol(), (errs, R.band())
 
 
-@pytest.mark.parametrize("path", ["p2p", "nccl"])
+@pytest.mark.parametrize("path", ["p2p", "nccl", "persistent"])
 def test_tp2_matches_reference_and_single_gpu(gpu_lib, oracle_mod, tmp_path, path):
     """Both reductions: partial sums pushed over peer memory by the Wo / down
-    matvecs and summed by the next kernel (p2p), and NCCL allreduces."""
+    matvecs and summed by the next kernel (p2p), and NCCL allreduces; and the
+    persistent layer kernel, whose Wo / down phases push over peer memory
+    and whose reduce phase sums the ranks' rows inside the same launch."""
     import torch
     import torch.multiprocessing as mp
     import synthetic
