@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--config", default="llama3.1-8b")
     ap.add_argument("--prefill", type=int, default=4096)
     ap.add_argument("--kv", default="f32", choices=["f32", "f16"])
+    ap.add_argument("--prefill-mode", default="batched", choices=["batched", "token"],
+                    help="how the decode workload's prompt is ingested (not timed in value)")
     ap.add_argument("--persistent", action="store_true",
                     help="decode with the persistent layer kernel (every layer in one launch)")
     ap.add_argument("--seed", type=int, default=0)
@@ -467,7 +469,10 @@ def run_l3g(args):
     prompt = synthetic.prompt_ids(cfg, args.prefill, seed=args.seed)
     progress(world, rank, "prefill")
     t0 = time.perf_counter()
-    m.Prefill(s, prompt[:-1], ws)
+    if args.prefill_mode == "batched":  # the tensor-core product, 512 tokens per pass
+        m.PrefillBatched(s, prompt[:-1], ws)
+    else:  # token by token, like the reference's ingest (main.go:276-286)
+        m.Prefill(s, prompt[:-1], ws)
     prefill_s = time.perf_counter() - t0
     p0 = s.Pos
 
@@ -597,6 +602,7 @@ def run_l3g(args):
         **({"persistent_phase_us": phases} if phases else {}),
         "clocks": clocks,
         "prefill_s": round(prefill_s, 3),
+        "prefill_mode": args.prefill_mode,
         **extras,
     }
     if cpu is not None:

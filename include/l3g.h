@@ -453,7 +453,9 @@ int l3g_batch_step(l3g_batch *b, l3g_state *const *states, int32_t n,
  *    product's activation buffer act (DEVICE, l3g_gemm_act_bytes bytes,
  *    16-byte aligned), bit-identical to QuantizeQ8_0Into per row.
  *  - l3g_gemm_q8 writes out [n_tok][rows] (DEVICE f32); asynchronous on
- *    stream.  l3g_gemm_status synchronizes the device and returns (and
+ *    stream.  A matrix with fewer 128-row tiles than SMs splits its K range
+ *    over CTAs into scratch the matrix owns (sized for 128 tokens), so
+ *    products over one matrix must not overlap in time (one stream).  l3g_gemm_status synchronizes the device and returns (and
  *    clears) the error word of the kernel's bounded waits: err 0, or 1 with
  *    `where` naming the wait that gave up. */
 int l3g_gemm_matrix_bytes(int32_t rows, int32_t cols, uint64_t *bytes);

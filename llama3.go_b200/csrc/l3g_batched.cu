@@ -72,6 +72,8 @@ struct l3g_gemm_matrix {
   GemmMat w;                // weight chunks, gemm::A_CHUNK bytes each
   int device = 0, nsm = 1;
   Result* d_res = nullptr;  // device error word of the kernel's bounded waits
+  float* part = nullptr;    // split-K partial sums for up to 128 tokens
+  size_t part_floats = 0;
 };
 
 // Kernel attributes of the batched product, once per device (kept apart from
@@ -179,6 +181,7 @@ extern "C" void l3g_gemm_matrix_free(l3g_gemm_matrix* w) {
   cudaSetDevice(w->device);
   free_gemm(w->w);
   if (w->d_res) cudaFree(w->d_res);
+  if (w->part) cudaFree(w->part);
   delete w;
 }
 
@@ -206,6 +209,9 @@ extern "C" int l3g_gemm_matrix_upload(const void* q8, int32_t rows, int32_t cols
   if (e == cudaSuccess) e = cudaMemcpy(w->w.data, host.data(), bytes, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMalloc(&w->d_res, sizeof(Result));
   if (e == cudaSuccess) e = cudaMemset(w->d_res, 0, sizeof(Result));
+  // a matrix with fewer row tiles than SMs splits K over CTAs
+  w->part_floats = gemm_part_bound(w->w, 128, w->nsm);
+  if (e == cudaSuccess && w->part_floats) e = cudaMalloc(&w->part, w->part_floats * sizeof(float));
   if (e != cudaSuccess) {
     l3g_gemm_matrix_free(w);
     return l3g_fail(L3G_E_CUDA, "gemm matrix upload: %s", cudaGetErrorString(e));
@@ -252,7 +258,8 @@ extern "C" int l3g_gemm_q8(const l3g_gemm_matrix* w, const void* act, int32_t n_
   CUDA_TRY(cudaSetDevice(w->device));
   if (int rc = gemm_setup()) return rc;
   CUDA_TRY(launch_gemm(w->w, static_cast<const uint8_t*>(act), n_tok, out, w->d_res,
-                       WAIT_TIMEOUT_NS, w->nsm, (cudaStream_t)stream));
+                       WAIT_TIMEOUT_NS, w->nsm, (cudaStream_t)stream, 0, w->part,
+                       w->part_floats));
   return L3G_OK;
 }
 

@@ -21,14 +21,19 @@ struct GemmArgs {
   unsigned long long wait_ns;
 };
 
-constexpr int GEMM_EPI_WARPS = 8;                      // two warpgroups
+// Four warpgroups rescale: each TMEM lane quarter (weight rows 32q..) is
+// read by four warps, one per quarter of the token tile's columns, so every
+// scheduler has four rescale warps to hide the tensor-memory and
+// shared-memory latencies of the per-block rescale.
+constexpr int GEMM_EPI_WARPS = 16;
+constexpr int GEMM_COL_GROUPS = GEMM_EPI_WARPS / 4;
 constexpr int GEMM_THREADS = 32 * (2 + GEMM_EPI_WARPS);  // producer, MMA, rescale
 
 struct GemmSmem {
   uint64_t full[gemm::MAX_STAGES_G];   // stage landed (A and B copies)
-  uint64_t empty[gemm::MAX_STAGES_G];  // stage consumed: 1 MMA commit + 8 rescale warps
+  uint64_t empty[gemm::MAX_STAGES_G];  // stage consumed: 1 MMA commit + every rescale warp
   uint64_t tfull[8];                   // TMEM buffer holds a finished block product
-  uint64_t tempty[8];                  // TMEM buffer read by all 8 rescale warps
+  uint64_t tempty[8];                  // TMEM buffer read by every rescale warp
   uint64_t drain;                      // every MMA issued has completed
   uint32_t tmem_base;
   int abort_flag;
@@ -46,12 +51,13 @@ static_assert(sizeof(GemmSmem) <= gemm::SMEM_HEAD, "gemm smem head");
 // first stages are issued before griddepcontrol.wait: weights never depend on
 // the previous kernel); warp 1 lane 0 issues one kind::i8 MMA per Q8_0 block
 // (M = 128 weight rows, N = NT tokens, K = 32) into one of NB tensor-memory
-// buffers and commits its completion to that buffer's barrier; warps 2-9 read
-// each block's int32 products back (warp w reads TMEM lanes 32*(w%4).., i.e.
-// weight rows, and columns of its half of the token tile), rescale them by
+// buffers and commits its completion to that buffer's barrier; warps 2-17
+// read each block's int32 products back (warp w reads TMEM lanes 32*(w%4)..,
+// i.e. weight rows, and the columns of its quarter of the token tile),
+// rescale them by
 // d_w * d_x and accumulate in fp32 registers, then release the buffer.  A
-// stage is refilled once its four MMAs have completed and all eight rescale
-// warps have read its scales.  Work units (row tile, token tile, K range)
+// stage is refilled once its four MMAs have completed and all sixteen
+// rescale warps have read its scales.  Work units (row tile, token tile, K range)
 // are dealt round-robin over the grid; after the last chunk of a unit the
 // rescale warps store its outputs, or with a split K its partial sums
 // (k_gemm_reduce adds them in split order).
@@ -61,11 +67,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   using namespace gemm;
   constexpr int NB = tmem_buffers(NT);
   constexpr uint32_t TCOLS = tmem_cols(NT);
-  constexpr int CPT = NT / 2;  // token columns per rescale thread
+  constexpr int CPT = NT / GEMM_COL_GROUPS;  // token columns per rescale thread
   constexpr uint32_t IDESC = idesc_i8(TILE_M, NT);
   constexpr int SB = stage_bytes(NT);
   static_assert(NB * NT <= (int)TCOLS && TCOLS <= 512, "tensor memory budget");
-  static_assert(CPT % 8 == 0, "tcgen05.ld granularity");
+  static_assert(CPT % 4 == 0, "tcgen05.ld granularity");
   L3G_DYNAMIC_SMEM(smem);
   GemmSmem* sh = reinterpret_cast<GemmSmem*>(smem);
   uint8_t* ring = smem + SMEM_HEAD;
@@ -169,7 +175,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---- rescale warps --------------------------------------------------
     const int ep = warp - 2;
     const int quarter = warp & 3;      // TMEM lanes this warp may read
-    const int half = ep >> 2;          // token columns [half*CPT, half*CPT+CPT)
+    const int half = ep >> 2;          // column group: token columns [half*CPT, half*CPT+CPT)
     const int m = quarter * 32 + lane; // weight row within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * CPT);
     int c = 0, blk = 0;
@@ -197,9 +203,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!ok) break;
           tc_fence_after();
           uint32_t v[CPT];
+          if constexpr (CPT % 8 == 0) {
 #pragma unroll
-          for (int i = 0; i < CPT / 8; ++i)
-            tmem_ld8(t_lane + (uint32_t)(buf * NT + i * 8), v + i * 8);
+            for (int i = 0; i < CPT / 8; ++i)
+              tmem_ld8(t_lane + (uint32_t)(buf * NT + i * 8), v + i * 8);
+          } else {
+#pragma unroll
+            for (int i = 0; i < CPT / 4; ++i)
+              tmem_ld4(t_lane + (uint32_t)(buf * NT + i * 4), v + i * 4);
+          }
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();

@@ -50,6 +50,17 @@ inline void tmem_ld8(uint32_t taddr, uint32_t* v) {
     if (!(t->blk->tmem_used >> u & 1u)) ::simt::fail("tcgen05.ld of unallocated tensor memory");
   for (int i = 0; i < 8; ++i) v[i] = t->blk->tmem[(size_t)(lane0 + t->lane) * 512 + col + i];
 }
+// whole warp: lane i reads 4 columns of tensor-memory lane (taddr lane) + i
+inline void tmem_ld4(uint32_t taddr, uint32_t* v) {
+  ::simt::Thread* t = ::simt::cur();
+  __syncwarp();
+  const uint32_t lane0 = taddr >> 16, col = taddr & 0xFFFFu;
+  if (lane0 != 32u * (uint32_t)(t->warp % 4))
+    ::simt::fail("tcgen05.ld: a warp may only read its own quarter of the lanes");
+  for (uint32_t u = col / 32; u <= (col + 3) / 32; ++u)
+    if (!(t->blk->tmem_used >> u & 1u)) ::simt::fail("tcgen05.ld of unallocated tensor memory");
+  for (int i = 0; i < 4; ++i) v[i] = t->blk->tmem[(size_t)(lane0 + t->lane) * 512 + col + i];
+}
 inline void tmem_wait_ld() {}
 
 inline unsigned long long pk2(float a, float b) {

@@ -7,8 +7,10 @@ session:
 - the logits equal the single-session l3g_forward logits on a clone of the
   state within the parity tolerance (1e-2 relative L2; both compute the
   same quantized arithmetic, the batched path with fp32 sums in another
-  order), and the K/V rows the step appends match within 1e-4 at layer 0
-  (2e-3 with the f16 cache) and within the fixed 1e-2 bar deeper, where an
+  order; at depth the bar is max(1e-2, 1.5 x the band by which the
+  reference's own cgo and pure-Go builds differ on the longest session's
+  last tokens), and the K/V rows the step appends match within 1e-4 at
+  layer 0 (2e-3 with the f16 cache) and within that bar deeper, where an
   fp32 order difference can flip an int8 activation rounding;
 - the sampled id equals SampleTopK restated on the host (tests/sampler_ref)
   over the top-K of the returned logits, with the Philox draw keyed by the
@@ -21,7 +23,7 @@ import numpy as np
 import pytest
 
 from conftest import synthetic_model
-from refspread import LOGIT_TOL, rel_l2
+from refspread import LOGIT_TOL, ReferenceRuns, rel_l2
 from sampler_ref import sample_topk
 
 pytestmark = pytest.mark.gpu
@@ -38,9 +40,16 @@ def _topk(logits, k):
     ("mid", [2, 255, 256, 600], 1024, 0),
     ("small", [7, 120, 260], 512, 1),
 ])
-def test_batch_step_matches_single_session(gpu_lib, name, lens, ctx, kv):
+def test_batch_step_matches_single_session(gpu_lib, oracle_mod, name, lens, ctx, kv):
     import synthetic
     cfg, T = synthetic_model(name)
+    # the reference builds' own spread on the longest session's last tokens
+    longest = int(np.argmax(lens))
+    ids_l = synthetic.prompt_ids(cfg, lens[longest], seed=100 + longest)
+    tail = min(3, len(ids_l) - 1)
+    R = ReferenceRuns(oracle_mod, cfg, T, ids_l[-tail:], ctx, with_f64=False,
+                      prefix_ids=ids_l[:-tail]) if tail > 0 else None
+    bar = R.tol() if R is not None else LOGIT_TOL
     opts = gpu_lib.default_options(device=0, kv_dtype=kv)
     m = gpu_lib.LoadModelFromTensors(gpu_lib.hparams_for(cfg), T, opts)
     ws = m.NewWorkspace(ctx, 40)
@@ -65,13 +74,13 @@ def test_batch_step_matches_single_session(gpu_lib, name, lens, ctx, kv):
         for i in range(n):
             assert states[i].Pos == pos[i] + 1
             m.ForwardIntoWorkspace(clones[i], tokens[i], buf, ws)
-            assert rel_l2(logits[i], buf) < LOGIT_TOL, (step, i, rel_l2(logits[i], buf))
+            assert rel_l2(logits[i], buf) < bar, (step, i, rel_l2(logits[i], buf), bar)
             for layer in range(cfg.n_layers):
                 kb, vb = states[i].read_kv(layer, pos[i], 1)
                 kc, vc = clones[i].read_kv(layer, pos[i], 1)
                 tol = 2e-3 if kv else 1e-4
                 if layer > 0:
-                    tol = LOGIT_TOL
+                    tol = max(tol, bar)
                 assert rel_l2(kb, kc) < tol and rel_l2(vb, vc) < tol, (step, i, layer)
             ids, lg = _topk(logits[i], 40)
             assert nxt[i] == sample_topk(ids, lg, 1.3, seeds[i], pos[i]), (step, i)

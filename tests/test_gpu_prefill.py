@@ -7,7 +7,8 @@ quantization, exact int32 block sums) with fp32 sums in another order, so:
   within 1e-4 relative L2; from layer 1 on, an fp32 summation-order
   difference can round an activation onto the other side of an int8
   boundary (QuantizeQ8_0Into before every matvec), and the deeper layers'
-  rows are held to the fixed 1e-2 bar instead;
+  rows are held to max(1e-2, 1.5 x the band by which the reference's own
+  cgo and pure-Go builds differ on the same tokens) instead;
 - the logits of the tokens decoded after it match the token-by-token run's
   and, within the reference's own band, the cgo reference's (the oracle with
   the reference's simd.c, teacher-forced on the same ids).
@@ -24,13 +25,14 @@ from refspread import LOGIT_TOL, ReferenceRuns, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-def _kv_close(gpu_lib, cfg, s_a, s_b, npos, tol=1e-4):
+def _kv_close(gpu_lib, cfg, s_a, s_b, npos, tol=1e-4, deep_tol=LOGIT_TOL):
     """Layer 0 within tol; deeper layers (past the first int8 re-quantization
-    of the stream) within the fixed 1e-2 bar."""
+    of the stream) within deep_tol: the fixed 1e-2 bar, or the reference
+    builds' own band where that is wider."""
     for layer in range(cfg.n_layers):
         ka, va = s_a.read_kv(layer, 0, npos)
         kb, vb = s_b.read_kv(layer, 0, npos)
-        t = tol if layer == 0 else max(tol, LOGIT_TOL)
+        t = tol if layer == 0 else max(tol, deep_tol)
         assert rel_l2(ka, kb) < t, (layer, rel_l2(ka, kb))
         assert rel_l2(va, vb) < t, (layer, rel_l2(va, vb))
 
@@ -58,7 +60,8 @@ def test_batched_prefill_matches_token_by_token(gpu_lib, oracle_mod, name, n_pro
         assert s_bat.Pos == split
         m.PrefillBatched(s_bat, prompt[split:], ws)
     assert s_bat.Pos == s_tok.Pos == n_prompt
-    _kv_close(gpu_lib, cfg, s_tok, s_bat, n_prompt)
+    R = ReferenceRuns(oracle_mod, cfg, T, tail, ctx, with_f64=False, prefix_ids=prompt)
+    _kv_close(gpu_lib, cfg, s_tok, s_bat, n_prompt, deep_tol=R.tol())
     # decode the tail from both states
     logits_tok, logits_bat = [], []
     buf = np.empty(cfg.vocab, np.float32)
@@ -67,7 +70,6 @@ def test_batched_prefill_matches_token_by_token(gpu_lib, oracle_mod, name, n_pro
         logits_tok.append(buf.copy())
         m.ForwardIntoWorkspace(s_bat, int(t), buf, ws)
         logits_bat.append(buf.copy())
-    R = ReferenceRuns(oracle_mod, cfg, T, tail, ctx, with_f64=False, prefix_ids=prompt)
     for i in range(len(tail)):
         assert rel_l2(logits_bat[i], logits_tok[i]) < R.tol()
         assert rel_l2(logits_bat[i], R.cgo[i]) < R.tol(), (i, R.band())
