@@ -110,6 +110,54 @@ __host__ __device__ __forceinline__ int at_scratch_floats(int G, int hd) {
   return NW * MAXG * 2 + NW * G * hd + MAXG * 2 + G * hd;
 }
 
+// Merge of one 32-output block of a kv head across its S splits (one warp;
+// lane = output).  Split s published its query head h's running max and sum
+// at ml[(s * G + h) * 2 + {0, 1}] and its unnormalised outputs at po[s * gh
+// + col].  out = (sum_s o_s e_s) / (sum_s l_s e_s), e_s = exp(m_s - max_s
+// m_s); the sums run in split order (deterministic).  The loads are issued
+// together -- every split's (m, l) pair and, for up to 32 splits at a time,
+// this lane's outputs -- so a merge costs one round trip to L2 per 32
+// splits instead of one per step of the arithmetic.  wbuf: 32 floats of
+// shared memory per 32 splits for the weights e_s.
+__device__ __forceinline__ float merge_split_block(const float* ml, const float* po, int S,
+                                                   int G, int gh, int h, int col, int lane,
+                                                   float* wbuf) {
+  constexpr int MB = 32;  // splits loaded per batch
+  float ov[MB];
+#pragma unroll
+  for (int u = 0; u < MB; ++u) ov[u] = u < S ? __ldcg(po + (size_t)u * gh + col) : 0.0f;
+  float M = -INFINITY;
+  for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
+  M = warp_max(M);
+  float L = 0.0f;
+  for (int s0 = 0; s0 < S; s0 += 32) {
+    const int s2 = s0 + lane;
+    float le = 0.0f;
+    if (s2 < S) {
+      const float2 p = __ldcg(reinterpret_cast<const float2*>(ml + ((size_t)s2 * G + h) * 2));
+      const float e = p.x == -INFINITY ? 0.0f : expf(p.x - M);
+      wbuf[s2] = e;
+      le = p.y * e;
+    }
+    L += warp_sum(le);
+  }
+  __syncwarp();
+  float O = 0.0f;
+#pragma unroll
+  for (int u = 0; u < MB; ++u)
+    if (u < S) O = fmaf(ov[u], wbuf[u], O);
+  for (int s0 = MB; s0 < S; s0 += MB) {
+#pragma unroll
+    for (int u = 0; u < MB; ++u)
+      ov[u] = s0 + u < S ? __ldcg(po + (size_t)(s0 + u) * gh + col) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < MB; ++u)
+      if (s0 + u < S) O = fmaf(ov[u], wbuf[s0 + u], O);
+  }
+  __syncwarp();
+  return __fmul_rn(O, __fdiv_rn(1.0f, L));
+}
+
 template <int DPL, typename KT, int GP, bool CL>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ AttnArgs a) {
@@ -451,36 +499,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const float* po = a.part_o + (size_t)kvh * S * gh;
   for (int blk = b0 + warp; blk < b1; blk += NW) {  // one warp per block of 32 outputs
     const int h = blk * 32 / hd;
-    float M = -INFINITY;
-    for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
-    M = warp_max(M);
-    float L = 0.0f;
-    for (int s0 = 0; s0 < S; s0 += 32) {
-      const int s2 = s0 + lane;
-      float le = 0.0f;
-      if (s2 < S) {
-        const float ms = __ldcg(ml + ((size_t)s2 * G + h) * 2);
-        const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
-        wbuf[s2] = e;
-        le = __ldcg(ml + ((size_t)s2 * G + h) * 2 + 1) * e;
-      }
-      L += warp_sum(le);
-    }
-    __syncwarp();
-    // O = sum over splits in split order of o_s * e_s, loads batched by 8
-    const float* col = po + (size_t)blk * 32 + lane;
-    float O = 0.0f;
-    int s2 = 0;
-    for (; s2 + 8 <= S; s2 += 8) {
-      float ov[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) ov[u] = __ldcg(col + (size_t)(s2 + u) * gh);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) O = fmaf(ov[u], wbuf[s2 + u], O);
-    }
-    for (; s2 < S; ++s2) O = fmaf(__ldcg(col + (size_t)s2 * gh), wbuf[s2], O);
-    __syncwarp();
-    const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
+    const float v = merge_split_block(ml, po, S, G, gh, h, blk * 32 + lane, lane, wbuf);
     a.out[(size_t)kvh * gh + blk * 32 + lane] = v;
     quant_block(v, kvh * gh / 32 + blk, lane, a.out_d, a.out_q);
   }

@@ -68,6 +68,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   constexpr int NB = tmem_buffers(NT);
   constexpr uint32_t TCOLS = tmem_cols(NT);
   constexpr int CPT = NT / GEMM_COL_GROUPS;  // token columns per rescale thread
+  // blocks rescaled per group: 32 loaded products per thread at most
+  constexpr int GB = 32 / CPT >= BPC ? BPC : (32 / CPT >= 2 ? 32 / CPT : 1);
+  static_assert(BPC % GB == 0 && tmem_buffers(NT) >= 2 * GB, "rescale groups");
   constexpr uint32_t IDESC = idesc_i8(TILE_M, NT);
   constexpr int SB = stage_bytes(NT);
   static_assert(NB * NT <= (int)TCOLS && TCOLS <= 512, "tensor memory budget");
@@ -195,41 +198,54 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const uint8_t* st = ring + (size_t)s * SB;
         const __half* dw = reinterpret_cast<const __half*>(st + A_Q_BYTES);
         const float* dx = reinterpret_cast<const float*>(st + A_CHUNK + b_q_bytes(NT));
+        // blocks in groups of GB: every block's products are loaded from
+        // tensor memory before one wait for the loads, so the latency of a
+        // wait, a load and a release is paid once per group
 #pragma unroll 1
-        for (int j = 0; j < BPC; ++j, ++blk) {
-          const int buf = blk % NB, use = blk / NB;
-          ok = __all_sync(0xffffffffu, mbar_wait(&sh->tfull[buf], use & 1, &sh->abort_flag,
-                                                 g.res, 25, g.wait_ns));
-          if (!ok) break;
-          tc_fence_after();
-          uint32_t v[CPT];
-          if constexpr (CPT % 8 == 0) {
+        for (int j0 = 0; j0 < BPC; j0 += GB, blk += GB) {
+          uint32_t v[GB][CPT];
 #pragma unroll
-            for (int i = 0; i < CPT / 8; ++i)
-              tmem_ld8(t_lane + (uint32_t)(buf * NT + i * 8), v + i * 8);
-          } else {
+          for (int gi = 0; gi < GB; ++gi) {
+            const int buf = (blk + gi) % NB, use = (blk + gi) / NB;
+            ok = __all_sync(0xffffffffu, mbar_wait(&sh->tfull[buf], use & 1, &sh->abort_flag,
+                                                   g.res, 25, g.wait_ns));
+            if (!ok) break;
+            tc_fence_after();
+            if constexpr (CPT % 8 == 0) {
 #pragma unroll
-            for (int i = 0; i < CPT / 4; ++i)
-              tmem_ld4(t_lane + (uint32_t)(buf * NT + i * 4), v + i * 4);
+              for (int i = 0; i < CPT / 8; ++i)
+                tmem_ld8(t_lane + (uint32_t)(buf * NT + i * 8), v[gi] + i * 8);
+            } else {
+#pragma unroll
+              for (int i = 0; i < CPT / 4; ++i)
+                tmem_ld4(t_lane + (uint32_t)(buf * NT + i * 4), v[gi] + i * 4);
+            }
           }
+          if (!ok) break;
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sh->tempty[buf]);
-          // acc += float(I) * (d_w * d_x), per column, as fmaf(I, d_w * d_x, acc)
-          const float w = __half2float(dw[j * TILE_M + m]);
-          const unsigned long long w2 = pk2(w, w);
-          const unsigned long long nbias2 = pk2(-GEMM_BIAS, -GEMM_BIAS);
-          const float2* dxj = reinterpret_cast<const float2*>(dx + j * NT + half * CPT);
+          if (lane == 0)
 #pragma unroll
-          for (int i = 0; i < CPT / 2; ++i) {
-            const float2 d2 = dxj[i];
-            const unsigned long long s2 = mul2(w2, pk2(d2.x, d2.y));
-            const unsigned long long f2 =
-                add2(pk2(__int_as_float((int)v[2 * i] + GEMM_BIAS_BITS),
-                         __int_as_float((int)v[2 * i + 1] + GEMM_BIAS_BITS)),
-                     nbias2);
-            acc2[i] = fma2(f2, s2, acc2[i]);
+            for (int gi = 0; gi < GB; ++gi) mbar_arrive(&sh->tempty[(blk + gi) % NB]);
+          // acc += float(I) * (d_w * d_x), per column, as fmaf(I, d_w * d_x, acc)
+          const unsigned long long nbias2 = pk2(-GEMM_BIAS, -GEMM_BIAS);
+#pragma unroll
+          for (int gi = 0; gi < GB; ++gi) {
+            const int j = j0 + gi;
+            const float w = __half2float(dw[j * TILE_M + m]);
+            const unsigned long long w2 = pk2(w, w);
+            const float2* dxj = reinterpret_cast<const float2*>(dx + j * NT + half * CPT);
+#pragma unroll
+            for (int i = 0; i < CPT / 2; ++i) {
+              const float2 d2 = dxj[i];
+              const unsigned long long s2 = mul2(w2, pk2(d2.x, d2.y));
+              const unsigned long long f2 =
+                  add2(pk2(__int_as_float((int)v[gi][2 * i] + GEMM_BIAS_BITS),
+                           __int_as_float((int)v[gi][2 * i + 1] + GEMM_BIAS_BITS)),
+                       nbias2);
+              acc2[i] = fma2(f2, s2, acc2[i]);
+            }
           }
         }
         if (!ok) break;

@@ -667,35 +667,7 @@ static __device__ void ps_merge_block(const PersistArgs& a, float* wbuf, int kvh
   const int h = blk * 32 / hd;
   const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
   const float* po = a.part_o + (size_t)kvh * S * gh;
-  float M = -INFINITY;
-  for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
-  M = warp_max(M);
-  float L = 0.0f;
-  for (int s0 = 0; s0 < S; s0 += 32) {
-    const int s2 = s0 + lane;
-    float le = 0.0f;
-    if (s2 < S) {
-      const float ms = __ldcg(ml + ((size_t)s2 * G + h) * 2);
-      const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
-      wbuf[s2] = e;
-      le = __ldcg(ml + ((size_t)s2 * G + h) * 2 + 1) * e;
-    }
-    L += warp_sum(le);
-  }
-  __syncwarp();
-  const float* col = po + (size_t)blk * 32 + lane;
-  float O = 0.0f;
-  int s2 = 0;
-  for (; s2 + 8 <= S; s2 += 8) {
-    float ov[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) ov[u] = __ldcg(col + (size_t)(s2 + u) * gh);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) O = fmaf(ov[u], wbuf[s2 + u], O);
-  }
-  for (; s2 < S; ++s2) O = fmaf(__ldcg(col + (size_t)s2 * gh), wbuf[s2], O);
-  __syncwarp();
-  const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
+  const float v = merge_split_block(ml, po, S, G, gh, h, blk * 32 + lane, lane, wbuf);
   a.attn[(size_t)kvh * gh + blk * 32 + lane] = v;
   quant_block(v, kvh * gh / 32 + blk, lane, a.attn_d, a.attn_q);
 }
