@@ -32,8 +32,8 @@ constexpr int GEMM_THREADS = 32 * (2 + GEMM_EPI_WARPS);  // producer, MMA, resca
 struct GemmSmem {
   uint64_t full[gemm::MAX_STAGES_G];   // stage landed (A and B copies)
   uint64_t empty[gemm::MAX_STAGES_G];  // stage consumed: 1 MMA commit + every rescale warp
-  uint64_t tfull[8];                   // TMEM buffer holds a finished block product
-  uint64_t tempty[8];                  // TMEM buffer read by every rescale warp
+  uint64_t tfull[32];                  // TMEM buffer holds a finished block product
+  uint64_t tempty[32];                 // TMEM buffer read by every rescale warp
   uint64_t drain;                      // every MMA issued has completed
   uint32_t tmem_base;
   int abort_flag;

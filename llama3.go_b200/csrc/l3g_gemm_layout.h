@@ -89,8 +89,10 @@ L3G_HD constexpr uint32_t idesc_i8(int m, int n) {
 }
 
 // Tensor-memory buffers of one CTA: NB buffers of NT columns (one per block
-// in flight between the MMA issuer and the rescaling warps).
-L3G_HD constexpr int tmem_buffers(int nt) { return nt >= 128 ? 4 : 8; }
+// in flight between the MMA issuer and the rescaling warps), all 512 columns
+// of the SM's tensor memory: 8, 4, 2 and 1 chunks in flight at 16, 32, 64
+// and 128 tokens, so the MMAs run that far ahead of the rescale.
+L3G_HD constexpr int tmem_buffers(int nt) { return 512 / nt < 32 ? 512 / nt : 32; }
 L3G_HD constexpr int tmem_cols(int nt) {
   return tmem_buffers(nt) * nt <= 32 ? 32 : tmem_buffers(nt) * nt <= 64 ? 64
        : tmem_buffers(nt) * nt <= 128 ? 128 : tmem_buffers(nt) * nt <= 256 ? 256 : 512;

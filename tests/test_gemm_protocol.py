@@ -11,9 +11,9 @@ arrivals) as separate events that fire at any later time:
   block wait tempty[buf] (parity (use - 1) & 1 from its second use), issue
   the MMA into buf, commit to tfull[buf]; after the chunk's 4 blocks commit
   to empty[s];
-- 8 rescale warps: per chunk wait full[s]; per block wait tfull[buf]
-  (parity use & 1), read the buffer, arrive tempty[buf]; after the chunk
-  arrive empty[s].
+- 16 rescale warps: per chunk wait full[s]; per group of GB blocks wait
+  tfull[buf] of each block in order (parity use & 1) and read the buffer,
+  then arrive tempty[buf] of each; after the chunk arrive empty[s].
 mbarrier model: a phase completes when its pending arrivals reach zero and
 its transaction count is zero; try_wait.parity(P) succeeds when the current
 phase's parity differs from P.  tcgen05.commit arrives once every MMA the
@@ -21,13 +21,13 @@ thread issued before it has completed.  Checked: no deadlock; a stage is read
 (by an MMA or for its scales) only while it holds the chunk the reader
 expects; a copy never lands in a stage an unfinished reader still uses; a
 TMEM buffer is read only while it holds the expected block and is never
-overwritten before all 8 warps read it.
+overwritten before all 16 warps read it.
 """
 import random
 
 import pytest
 
-EPI = 8
+EPI = 16
 BPC = 4
 
 
@@ -71,9 +71,9 @@ class Bar:
         return (self.phase & 1) != parity
 
 
-def run(ns, nb, nchunks, seed, skip_tempty_wait=False):
-    """One replay; skip_tempty_wait plants a protocol bug (in the model) for
-    the negative test."""
+def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1):
+    """One replay (gb: blocks per rescale group); skip_tempty_wait plants a
+    protocol bug (in the model) for the negative test."""
     rng = random.Random(seed)
     mdl = Model()
     full = [Bar(mdl, 1) for _ in range(ns)]
@@ -141,15 +141,20 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False):
                 yield
             assert stage[s] == c, "scales read from the wrong chunk"
             readers[s].add(("epi", w))
-            for _ in range(BPC):
-                buf, use = blk % nb, blk // nb
-                while not tfull[buf].ready(use & 1):
+            for _ in range(BPC // gb):
+                group = []
+                for _ in range(gb):
+                    buf, use = blk % nb, blk // nb
+                    while not tfull[buf].ready(use & 1):
+                        yield
+                    assert tmem[buf] == blk, ("stale TMEM buffer", tmem[buf], blk)
+                    group.append(buf)
+                    blk += 1
                     yield
-                assert tmem[buf] == blk, ("stale TMEM buffer", tmem[buf], blk)
-                unread[buf] -= 1
-                assert unread[buf] >= 0
-                tempty[buf].arrive()
-                blk += 1
+                for buf in group:
+                    unread[buf] -= 1
+                    assert unread[buf] >= 0
+                    tempty[buf].arrive()
                 yield
             readers[s].discard(("epi", w))
             empty[s].arrive()
@@ -206,11 +211,15 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False):
     assert all(b.pending == b.count and b.tx == 0 for b in full + empty + tfull + tempty)
 
 
-@pytest.mark.parametrize("ns,nb", [(1, 4), (2, 4), (3, 8), (5, 4), (7, 4), (8, 8)])
-def test_gemm_barrier_protocol(ns, nb):
+# (stages, TMEM buffers, blocks per rescale group): the kernel's pairs are
+# NB = 32 / 16 / 8 / 4 buffers with groups of 4 / 4 / 2 / 1 blocks at 16 /
+# 32 / 64 / 128 tokens; smaller rings and buffer counts stress the waits
+@pytest.mark.parametrize("ns,nb,gb", [(1, 4, 1), (2, 4, 2), (3, 8, 4), (5, 4, 1), (7, 4, 2),
+                                      (8, 8, 4), (8, 32, 4), (8, 16, 4), (8, 8, 2), (6, 4, 1)])
+def test_gemm_barrier_protocol(ns, nb, gb):
     for trial in range(30):
         nchunks = random.Random(trial).randint(1, 3 * ns + 5)
-        run(ns, nb, nchunks, seed=ns * 1000 + nb * 100 + trial)
+        run(ns, nb, nchunks, seed=ns * 1000 + nb * 100 + gb * 10 + trial, gb=gb)
 
 
 def test_model_catches_a_parity_slip():
