@@ -14,11 +14,7 @@ ABI, against the per-kernel step and the oracle.
   within the band of test_gpu_parity, and greedy ids under teacher forcing.
 - The device-fed greedy loop gives the per-token loop's tokens; the traced
   step stamps every CTA at every grid barrier.
-
-Opt-in (L3G_PERSIST_GPU=1) until the kernel's first controlled run on a
-B200: the file is then collected like every other GPU test.
 """
-import os
 
 import numpy as np
 import pytest
@@ -26,11 +22,7 @@ import pytest
 from conftest import synthetic_model
 from refspread import ReferenceRuns, rel_l2
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("L3G_PERSIST_GPU") != "1",
-                       reason="persistent layer kernel not yet run on a B200 (set L3G_PERSIST_GPU=1)"),
-]
+pytestmark = pytest.mark.gpu
 
 
 def _fusions(fuse):

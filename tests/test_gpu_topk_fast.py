@@ -9,11 +9,7 @@ against the oracle's ForwardTopKIntoWorkspace restatement.
 - The mode switches only the top-K and sampled calls: with it on, the full
   logits are still the exact-exp path's; turning it off gives back the exact
   top-K bit for bit; turning it on again repeats the fast items bit for bit.
-
-Opt-in (L3G_FASTEXP_GPU=1) until the kernels' first controlled run on a
-B200: the file is then collected like every other GPU test.
 """
-import os
 
 import numpy as np
 import pytest
@@ -21,11 +17,7 @@ import pytest
 from conftest import synthetic_model
 from refspread import BAND_MARGIN, LOGIT_TOL, rel_l2
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("L3G_FASTEXP_GPU") != "1",
-                       reason="opt-in until the first controlled B200 run (L3G_FASTEXP_GPU=1)"),
-]
+pytestmark = pytest.mark.gpu
 
 
 def _load_gpu(gpu_lib, cfg, T, **kw):
