@@ -99,8 +99,9 @@ static __global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seq
 }
 
 // Split-K decode attention (infer.go:130-175) of every sequence: CTA (split,
-// kv head, sequence) covers positions [split * BD_SPLIT, ...) up to the
-// sequence's own position.  A producer warp streams the split's cache rows
+// kv head, sequence) covers positions [split * split_len, ...) up to the
+// sequence's own position (split_len a multiple of BD_SPLIT, chosen per step
+// by the host so that the grid holds a few waves of CTAs).  A producer warp streams the split's cache rows
 // (K | V of 32 positions, contiguous in the cache) into a ring of BD_STAGES
 // shared-memory stages with 1-D bulk copies; compute warp w takes positions
 // w, w + 8, w + 16, w + 24 of every 32-position tile (so across the split it
@@ -110,7 +111,7 @@ static __global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seq
 // partial (max, sum, o[HD]) per query head, merged across splits by
 // k_bd_merge.  Every wait is bounded; after an abort the CTA drains its
 // copies and writes nothing.
-constexpr int BD_SPLIT = 256;
+constexpr int BD_SPLIT = 256;  // split lengths are multiples of this
 constexpr int BD_TILE = 32;    // positions per ring stage
 constexpr int BD_STAGES = 3;
 constexpr int BD_THREADS = 288;  // 8 compute warps + 1 producer warp
@@ -131,7 +132,8 @@ __host__ __device__ constexpr int bd_smem_bytes(int hd, int es, int gp) {
 template <int HD, int GP, typename KT>
 __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
     const float* Q, const SeqInfo* seqs, int layer, int group, int nq_heads, float scale,
-    float* part_o, float* part_ml, int max_splits, Result* res, unsigned long long wait_ns) {
+    float* part_o, float* part_ml, int max_splits, int split_len, Result* res,
+    unsigned long long wait_ns) {
   constexpr int DPL = HD / 32;
   constexpr int SB = bd_stage_bytes(HD, (int)sizeof(KT));
   static_assert(sizeof(BdSmem) <= 1024, "smem head");
@@ -141,8 +143,8 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
   float(*sm_o)[GP][HD] = reinterpret_cast<float(*)[GP][HD]>(ring);  // after the ring drains
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const SeqInfo& sq = seqs[b];
-  const int p0 = split * BD_SPLIT;
-  const int p1 = min(sq.pos + 1, p0 + BD_SPLIT);
+  const int p0 = split * split_len;
+  const int p1 = min(sq.pos + 1, p0 + split_len);
   const int ntiles = p1 > p0 ? (p1 - p0 + BD_TILE - 1) / BD_TILE : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -281,10 +283,10 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
 // out[b][head] = sum over splits of o_s * exp(m_s - M) / sum of l_s * exp(m_s - M).
 // grid (query heads, n), HD threads.
 static __global__ void k_bd_merge(const float* part_o, const float* part_ml, const SeqInfo* seqs,
-                           int nq_heads, int hd, int max_splits, float* out) {
+                           int nq_heads, int hd, int max_splits, int split_len, float* out) {
   const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   if (d >= hd) return;
-  const int ns = (seqs[b].pos + 1 + BD_SPLIT - 1) / BD_SPLIT;
+  const int ns = (seqs[b].pos + 1 + split_len - 1) / split_len;
   const size_t slot0 = ((size_t)b * nq_heads + head) * max_splits;
   float M = -INFINITY;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, part_ml[(slot0 + s) * 2]);

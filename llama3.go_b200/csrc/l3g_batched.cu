@@ -53,10 +53,10 @@ static cudaError_t launch_gemm(const GemmMat& w, const uint8_t* act, int n_tok, 
   const long long units = (long long)g.n_rt * g.n_tt * g.ksplit;
   const int grid = (int)std::max<long long>(1, std::min<long long>(nsm, units));
   switch (nt) {
-    case 16: k_gemm_q8<16><<<grid, GEMM_THREADS, gemm::smem_bytes(16), st>>>(g); break;
-    case 32: k_gemm_q8<32><<<grid, GEMM_THREADS, gemm::smem_bytes(32), st>>>(g); break;
-    case 64: k_gemm_q8<64><<<grid, GEMM_THREADS, gemm::smem_bytes(64), st>>>(g); break;
-    default: k_gemm_q8<128><<<grid, GEMM_THREADS, gemm::smem_bytes(128), st>>>(g); break;
+    case 16: k_gemm_q8<16><<<grid, gemm_threads(16), gemm::smem_bytes(16), st>>>(g); break;
+    case 32: k_gemm_q8<32><<<grid, gemm_threads(32), gemm::smem_bytes(32), st>>>(g); break;
+    case 64: k_gemm_q8<64><<<grid, gemm_threads(64), gemm::smem_bytes(64), st>>>(g); break;
+    default: k_gemm_q8<128><<<grid, gemm_threads(128), gemm::smem_bytes(128), st>>>(g); break;
   }
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && g.ksplit > 1) {
@@ -643,7 +643,16 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
   const unsigned long long wait_ns = m->world > 1 ? WAIT_TIMEOUT_PEER_NS : WAIT_TIMEOUT_NS;
   const int nt = gemm::token_tile(n);
   const int n_pad = (n + nt - 1) / nt * nt;
-  const int splits = (max_pos + 1 + BD_SPLIT - 1) / BD_SPLIT;
+  // split length: a few waves of CTAs over every session's positions (two
+  // CTAs per SM), long splits for long sessions, at least BD_SPLIT
+  long long total = 0;
+  for (int i = 0; i < n; ++i) total += states[i]->pos + 1;
+  const long long target = 8LL * m->nsm;
+  int split_len = (int)((total * m->hkv_l + target - 1) / target);
+  // L3G_BD_SPLIT=n fixes it (a multiple of BD_SPLIT; for tests and sweeps)
+  if (const char* env = getenv("L3G_BD_SPLIT")) split_len = atoi(env);
+  split_len = std::min(16 * BD_SPLIT, std::max(BD_SPLIT, (split_len + BD_SPLIT - 1) / BD_SPLIT * BD_SPLIT));
+  const int splits = (max_pos + 1 + split_len - 1) / split_len;
   const float scale = (float)(1.0 / sqrt((double)hd));
   for (int i = 0; i < n; ++i)  // each session's page for this step's position
     if (int rc = state_map(states[i], states[i]->pos + 1, st)) return rc;
@@ -672,11 +681,11 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
   if (m->kv_f16)                                                                             \
     k_bd_attention<HD, GP, __half><<<grid, BD_THREADS, bd_smem_bytes(HD, 2, GP), st>>>(      \
         b->q, b->d_seq, l, m->group, m->hq_l, scale, b->part_o, b->part_ml, b->max_splits,     \
-        b->d_res, wait_ns);                                                                   \
+        split_len, b->d_res, wait_ns);                                                        \
   else                                                                                       \
     k_bd_attention<HD, GP, float><<<grid, BD_THREADS, bd_smem_bytes(HD, 4, GP), st>>>(       \
         b->q, b->d_seq, l, m->group, m->hq_l, scale, b->part_o, b->part_ml, b->max_splits,     \
-        b->d_res, wait_ns)
+        split_len, b->d_res, wait_ns)
 #define BDATT_G(HD)          \
   if (gp == 1) {             \
     BDATT(HD, 1);            \
@@ -698,7 +707,7 @@ extern "C" int l3g_batch_step(l3g_batch* b, l3g_state* const* states, int32_t n,
 #undef BDATT
       CUDA_TRY(cudaGetLastError());
       k_bd_merge<<<dim3(m->hq_l, n), 128, 0, st>>>(b->part_o, b->part_ml, b->d_seq, m->hq_l, hd,
-                                                   b->max_splits, b->att);
+                                                   b->max_splits, split_len, b->att);
       CUDA_TRY(cudaGetLastError());
     }
     {

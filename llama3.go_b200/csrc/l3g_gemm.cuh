@@ -21,13 +21,16 @@ struct GemmArgs {
   unsigned long long wait_ns;
 };
 
-// Four warpgroups rescale: each TMEM lane quarter (weight rows 32q..) is
-// read by four warps, one per quarter of the token tile's columns, so every
-// scheduler has four rescale warps to hide the tensor-memory and
-// shared-memory latencies of the per-block rescale.
-constexpr int GEMM_EPI_WARPS = 16;
-constexpr int GEMM_COL_GROUPS = GEMM_EPI_WARPS / 4;
-constexpr int GEMM_THREADS = 32 * (2 + GEMM_EPI_WARPS);  // producer, MMA, rescale
+// Rescale warps: each TMEM lane quarter (weight rows 32q..) is read by one
+// warp per group of 16 token columns (at most four groups), so a warp
+// rescales 16 products per row and block at 16-64 tokens (32 at 128): the
+// per-block cost of waiting, loading from tensor memory and releasing is
+// paid for at least 16 products, and a scheduler has one to four rescale
+// warps.
+__host__ __device__ constexpr int gemm_epi_warps(int nt) { return nt >= 64 ? 16 : nt / 4; }
+__host__ __device__ constexpr int gemm_threads(int nt) {
+  return 32 * (2 + gemm_epi_warps(nt));  // producer, MMA issuer, rescale
+}
 
 struct GemmSmem {
   uint64_t full[gemm::MAX_STAGES_G];   // stage landed (A and B copies)
@@ -51,25 +54,27 @@ static_assert(sizeof(GemmSmem) <= gemm::SMEM_HEAD, "gemm smem head");
 // first stages are issued before griddepcontrol.wait: weights never depend on
 // the previous kernel); warp 1 lane 0 issues one kind::i8 MMA per Q8_0 block
 // (M = 128 weight rows, N = NT tokens, K = 32) into one of NB tensor-memory
-// buffers and commits its completion to that buffer's barrier; warps 2-17
+// buffers and commits its completion to that buffer's barrier; warps 2..
 // read each block's int32 products back (warp w reads TMEM lanes 32*(w%4)..,
-// i.e. weight rows, and the columns of its quarter of the token tile),
+// i.e. weight rows, and the columns of its group of the token tile),
 // rescale them by
 // d_w * d_x and accumulate in fp32 registers, then release the buffer.  A
-// stage is refilled once its four MMAs have completed and all sixteen
-// rescale warps have read its scales.  Work units (row tile, token tile, K range)
+// stage is refilled once its four MMAs have completed and every rescale
+// warp has read its scales.  Work units (row tile, token tile, K range)
 // are dealt round-robin over the grid; after the last chunk of a unit the
 // rescale warps store its outputs, or with a split K its partial sums
 // (k_gemm_reduce adds them in split order).
 template <int NT>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(gemm_threads(NT), 1)
     k_gemm_q8(const __grid_constant__ GemmArgs g) {
   using namespace gemm;
   constexpr int NB = tmem_buffers(NT);
   constexpr uint32_t TCOLS = tmem_cols(NT);
-  constexpr int CPT = NT / GEMM_COL_GROUPS;  // token columns per rescale thread
-  // blocks rescaled per group: 32 loaded products per thread at most
-  constexpr int GB = 32 / CPT >= BPC ? BPC : (32 / CPT >= 2 ? 32 / CPT : 1);
+  constexpr int EPI = gemm_epi_warps(NT);
+  constexpr int CPT = NT / (EPI / 4);  // token columns per rescale thread
+  // blocks rescaled per group: 64 (16 warps: 32) loaded products per thread
+  constexpr int LP = EPI >= 16 ? 32 : 64;
+  constexpr int GB = LP / CPT >= BPC ? BPC : (LP / CPT >= 2 ? LP / CPT : 1);
   static_assert(BPC % GB == 0 && tmem_buffers(NT) >= 2 * GB, "rescale groups");
   constexpr uint32_t IDESC = idesc_i8(TILE_M, NT);
   constexpr int SB = stage_bytes(NT);
@@ -89,11 +94,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&sh->full[s], 1);
-      mbar_init(&sh->empty[s], 1 + GEMM_EPI_WARPS);
+      mbar_init(&sh->empty[s], 1 + EPI);
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(&sh->tfull[i], 1);
-      mbar_init(&sh->tempty[i], GEMM_EPI_WARPS);
+      mbar_init(&sh->tempty[i], EPI);
     }
     mbar_init(&sh->drain, 1);
     sh->abort_flag = 0;

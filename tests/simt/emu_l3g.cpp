@@ -400,7 +400,7 @@ static void run_gemm(const uint8_t* w, int rows, int cols, const uint8_t* act, i
   const size_t smem = gemm::SMEM_HEAD + (size_t)g.nstages * gemm::stage_bytes(nt);
   auto go = [&](auto nt_c) {
     constexpr int NT = decltype(nt_c)::value;
-    simt::launch(dim3(G), dim3(GEMM_THREADS), smem, [&] { k_gemm_q8<NT>(g); });
+    simt::launch(dim3(G), dim3(gemm_threads(NT)), smem, [&] { k_gemm_q8<NT>(g); });
   };
   switch (nt) {
     case 16: go(std::integral_constant<int, 16>{}); break;
@@ -670,7 +670,7 @@ int emu_batch_step(EmuBatch* e) {
             using KT = decltype(kt);
             simt::launch(grid, dim3(BD_THREADS), bd_smem_bytes(HD, (int)sizeof(KT), GPc), [&] {
               k_bd_attention<HD, GPc, KT>(Q, e->seqs, l, G, e->hq, scale, part_o, part_ml,
-                                          e->max_splits, res, WAIT_TIMEOUT_NS);
+                                          e->max_splits, BD_SPLIT, res, WAIT_TIMEOUT_NS);
             });
           };
           auto by_gp = [&](auto hd_c, auto kt) {
@@ -692,7 +692,7 @@ int emu_batch_step(EmuBatch* e) {
             default: simt::fail("head dim");
           }
           simt::launch(dim3(e->hq, n), dim3(128), 0, [&] {
-            k_bd_merge(part_o, part_ml, e->seqs, e->hq, hd, e->max_splits, ATT);
+            k_bd_merge(part_o, part_ml, e->seqs, e->hq, hd, e->max_splits, BD_SPLIT, ATT);
           });
         }
         {

@@ -11,7 +11,7 @@ arrivals) as separate events that fire at any later time:
   block wait tempty[buf] (parity (use - 1) & 1 from its second use), issue
   the MMA into buf, commit to tfull[buf]; after the chunk's 4 blocks commit
   to empty[s];
-- 16 rescale warps: per chunk wait full[s]; per group of GB blocks wait
+- the rescale warps (4, 8 or 16 by token tile): per chunk wait full[s]; per group of GB blocks wait
   tfull[buf] of each block in order (parity use & 1) and read the buffer,
   then arrive tempty[buf] of each; after the chunk arrive empty[s].
 mbarrier model: a phase completes when its pending arrivals reach zero and
@@ -21,7 +21,7 @@ thread issued before it has completed.  Checked: no deadlock; a stage is read
 (by an MMA or for its scales) only while it holds the chunk the reader
 expects; a copy never lands in a stage an unfinished reader still uses; a
 TMEM buffer is read only while it holds the expected block and is never
-overwritten before all 16 warps read it.
+overwritten before every rescale warp read it.
 """
 import random
 
@@ -71,15 +71,15 @@ class Bar:
         return (self.phase & 1) != parity
 
 
-def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1):
+def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1, epi=EPI):
     """One replay (gb: blocks per rescale group); skip_tempty_wait plants a
     protocol bug (in the model) for the negative test."""
     rng = random.Random(seed)
     mdl = Model()
     full = [Bar(mdl, 1) for _ in range(ns)]
-    empty = [Bar(mdl, 1 + EPI) for _ in range(ns)]
+    empty = [Bar(mdl, 1 + epi) for _ in range(ns)]
     tfull = [Bar(mdl, 1) for _ in range(nb)]
-    tempty = [Bar(mdl, EPI) for _ in range(nb)]
+    tempty = [Bar(mdl, epi) for _ in range(nb)]
     stage = [None] * ns        # chunk whose two copies have landed in stage s
     landed = [0] * ns
     readers = [set() for _ in range(ns)]  # unfinished readers of the stage's chunk
@@ -133,7 +133,7 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1):
             mdl.bump()
             yield
 
-    def epi(w):
+    def rescale(w):
         blk = 0
         for c in range(nchunks):
             s = c % ns
@@ -173,7 +173,7 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1):
             blk, buf, s = issued[done[0]]
             assert unread[buf] == 0, "MMA result overwrites an unread buffer"
             tmem[buf] = blk
-            unread[buf] = EPI
+            unread[buf] = epi
             readers[s].discard(("mma", blk))
             done[0] += 1
             mdl.bump()
@@ -190,7 +190,7 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1):
             bar.arrive()
 
     roles = {0: producer(), 1: mma()}
-    roles.update({2 + w: epi(w) for w in range(EPI)})
+    roles.update({2 + w: rescale(w) for w in range(epi)})
     idle = 0
     while roles or copies or commits or done[0] < len(issued):
         v = mdl.version
@@ -214,12 +214,13 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1):
 # (stages, TMEM buffers, blocks per rescale group): the kernel's pairs are
 # NB = 32 / 16 / 8 / 4 buffers with groups of 4 / 4 / 2 / 1 blocks at 16 /
 # 32 / 64 / 128 tokens; smaller rings and buffer counts stress the waits
-@pytest.mark.parametrize("ns,nb,gb", [(1, 4, 1), (2, 4, 2), (3, 8, 4), (5, 4, 1), (7, 4, 2),
-                                      (8, 8, 4), (8, 32, 4), (8, 16, 4), (8, 8, 2), (6, 4, 1)])
-def test_gemm_barrier_protocol(ns, nb, gb):
+@pytest.mark.parametrize("ns,nb,gb,epi", [(1, 4, 1, 16), (2, 4, 2, 16), (3, 8, 4, 4), (5, 4, 1, 16),
+                                          (7, 4, 2, 8), (8, 8, 4, 4), (8, 32, 4, 4), (8, 16, 4, 8),
+                                          (8, 8, 2, 16), (6, 4, 1, 16)])
+def test_gemm_barrier_protocol(ns, nb, gb, epi):
     for trial in range(30):
         nchunks = random.Random(trial).randint(1, 3 * ns + 5)
-        run(ns, nb, nchunks, seed=ns * 1000 + nb * 100 + gb * 10 + trial, gb=gb)
+        run(ns, nb, nchunks, seed=ns * 1000 + nb * 100 + gb * 10 + trial, gb=gb, epi=epi)
 
 
 def test_model_catches_a_parity_slip():

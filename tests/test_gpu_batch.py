@@ -34,14 +34,20 @@ def _topk(logits, k):
     return order, logits[order]
 
 
-@pytest.mark.parametrize("name,lens,ctx,kv", [
-    ("tiny-g3", [1, 5, 40, 90], 128, 0),
-    ("small", [3, 17, 100, 300, 511 - 4], 512, 0),
-    ("mid", [2, 255, 256, 600], 1024, 0),
-    ("small", [7, 120, 260], 512, 1),
+@pytest.mark.parametrize("name,lens,ctx,kv,split", [
+    ("tiny-g3", [1, 5, 40, 90], 128, 0, ""),
+    ("small", [3, 17, 100, 300, 511 - 4], 512, 0, ""),
+    ("mid", [2, 255, 256, 600], 1024, 0, ""),
+    ("small", [7, 120, 260], 512, 1, ""),
+    # attention splits of 512 positions (the host picks longer splits when
+    # the sessions' positions fill several waves of CTAs)
+    ("mid", [2, 511, 512, 600], 1024, 0, "512"),
 ])
-def test_batch_step_matches_single_session(gpu_lib, oracle_mod, name, lens, ctx, kv):
+def test_batch_step_matches_single_session(gpu_lib, oracle_mod, monkeypatch, name, lens, ctx, kv,
+                                           split):
     import synthetic
+    if split:
+        monkeypatch.setenv("L3G_BD_SPLIT", split)
     cfg, T = synthetic_model(name)
     # the reference builds' own spread on the longest session's last tokens
     longest = int(np.argmax(lens))
