@@ -101,15 +101,17 @@ static __global__ void k_bd_qkv_rope(const float* QKV, int n, const SeqInfo* seq
 // Split-K decode attention (infer.go:130-175) of every sequence: CTA (split,
 // kv head, sequence) covers positions [split * split_len, ...) up to the
 // sequence's own position (split_len a multiple of BD_SPLIT, chosen per step
-// by the host so that the grid holds a few waves of CTAs).  A producer warp streams the split's cache rows
-// (K | V of 32 positions, contiguous in the cache) into a ring of BD_STAGES
-// shared-memory stages with 1-D bulk copies; compute warp w takes positions
-// w, w + 8, w + 16, w + 24 of every 32-position tile (so across the split it
-// visits split start + w + 8i in order), lane = dims j*32 + lane.  Per query
-// row of the kv head's group a warp keeps an online softmax (max, sum,
-// weighted V); the 8 warps merge in shared memory and the CTA writes one
-// partial (max, sum, o[HD]) per query head, merged across splits by
-// k_bd_merge.  Every wait is bounded; after an abort the CTA drains its
+// by the host so that the grid holds a few waves of CTAs).  A producer warp
+// streams the split's cache rows (K | V of 32 positions, contiguous in the
+// cache) into a ring of BD_STAGES shared-memory stages with 1-D bulk copies.
+// Compute warp w takes positions 4w..4w+3 of every 32-position tile: the
+// partial dot products of its (position, query row) pairs (lane = dims
+// lane * DPL..; 8 row slots per position) are reduced together by one
+// transposed reduction (31 shuffles for 32 slots), then each lane holds
+// one pair's score and the online softmax per query row (max, sum,
+// weighted V) runs on those.  The 8 warps merge
+// in shared memory and the CTA writes one partial (max, sum, o[HD]) per
+// query head, merged across splits by k_bd_merge.  Every wait is bounded; after an abort the CTA drains its
 // copies and writes nothing.
 constexpr int BD_SPLIT = 256;  // split lengths are multiples of this
 constexpr int BD_TILE = 32;    // positions per ring stage
@@ -122,11 +124,14 @@ struct BdSmem {
   float m[8][MAXG], l[8][MAXG];
 };
 __host__ __device__ constexpr int bd_stage_bytes(int hd, int es) { return BD_TILE * 2 * hd * es; }
-// the merge buffer (8 warps x GP rows x hd floats) reuses the ring
+// the merge buffer (8 warps x GP rows x hd floats) reuses the ring; after
+// it, each compute warp's sub-batch weights [32] and head statistics
+// [MAXG][4]
+constexpr int BD_WBUF = (8 * 32 + 8 * MAXG * 4) * 4;
 __host__ __device__ constexpr int bd_smem_bytes(int hd, int es, int gp) {
   return 1024 + (BD_STAGES * bd_stage_bytes(hd, es) > 8 * gp * hd * 4
                      ? BD_STAGES * bd_stage_bytes(hd, es)
-                     : 8 * gp * hd * 4);
+                     : 8 * gp * hd * 4) + BD_WBUF;
 }
 // GP: the group size rounded up to 1, 2, 4 or 8 (register arrays per row)
 template <int HD, int GP, typename KT>
@@ -141,6 +146,16 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
   BdSmem* sh = reinterpret_cast<BdSmem*>(bd_smem);
   uint8_t* ring = bd_smem + 1024;
   float(*sm_o)[GP][HD] = reinterpret_cast<float(*)[GP][HD]>(ring);  // after the ring drains
+  // sub-batches: every warp takes SBP = 4 positions of every tile, and their
+  // (position, query row) scores, 4 x 8 slots (rows beyond the group empty),
+  // are reduced together; all 8 warps share each tile, so a stage is
+  // consumed by one set of warps at a time and no wait can run two phases
+  // ahead of its barrier
+  constexpr int RS = 8;                 // row slots of the reduction
+  constexpr int SBP = 32 / RS;
+  static_assert(GP <= RS && SBP * 8 == BD_TILE, "sub-batch layout");
+  float* wbuf = reinterpret_cast<float*>(
+      ring + (BD_STAGES * SB > 8 * GP * HD * 4 ? BD_STAGES * SB : 8 * GP * HD * 4));
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const SeqInfo& sq = seqs[b];
   const int p0 = split * split_len;
@@ -178,6 +193,7 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
       *(volatile int*)&sh->producer_done = 1;
     }
   } else {
+    // lane = dims lane * DPL .. + DPL - 1 (K, V and q rows alike)
 #pragma unroll
     for (int g = 0; g < GP; ++g) {
       m[g] = -INFINITY;
@@ -186,43 +202,82 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
       for (int j = 0; j < DPL; ++j) {
         o[g][j] = 0.0f;
         q[g][j] = g < group ? Q[(size_t)b * nq_heads * HD + (size_t)(kvh * group + g) * HD +
-                                j * 32 + lane]
+                                lane * DPL + j]
                             : 0.0f;
       }
     }
+    float* pbuf = wbuf + warp * 32;
+    float* hbuf = wbuf + 8 * 32 + warp * MAXG * 4;
+    const int my_h = lane % RS, my_p = lane / RS;  // after the transposed reduction
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % BD_STAGES;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&sh->full[s], (t / BD_STAGES) & 1,
                                                         &sh->abort_flag, res, 31, wait_ns));
       if (!ok) break;
       const KT* tile = reinterpret_cast<const KT*>(ring + (size_t)s * SB);
-      const int q0 = p0 + t * BD_TILE;
+      const int cnt = min(BD_TILE, p1 - (p0 + t * BD_TILE));  // positions in this tile
+      const int pb = warp * SBP;                               // the warp's first position
+      // partial dots of (position, row), then one transposed reduction
+      float v[32];
 #pragma unroll
-      for (int i = 0; i < BD_TILE / 8; ++i) {
-        const int pi = warp + 8 * i;  // position within the tile
-        if (q0 + pi >= p1) break;     // warp-uniform
-        const KT* kr = tile + (size_t)pi * 2 * HD;
-        float kf[DPL], vf[DPL];
+      for (int p = 0; p < SBP; ++p) {
+        float kf[DPL];
+        if (pb + p < cnt) {
+          load_row<DPL, KT>(tile + (size_t)(pb + p) * 2 * HD + lane * DPL, kf);
+        } else {
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-          kf[j] = (float)kr[j * 32 + lane];
-          vf[j] = (float)kr[HD + j * 32 + lane];
+          for (int j = 0; j < DPL; ++j) kf[j] = 0.0f;
         }
 #pragma unroll
-        for (int g = 0; g < GP; ++g) {
-          if (g >= group) break;  // uniform
+        for (int g = 0; g < RS; ++g) {
           float d = 0.0f;
+          if (g < GP) {
 #pragma unroll
-          for (int j = 0; j < DPL; ++j) d = fmaf(q[g][j], kf[j], d);
-          d = warp_sum(d);
-          const float sc = __fmul_rn(d, scale);
-          const float mn = fmaxf(m[g], sc);
-          const float corr = expf(m[g] - mn);  // 0 while m is -inf
-          const float pe = expf(sc - mn);
-          l[g] = fmaf(l[g], corr, pe);
+            for (int j = 0; j < DPL; ++j) d = fmaf(q[g][j], kf[j], d);
+          }
+          v[p * RS + g] = d;
+        }
+      }
+      const float dot = transpose_reduce32(v, lane);
+      const bool valid = pb + my_p < cnt && my_h < group;
+      const float sc = valid ? __fmul_rn(dot, scale) : -INFINITY;
+      // per-row maximum and sum over the sub-batch's positions
+      float mb = sc;
 #pragma unroll
-          for (int j = 0; j < DPL; ++j) o[g][j] = fmaf(pe, vf[j], o[g][j] * corr);
-          m[g] = mn;
+      for (int off = RS; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+      float mo = -INFINITY;
+#pragma unroll
+      for (int g = 0; g < GP; ++g)
+        if (g == my_h) mo = m[g];
+      const float mn = fmaxf(mo, mb);
+      const float pe = valid ? expf(sc - mn) : 0.0f;
+      const float corr = mn == -INFINITY ? 1.0f : expf(mo - mn);
+      float lb = pe;
+#pragma unroll
+      for (int off = RS; off < 32; off <<= 1) lb += __shfl_xor_sync(0xffffffffu, lb, off);
+      pbuf[lane] = pe;
+      if (lane < GP) {
+        hbuf[lane * 4 + 0] = mn;
+        hbuf[lane * 4 + 1] = corr;
+        hbuf[lane * 4 + 2] = lb;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int g = 0; g < GP; ++g) {
+        const float c = hbuf[g * 4 + 1];
+        m[g] = hbuf[g * 4 + 0];
+        l[g] = fmaf(l[g], c, hbuf[g * 4 + 2]);
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) o[g][j] *= c;
+      }
+      for (int p = 0; p < SBP && pb + p < cnt; ++p) {
+        float vf[DPL];
+        load_row<DPL, KT>(tile + (size_t)(pb + p) * 2 * HD + HD + lane * DPL, vf);
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+          const float w = pbuf[p * RS + g];
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) o[g][j] = fmaf(w, vf[j], o[g][j]);
         }
       }
       __syncwarp();
@@ -253,7 +308,7 @@ __global__ void __launch_bounds__(BD_THREADS) k_bd_attention(
         sh->l[warp][g] = l[g];
       }
 #pragma unroll
-      for (int j = 0; j < DPL; ++j) sm_o[warp][g][j * 32 + lane] = o[g][j];
+      for (int j = 0; j < DPL; ++j) sm_o[warp][g][lane * DPL + j] = o[g][j];
     }
   }
   __syncthreads();
