@@ -158,8 +158,14 @@ __device__ __forceinline__ float merge_split_block(const float* ml, const float*
   return __fmul_rn(O, __fdiv_rn(1.0f, L));
 }
 
+// At most 128 registers a thread: with the matvec kernels' (at most 96) an
+// attention CTA and a matvec CTA fit on one SM together (9 warps each,
+// 36,864 + 27,648 of the 65,536 registers; about 99 + 112 KB of shared
+// memory), so the attention CTAs become resident, and stream the K|V
+// stages of past positions, while the QKV matvec still runs, and the Wo
+// matvec's CTAs load their first weight tiles while attention runs.
 template <int DPL, typename KT, int GP, bool CL>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __maxnreg__(128)
     k_attention(const __grid_constant__ AttnArgs a) {
   constexpr int SB = 32 / GP;  // positions per sub-batch
   L3G_DYNAMIC_SMEM(smem);

@@ -466,7 +466,7 @@ extern "C" int l3g_prefill_batched(l3g_model* m, l3g_state* s, l3g_workspace* ws
     CUDA_TRY(cudaStreamSynchronize(ws->stream));
     if (ws->h_res->err) {
       const int code = ws->h_res->err, where = ws->h_res->where;
-      cudaMemset(ws->d_res, 0, sizeof(Result));
+      ws_clear_device_error(ws);
       return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d (%s)", code, where,
                       code == ERR_TIMEOUT ? "bounded wait ran out" : "bad input");
     }

@@ -61,6 +61,11 @@ struct MatvecArgs {
   const float* rope_sin;
   const int* io;          // io[0] token, io[1] position
   KvMap kv;               // the state's KV cache; this layer's rows are written
+  // EPI_SWIGLU: Q8_0 quantization of the output fused behind the epilogue
+  // (q_cnt null: not fused, the output is quantized by a separate launch)
+  float* q_d;             // [rows / 64] block scales
+  int8_t* q_qs;           // [rows / 2] int8 values
+  unsigned* q_cnt;        // [rows / 64] arrivals per block, zero between launches
   // EPI_LOGITS: fused argmax
   int row_offset;         // vocab id of local row 0
   float* am_val;          // [gridDim.x] per-CTA best
@@ -279,6 +284,46 @@ __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int n
   }
 }
 
+// Act-quant of the SwiGLU output (QuantizeQ8_0Into, infer.go:233-234) fused
+// behind the epilogue of row group g, the CTA's k-th: the group holds act
+// values [g * wr / 2, (g + 1) * wr / 2).  With `count` (every warp ran the
+// epilogue of its own rows) the last of the CTA's warps to get here, by a
+// shared-memory count, goes on; otherwise the caller alone wrote the group.
+// A group of 32 or more values holds whole Q8_0 blocks and quantizes them at
+// once.  A smaller group adds one to its block's counter in global memory;
+// whoever completes the block, in this CTA or another, reads its 32 values
+// back and quantizes them (quant_block, as k_quantize does), then zeroes the
+// counter for the next launch.  Ordering: each warp's act stores come
+// before its CTA-scope acquire-release count (__syncwarp first), so the
+// warp that completes the group follows every warp's stores; its
+// device-scope acquire-release add on the block's counter publishes them
+// and, for the warp that completes the block, acquires the other groups'.
+__device__ __forceinline__ void mv_swiglu_quant(const MatvecArgs& a, MatvecSmem* sh, int k,
+                                                int g, int lane, bool count) {
+  __syncwarp();
+  if (count) {
+    int last = 0;
+    if (lane == 0)
+      last = atom_add_acq_rel_cta_shared(reinterpret_cast<unsigned*>(&sh->cnt[k % RED_SLOTS]),
+                                         1u) == (unsigned)(NW - 1);
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
+    if (lane == 0) sh->cnt[k % RED_SLOTS] = 0;  // its next use is RED_SLOTS groups later
+  }
+  const int n = a.w.rows >> 1;   // act values
+  const int per = a.w.wr >> 1;   // act values per group
+  if (per >= 32) {
+    for (int blk = g * per / 32; blk < (g + 1) * per / 32 && blk * 32 < n; ++blk)
+      quant_block(__ldcg(a.out + blk * 32 + lane), blk, lane, a.q_d, a.q_qs);
+    return;
+  }
+  const int blk = g * per / 32;
+  int done = 0;
+  if (lane == 0) done = atom_add_acq_rel_gpu(a.q_cnt + blk, 1u) == (unsigned)(32 / per - 1);
+  if (!__shfl_sync(0xffffffffu, done, 0)) return;
+  quant_block(__ldcg(a.out + blk * 32 + lane), blk, lane, a.q_d, a.q_qs);
+  if (lane == 0) a.q_cnt[blk] = 0u;
+}
+
 // Batch-1 Q8_0 matvec, out[r] = sum_b d_w[r,b]*d_x[b] * sum_i q_w[r,b,i]*q_x[b,i]
 // (matvec_q8_c, simd.c:33-110), with a fused prologue producing the int8
 // activation and a fused epilogue consuming the row results.
@@ -425,6 +470,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
       }
       if constexpr (RPW >= 2) {
         mv_epilogue<EPI>(a, g * wr + warp * RPW, RPW, v, lane, best_v, best_i, push_off, push_e);
+        if constexpr (EPI == EPI_SWIGLU)
+          if (a.q_cnt) mv_swiglu_quant(a, sh, k, g, lane, true);
       } else {
         const int slot = k % RED_SLOTS;
         int old = 0;
@@ -440,6 +487,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
           __syncwarp();
           if (lane == 0) sh->cnt[slot] = 0;
           mv_epilogue<EPI>(a, g * wr, NW, vv, lane, best_v, best_i, push_off, push_e);
+          if constexpr (EPI == EPI_SWIGLU)
+            if (a.q_cnt) mv_swiglu_quant(a, sh, k, g, lane, false);
         }
       }
     }

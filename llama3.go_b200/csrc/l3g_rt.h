@@ -221,6 +221,7 @@ struct l3g_workspace {
   float* part_o = nullptr;
   float* part_ml = nullptr;
   unsigned* att_cnt = nullptr;
+  unsigned* act_cnt = nullptr; // [ff_l / 32] arrivals per Q8_0 block of the SwiGLU output
   float* am_val = nullptr;
   int* am_idx = nullptr;
   unsigned* am_cnt = nullptr;
@@ -229,6 +230,7 @@ struct l3g_workspace {
   float* d_tk_logits = nullptr;
   int* h_tk_ids = nullptr;
   float* h_tk_logits = nullptr;
+  int att_cnt_n = 0, act_cnt_n = 0;  // entries of att_cnt, act_cnt
   int n_splits = 1, att_P = 16, att_ns = 3, att_stage = 0, att_smem = 0, att_gp = 1;
   int att_cluster = 0;         // > 0: the splits of a kv head form one cluster
   unsigned* d_step = nullptr;  // steps run (advanced by k_embed)
@@ -295,7 +297,10 @@ int upload_tiled(DevMat& out, const RowSrc* segs, int nseg, bool interleave2, in
                  int blk0, int cols, int nsm, size_t* dev_bytes, int rpw = 0);  // l3g_model.cu
 void free_mat(DevMat& m);                             // l3g_model.cu
 void free_gemm(GemmMat& g);                           // l3g_model.cu
-void ws_release(l3g_workspace* ws);                   // l3g_step.cu
+void ws_release(l3g_workspace* ws);
+// After a step reported a device error: clears the result word and every
+// last-arriver counter an aborted kernel may have left mid-count.
+void ws_clear_device_error(l3g_workspace* ws);                   // l3g_step.cu
 void ws_detach(l3g_workspace* ws);                    // l3g_step.cu: releases its graphs, forgets the model
 int tp_setup(l3g_workspace* ws);                      // l3g_tp.cu
 TpExchange tp_exchange(const l3g_workspace* ws, int phase);  // l3g_tp.cu

@@ -112,7 +112,7 @@ void ws_release(l3g_workspace* ws) {
     if (p) cudaFree(p);
   void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
                    ws->attn, ws->act, ws->attn_d, ws->attn_q, ws->act_d, ws->act_q, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
-                   ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
+                   ws->att_cnt, ws->act_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
                    ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens, ws->d_trace, ws->d_samp};
   for (void* p : dptrs)
     if (p) cudaFree(p);
@@ -125,6 +125,13 @@ void ws_release(l3g_workspace* ws) {
   for (void* p : hptrs)
     if (p) cudaFreeHost(p);
   if (ws->stream) cudaStreamDestroy(ws->stream);
+}
+
+void ws_clear_device_error(l3g_workspace* ws) {
+  cudaMemset(ws->d_res, 0, sizeof(Result));
+  if (ws->att_cnt) cudaMemset(ws->att_cnt, 0, (size_t)ws->att_cnt_n * 4);
+  if (ws->act_cnt) cudaMemset(ws->act_cnt, 0, (size_t)ws->act_cnt_n * 4);
+  if (ws->am_cnt) cudaMemset(ws->am_cnt, 0, 4);
 }
 
 void ws_detach(l3g_workspace* ws) {
@@ -260,7 +267,10 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   const int part_splits = std::max(ws->n_splits, std::max(1, m->nsm / m->hkv_l));
   DM(ws->part_o, (size_t)m->hkv_l * part_splits * G * hd * 4);
   DM(ws->part_ml, (size_t)m->hkv_l * part_splits * G * 2 * 4);
-  DM(ws->att_cnt, (size_t)m->hkv_l * 2 * 4);  // arrivals, departures
+  ws->att_cnt_n = m->hkv_l * 2;  // arrivals, departures
+  DM(ws->att_cnt, (size_t)ws->att_cnt_n * 4);
+  ws->act_cnt_n = std::max(1, m->ff_l / 32);
+  DM(ws->act_cnt, (size_t)ws->act_cnt_n * 4);
   DM(ws->am_val, (size_t)m->nsm * 4);
   DM(ws->am_idx, (size_t)m->nsm * 4);
   DM(ws->am_cnt, 4);
@@ -280,7 +290,8 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
 #undef DM
 #undef HM
   if (e == cudaSuccess) e = cudaMemset(ws->d_res, 0, sizeof(Result));
-  if (e == cudaSuccess) e = cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 2 * 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->att_cnt, 0, (size_t)ws->att_cnt_n * 4);
+  if (e == cudaSuccess) e = cudaMemset(ws->act_cnt, 0, (size_t)ws->act_cnt_n * 4);
   if (e == cudaSuccess) e = cudaMemset(ws->am_cnt, 0, 4);
   if (e == cudaSuccess) e = cudaMemset(ws->x[0], 0, ne * 4);
   if (e == cudaSuccess) e = cudaMemset(ws->x[1], 0, ne * 4);
@@ -641,15 +652,15 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.x_out = ws->x[0];
       a.eps = hp.rms_eps;
       a.out = ws->act;
+      // act-quant of the SwiGLU output fused behind the epilogue (each Q8_0
+      // block once, by whichever warp completes it), infer.go:233-234
+      a.q_d = ws->act_d;
+      a.q_qs = ws->act_q;
+      a.q_cnt = ws->act_cnt;
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
       KL(L3G_K_UPGATE, (launch_mv<PRO_RMS, EPI_SWIGLU>(L.upgate, a, m->nsm, st)));
-    }
-    {  // act-quant of the SwiGLU output (once, not per CTA), infer.go:233-234
-      const int nb = m->ff_l / 32;
-      KL(L3G_K_ACT_QUANT, launch(k_quantize, dim3((nb + NW - 1) / NW), dim3(NW * 32), 0, st,
-                                 (const float*)ws->act, m->ff_l, ws->act_d, ws->act_q));
     }
     {  // down, infer.go:235-242
       MatvecArgs a = mv_args(L.down);
@@ -804,10 +815,7 @@ static int run_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int32_t token
   CUDA_TRY(cudaStreamSynchronize(ws->stream));
   if (ws->h_res->err) {
     const int code = ws->h_res->err, where = ws->h_res->where;
-    cudaMemset(ws->d_res, 0, sizeof(Result));
-    // an aborted kernel may have left its last-CTA counters mid-count
-    cudaMemset(ws->att_cnt, 0, (size_t)m->hkv_l * 2 * 4);
-    cudaMemset(ws->am_cnt, 0, 4);
+    ws_clear_device_error(ws);
     ws->logits_valid = false;
     return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d (%s)", code, where,
                     code == ERR_TIMEOUT ? "bounded wait ran out" : "bad input");
@@ -903,7 +911,7 @@ extern "C" int l3g_decode_greedy(l3g_model* m, l3g_state* s, l3g_workspace* ws,
   if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "greedy decode: %s", cudaGetErrorString(e));
   if (ws->h_res->err) {
     const int code = ws->h_res->err, where = ws->h_res->where;
-    cudaMemset(ws->d_res, 0, sizeof(Result));
+    ws_clear_device_error(ws);
     return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d", code, where);
   }
   if (device_ms) *device_ms = ms;
@@ -986,7 +994,7 @@ extern "C" int l3g_decode_sample(l3g_model* m, l3g_state* s, l3g_workspace* ws,
   if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "sampled decode: %s", cudaGetErrorString(e));
   if (ws->h_res->err) {
     const int code = ws->h_res->err, where = ws->h_res->where;
-    cudaMemset(ws->d_res, 0, sizeof(Result));
+    ws_clear_device_error(ws);
     return l3g_fail(L3G_E_DEVICE, "device check failed: code %d at site %d", code, where);
   }
   ws->draws += (uint64_t)n;
@@ -1050,7 +1058,7 @@ extern "C" int l3g_profile_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, i
   if (rc) return rc;
   if (e != cudaSuccess) return l3g_fail(L3G_E_CUDA, "profile step: %s", cudaGetErrorString(e));
   if (ws->h_res->err) {
-    cudaMemset(ws->d_res, 0, sizeof(Result));
+    ws_clear_device_error(ws);
     return l3g_fail(L3G_E_DEVICE, "device check failed during profiling");
   }
   *n = std::min(cnt, *n);
@@ -1084,7 +1092,7 @@ extern "C" int l3g_trace_step(l3g_model* m, l3g_state* s, l3g_workspace* ws, int
   CUDA_TRY(cudaMemcpyAsync(ws->h_res, ws->d_res, sizeof(Result), cudaMemcpyDeviceToHost, ws->stream));
   CUDA_TRY(cudaStreamSynchronize(ws->stream));
   if (ws->h_res->err) {
-    cudaMemset(ws->d_res, 0, sizeof(Result));
+    ws_clear_device_error(ws);
     return l3g_fail(L3G_E_DEVICE, "device check failed during trace");
   }
   const int out_n = std::min(cnt, *n);

@@ -785,6 +785,59 @@ int emu_matvec(const uint8_t* tiles, int rows, int cols, int rpw, const float* x
   });
 }
 
+// k_matvec with a fused epilogue on a pre-quantized activation, grid CTAs:
+//  epi 2 (EPI_SWIGLU): rows interleave (up_i, gate_i), out[i] = silu(gate_i)
+//    * up_i; with q_cnt non-null the output's Q8_0 quantization is fused
+//    (q_d, q_qs, per-block counters q_cnt) as the decode step runs it;
+//  epi 3 (EPI_LOGITS): out[r] (or no store when out is null) and the argmax
+//    through per-CTA slots am_val / am_idx and the arrival counter
+//    am_counter, into *result (index, value, status, detail), as
+//    l3g_matvec_q8_argmax_static runs it on its static scratch.
+int emu_matvec_epi(const uint8_t* tiles, int rows, int cols, int rpw, const float* xd,
+                   const int8_t* xq, float* out, int epi, float* q_d, int8_t* q_qs,
+                   unsigned* q_cnt, float* am_val, int* am_idx, unsigned* am_counter,
+                   int* result, int grid) {
+  return guarded_call([&] {
+    using namespace l3g;
+    const TileGeom g = tile_geometry(rows, cols, rpw, NW, TILE_TARGET);
+    MatvecArgs a{};
+    a.w = Q8Tiles{tiles, rows, cols, g.wr, g.ck, g.nslices, g.tile_bytes, g.n_groups};
+    const int fixed = mv_smem_bytes(cols, 0, g.tile_bytes);
+    a.nstages = std::max(2, std::min(MAX_STAGES, (CTA_SMEM_SHARE - fixed) / g.tile_bytes));
+    const size_t smem = mv_smem_bytes(cols, a.nstages, g.tile_bytes);
+    a.row_lo = 0;
+    a.row_hi = rows;
+    a.xd_in = xd;
+    a.xqs_in = xq;
+    a.out = out;
+    a.q_d = q_d;
+    a.q_qs = q_qs;
+    a.q_cnt = q_cnt;
+    a.am_val = am_val;
+    a.am_idx = am_idx;
+    a.am_counter = am_counter;
+    a.res = reinterpret_cast<Result*>(result);
+    a.wait_ns = WAIT_TIMEOUT_NS;
+    auto go = [&](auto r_c, auto e_c) {
+      constexpr int R = decltype(r_c)::value;
+      constexpr int E = decltype(e_c)::value;
+      simt::launch(dim3(grid), dim3(NTHREADS), smem, [&] { k_matvec<PRO_PREQ, E, R, 1>(a); });
+    };
+    auto by_rpw = [&](auto e_c) {
+      switch (rpw) {
+        case 1: go(std::integral_constant<int, 1>{}, e_c); break;
+        case 2: go(std::integral_constant<int, 2>{}, e_c); break;
+        case 4: go(std::integral_constant<int, 4>{}, e_c); break;
+        case 8: go(std::integral_constant<int, 8>{}, e_c); break;
+        default: simt::fail("rows per warp");
+      }
+    };
+    if (epi == EPI_SWIGLU) by_rpw(std::integral_constant<int, EPI_SWIGLU>{});
+    else if (epi == EPI_LOGITS) by_rpw(std::integral_constant<int, EPI_LOGITS>{});
+    else simt::fail("epilogue");
+  });
+}
+
 // The decode step's split-K attention (k_attention, global merge through
 // partials in device memory, the CTAs of a kv head waiting on each other's
 // arrival counters) for one layer, set up as l3g_workspace_new and
