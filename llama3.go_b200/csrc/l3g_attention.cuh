@@ -165,7 +165,7 @@ __device__ __forceinline__ float merge_split_block(const float* ml, const float*
 // stages of past positions, while the QKV matvec still runs, and the Wo
 // matvec's CTAs load their first weight tiles while attention runs.
 template <int DPL, typename KT, int GP, bool CL>
-__global__ void __maxnreg__(128)
+__global__ void __maxnreg__(96)
     k_attention(const __grid_constant__ AttnArgs a) {
   constexpr int SB = 32 / GP;  // positions per sub-batch
   L3G_DYNAMIC_SMEM(smem);

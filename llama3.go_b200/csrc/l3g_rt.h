@@ -222,6 +222,12 @@ struct l3g_workspace {
   float* part_ml = nullptr;
   unsigned* att_cnt = nullptr;
   unsigned* act_cnt = nullptr; // [ff_l / 32] arrivals per Q8_0 block of the SwiGLU output
+  // even tile ranges of the step's matvecs: partial rows of the row groups
+  // that CTAs share, and their counts (null: round-robin row groups)
+  float* sk_part = nullptr;
+  unsigned* sk_cnt = nullptr;
+  size_t sk_cnt_n = 0;
+  bool fuse_act_quant = true;  // SwiGLU act-quant inside up/gate when it runs on even tile ranges
   float* am_val = nullptr;
   int* am_idx = nullptr;
   unsigned* am_cnt = nullptr;

@@ -667,6 +667,10 @@ template <typename T>
 inline T __ldg(const T* p) {
   return *p;
 }
+template <typename T>
+inline void __stcg(T* p, T v) {
+  *p = v;
+}
 
 // atomics: every atomic is a point where another thread may run first
 template <typename T>

@@ -192,7 +192,7 @@ def test_static_argmax_merge_under_the_emulator(oracle_mod, rpw):
             res = S.Dev(np.array([-1, 0, 0, 0], np.int32))
             S.check(S.lib().emu_matvec_epi(tiles.ptr, rows, cols, rpw, xd.ptr, xq.ptr,
                                            out.ptr if i % 2 == 0 else None, 3, None, None, None,
-                                           am_val.ptr, am_idx.ptr, counter.ptr, res.ptr, grid))
+                                           am_val.ptr, am_idx.ptr, counter.ptr, res.ptr, grid, 0, None))
             r = res.read(np.int32)
             assert r[0] == 130 and r[2] == 0, (grid, r)
             v = r[1:2].view(np.float32)[0]
