@@ -158,14 +158,13 @@ __device__ __forceinline__ float merge_split_block(const float* ml, const float*
   return __fmul_rn(O, __fdiv_rn(1.0f, L));
 }
 
-// At most 128 registers a thread: with the matvec kernels' (at most 96) an
-// attention CTA and a matvec CTA fit on one SM together (9 warps each,
-// 36,864 + 27,648 of the 65,536 registers; about 99 + 112 KB of shared
-// memory), so the attention CTAs become resident, and stream the K|V
-// stages of past positions, while the QKV matvec still runs, and the Wo
-// matvec's CTAs load their first weight tiles while attention runs.
+// One CTA per SM (the registers of one attention CTA leave no room for a
+// matvec CTA beside it).  Capping the registers so that an attention CTA
+// and a matvec CTA share an SM was measured slower: the early K|V stream
+// then competes with the QKV matvec's prologue and weight stream and every
+// kernel of the layer slows down.
 template <int DPL, typename KT, int GP, bool CL>
-__global__ void __maxnreg__(96)
+__global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ AttnArgs a) {
   constexpr int SB = 32 / GP;  // positions per sub-batch
   L3G_DYNAMIC_SMEM(smem);
