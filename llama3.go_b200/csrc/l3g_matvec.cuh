@@ -314,7 +314,7 @@ __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int n
 // group or block follows every contributing warp's stores, at CTA scope for
 // a CTA-local block and at device scope otherwise; a __syncwarp after the
 // broadcast of its result orders every lane's loads after it.
-__device__ __forceinline__ void mv_swiglu_quant(const MatvecArgs& a, MatvecSmem* sh, int k,
+static __device__ __noinline__ void mv_swiglu_quant(const MatvecArgs& a, MatvecSmem* sh, int k,
                                                 int g, int lane, bool count, bool sk, int u0,
                                                 int ntiles) {
   __syncwarp();
@@ -371,7 +371,7 @@ __device__ __forceinline__ int sk_owner(long long u, int G, long long T) {
 // quantizes.  Ordering as in mv_swiglu_quant: __syncwarp before each
 // device-scope acquire-release count, and after the broadcast of its result.
 template <int EPI, int RPW>
-__device__ __forceinline__ void sk_finish(const MatvecArgs& a, MatvecSmem* sh, int gloc, int g,
+static __device__ __noinline__ void sk_finish(const MatvecArgs& a, MatvecSmem* sh, int gloc, int g,
                                           float v, int lane, int warp, float& best_v,
                                           int& best_i, size_t push_off, unsigned push_e) {
   const int nsl = a.w.nslices, wr = a.w.wr;
