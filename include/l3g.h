@@ -303,8 +303,7 @@ int l3g_workspace_tp_p2p(const l3g_workspace *ws, int32_t *p2p);
 #define L3G_K_DOWN 5
 #define L3G_K_LOGITS 6
 #define L3G_K_OTHER 7
-#define L3G_K_ACT_QUANT 8 /* act-quant of the SwiGLU output for down, when
-                             the up/gate kernel does not fuse it          */
+#define L3G_K_ACT_QUANT 8 /* act-quant of the SwiGLU output for down     */
 #define L3G_K_LAYERS 9    /* every layer in one persistent launch         */
 int l3g_profile_step(l3g_model *m, l3g_state *s, l3g_workspace *ws,
                      int32_t token, int32_t *kinds, float *us, int32_t *n);

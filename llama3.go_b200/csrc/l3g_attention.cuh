@@ -22,9 +22,9 @@
 //     (one or more Q8_0 blocks) reading the others' partials over
 //     distributed shared memory, then a second barrier keeps every CTA's
 //     shared memory alive until all reads are done;
-//   - otherwise through global partials: every CTA publishes its own, waits
-//     until all splits of its kv head have (they are all resident), and
-//     merges one slice of the outputs.
+//   - otherwise through global partials: every CTA publishes its own and
+//     the last of the kv head's CTAs to publish (an arrival counter) merges
+//     all of the head's outputs; the others leave at once.
 #pragma once
 
 struct AttnArgs {
@@ -474,45 +474,71 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     trace_mark(a.trace, a.trace_seq, TR_EXIT);
     return;
   }
-  // Publish this split's partial, then wait (bounded) until every split of
-  // this kv head has published: the grid has at most one CTA per SM, so all
-  // of them are resident.  Then each CTA merges its own slice of the G*hd
-  // outputs (whole Q8_0 blocks), reading every split's (m, l) and that
-  // slice of their partial outputs: one small gather per CTA instead of one
-  // CTA gathering everything.  counters[kvh] counts arrivals,
-  // counters[gridDim.x + kvh] departures; the last to depart resets both.
+  // Publish this split's partial; the last of the kv head's S splits to
+  // publish merges every output of the head, the others are done.  No CTA
+  // waits for another, so the grid need not be resident at once, and all
+  // but one CTA per kv head leave their SM at once (the next kernel's CTAs
+  // start loading there).  counters[kvh] counts arrivals; the last CTA
+  // zeroes it (the next launch's CTAs arrive only after this grid has
+  // completed).  Ordering: every thread's partial stores, the CTA barrier,
+  // thread 0's device-scope acquire-release add; the last arriver's
+  // acquire, then a CTA barrier before any thread reads the partials.
   consumer_sync();
   unsigned* arrived = a.counters + kvh;
-  unsigned* departed = a.counters + gridDim.x + kvh;
-  if (threadIdx.x == 0) {
-    atom_add_acq_rel_gpu(arrived, 1u);
-    const uint64_t t0 = gtime();
-    while (ld_acquire_gpu_u32(arrived) < (unsigned)S) {
-      if (gtime() - t0 > a.wait_ns) {
-        report(a.res, ERR_TIMEOUT, 9);
-        break;
-      }
-    }
-  }
+  if (threadIdx.x == 0)
+    *(volatile int*)&sh->last = atom_add_acq_rel_gpu(arrived, 1u) == (unsigned)S - 1;
   consumer_sync();
-  trace_mark(a.trace, a.trace_seq, 5);  // every split published
+  trace_mark(a.trace, a.trace_seq, 5);  // published
+  if (!*(volatile int*)&sh->last) {
+    trace_mark(a.trace, a.trace_seq, TR_EXIT);
+    return;
+  }
   const int gh = G * hd;
-  const int slice = align_up((gh + S - 1) / S, 32);  // outputs merged per CTA
-  const int b0 = min(gh, split * slice) / 32, b1 = min(gh, (split + 1) * slice) / 32;
-  float* wbuf = reinterpret_cast<float*>(ring) + warp * align_up(S, 32);  // e_s per warp
+  const int SP = align_up(S, 32);
+  float* wsm = reinterpret_cast<float*>(ring);  // [MAXG][SP] weights e_s, then [MAXG] sums
+  float* lsm = wsm + MAXG * SP;
   const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
   const float* po = a.part_o + (size_t)kvh * S * gh;
-  for (int blk = b0 + warp; blk < b1; blk += NW) {  // one warp per block of 32 outputs
-    const int h = blk * 32 / hd;
-    const float v = merge_split_block(ml, po, S, G, gh, h, blk * 32 + lane, lane, wbuf);
-    a.out[(size_t)kvh * gh + blk * 32 + lane] = v;
+  // per query head (one warp each): e_s = exp(m_s - max m) and L = sum l_s
+  // e_s, in the order merge_split_block takes them
+  for (int h = warp; h < G; h += NW) {
+    float M = -INFINITY;
+    for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
+    M = warp_max(M);
+    float L = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 32) {
+      const int s2 = s0 + lane;
+      float le = 0.0f;
+      if (s2 < S) {
+        const float2 p = __ldcg(reinterpret_cast<const float2*>(ml + ((size_t)s2 * G + h) * 2));
+        const float e = p.x == -INFINITY ? 0.0f : expf(p.x - M);
+        wsm[h * SP + s2] = e;
+        le = p.y * e;
+      }
+      L += warp_sum(le);
+    }
+    if (lane == 0) lsm[h] = L;
+  }
+  consumer_sync();
+  // one warp per block of 32 outputs: O = sum_s o_s e_s in split order,
+  // out = O / L, then the block's Q8_0 quantization for Wo
+  for (int blk = warp; blk < gh / 32; blk += NW) {
+    const int h = blk * 32 / hd, col = blk * 32 + lane;
+    const float* e = wsm + h * SP;
+    float O = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 32) {
+      float ov[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) ov[u] = s0 + u < S ? __ldcg(po + (size_t)(s0 + u) * gh + col) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 32; ++u)
+        if (s0 + u < S) O = fmaf(ov[u], e[s0 + u], O);
+    }
+    const float v = __fmul_rn(O, __fdiv_rn(1.0f, lsm[h]));
+    a.out[(size_t)kvh * gh + col] = v;
     quant_block(v, kvh * gh / 32 + blk, lane, a.out_d, a.out_q);
   }
-  trace_mark(a.trace, a.trace_seq, 7);  // slice merged
-  consumer_sync();
-  if (threadIdx.x == 0 && atom_add_acq_rel_gpu(departed, 1u) == (unsigned)S - 1) {
-    *arrived = 0u;
-    *departed = 0u;
-  }
+  trace_mark(a.trace, a.trace_seq, 7);  // merged
+  if (threadIdx.x == 0) *arrived = 0u;
   trace_mark(a.trace, a.trace_seq, TR_EXIT);
 }

@@ -61,19 +61,6 @@ struct MatvecArgs {
   const float* rope_sin;
   const int* io;          // io[0] token, io[1] position
   KvMap kv;               // the state's KV cache; this layer's rows are written
-  // EPI_SWIGLU: Q8_0 quantization of the output fused behind the epilogue
-  // (q_cnt null: not fused, the output is quantized by a separate launch)
-  float* q_d;             // [rows / 64] block scales
-  int8_t* q_qs;           // [rows / 2] int8 values
-  unsigned* q_cnt;        // [rows / 64] arrivals per block, zero between launches
-  // Even tile ranges (sk_part non-null; RPW >= 2, every CTA at least one
-  // tile): CTA b streams tiles [b*T/G, (b+1)*T/G) of the T = groups x slices
-  // tiles in storage order.  A row group whose slices several CTAs share is
-  // finished, per warp, by the last of them to post its partial rows, which
-  // sums the partials in CTA order and runs the epilogue.
-  float* sk_part;         // [groups][sk_maxc][wr] partial rows
-  unsigned* sk_cnt;       // [groups][NW + 1]: posts per warp, then warps finished; zero between launches
-  int sk_maxc;            // most CTAs sharing one group
   // EPI_LOGITS: fused argmax
   int row_offset;         // vocab id of local row 0
   float* am_val;          // [gridDim.x] per-CTA best
@@ -94,10 +81,7 @@ constexpr int RED_SLOTS = MAX_STAGES + 2;
 struct MatvecSmem {
   uint64_t full[MAX_STAGES];
   uint64_t empty[MAX_STAGES];
-  union {
-    float red[RED_SLOTS][NW];  // one row per warp (RPW == 1)
-    unsigned qloc[RED_SLOTS];  // the fused act-quant's CTA-local block counts (RPW >= 2)
-  };
+  float red[RED_SLOTS][NW];
   int cnt[RED_SLOTS];
   float ssred[NW];
   float best_v[NW];
@@ -295,124 +279,11 @@ __device__ __forceinline__ void mv_epilogue(const MatvecArgs& a, int row0, int n
   }
 }
 
-// Act-quant of the SwiGLU output (QuantizeQ8_0Into, infer.go:233-234) fused
-// behind the epilogue of row group g, the CTA's k-th: the group holds act
-// values [g * wr / 2, (g + 1) * wr / 2).  With `count` (every warp ran the
-// epilogue of its own rows) the last of the CTA's warps to get here, by a
-// shared-memory count, goes on; otherwise the caller alone wrote the group.
-// A group of 32 or more values holds whole Q8_0 blocks and quantizes them at
-// once.  A smaller group is part of a block:
-//  - under even tile ranges (u0, ntiles: this CTA's tiles) a block whose
-//    every group lies whole in this CTA's range is counted in shared memory
-//    (CTA scope only) and quantized by the warp that completes it;
-//  - otherwise the group adds one to the block's counter in global memory
-//    and whoever completes the block, in this CTA or another, quantizes it
-//    and zeroes the counter for the next launch.
-// The quantizing warp reads the block's 32 values back (quant_block, as
-// k_quantize does).  Ordering: each warp's act stores come before its
-// acquire-release count (__syncwarp first); the count that completes the
-// group or block follows every contributing warp's stores, at CTA scope for
-// a CTA-local block and at device scope otherwise; a __syncwarp after the
-// broadcast of its result orders every lane's loads after it.
-static __device__ __noinline__ void mv_swiglu_quant(const MatvecArgs& a, MatvecSmem* sh, int k,
-                                                int g, int lane, bool count, bool sk, int u0,
-                                                int ntiles) {
-  __syncwarp();
-  if (count) {
-    int last = 0;
-    if (lane == 0)
-      last = atom_add_acq_rel_cta_shared(reinterpret_cast<unsigned*>(&sh->cnt[k % RED_SLOTS]),
-                                         1u) == (unsigned)(NW - 1);
-    if (!__shfl_sync(0xffffffffu, last, 0)) return;
-    __syncwarp();  // lane 0's acquire comes before every lane's loads
-    if (lane == 0) sh->cnt[k % RED_SLOTS] = 0;  // its next use is RED_SLOTS groups later
-  }
-  const int n = a.w.rows >> 1;   // act values
-  const int per = a.w.wr >> 1;   // act values per group
-  if (per >= 32) {
-    for (int blk = g * per / 32; blk < (g + 1) * per / 32 && blk * 32 < n; ++blk)
-      quant_block(__ldcg(a.out + blk * 32 + lane), blk, lane, a.q_d, a.q_qs);
-    return;
-  }
-  const int gpb = 32 / per;      // groups per block
-  const int blk = g * per / 32;
-  const int gl = a.row_lo / a.w.wr;
-  const long long b0 = (long long)(blk * gpb - gl) * a.w.nslices;  // the block's first tile
-  const bool local = sk && b0 >= u0 && b0 + (long long)gpb * a.w.nslices <= (long long)u0 + ntiles;
-  int done = 0;
-  if (local) {
-    unsigned* c = &sh->qloc[blk % RED_SLOTS];
-    if (lane == 0) done = atom_add_acq_rel_cta_shared(c, 1u) == (unsigned)(gpb - 1);
-    if (!__shfl_sync(0xffffffffu, done, 0)) return;
-    __syncwarp();
-    if (lane == 0) *c = 0u;
-  } else {
-    if (lane == 0) done = atom_add_acq_rel_gpu(a.q_cnt + blk, 1u) == (unsigned)(gpb - 1);
-    if (!__shfl_sync(0xffffffffu, done, 0)) return;
-    __syncwarp();
-    if (lane == 0) a.q_cnt[blk] = 0u;
-  }
-  quant_block(__ldcg(a.out + blk * 32 + lane), blk, lane, a.q_d, a.q_qs);
-}
-
-// CTA of an even tile range that holds tile u: the c with
-// floor(c*T/G) <= u < floor((c+1)*T/G).
-__device__ __forceinline__ int sk_owner(long long u, int G, long long T) {
-  return (int)(((u + 1) * G - 1) / T);
-}
-
-// A row group whose tiles several CTAs share (even tile ranges): this warp
-// posts its RPW partial rows (lane r < RPW holds row r) as contributor
-// b - first; the last of the group's contributors to post for this warp
-// index sums the posts in contributor order (so the result does not depend
-// on arrival order), zeroes the count and runs the epilogue of the warp's
-// rows.  With the fused SwiGLU act-quant the group's NW finished warps are
-// counted in global memory (they may be in different CTAs); the last one
-// quantizes.  Ordering as in mv_swiglu_quant: __syncwarp before each
-// device-scope acquire-release count, and after the broadcast of its result.
-template <int EPI, int RPW>
-static __device__ __noinline__ void sk_finish(const MatvecArgs& a, MatvecSmem* sh, int gloc, int g,
-                                          float v, int lane, int warp, float& best_v,
-                                          int& best_i, size_t push_off, unsigned push_e) {
-  const int nsl = a.w.nslices, wr = a.w.wr;
-  const int G = (int)gridDim.x;
-  const long long T = (long long)((a.row_hi + wr - 1) / wr - a.row_lo / wr) * nsl;
-  const int first = sk_owner((long long)gloc * nsl, G, T);
-  const int nc = sk_owner((long long)gloc * nsl + nsl - 1, G, T) - first + 1;
-  float* part = a.sk_part + (size_t)gloc * a.sk_maxc * wr + warp * RPW;
-  if (lane < RPW) __stcg(part + (size_t)((int)blockIdx.x - first) * wr + lane, v);
-  __syncwarp();
-  unsigned* cnt = a.sk_cnt + (size_t)gloc * (NW + 1);
-  int last = 0;
-  if (lane == 0) last = atom_add_acq_rel_gpu(cnt + warp, 1u) == (unsigned)(nc - 1);
-  if (!__shfl_sync(0xffffffffu, last, 0)) return;
-  __syncwarp();
-  float sum = 0.0f;
-  if (lane < RPW) {
-    sum = __ldcg(part + lane);
-    for (int j = 1; j < nc; ++j) sum = __fadd_rn(sum, __ldcg(part + (size_t)j * wr + lane));
-  }
-  if (lane == 0) cnt[warp] = 0u;
-  mv_epilogue<EPI>(a, g * wr + warp * RPW, RPW, sum, lane, best_v, best_i, push_off, push_e);
-  if constexpr (EPI == EPI_SWIGLU) {
-    if (a.q_cnt) {
-      __syncwarp();
-      int done = 0;
-      if (lane == 0) done = atom_add_acq_rel_gpu(cnt + NW, 1u) == (unsigned)(NW - 1);
-      if (!__shfl_sync(0xffffffffu, done, 0)) return;
-      __syncwarp();
-      if (lane == 0) cnt[NW] = 0u;
-      mv_swiglu_quant(a, sh, 0, g, lane, false, false, 0, 0);
-    }
-  }
-}
-
 // Batch-1 Q8_0 matvec, out[r] = sum_b d_w[r,b]*d_x[b] * sum_i q_w[r,b,i]*q_x[b,i]
 // (matvec_q8_c, simd.c:33-110), with a fused prologue producing the int8
 // activation and a fused epilogue consuming the row results.
 //
-// Schedule: CTA b takes row groups b, b + grid, b + 2*grid, ..., or with
-// even tile ranges (sk_part set) tiles [b*T/G, (b+1)*T/G); a tile is
+// Schedule: CTA b takes row groups b, b + grid, b + 2*grid, ...; a tile is
 // ~32 KB (one bulk copy: the per-copy cost of the TMA path makes small copies
 // slow) and the ring holds ~3 of them.  Warp w owns rows [w*RPW, w*RPW+RPW)
 // of every tile, loads each activation chunk once for all of them, and
@@ -432,30 +303,19 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
   const int ns = a.nstages;
   const int wr = a.w.wr, ck = a.w.ck, nsl = a.w.nslices, tb = a.w.tile_bytes;
 
-  // row groups covering [row_lo, row_hi), dealt round-robin over the grid,
-  // or this CTA's even range [u0, u0 + ntiles) of their tiles
+  // row groups covering [row_lo, row_hi), dealt round-robin over the grid
   const int gl = a.row_lo / wr;
   const int ng = (a.row_hi + wr - 1) / wr - gl;
   const int G = (int)gridDim.x, b = (int)blockIdx.x;
-  const bool sk = RPW >= 2 && a.sk_part != nullptr;
-  int u0 = 0, ntiles;
-  if (sk) {
-    const long long T = (long long)ng * nsl;
-    u0 = (int)((long long)b * T / G);
-    ntiles = (int)((long long)(b + 1) * T / G) - u0;
-  } else {
-    ntiles = (b < ng ? (ng - b + G - 1) / G : 0) * nsl;
-  }
+  const int my_groups = b < ng ? (ng - b + G - 1) / G : 0;
+  const int ntiles = my_groups * nsl;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&sh->full[s], 1);
       mbar_init(&sh->empty[s], NW);
     }
-    for (int s = 0; s < RED_SLOTS; ++s) {
-      sh->cnt[s] = 0;
-      if (RPW >= 2) sh->qloc[s] = 0u;
-    }
+    for (int s = 0; s < RED_SLOTS; ++s) sh->cnt[s] = 0;
     sh->abort_flag = 0;
     sh->issued = 0;
     sh->producer_done = 0;
@@ -472,9 +332,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
         if (t >= ns &&
             !mbar_wait(&sh->empty[s], ((t / ns) - 1) & 1, &sh->abort_flag, a.res, 1, a.wait_ns))
           break;
-        const size_t tile = sk ? (size_t)gl * nsl + u0 + t
-                               : (size_t)(gl + b + (t / nsl) * G) * nsl + t % nsl;
-        const uint8_t* src = a.w.data + tile * tb;
+        const int g = gl + b + (t / nsl) * G;
+        const uint8_t* src = a.w.data + ((size_t)g * nsl + (t % nsl)) * tb;
         mbar_arrive_expect_tx(&sh->full[s], tb);
         bulk_g2s(ring + (size_t)s * tb, src, tb, &sh->full[s]);
         *(volatile int*)&sh->issued = t + 1;
@@ -530,7 +389,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     const bool ok = __all_sync(0xffffffffu,
                                mbar_wait(&sh->full[s], (t / ns) & 1, &sh->abort_flag, a.res, 2, a.wait_ns));
     if (!ok) break;
-    const int slice = (u0 + t) % nsl;  // u0 is 0 unless sk
+    const int slice = t % nsl;
     {
       const uint8_t* tile = ring + (size_t)s * tb;
       const uint8_t* wq = tile + (size_t)warp * RPW * ck;
@@ -554,10 +413,9 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty[s]);
-    if (slice == nsl - 1 || (sk && t == ntiles - 1)) {  // the end of this CTA's part of a group
-      const int gloc = (u0 + t) / nsl;                      // sk: group within the launch
-      const int k = sk ? gloc - u0 / nsl : t / nsl;         // the CTA's group ordinal
-      const int g = sk ? gl + gloc : gl + b + k * G;
+    if (slice == nsl - 1) {
+      const int k = t / nsl;
+      const int g = gl + b + k * G;
       float v = 0.0f;
 #pragma unroll
       for (int r = 0; r < RPW; ++r) {
@@ -566,13 +424,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
         acc[r] = 0.0f;
       }
       if constexpr (RPW >= 2) {
-        if (sk && (slice != nsl - 1 || gloc * nsl < u0)) {
-          sk_finish<EPI, RPW>(a, sh, gloc, g, v, lane, warp, best_v, best_i, push_off, push_e);
-        } else {
-          mv_epilogue<EPI>(a, g * wr + warp * RPW, RPW, v, lane, best_v, best_i, push_off, push_e);
-          if constexpr (EPI == EPI_SWIGLU)
-            if (a.q_cnt) mv_swiglu_quant(a, sh, k, g, lane, true, sk, u0, ntiles);
-        }
+        mv_epilogue<EPI>(a, g * wr + warp * RPW, RPW, v, lane, best_v, best_i, push_off, push_e);
       } else {
         const int slot = k % RED_SLOTS;
         int old = 0;
@@ -588,8 +440,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
           __syncwarp();
           if (lane == 0) sh->cnt[slot] = 0;
           mv_epilogue<EPI>(a, g * wr, NW, vv, lane, best_v, best_i, push_off, push_e);
-          if constexpr (EPI == EPI_SWIGLU)
-            if (a.q_cnt) mv_swiglu_quant(a, sh, k, g, lane, false, false, 0, 0);
         }
       }
     }

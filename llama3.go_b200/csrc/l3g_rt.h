@@ -221,13 +221,6 @@ struct l3g_workspace {
   float* part_o = nullptr;
   float* part_ml = nullptr;
   unsigned* att_cnt = nullptr;
-  unsigned* act_cnt = nullptr; // [ff_l / 32] arrivals per Q8_0 block of the SwiGLU output
-  // even tile ranges of the step's matvecs: partial rows of the row groups
-  // that CTAs share, and their counts (null: round-robin row groups)
-  float* sk_part = nullptr;
-  unsigned* sk_cnt = nullptr;
-  size_t sk_cnt_n = 0;
-  bool fuse_act_quant = true;  // SwiGLU act-quant inside up/gate when it runs on even tile ranges
   float* am_val = nullptr;
   int* am_idx = nullptr;
   unsigned* am_cnt = nullptr;
@@ -236,7 +229,7 @@ struct l3g_workspace {
   float* d_tk_logits = nullptr;
   int* h_tk_ids = nullptr;
   float* h_tk_logits = nullptr;
-  int att_cnt_n = 0, act_cnt_n = 0;  // entries of att_cnt, act_cnt
+  int att_cnt_n = 0;  // entries of att_cnt
   int n_splits = 1, att_P = 16, att_ns = 3, att_stage = 0, att_smem = 0, att_gp = 1;
   int att_cluster = 0;         // > 0: the splits of a kv head form one cluster
   unsigned* d_step = nullptr;  // steps run (advanced by k_embed)

@@ -112,7 +112,7 @@ void ws_release(l3g_workspace* ws) {
     if (p) cudaFree(p);
   void* dptrs[] = {ws->d_io, ws->d_res, ws->d_gather, ws->x[0], ws->x[1], ws->y, ws->q,
                    ws->attn, ws->act, ws->attn_d, ws->attn_q, ws->act_d, ws->act_q, ws->logits, ws->logits_full, ws->part_o, ws->part_ml,
-                   ws->att_cnt, ws->act_cnt, ws->sk_part, ws->sk_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
+                   ws->att_cnt, ws->am_val, ws->am_idx, ws->am_cnt, ws->tk_part,
                    ws->d_tk_ids, ws->d_tk_logits, ws->d_tokens, ws->d_trace, ws->d_samp};
   for (void* p : dptrs)
     if (p) cudaFree(p);
@@ -130,9 +130,7 @@ void ws_release(l3g_workspace* ws) {
 void ws_clear_device_error(l3g_workspace* ws) {
   cudaMemset(ws->d_res, 0, sizeof(Result));
   if (ws->att_cnt) cudaMemset(ws->att_cnt, 0, (size_t)ws->att_cnt_n * 4);
-  if (ws->act_cnt) cudaMemset(ws->act_cnt, 0, (size_t)ws->act_cnt_n * 4);
   if (ws->am_cnt) cudaMemset(ws->am_cnt, 0, 4);
-  if (ws->sk_cnt) cudaMemset(ws->sk_cnt, 0, ws->sk_cnt_n * 4);
 }
 
 void ws_detach(l3g_workspace* ws) {
@@ -210,56 +208,6 @@ static void choose_attention_cluster(l3g_workspace* ws) {
   return;
 }
 
-// Even tile ranges over G CTAs (k_matvec's sk mode): the most CTAs that
-// share one row group, or 0 where the mode does not apply (one row per
-// warp, or fewer tiles than CTAs).  Same ranges as the kernel's:
-// CTA c streams tiles [floor(c*T/G), floor((c+1)*T/G)).
-static int sk_contributors(const Q8Tiles& t, int G) {
-  if (t.wr / NW < 2 || G < 1) return 0;
-  const long long T = (long long)t.n_groups * t.nslices;
-  if (T < G) return 0;
-  int most = 1;
-  for (int g = 0; g < t.n_groups; ++g) {
-    const long long u0 = (long long)g * t.nslices, u1 = u0 + t.nslices - 1;
-    const int first = (int)(((u0 + 1) * G - 1) / T), last = (int)(((u1 + 1) * G - 1) / T);
-    most = std::max(most, last - first + 1);
-  }
-  return most;
-}
-constexpr int kSkMaxContributors = 8;
-
-// Scratch of the step's matvecs under even tile ranges (partial rows,
-// counts), sized for the largest of the model's matrices; off with
-// L3G_MV_EVEN=0 (round-robin row groups, as the persistent kernel deals
-// them).
-static void sk_need(const l3g_model* m, size_t* part_floats, size_t* counters) {
-  *part_floats = 0;
-  *counters = 0;
-  const char* env = getenv("L3G_MV_EVEN");
-  if (env && atoi(env) == 0) return;
-  if (m->layers.empty()) return;
-  const LayerW& L = m->layers[0];
-  const Q8Tiles* mats[] = {&L.qkv.t, &L.wo.t, &L.upgate.t, &L.down.t, &m->logits.t};
-  for (const Q8Tiles* t : mats) {
-    const int c = sk_contributors(*t, m->nsm);
-    if (c < 1 || c > kSkMaxContributors) continue;
-    *part_floats = std::max(*part_floats, (size_t)t->n_groups * c * t->wr);
-    *counters = std::max(*counters, (size_t)t->n_groups * (NW + 1));
-  }
-}
-
-// Sets the even-range fields of a step matvec's arguments when its matrix
-// qualifies and the workspace holds the scratch.
-static void sk_args(const l3g_workspace* ws, const DevMat& w, int nsm, MatvecArgs& a) {
-  if (!ws->sk_part || a.row_lo != 0 || a.row_hi != w.t.rows) return;
-  const int c = sk_contributors(w.t, nsm);
-  if (c < 1 || c > kSkMaxContributors) return;
-  if ((size_t)w.t.n_groups * (NW + 1) > ws->sk_cnt_n) return;
-  a.sk_part = ws->sk_part;
-  a.sk_cnt = ws->sk_cnt;
-  a.sk_maxc = c;
-}
-
 extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_workspace** out) {
   if (!m || !out) return l3g_fail(L3G_E_INVALID, "null argument");
   *out = nullptr;
@@ -285,7 +233,10 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   ws->att_gp = 1;
   while (ws->att_gp < G) ws->att_gp <<= 1;
   ws->n_splits = std::max(1, std::min(m->nsm / m->hkv_l, (ctx + ws->att_P - 1) / ws->att_P));
-  const int scratch = std::max(at_scratch_floats(G, hd) * 4, NW * align_up(ws->n_splits, 32) * 4);
+  // merge scratch: the per-warp states, or the last arriver's weights
+  // [MAXG][splits rounded up to 32] and sums [MAXG]
+  const int scratch = std::max(at_scratch_floats(G, hd) * 4,
+                               (MAXG * align_up(ws->n_splits, 32) + MAXG) * 4);
   ws->att_smem = at_ring_offset() + std::max(ws->att_ns * ws->att_stage, scratch);
   choose_attention_cluster(ws);
   const int vloc = m->v_l;
@@ -320,20 +271,6 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   DM(ws->part_ml, (size_t)m->hkv_l * part_splits * G * 2 * 4);
   ws->att_cnt_n = m->hkv_l * 2;  // arrivals, departures
   DM(ws->att_cnt, (size_t)ws->att_cnt_n * 4);
-  ws->act_cnt_n = std::max(1, m->ff_l / 32);
-  DM(ws->act_cnt, (size_t)ws->act_cnt_n * 4);
-  {
-    const char* fq = getenv("L3G_FUSE_ACT_QUANT");
-    ws->fuse_act_quant = !(fq && atoi(fq) == 0);
-    size_t part = 0, cnt = 0;
-    sk_need(m, &part, &cnt);
-    if (part) {
-      DM(ws->sk_part, part * 4);
-      DM(ws->sk_cnt, cnt * 4);
-      ws->sk_cnt_n = cnt;
-      if (e == cudaSuccess) e = cudaMemset(ws->sk_cnt, 0, cnt * 4);
-    }
-  }
   DM(ws->am_val, (size_t)m->nsm * 4);
   DM(ws->am_idx, (size_t)m->nsm * 4);
   DM(ws->am_cnt, 4);
@@ -354,7 +291,6 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
 #undef HM
   if (e == cudaSuccess) e = cudaMemset(ws->d_res, 0, sizeof(Result));
   if (e == cudaSuccess) e = cudaMemset(ws->att_cnt, 0, (size_t)ws->att_cnt_n * 4);
-  if (e == cudaSuccess) e = cudaMemset(ws->act_cnt, 0, (size_t)ws->act_cnt_n * 4);
   if (e == cudaSuccess) e = cudaMemset(ws->am_cnt, 0, 4);
   if (e == cudaSuccess) e = cudaMemset(ws->x[0], 0, ne * 4);
   if (e == cudaSuccess) e = cudaMemset(ws->x[1], 0, ne * 4);
@@ -431,8 +367,7 @@ template <int PRO, int EPI>
 static cudaError_t launch_mv(const DevMat& w, const MatvecArgs& a, int nsm, cudaStream_t st) {
   const int gl = a.row_lo / w.t.wr;
   const int ng = (a.row_hi + w.t.wr - 1) / w.t.wr - gl;
-  // even tile ranges: one CTA per SM (sk_args checked that every CTA gets a tile)
-  const dim3 grid(a.sk_part ? nsm : std::max(1, std::min(ng, nsm)));
+  const dim3 grid(std::max(1, std::min(ng, nsm)));
   switch (w.t.wr / NW) {
     case 1: return launch_mv_r<PRO, EPI, 1>(w, a, grid, st);
     case 2: return launch_mv_r<PRO, EPI, 2>(w, a, grid, st);
@@ -636,7 +571,6 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      sk_args(ws, L.qkv, m->nsm, a);
       KL(L3G_K_QKV, (launch_mv<PRO_RMS, EPI_QKV>(L.qkv, a, m->nsm, st)));
     }
     {  // attention, infer.go:130-175
@@ -696,7 +630,6 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      sk_args(ws, L.wo, m->nsm, a);
       if (ws->tp_p2p) {  // partial rows pushed to every rank (phase 2l)
         a.tp_out = tp_exchange(ws, 2 * l);
         KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_PUSH>(L.wo, a, m->nsm, st)));
@@ -721,23 +654,12 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      sk_args(ws, L.upgate, m->nsm, a);
-      // act-quant of the SwiGLU output, infer.go:233-234: under even tile
-      // ranges fused behind the epilogue (each Q8_0 block once, by the warp
-      // that completes it; counted in shared memory unless the block's
-      // groups span two CTAs), else one launch after up/gate
-      const bool fuse_quant = a.sk_part != nullptr && ws->fuse_act_quant;
-      if (fuse_quant) {
-        a.q_d = ws->act_d;
-        a.q_qs = ws->act_q;
-        a.q_cnt = ws->act_cnt;
-      }
       KL(L3G_K_UPGATE, (launch_mv<PRO_RMS, EPI_SWIGLU>(L.upgate, a, m->nsm, st)));
-      if (!fuse_quant) {
-        const int nb = m->ff_l / 32;
-        KL(L3G_K_ACT_QUANT, launch(k_quantize, dim3((nb + NW - 1) / NW), dim3(NW * 32), 0, st,
-                                   (const float*)ws->act, m->ff_l, ws->act_d, ws->act_q));
-      }
+    }
+    {  // act-quant of the SwiGLU output (once, not per CTA), infer.go:233-234
+      const int nb = m->ff_l / 32;
+      KL(L3G_K_ACT_QUANT, launch(k_quantize, dim3((nb + NW - 1) / NW), dim3(NW * 32), 0, st,
+                                 (const float*)ws->act, m->ff_l, ws->act_d, ws->act_q));
     }
     {  // down, infer.go:235-242
       MatvecArgs a = mv_args(L.down);
@@ -748,7 +670,6 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.res = ws->d_res;
       a.trace = ws->kernels < kTraceCap ? tr : nullptr;
       a.trace_seq = ws->kernels;
-      sk_args(ws, L.down, m->nsm, a);
       if (ws->tp_p2p) {  // phase 2l + 1
         a.tp_out = tp_exchange(ws, 2 * l + 1);
         KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_PUSH>(L.down, a, m->nsm, st)));
@@ -779,7 +700,6 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
     a.res = ws->d_res;
     a.trace = ws->kernels < kTraceCap ? tr : nullptr;
     a.trace_seq = ws->kernels;
-    sk_args(ws, m->logits, m->nsm, a);
     KL(L3G_K_LOGITS, (launch_mv<PRO_RMS, EPI_LOGITS>(m->logits, a, m->nsm, st)));
     const float* full = ws->logits;
     if (m->world > 1) {

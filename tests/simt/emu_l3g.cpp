@@ -1,7 +1,5 @@
 // Host build of libl3g's device kernels under the SIMT emulator, with a C
 // entry point per kernel for the CPU tests (ctypes).  Test infrastructure.
-#include <cstring>
-
 #include "simt.h"
 
 #include "simt_tcgen05.h"
@@ -788,24 +786,15 @@ int emu_matvec(const uint8_t* tiles, int rows, int cols, int rpw, const float* x
 }
 
 // k_matvec with a fused epilogue on a pre-quantized activation, grid CTAs:
-//  epi 2 (EPI_SWIGLU): rows interleave (up_i, gate_i), out[i] = silu(gate_i)
-//    * up_i; with q_cnt non-null the output's Q8_0 quantization is fused
-//    (q_d, q_qs, per-block counters q_cnt) as the decode step runs it;
+//  epi 0 (EPI_STORE): out[r];
 //  epi 3 (EPI_LOGITS): out[r] (or no store when out is null) and the argmax
 //    through per-CTA slots am_val / am_idx and the arrival counter
 //    am_counter, into *result (index, value, status, detail), as
-//    l3g_matvec_q8_argmax_static runs it on its static scratch;
-//  epi 0 (EPI_STORE): out[r].
-// sk != 0: even tile ranges over the grid, with the partial-row scratch and
-// counts sized as the runtime's sk_contributors does (the counts must be
-// zero again after the launch).
+//    l3g_matvec_q8_argmax_static runs it on its static scratch.
 int emu_matvec_epi(const uint8_t* tiles, int rows, int cols, int rpw, const float* xd,
-                   const int8_t* xq, float* out, int epi, float* q_d, int8_t* q_qs,
-                   unsigned* q_cnt, float* am_val, int* am_idx, unsigned* am_counter,
-                   int* result, int grid, int sk, int* sk_maxc_out) {
-  float* sk_part = nullptr;
-  unsigned* sk_cnt = nullptr;
-  const int rc = guarded_call([&] {
+                   const int8_t* xq, float* out, int epi, float* am_val, int* am_idx,
+                   unsigned* am_counter, int* result, int grid) {
+  return guarded_call([&] {
     using namespace l3g;
     const TileGeom g = tile_geometry(rows, cols, rpw, NW, TILE_TARGET);
     MatvecArgs a{};
@@ -818,33 +807,11 @@ int emu_matvec_epi(const uint8_t* tiles, int rows, int cols, int rpw, const floa
     a.xd_in = xd;
     a.xqs_in = xq;
     a.out = out;
-    a.q_d = q_d;
-    a.q_qs = q_qs;
-    a.q_cnt = q_cnt;
     a.am_val = am_val;
     a.am_idx = am_idx;
     a.am_counter = am_counter;
     a.res = reinterpret_cast<Result*>(result);
     a.wait_ns = WAIT_TIMEOUT_NS;
-    size_t ncnt = 0;
-    if (sk) {
-      // the runtime's rule: rows per warp >= 2, at least one tile per CTA
-      const long long T = (long long)g.n_groups * g.nslices;
-      if (rpw < 2 || T < grid) simt::fail("even tile ranges need rpw >= 2 and a tile per CTA");
-      int most = 1;
-      for (int gi = 0; gi < g.n_groups; ++gi) {
-        const long long u0 = (long long)gi * g.nslices, u1 = u0 + g.nslices - 1;
-        most = std::max(most, (int)(((u1 + 1) * grid - 1) / T) - (int)(((u0 + 1) * grid - 1) / T) + 1);
-      }
-      ncnt = (size_t)g.n_groups * (NW + 1);
-      sk_part = static_cast<float*>(simt::dmalloc((size_t)g.n_groups * most * g.wr * 4));
-      sk_cnt = static_cast<unsigned*>(simt::dmalloc(ncnt * 4));
-      std::memset(sk_cnt, 0, ncnt * 4);
-      a.sk_part = sk_part;
-      a.sk_cnt = sk_cnt;
-      a.sk_maxc = most;
-      if (sk_maxc_out) *sk_maxc_out = most;
-    }
     auto go = [&](auto r_c, auto e_c) {
       constexpr int R = decltype(r_c)::value;
       constexpr int E = decltype(e_c)::value;
@@ -859,16 +826,10 @@ int emu_matvec_epi(const uint8_t* tiles, int rows, int cols, int rpw, const floa
         default: simt::fail("rows per warp");
       }
     };
-    if (epi == EPI_SWIGLU) by_rpw(std::integral_constant<int, EPI_SWIGLU>{});
-    else if (epi == EPI_LOGITS) by_rpw(std::integral_constant<int, EPI_LOGITS>{});
+    if (epi == EPI_LOGITS) by_rpw(std::integral_constant<int, EPI_LOGITS>{});
     else if (epi == EPI_STORE) by_rpw(std::integral_constant<int, EPI_STORE>{});
     else simt::fail("epilogue");
-    for (size_t i = 0; i < ncnt; ++i)
-      if (sk_cnt[i]) simt::fail("an even-range count was left nonzero");
   });
-  if (sk_part) guarded_call([&] { simt::dfree(sk_part); });
-  if (sk_cnt) guarded_call([&] { simt::dfree(sk_cnt); });
-  return rc;
 }
 
 // The decode step's split-K attention (k_attention, global merge through

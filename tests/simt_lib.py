@@ -74,7 +74,7 @@ def lib():
         L.emu_matvec.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int, C.c_int,
                                  C.c_int]
         L.emu_matvec_epi.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int, _P, _P,
-                                     _P, _P, _P, _P, _P, C.c_int, C.c_int, C.POINTER(C.c_int)]
+                                     _P, _P, C.c_int]
         L.emu_gemm.argtypes = [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, _P, C.c_int,
                                C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
         _lib = L

@@ -4,8 +4,7 @@ ABI, against the per-kernel step and the oracle.
 
 - Same model and tokens: logits, every layer's KV cache and the hidden state
   are bit-identical to the per-kernel step's when that step uses the same
-  tile layout (four rows per warp, L3G_RPW=4), the same row-group schedule
-  (whole groups dealt round-robin, L3G_MV_EVEN=0) and the same split merge
+  tile layout (four rows per warp, L3G_RPW=4) and the same split merge
   (global partials, L3G_ATT_CLUSTER=0): both compute the same Q8_0 block
   products, norms, RoPE, attention partials and merges in the same order.
   Covered: head sizes 32, 64 and 128, query heads per kv head 2, 3 and 4,
@@ -35,7 +34,6 @@ def _load(gpu_lib, monkeypatch, cfg, T, persistent, fuse="0", spread="1", **kw):
     fq, fm = _fusions(fuse)
     monkeypatch.setenv("L3G_RPW", "4")
     monkeypatch.setenv("L3G_ATT_CLUSTER", "0")
-    monkeypatch.setenv("L3G_MV_EVEN", "0")
     monkeypatch.setenv("L3G_PERSIST_FUSE_QUANT", "1" if fq else "0")
     monkeypatch.setenv("L3G_PERSIST_FUSE_MERGE", "1" if fm else "0")
     monkeypatch.setenv("L3G_PERSIST_BAR_SPREAD", spread)

@@ -494,128 +494,6 @@ def test_decode_matvec_matches_reference_simd(S, oracle_mod, rows, cols, rpw, lo
         d.free()
 
 
-@pytest.mark.parametrize("rpw,grid,nff,sched", [(1, 5, 256, 0), (2, 7, 256, 1), (4, 148, 512, 1),
-                                                (4, 3, 256, 2), (8, 4, 320, 1)])
-def test_upgate_swiglu_with_fused_act_quant(S, oracle_mod, rpw, grid, nff, sched):
-    """The decode step's up/gate matvec (k_matvec, EPI_SWIGLU) with the
-    SwiGLU output's Q8_0 quantization fused behind the epilogue
-    (QuantizeQ8_0Into, infer.go:233-234): row groups of 4 to 32 act values,
-    so a Q8_0 block is completed by 1 to 8 groups spread over the CTAs
-    (the per-block counters) or held whole by one group.  The act values
-    equal silu(gate) * up of the reference's matvec_q8_c rows within 1e-6;
-    the scales and int8 values equal the oracle's quantization of the act
-    values the kernel wrote, bit for bit; every block counter is back to
-    zero after each of two launches; random schedules and copy delays."""
-    import synthetic
-    import torch
-    rows, cols = 2 * nff, 256
-    g = torch.Generator().manual_seed(rows + rpw)
-    w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g) * 0.05, torch).numpy()
-    x = np.random.default_rng(rpw).standard_normal(cols).astype(np.float32)
-    d0, q0 = oracle_mod.quantize_q8_0(x)
-    ref = oracle_mod.ref_matvec_q8(w, d0, q0, rows, cols)
-    act_ref = np.array([np.float32(oracle_mod.silu(float(ref[2 * i + 1]))) * ref[2 * i]
-                        for i in range(nff)], np.float32)
-    raw = S.Dev(w)
-    tiles = S.repack([(raw, 0, rows)], cols, rows, rpw=rpw)
-    xd, xq = S.Dev(d0), S.Dev(q0)
-    nb = nff // 32
-    out = S.Dev(np.zeros(nff, np.float32))
-    qd, qq = S.Dev(np.zeros(nb, np.float32)), S.Dev(np.zeros(nff, np.int8))
-    cnt = S.Dev(np.zeros(nb, np.uint32))
-    res = S.Dev(np.zeros(4, np.int32))
-    ng = S.tile_geometry(rows, cols, rpw)["n_groups"]
-    try:
-        for rep in range(2):
-            S.lib().emu_schedule(sched, 100 * rpw + rep, 3 if sched else 0)
-            S.check(S.lib().emu_matvec_epi(tiles.ptr, rows, cols, rpw, xd.ptr, xq.ptr, out.ptr, 2,
-                                           qd.ptr, qq.ptr, cnt.ptr, None, None, None, res.ptr,
-                                           min(grid, ng), 0, None))
-            act = out.read(np.float32)
-            assert rel_l2(act, act_ref) < 1e-6
-            dref, qref = oracle_mod.quantize_q8_0(act)
-            assert np.array_equal(qd.read(np.float32), dref)
-            assert np.array_equal(qq.read(np.int8), qref)
-            assert (cnt.read(np.uint32) == 0).all()
-            assert (res.read(np.int32) == 0).all()
-    finally:
-        S.lib().emu_schedule(0, 0, 0)
-    for d in (raw, tiles, xd, xq, out, qd, qq, cnt, res):
-        d.free()
-
-
-@pytest.mark.parametrize("epi,rows,cols,rpw,grid,sched", [
-    (0, 256, 4096, 4, 12, 1), (0, 256, 4096, 2, 29, 2), (0, 300, 2048, 8, 7, 1),
-    (2, 512, 4096, 4, 12, 1), (2, 512, 4096, 8, 11, 2), (2, 512, 4096, 2, 40, 1),
-    (3, 400, 4096, 4, 11, 1)])
-def test_matvec_even_tile_ranges(S, oracle_mod, epi, rows, cols, rpw, grid, sched):
-    """k_matvec with even tile ranges (the decode step's schedule: CTA c
-    streams tiles [c*T/G, (c+1)*T/G) of the matrix in storage order, row
-    groups shared by two or more CTAs finished by the last to post its
-    partial rows, in contributor order): plain store, up/gate with SwiGLU and
-    the fused act-quant, and logits with the cross-CTA argmax; grids that
-    leave groups split over 2 to 3 CTAs.  Rows equal the reference's
-    matvec_q8_c within 1e-6 (SwiGLU: silu(gate) * up of them), the act
-    quantization equals the oracle's of the kernel's act values bit for
-    bit, the argmax is the largest row, every count is zero afterwards (the
-    entry checks), and two launches under random schedules agree bit for
-    bit."""
-    import synthetic
-    import torch
-    g = torch.Generator().manual_seed(rows * 3 + grid)
-    w = synthetic.quantize_q8_0_rows(torch.randn(rows, cols, generator=g) * 0.05, torch).numpy()
-    x = np.random.default_rng(grid).standard_normal(cols).astype(np.float32)
-    d0, q0 = oracle_mod.quantize_q8_0(x)
-    ref = oracle_mod.ref_matvec_q8(w, d0, q0, rows, cols)
-    raw = S.Dev(w)
-    tiles = S.repack([(raw, 0, rows)], cols, rows, rpw=rpw)
-    xd, xq = S.Dev(d0), S.Dev(q0)
-    n_out = rows // 2 if epi == 2 else rows
-    nb = max(1, n_out // 32)
-    qd, qq = S.Dev(np.zeros(nb, np.float32)), S.Dev(np.zeros(nb * 32, np.int8))
-    qcnt = S.Dev(np.zeros(nb, np.uint32))
-    am_val, am_idx = S.Dev(np.zeros(grid, np.float32)), S.Dev(np.zeros(grid, np.int32))
-    counter = S.Dev(np.zeros(1, np.uint32))
-    maxc = S.C.c_int(0)
-    outs = []
-    try:
-        for rep in range(2):
-            S.lib().emu_schedule(sched, 31 * rep + grid, 3)
-            out = S.Dev(np.full(n_out, 5.0, np.float32))
-            res = S.Dev(np.array([-1, 0, 0, 0], np.int32))
-            S.check(S.lib().emu_matvec_epi(
-                tiles.ptr, rows, cols, rpw, xd.ptr, xq.ptr, out.ptr, epi,
-                qd.ptr if epi == 2 else None, qq.ptr if epi == 2 else None,
-                qcnt.ptr if epi == 2 else None, am_val.ptr if epi == 3 else None,
-                am_idx.ptr if epi == 3 else None, counter.ptr if epi == 3 else None, res.ptr,
-                grid, 1, S.C.byref(maxc)))
-            got = out.read(np.float32)
-            r = res.read(np.int32)
-            assert r[2] == 0
-            if epi == 2:
-                act_ref = np.array([np.float32(oracle_mod.silu(float(ref[2 * i + 1]))) * ref[2 * i]
-                                    for i in range(n_out)], np.float32)
-                assert rel_l2(got, act_ref) < 1e-6
-                dref, qref = oracle_mod.quantize_q8_0(got)
-                assert np.array_equal(qd.read(np.float32), dref)
-                assert np.array_equal(qq.read(np.int8), qref)
-                assert (qcnt.read(np.uint32) == 0).all()
-            else:
-                assert rel_l2(got, ref) < 1e-6
-            if epi == 3:
-                assert r[0] == int(np.argmax(got)) and r[1:2].view(np.float32)[0] == got.max()
-                assert counter.read(np.uint32)[0] == 0
-            outs.append(got)
-            out.free()
-            res.free()
-    finally:
-        S.lib().emu_schedule(0, 0, 0)
-    assert maxc.value >= 2  # some row group was shared
-    assert np.array_equal(outs[0], outs[1])
-    for d in (raw, tiles, xd, xq, qd, qq, qcnt, am_val, am_idx, counter):
-        d.free()
-
-
 @pytest.mark.parametrize("G,hd,hkv,n,f16", [(4, 128, 2, 700, False), (3, 64, 2, 37, False),
                                             (2, 32, 3, 300, False), (4, 128, 1, 90, True)])
 def test_decode_attention_matches_exact_softmax(S, G, hd, hkv, n, f16):

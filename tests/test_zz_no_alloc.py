@@ -191,8 +191,8 @@ def test_static_argmax_merge_under_the_emulator(oracle_mod, rpw):
             out = S.Dev(np.full(rows, 9.0, np.float32))
             res = S.Dev(np.array([-1, 0, 0, 0], np.int32))
             S.check(S.lib().emu_matvec_epi(tiles.ptr, rows, cols, rpw, xd.ptr, xq.ptr,
-                                           out.ptr if i % 2 == 0 else None, 3, None, None, None,
-                                           am_val.ptr, am_idx.ptr, counter.ptr, res.ptr, grid, 0, None))
+                                           out.ptr if i % 2 == 0 else None, 3, am_val.ptr,
+                                           am_idx.ptr, counter.ptr, res.ptr, grid))
             r = res.read(np.int32)
             assert r[0] == 130 and r[2] == 0, (grid, r)
             v = r[1:2].view(np.float32)[0]
