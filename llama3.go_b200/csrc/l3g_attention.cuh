@@ -493,50 +493,59 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     trace_mark(a.trace, a.trace_seq, TR_EXIT);
     return;
   }
-  const int gh = G * hd;
-  const int SP = align_up(S, 32);
-  float* wsm = reinterpret_cast<float*>(ring);  // [MAXG][SP] weights e_s, then [MAXG] sums
-  float* lsm = wsm + MAXG * SP;
+  const int gh = G * hd, nblk = gh / 32;
   const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
   const float* po = a.part_o + (size_t)kvh * S * gh;
-  // per query head (one warp each): e_s = exp(m_s - max m) and L = sum l_s
-  // e_s, in the order merge_split_block takes them
-  for (int h = warp; h < G; h += NW) {
-    float M = -INFINITY;
-    for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(ml + ((size_t)s2 * G + h) * 2));
-    M = warp_max(M);
-    float L = 0.0f;
-    for (int s0 = 0; s0 < S; s0 += 32) {
-      const int s2 = s0 + lane;
-      float le = 0.0f;
-      if (s2 < S) {
-        const float2 p = __ldcg(reinterpret_cast<const float2*>(ml + ((size_t)s2 * G + h) * 2));
-        const float e = p.x == -INFINITY ? 0.0f : expf(p.x - M);
-        wsm[h * SP + s2] = e;
-        le = p.y * e;
+  if (S <= 32) {
+    // one warp per block of 32 outputs, two blocks at a time, every load
+    // of both issued together (one round trip to L2): lane s holds split
+    // s's (m, l) of the block's head and lane = output holds every split's
+    // partial output; the weights e_s reach the lanes by shuffles.  Same
+    // arithmetic, in the same order, as merge_split_block.
+    for (int b0 = warp; b0 < nblk; b0 += 2 * NW) {
+      const int b1 = b0 + NW;
+      const bool two = b1 < nblk;
+      const int h0 = b0 * 32 / hd, h1 = two ? b1 * 32 / hd : h0;
+      const float2 p0 = lane < S ? __ldcg(reinterpret_cast<const float2*>(ml + ((size_t)lane * G + h0) * 2))
+                                 : make_float2(-INFINITY, 0.0f);
+      const float2 p1 = lane < S ? __ldcg(reinterpret_cast<const float2*>(ml + ((size_t)lane * G + h1) * 2))
+                                 : make_float2(-INFINITY, 0.0f);
+      float o0[32], o1[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        o0[u] = u < S ? __ldcg(po + (size_t)u * gh + b0 * 32 + lane) : 0.0f;
+        o1[u] = u < S && two ? __ldcg(po + (size_t)u * gh + b1 * 32 + lane) : 0.0f;
       }
-      L += warp_sum(le);
-    }
-    if (lane == 0) lsm[h] = L;
-  }
-  consumer_sync();
-  // one warp per block of 32 outputs: O = sum_s o_s e_s in split order,
-  // out = O / L, then the block's Q8_0 quantization for Wo
-  for (int blk = warp; blk < gh / 32; blk += NW) {
-    const int h = blk * 32 / hd, col = blk * 32 + lane;
-    const float* e = wsm + h * SP;
-    float O = 0.0f;
-    for (int s0 = 0; s0 < S; s0 += 32) {
-      float ov[32];
+      const float M0 = warp_max(p0.x), M1 = warp_max(p1.x);
+      const float e0 = p0.x == -INFINITY ? 0.0f : expf(p0.x - M0);
+      const float e1 = p1.x == -INFINITY ? 0.0f : expf(p1.x - M1);
+      const float L0 = 0.0f + warp_sum(lane < S ? p0.y * e0 : 0.0f);
+      const float L1 = 0.0f + warp_sum(lane < S ? p1.y * e1 : 0.0f);
+      float O0 = 0.0f, O1 = 0.0f;
 #pragma unroll
-      for (int u = 0; u < 32; ++u) ov[u] = s0 + u < S ? __ldcg(po + (size_t)(s0 + u) * gh + col) : 0.0f;
-#pragma unroll
-      for (int u = 0; u < 32; ++u)
-        if (s0 + u < S) O = fmaf(ov[u], e[s0 + u], O);
+      for (int u = 0; u < 32; ++u) {
+        const float w0 = __shfl_sync(0xffffffffu, e0, u), w1 = __shfl_sync(0xffffffffu, e1, u);
+        if (u < S) {
+          O0 = fmaf(o0[u], w0, O0);
+          O1 = fmaf(o1[u], w1, O1);
+        }
+      }
+      const float v0 = __fmul_rn(O0, __fdiv_rn(1.0f, L0));
+      a.out[(size_t)kvh * gh + b0 * 32 + lane] = v0;
+      quant_block(v0, kvh * gh / 32 + b0, lane, a.out_d, a.out_q);
+      if (two) {
+        const float v1 = __fmul_rn(O1, __fdiv_rn(1.0f, L1));
+        a.out[(size_t)kvh * gh + b1 * 32 + lane] = v1;
+        quant_block(v1, kvh * gh / 32 + b1, lane, a.out_d, a.out_q);
+      }
     }
-    const float v = __fmul_rn(O, __fdiv_rn(1.0f, lsm[h]));
-    a.out[(size_t)kvh * gh + col] = v;
-    quant_block(v, kvh * gh / 32 + blk, lane, a.out_d, a.out_q);
+  } else {
+    float* wbuf = reinterpret_cast<float*>(ring) + warp * align_up(S, 32);  // e_s per warp
+    for (int blk = warp; blk < nblk; blk += NW) {
+      const float v = merge_split_block(ml, po, S, G, gh, blk * 32 / hd, blk * 32 + lane, lane, wbuf);
+      a.out[(size_t)kvh * gh + blk * 32 + lane] = v;
+      quant_block(v, kvh * gh / 32 + blk, lane, a.out_d, a.out_q);
+    }
   }
   trace_mark(a.trace, a.trace_seq, 7);  // merged
   if (threadIdx.x == 0) *arrived = 0u;

@@ -233,10 +233,7 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   ws->att_gp = 1;
   while (ws->att_gp < G) ws->att_gp <<= 1;
   ws->n_splits = std::max(1, std::min(m->nsm / m->hkv_l, (ctx + ws->att_P - 1) / ws->att_P));
-  // merge scratch: the per-warp states, or the last arriver's weights
-  // [MAXG][splits rounded up to 32] and sums [MAXG]
-  const int scratch = std::max(at_scratch_floats(G, hd) * 4,
-                               (MAXG * align_up(ws->n_splits, 32) + MAXG) * 4);
+  const int scratch = std::max(at_scratch_floats(G, hd) * 4, NW * align_up(ws->n_splits, 32) * 4);
   ws->att_smem = at_ring_offset() + std::max(ws->att_ns * ws->att_stage, scratch);
   choose_attention_cluster(ws);
   const int vloc = m->v_l;
