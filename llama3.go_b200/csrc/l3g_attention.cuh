@@ -22,9 +22,9 @@
 //     (one or more Q8_0 blocks) reading the others' partials over
 //     distributed shared memory, then a second barrier keeps every CTA's
 //     shared memory alive until all reads are done;
-//   - otherwise through global partials: every CTA publishes its own and
-//     the last of the kv head's CTAs to publish (an arrival counter) merges
-//     all of the head's outputs; the others leave at once.
+//   - otherwise through global partials: every CTA publishes its own, waits
+//     until all splits of its kv head have (they are all resident), and
+//     merges one slice of the outputs.
 #pragma once
 
 struct AttnArgs {
@@ -162,7 +162,9 @@ __device__ __forceinline__ float merge_split_block(const float* ml, const float*
 // matvec CTA beside it).  Capping the registers so that an attention CTA
 // and a matvec CTA share an SM was measured slower: the early K|V stream
 // then competes with the QKV matvec's prologue and weight stream and every
-// kernel of the layer slows down.
+// kernel of the layer slows down.  A merge by the last CTA of each kv head
+// to publish (no waiting) was measured slower too: the one CTA's merge of
+// all the head's outputs takes longer than the wait plus one slice each.
 template <int DPL, typename KT, int GP, bool CL>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attention(const __grid_constant__ AttnArgs a) {
@@ -474,80 +476,45 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     trace_mark(a.trace, a.trace_seq, TR_EXIT);
     return;
   }
-  // Publish this split's partial; the last of the kv head's S splits to
-  // publish merges every output of the head, the others are done.  No CTA
-  // waits for another, so the grid need not be resident at once, and all
-  // but one CTA per kv head leave their SM at once (the next kernel's CTAs
-  // start loading there).  counters[kvh] counts arrivals; the last CTA
-  // zeroes it (the next launch's CTAs arrive only after this grid has
-  // completed).  Ordering: every thread's partial stores, the CTA barrier,
-  // thread 0's device-scope acquire-release add; the last arriver's
-  // acquire, then a CTA barrier before any thread reads the partials.
+  // Publish this split's partial, then wait (bounded) until every split of
+  // this kv head has published: the grid has at most one CTA per SM, so all
+  // of them are resident.  Then each CTA merges its own slice of the G*hd
+  // outputs (whole Q8_0 blocks), reading every split's (m, l) and that
+  // slice of their partial outputs: one small gather per CTA instead of one
+  // CTA gathering everything.  counters[kvh] counts arrivals,
+  // counters[gridDim.x + kvh] departures; the last to depart resets both.
   consumer_sync();
   unsigned* arrived = a.counters + kvh;
-  if (threadIdx.x == 0)
-    *(volatile int*)&sh->last = atom_add_acq_rel_gpu(arrived, 1u) == (unsigned)S - 1;
-  consumer_sync();
-  trace_mark(a.trace, a.trace_seq, 5);  // published
-  if (!*(volatile int*)&sh->last) {
-    trace_mark(a.trace, a.trace_seq, TR_EXIT);
-    return;
+  unsigned* departed = a.counters + gridDim.x + kvh;
+  if (threadIdx.x == 0) {
+    atom_add_acq_rel_gpu(arrived, 1u);
+    const uint64_t t0 = gtime();
+    while (ld_acquire_gpu_u32(arrived) < (unsigned)S) {
+      if (gtime() - t0 > a.wait_ns) {
+        report(a.res, ERR_TIMEOUT, 9);
+        break;
+      }
+    }
   }
-  const int gh = G * hd, nblk = gh / 32;
+  consumer_sync();
+  trace_mark(a.trace, a.trace_seq, 5);  // every split published
+  const int gh = G * hd;
+  const int slice = align_up((gh + S - 1) / S, 32);  // outputs merged per CTA
+  const int b0 = min(gh, split * slice) / 32, b1 = min(gh, (split + 1) * slice) / 32;
+  float* wbuf = reinterpret_cast<float*>(ring) + warp * align_up(S, 32);  // e_s per warp
   const float* ml = a.part_ml + (size_t)kvh * S * G * 2;
   const float* po = a.part_o + (size_t)kvh * S * gh;
-  if (S <= 32) {
-    // one warp per block of 32 outputs, two blocks at a time, every load
-    // of both issued together (one round trip to L2): lane s holds split
-    // s's (m, l) of the block's head and lane = output holds every split's
-    // partial output; the weights e_s reach the lanes by shuffles.  Same
-    // arithmetic, in the same order, as merge_split_block.
-    for (int b0 = warp; b0 < nblk; b0 += 2 * NW) {
-      const int b1 = b0 + NW;
-      const bool two = b1 < nblk;
-      const int h0 = b0 * 32 / hd, h1 = two ? b1 * 32 / hd : h0;
-      const float2 p0 = lane < S ? __ldcg(reinterpret_cast<const float2*>(ml + ((size_t)lane * G + h0) * 2))
-                                 : make_float2(-INFINITY, 0.0f);
-      const float2 p1 = lane < S ? __ldcg(reinterpret_cast<const float2*>(ml + ((size_t)lane * G + h1) * 2))
-                                 : make_float2(-INFINITY, 0.0f);
-      float o0[32], o1[32];
-#pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        o0[u] = u < S ? __ldcg(po + (size_t)u * gh + b0 * 32 + lane) : 0.0f;
-        o1[u] = u < S && two ? __ldcg(po + (size_t)u * gh + b1 * 32 + lane) : 0.0f;
-      }
-      const float M0 = warp_max(p0.x), M1 = warp_max(p1.x);
-      const float e0 = p0.x == -INFINITY ? 0.0f : expf(p0.x - M0);
-      const float e1 = p1.x == -INFINITY ? 0.0f : expf(p1.x - M1);
-      const float L0 = 0.0f + warp_sum(lane < S ? p0.y * e0 : 0.0f);
-      const float L1 = 0.0f + warp_sum(lane < S ? p1.y * e1 : 0.0f);
-      float O0 = 0.0f, O1 = 0.0f;
-#pragma unroll
-      for (int u = 0; u < 32; ++u) {
-        const float w0 = __shfl_sync(0xffffffffu, e0, u), w1 = __shfl_sync(0xffffffffu, e1, u);
-        if (u < S) {
-          O0 = fmaf(o0[u], w0, O0);
-          O1 = fmaf(o1[u], w1, O1);
-        }
-      }
-      const float v0 = __fmul_rn(O0, __fdiv_rn(1.0f, L0));
-      a.out[(size_t)kvh * gh + b0 * 32 + lane] = v0;
-      quant_block(v0, kvh * gh / 32 + b0, lane, a.out_d, a.out_q);
-      if (two) {
-        const float v1 = __fmul_rn(O1, __fdiv_rn(1.0f, L1));
-        a.out[(size_t)kvh * gh + b1 * 32 + lane] = v1;
-        quant_block(v1, kvh * gh / 32 + b1, lane, a.out_d, a.out_q);
-      }
-    }
-  } else {
-    float* wbuf = reinterpret_cast<float*>(ring) + warp * align_up(S, 32);  // e_s per warp
-    for (int blk = warp; blk < nblk; blk += NW) {
-      const float v = merge_split_block(ml, po, S, G, gh, blk * 32 / hd, blk * 32 + lane, lane, wbuf);
-      a.out[(size_t)kvh * gh + blk * 32 + lane] = v;
-      quant_block(v, kvh * gh / 32 + blk, lane, a.out_d, a.out_q);
-    }
+  for (int blk = b0 + warp; blk < b1; blk += NW) {  // one warp per block of 32 outputs
+    const int h = blk * 32 / hd;
+    const float v = merge_split_block(ml, po, S, G, gh, h, blk * 32 + lane, lane, wbuf);
+    a.out[(size_t)kvh * gh + blk * 32 + lane] = v;
+    quant_block(v, kvh * gh / 32 + blk, lane, a.out_d, a.out_q);
   }
-  trace_mark(a.trace, a.trace_seq, 7);  // merged
-  if (threadIdx.x == 0) *arrived = 0u;
+  trace_mark(a.trace, a.trace_seq, 7);  // slice merged
+  consumer_sync();
+  if (threadIdx.x == 0 && atom_add_acq_rel_gpu(departed, 1u) == (unsigned)S - 1) {
+    *arrived = 0u;
+    *departed = 0u;
+  }
   trace_mark(a.trace, a.trace_seq, TR_EXIT);
 }
