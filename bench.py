@@ -840,6 +840,12 @@ def run_batched(args):
     D.barrier()
     clocks = clk.stop()
     wall = D.max(time.perf_counter() - t0)
+    # one more step, untimed, inside an NVTX range: the launch list of a
+    # single step for `ncu --nvtx --nvtx-include batched_step/`
+    torch.cuda.nvtx.range_push("batched_step")
+    tokens = batch.step(states, tokens, seeds)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     value = args.seqs * args.steps / wall
     es = 2 if args.kv == "f16" else 4
     kv_step = sum(cfg.kv_bytes(int(p) + i + 1, es) for p in pos0 for i in range(args.steps)) / args.steps
