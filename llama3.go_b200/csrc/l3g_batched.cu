@@ -5,16 +5,14 @@
 // ---------------------------------------------------------------------------
 // batched Q8_0 product on the tensor cores (tcgen05 kind::i8)
 // ---------------------------------------------------------------------------
-// One batched product out[n][r] (n < n_tok) on stream st: one CTA per SM at
-// most, tiles dealt round-robin.
 // K split of a product with few (row tile, token tile) tiles: the largest
-// divisor of the chunk count that keeps the units within the SM count and
-// the partial sums within part_floats (1: no split).
-static int gemm_ksplit(const GemmMat& w, int n_tok, int nsm, size_t part_floats) {
+// divisor of the chunk count that keeps the units within the CTA slots (SMs
+// times CTAs per SM) and the partial sums within part_floats (1: no split).
+static int gemm_ksplit(const GemmMat& w, int n_tok, int slots, size_t part_floats) {
   const int nt = gemm::token_tile(n_tok);
   const long long tiles = (long long)w.n_rt * ((n_tok + nt - 1) / nt);
-  if (part_floats == 0 || tiles >= nsm) return 1;
-  const long long want = nsm / tiles;
+  if (part_floats == 0 || tiles >= slots) return 1;
+  const long long want = slots / tiles;
   int best = 1;
   for (int d = 2; d <= w.nk && d <= want; ++d)
     if (w.nk % d == 0 && (size_t)d * n_tok * w.rows <= part_floats) best = d;
@@ -23,18 +21,22 @@ static int gemm_ksplit(const GemmMat& w, int n_tok, int nsm, size_t part_floats)
 // Partial-sum floats that gemm_ksplit can ask of matrix w for up to cap tokens.
 static size_t gemm_part_bound(const GemmMat& w, int cap, int nsm) {
   if (!w.data) return 0;
-  const long long d = std::min<long long>(w.nk, std::max(1, nsm / std::max(1, w.n_rt)));
+  // the most CTA slots any token tile gets (two per SM at 64 tokens)
+  const int slots = nsm * 2;
+  const long long d = std::min<long long>(w.nk, std::max(1, slots / std::max(1, w.n_rt)));
   return d > 1 ? (size_t)d * cap * w.rows : 0;
 }
 
-// One batched product out[n][r] (n < n_tok) on stream st: one CTA per SM at
-// most, work units dealt round-robin; with few tiles the K range is split
-// over more CTAs (partial sums in part, then k_gemm_reduce).
+// One batched product out[n][r] (n < n_tok) on stream st: at most the CTAs
+// that fit at once (one per SM, two at 64 tokens), work units dealt
+// round-robin; with few tiles the K range is split over more CTAs (partial
+// sums in part, then k_gemm_reduce).
 static cudaError_t launch_gemm(const GemmMat& w, const uint8_t* act, int n_tok, float* out,
                                Result* res, unsigned long long wait_ns, int nsm,
                                cudaStream_t st, int ldo = 0, float* part = nullptr,
                                size_t part_floats = 0) {
   const int nt = gemm::token_tile(n_tok);
+  const int slots = nsm * gemm::ctas_per_sm(nt);  // CTAs resident at once
   GemmArgs g{};
   g.a = w.data;
   g.b = act;
@@ -45,13 +47,13 @@ static cudaError_t launch_gemm(const GemmMat& w, const uint8_t* act, int n_tok, 
   g.nk = w.nk;
   g.n_rt = w.n_rt;
   g.n_tt = (n_tok + nt - 1) / nt;
-  g.ksplit = part ? gemm_ksplit(w, n_tok, nsm, part_floats) : 1;
+  g.ksplit = part ? gemm_ksplit(w, n_tok, slots, part_floats) : 1;
   g.part = part;
   g.nstages = gemm::stages(nt);
   g.res = res;
   g.wait_ns = wait_ns;
   const long long units = (long long)g.n_rt * g.n_tt * g.ksplit;
-  const int grid = (int)std::max<long long>(1, std::min<long long>(nsm, units));
+  const int grid = (int)std::max<long long>(1, std::min<long long>(slots, units));
   switch (nt) {
     case 16: k_gemm_q8<16><<<grid, gemm_threads(16), gemm::smem_bytes(16), st>>>(g); break;
     case 32: k_gemm_q8<32><<<grid, gemm_threads(32), gemm::smem_bytes(32), st>>>(g); break;

@@ -22,12 +22,14 @@ struct GemmArgs {
 };
 
 // Rescale warps: each TMEM lane quarter (weight rows 32q..) is read by one
-// warp per group of 16 token columns (at most four groups), so a warp
-// rescales 16 products per row and block at 16-64 tokens (32 at 128): the
-// per-block cost of waiting, loading from tensor memory and releasing is
-// paid for at least 16 products, and a scheduler has one to four rescale
-// warps.
-__host__ __device__ constexpr int gemm_epi_warps(int nt) { return nt >= 64 ? 16 : nt / 4; }
+// warp per group of token columns, so a warp rescales 16 products per row
+// and block at 16 and 32 tokens, 32 at 64 (two CTAs per SM, eight warps
+// each) and 128: the per-block cost of waiting, loading from tensor memory
+// and releasing is paid for at least 16 products, and a scheduler has one
+// to four rescale warps.
+__host__ __device__ constexpr int gemm_epi_warps(int nt) {
+  return nt >= 64 ? (gemm::ctas_per_sm(nt) == 2 ? 8 : 16) : nt / 4;
+}
 __host__ __device__ constexpr int gemm_threads(int nt) {
   return 32 * (2 + gemm_epi_warps(nt));  // producer, MMA issuer, rescale
 }
@@ -65,15 +67,16 @@ static_assert(sizeof(GemmSmem) <= gemm::SMEM_HEAD, "gemm smem head");
 // rescale warps store its outputs, or with a split K its partial sums
 // (k_gemm_reduce adds them in split order).
 template <int NT>
-__global__ void __launch_bounds__(gemm_threads(NT), 1)
+__global__ void __launch_bounds__(gemm_threads(NT), gemm::ctas_per_sm(NT))
     k_gemm_q8(const __grid_constant__ GemmArgs g) {
   using namespace gemm;
   constexpr int NB = tmem_buffers(NT);
   constexpr uint32_t TCOLS = tmem_cols(NT);
   constexpr int EPI = gemm_epi_warps(NT);
   constexpr int CPT = NT / (EPI / 4);  // token columns per rescale thread
-  // blocks rescaled per group: 64 (16 warps: 32) loaded products per thread
-  constexpr int LP = EPI >= 16 ? 32 : 64;
+  // blocks rescaled per group: 64 (16 warps, or two CTAs per SM: 32)
+  // loaded products per thread
+  constexpr int LP = EPI >= 16 || ctas_per_sm(NT) == 2 ? 32 : 64;
   constexpr int GB = LP / CPT >= BPC ? BPC : (LP / CPT >= 2 ? LP / CPT : 1);
   static_assert(BPC % GB == 0 && tmem_buffers(NT) >= 2 * GB, "rescale groups");
   constexpr uint32_t IDESC = idesc_i8(TILE_M, NT);

@@ -88,11 +88,19 @@ L3G_HD constexpr uint32_t idesc_i8(int m, int n) {
          ((uint32_t)(m >> 4) << 24);
 }
 
+// CTAs of the product resident per SM: two at 64 tokens, each with half of
+// the SM's tensor memory and of its shared-memory ring, so that two CTAs'
+// block chains (MMA, commit, tensor-memory load, rescale, release)
+// interleave on the SM; one otherwise.
+L3G_HD constexpr int ctas_per_sm(int nt) { return nt == 64 ? 2 : 1; }
+
 // Tensor-memory buffers of one CTA: NB buffers of NT columns (one per block
-// in flight between the MMA issuer and the rescaling warps), all 512 columns
-// of the SM's tensor memory: 8, 4, 2 and 1 chunks in flight at 16, 32, 64
-// and 128 tokens, so the MMAs run that far ahead of the rescale.
-L3G_HD constexpr int tmem_buffers(int nt) { return 512 / nt < 32 ? 512 / nt : 32; }
+// in flight between the MMA issuer and the rescaling warps), the CTA's share
+// of the SM's 512 columns: 32, 16, 4 (two CTAs) and 4 blocks in flight at
+// 16, 32, 64 and 128 tokens, so the MMAs run that far ahead of the rescale.
+L3G_HD constexpr int tmem_buffers(int nt) {
+  return 512 / ctas_per_sm(nt) / nt < 32 ? 512 / ctas_per_sm(nt) / nt : 32;
+}
 L3G_HD constexpr int tmem_cols(int nt) {
   return tmem_buffers(nt) * nt <= 32 ? 32 : tmem_buffers(nt) * nt <= 64 ? 64
        : tmem_buffers(nt) * nt <= 128 ? 128 : tmem_buffers(nt) * nt <= 256 ? 256 : 512;
@@ -101,11 +109,13 @@ L3G_HD constexpr int tmem_cols(int nt) {
 // Ring stage = one weight chunk + one activation chunk.
 L3G_HD constexpr int stage_bytes(int nt) { return A_CHUNK + b_chunk(nt); }
 constexpr int SMEM_HEAD = 1024;
-constexpr int SMEM_BUDGET = 200 * 1024;
+constexpr int SMEM_BUDGET = 200 * 1024;     // ring bytes of a CTA alone on its SM
+constexpr int SMEM_BUDGET_2 = 107 * 1024;   // each of two CTAs on an SM
 constexpr int MAX_STAGES_G = 8;
 L3G_HD constexpr int stages(int nt) {
-  return (SMEM_BUDGET / stage_bytes(nt)) < MAX_STAGES_G ? (SMEM_BUDGET / stage_bytes(nt))
-                                                        : MAX_STAGES_G;
+  return ((ctas_per_sm(nt) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET) / stage_bytes(nt)) < MAX_STAGES_G
+             ? ((ctas_per_sm(nt) == 2 ? SMEM_BUDGET_2 : SMEM_BUDGET) / stage_bytes(nt))
+             : MAX_STAGES_G;
 }
 L3G_HD constexpr int smem_bytes(int nt) { return SMEM_HEAD + stages(nt) * stage_bytes(nt); }
 
