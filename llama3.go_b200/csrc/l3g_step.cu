@@ -230,6 +230,10 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   while (ws->att_P * 2 <= std::min(KV_PAGE, (int)(32768 / (2 * hd * es)))) ws->att_P *= 2;
   ws->att_stage = 2 * ws->att_P * hd * (int)es;
   ws->att_ns = 3;
+  if (const char* e = getenv("L3G_ATT_STAGES")) {  // ring depth override, 2..6 stages
+    const int v = atoi(e);
+    if (v >= 2 && v <= 6) ws->att_ns = v;
+  }
   ws->att_gp = 1;
   while (ws->att_gp < G) ws->att_gp <<= 1;
   ws->n_splits = std::max(1, std::min(m->nsm / m->hkv_l, (ctx + ws->att_P - 1) / ws->att_P));
