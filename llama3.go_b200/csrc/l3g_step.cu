@@ -224,12 +224,15 @@ extern "C" int l3g_workspace_new(l3g_model* m, int32_t ctx, int32_t topk, l3g_wo
   const int G = m->group;
   const size_t es = m->kv_f16 ? 2 : 4;
   // attention geometry: splits fill the SMs; a stage holds the interleaved
-  // K|V rows of P positions, one ~32 KB bulk copy; three stages in flight
+  // K|V rows of P positions, one ~32 KB bulk copy; four or six stages in flight
   // (a power of two, so stages start at multiples of P that divide KV_PAGE)
   ws->att_P = NW;
   while (ws->att_P * 2 <= std::min(KV_PAGE, (int)(32768 / (2 * hd * es)))) ws->att_P *= 2;
   ws->att_stage = 2 * ws->att_P * hd * (int)es;
-  ws->att_ns = 3;
+  // four stages in flight (measured 428 vs 418 tok/s for three at one GPU);
+  // six under tensor parallelism, where fewer CTAs stream a rank's heads
+  // (541 vs 527 tok/s at two GPUs)
+  ws->att_ns = m->world > 1 ? 6 : 4;
   if (const char* e = getenv("L3G_ATT_STAGES")) {  // ring depth override, 2..6 stages
     const int v = atoi(e);
     if (v >= 2 && v <= 6) ws->att_ns = v;
@@ -633,12 +636,13 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.trace_seq = ws->kernels;
       if (ws->tp_p2p) {  // partial rows pushed to every rank (phase 2l)
         a.tp_out = tp_exchange(ws, 2 * l);
+        if (ws->tp_fused_reduce) a.tp_y = ws->y;  // and reduced by the pushing CTAs
         KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_PUSH>(L.wo, a, m->nsm, st)));
       } else {
         KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_STORE>(L.wo, a, m->nsm, st)));
       }
     }
-    if (ws->tp_p2p)
+    if (ws->tp_p2p && !ws->tp_fused_reduce)
       KL(L3G_K_OTHER, launch(k_tp_reduce, dim3((ne / 4 + 255) / 256), dim3(256), 0, st,
                              tp_exchange(ws, 2 * l), ws->y, ws->d_res, wait_ns));
     else if (m->world > 1)
@@ -673,12 +677,13 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.trace_seq = ws->kernels;
       if (ws->tp_p2p) {  // phase 2l + 1
         a.tp_out = tp_exchange(ws, 2 * l + 1);
+        if (ws->tp_fused_reduce) a.tp_y = ws->y;
         KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_PUSH>(L.down, a, m->nsm, st)));
       } else {
         KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_STORE>(L.down, a, m->nsm, st)));
       }
     }
-    if (ws->tp_p2p)
+    if (ws->tp_p2p && !ws->tp_fused_reduce)
       KL(L3G_K_OTHER, launch(k_tp_reduce, dim3((ne / 4 + 255) / 256), dim3(256), 0, st,
                              tp_exchange(ws, 2 * l + 1), ws->y, ws->d_res, wait_ns));
     else if (m->world > 1)
