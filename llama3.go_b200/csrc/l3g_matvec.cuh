@@ -70,10 +70,6 @@ struct MatvecArgs {
   unsigned long long* trace;  // device timeline (nullptr: off)
   int trace_seq;
   TpExchange tp_out;      // EPI_PUSH
-  float* tp_y;            // EPI_PUSH: non-null: after its pushes each CTA waits
-                          // for every rank's partials of its own rows and
-                          // writes their sum here (the reduction of
-                          // k_tp_reduce, done by the producing CTA)
   unsigned long long wait_ns;  // bound of every wait (WAIT_TIMEOUT_NS or _PEER_NS)
 };
 
@@ -449,38 +445,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)  // two CTAs per SM (PDL overlap)
     }
   }
   trace_mark(a.trace, a.trace_seq, TR_LOOP);
-
-  if constexpr (EPI == EPI_PUSH) {
-    // The rows this CTA pushed, reduced over the ranks in rank order, as
-    // k_tp_reduce does: each rank's CTA of the same index pushes the same
-    // rows (same grid and row groups on every rank), and the words carry
-    // the phase's epoch, so a value has arrived when its epoch matches.
-    if (a.tp_y && !*(volatile int*)&sh->abort_flag) {
-      consumer_sync();  // every warp's pushes of this CTA are issued
-      const TpExchange& t = a.tp_out;
-      const unsigned long long* rb = t.my_recv + (size_t)(push_e & 1u) * t.world * t.n;
-      const uint64_t t_start = gtime();
-      for (int i = threadIdx.x; i < my_groups * wr; i += NW * 32) {
-        const int g = gl + b + (i / wr) * G;
-        const int row = g * wr + i % wr;
-        if (row < a.row_lo || row >= a.row_hi || row >= a.w.rows) continue;
-        float acc = 0.0f;
-        for (int r = 0; r < t.world; ++r) {
-          unsigned long long w = ld_relaxed_sys_u64(rb + (size_t)r * t.n + row);
-          while ((unsigned)(w >> 32) != push_e) {
-            if (gtime() - t_start > a.wait_ns) {
-              report(a.res, ERR_TIMEOUT, 12);
-              break;
-            }
-            w = ld_relaxed_sys_u64(rb + (size_t)r * t.n + row);
-          }
-          const float v = __uint_as_float((unsigned)w);
-          acc = r == 0 ? v : __fadd_rn(acc, v);
-        }
-        a.tp_y[row] = acc;
-      }
-    }
-  }
 
   if constexpr (EPI == EPI_LOGITS) {
     // per-warp best -> per-CTA best -> the last CTA merges in a fixed order

@@ -239,9 +239,6 @@ struct l3g_workspace {
   int* d_sync = nullptr;       // operand of the ranks' line-up after a capture
   // tensor parallel exchange over peer memory (world > 1 and IPC available)
   bool tp_p2p = false;
-  // the Wo / down CTAs reduce the rows they pushed (no k_tp_reduce launch);
-  // L3G_TP_FUSED_REDUCE=0 keeps the separate reduce kernel
-  bool tp_fused_reduce = true;
   unsigned long long* tp_recv = nullptr;               // [2][world][n_emb] {value, epoch}
   unsigned long long* tp_peer_recv[MAX_WORLD] = {};    // every rank's (self: own)
   bool tp_peer_same_process[MAX_WORLD] = {};            // mapped without IPC

@@ -636,13 +636,12 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.trace_seq = ws->kernels;
       if (ws->tp_p2p) {  // partial rows pushed to every rank (phase 2l)
         a.tp_out = tp_exchange(ws, 2 * l);
-        if (ws->tp_fused_reduce) a.tp_y = ws->y;  // and reduced by the pushing CTAs
         KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_PUSH>(L.wo, a, m->nsm, st)));
       } else {
         KL(L3G_K_WO, (launch_mv<PRO_PREQ, EPI_STORE>(L.wo, a, m->nsm, st)));
       }
     }
-    if (ws->tp_p2p && !ws->tp_fused_reduce)
+    if (ws->tp_p2p)
       KL(L3G_K_OTHER, launch(k_tp_reduce, dim3((ne / 4 + 255) / 256), dim3(256), 0, st,
                              tp_exchange(ws, 2 * l), ws->y, ws->d_res, wait_ns));
     else if (m->world > 1)
@@ -677,13 +676,12 @@ static int enqueue_step(l3g_workspace* ws, const l3g_state* s, int variant, int 
       a.trace_seq = ws->kernels;
       if (ws->tp_p2p) {  // phase 2l + 1
         a.tp_out = tp_exchange(ws, 2 * l + 1);
-        if (ws->tp_fused_reduce) a.tp_y = ws->y;
         KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_PUSH>(L.down, a, m->nsm, st)));
       } else {
         KL(L3G_K_DOWN, (launch_mv<PRO_PREQ, EPI_STORE>(L.down, a, m->nsm, st)));
       }
     }
-    if (ws->tp_p2p && !ws->tp_fused_reduce)
+    if (ws->tp_p2p)
       KL(L3G_K_OTHER, launch(k_tp_reduce, dim3((ne / 4 + 255) / 256), dim3(256), 0, st,
                              tp_exchange(ws, 2 * l + 1), ws->y, ws->d_res, wait_ns));
     else if (m->world > 1)

@@ -114,7 +114,6 @@ int tp_setup(l3g_workspace* ws) {
   if (ok)
     if (int rc = agree(&mapped)) return rc;
   ws->tp_p2p = ok && mapped;
-  if (const char* e = getenv("L3G_TP_FUSED_REDUCE")) ws->tp_fused_reduce = atoi(e) != 0;
   if (!ws->tp_p2p) {  // the NCCL path: drop whatever was set up
     for (int r = 0; r < MAX_WORLD; ++r) {
       if (ws->tp_peer_recv[r] && ws->tp_peer_recv[r] != ws->tp_recv && !ws->tp_peer_same_process[r])
