@@ -341,9 +341,10 @@ def time_matvec_kernel(l3g, cfg, seed, hbm):
 def trace_summary(m, s, ws, tok, pos, reps=3):
     """Device timeline of one step replayed as its graph (kernels overlapping
     as in the timed loop): per kind, the time between consecutive kernel
-    completions (sums to the step), the span from entry to exit, the time
-    from dependency release to the end of the prologue, and the tail from
-    the last CTA's end of tile loop to the last exit."""
+    completions (sums to the step), the span from entry to exit, the active
+    time from dependency release to the last exit, the time from dependency
+    release to the end of the prologue, and the tail from the last CTA's end
+    of tile loop to the last exit."""
     import numpy as np
     acc = {}
     step_us = []
@@ -357,10 +358,11 @@ def trace_summary(m, s, ws, tok, pos, reps=3):
             ent = st[live, 0].min()
             ext = st[live, 4].max()
             released = st[live, 1].min()
-            d = acc.setdefault(kind, {"critical": 0.0, "span": 0.0, "prologue": 0.0, "wake": 0.0,
-                                      "tail": 0.0, "n": 0})
+            d = acc.setdefault(kind, {"critical": 0.0, "span": 0.0, "active": 0.0, "prologue": 0.0,
+                                      "wake": 0.0, "tail": 0.0, "n": 0})
             d["critical"] += (ext - prev_exit) / 1e3
             d["span"] += (ext - ent) / 1e3
+            d["active"] += (ext - released) / 1e3
             d["wake"] += max(0, released - prev_exit) / 1e3
             pro = st[live, 2]
             if (pro > 0).all():
@@ -372,6 +374,7 @@ def trace_summary(m, s, ws, tok, pos, reps=3):
             prev_exit = max(prev_exit, ext)
         step_us.append((prev_exit - first) / 1e3)
     out = {k: {"critical_us": round(v["critical"] / reps, 1), "avg_span_us": round(v["span"] / v["n"], 2),
+               "avg_active_us": round(v["active"] / v["n"], 3),
                "avg_wake_us": round(v["wake"] / v["n"], 2), "avg_prologue_us": round(v["prologue"] / v["n"], 2),
                "avg_tail_us": round(v["tail"] / v["n"], 2),
                "launches": v["n"] // reps}
@@ -541,7 +544,28 @@ def run_l3g(args):
         mv = {"kernel": "k_layers (persistent: every layer of the step, %d CTAs)" % ws_grid,
               "bytes_per_launch": alg, "ms_per_launch": ms, "achieved_gbs": alg / ms / 1e6}
     else:
-        mv = time_matvec_kernel(l3g, cfg, args.seed, hbm) if rank == 0 else None
+        # the dominant kernel as the step runs it: the up/gate matvec
+        # (k_matvec<PRO_RMS, EPI_SWIGLU>: residual + RMSNorm + act-quant
+        # prologue, the 2*n_ff x n_emb Q8_0 matrix, SwiGLU epilogue), its
+        # active time on the step's device timeline (dependency release to
+        # the last CTA's exit, averaged over the layers of the traced steps)
+        ug = timeline.get("upgate_swiglu") if isinstance(timeline, dict) else None
+        rows_ug = 2 * cfg.n_ff // world
+        alg_ug = rows_ug * cfg.n_emb // 32 * 34 + 3 * cfg.n_emb * 4 + rows_ug // 2 * 4
+        standalone = time_matvec_kernel(l3g, cfg, args.seed, hbm) if rank == 0 else None
+        if ug and ug.get("avg_active_us", 0) > 0:
+            ms = ug["avg_active_us"] / 1e3
+            mv = {"kernel": "k_matvec<PRO_RMS, EPI_SWIGLU> in the decode step (FFN up/gate %dx%d)"
+                            % (rows_ug, cfg.n_emb),
+                  "bytes_per_launch": alg_ug, "ms_per_launch": ms, "achieved_gbs": alg_ug / ms / 1e6,
+                  "timing": "device timeline of the step replayed as its graph: dependency release "
+                            "to the last CTA's exit, mean over %d launches" % ug.get("launches", 0),
+                  "standalone_events": None if standalone is None else {
+                      "kernel": standalone["kernel"], "ms_per_launch": round(standalone["ms_per_launch"], 5),
+                      "achieved_gbs": round(standalone["achieved_gbs"], 1),
+                      "timing": "CUDA events over 90 launches of the pre-quantized matvec on rotating copies"}}
+        else:
+            mv = standalone
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -588,7 +612,9 @@ def run_l3g(args):
                                        "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
                                        "(profiles/k_matvec_q8_upgate_28672x4096.md)",
                      "kernel": mv["kernel"], "bytes_per_launch": mv["bytes_per_launch"],
-                     "ms_per_launch": round(mv["ms_per_launch"], 5), "peak_kind": hbm_kind},
+                     "ms_per_launch": round(mv["ms_per_launch"], 5), "peak_kind": hbm_kind,
+                     **({"timing": mv["timing"]} if "timing" in mv else {}),
+                     **({"standalone_events": mv["standalone_events"]} if mv.get("standalone_events") else {})},
         "decode_roofline": {"bytes_per_token": int(step_bytes), "weight_bytes": cfg.weight_bytes(),
                             "kv_bytes_avg": int(kv_bytes), "achieved_gbs": round(decode_gbs, 1),
                             "frac": round(decode_gbs / (hbm * world), 4), "peak_gbs_aggregate": hbm * world},
