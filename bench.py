@@ -12,8 +12,10 @@ Prints one JSON line:
          fed from the previous step's on-device argmax), CUDA-event timed;
   e2e    the same tok/s through the public per-step call
          (l3g_forward_argmax: host token in, pinned H2D, graph, D2H result);
-  roofline       the dominant kernel (the Q8_0 matvec, FFN up/gate shape)
-                 timed live with CUDA events against measured HBM bandwidth;
+  roofline       the dominant kernel as the step runs it (the up/gate matvec
+                 with its RMSNorm prologue and SwiGLU epilogue), its active
+                 time on the step's device timeline against measured HBM
+                 bandwidth (the standalone matvec, CUDA-event timed, beside it);
   decode_roofline  (weight + KV bytes per token) x tok/s / HBM bandwidth;
   cpu_baseline   the oracle (C restatement + the reference's own simd.c) on
                  the host cores, on a bounded sample of the same workload.
@@ -607,10 +609,14 @@ def run_l3g(args):
                    "weights": "seeded N(0,0.02) quantized to Q8_0, norms 1.0; random-init synthetic"},
         "roofline": {"bound": "hbm", "achieved": round(mv["achieved_gbs"], 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(mv["achieved_gbs"] / hbm, 4),
-                     "traffic": None if args.persistent else profiled_traffic("k_matvec_q8_upgate_28672x4096.md"),
+                     "traffic": None if args.persistent else profiled_traffic(
+                         "k_matvec_upgate_swiglu_in_step_28672x4096.md" if "timing" in mv
+                         else "k_matvec_q8_upgate_28672x4096.md"),
                      "traffic_source": "not captured for the persistent kernel" if args.persistent else
-                                       "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
-                                       "(profiles/k_matvec_q8_upgate_28672x4096.md)",
+                                       "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch (%s)" % (
+                                           "profiles/k_matvec_upgate_swiglu_in_step_28672x4096.md: the "
+                                           "in-step kernel, mean of 3 launches" if "timing" in mv else
+                                           "profiles/k_matvec_q8_upgate_28672x4096.md"),
                      "kernel": mv["kernel"], "bytes_per_launch": mv["bytes_per_launch"],
                      "ms_per_launch": round(mv["ms_per_launch"], 5), "peak_kind": hbm_kind,
                      **({"timing": mv["timing"]} if "timing" in mv else {}),
