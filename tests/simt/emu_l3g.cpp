@@ -835,9 +835,11 @@ int emu_matvec_epi(const uint8_t* tiles, int rows, int cols, int rpw, const floa
 // The decode step's split-K attention (k_attention, global merge through
 // partials in device memory, the CTAs of a kv head waiting on each other's
 // arrival counters) for one layer, set up as l3g_workspace_new and
-// enqueue_step do: P positions per stage, three stages, splits filling nsm.
+// enqueue_step do: P positions per stage, nstages stages (the runtime's 4 at
+// one GPU, 6 under tensor parallelism), splits filling nsm.
 int emu_attention(const float* q, const void* kv, int ctx, int hd, int group, int hkv, int kv_f16,
-                  const int* io, float* out, float* out_d, int8_t* out_q, int nsm, int* splits_out) {
+                  const int* io, float* out, float* out_d, int8_t* out_q, int nsm, int nstages,
+                  int* splits_out) {
   return guarded_call([&] {
     using namespace l3g;
     const int es = kv_f16 ? 2 : 4;
@@ -845,7 +847,8 @@ int emu_attention(const float* q, const void* kv, int ctx, int hd, int group, in
     a.P = NW;  // the runtime's stage size: a power of two dividing KV_PAGE
     while (a.P * 2 <= std::min(KV_PAGE, (int)(32768 / (2 * hd * es)))) a.P *= 2;
     a.stage_bytes = 2 * a.P * hd * es;
-    a.nstages = 3;
+    if (nstages < 2 || nstages > 6) simt::fail("stages outside 2..6");
+    a.nstages = nstages;
     a.n_splits = std::max(1, std::min(nsm / hkv, (ctx + a.P - 1) / a.P));
     *splits_out = a.n_splits;
     int gp = 1;

@@ -70,7 +70,7 @@ def lib():
         L.emu_prefill.argtypes = [C.c_void_p]
         L.emu_batch_step.argtypes = [C.c_void_p]
         L.emu_attention.argtypes = [_P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P,
-                                    _P, _P, C.c_int, C.POINTER(C.c_int)]
+                                    _P, _P, C.c_int, C.c_int, C.POINTER(C.c_int)]
         L.emu_matvec.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int, C.c_int,
                                  C.c_int]
         L.emu_matvec_epi.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int, _P, _P,

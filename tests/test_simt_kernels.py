@@ -494,14 +494,18 @@ def test_decode_matvec_matches_reference_simd(S, oracle_mod, rows, cols, rpw, lo
         d.free()
 
 
-@pytest.mark.parametrize("G,hd,hkv,n,f16", [(4, 128, 2, 700, False), (3, 64, 2, 37, False),
-                                            (2, 32, 3, 300, False), (4, 128, 1, 90, True)])
-def test_decode_attention_matches_exact_softmax(S, G, hd, hkv, n, f16):
+@pytest.mark.parametrize("G,hd,hkv,n,f16,nsm,ns", [
+    (4, 128, 2, 700, False, 148, 4), (3, 64, 2, 37, False, 148, 4), (2, 32, 3, 300, False, 148, 6),
+    (4, 128, 1, 90, True, 148, 4), (4, 128, 2, 700, False, 8, 4), (2, 64, 2, 600, False, 2, 6),
+    (4, 128, 2, 500, False, 4, 3)])
+def test_decode_attention_matches_exact_softmax(S, G, hd, hkv, n, f16, nsm, ns):
     """The decode step's k_attention (measured on the B200) under the
     emulator: split-K over the cache with the distributed global merge (the
     CTAs of a kv head wait on each other's arrival counters, which must come
     back to zero), against the reference's exact-exp loop (infer.go:130-175)
-    in float64, and its act-quant for Wo bit for bit."""
+    in float64, and its act-quant for Wo bit for bit; rings of 3, 4 (the
+    one-GPU default) and 6 stages (the tensor-parallel default), with few
+    SMs so that a split streams many stages through the ring."""
     import oracle
     rng = np.random.default_rng(G * 100 + n)
     ctx = S.kv_len(n + 5)  # a whole number of KV pages
@@ -515,7 +519,12 @@ def test_decode_attention_matches_exact_softmax(S, G, hd, hkv, n, f16):
     import ctypes as C
     splits = C.c_int()
     S.check(S.lib().emu_attention(dq.ptr, dkv.ptr, ctx, hd, G, hkv, 1 if f16 else 0, io.ptr, out.ptr,
-                                  od.ptr, oq.ptr, 148, C.byref(splits)))
+                                  od.ptr, oq.ptr, nsm, ns, C.byref(splits)))
+    if nsm < 148:  # every split streams more stages than its ring holds
+        P = 8
+        while P * 2 <= min(S.KV_PAGE, 32768 // (2 * hd * (2 if f16 else 4))):
+            P *= 2
+        assert -(-n // splits.value) > ns * P
     got = out.read(np.float32).reshape(hkv * G, hd)
     scale = np.float32(1.0 / np.sqrt(hd))
     for h in range(hkv * G):
