@@ -105,9 +105,10 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
 
 // Shared-memory merge scratch in the ring after the loop (floats):
 // [NW][MAXG][2] per-warp (m, l), [NW][G][hd] per-warp o, then (CL) the CTA's
-// combined [MAXG][2] (m, l) and [G][hd] o read by the cluster's other CTAs.
+// combined [MAXG][2] (m, l) and [G][hd] o read by the cluster's other CTAs,
+// then the per-head warp weights [NW][MAXG] and (M, L) [MAXG][2].
 __host__ __device__ __forceinline__ int at_scratch_floats(int G, int hd) {
-  return NW * MAXG * 2 + NW * G * hd + MAXG * 2 + G * hd;
+  return NW * MAXG * 2 + NW * G * hd + MAXG * 2 + G * hd + NW * MAXG + MAXG * 2;
 }
 
 // Merge of one 32-output block of a kv head across its S splits (one warp;
@@ -155,7 +156,7 @@ __device__ __forceinline__ float merge_split_block(const float* ml, const float*
       if (s0 + u < S) O = fmaf(ov[u], wbuf[s0 + u], O);
   }
   __syncwarp();
-  return __fmul_rn(O, __fdiv_rn(1.0f, L));
+  return __fmul_rn(O, __frcp_rn(L));
 }
 
 // One CTA per SM (the registers of one attention CTA leave no room for a
@@ -397,28 +398,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   consumer_sync();
   float* cta_ml = sm_o + NW * G * hd;  // CL: this CTA's combined state
   float* cta_o = cta_ml + MAXG * 2;
+  float* sm_e = cta_o + G * hd;        // [NW][MAXG] the warps' weights per query head
+  float* sm_hl = sm_e + NW * MAXG;     // [MAXG][2] per query head: M, L
+  // per query head (one thread each): M = max_w m_w, e_w = exp(m_w - M),
+  // L = sum_w l_w e_w in warp order; every output of the head then only
+  // weighs the warps' partial outputs by e_w
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_ml[(w * MAXG + h) * 2]);
+    float L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float mw = sm_ml[(w * MAXG + h) * 2];
+      const float e = M == -INFINITY || mw == -INFINITY ? 0.0f : expf(mw - M);
+      L = fmaf(sm_ml[(w * MAXG + h) * 2 + 1], e, L);
+      sm_e[w * MAXG + h] = e;
+    }
+    sm_hl[h * 2] = M;
+    sm_hl[h * 2 + 1] = L;
+  }
+  consumer_sync();
   const size_t pbase = ((size_t)kvh * S + split) * G;
   for (int idx = threadIdx.x; idx < G * hd; idx += NW * 32) {
     const int h = idx / hd, d = idx % hd;
     // all NW warps' values loaded up front (independent), then combined
-    float mw[NW], lw[NW], ow[NW];
+    float ow[NW];
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      mw[w] = sm_ml[(w * MAXG + h) * 2];
-      lw[w] = sm_ml[(w * MAXG + h) * 2 + 1];
-      ow[w] = sm_o[((size_t)w * G + h) * hd + d];
-    }
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, mw[w]);
-    float L = 0.0f, O = 0.0f;
+    for (int w = 0; w < NW; ++w) ow[w] = sm_o[((size_t)w * G + h) * hd + d];
+    const float M = sm_hl[h * 2], L = sm_hl[h * 2 + 1];
+    float O = 0.0f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float e = mw[w] == -INFINITY ? 0.0f : expf(mw[w] - M);
-        L = fmaf(lw[w], e, L);
-        O = fmaf(ow[w], e, O);
-      }
+      for (int w = 0; w < NW; ++w) O = fmaf(ow[w], sm_e[w * MAXG + h], O);
     }
     if constexpr (CL) {
       cta_o[idx] = O;
@@ -467,7 +480,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           O = fmaf(os[s2], e, O);
         }
       }
-      const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
+      const float v = __fmul_rn(O, __frcp_rn(L));
       a.out[(size_t)kvh * gh + idx] = v;
       quant_block(v, (kvh * gh + idx) >> 5, lane, a.out_d, a.out_q);
     }

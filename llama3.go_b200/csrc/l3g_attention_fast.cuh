@@ -199,7 +199,7 @@ static __global__ void __launch_bounds__(ATTF_THREADS) k_attf_merge(const __grid
     O = __fadd_rn(O, __ldcg(a.po + pb * hd + blk * 32 + lane));
   }
   // invSumExp := float32(1.0) / sumExp; out = sum(e * V) * invSumExp
-  const float v = __fmul_rn(O, __fdiv_rn(1.0f, L));
+  const float v = __fmul_rn(O, __frcp_rn(L));
   a.out[(size_t)kvh * gh + blk * 32 + lane] = v;
   quant_block(v, gb, lane, a.out_d, a.out_q);
 }

@@ -330,7 +330,7 @@ static __global__ void k_gemm_quantize(const float* x, int n_tok, int cols, int 
   const float mx = warp_max(fabsf(v));
   float scale = __fdiv_rn(mx, 127.0f);
   if (scale == 0.0f) scale = 1e-8f;
-  const float inv = __fdiv_rn(1.0f, scale);
+  const float inv = __frcp_rn(scale);
   const int8_t q = live ? quant_one(v, inv) : (int8_t)0;
   const int ti = n / nt, nn = n % nt, c = bk / BPC, j = bk % BPC;
   uint8_t* ch = act + ((size_t)ti * nk + c) * b_chunk(nt);

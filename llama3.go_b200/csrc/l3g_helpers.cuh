@@ -68,7 +68,7 @@ __device__ __forceinline__ void quant_block(float v, int b, int lane,
   const float m = warp_max(fabsf(v));
   float scale = __fdiv_rn(m, 127.0f);
   if (scale == 0.0f) scale = 1e-8f;
-  const float inv = __fdiv_rn(1.0f, scale);
+  const float inv = __frcp_rn(scale);
   const float f = __fmul_rn(v, inv);
   int q = f >= 0.0f ? (int)__fadd_rn(f, 0.5f) : (int)__fsub_rn(f, 0.5f);
   q = min(127, max(-128, q));
@@ -94,7 +94,7 @@ __device__ __forceinline__ void quant_quad(float4 u, bool live, int blk, int sub
   if (!live) return;
   float scale = __fdiv_rn(m, 127.0f);
   if (scale == 0.0f) scale = 1e-8f;
-  const float inv = __fdiv_rn(1.0f, scale);
+  const float inv = __frcp_rn(scale);
   char4 q;
   q.x = quant_one(u.x, inv);
   q.y = quant_one(u.y, inv);

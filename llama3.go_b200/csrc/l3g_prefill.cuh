@@ -101,7 +101,7 @@ static __global__ void __launch_bounds__(PF_THREADS) k_pf_rms_quant(float* X, co
     if (!live) continue;
     float sc = __fdiv_rn(m, 127.0f);
     if (sc == 0.0f) sc = 1e-8f;
-    const float inv = __fdiv_rn(1.0f, sc);
+    const float inv = __frcp_rn(sc);
     char4 q;
     q.x = quant_one(u.x, inv);
     q.y = quant_one(u.y, inv);
@@ -127,7 +127,7 @@ static __global__ void k_pf_swiglu_quant(const float* UG, int P, int ff, int nt,
   const float mx = warp_max(fabsf(v));
   float scale = __fdiv_rn(mx, 127.0f);
   if (scale == 0.0f) scale = 1e-8f;
-  const float inv = __fdiv_rn(1.0f, scale);
+  const float inv = __frcp_rn(scale);
   const int8_t q = quant_one(v, inv);
   const int ti = p / nt, nn = p % nt, c = i / KC, kin = i % KC;
   uint8_t* ch = act + ((size_t)ti * nk + c) * b_chunk(nt);
