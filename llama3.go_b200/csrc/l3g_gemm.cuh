@@ -4,11 +4,8 @@
 #pragma once
 
 // An int32 block sum (|v| < 2^22: at most 32 * 128 * 128) as fp32, exactly,
-// without the conversion unit: the bits of 1.5 * 2^23 + v, minus 1.5 * 2^23.
-// The first step is done by the tensor core: every tensor-memory buffer
-// holds the integer GEMM_BIAS_BITS before its MMA, which accumulates onto
-// it, so the buffer reads back as the fp32 bits of 1.5 * 2^23 + v; the
-// second is the rescale's packed add of -1.5 * 2^23.
+// without the conversion unit: the bits of 1.5 * 2^23 + v, minus 1.5 * 2^23
+// (the second step is the caller's packed add of -1.5 * 2^23).
 constexpr int GEMM_BIAS_BITS = 0x4B400000;
 constexpr float GEMM_BIAS = 12582912.0f;
 
@@ -85,7 +82,7 @@ __global__ void __launch_bounds__(gemm_threads(NT), gemm::ctas_per_sm(NT))
   constexpr uint32_t IDESC = idesc_i8(TILE_M, NT);
   constexpr int SB = stage_bytes(NT);
   static_assert(NB * NT <= (int)TCOLS && TCOLS <= 512, "tensor memory budget");
-  static_assert(CPT % 8 == 0, "tcgen05.ld / st granularity");
+  static_assert(CPT % 4 == 0, "tcgen05.ld granularity");
   L3G_DYNAMIC_SMEM(smem);
   GemmSmem* sh = reinterpret_cast<GemmSmem*>(smem);
   uint8_t* ring = smem + SMEM_HEAD;
@@ -166,14 +163,13 @@ __global__ void __launch_bounds__(gemm_threads(NT), gemm::ctas_per_sm(NT))
 #pragma unroll
         for (int j = 0; j < BPC; ++j, ++blk) {
           const int buf = blk % NB, use = blk / NB;
-          // phase `use` of the buffer's release: the initial bias fill
-          // (use 0), then each read of the previous block in it
-          if (!mbar_wait(&sh->tempty[buf], use & 1, &sh->abort_flag, g.res, 22, g.wait_ns)) {
+          if (use > 0 &&
+              !mbar_wait(&sh->tempty[buf], (use - 1) & 1, &sh->abort_flag, g.res, 22, g.wait_ns)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          mma_i8(tmem + (uint32_t)(buf * NT), a_desc(a0, j), b_desc(b0, j, NT), IDESC, 1u);
+          mma_i8(tmem + (uint32_t)(buf * NT), a_desc(a0, j), b_desc(b0, j, NT), IDESC, 0u);
           mma_commit(&sh->tfull[buf]);
         }
         if (ok) mma_commit(&sh->empty[s]);
@@ -193,18 +189,6 @@ __global__ void __launch_bounds__(gemm_threads(NT), gemm::ctas_per_sm(NT))
     const int half = ep >> 2;          // column group: token columns [half*CPT, half*CPT+CPT)
     const int m = quarter * 32 + lane; // weight row within the tile
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * CPT);
-    // every buffer's columns of this warp start at the bias, then are
-    // released for their first MMA
-#pragma unroll 1
-    for (int b2 = 0; b2 < NB; ++b2)
-#pragma unroll
-      for (int i = 0; i < CPT / 4; ++i)
-        tmem_fill4(t_lane + (uint32_t)(b2 * NT + i * 4), (uint32_t)GEMM_BIAS_BITS);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0)
-      for (int b2 = 0; b2 < NB; ++b2) mbar_arrive(&sh->tempty[b2]);
     int c = 0, blk = 0;
     bool ok = true;
     for (int ui = 0; ui < my_units && ok; ++ui) {
@@ -235,12 +219,23 @@ __global__ void __launch_bounds__(gemm_threads(NT), gemm::ctas_per_sm(NT))
                                                    g.res, 25, g.wait_ns));
             if (!ok) break;
             tc_fence_after();
-        #pragma unroll
-            for (int i = 0; i < CPT / 8; ++i)
-              tmem_ld8(t_lane + (uint32_t)(buf * NT + i * 8), v[gi] + i * 8);
+            if constexpr (CPT % 8 == 0) {
+#pragma unroll
+              for (int i = 0; i < CPT / 8; ++i)
+                tmem_ld8(t_lane + (uint32_t)(buf * NT + i * 8), v[gi] + i * 8);
+            } else {
+#pragma unroll
+              for (int i = 0; i < CPT / 4; ++i)
+                tmem_ld4(t_lane + (uint32_t)(buf * NT + i * 4), v[gi] + i * 4);
+            }
           }
           if (!ok) break;
           tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+#pragma unroll
+            for (int gi = 0; gi < GB; ++gi) mbar_arrive(&sh->tempty[(blk + gi) % NB]);
           // acc += float(I) * (d_w * d_x), per column, as fmaf(I, d_w * d_x, acc)
           const unsigned long long nbias2 = pk2(-GEMM_BIAS, -GEMM_BIAS);
 #pragma unroll
@@ -254,24 +249,12 @@ __global__ void __launch_bounds__(gemm_threads(NT), gemm::ctas_per_sm(NT))
               const float2 d2 = dxj[i];
               const unsigned long long s2 = mul2(w2, pk2(d2.x, d2.y));
               const unsigned long long f2 =
-                  add2(pk2(__uint_as_float(v[gi][2 * i]), __uint_as_float(v[gi][2 * i + 1])),
+                  add2(pk2(__int_as_float((int)v[gi][2 * i] + GEMM_BIAS_BITS),
+                           __int_as_float((int)v[gi][2 * i + 1] + GEMM_BIAS_BITS)),
                        nbias2);
               acc2[i] = fma2(f2, s2, acc2[i]);
             }
           }
-          // the bias back into the columns just read (their products are in
-          // registers now), then the buffers are released for their next MMA
-#pragma unroll
-          for (int gi = 0; gi < GB; ++gi)
-#pragma unroll
-            for (int i = 0; i < CPT / 4; ++i)
-              tmem_fill4(t_lane + (uint32_t)(((blk + gi) % NB) * NT + i * 4), (uint32_t)GEMM_BIAS_BITS);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0)
-#pragma unroll
-            for (int gi = 0; gi < GB; ++gi) mbar_arrive(&sh->tempty[(blk + gi) % NB]);
         }
         if (!ok) break;
         __syncwarp();

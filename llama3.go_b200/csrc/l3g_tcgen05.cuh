@@ -60,14 +60,6 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* v) {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-// whole warp: the same 32-bit value into 4 consecutive columns of this
-// warp's 32 lanes
-__device__ __forceinline__ void tmem_fill4(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(taddr), "r"(v));
-}
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
 
 // Packed pairs of fp32 (sm_100 f32x2 arithmetic: two IEEE round-to-nearest
 // operations per instruction, the same results as two scalar ones).

@@ -62,18 +62,6 @@ inline void tmem_ld4(uint32_t taddr, uint32_t* v) {
   for (int i = 0; i < 4; ++i) v[i] = t->blk->tmem[(size_t)(lane0 + t->lane) * 512 + col + i];
 }
 inline void tmem_wait_ld() {}
-// whole warp: lane i writes v into 4 columns of tensor-memory lane (taddr lane) + i
-inline void tmem_fill4(uint32_t taddr, uint32_t v) {
-  ::simt::Thread* t = ::simt::cur();
-  __syncwarp();
-  const uint32_t lane0 = taddr >> 16, col = taddr & 0xFFFFu;
-  if (lane0 != 32u * (uint32_t)(t->warp % 4))
-    ::simt::fail("tcgen05.st: a warp may only write its own quarter of the lanes");
-  for (uint32_t u = col / 32; u <= (col + 3) / 32; ++u)
-    if (!(t->blk->tmem_used >> u & 1u)) ::simt::fail("tcgen05.st to unallocated tensor memory");
-  for (int i = 0; i < 4; ++i) t->blk->tmem[(size_t)(lane0 + t->lane) * 512 + col + i] = v;
-}
-inline void tmem_wait_st() {}
 
 inline unsigned long long pk2(float a, float b) {
   return (unsigned long long)__float_as_uint(a) | ((unsigned long long)__float_as_uint(b) << 32);

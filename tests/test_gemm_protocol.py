@@ -8,24 +8,20 @@ arrivals) as separate events that fire at any later time:
   activation copies, then for every later chunk: wait empty[s] (parity
   ((c / ns) - 1) & 1), arrive.expect_tx on full[s], both copies;
 - MMA issuer (warp 1): per chunk wait full[s] (parity (c / ns) & 1); per
-  block wait tempty[buf] (parity use & 1: phase 0 is the initial bias fill,
-  phase u the read of the buffer's block u - 1), issue the MMA into buf
-  (accumulating onto the bias), commit to tfull[buf]; after the chunk's 4
-  blocks commit to empty[s];
-- the rescale warps (4, 8 or 16 by token tile): first fill every buffer's
-  columns with the bias and arrive tempty of each; per chunk wait full[s];
-  per group of GB blocks wait tfull[buf] of each block in order (parity
-  use & 1) and read the buffer, then refill those columns with the bias
-  and arrive tempty[buf] of each; after the chunk arrive empty[s].
+  block wait tempty[buf] (parity (use - 1) & 1 from its second use), issue
+  the MMA into buf, commit to tfull[buf]; after the chunk's 4 blocks commit
+  to empty[s];
+- the rescale warps (4, 8 or 16 by token tile): per chunk wait full[s]; per group of GB blocks wait
+  tfull[buf] of each block in order (parity use & 1) and read the buffer,
+  then arrive tempty[buf] of each; after the chunk arrive empty[s].
 mbarrier model: a phase completes when its pending arrivals reach zero and
 its transaction count is zero; try_wait.parity(P) succeeds when the current
 phase's parity differs from P.  tcgen05.commit arrives once every MMA the
 thread issued before it has completed.  Checked: no deadlock; a stage is read
 (by an MMA or for its scales) only while it holds the chunk the reader
 expects; a copy never lands in a stage an unfinished reader still uses; a
-TMEM buffer is read only while it holds the expected block, is never
-overwritten before every rescale warp read it, and every MMA lands on a
-buffer every rescale warp has refilled with the bias since the last one.
+TMEM buffer is read only while it holds the expected block and is never
+overwritten before every rescale warp read it.
 """
 import random
 
@@ -89,7 +85,6 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1, epi=EPI):
     readers = [set() for _ in range(ns)]  # unfinished readers of the stage's chunk
     tmem = [None] * nb         # block the buffer holds
     unread = [0] * nb          # rescale warps yet to read it
-    filled = [0] * nb          # rescale warps that refilled it with the bias since its last MMA
     copies = []                # copies in flight: (stage, chunk)
     commits = []               # commits in flight: (MMAs issued before it, barrier)
     issued = []                # MMAs in issue order: (block, buffer, stage)
@@ -124,8 +119,8 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1, epi=EPI):
             assert stage[s] == c, "MMA reads the wrong chunk"
             for _ in range(BPC):
                 buf, use = blk % nb, blk // nb
-                if not skip_tempty_wait:
-                    while not tempty[buf].ready(use & 1):
+                if use > 0 and not skip_tempty_wait:
+                    while not tempty[buf].ready((use - 1) & 1):
                         yield
                 assert unread[buf] == 0, "MMA issued into an unread buffer"
                 readers[s].add(("mma", blk))
@@ -139,10 +134,6 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1, epi=EPI):
             yield
 
     def rescale(w):
-        for buf in range(nb):          # the initial bias fill of every buffer
-            filled[buf] += 1
-            tempty[buf].arrive()
-        yield
         blk = 0
         for c in range(nchunks):
             s = c % ns
@@ -163,9 +154,6 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1, epi=EPI):
                 for buf in group:
                     unread[buf] -= 1
                     assert unread[buf] >= 0
-                yield                  # the rescale arithmetic
-                for buf in group:      # refill with the bias, release
-                    filled[buf] += 1
                     tempty[buf].arrive()
                 yield
             readers[s].discard(("epi", w))
@@ -184,8 +172,6 @@ def run(ns, nb, nchunks, seed, skip_tempty_wait=False, gb=1, epi=EPI):
         if kind == "mma":
             blk, buf, s = issued[done[0]]
             assert unread[buf] == 0, "MMA result overwrites an unread buffer"
-            assert filled[buf] == epi, "MMA lands on a buffer not refilled with the bias"
-            filled[buf] = 0
             tmem[buf] = blk
             unread[buf] = epi
             readers[s].discard(("mma", blk))
