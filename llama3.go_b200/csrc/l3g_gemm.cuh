@@ -243,11 +243,14 @@ __global__ void __launch_bounds__(gemm_threads(NT), gemm::ctas_per_sm(NT))
             const int j = j0 + gi;
             const float w = __half2float(dw[j * TILE_M + m]);
             const unsigned long long w2 = pk2(w, w);
-            const float2* dxj = reinterpret_cast<const float2*>(dx + j * NT + half * CPT);
+            // the column scales of this block: 16-byte loads (NT and CPT are
+            // multiples of 4, the stage 128-byte aligned), a pair per product pair
+            const float4* dxj = reinterpret_cast<const float4*>(dx + j * NT + half * CPT);
 #pragma unroll
             for (int i = 0; i < CPT / 2; ++i) {
-              const float2 d2 = dxj[i];
-              const unsigned long long s2 = mul2(w2, pk2(d2.x, d2.y));
+              const float4 d4 = dxj[i >> 1];
+              const unsigned long long s2 =
+                  mul2(w2, (i & 1) ? pk2(d4.z, d4.w) : pk2(d4.x, d4.y));
               const unsigned long long f2 =
                   add2(pk2(__int_as_float((int)v[gi][2 * i] + GEMM_BIAS_BITS),
                            __int_as_float((int)v[gi][2 * i + 1] + GEMM_BIAS_BITS)),
