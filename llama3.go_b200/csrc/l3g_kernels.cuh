@@ -225,22 +225,49 @@ __device__ __forceinline__ int key_index(uint64_t k) {
   return (int)(~(uint32_t)k);
 }
 
+__device__ __forceinline__ void bitonic_step(uint64_t* keys, int i, int j, int k) {
+  const int ixj = i ^ j;
+  if (ixj > i) {
+    const uint64_t x = keys[i], y = keys[ixj];
+    const bool desc = (i & k) == 0;
+    if (desc ? (x < y) : (x > y)) {
+      keys[i] = y;
+      keys[ixj] = x;
+    }
+  }
+}
+// Descending bitonic sort of n keys (a power of two) in shared memory by the
+// whole block.  When n is a multiple of the block size and each warp's share
+// n / warps a multiple of 32, warp w owns the contiguous segment [w * seg,
+// (w + 1) * seg): a step whose partner distance j is below seg pairs keys of
+// one segment, so only the warp synchronizes; the few steps with j >= seg
+// (log2(warps) per merge level) span the block and take block barriers.
+// The keys here are unique, so the result is the same whichever order the
+// steps run in.
 static __device__ void bitonic_desc(uint64_t* keys, int n) {
+  const int T = (int)blockDim.x, W = T >> 5;
+  const int seg = n / W;
+  if (n % T != 0 || seg % 32 != 0) {
+    for (int k = 2; k <= n; k <<= 1)
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < n; i += T) bitonic_step(keys, i, j, k);
+        __syncthreads();
+      }
+    return;
+  }
+  const int base = (threadIdx.x >> 5) * seg + (threadIdx.x & 31);
   for (int k = 2; k <= n; k <<= 1)
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t x = keys[i], y = keys[ixj];
-          const bool desc = (i & k) == 0;
-          if (desc ? (x < y) : (x > y)) {
-            keys[i] = y;
-            keys[ixj] = x;
-          }
-        }
+      if (j >= seg) {
+        __syncthreads();  // the warps' last in-segment steps are done
+        for (int i = threadIdx.x; i < n; i += T) bitonic_step(keys, i, j, k);
+        __syncthreads();
+      } else {
+        for (int m = 0; m < seg; m += 32) bitonic_step(keys, base + m, j, k);
+        __syncwarp();
       }
-      __syncthreads();
     }
+  __syncthreads();
 }
 
 constexpr int TOPK_CHUNK = 2048;

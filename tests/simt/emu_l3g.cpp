@@ -832,6 +832,22 @@ int emu_matvec_epi(const uint8_t* tiles, int rows, int cols, int rpw, const floa
   });
 }
 
+// bitonic_desc (the top-K kernels' sort) of n keys by one block of `threads`
+// threads, in shared memory; keys sorted in place (device).
+int emu_bitonic(unsigned long long* keys, int n, int threads) {
+  return guarded_call([&] {
+    using namespace l3g;
+    simt::launch(dim3(1), dim3(threads), (size_t)n * 8, [&] {
+      L3G_DYNAMIC_SMEM(raw);
+      uint64_t* k = reinterpret_cast<uint64_t*>(raw);
+      for (int i = threadIdx.x; i < n; i += blockDim.x) k[i] = keys[i];
+      __syncthreads();
+      bitonic_desc(k, n);
+      for (int i = threadIdx.x; i < n; i += blockDim.x) keys[i] = k[i];
+    });
+  });
+}
+
 // The decode step's split-K attention (k_attention, global merge through
 // partials in device memory, the CTAs of a kv head waiting on each other's
 // arrival counters) for one layer, set up as l3g_workspace_new and

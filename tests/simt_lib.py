@@ -75,6 +75,7 @@ def lib():
                                  C.c_int]
         L.emu_matvec_epi.argtypes = [_P, C.c_int, C.c_int, C.c_int, _P, _P, _P, C.c_int, _P, _P,
                                      _P, _P, C.c_int]
+        L.emu_bitonic.argtypes = [_P, C.c_int, C.c_int]
         L.emu_gemm.argtypes = [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, _P, C.c_int,
                                C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
         _lib = L

@@ -494,6 +494,26 @@ def test_decode_matvec_matches_reference_simd(S, oracle_mod, rows, cols, rpw, lo
         d.free()
 
 
+@pytest.mark.parametrize("n,threads", [(2048, 256), (2048, 512), (4096, 1024), (4096, 256),
+                                       (64, 256), (512, 1024), (256, 256), (1024, 64)])
+def test_bitonic_sort_of_topk_keys(S, n, threads):
+    """bitonic_desc, the sort of every top-K kernel, under the emulator: n
+    unique keys (ordered logit bits, inverted id, as the top-K kernels build
+    them) come out in descending order, whether warps sort their own
+    segments between block barriers (n a multiple of the block, 32 or more
+    keys per warp) or every step is block-wide (the others)."""
+    rng = np.random.default_rng(n * 7 + threads)
+    ids = rng.permutation(n).astype(np.uint64)
+    vals = rng.integers(0, 2**31, n, dtype=np.uint64)
+    vals[: n // 8] = vals[0]  # ties in value, broken by the id
+    keys = (vals << np.uint64(32)) | (~ids & np.uint64(0xFFFFFFFF))
+    d = S.Dev(keys)
+    S.check(S.lib().emu_bitonic(d.ptr, n, threads))
+    got = d.read(np.uint64)
+    assert np.array_equal(got, np.sort(keys)[::-1])
+    d.free()
+
+
 @pytest.mark.parametrize("G,hd,hkv,n,f16,nsm,ns", [
     (4, 128, 2, 700, False, 148, 4), (3, 64, 2, 37, False, 148, 4), (2, 32, 3, 300, False, 148, 6),
     (4, 128, 1, 90, True, 148, 4), (4, 128, 2, 700, False, 8, 4), (2, 64, 2, 600, False, 2, 6),
